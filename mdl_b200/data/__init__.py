@@ -1,0 +1,1 @@
+"""mdl_b200 package."""

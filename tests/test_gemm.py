@@ -1,0 +1,94 @@
+"""Numerics of the tcgen05 batched GEMM against a plain PyTorch fp32 reference."""
+
+import pytest
+import torch
+
+from mdl_b200.ops import gemm as G
+
+
+def _ref(a, b, M, N, K, Gn, lda, gsA, a_mn, ldb, gsB, b_mn):
+    av = G._view(a, Gn, M, K, gsA, lda, a_mn).float()
+    bv = G._view(b, Gn, N, K, gsB, ldb, b_mn).float()
+    return torch.bmm(av, bv.transpose(1, 2))
+
+
+def _operands(M, N, K, Gn, a_mn, b_mn, device):
+    torch.manual_seed(0)
+    if a_mn:
+        a = torch.randn(Gn, K, M, device=device).bfloat16()
+        lda, gsA = M, K * M
+    else:
+        a = torch.randn(Gn, M, K, device=device).bfloat16()
+        lda, gsA = K, M * K
+    if b_mn:
+        b = torch.randn(Gn, K, N, device=device).bfloat16()
+        ldb, gsB = N, K * N
+    else:
+        b = torch.randn(Gn, N, K, device=device).bfloat16()
+        ldb, gsB = K, N * K
+    return a, lda, gsA, b, ldb, gsB
+
+
+@pytest.mark.parametrize("a_mn", [False, True])
+@pytest.mark.parametrize("b_mn", [False, True])
+@pytest.mark.parametrize("shape", [(128, 256, 64, 1), (256, 512, 192, 3), (200, 296, 136, 2)])
+def test_gemm_cpu_reference_matches_bmm(a_mn, b_mn, shape):
+    M, N, K, Gn = shape
+    a, lda, gsA, b, ldb, gsB = _operands(M, N, K, Gn, a_mn, b_mn, "cpu")
+    out = torch.empty(Gn, M, N)
+    G.bgemm(a, b, out, M=M, N=N, K=K, G=Gn, lda=lda, gsA=gsA, a_mn=a_mn, ldb=ldb, gsB=gsB, b_mn=b_mn,
+            ldc=N, gsC=M * N)
+    ref = _ref(a, b, M, N, K, Gn, lda, gsA, a_mn, ldb, gsB, b_mn)
+    torch.testing.assert_close(out, ref)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("a_mn", [False, True])
+@pytest.mark.parametrize("b_mn", [False, True])
+@pytest.mark.parametrize("shape", [(128, 256, 64, 1), (256, 512, 192, 3), (200, 296, 136, 2), (1024, 768, 1024, 4)])
+def test_gemm_tcgen05_layouts(a_mn, b_mn, shape):
+    M, N, K, Gn = shape
+    a, lda, gsA, b, ldb, gsB = _operands(M, N, K, Gn, a_mn, b_mn, "cuda")
+    out = torch.empty(Gn, M, N, device="cuda", dtype=torch.float32)
+    G.bgemm(a, b, out, M=M, N=N, K=K, G=Gn, lda=lda, gsA=gsA, a_mn=a_mn, ldb=ldb, gsB=gsB, b_mn=b_mn,
+            ldc=N, gsC=M * N)
+    torch.cuda.synchronize()
+    ref = _ref(a, b, M, N, K, Gn, lda, gsA, a_mn, ldb, gsB, b_mn)
+    torch.testing.assert_close(out, ref, atol=2e-3 * K ** 0.5, rtol=1e-3)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("act", [G.ACT_NONE, G.ACT_GELU, G.ACT_DGELU, G.ACT_RELU])
+def test_gemm_tcgen05_epilogues(act):
+    M, N, K, Gn = 384, 512, 256, 2
+    a, lda, gsA, b, ldb, gsB = _operands(M, N, K, Gn, False, True, "cuda")
+    bias = torch.randn(Gn, N, device="cuda")
+    aux = torch.randn(Gn, M, N, device="cuda").bfloat16()
+    out = torch.empty(Gn, M, N, device="cuda", dtype=torch.bfloat16)
+    out2 = torch.empty_like(out)
+    colsum = torch.zeros(Gn, N, device="cuda")
+    G.bgemm(a, b, out, M=M, N=N, K=K, G=Gn, lda=lda, gsA=gsA, ldb=ldb, gsB=gsB, b_mn=True, ldc=N, gsC=M * N,
+            out2=out2, bias=bias, gs_bias=N, aux=aux, ld_aux=N, gs_aux=M * N, colsum=colsum, gs_colsum=N,
+            act=act, alpha=0.5)
+    ref_out = torch.empty(Gn, M, N, dtype=torch.bfloat16)
+    ref_out2 = torch.empty_like(ref_out)
+    ref_cs = torch.zeros(Gn, N)
+    G.bgemm(a.cpu(), b.cpu(), ref_out, M=M, N=N, K=K, G=Gn, lda=lda, gsA=gsA, ldb=ldb, gsB=gsB, b_mn=True, ldc=N,
+            gsC=M * N, out2=ref_out2, bias=bias.cpu(), gs_bias=N, aux=aux.cpu(), ld_aux=N, gs_aux=M * N,
+            colsum=ref_cs, gs_colsum=N, act=act, alpha=0.5)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(out.cpu().float(), ref_out.float(), atol=0.05, rtol=0.02)
+    if act == G.ACT_GELU:
+        torch.testing.assert_close(out2.cpu().float(), ref_out2.float(), atol=0.05, rtol=0.02)
+    torch.testing.assert_close(colsum.cpu(), ref_cs, atol=0.5, rtol=0.02)
+
+
+@pytest.mark.gpu
+def test_gemm_tcgen05_accumulate_fp32():
+    M, N, K = 256, 256, 128
+    a, lda, gsA, b, ldb, gsB = _operands(M, N, K, 1, True, True, "cuda")
+    out = torch.ones(M, N, device="cuda")
+    G.bgemm(a, b, out, M=M, N=N, K=K, lda=lda, a_mn=True, ldb=ldb, b_mn=True, ldc=N, accumulate=True)
+    ref = _ref(a, b, M, N, K, 1, lda, gsA, True, ldb, gsB, True)[0] + 1.0
+    torch.cuda.synchronize()
+    torch.testing.assert_close(out, ref, atol=2e-2, rtol=1e-3)
