@@ -1,0 +1,188 @@
+"""Benchmark entry point: train samples/sec of the BASELINE RankMixer workload (config 2).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+For N > 1 run it under ``python -m torch.distributed.run --nproc-per-node N``.
+Every rank trains on its own synthetic batch of 2048 rows (weak scaling); the
+embedding tables (about 200M rows x 64 fp32) are sharded across ranks.
+
+Timing: W warm-up steps, then K steps bracketed by a barrier and a device
+synchronize on both sides, timed with CUDA events on the launching stream; the
+reported time is the max over ranks. Per-step inputs live in distinct batches
+and the working set (51 GB of tables, GBs of activations) is far above the
+126 MB L2. A second timed loop measures the same metric end to end through
+``Trainer.step_from_host``: each step copies a pinned host batch to the device
+and the loss back to the host. SM clocks and throttle reasons are sampled with
+nvidia-smi during the timed loops. Rank 0 prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import sys
+import time
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+BASELINE_VALUE = None  # BASELINE.md publishes no B200 number for this workload
+METRIC = "train samples/sec"
+
+
+def _dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def _max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(world):
+    if world > 1:
+        dist.barrier()
+
+
+def run_ours(args) -> dict:
+    from mdl_b200.config import app_config_from_mapping
+    from mdl_b200.data.baseline_configs import baseline_config
+    from mdl_b200.data.synthetic import BatchPool, SyntheticGenerator
+    from mdl_b200.models.factory import build_model
+    from mdl_b200.ops._ext import check_error_word, ext
+    from mdl_b200.train.trainer import Trainer
+    from mdl_b200.utils.clocks import ClockSampler
+
+    rank, world, local = _dist_setup(args)
+    device = torch.device("cuda", local)
+    mapping, spec = baseline_config(2, batch=args.batch)
+    cfg = app_config_from_mapping(mapping)
+    torch.manual_seed(1234)
+    pg = dist.group.WORLD if world > 1 else None
+    model = build_model(cfg, device=device, rank=rank, world=world, process_group=pg, base_seed=1234)
+    trainer = Trainer(cfg, model, device=device, rank=rank, world=world, process_group=pg)
+    gen = SyntheticGenerator(model.encoder.plan, spec, rank=rank)
+    pool = BatchPool(gen, args.batch, count=args.pool, pin=True)
+    dev_batches = [b.to(device) for b in pool.batches]
+    torch.cuda.synchronize(device)
+
+    for i in range(args.warmup):
+        trainer.train_step(dev_batches[i % len(dev_batches)])
+    torch.cuda.synchronize(device)
+    check_error_word(device)
+
+    # ---- device-timed loop
+    props = torch.cuda.get_device_properties(device)
+    sampler = ClockSampler(f"GPU-{props.uuid}" if getattr(props, "uuid", None) else local).start()
+    launches0 = ext().launch_count()
+    _barrier(world)
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(args.steps):
+        trainer.train_step(dev_batches[i % len(dev_batches)])
+    end.record()
+    torch.cuda.synchronize(device)
+    _barrier(world)
+    launches = ext().launch_count() - launches0
+    ms = start.elapsed_time(end)
+    clocks = sampler.stop()
+    check_error_word(device)
+    ms_max = _max_over_ranks(ms, world)
+
+    # ---- end-to-end loop through the public API (pinned H2D in, loss D2H out, every step)
+    loss_host = torch.zeros(args.steps, dtype=torch.float32, pin_memory=True)
+    _barrier(world)
+    torch.cuda.synchronize(device)
+    start2, end2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start2.record()
+    for i in range(args.steps):
+        trainer.step_from_host(pool.next(), loss_out=loss_host[i:i + 1])
+    end2.record()
+    torch.cuda.synchronize(device)
+    _barrier(world)
+    ms_e2e = _max_over_ranks(start2.elapsed_time(end2), world)
+    check_error_word(device)
+    h2d = pool.batches[0].nbytes()
+
+    rows_total = args.batch * world * args.steps
+    value = rows_total / (ms_max / 1000.0)
+    e2e = rows_total / (ms_e2e / 1000.0)
+    n_params = sum(p.numel() for p in model.parameters())
+    return {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "samples/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_max / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None if BASELINE_VALUE is None else round(value / BASELINE_VALUE, 3),
+        "dtype": "bf16",
+        "data": "synthetic (seeded Zipf(1.05) ids, N(0,1) dense, labels from a hidden model); random-init weights",
+        "config": {
+            "model": "rankmixer (BASELINE config 2: 300 fields, ~200M x 64 fp32 rows, T=16 D=768 L=2 FFNx4, 2 heads)",
+            "global_batch": args.batch * world,
+            "seq_len": None,
+            "parallelism": f"dp{world}+emb-rowwise/tablewise-mp{world}",
+            "dense_params": n_params,
+            "embedding_rows": sum(t.num_embeddings for t in model.store.layouts),
+            "l2": "inputs larger than L2 (tables 51 GB, activations GBs; 4 distinct batches rotated)",
+            "comm": cfg.training.comm,
+        },
+        "clocks": clocks,
+        "e2e": {"value": round(e2e, 1), "unit": "samples/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},
+        "gpu_launches": launches,
+        "final_loss": float(loss_host[-1]),
+    }
+
+
+def run_reference(args) -> dict:
+    from baseline import reference_harness
+
+    return reference_harness.run(args)
+
+
+def main(argv=None) -> int:
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--batch", type=int, default=2048, help="rows per GPU")
+    p.add_argument("--pool", type=int, default=4, help="distinct pinned host batches rotated per step")
+    args = p.parse_args(argv)
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    result = run_reference(args) if args.impl == "reference" else run_ours(args)
+    rank = int(os.environ.get("RANK", "0"))
+    if rank == 0 and result is not None:
+        print(json.dumps(result), flush=True)
+    if dist.is_initialized():
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -13,6 +13,10 @@
 
 namespace {
 
+// Number of kernels launched through these bindings (benchmarks report it).
+long long g_launches = 0;
+int64_t launch_count() { return g_launches; }
+
 void check(cudaError_t e, const char* what) {
   if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
 }
@@ -81,6 +85,424 @@ void gemm(const at::Tensor& A, int64_t lda, int64_t gsA, bool a_mn, const at::Te
   a.err = optr<int>(err);
   a.max_ctas = static_cast<int>(max_ctas);
   check(mdl::gemm_bf16_tcgen05(a, stream_of(A)), "gemm_bf16_tcgen05");
+  g_launches += 1;
+}
+
+
+// ------------------------------------------------------------------ embedding
+template <typename T>
+const T* dptr(const at::Tensor& t) { return t.defined() && t.numel() ? reinterpret_cast<const T*>(t.data_ptr()) : nullptr; }
+
+mdl::EmbPlan make_plan(const std::vector<at::Tensor>& meta, const std::vector<int64_t>& slabs,
+                       const std::vector<int64_t>& grad_slabs, const std::vector<int64_t>& flags,
+                       const std::vector<int64_t>& touched, const std::vector<int64_t>& counts, int64_t touched_cap,
+                       int64_t rank, const at::Tensor& ids, const at::Tensor& id_offsets,
+                       const std::optional<at::Tensor>& dense, int64_t dense_ld, const std::optional<at::Tensor>& err) {
+  // meta order (all device tensors):
+  //  0 f_chunk_prefix(i64) 1 f_bag_prefix(i64) 2 f_table(i32) 3 f_pool(i32) 4 f_hash(i32) 5 f_buckets(i64)
+  //  6 f_width(i32) 7 f_lanes(i32) 8 f_out_base(i64) 9 f_out_ld(i64) 10 f_out_col(i32) 11 f_slice(i32)
+  //  12 f_slice_stride(i32) 13 f_dense_col(i32) 14 t_base(i64) 15 t_row_base(i64) 16 t_dim(i32) 17 t_mode(i32)
+  //  18 t_cyc(i32) 19 t_owner(i32) 20 t_rows(i64)
+  TORCH_CHECK(meta.size() == 21, "embedding plan needs 21 metadata tensors");
+  mdl::EmbPlan p;
+  p.num_features = static_cast<int>(meta[2].numel());
+  p.world = static_cast<int>(slabs.size());
+  TORCH_CHECK(p.world >= 1 && p.world <= mdl::kMaxWorld, "world size out of range");
+  p.rank = static_cast<int>(rank);
+  p.f_chunk_prefix = dptr<long long>(meta[0]);
+  p.f_bag_prefix = dptr<long long>(meta[1]);
+  p.f_table = dptr<int>(meta[2]);
+  p.f_pool = dptr<int>(meta[3]);
+  p.f_hash = dptr<int>(meta[4]);
+  p.f_buckets = dptr<long long>(meta[5]);
+  p.f_width = dptr<int>(meta[6]);
+  p.f_lanes = dptr<int>(meta[7]);
+  p.f_out_base = dptr<long long>(meta[8]);
+  p.f_out_ld = dptr<long long>(meta[9]);
+  p.f_out_col = dptr<int>(meta[10]);
+  p.f_slice = dptr<int>(meta[11]);
+  p.f_slice_stride = dptr<int>(meta[12]);
+  p.f_dense_col = dptr<int>(meta[13]);
+  p.t_base = dptr<long long>(meta[14]);
+  p.t_row_base = dptr<long long>(meta[15]);
+  p.t_dim = dptr<int>(meta[16]);
+  p.t_mode = dptr<int>(meta[17]);
+  p.t_cyc = dptr<int>(meta[18]);
+  p.t_owner = dptr<int>(meta[19]);
+  p.t_rows = dptr<long long>(meta[20]);
+  for (int r = 0; r < p.world; ++r) {
+    p.slabs[r] = reinterpret_cast<float*>(slabs[r]);
+    if (r < static_cast<int>(grad_slabs.size())) p.grad_slabs[r] = reinterpret_cast<float*>(grad_slabs[r]);
+    if (r < static_cast<int>(flags.size())) p.flags[r] = reinterpret_cast<unsigned*>(flags[r]);
+    if (r < static_cast<int>(touched.size())) p.touched[r] = reinterpret_cast<long long*>(touched[r]);
+    if (r < static_cast<int>(counts.size())) p.touched_count[r] = reinterpret_cast<int*>(counts[r]);
+  }
+  p.touched_cap = touched_cap;
+  p.ids = dptr<long long>(ids);
+  p.id_offsets = dptr<long long>(id_offsets);
+  p.dense = dense.has_value() ? dptr<float>(*dense) : nullptr;
+  p.dense_ld = dense_ld;
+  p.err = optr<int>(err);
+  return p;
+}
+
+void emb_forward(const std::vector<at::Tensor>& meta, const std::vector<int64_t>& slabs, int64_t rank,
+                 const at::Tensor& ids, const at::Tensor& id_offsets, const std::optional<at::Tensor>& dense,
+                 int64_t dense_ld, const at::Tensor& out, int64_t total_chunks, const std::optional<at::Tensor>& err) {
+  c10::cuda::CUDAGuard guard(out.device());
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16, "embedding output must be bf16");
+  mdl::EmbPlan p = make_plan(meta, slabs, {}, {}, {}, {}, 0, rank, ids, id_offsets, dense, dense_ld, err);
+  p.out = out.data_ptr();
+  check(mdl::emb_pool_forward(p, total_chunks, stream_of(out)), "emb_pool_forward");
+  g_launches += 1;
+}
+
+void emb_backward(const std::vector<at::Tensor>& meta, const std::vector<int64_t>& slabs,
+                  const std::vector<int64_t>& grad_slabs, const std::vector<int64_t>& flags,
+                  const std::vector<int64_t>& touched, const std::vector<int64_t>& counts, int64_t touched_cap,
+                  int64_t rank, const at::Tensor& ids, const at::Tensor& id_offsets, const at::Tensor& grad_out,
+                  int64_t total_chunks, const std::optional<at::Tensor>& err) {
+  c10::cuda::CUDAGuard guard(grad_out.device());
+  TORCH_CHECK(grad_out.scalar_type() == at::kBFloat16, "embedding grad must be bf16");
+  mdl::EmbPlan p = make_plan(meta, slabs, grad_slabs, flags, touched, counts, touched_cap, rank, ids, id_offsets,
+                             std::nullopt, 0, err);
+  check(mdl::emb_pool_backward(p, grad_out.data_ptr(), total_chunks, stream_of(grad_out)), "emb_pool_backward");
+  g_launches += 1;
+}
+
+mdl::AdagradArgs adagrad_args(const at::Tensor& slab, const at::Tensor& grad_slab, const at::Tensor& acc,
+                              const at::Tensor& flags, const at::Tensor& touched, const at::Tensor& count,
+                              const at::Tensor& t_base, const at::Tensor& t_row_base, const at::Tensor& t_dim,
+                              double lr, double eps, double grad_scale, const std::optional<at::Tensor>& clip,
+                              const std::optional<at::Tensor>& err) {
+  mdl::AdagradArgs a;
+  a.slab = ptr<float>(slab);
+  a.grad_slab = ptr<float>(grad_slab);
+  a.acc = ptr<float>(acc);
+  a.flags = ptr<unsigned>(flags);
+  a.touched = ptr<const long long>(touched);
+  a.touched_count = ptr<int>(count);
+  a.t_base = ptr<const long long>(t_base);
+  a.t_row_base = ptr<const long long>(t_row_base);
+  a.t_dim = ptr<const int>(t_dim);
+  a.lr = static_cast<float>(lr);
+  a.eps = static_cast<float>(eps);
+  a.grad_scale = static_cast<float>(grad_scale);
+  a.clip_scale = optr<const float>(clip);
+  a.cap = touched.numel();
+  a.err = optr<int>(err);
+  return a;
+}
+
+void adagrad_apply(const at::Tensor& slab, const at::Tensor& grad_slab, const at::Tensor& acc, const at::Tensor& flags,
+                   const at::Tensor& touched, const at::Tensor& count, const at::Tensor& t_base,
+                   const at::Tensor& t_row_base, const at::Tensor& t_dim, double lr, double eps, double grad_scale,
+                   const std::optional<at::Tensor>& clip, const std::optional<at::Tensor>& err) {
+  c10::cuda::CUDAGuard guard(slab.device());
+  auto a = adagrad_args(slab, grad_slab, acc, flags, touched, count, t_base, t_row_base, t_dim, lr, eps, grad_scale,
+                        clip, err);
+  check(mdl::rowwise_adagrad_apply(a, stream_of(slab)), "rowwise_adagrad_apply");
+  g_launches += 1;
+}
+
+void touched_sqnorm(const at::Tensor& grad_slab, const at::Tensor& touched, const at::Tensor& count,
+                    const at::Tensor& t_base, const at::Tensor& t_row_base, const at::Tensor& t_dim, double grad_scale,
+                    const at::Tensor& out) {
+  c10::cuda::CUDAGuard guard(grad_slab.device());
+  mdl::AdagradArgs a = adagrad_args(grad_slab, grad_slab, grad_slab, grad_slab, touched, count, t_base, t_row_base,
+                                    t_dim, 0.0, 1.0, grad_scale, std::nullopt, std::nullopt);
+  check(mdl::touched_grad_sqnorm(a, ptr<float>(out), stream_of(grad_slab)), "touched_grad_sqnorm");
+  g_launches += 1;
+}
+
+// ------------------------------------------------------------------ norms
+void ln_fwd(const at::Tensor& a, const std::optional<at::Tensor>& b, const std::optional<at::Tensor>& gamma,
+            const std::optional<at::Tensor>& beta, const at::Tensor& out, const at::Tensor& mean,
+            const at::Tensor& rstd, int64_t B, int64_t T, int64_t D, bool mix, double eps) {
+  c10::cuda::CUDAGuard guard(a.device());
+  mdl::LNFwdArgs p;
+  p.a = a.data_ptr();
+  p.b = optr(b);
+  p.gamma = optr<const float>(gamma);
+  p.beta = optr<const float>(beta);
+  p.out = out.data_ptr();
+  p.mean = ptr<float>(mean);
+  p.rstd = ptr<float>(rstd);
+  p.B = static_cast<int>(B);
+  p.T = static_cast<int>(T);
+  p.D = static_cast<int>(D);
+  p.mix = mix ? 1 : 0;
+  p.eps = static_cast<float>(eps);
+  check(mdl::layernorm_fwd(p, stream_of(a)), "layernorm_fwd");
+  g_launches += 1;
+}
+
+int64_t ln_bwd_grid(int64_t B) { return mdl::layernorm_bwd_grid(static_cast<int>(B)); }
+
+void ln_bwd(const std::optional<at::Tensor>& dy, const std::optional<at::Tensor>& dy_bcast, double bcast_scale,
+            const at::Tensor& a, const std::optional<at::Tensor>& b, const at::Tensor& mean, const at::Tensor& rstd,
+            const std::optional<at::Tensor>& gamma, const at::Tensor& dx, const std::optional<at::Tensor>& dx2,
+            const at::Tensor& partials, const std::optional<at::Tensor>& dgamma, const std::optional<at::Tensor>& dbeta,
+            int64_t B, int64_t T, int64_t D, bool mix, int64_t grid) {
+  c10::cuda::CUDAGuard guard(a.device());
+  mdl::LNBwdArgs p;
+  p.dy = optr(dy);
+  p.dy_bcast = optr(dy_bcast);
+  p.bcast_scale = static_cast<float>(bcast_scale);
+  p.a = a.data_ptr();
+  p.b = optr(b);
+  p.mean = ptr<float>(mean);
+  p.rstd = ptr<float>(rstd);
+  p.gamma = optr<const float>(gamma);
+  p.dx = dx.data_ptr();
+  p.dx2 = optr(dx2);
+  p.partials = ptr<float>(partials);
+  p.dgamma = optr<float>(dgamma);
+  p.dbeta = optr<float>(dbeta);
+  p.B = static_cast<int>(B);
+  p.T = static_cast<int>(T);
+  p.D = static_cast<int>(D);
+  p.mix = mix ? 1 : 0;
+  p.grid = static_cast<int>(grid);
+  check(mdl::layernorm_bwd(p, stream_of(a)), "layernorm_bwd");
+  g_launches += 2;
+}
+
+void rms_fwd(const at::Tensor& x, const std::optional<at::Tensor>& w, const at::Tensor& out, const at::Tensor& rstd,
+             int64_t rows, int64_t D, double eps) {
+  c10::cuda::CUDAGuard guard(x.device());
+  mdl::RMSArgs p;
+  p.x = x.data_ptr();
+  p.weight = optr<const float>(w);
+  p.out = out.data_ptr();
+  p.rstd = ptr<float>(rstd);
+  p.rows = rows;
+  p.D = static_cast<int>(D);
+  p.eps = static_cast<float>(eps);
+  check(mdl::rmsnorm_fwd(p, stream_of(x)), "rmsnorm_fwd");
+  g_launches += 1;
+}
+
+void rms_bwd(const at::Tensor& x, const std::optional<at::Tensor>& w, const at::Tensor& rstd, const at::Tensor& dy,
+             const at::Tensor& dx, const std::optional<at::Tensor>& dw, int64_t rows, int64_t D) {
+  c10::cuda::CUDAGuard guard(x.device());
+  mdl::RMSArgs p;
+  p.x = x.data_ptr();
+  p.weight = optr<const float>(w);
+  p.rstd = ptr<float>(rstd);
+  p.dy = dy.data_ptr();
+  p.dx = dx.data_ptr();
+  p.dweight = optr<float>(dw);
+  p.rows = rows;
+  p.D = static_cast<int>(D);
+  check(mdl::rmsnorm_bwd(p, stream_of(x)), "rmsnorm_bwd");
+  g_launches += 1;
+}
+
+// ------------------------------------------------------------------ misc
+void token_mean(const at::Tensor& x, const at::Tensor& out, int64_t B, int64_t T, int64_t D) {
+  c10::cuda::CUDAGuard guard(x.device());
+  check(mdl::token_mean_fwd(x.data_ptr(), out.data_ptr(), static_cast<int>(B), static_cast<int>(T),
+                            static_cast<int>(D), stream_of(x)),
+        "token_mean_fwd");
+  g_launches += 1;
+}
+
+void colsum(const at::Tensor& x, const at::Tensor& out, int64_t G, int64_t M, int64_t N, int64_t ld, int64_t gs,
+            double scale) {
+  c10::cuda::CUDAGuard guard(x.device());
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && out.scalar_type() == at::kFloat, "colsum: bf16 in, fp32 out");
+  check(mdl::colsum_bf16(x.data_ptr(), ptr<float>(out), static_cast<int>(G), M, static_cast<int>(N), ld, gs,
+                         static_cast<float>(scale), stream_of(x)),
+        "colsum_bf16");
+  g_launches += 1;
+}
+
+void head_bce(const at::Tensor& act, const at::Tensor& pre, const at::Tensor& w2, const std::optional<at::Tensor>& b2,
+              const std::optional<at::Tensor>& labels, const std::optional<at::Tensor>& mask,
+              const std::optional<at::Tensor>& task_scale, const std::optional<at::Tensor>& logits,
+              const std::optional<at::Tensor>& loss, const std::optional<at::Tensor>& dpre,
+              const std::optional<at::Tensor>& dw2, const std::optional<at::Tensor>& db2, int64_t B, int64_t ntask,
+              int64_t H, bool relu) {
+  c10::cuda::CUDAGuard guard(act.device());
+  mdl::HeadArgs p;
+  p.act = act.data_ptr();
+  p.pre = pre.data_ptr();
+  p.w2 = ptr<const float>(w2);
+  p.b2 = optr<const float>(b2);
+  p.labels = optr<const float>(labels);
+  p.mask = optr<const float>(mask);
+  p.task_scale = optr<const float>(task_scale);
+  p.logits = optr<float>(logits);
+  p.loss = optr<float>(loss);
+  p.dpre = optr(dpre);
+  p.dw2 = optr<float>(dw2);
+  p.db2 = optr<float>(db2);
+  p.B = static_cast<int>(B);
+  p.ntask = static_cast<int>(ntask);
+  p.H = static_cast<int>(H);
+  p.relu = relu ? 1 : 0;
+  check(mdl::head_bce(p, stream_of(act)), "head_bce");
+  g_launches += 1;
+}
+
+mdl::OptimArgs optim_args(const at::Tensor& param, const at::Tensor& grad, const at::Tensor& s1,
+                          const std::optional<at::Tensor>& s2, const std::optional<at::Tensor>& shadow, double lr,
+                          double beta1, double beta2, double eps, double wd, double bc1, double bc2, double alpha,
+                          double grad_scale, const std::optional<at::Tensor>& clip) {
+  mdl::OptimArgs a;
+  a.param = ptr<float>(param);
+  a.grad = ptr<const float>(grad);
+  a.state1 = ptr<float>(s1);
+  a.state2 = optr<float>(s2);
+  a.shadow = optr(shadow);
+  a.n = param.numel();
+  a.lr = static_cast<float>(lr);
+  a.beta1 = static_cast<float>(beta1);
+  a.beta2 = static_cast<float>(beta2);
+  a.eps = static_cast<float>(eps);
+  a.weight_decay = static_cast<float>(wd);
+  a.bias_correction1 = static_cast<float>(bc1);
+  a.bias_correction2 = static_cast<float>(bc2);
+  a.alpha = static_cast<float>(alpha);
+  a.grad_scale = static_cast<float>(grad_scale);
+  a.clip = optr<const float>(clip);
+  return a;
+}
+
+void adam(const at::Tensor& param, const at::Tensor& grad, const at::Tensor& m, const at::Tensor& v,
+          const std::optional<at::Tensor>& shadow, double lr, double beta1, double beta2, double eps, double wd,
+          double bc1, double bc2, double grad_scale, const std::optional<at::Tensor>& clip) {
+  c10::cuda::CUDAGuard guard(param.device());
+  auto a = optim_args(param, grad, m, v, shadow, lr, beta1, beta2, eps, wd, bc1, bc2, 0.0, grad_scale, clip);
+  check(mdl::adam_step(a, stream_of(param)), "adam_step");
+  g_launches += 1;
+}
+
+void rmsprop(const at::Tensor& param, const at::Tensor& grad, const at::Tensor& sq,
+             const std::optional<at::Tensor>& shadow, double lr, double alpha, double eps, double wd,
+             double grad_scale, const std::optional<at::Tensor>& clip) {
+  c10::cuda::CUDAGuard guard(param.device());
+  auto a = optim_args(param, grad, sq, std::nullopt, shadow, lr, 0.0, 0.0, eps, wd, 1.0, 1.0, alpha, grad_scale, clip);
+  check(mdl::rmsprop_step(a, stream_of(param)), "rmsprop_step");
+  g_launches += 1;
+}
+
+void sqnorm(const at::Tensor& grad, double grad_scale, const at::Tensor& out) {
+  c10::cuda::CUDAGuard guard(grad.device());
+  check(mdl::grad_sqnorm(ptr<const float>(grad), grad.numel(), static_cast<float>(grad_scale), ptr<float>(out),
+                         stream_of(grad)),
+        "grad_sqnorm");
+  g_launches += 1;
+}
+
+void clip_factor(const at::Tensor& sum_sq, double max_norm, const at::Tensor& clip) {
+  c10::cuda::CUDAGuard guard(sum_sq.device());
+  check(mdl::clip_factor(ptr<const float>(sum_sq), static_cast<float>(max_norm), ptr<float>(clip), stream_of(sum_sq)),
+        "clip_factor");
+  g_launches += 1;
+}
+
+void cast_bf16(const at::Tensor& src, const at::Tensor& dst) {
+  c10::cuda::CUDAGuard guard(src.device());
+  check(mdl::cast_f32_bf16(ptr<const float>(src), dst.data_ptr(), src.numel(), stream_of(src)), "cast_f32_bf16");
+  g_launches += 1;
+}
+
+
+// ------------------------------------------------------------------ symmetric memory
+py::tuple ipc_alloc(int64_t bytes, int64_t device) {
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  void* p = nullptr;
+  cudaIpcMemHandle_t h;
+  check(mdl::ipc_alloc(static_cast<size_t>(bytes), &p, &h), "ipc_alloc");
+  return py::make_tuple(reinterpret_cast<int64_t>(p), py::bytes(reinterpret_cast<const char*>(&h), sizeof(h)));
+}
+
+int64_t ipc_open(const py::bytes& handle, int64_t device) {
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  std::string s = handle;
+  TORCH_CHECK(s.size() == sizeof(cudaIpcMemHandle_t), "bad IPC handle size");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, s.data(), sizeof(h));
+  void* p = nullptr;
+  check(mdl::ipc_open(h, &p), "ipc_open");
+  return reinterpret_cast<int64_t>(p);
+}
+
+void ipc_close(int64_t ptr_, int64_t device) {
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  check(mdl::ipc_close(reinterpret_cast<void*>(ptr_)), "ipc_close");
+}
+
+void ipc_free(int64_t ptr_, int64_t device) {
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  check(mdl::ipc_free(reinterpret_cast<void*>(ptr_)), "ipc_free");
+}
+
+at::Tensor tensor_from_ptr(int64_t ptr_, int64_t numel, at::ScalarType dtype, int64_t device) {
+  auto opts = at::TensorOptions().dtype(dtype).device(at::Device(at::kCUDA, static_cast<c10::DeviceIndex>(device)));
+  return torch::from_blob(reinterpret_cast<void*>(ptr_), {numel}, opts);
+}
+
+void set_barrier_limit(double seconds) { mdl::set_barrier_limit_ns(static_cast<uint64_t>(seconds * 1e9)); }
+
+void barrier(const std::vector<int64_t>& signals, const at::Tensor& counter, int64_t rank,
+             const std::optional<at::Tensor>& err) {
+  c10::cuda::CUDAGuard guard(counter.device());
+  unsigned* s[mdl::kMaxWorld] = {};
+  for (size_t r = 0; r < signals.size() && r < mdl::kMaxWorld; ++r) s[r] = reinterpret_cast<unsigned*>(signals[r]);
+  check(mdl::symm_barrier(s, ptr<unsigned>(counter), static_cast<int>(rank), static_cast<int>(signals.size()),
+                          optr<int>(err), stream_of(counter)),
+        "symm_barrier");
+  g_launches += 1;
+}
+
+void dense_sync(const std::vector<int64_t>& grads, const std::vector<int64_t>& params,
+                const std::vector<int64_t>& shadows, const at::Tensor& state1, const std::optional<at::Tensor>& state2,
+                int64_t begin, int64_t end, int64_t fp32_from, int64_t rank, int64_t optimizer, double lr,
+                double beta1, double beta2, double eps, double wd, double bc1, double bc2, double alpha,
+                double grad_scale, const std::optional<at::Tensor>& clip, const std::optional<at::Tensor>& sqnorm_out,
+                int64_t phase) {
+  c10::cuda::CUDAGuard guard(state1.device());
+  mdl::DenseSyncArgs a;
+  a.world = static_cast<int>(grads.size());
+  TORCH_CHECK(a.world >= 1 && a.world <= mdl::kMaxWorld, "world out of range");
+  for (int r = 0; r < a.world; ++r) {
+    a.grads[r] = reinterpret_cast<float*>(grads[r]);
+    a.params[r] = reinterpret_cast<float*>(params[r]);
+    a.shadows[r] = r < static_cast<int>(shadows.size()) ? reinterpret_cast<void*>(shadows[r]) : nullptr;
+  }
+  a.state1 = ptr<float>(state1);
+  a.state2 = optr<float>(state2);
+  a.begin = begin;
+  a.end = end;
+  a.fp32_from = fp32_from;
+  a.rank = static_cast<int>(rank);
+  a.optimizer = static_cast<int>(optimizer);
+  a.lr = static_cast<float>(lr);
+  a.beta1 = static_cast<float>(beta1);
+  a.beta2 = static_cast<float>(beta2);
+  a.eps = static_cast<float>(eps);
+  a.weight_decay = static_cast<float>(wd);
+  a.bias_correction1 = static_cast<float>(bc1);
+  a.bias_correction2 = static_cast<float>(bc2);
+  a.alpha = static_cast<float>(alpha);
+  a.grad_scale = static_cast<float>(grad_scale);
+  a.clip = optr<const float>(clip);
+  a.sqnorm_out = optr<float>(sqnorm_out);
+  a.phase = static_cast<int>(phase);
+  check(mdl::dense_sync_update(a, stream_of(state1)), "dense_sync_update");
+  g_launches += 1;
+}
+
+void small_allreduce(const std::vector<int64_t>& bufs, const at::Tensor& out, int64_t n) {
+  c10::cuda::CUDAGuard guard(out.device());
+  float* b[mdl::kMaxWorld] = {};
+  for (size_t r = 0; r < bufs.size() && r < mdl::kMaxWorld; ++r) b[r] = reinterpret_cast<float*>(bufs[r]);
+  check(mdl::small_allreduce(b, ptr<float>(out), static_cast<int>(n), static_cast<int>(bufs.size()), stream_of(out)),
+        "small_allreduce");
+  g_launches += 1;
 }
 
 }  // namespace
@@ -94,4 +516,32 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("gs_aux") = 0, py::arg("colsum") = py::none(), py::arg("gs_colsum") = 0, py::arg("act") = 0,
         py::arg("alpha") = 1.0, py::arg("accumulate") = false, py::arg("err") = py::none(),
         py::arg("max_ctas") = 0);
+
+  m.def("emb_forward", &emb_forward);
+  m.def("emb_backward", &emb_backward);
+  m.def("adagrad_apply", &adagrad_apply);
+  m.def("touched_sqnorm", &touched_sqnorm);
+  m.def("ln_fwd", &ln_fwd);
+  m.def("ln_bwd_grid", &ln_bwd_grid);
+  m.def("ln_bwd", &ln_bwd);
+  m.def("rms_fwd", &rms_fwd);
+  m.def("rms_bwd", &rms_bwd);
+  m.def("token_mean", &token_mean);
+  m.def("colsum", &colsum);
+  m.def("head_bce", &head_bce);
+  m.def("adam", &adam);
+  m.def("rmsprop", &rmsprop);
+  m.def("sqnorm", &sqnorm);
+  m.def("clip_factor", &clip_factor);
+  m.def("cast_bf16", &cast_bf16);
+  m.def("ipc_alloc", &ipc_alloc);
+  m.def("ipc_open", &ipc_open);
+  m.def("ipc_close", &ipc_close);
+  m.def("ipc_free", &ipc_free);
+  m.def("tensor_from_ptr", &tensor_from_ptr);
+  m.def("set_barrier_limit", &set_barrier_limit);
+  m.def("barrier", &barrier);
+  m.def("dense_sync", &dense_sync);
+  m.def("small_allreduce", &small_allreduce);
+  m.def("launch_count", &launch_count);
 }

@@ -1,0 +1,383 @@
+// Fused embedding-bag lookup / gradient push / row-wise Adagrad for sm_100a.
+//
+// Replaces the reference's owner-routed lookup (src/embeddings.py:476-674,
+// 1112-1517: unique -> argsort -> all_to_all of split counts with a host read
+// -> all_to_all of ids -> gather -> all_to_all of rows -> index_copy), its
+// mean pooling of bags (src/model.py:509-678) and its Triton row-wise Adagrad
+// (src/optim.py:31-62).
+//
+// Every rank's table shards live in one fp32 slab. Peer slabs are mapped into
+// this process (CUDA IPC over NVLink), so a lookup is ONE kernel: each warp
+// hashes its ids, computes owner = (id + cyclic_offset) % W and
+// row = id / W (the reference's EmbeddingShardSpec.owner/local_row_ids, kept
+// bit-compatible for checkpoints), loads the rows straight from the owner's
+// slab with plain global loads (local HBM or NVLink peer memory), pools them
+// in registers and stores bf16 into the tokenizer GEMM's input layout. There
+// is no id exchange, no split-count host sync and no unpooled row traffic back
+// to the requester.
+//
+// The backward pushes each id's gradient into the owner's fp32 grad slab with
+// vector reductions (red.add.v4.f32, system scope when peers are involved) and
+// records each newly touched row once in the owner's fixed-capacity touched
+// list (overflow is reported through the error word). After a device-side
+// barrier the owner applies row-wise Adagrad to exactly those rows.
+#include "common.cuh"
+#include "embedding.h"
+
+namespace mdl {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kMaxVec = 8;  // float4 vectors per lane -> width <= 32 * lanes... see f_lanes
+
+__device__ __forceinline__ long long find_feature(const long long* prefix, int nf, long long w) {
+  int lo = 0, hi = nf;  // find f with prefix[f] <= w < prefix[f+1]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (__ldg(prefix + mid) <= w) lo = mid; else hi = mid;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ long long hash_id(long long v, int mode, long long buckets) {
+  if (mode == 1) {
+    if (v == 0) return 0;  // null -> padding
+    return static_cast<long long>(static_cast<unsigned long long>(v) & static_cast<unsigned long long>(buckets - 1)) + 1;
+  }
+  return v;
+}
+
+__device__ __forceinline__ long long phys_col(int c, int slice, int stride) {
+  return slice > 0 ? static_cast<long long>(c / slice) * stride + (c % slice) : c;
+}
+
+__device__ __forceinline__ void store4_bf16(__nv_bfloat16* out, long long row_off, int c, int slice, int stride,
+                                            int valid, const float* v) {
+  const long long p0 = phys_col(c, slice, stride);
+  const bool contiguous = slice <= 0 || (c / slice) == ((c + 3) / slice);
+  if (valid == 4 && contiguous && ((row_off + p0) & 3) == 0) {
+    __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]);
+    __nv_bfloat162 b = __floats2bfloat162_rn(v[2], v[3]);
+    uint2 u;
+    u.x = *reinterpret_cast<uint32_t*>(&a);
+    u.y = *reinterpret_cast<uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(out + row_off + p0) = u;
+  } else {
+    for (int j = 0; j < valid; ++j) out[row_off + phys_col(c + j, slice, stride)] = __float2bfloat16_rn(v[j]);
+  }
+}
+
+__device__ __forceinline__ void load4_bf16(const __nv_bfloat16* g, long long row_off, int c, int slice, int stride,
+                                           int valid, float* v) {
+  const long long p0 = phys_col(c, slice, stride);
+  const bool contiguous = slice <= 0 || (c / slice) == ((c + 3) / slice);
+  if (valid == 4 && contiguous && ((row_off + p0) & 3) == 0) {
+    const uint2 u = *reinterpret_cast<const uint2*>(g + row_off + p0);
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+    v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+  } else {
+    for (int j = 0; j < 4; ++j) v[j] = j < valid ? __bfloat162float(g[row_off + phys_col(c + j, slice, stride)]) : 0.f;
+  }
+}
+
+template <bool SYS>
+__device__ __forceinline__ void red_add4(float* dst, const float* v) {
+  if (SYS) {
+    asm volatile("red.relaxed.sys.global.add.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(dst), "f"(v[0]), "f"(v[1]),
+                 "f"(v[2]), "f"(v[3])
+                 : "memory");
+  } else {
+    asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(dst), "f"(v[0]), "f"(v[1]),
+                 "f"(v[2]), "f"(v[3])
+                 : "memory");
+  }
+}
+
+struct BagCtx {
+  int f, lanes, sl;
+  long long bag_local, gbag;
+  bool active;
+};
+
+__device__ __forceinline__ BagCtx bag_of_lane(const EmbPlan& p) {
+  BagCtx b;
+  const long long warp = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  b.f = static_cast<int>(find_feature(p.f_chunk_prefix, p.num_features, warp));
+  b.lanes = __ldg(p.f_lanes + b.f);
+  const int bags_per_warp = 32 / b.lanes;
+  const long long chunk = warp - __ldg(p.f_chunk_prefix + b.f);
+  const int sub = lane / b.lanes;
+  b.sl = lane % b.lanes;
+  b.bag_local = chunk * bags_per_warp + sub;
+  const long long n_bags = __ldg(p.f_bag_prefix + b.f + 1) - __ldg(p.f_bag_prefix + b.f);
+  b.active = b.bag_local < n_bags;
+  b.gbag = __ldg(p.f_bag_prefix + b.f) + b.bag_local;
+  return b;
+}
+
+__device__ __forceinline__ void route(const EmbPlan& p, int t, long long id, int& owner, long long& row) {
+  if (__ldg(p.t_mode + t) == 0) {
+    owner = static_cast<int>((id + __ldg(p.t_cyc + t)) % p.world);
+    row = id / p.world;
+  } else {
+    owner = __ldg(p.t_owner + t);
+    row = id;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) emb_pool_fwd_kernel(const EmbPlan p, long long total_chunks) {
+  const long long warp = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+  if (warp >= total_chunks) return;
+  const BagCtx b = bag_of_lane(p);
+  if (!b.active) return;
+  const int f = b.f;
+  const int width = __ldg(p.f_width + f);
+  const int t = __ldg(p.f_table + f);
+  const int pool = __ldg(p.f_pool + f);
+  float acc[kMaxVec][4];
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  const int stride_cols = 4 * b.lanes;
+  int count = 0;
+  if (t < 0) {
+    const float* src = p.dense + b.bag_local * p.dense_ld + __ldg(p.f_dense_col + f);
+#pragma unroll
+    for (int i = 0; i < kMaxVec; ++i) {
+      const int col = b.sl * 4 + i * stride_cols;
+      if (col < width)
+        for (int j = 0; j < 4; ++j) acc[i][j] = (col + j < width) ? __ldg(src + col + j) : 0.f;
+    }
+    count = 1;
+  } else {
+    const int hmode = __ldg(p.f_hash + f);
+    const long long buckets = __ldg(p.f_buckets + f);
+    const long long rows = __ldg(p.t_rows + t);
+    const long long tbase = __ldg(p.t_base + t);
+    const int dim = __ldg(p.t_dim + t);
+    const long long beg = __ldg(p.id_offsets + b.gbag);
+    const long long end = __ldg(p.id_offsets + b.gbag + 1);
+    for (long long q = beg; q < end; ++q) {
+      const long long id = hash_id(__ldg(p.ids + q), hmode, buckets);
+      if (id <= 0) continue;  // padding id 0 contributes nothing (null policy "exclude")
+      if (id >= rows) {
+        record_error(p.err, MDL_ERR_BAD_INDEX);
+        continue;
+      }
+      int owner;
+      long long row;
+      route(p, t, id, owner, row);
+      const float* src = p.slabs[owner] + tbase + row * dim;
+#pragma unroll
+      for (int i = 0; i < kMaxVec; ++i) {
+        const int col = b.sl * 4 + i * stride_cols;
+        if (col < dim) {
+          const float4 v = *reinterpret_cast<const float4*>(src + col);
+          acc[i][0] += v.x; acc[i][1] += v.y; acc[i][2] += v.z; acc[i][3] += v.w;
+        }
+      }
+      ++count;
+      if (pool == 0) break;  // single-valued feature: first non-null id only
+    }
+    if (pool == 1 && count > 0) {
+      const float inv = 1.f / static_cast<float>(count);
+#pragma unroll
+      for (int i = 0; i < kMaxVec; ++i)
+        for (int j = 0; j < 4; ++j) acc[i][j] *= inv;
+    }
+  }
+  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out) + __ldg(p.f_out_base + f);
+  const long long row_off = b.bag_local * __ldg(p.f_out_ld + f);
+  const int c0 = __ldg(p.f_out_col + f);
+  const int slice = __ldg(p.f_slice + f), sstride = __ldg(p.f_slice_stride + f);
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int col = b.sl * 4 + i * stride_cols;
+    if (col < width) store4_bf16(out, row_off, c0 + col, slice, sstride, min(4, width - col), acc[i]);
+  }
+}
+
+template <bool SYS>
+__global__ void __launch_bounds__(kThreads)
+    emb_pool_bwd_kernel(const EmbPlan p, const __nv_bfloat16* __restrict__ grad_out, long long total_chunks) {
+  const long long warp = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+  if (warp >= total_chunks) return;
+  const BagCtx b = bag_of_lane(p);
+  if (!b.active) return;
+  const int f = b.f;
+  const int t = __ldg(p.f_table + f);
+  if (t < 0) return;  // dense inputs have no trainable table
+  const int pool = __ldg(p.f_pool + f);
+  const int hmode = __ldg(p.f_hash + f);
+  const long long buckets = __ldg(p.f_buckets + f);
+  const long long rows = __ldg(p.t_rows + t);
+  const long long tbase = __ldg(p.t_base + t);
+  const long long rbase = __ldg(p.t_row_base + t);
+  const int dim = __ldg(p.t_dim + t);
+  const long long beg = __ldg(p.id_offsets + b.gbag);
+  const long long end = __ldg(p.id_offsets + b.gbag + 1);
+  float scale = 1.f;
+  if (pool == 1) {
+    int count = 0;
+    for (long long q = beg; q < end; ++q) {
+      const long long id = hash_id(__ldg(p.ids + q), hmode, buckets);
+      if (id > 0 && id < rows) ++count;
+    }
+    if (count == 0) return;
+    scale = 1.f / static_cast<float>(count);
+  }
+  const int stride_cols = 4 * b.lanes;
+  float g[kMaxVec][4];
+  const long long row_off = b.bag_local * __ldg(p.f_out_ld + f);
+  const int c0 = __ldg(p.f_out_col + f);
+  const int slice = __ldg(p.f_slice + f), sstride = __ldg(p.f_slice_stride + f);
+  const __nv_bfloat16* gbase = grad_out + __ldg(p.f_out_base + f);
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int col = b.sl * 4 + i * stride_cols;
+    if (col < dim) {
+      load4_bf16(gbase, row_off, c0 + col, slice, sstride, min(4, dim - col), g[i]);
+      for (int j = 0; j < 4; ++j) g[i][j] *= scale;
+    }
+  }
+  for (long long q = beg; q < end; ++q) {
+    const long long id = hash_id(__ldg(p.ids + q), hmode, buckets);
+    if (id <= 0 || id >= rows) continue;
+    int owner;
+    long long row;
+    route(p, t, id, owner, row);
+    float* dst = p.grad_slabs[owner] + tbase + row * dim;
+#pragma unroll
+    for (int i = 0; i < kMaxVec; ++i) {
+      const int col = b.sl * 4 + i * stride_cols;
+      if (col < dim) red_add4<SYS>(dst + col, g[i]);
+    }
+    if (b.sl == 0) {
+      const long long rs = rbase + row;
+      unsigned prev;
+      if (SYS) prev = atomicExch_system(p.flags[owner] + rs, 1u);
+      else prev = atomicExch(p.flags[owner] + rs, 1u);
+      if (prev == 0u) {
+        const int idx = SYS ? atomicAdd_system(p.touched_count[owner], 1) : atomicAdd(p.touched_count[owner], 1);
+        if (idx < p.touched_cap) p.touched[owner][idx] = (static_cast<long long>(t) << 40) | row;
+        else record_error(p.err, MDL_ERR_CAPACITY);
+      }
+    }
+    if (pool == 0) break;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) rowwise_adagrad_kernel(const AdagradArgs a) {
+  const int lane = threadIdx.x & 31;
+  const long long warps = static_cast<long long>(gridDim.x) * (kThreads / 32);
+  const long long n = min(static_cast<long long>(*a.touched_count), a.cap);
+  const float clip = a.clip_scale != nullptr ? *a.clip_scale : 1.f;
+  const float gscale = a.grad_scale * clip;
+  for (long long e = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5; e < n; e += warps) {
+    const long long packed = a.touched[e];
+    const int t = static_cast<int>(packed >> 40);
+    const long long row = packed & ((1ll << 40) - 1);
+    const int dim = __ldg(a.t_dim + t);
+    const long long base = __ldg(a.t_base + t) + row * dim;
+    const long long rs = __ldg(a.t_row_base + t) + row;
+    float g[kMaxVec][4];
+    float sq = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxVec; ++i) {
+      const int col = lane * 4 + i * 128;
+      if (col < dim) {
+        const float4 v = *reinterpret_cast<const float4*>(a.grad_slab + base + col);
+        g[i][0] = v.x * gscale; g[i][1] = v.y * gscale; g[i][2] = v.z * gscale; g[i][3] = v.w * gscale;
+        sq += g[i][0] * g[i][0] + g[i][1] * g[i][1] + g[i][2] * g[i][2] + g[i][3] * g[i][3];
+      }
+    }
+    sq = warp_sum(sq);
+    float acc = 0.f;
+    if (lane == 0) {
+      acc = a.acc[rs] + sq / static_cast<float>(dim);
+      a.acc[rs] = acc;
+      a.flags[rs] = 0u;
+    }
+    acc = __shfl_sync(0xffffffffu, acc, 0);
+    const float step = a.lr / (sqrtf(acc) + a.eps);
+#pragma unroll
+    for (int i = 0; i < kMaxVec; ++i) {
+      const int col = lane * 4 + i * 128;
+      if (col < dim) {
+        float4* w = reinterpret_cast<float4*>(a.slab + base + col);
+        float4 v = *w;
+        v.x -= step * g[i][0]; v.y -= step * g[i][1]; v.z -= step * g[i][2]; v.w -= step * g[i][3];
+        *w = v;
+        *reinterpret_cast<float4*>(a.grad_slab + base + col) = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) touched_sqnorm_kernel(const AdagradArgs a, float* out_sq) {
+  const int lane = threadIdx.x & 31;
+  const long long warps = static_cast<long long>(gridDim.x) * (kThreads / 32);
+  const long long n = min(static_cast<long long>(*a.touched_count), a.cap);
+  float sq = 0.f;
+  for (long long e = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5; e < n; e += warps) {
+    const long long packed = a.touched[e];
+    const int t = static_cast<int>(packed >> 40);
+    const long long row = packed & ((1ll << 40) - 1);
+    const int dim = __ldg(a.t_dim + t);
+    const long long base = __ldg(a.t_base + t) + row * dim;
+    for (int col = lane * 4; col < dim; col += 128) {
+      const float4 v = *reinterpret_cast<const float4*>(a.grad_slab + base + col);
+      sq += (v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w) * a.grad_scale * a.grad_scale;
+    }
+  }
+  sq = warp_sum(sq);
+  if (lane == 0) atomicAdd(out_sq, sq);
+}
+
+int blocks_for(long long warps) { return static_cast<int>((warps * 32 + kThreads - 1) / kThreads); }
+
+}  // namespace
+
+cudaError_t emb_pool_forward(const EmbPlan& plan, long long total_chunks, cudaStream_t stream) {
+  if (total_chunks <= 0) return cudaSuccess;
+  emb_pool_fwd_kernel<<<blocks_for(total_chunks), kThreads, 0, stream>>>(plan, total_chunks);
+  return cudaGetLastError();
+}
+
+cudaError_t emb_pool_backward(const EmbPlan& plan, const void* grad_out, long long total_chunks,
+                              cudaStream_t stream) {
+  if (total_chunks <= 0) return cudaSuccess;
+  const auto* g = reinterpret_cast<const __nv_bfloat16*>(grad_out);
+  if (plan.world > 1)
+    emb_pool_bwd_kernel<true><<<blocks_for(total_chunks), kThreads, 0, stream>>>(plan, g, total_chunks);
+  else
+    emb_pool_bwd_kernel<false><<<blocks_for(total_chunks), kThreads, 0, stream>>>(plan, g, total_chunks);
+  return cudaGetLastError();
+}
+
+cudaError_t rowwise_adagrad_apply(const AdagradArgs& a, cudaStream_t stream) {
+  if (a.cap <= 0) return cudaSuccess;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long want = blocks_for(a.cap);
+  const int grid = static_cast<int>(want < sms * 8 ? want : sms * 8);
+  rowwise_adagrad_kernel<<<grid, kThreads, 0, stream>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  return cudaMemsetAsync(a.touched_count, 0, sizeof(int), stream);
+}
+
+cudaError_t touched_grad_sqnorm(const AdagradArgs& a, float* out_sq, cudaStream_t stream) {
+  if (a.cap <= 0) return cudaSuccess;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long want = blocks_for(a.cap);
+  const int grid = static_cast<int>(want < sms * 8 ? want : sms * 8);
+  touched_sqnorm_kernel<<<grid, kThreads, 0, stream>>>(a, out_sq);
+  return cudaGetLastError();
+}
+
+}  // namespace mdl

@@ -1,0 +1,92 @@
+// Host interface of the fused embedding-bag kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mdl {
+
+constexpr int kMaxWorld = 8;
+
+// Everything a lookup/update launch needs. Arrays are device pointers.
+// "Slab": one fp32 buffer per rank holding the local shard of every table;
+// table t occupies elements [t_base[t], t_base[t] + local_rows_t * dim_t).
+// The "row space" numbers the local rows of all tables: row r of table t has
+// row-space index t_row_base[t] + r (used by the Adagrad accumulator and the
+// touched-row flags).
+struct EmbPlan {
+  int num_features = 0;
+  int world = 1;
+  int rank = 0;
+  // work list: feature f owns warp-chunks [f_chunk_prefix[f], f_chunk_prefix[f+1])
+  const long long* f_chunk_prefix = nullptr;  // [F+1]
+  const long long* f_bag_prefix = nullptr;    // [F+1] first global bag of feature f
+  const long long* id_offsets = nullptr;      // [total_bags+1] CSR offsets into ids
+  const long long* ids = nullptr;             // raw ids (int64)
+  // per feature
+  const int* f_table = nullptr;        // table index, -1 for a dense feature
+  const int* f_pool = nullptr;         // 0 none (first id), 1 mean, 2 sum
+  const int* f_hash = nullptr;         // 0 ids used as-is, 1 pre_hashed low bits (+1)
+  const long long* f_buckets = nullptr;// pre_hashed bucket count (power of two)
+  const int* f_width = nullptr;        // output width (embedding dim or dense width)
+  const int* f_lanes = nullptr;        // lanes per bag (power of two, width <= 4*lanes*iters)
+  const long long* f_out_base = nullptr;  // element offset of the feature's output matrix
+  const long long* f_out_ld = nullptr;    // row stride of that matrix (elements)
+  const int* f_out_col = nullptr;      // first logical column of the feature
+  const int* f_slice = nullptr;        // per-feature column map: phys = (c/slice)*stride + c%slice (0 = identity)
+  const int* f_slice_stride = nullptr;
+  const int* f_dense_col = nullptr;    // dense features: first column in `dense`
+  // per table
+  const long long* t_base = nullptr;
+  const long long* t_row_base = nullptr;
+  const int* t_dim = nullptr;
+  const int* t_mode = nullptr;         // 0 row-wise cyclic, 1 table-wise
+  const int* t_cyc = nullptr;          // row-wise cyclic offset
+  const int* t_owner = nullptr;        // table-wise owner rank
+  const long long* t_rows = nullptr;   // global row count (bounds check)
+  // peer-visible buffers, one pointer per rank (index = rank)
+  float* slabs[kMaxWorld] = {};
+  float* grad_slabs[kMaxWorld] = {};
+  unsigned* flags[kMaxWorld] = {};
+  long long* touched[kMaxWorld] = {};
+  int* touched_count[kMaxWorld] = {};
+  long long touched_cap = 0;
+  // dense inputs (fp32 [rows, dense_ld]) and the pooled output (bf16)
+  const float* dense = nullptr;
+  long long dense_ld = 0;
+  void* out = nullptr;   // bf16
+  int* err = nullptr;
+};
+
+// Forward: pool every bag of every feature into `out` (bf16).
+cudaError_t emb_pool_forward(const EmbPlan& plan, long long total_chunks, cudaStream_t stream);
+
+// Backward: push d(out) of every id to its owner's grad slab and mark the
+// touched rows. `grad_out` has the same layout as `out`.
+cudaError_t emb_pool_backward(const EmbPlan& plan, const void* grad_out, long long total_chunks,
+                              cudaStream_t stream);
+
+// Row-wise Adagrad over this rank's touched rows (reference optim.py:31-62):
+//   g = grad * grad_scale * clip_scale[0]; acc += mean(g^2); w -= lr * g / (sqrt(acc) + eps)
+// then zero the grad rows, clear the flags and reset the touched count.
+struct AdagradArgs {
+  float* slab;
+  float* grad_slab;
+  float* acc;            // fp32 [row space]
+  unsigned* flags;
+  const long long* touched;
+  int* touched_count;
+  const long long* t_base;
+  const long long* t_row_base;
+  const int* t_dim;
+  float lr, eps, grad_scale;
+  const float* clip_scale;  // optional device scalar (nullptr = 1)
+  long long cap;
+  int* err;
+};
+cudaError_t rowwise_adagrad_apply(const AdagradArgs& a, cudaStream_t stream);
+
+// Sum of squared (scaled) gradients over the touched rows (for global sparse clipping).
+cudaError_t touched_grad_sqnorm(const AdagradArgs& a, float* out_sq, cudaStream_t stream);
+
+}  // namespace mdl

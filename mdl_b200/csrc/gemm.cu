@@ -308,6 +308,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             __nv_bfloat16* op2 = ep.out2 != nullptr ? ep.out2 + off : nullptr;
             if (full_chunk) {
               uint4* o4 = reinterpret_cast<uint4*>(op);
+              if (ep.accumulate) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  float old[8];
+                  unpack_bf16x8(o4[q], old);
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) v[8 * q + e] += old[e];
+                }
+              }
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
                 uint4 t;
@@ -332,6 +341,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             } else {
               for (int i = 0; i < 32; ++i) {
                 if (col0 + i < ep.N) {
+                  if (ep.accumulate) v[i] += __bfloat162float(op[i]);
                   op[i] = __float2bfloat16_rn(v[i]);
                   if (ep.act == GEMM_ACT_GELU) op2[i] = __float2bfloat16_rn(gelu_erf(v[i]));
                 }
@@ -424,7 +434,6 @@ cudaError_t gemm_bf16_tcgen05(const GemmArgs& a, cudaStream_t stream) {
   if ((a.lda % 8) || (a.ldb % 8) || (a.G > 1 && ((a.gsA % 8) || (a.gsB % 8))) ||
       (reinterpret_cast<uintptr_t>(a.A) & 15) || (reinterpret_cast<uintptr_t>(a.B) & 15))
     return cudaErrorInvalidValue;
-  if (a.K % 8) return cudaErrorInvalidValue;
   if (!a.out_fp32 && (a.ldc % 8)) return cudaErrorInvalidValue;
   if (a.out_fp32 && (a.ldc % 4)) return cudaErrorInvalidValue;
   CUtensorMap ta, tb;

@@ -36,7 +36,7 @@ struct GemmArgs {
   void* out = nullptr;
   long long ldc = 0, gsC = 0;
   bool out_fp32 = false;
-  bool accumulate = false;          // fp32 out only: out += result
+  bool accumulate = false;          // out += result (fp32 or bf16 out)
   void* out2 = nullptr;             // bf16, same layout as out (GELU output)
   const float* bias = nullptr;      // bias[g*gs_bias + n]
   long long gs_bias = 0;

@@ -1,4 +1,8 @@
 // Umbrella header: host entry points of every mdl_b200 kernel family.
 #pragma once
 
+#include "comm.h"
+#include "embedding.h"
 #include "gemm.h"
+#include "misc.h"
+#include "norm.h"

@@ -1,0 +1,433 @@
+// Fused normalisation kernels for sm_100a.
+//
+// RankMixer blocks compute LN(mix(x) + x) and LN(ffn + mixed)
+// (reference src/model.py:6663-6665, token mixing src/modules/attention.py:354-363
+// as permute(0,2,1,3).contiguous()). Here the token-mixing permutation is an
+// index remap inside the LayerNorm kernel: no permuted copy is materialised.
+// The backward recomputes the normalised row from the inputs and the saved
+// (mean, rstd), so only those two floats per row are kept from the forward.
+// gamma/beta and the per-token bias gradient of the producing layer are
+// accumulated per CTA in registers and folded by a second small kernel.
+#include "common.cuh"
+#include "norm.h"
+
+namespace mdl {
+namespace {
+
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float* v) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float* v) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+// Pre-norm value of row (b, i): mix(a)+a or a+b, 8 elements at column c.
+template <bool MIX>
+__device__ __forceinline__ void load_v(const __nv_bfloat16* a, const __nv_bfloat16* bsrc, long long b, int i,
+                                       int T, int D, int c, float* v) {
+  const long long row = (b * T + i) * static_cast<long long>(D);
+  load8(a + row + c, v);
+  float u[8];
+  if (MIX) {
+    const int dh = D / T;
+    const int j = c / dh;
+    const int w = c - j * dh;
+    load8(a + (b * T + j) * static_cast<long long>(D) + i * dh + w, u);
+  } else if (bsrc != nullptr) {
+    load8(bsrc + row + c, u);
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) u[k] = 0.f;
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) v[k] += u[k];
+}
+
+template <int NCH, bool MIX>
+__global__ void __launch_bounds__(256) ln_fwd_kernel(const LNFwdArgs p) {
+  const long long r = (static_cast<long long>(blockIdx.x) * 256 + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (r >= static_cast<long long>(p.B) * p.T) return;
+  const long long b = r / p.T;
+  const int i = static_cast<int>(r - b * p.T);
+  const auto* a = reinterpret_cast<const __nv_bfloat16*>(p.a);
+  const auto* bb = reinterpret_cast<const __nv_bfloat16*>(p.b);
+  float v[NCH][8];
+  float s = 0.f;
+#pragma unroll
+  for (int k = 0; k < NCH; ++k) {
+    const int c = (lane + 32 * k) * 8;
+    if (c < p.D) {
+      load_v<MIX>(a, bb, b, i, p.T, p.D, c, v[k]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s += v[k][e];
+    }
+  }
+  const float mean = warp_sum(s) / p.D;
+  float q = 0.f;
+#pragma unroll
+  for (int k = 0; k < NCH; ++k) {
+    const int c = (lane + 32 * k) * 8;
+    if (c < p.D) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float d = v[k][e] - mean;
+        q += d * d;
+      }
+    }
+  }
+  const float rstd = rsqrtf(warp_sum(q) / p.D + p.eps);
+  auto* out = reinterpret_cast<__nv_bfloat16*>(p.out) + r * p.D;
+#pragma unroll
+  for (int k = 0; k < NCH; ++k) {
+    const int c = (lane + 32 * k) * 8;
+    if (c < p.D) {
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float g = p.gamma ? __ldg(p.gamma + c + e) : 1.f;
+        const float bt = p.beta ? __ldg(p.beta + c + e) : 0.f;
+        o[e] = (v[k][e] - mean) * rstd * g + bt;
+      }
+      store8(out + c, o);
+    }
+  }
+  if (lane == 0) {
+    if (p.mean) p.mean[r] = mean;
+    if (p.rstd) p.rstd[r] = rstd;
+  }
+}
+
+// CTAs of 8 warps. Non-mix: warps walk rows in a grid-stride loop. Mix: a CTA
+// walks whole samples (all T rows of sample b are needed to undo the token
+// permutation); the dv rows of the current sample are staged in shared memory.
+// gamma/beta gradients are accumulated per warp in registers and written as one
+// partial row per CTA.
+template <int NCH, bool MIX>
+__global__ void __launch_bounds__(256) ln_bwd_kernel(const LNBwdArgs p) {
+  extern __shared__ float sm[];  // [max(T, 8)][D] fp32
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int T = p.T, D = p.D;
+  const auto* a = reinterpret_cast<const __nv_bfloat16*>(p.a);
+  const auto* bb = reinterpret_cast<const __nv_bfloat16*>(p.b);
+  const auto* dy = reinterpret_cast<const __nv_bfloat16*>(p.dy);
+  const auto* dyb = reinterpret_cast<const __nv_bfloat16*>(p.dy_bcast);
+  auto* dx = reinterpret_cast<__nv_bfloat16*>(p.dx);
+  auto* dx2 = reinterpret_cast<__nv_bfloat16*>(p.dx2);
+  float dg[NCH][8], db[NCH][8];
+#pragma unroll
+  for (int k = 0; k < NCH; ++k)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) dg[k][e] = db[k][e] = 0.f;
+
+  // dv of row (b, i); returns via `dv` (registers); accumulates dg/db
+  auto row_dv = [&](long long b, int i, float (*dv)[8]) {
+    const long long r = b * T + i;
+    const float mean = p.mean[r];
+    const float rstd = p.rstd[r];
+    float xh[NCH][8], gy[NCH][8], g[NCH][8];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int k = 0; k < NCH; ++k) {
+      const int c = (lane + 32 * k) * 8;
+      if (c < D) {
+        load_v<MIX>(a, bb, b, i, T, D, c, xh[k]);
+        if (dy != nullptr) {
+          load8(dy + r * D + c, g[k]);
+        } else {
+          load8(dyb + b * D + c, g[k]);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) g[k][e] *= p.bcast_scale;
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          xh[k][e] = (xh[k][e] - mean) * rstd;
+          const float gm = p.gamma ? __ldg(p.gamma + c + e) : 1.f;
+          gy[k][e] = g[k][e] * gm;
+          s1 += gy[k][e];
+          s2 += gy[k][e] * xh[k][e];
+        }
+      }
+    }
+    s1 = warp_sum(s1) / D;
+    s2 = warp_sum(s2) / D;
+#pragma unroll
+    for (int k = 0; k < NCH; ++k) {
+      const int c = (lane + 32 * k) * 8;
+      if (c < D) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          dv[k][e] = rstd * (gy[k][e] - s1 - xh[k][e] * s2);
+          dg[k][e] += g[k][e] * xh[k][e];
+          db[k][e] += g[k][e];
+        }
+      }
+    }
+  };
+
+  if (MIX) {
+    const int dh = D / T;
+    for (long long b = blockIdx.x; b < p.B; b += gridDim.x) {
+      for (int i = warp; i < T; i += 8) {
+        float dv[NCH][8];
+        row_dv(b, i, dv);
+#pragma unroll
+        for (int k = 0; k < NCH; ++k) {
+          const int c = (lane + 32 * k) * 8;
+          if (c < D)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) sm[i * D + c + e] = dv[k][e];
+        }
+      }
+      __syncthreads();
+      for (int i = warp; i < T; i += 8) {
+        const long long r = b * T + i;
+#pragma unroll
+        for (int k = 0; k < NCH; ++k) {
+          const int c = (lane + 32 * k) * 8;
+          if (c < D) {
+            const int j = c / dh;
+            const int w = c - j * dh;
+            float o[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o[e] = sm[i * D + c + e] + sm[j * D + i * dh + w + e];
+            store8(dx + r * D + c, o);
+            if (dx2 != nullptr) store8(dx2 + r * D + c, o);
+          }
+        }
+      }
+      __syncthreads();
+    }
+  } else {
+    const long long rows = static_cast<long long>(p.B) * T;
+    for (long long r = static_cast<long long>(blockIdx.x) * 8 + warp; r < rows; r += static_cast<long long>(gridDim.x) * 8) {
+      const long long b = r / T;
+      const int i = static_cast<int>(r - b * T);
+      float dv[NCH][8];
+      row_dv(b, i, dv);
+#pragma unroll
+      for (int k = 0; k < NCH; ++k) {
+        const int c = (lane + 32 * k) * 8;
+        if (c < D) {
+          store8(dx + r * D + c, dv[k]);
+          if (dx2 != nullptr) store8(dx2 + r * D + c, dv[k]);
+        }
+      }
+    }
+  }
+  // ---- fold per-warp gamma/beta partials into this CTA's row of `partials`
+  float* prow = p.partials + static_cast<long long>(blockIdx.x) * 2 * D;
+  for (int pass = 0; pass < 2; ++pass) {
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < NCH; ++k) {
+      const int c = (lane + 32 * k) * 8;
+      if (c < D)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) sm[warp * D + c + e] = pass == 0 ? dg[k][e] : db[k][e];
+    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < D; c += blockDim.x) {
+      float s = 0.f;
+      for (int w = 0; w < 8; ++w) s += sm[w * D + c];
+      prow[pass * D + c] = s;
+    }
+  }
+}
+
+__global__ void ln_partials_reduce_kernel(const float* partials, int grid, int D, float* dgamma, float* dbeta) {
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  if (col >= 2 * D) return;
+  float s = 0.f;
+  for (int g = 0; g < grid; ++g) s += partials[static_cast<long long>(g) * 2 * D + col];
+  if (col < D) {
+    if (dgamma) dgamma[col] += s;
+  } else if (dbeta) {
+    dbeta[col - D] += s;
+  }
+}
+
+// ------------------------------------------------------------------ RMSNorm
+template <int NCH>
+__global__ void __launch_bounds__(256) rms_fwd_kernel(const RMSArgs p) {
+  const long long r = (static_cast<long long>(blockIdx.x) * 256 + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (r >= p.rows) return;
+  const auto* x = reinterpret_cast<const __nv_bfloat16*>(p.x) + r * p.D;
+  float v[NCH][8];
+  float q = 0.f;
+#pragma unroll
+  for (int k = 0; k < NCH; ++k) {
+    const int c = (lane + 32 * k) * 8;
+    if (c < p.D) {
+      load8(x + c, v[k]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) q += v[k][e] * v[k][e];
+    }
+  }
+  const float rstd = rsqrtf(warp_sum(q) / p.D + p.eps);
+  auto* out = reinterpret_cast<__nv_bfloat16*>(p.out) + r * p.D;
+#pragma unroll
+  for (int k = 0; k < NCH; ++k) {
+    const int c = (lane + 32 * k) * 8;
+    if (c < p.D) {
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = v[k][e] * rstd * (p.weight ? __ldg(p.weight + c + e) : 1.f);
+      store8(out + c, o);
+    }
+  }
+  if (lane == 0 && p.rstd) p.rstd[r] = rstd;
+}
+
+template <int NCH>
+__global__ void __launch_bounds__(256) rms_bwd_kernel(const RMSArgs p) {
+  const int lane = threadIdx.x & 31;
+  const long long warps = static_cast<long long>(gridDim.x) * 8;
+  float dw[NCH][8];
+#pragma unroll
+  for (int k = 0; k < NCH; ++k)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) dw[k][e] = 0.f;
+  for (long long r = (static_cast<long long>(blockIdx.x) * 256 + threadIdx.x) >> 5; r < p.rows; r += warps) {
+    const auto* x = reinterpret_cast<const __nv_bfloat16*>(p.x) + r * p.D;
+    const auto* dy = reinterpret_cast<const __nv_bfloat16*>(p.dy) + r * p.D;
+    const float rstd = p.rstd[r];
+    float xv[NCH][8], gv[NCH][8];
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < NCH; ++k) {
+      const int c = (lane + 32 * k) * 8;
+      if (c < p.D) {
+        load8(x + c, xv[k]);
+        load8(dy + c, gv[k]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float w = p.weight ? __ldg(p.weight + c + e) : 1.f;
+          s += gv[k][e] * w * xv[k][e];
+          dw[k][e] += gv[k][e] * xv[k][e] * rstd;
+        }
+      }
+    }
+    s = warp_sum(s) / p.D;
+    auto* dx = reinterpret_cast<__nv_bfloat16*>(p.dx) + r * p.D;
+#pragma unroll
+    for (int k = 0; k < NCH; ++k) {
+      const int c = (lane + 32 * k) * 8;
+      if (c < p.D) {
+        float o[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float w = p.weight ? __ldg(p.weight + c + e) : 1.f;
+          o[e] = rstd * (gv[k][e] * w - xv[k][e] * rstd * rstd * s);
+        }
+        store8(dx + c, o);
+      }
+    }
+  }
+  if (p.dweight) {
+#pragma unroll
+    for (int k = 0; k < NCH; ++k) {
+      const int c = (lane + 32 * k) * 8;
+      if (c < p.D)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) atomicAdd(p.dweight + c + e, dw[k][e]);
+    }
+  }
+}
+
+int sm_count() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+
+}  // namespace
+
+#define MDL_NCH_DISPATCH(D, MACRO) \
+  if ((D) <= 256) { MACRO(1) } else if ((D) <= 512) { MACRO(2) } else if ((D) <= 768) { MACRO(3) } \
+  else if ((D) <= 1024) { MACRO(4) } else if ((D) <= 2048) { MACRO(8) } else { return cudaErrorInvalidValue; }
+
+cudaError_t layernorm_fwd(const LNFwdArgs& a, cudaStream_t stream) {
+  if (a.D % 8 || a.T <= 0) return cudaErrorInvalidValue;
+  if (a.mix && ((a.D % a.T) || ((a.D / a.T) % 8))) return cudaErrorInvalidValue;
+  const long long rows = static_cast<long long>(a.B) * a.T;
+  if (rows == 0) return cudaSuccess;
+  const int grid = static_cast<int>((rows + 7) / 8);
+#define LNF(N)                                                                   \
+  if (a.mix) ln_fwd_kernel<N, true><<<grid, 256, 0, stream>>>(a);               \
+  else ln_fwd_kernel<N, false><<<grid, 256, 0, stream>>>(a);
+  MDL_NCH_DISPATCH(a.D, LNF)
+#undef LNF
+  return cudaGetLastError();
+}
+
+int layernorm_bwd_grid(int B) {
+  const int cap = sm_count() * 2;
+  return B < cap ? (B > 0 ? B : 1) : cap;
+}
+
+cudaError_t layernorm_bwd(const LNBwdArgs& a, cudaStream_t stream) {
+  if (a.D % 8 || a.T <= 0) return cudaErrorInvalidValue;
+  if (a.mix && ((a.D % a.T) || ((a.D / a.T) % 8))) return cudaErrorInvalidValue;
+  if (a.B == 0) return cudaSuccess;
+  const int grid = a.grid > 0 ? a.grid : layernorm_bwd_grid(a.B);
+  const size_t smem = static_cast<size_t>(a.T > 8 ? a.T : 8) * a.D * sizeof(float);
+#define LNB(N)                                                                                    \
+  if (a.mix) {                                                                                    \
+    auto k = ln_bwd_kernel<N, true>;                                                              \
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)); \
+    k<<<grid, 256, smem, stream>>>(a);                                                            \
+  } else {                                                                                        \
+    auto k = ln_bwd_kernel<N, false>;                                                             \
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)); \
+    k<<<grid, 256, smem, stream>>>(a);                                                            \
+  }
+  MDL_NCH_DISPATCH(a.D, LNB)
+#undef LNB
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  ln_partials_reduce_kernel<<<(2 * a.D + 255) / 256, 256, 0, stream>>>(a.partials, grid, a.D, a.dgamma, a.dbeta);
+  return cudaGetLastError();
+}
+
+cudaError_t rmsnorm_fwd(const RMSArgs& a, cudaStream_t stream) {
+  if (a.D % 8) return cudaErrorInvalidValue;
+  if (a.rows == 0) return cudaSuccess;
+  const int grid = static_cast<int>((a.rows + 7) / 8);
+#define RMF(N) rms_fwd_kernel<N><<<grid, 256, 0, stream>>>(a);
+  MDL_NCH_DISPATCH(a.D, RMF)
+#undef RMF
+  return cudaGetLastError();
+}
+
+cudaError_t rmsnorm_bwd(const RMSArgs& a, cudaStream_t stream) {
+  if (a.D % 8) return cudaErrorInvalidValue;
+  if (a.rows == 0) return cudaSuccess;
+  long long want = (a.rows + 7) / 8;
+  const int grid = static_cast<int>(want < sm_count() * 4 ? want : sm_count() * 4);
+#define RMB(N) rms_bwd_kernel<N><<<grid, 256, 0, stream>>>(a);
+  MDL_NCH_DISPATCH(a.D, RMB)
+#undef RMB
+  return cudaGetLastError();
+}
+
+}  // namespace mdl

@@ -1,0 +1,167 @@
+"""Seeded synthetic data in the shapes of the benchmark configs.
+
+There is no network in the benchmark environment, so every benchmark and
+parity run uses generated data of the configured shape:
+
+* categorical ids: Zipf(s) over ``[1, vocab]`` (inverse-CDF of the continuous
+  power law, then a fixed per-field multiplicative scramble so frequent ids do
+  not cluster at small row numbers) or uniform;
+* multi-hot bags with uniform lengths in ``[min_len, max_len]``;
+* dense features ``N(0, 1)``;
+* labels ``Bernoulli`` drawn from a hidden ground-truth logit (a fixed random
+  score per (field, id), averaged over bags, plus a dense projection), shifted
+  per task so the positive rate matches the configured one. A model can
+  therefore learn something, and AUC comparisons are meaningful.
+
+Generation is vectorised numpy; ``BatchPool`` pre-generates a few distinct
+batches in pinned host memory for the timed loops.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from hashlib import sha256
+
+import numpy as np
+import torch
+
+from ..ops.embedding import LookupPlan
+from .batch import PackedBatch
+
+
+@dataclass
+class FieldSpec:
+    vocab: int             # ids drawn from [1, vocab]
+    multi_hot: bool = False
+    min_len: int = 1
+    max_len: int = 1
+
+
+@dataclass
+class SyntheticSpec:
+    fields: dict[str, FieldSpec]
+    dense_width: int
+    task_rates: list[float]
+    zipf_s: float | None = 1.05      # None -> uniform ids
+    num_scenarios: int = 1
+    seed: int = 0
+
+
+def zipf_ids(rng: np.random.Generator, n: int, vocab: int, s: float | None, scramble: int) -> np.ndarray:
+    if vocab <= 1:
+        return np.ones(n, dtype=np.int64)
+    if s is None:
+        k = rng.integers(1, vocab + 1, size=n, dtype=np.int64)
+    else:
+        u = rng.random(n)
+        if abs(s - 1.0) < 1e-9:
+            x = np.exp(u * math.log(vocab + 1.0))
+        else:
+            a = 1.0 - s
+            x = np.power(1.0 + u * (math.pow(vocab + 1.0, a) - 1.0), 1.0 / a)
+        k = np.clip(np.floor(x).astype(np.int64), 1, vocab)
+    # fixed bijection of [1, vocab]: (k-1)*scramble mod vocab + 1 (scramble coprime to vocab)
+    return ((k - 1) * scramble) % vocab + 1
+
+
+def _coprime(vocab: int, seed: int) -> int:
+    cand = 1000003 + 2 * (seed % 1000)
+    while math.gcd(cand, vocab) != 1:
+        cand += 2
+    return cand
+
+
+def _id_score(ids: np.ndarray, salt: int) -> np.ndarray:
+    """Deterministic pseudo-random score in [-1, 1) per id (hash of id and salt)."""
+
+    h = (ids.astype(np.uint64) * np.uint64(0x9E3779B97F4A7C15) + np.uint64(salt & 0xFFFFFFFF)) & np.uint64(0xFFFFFFFFFFFF)
+    h ^= h >> np.uint64(17)
+    return (h % np.uint64(1 << 20)).astype(np.float64) / float(1 << 19) - 1.0
+
+
+class SyntheticGenerator:
+    """Draws ``PackedBatch``es for a lookup plan from a ``SyntheticSpec``."""
+
+    def __init__(self, plan: LookupPlan, spec: SyntheticSpec, rank: int = 0) -> None:
+        self.plan = plan
+        self.spec = spec
+        self.rng = np.random.default_rng([spec.seed, rank])
+        self.truth_rng = np.random.default_rng([spec.seed, 999])
+        self.scramble = {name: _coprime(fs.vocab, i) for i, (name, fs) in enumerate(spec.fields.items())}
+        self.field_weight = {name: float(self.truth_rng.normal(0.0, 1.0)) for name in spec.fields}
+        self.dense_proj = self.truth_rng.normal(0.0, 1.0, size=(max(spec.dense_width, 1), len(spec.task_rates)))
+        self.task_mix = self.truth_rng.normal(0.0, 1.0, size=(len(spec.task_rates),))
+        self.task_bias = None
+
+    def _truth_logits(self, per_field_scores: np.ndarray, dense: np.ndarray) -> np.ndarray:
+        nf = max(1, per_field_scores.shape[1])
+        base = per_field_scores.sum(axis=1, keepdims=True) * (2.0 / math.sqrt(nf))
+        dense_part = dense @ self.dense_proj[: dense.shape[1]] * (0.5 / math.sqrt(max(1, dense.shape[1])))
+        return base * (1.0 + 0.3 * self.task_mix[None, :]) + dense_part
+
+    def _calibrate(self, logits: np.ndarray) -> np.ndarray:
+        if self.task_bias is None:
+            biases = []
+            for t, rate in enumerate(self.spec.task_rates):
+                lo, hi = -30.0, 30.0
+                for _ in range(60):
+                    mid = 0.5 * (lo + hi)
+                    p = 1.0 / (1.0 + np.exp(-(logits[:, t] + mid)))
+                    if p.mean() > rate:
+                        hi = mid
+                    else:
+                        lo = mid
+                biases.append(0.5 * (lo + hi))
+            self.task_bias = np.array(biases)
+        return logits + self.task_bias[None, :]
+
+    def batch(self, rows: int, pin: bool = False) -> PackedBatch:
+        rng = self.rng
+        spec = self.spec
+        ids_parts = []
+        lengths_parts = []
+        scores = []
+        for f in self.plan.features:
+            if f.table is None:
+                lengths_parts.append(np.zeros(rows, dtype=np.int64))
+                continue
+            fs = spec.fields[f.name]
+            if fs.multi_hot:
+                lengths = rng.integers(fs.min_len, fs.max_len + 1, size=rows, dtype=np.int64)
+            else:
+                lengths = np.ones(rows, dtype=np.int64)
+            n = int(lengths.sum())
+            ids = zipf_ids(rng, n, fs.vocab, spec.zipf_s, self.scramble[f.name])
+            ids_parts.append(ids)
+            lengths_parts.append(lengths)
+            s = _id_score(ids, int.from_bytes(sha256(f.name.encode()).digest()[:4], 'little')) * self.field_weight[f.name]
+            bag = np.repeat(np.arange(rows), lengths)
+            per_row = np.bincount(bag, weights=s, minlength=rows) / np.maximum(lengths, 1)
+            scores.append(per_row)
+        dense = rng.standard_normal((rows, spec.dense_width)).astype(np.float32) if spec.dense_width else \
+            np.zeros((rows, 0), dtype=np.float32)
+        per_field = np.stack(scores, axis=1) if scores else np.zeros((rows, 0))
+        logits = self._calibrate(self._truth_logits(per_field, dense.astype(np.float64)))
+        probs = 1.0 / (1.0 + np.exp(-logits))
+        labels = (rng.random(probs.shape) < probs).astype(np.float32)
+        offsets = np.zeros(len(self.plan.features) * rows + 1, dtype=np.int64)
+        np.cumsum(np.concatenate(lengths_parts), out=offsets[1:])
+        ids_all = np.concatenate(ids_parts) if ids_parts else np.zeros(0, dtype=np.int64)
+        scen = rng.integers(0, spec.num_scenarios, size=rows, dtype=np.int64)
+        return PackedBatch.pack(torch.from_numpy(ids_all), torch.from_numpy(offsets),
+                                torch.from_numpy(dense) if spec.dense_width else None, torch.from_numpy(labels), None,
+                                torch.from_numpy(scen), rows, pin=pin)
+
+
+class BatchPool:
+    """A fixed set of pre-generated pinned host batches, served round-robin."""
+
+    def __init__(self, gen: SyntheticGenerator, rows: int, count: int, pin: bool = True) -> None:
+        self.batches = [gen.batch(rows, pin=pin and torch.cuda.is_available()) for _ in range(count)]
+        self.i = 0
+
+    def next(self) -> PackedBatch:
+        b = self.batches[self.i % len(self.batches)]
+        self.i += 1
+        return b

@@ -1,0 +1,220 @@
+"""Flat storage for the dense (data-parallel) parameters of a model.
+
+Every dense ``nn.Parameter`` is re-homed into one flat fp32 *master* buffer;
+its gradient lives in one flat fp32 *grad* buffer and, on CUDA, its bf16
+*shadow* (the operand the tcgen05 GEMMs read) in one flat bf16 buffer. The
+fused kernels write parameter gradients straight into the grad buffer, and one
+optimizer kernel (Adam or RMSprop, with the clip factor applied on the fly)
+updates master + state + shadow in a single pass. With ``world > 1`` the grad,
+master and shadow buffers are symmetric (IPC-mapped by every peer) and the
+update is the fused NVLink reduce-scatter / optimizer / all-gather kernel
+(``csrc/comm.cu``), bucket by bucket.
+
+Layout: parameters whose consumers read the bf16 shadow (GEMM weights) come
+first, parameters read as fp32 (norm scales, biases, head vectors) after
+``fp32_from``; each parameter starts on a 32-element boundary.
+
+Reference counterpart: DDP (``src/train.py:5276-5328``) + RMSprop
+(``src/train.py:4826-4893``) + dense clipping (``src/train.py:5745-5775``).
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Iterable
+
+import torch
+import torch.distributed as dist
+from torch import nn
+
+from ._ext import ext
+
+ALIGN = 32
+
+
+def _round(n: int, a: int = ALIGN) -> int:
+    return (n + a - 1) // a * a
+
+
+class DenseParams:
+    def __init__(self, named_params: Iterable[tuple[str, nn.Parameter]], *, device: torch.device,
+                 bf16_names: set[str] | None = None, world: int = 1, rank: int = 0, process_group=None,
+                 optimizer: str = "adam", lr: float = 1e-3, betas=(0.9, 0.999), eps: float = 1e-8,
+                 weight_decay: float = 0.0, rmsprop_alpha: float = 0.99, comm: str = "fused") -> None:
+        self.device = torch.device(device)
+        self.world, self.rank, self.group = world, rank, process_group
+        self.optimizer, self.lr, self.betas, self.eps = optimizer, lr, betas, eps
+        self.weight_decay, self.rmsprop_alpha = weight_decay, rmsprop_alpha
+        self.comm = comm
+        named = list(named_params)
+        bf16_names = set(bf16_names or ())
+        ordered = [x for x in named if x[0] in bf16_names] + [x for x in named if x[0] not in bf16_names]
+        self.names = [n for n, _ in ordered]
+        self.params = {n: p for n, p in ordered}
+        self.offsets: dict[str, int] = {}
+        off = 0
+        self.fp32_from = 0
+        for i, (name, p) in enumerate(ordered):
+            if name not in bf16_names and self.fp32_from == 0 and i > 0 and ordered[i - 1][0] in bf16_names:
+                self.fp32_from = off
+            self.offsets[name] = off
+            off += _round(p.numel())
+        if not any(n in bf16_names for n in self.names):
+            self.fp32_from = 0
+        elif all(n in bf16_names for n in self.names):
+            self.fp32_from = off
+        self.total = _round(max(off, ALIGN), ALIGN * max(1, world))
+        self.fp32_from = min(self.fp32_from, self.total)
+        self._alloc()
+        with torch.no_grad():
+            for name, p in ordered:
+                o = self.offsets[name]
+                self.master[o:o + p.numel()].copy_(p.detach().flatten().to(self.device, torch.float32))
+                p.data = self.master[o:o + p.numel()].view_as(p)
+                if self.device.type != "cuda":
+                    p.grad = self.grad[o:o + p.numel()].view_as(p)
+                p._mdl_grad = self.grad[o:o + p.numel()].view_as(p)
+                if self.shadow is not None:
+                    p._mdl_shadow = self.shadow[o:o + p.numel()].view_as(p)
+        if self.shadow is not None:
+            self.refresh_shadow()
+        self.step_count = 0
+
+    def _alloc(self) -> None:
+        dev = self.device
+        n = self.total
+        self._symm = None
+        if dev.type == "cuda" and self.world > 1 and self.comm == "fused":
+            from ..parallel.symm import SymmetricBuffers
+
+            self._symm = SymmetricBuffers({"master": (n, torch.float32), "grad": (n, torch.float32),
+                                           "shadow": (n, torch.bfloat16)}, device=dev, process_group=self.group)
+            self.master = self._symm.local("master")
+            self.grad = self._symm.local("grad")
+            self.shadow = self._symm.local("shadow")
+            self.master.zero_()
+        else:
+            self.master = torch.zeros(n, dtype=torch.float32, device=dev)
+            self.grad = torch.zeros(n, dtype=torch.float32, device=dev)
+            self.shadow = torch.zeros(n, dtype=torch.bfloat16, device=dev) if dev.type == "cuda" else None
+        self.grad.zero_()
+        self.state1 = torch.zeros(n, dtype=torch.float32, device=dev)
+        self.state2 = torch.zeros(n, dtype=torch.float32, device=dev) if self.optimizer == "adam" else None
+        self._sq = torch.zeros(1, dtype=torch.float32, device=dev)
+        self._clip = torch.ones(1, dtype=torch.float32, device=dev)
+
+    def refresh_shadow(self) -> None:
+        if self.shadow is not None:
+            ext().cast_bf16(self.master, self.shadow)
+
+    def zero_grad(self) -> None:
+        self.grad.zero_()
+
+    def broadcast_from_rank0(self) -> None:
+        """Make every rank start from rank 0's dense weights (DDP init semantics)."""
+
+        if self.world > 1 and dist.is_initialized():
+            dist.broadcast(self.master, src=0, group=self.group)
+            self.refresh_shadow()
+
+    # ------------------------------------------------------------------ step
+    @torch.no_grad()
+    def step(self, lr: float | None = None, clip_norm: float | None = None) -> torch.Tensor | None:
+        """Average gradients over ranks and apply the optimizer. Returns the grad norm if clipping."""
+
+        lr = self.lr if lr is None else lr
+        self.step_count += 1
+        t = self.step_count
+        b1, b2 = self.betas
+        bc1 = 1.0 - b1 ** t
+        bc2 = 1.0 - b2 ** t
+        opt = 0 if self.optimizer == "adam" else 1
+        if self.device.type != "cuda":
+            return self._cpu_step(lr, clip_norm, bc1, bc2)
+        C = ext()
+        scale = 1.0 / self.world
+        norm = None
+        if self._symm is not None:
+            sym = self._symm
+            sym.barrier()
+            clip = None
+            if clip_norm is not None:
+                self._sq.zero_()
+                C.dense_sync(sym.peer_ptrs("grad"), sym.peer_ptrs("master"), sym.peer_ptrs("shadow"), self.state1,
+                             self.state2, 0, self.total, self.fp32_from, self.rank, opt, lr, b1, b2, self.eps,
+                             self.weight_decay, bc1, bc2, self.rmsprop_alpha, scale, None, self._sq, 1)
+                sym.allreduce_small(self._sq)
+                C.clip_factor(self._sq, float(clip_norm), self._clip)
+                norm = self._sq.sqrt()
+                clip = self._clip
+            C.dense_sync(sym.peer_ptrs("grad"), sym.peer_ptrs("master"), sym.peer_ptrs("shadow"), self.state1,
+                         self.state2, 0, self.total, self.fp32_from, self.rank, opt, lr, b1, b2, self.eps,
+                         self.weight_decay, bc1, bc2, self.rmsprop_alpha, scale, clip, None,
+                         2 if clip_norm is not None else 0)
+            sym.barrier()
+            self.grad.zero_()
+            return norm
+        if self.world > 1 and dist.is_initialized():
+            dist.all_reduce(self.grad, group=self.group)  # NCCL baseline path
+        clip = None
+        if clip_norm is not None:
+            self._sq.zero_()
+            C.sqnorm(self.grad, scale, self._sq)
+            C.clip_factor(self._sq, float(clip_norm), self._clip)
+            clip = self._clip
+            norm = self._sq.sqrt()
+        if opt == 0:
+            C.adam(self.master, self.grad, self.state1, self.state2, self.shadow, lr, b1, b2, self.eps,
+                   self.weight_decay, bc1, bc2, scale, clip)
+        else:
+            C.rmsprop(self.master, self.grad, self.state1, self.shadow, lr, self.rmsprop_alpha, self.eps,
+                      self.weight_decay, scale, clip)
+        self.grad.zero_()
+        return norm
+
+    def _cpu_step(self, lr, clip_norm, bc1, bc2):
+        g = self.grad
+        if self.world > 1 and dist.is_initialized():
+            dist.all_reduce(g, group=self.group)
+        g = g / self.world
+        norm = None
+        if clip_norm is not None:
+            norm = g.norm()
+            g = g * min(1.0, float(clip_norm) / (float(norm) + 1e-6))
+        if self.weight_decay:
+            g = g + self.weight_decay * self.master
+        if self.optimizer == "adam":
+            b1, b2 = self.betas
+            self.state1.mul_(b1).add_(g, alpha=1 - b1)
+            self.state2.mul_(b2).addcmul_(g, g, value=1 - b2)
+            denom = (self.state2.sqrt() / math.sqrt(bc2)).add_(self.eps)
+            self.master.addcdiv_(self.state1, denom, value=-lr / bc1)
+        else:
+            a = self.rmsprop_alpha
+            self.state1.mul_(a).addcmul_(g, g, value=1 - a)
+            self.master.addcdiv_(g, self.state1.sqrt().add_(self.eps), value=-lr)
+        self.grad.zero_()
+        return norm
+
+    def state_dict(self) -> dict:
+        return {
+            "params": {n: self.master[self.offsets[n]:self.offsets[n] + p.numel()].view_as(p).detach().cpu().clone()
+                       for n, p in self.params.items()},
+            "state1": self.state1.detach().cpu().clone(),
+            "state2": None if self.state2 is None else self.state2.detach().cpu().clone(),
+            "step": self.step_count,
+            "names": list(self.names),
+        }
+
+    def load_state_dict(self, state: dict) -> None:
+        with torch.no_grad():
+            for n, v in state["params"].items():
+                if n in self.params:
+                    o = self.offsets[n]
+                    self.master[o:o + v.numel()].copy_(v.flatten().to(self.master.device))
+            if state.get("names") == self.names:
+                self.state1.copy_(state["state1"].to(self.state1.device))
+                if self.state2 is not None and state.get("state2") is not None:
+                    self.state2.copy_(state["state2"].to(self.state2.device))
+            self.step_count = int(state.get("step", 0))
+        self.refresh_shadow()

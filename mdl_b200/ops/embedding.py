@@ -1,0 +1,531 @@
+"""Sharded embedding tables and the fused embedding-bag lookup.
+
+``EmbeddingStore`` keeps the local shard of every table of a model in one fp32
+*slab* per rank (plus the fp32 gradient slab, the row-wise Adagrad
+accumulator, touched-row flags and a fixed-capacity touched list). On CUDA
+with ``world > 1`` those buffers are exported over CUDA IPC and every rank maps
+its peers' buffers, so the lookup kernel loads rows straight from the owner's
+HBM over NVLink and the backward kernel reduces gradients straight into the
+owner's gradient slab (``csrc/embedding.cu``).
+
+``LookupPlan`` describes one batched lookup: which features, their tables,
+pooling and where each pooled result lands in the output matrix (including the
+per-token slice padding of the RankMixer tokenizer input).
+
+Reference behaviour reproduced here:
+* ownership / local rows (``src/embeddings.py:163-353``), per-table seeded
+  ``normal(0, init_std)`` init with the padding row zeroed
+  (``src/embeddings.py:724-749``);
+* padding id 0 contributes nothing and gets no gradient; ``mean`` pooling
+  excludes id 0 (``src/model.py:509-678``); ``sum`` pooling is an addition;
+* owner-side gradient = sum over requesters divided by W
+  (``src/embeddings.py:615-674``), then row-wise Adagrad (``src/optim.py:31-62``).
+
+On CPU (tests, the gloo plumbing config) the same semantics run in PyTorch;
+cross-rank rows are exchanged with ``all_gather`` collectives.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from hashlib import sha256
+from typing import Sequence
+
+import torch
+import torch.distributed as dist
+
+from ..parallel.sharding import EmbeddingShardingPlan, EmbeddingShardSpec
+from ._ext import error_word, ext
+
+POOL_NONE, POOL_MEAN, POOL_SUM = 0, 1, 2
+HASH_NONE, HASH_PREHASHED = 0, 1
+
+
+@dataclass
+class TableLayout:
+    name: str
+    num_embeddings: int
+    dim: int
+    spec: EmbeddingShardSpec
+    local_rows: int
+    base: int = 0       # element offset in the slab
+    row_base: int = 0   # offset in the row space
+
+
+def table_seed(name: str) -> int:
+    return int.from_bytes(sha256(name.encode("utf-8")).digest()[:8], "little")
+
+
+class EmbeddingStore:
+    """All local table shards of one rank, plus sparse optimizer state."""
+
+    def __init__(self, tables: Sequence[tuple[str, int, int]], plan: EmbeddingShardingPlan, *, rank: int,
+                 world: int, device: torch.device, init_std: float = 0.02, lr: float = 0.01, eps: float = 1e-10,
+                 initial_accumulator_value: float = 0.1, touched_capacity: int | None = None,
+                 process_group=None, base_seed: int | None = None) -> None:
+        self.rank = rank
+        self.world = world
+        self.device = torch.device(device)
+        self.lr = lr
+        self.eps = eps
+        self.process_group = process_group
+        self.layouts: list[TableLayout] = []
+        self.index: dict[str, int] = {}
+        elem = 0
+        rows = 0
+        for name, num, dim in tables:
+            spec = plan.tables[name]
+            local = spec.local_rows(num, rank)
+            layout = TableLayout(name, int(num), int(dim), spec, local, base=elem, row_base=rows)
+            self.index[name] = len(self.layouts)
+            self.layouts.append(layout)
+            elem += ((local * dim + 3) // 4) * 4  # keep each table 16-byte aligned
+            rows += local
+        self.total_elems = max(elem, 4)
+        self.total_rows = max(rows, 1)
+        self.touched_capacity = int(touched_capacity or self.total_rows)
+        self._peer_handles: list = []
+        self._alloc()
+        self.reset_parameters(init_std, base_seed)
+        self.acc.fill_(initial_accumulator_value)
+        self._meta_cache: dict = {}
+        self.step_count = 0
+
+    # ------------------------------------------------------------ storage
+    def _alloc(self) -> None:
+        dev = self.device
+        if dev.type == "cuda" and self.world > 1:
+            from ..parallel import symm
+
+            self._symm = symm.SymmetricBuffers(
+                {
+                    "slab": (self.total_elems, torch.float32),
+                    "grad": (self.total_elems, torch.float32),
+                    "flags": (self.total_rows, torch.int32),
+                    "touched": (self.touched_capacity, torch.int64),
+                    "count": (4, torch.int32),
+                },
+                device=dev,
+                process_group=self.process_group,
+            )
+            self.slab = self._symm.local("slab")
+            self.grad = self._symm.local("grad")
+            self.flags = self._symm.local("flags")
+            self.touched = self._symm.local("touched")
+            self.count = self._symm.local("count")
+            self.grad.zero_()
+            self.flags.zero_()
+            self.count.zero_()
+            self._symm.barrier_host()
+        else:
+            self._symm = None
+            self.slab = torch.empty(self.total_elems, dtype=torch.float32, device=dev)
+            self.grad = torch.zeros(self.total_elems, dtype=torch.float32, device=dev)
+            self.flags = torch.zeros(self.total_rows, dtype=torch.int32, device=dev)
+            self.touched = torch.zeros(self.touched_capacity, dtype=torch.int64, device=dev)
+            self.count = torch.zeros(4, dtype=torch.int32, device=dev)
+        self.acc = torch.empty(self.total_rows, dtype=torch.float32, device=dev)
+        # CPU path: dense gradient accumulation per table (sparse rows tracked by a mask)
+        self._cpu_touched = torch.zeros(self.total_rows, dtype=torch.bool) if dev.type != "cuda" else None
+
+    def weight(self, name: str) -> torch.Tensor:
+        """View of the local shard of table ``name`` as ``[local_rows, dim]``."""
+
+        t = self.layouts[self.index[name]]
+        return self.slab[t.base:t.base + t.local_rows * t.dim].view(t.local_rows, t.dim)
+
+    def grad_view(self, name: str) -> torch.Tensor:
+        t = self.layouts[self.index[name]]
+        return self.grad[t.base:t.base + t.local_rows * t.dim].view(t.local_rows, t.dim)
+
+    def accumulator(self, name: str) -> torch.Tensor:
+        t = self.layouts[self.index[name]]
+        return self.acc[t.row_base:t.row_base + t.local_rows]
+
+    @torch.no_grad()
+    def reset_parameters(self, init_std: float, base_seed: int | None = None) -> None:
+        """Per-table seeded normal init, padding row (id 0) zeroed on its owner."""
+
+        seed0 = torch.initial_seed() if base_seed is None else int(base_seed)
+        for t in self.layouts:
+            if t.local_rows == 0:
+                continue
+            w = self.weight(t.name)
+            seed = (seed0 + table_seed(t.name) + self.rank * 104729) % (2 ** 63 - 1)
+            gen = torch.Generator(device=w.device)
+            gen.manual_seed(seed)
+            w.normal_(0.0, init_std, generator=gen)
+            if t.spec.owner_of(0) == self.rank:
+                w[0 if t.spec.strategy == "table_wise" else 0 // self.world].zero_()
+
+    # ------------------------------------------------------------ metadata
+    def table_meta(self) -> dict[str, torch.Tensor]:
+        key = "tables"
+        meta = self._meta_cache.get(key)
+        if meta is None:
+            L = self.layouts
+            dev = self.device
+            meta = {
+                "t_base": torch.tensor([t.base for t in L] or [0], dtype=torch.int64, device=dev),
+                "t_row_base": torch.tensor([t.row_base for t in L] or [0], dtype=torch.int64, device=dev),
+                "t_dim": torch.tensor([t.dim for t in L] or [4], dtype=torch.int32, device=dev),
+                "t_mode": torch.tensor([0 if t.spec.strategy == "row_wise" else 1 for t in L] or [0],
+                                       dtype=torch.int32, device=dev),
+                "t_cyc": torch.tensor([t.spec.cyclic_offset for t in L] or [0], dtype=torch.int32, device=dev),
+                "t_owner": torch.tensor([t.spec.table_owner or 0 for t in L] or [0], dtype=torch.int32, device=dev),
+                "t_rows": torch.tensor([t.num_embeddings for t in L] or [1], dtype=torch.int64, device=dev),
+            }
+            self._meta_cache[key] = meta
+        return meta
+
+    def peer_ptrs(self, name: str) -> list[int]:
+        if self._symm is not None:
+            return self._symm.peer_ptrs(name)
+        return [getattr(self, {"slab": "slab", "grad": "grad", "flags": "flags", "touched": "touched",
+                               "count": "count"}[name]).data_ptr()]
+
+    # ------------------------------------------------------------ optimizer
+    @torch.no_grad()
+    def step(self, lr: float | None = None, clip_norm: float | None = None) -> torch.Tensor | None:
+        """Row-wise Adagrad on every row touched since the last step.
+
+        Returns the (pre-clip) global sparse gradient norm when ``clip_norm`` is set.
+        """
+
+        lr = self.lr if lr is None else lr
+        self.step_count += 1
+        grad_scale = 1.0 / self.world
+        if self.device.type != "cuda":
+            return self._cpu_step(lr, grad_scale, clip_norm)
+        m = self.table_meta()
+        if self._symm is not None:
+            self._symm.barrier()  # every rank finished pushing gradients
+        clip = None
+        norm = None
+        if clip_norm is not None:
+            sq = torch.zeros(1, dtype=torch.float32, device=self.device)
+            ext().touched_sqnorm(self.grad, self.touched, self.count, m["t_base"], m["t_row_base"], m["t_dim"],
+                                 grad_scale, sq)
+            if self.world > 1:
+                dist.all_reduce(sq, group=self.process_group)
+            clip = torch.empty(1, dtype=torch.float32, device=self.device)
+            ext().clip_factor(sq, float(clip_norm), clip)
+            norm = sq.sqrt()
+        ext().adagrad_apply(self.slab, self.grad, self.acc, self.flags, self.touched, self.count, m["t_base"],
+                            m["t_row_base"], m["t_dim"], float(lr), float(self.eps), grad_scale, clip,
+                            error_word(self.device))
+        if self._symm is not None:
+            self._symm.barrier()  # updated rows visible before any peer reads them
+        return norm
+
+    def _cpu_step(self, lr: float, grad_scale: float, clip_norm: float | None):
+        if self.world > 1 and dist.is_initialized():
+            # gradients were accumulated only for owned rows (see _cpu_backward); nothing to exchange
+            pass
+        touched = self._cpu_touched.nonzero().flatten()
+        norm = None
+        scale = grad_scale
+        if clip_norm is not None:
+            sq = torch.zeros(1)
+            for t in self.layouts:
+                rows = touched[(touched >= t.row_base) & (touched < t.row_base + t.local_rows)] - t.row_base
+                if rows.numel():
+                    sq += (self.grad_view(t.name)[rows] * grad_scale).square().sum()
+            if self.world > 1 and dist.is_initialized():
+                dist.all_reduce(sq, group=self.process_group)
+            norm = sq.sqrt()
+            scale = grad_scale * min(1.0, float(clip_norm) / (float(norm) + 1e-6))
+        for t in self.layouts:
+            rows = touched[(touched >= t.row_base) & (touched < t.row_base + t.local_rows)] - t.row_base
+            if rows.numel() == 0:
+                continue
+            g = self.grad_view(t.name)[rows] * scale
+            acc = self.accumulator(t.name)
+            acc[rows] += g.square().mean(dim=1)
+            w = self.weight(t.name)
+            w[rows] -= lr * g / (acc[rows].sqrt() + self.eps).unsqueeze(1)
+            self.grad_view(t.name)[rows] = 0.0
+        self._cpu_touched.zero_()
+        return norm
+
+    def state_dict(self) -> dict:
+        return {
+            "tables": {
+                t.name: {
+                    "weight": self.weight(t.name).detach().cpu().clone(),
+                    "sum": self.accumulator(t.name).detach().cpu().clone(),
+                    "num_embeddings": t.num_embeddings,
+                    "embedding_dim": t.dim,
+                    "shard_spec": {"table_name": t.spec.table_name, "strategy": t.spec.strategy,
+                                   "world_size": t.spec.world_size, "cyclic_offset": t.spec.cyclic_offset,
+                                   "table_owner": t.spec.table_owner},
+                }
+                for t in self.layouts
+            },
+            "step": self.step_count,
+        }
+
+
+# ====================================================================== lookup plan
+@dataclass
+class LookupFeature:
+    name: str
+    table: str | None          # None -> dense feature
+    pooling: int = POOL_NONE
+    hash_mode: int = HASH_NONE
+    buckets: int = 0
+    width: int = 0
+    out_col: int = 0
+    dense_col: int = 0
+
+
+@dataclass
+class LookupPlan:
+    """A batched lookup writing ``[rows, out_ld]`` bf16 (feature columns concatenated).
+
+    ``slice_k``/``slice_stride`` remap logical column ``c`` to
+    ``(c // slice_k) * slice_stride + c % slice_k`` so per-token input slices
+    of a per-token projection can be padded to a 16-byte multiple (TMA rule).
+    """
+
+    features: list[LookupFeature]
+    out_width: int               # logical width
+    slice_k: int = 0
+    slice_stride: int = 0
+    dense_width: int = 0
+    _meta: dict = field(default_factory=dict)
+
+    @property
+    def out_ld(self) -> int:
+        if self.slice_k:
+            return (self.out_width + self.slice_k - 1) // self.slice_k * self.slice_stride
+        return self.out_width
+
+    def phys_col(self, c: int) -> int:
+        return (c // self.slice_k) * self.slice_stride + c % self.slice_k if self.slice_k else c
+
+    def device_meta(self, store: EmbeddingStore, rows: int) -> tuple[list[torch.Tensor], int]:
+        key = (rows, store.device)
+        cached = self._meta.get(key)
+        if cached is not None:
+            return cached
+        dev = store.device
+        F = len(self.features)
+        chunk_prefix = [0]
+        bag_prefix = [0]
+        lanes_list = []
+        for f in self.features:
+            lanes = 1
+            while lanes * 4 < f.width and lanes < 32:
+                lanes *= 2
+            if f.width > 4 * lanes * 8:
+                raise ValueError(f"feature {f.name}: width {f.width} exceeds the lookup kernel limit")
+            lanes_list.append(lanes)
+            bags_per_warp = 32 // lanes
+            chunk_prefix.append(chunk_prefix[-1] + (rows + bags_per_warp - 1) // bags_per_warp)
+            bag_prefix.append(bag_prefix[-1] + rows)
+        tm = store.table_meta()
+        i32 = lambda xs: torch.tensor(xs, dtype=torch.int32, device=dev)
+        i64 = lambda xs: torch.tensor(xs, dtype=torch.int64, device=dev)
+        meta = [
+            i64(chunk_prefix),
+            i64(bag_prefix),
+            i32([store.index[f.table] if f.table is not None else -1 for f in self.features]),
+            i32([f.pooling for f in self.features]),
+            i32([f.hash_mode for f in self.features]),
+            i64([max(f.buckets, 1) for f in self.features]),
+            i32([f.width for f in self.features]),
+            i32(lanes_list),
+            i64([0] * F),
+            i64([self.out_ld] * F),
+            i32([f.out_col for f in self.features]),
+            i32([self.slice_k] * F),
+            i32([self.slice_stride] * F),
+            i32([f.dense_col for f in self.features]),
+            tm["t_base"], tm["t_row_base"], tm["t_dim"], tm["t_mode"], tm["t_cyc"], tm["t_owner"], tm["t_rows"],
+        ]
+        result = (meta, chunk_prefix[-1])
+        self._meta[key] = result
+        return result
+
+
+# ====================================================================== torch reference path
+def _hash_ids(ids: torch.Tensor, f: LookupFeature) -> torch.Tensor:
+    if f.hash_mode == HASH_PREHASHED:
+        return torch.where(ids == 0, torch.zeros_like(ids), (ids & (f.buckets - 1)) + 1)
+    return ids
+
+
+def _gather_rows_cpu(store: EmbeddingStore, table: str, ids: torch.Tensor) -> torch.Tensor:
+    """Rows for global ids (any owner); id 0 and out-of-range ids give zeros."""
+
+    t = store.layouts[store.index[table]]
+    out = torch.zeros(ids.numel(), t.dim, dtype=torch.float32)
+    if store.world == 1 or not dist.is_initialized():
+        valid = (ids > 0) & (ids < t.num_embeddings)
+        local = t.spec.local_row_ids(ids[valid])
+        out[valid] = store.weight(table)[local].float()
+        return out
+    # gather every rank's request ids, answer the owned ones, sum the answers
+    group = store.process_group
+    counts = [torch.zeros(1, dtype=torch.int64) for _ in range(store.world)]
+    dist.all_gather(counts, torch.tensor([ids.numel()], dtype=torch.int64), group=group)
+    cap = int(max(c.item() for c in counts))
+    padded = torch.zeros(cap, dtype=torch.int64)
+    padded[:ids.numel()] = ids
+    all_ids = [torch.zeros(cap, dtype=torch.int64) for _ in range(store.world)]
+    dist.all_gather(all_ids, padded, group=group)
+    answers = []
+    for r in range(store.world):
+        req = all_ids[r]
+        ans = torch.zeros(cap, t.dim, dtype=torch.float32)
+        owner = t.spec.owner(req)
+        mine = (owner == store.rank) & (req > 0) & (req < t.num_embeddings)
+        if mine.any():
+            ans[mine] = store.weight(table)[t.spec.local_row_ids(req[mine])].float()
+        answers.append(ans)
+    stacked = torch.stack(answers)  # [W, cap, dim]: my answers for every rank
+    # reduce-scatter by hand: everyone sums everyone's answers for rank r
+    total = stacked.clone()
+    dist.all_reduce(total, group=group)
+    return total[store.rank, :ids.numel()]
+
+
+def _push_grads_cpu(store: EmbeddingStore, table: str, ids: torch.Tensor, grads: torch.Tensor) -> None:
+    t = store.layouts[store.index[table]]
+    valid = (ids > 0) & (ids < t.num_embeddings)
+    if store.world == 1 or not dist.is_initialized():
+        ids_v = ids[valid]
+        local = t.spec.local_row_ids(ids_v)
+        store.grad_view(table).index_add_(0, local, grads[valid].float())
+        store._cpu_touched[t.row_base + local] = True
+        return
+    group = store.process_group
+    counts = [torch.zeros(1, dtype=torch.int64) for _ in range(store.world)]
+    dist.all_gather(counts, torch.tensor([ids.numel()], dtype=torch.int64), group=group)
+    cap = int(max(c.item() for c in counts))
+    pid = torch.zeros(cap, dtype=torch.int64)
+    pid[:ids.numel()] = torch.where(valid, ids, torch.zeros_like(ids))
+    pg = torch.zeros(cap, t.dim, dtype=torch.float32)
+    pg[:ids.numel()] = grads.float()
+    all_ids = [torch.zeros(cap, dtype=torch.int64) for _ in range(store.world)]
+    all_g = [torch.zeros(cap, t.dim, dtype=torch.float32) for _ in range(store.world)]
+    dist.all_gather(all_ids, pid, group=group)
+    dist.all_gather(all_g, pg, group=group)
+    for r in range(store.world):
+        req = all_ids[r]
+        mine = (t.spec.owner(req) == store.rank) & (req > 0)
+        if mine.any():
+            local = t.spec.local_row_ids(req[mine])
+            store.grad_view(table).index_add_(0, local, all_g[r][mine])
+            store._cpu_touched[t.row_base + local] = True
+
+
+def lookup_reference(store: EmbeddingStore, plan: LookupPlan, ids: torch.Tensor, offsets: torch.Tensor,
+                     dense: torch.Tensor | None, rows: int, out_dtype=torch.float32) -> torch.Tensor:
+    """PyTorch definition of the fused lookup (CPU path and test oracle)."""
+
+    out = torch.zeros(rows, plan.out_ld, dtype=torch.float32, device=ids.device)
+    cols = torch.tensor([plan.phys_col(c) for c in range(plan.out_width)], dtype=torch.long)
+    logical = torch.zeros(rows, plan.out_width, dtype=torch.float32)
+    for fi, f in enumerate(plan.features):
+        if f.table is None:
+            logical[:, f.out_col:f.out_col + f.width] = dense[:, f.dense_col:f.dense_col + f.width].float().cpu()
+            continue
+        beg = offsets[fi * rows:(fi + 1) * rows + 1].cpu()
+        lengths = beg[1:] - beg[:-1]
+        flat = ids[int(beg[0]):int(beg[-1])].cpu()
+        flat = _hash_ids(flat, f)
+        bag = torch.repeat_interleave(torch.arange(rows), lengths)
+        t = store.layouts[store.index[f.table]]
+        valid = (flat > 0) & (flat < t.num_embeddings)
+        if f.pooling == POOL_NONE:
+            # first valid id of each bag
+            first = torch.full((rows,), -1, dtype=torch.long)
+            idx = torch.arange(flat.numel())
+            cand = torch.where(valid, idx, torch.full_like(idx, flat.numel() + 1))
+            firsts = torch.full((rows,), flat.numel() + 1, dtype=torch.long).scatter_reduce(0, bag, cand, "amin")
+            keep = torch.zeros(flat.numel(), dtype=torch.bool)
+            ok = firsts <= flat.numel() - 1
+            keep[firsts[ok]] = True
+            valid = valid & keep
+        rows_v = _gather_rows_cpu(store, f.table, torch.where(valid, flat, torch.zeros_like(flat)))
+        pooled = torch.zeros(rows, t.dim).index_add_(0, bag, rows_v * valid.unsqueeze(1).float())
+        if f.pooling == POOL_MEAN:
+            cnt = torch.zeros(rows).index_add_(0, bag, valid.float()).clamp_min(1.0)
+            pooled = pooled / cnt.unsqueeze(1)
+        logical[:, f.out_col:f.out_col + t.dim] = pooled
+    out[:, cols] = logical.to(out.device)
+    return out.to(out_dtype)
+
+
+def backward_reference(store: EmbeddingStore, plan: LookupPlan, ids: torch.Tensor, offsets: torch.Tensor,
+                       grad_out: torch.Tensor, rows: int) -> None:
+    cols = torch.tensor([plan.phys_col(c) for c in range(plan.out_width)], dtype=torch.long)
+    g_logical = grad_out.float().cpu()[:, cols]
+    for fi, f in enumerate(plan.features):
+        if f.table is None:
+            continue
+        beg = offsets[fi * rows:(fi + 1) * rows + 1].cpu()
+        lengths = beg[1:] - beg[:-1]
+        flat = _hash_ids(ids[int(beg[0]):int(beg[-1])].cpu(), f)
+        bag = torch.repeat_interleave(torch.arange(rows), lengths)
+        t = store.layouts[store.index[f.table]]
+        valid = (flat > 0) & (flat < t.num_embeddings)
+        if f.pooling == POOL_NONE:
+            idx = torch.arange(flat.numel())
+            cand = torch.where(valid, idx, torch.full_like(idx, flat.numel() + 1))
+            firsts = torch.full((rows,), flat.numel() + 1, dtype=torch.long).scatter_reduce(0, bag, cand, "amin")
+            keep = torch.zeros(flat.numel(), dtype=torch.bool)
+            ok = firsts <= flat.numel() - 1
+            keep[firsts[ok]] = True
+            valid = valid & keep
+        g = g_logical[:, f.out_col:f.out_col + t.dim]
+        if f.pooling == POOL_MEAN:
+            cnt = torch.zeros(rows).index_add_(0, bag, valid.float()).clamp_min(1.0)
+            g = g / cnt.unsqueeze(1)
+        per_id = g[bag] * valid.unsqueeze(1).float()
+        _push_grads_cpu(store, f.table, torch.where(valid, flat, torch.zeros_like(flat)), per_id)
+
+
+# ====================================================================== autograd op
+class _FusedLookup(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, anchor, store, plan, ids, offsets, dense, rows):
+        ctx.store, ctx.plan, ctx.rows = store, plan, rows
+        ctx.save_for_backward(ids, offsets)
+        if ids.is_cuda:
+            meta, chunks = plan.device_meta(store, rows)
+            out = torch.empty(rows, plan.out_ld, dtype=torch.bfloat16, device=ids.device)
+            if plan.slice_k and plan.out_ld != plan.out_width:
+                out.zero_()  # padding columns of the per-token slices must read as zero
+            ext().emb_forward(meta, store.peer_ptrs("slab"), store.rank, ids, offsets, dense,
+                              plan.dense_width, out, chunks, error_word(ids.device))
+            return out
+        return lookup_reference(store, plan, ids, offsets, dense, rows, out_dtype=torch.float32)
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        ids, offsets = ctx.saved_tensors
+        store, plan, rows = ctx.store, ctx.plan, ctx.rows
+        if ids.is_cuda:
+            meta, chunks = plan.device_meta(store, rows)
+            g = grad_out if grad_out.dtype == torch.bfloat16 else grad_out.to(torch.bfloat16)
+            ext().emb_backward(meta, store.peer_ptrs("slab"), store.peer_ptrs("grad"), store.peer_ptrs("flags"),
+                               store.peer_ptrs("touched"), store.peer_ptrs("count"), store.touched_capacity,
+                               store.rank, ids, offsets, g.contiguous(), chunks, error_word(ids.device))
+        else:
+            backward_reference(store, plan, ids, offsets, grad_out, rows)
+        return (None,) * 7
+
+
+def fused_lookup(store: EmbeddingStore, plan: LookupPlan, ids: torch.Tensor, offsets: torch.Tensor,
+                 dense: torch.Tensor | None, rows: int, anchor: torch.Tensor) -> torch.Tensor:
+    """Pooled lookup of all plan features -> ``[rows, plan.out_ld]`` (bf16 on CUDA, fp32 on CPU).
+
+    ``anchor`` is any tensor with ``requires_grad=True``; it only makes autograd
+    call the backward, which pushes gradients into the store's gradient slab.
+    """
+
+    return _FusedLookup.apply(anchor, store, plan, ids, offsets, dense, rows)

@@ -1,0 +1,135 @@
+"""Training step engine shared by ``train``, ``benchmark`` and ``bench.py``.
+
+One ``Trainer`` owns a model, its flat dense parameters (``DenseParams``) and
+its embedding store, and runs the reference's optimizer-step semantics
+(``train_mdl`` ``src/train.py:6529-7431``, hot loop :6832-7360):
+
+* loss reduction ``sum`` / ``mean_per_task`` with per-task weights, scaled so
+  that the rank-averaged gradient equals the global objective
+  (``_loss_terms_from_batch`` ``src/train.py:5890-6031``);
+* LR schedule: linear warmup then constant or cosine (``src/train.py:5495-5512``);
+* dense optimizer (RMSprop or Adam) after the gradient average, optional
+  global clip (``src/train.py:5745-5826``);
+* row-wise Adagrad on the touched embedding rows with the owner-side ``1/W``
+  gradient scale and optional global sparse clip;
+* gradient accumulation over ``gradient_accumulation_steps`` micro-batches.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+import torch.distributed as dist
+
+from ..config.schema import AppConfig
+from ..ops.dense import DenseParams
+
+
+def lr_multiplier(config: AppConfig, step: int, decay_steps: int | None = None) -> float:
+    t = config.training
+    warm = t.lr_warmup_steps if t.warmup_steps is None else t.warmup_steps
+    if warm > 0 and step <= warm:
+        return float(step) / float(warm)
+    if t.lr_schedule == "constant":
+        return 1.0
+    decay = decay_steps if decay_steps is not None else t.lr_decay_steps
+    if decay is None:
+        raise RuntimeError("cosine lr_schedule requires lr_decay_steps")
+    if decay <= warm:
+        return min(1.0, float(step) / float(max(warm, 1)))
+    progress = min(max(float(step - warm) / float(decay - warm), 0.0), 1.0)
+    return t.lr_min_ratio + (1.0 - t.lr_min_ratio) * 0.5 * (1.0 + math.cos(math.pi * progress))
+
+
+@dataclass
+class StepResult:
+    loss: torch.Tensor
+    logits: torch.Tensor | None = None
+    dense_grad_norm: torch.Tensor | None = None
+    sparse_grad_norm: torch.Tensor | None = None
+    extras: dict = field(default_factory=dict)
+
+
+class Trainer:
+    def __init__(self, config: AppConfig, model, *, device: torch.device, rank: int = 0, world: int = 1,
+                 process_group=None) -> None:
+        self.config = config
+        self.model = model
+        self.device = torch.device(device)
+        self.rank, self.world, self.group = rank, world, process_group
+        t = config.training
+        self.dense = DenseParams(
+            model.named_parameters(), device=self.device, bf16_names=model.gemm_param_names(), world=world,
+            rank=rank, process_group=process_group, optimizer=t.dense_optimizer, lr=t.lr_dense,
+            betas=(t.adam_beta1, t.adam_beta2), eps=t.adam_eps if t.dense_optimizer == "adam" else 1e-8,
+            weight_decay=t.weight_decay, rmsprop_alpha=t.rmsprop_alpha, comm=t.comm)
+        self.dense.broadcast_from_rank0()
+        self.store = model.store
+        names = list(config.task_names)
+        self.task_weights = torch.tensor([float(t.task_loss_weights.get(n, 1.0)) for n in names],
+                                         dtype=torch.float32, device=self.device)
+        self.step_index = 0
+        self.micro_index = 0
+
+    def task_scale(self, batch) -> torch.Tensor:
+        """Per-task multiplier of the summed BCE terms (see module docstring)."""
+
+        red = self.config.training.loss_reduction
+        W = float(self.world)
+        if red == "sum":
+            return self.task_weights * W
+        if batch.label_mask is None:
+            counts = torch.full_like(self.task_weights, float(batch.rows))
+            global_counts = counts * W  # equal local batch on every rank
+        else:
+            counts = batch.label_mask.float().sum(dim=0).to(self.device)
+            global_counts = counts.clone()
+            if self.world > 1 and dist.is_initialized():
+                dist.all_reduce(global_counts, group=self.group)
+        scale = torch.where(global_counts > 0, W / global_counts.clamp_min(1.0), torch.zeros_like(global_counts))
+        return scale * self.task_weights
+
+    def forward_backward(self, batch) -> dict:
+        out = self.model(batch, task_scale=self.task_scale(batch))
+        out["loss"].backward()
+        return out
+
+    def optimizer_step(self) -> tuple[torch.Tensor | None, torch.Tensor | None]:
+        self.step_index += 1
+        t = self.config.training
+        mult = lr_multiplier(self.config, self.step_index)
+        lr_sparse = t.lr_sparse if t.lr_sparse is not None else t.lr_dense
+        dn = self.dense.step(lr=t.lr_dense * mult, clip_norm=t.dense_clip_norm)
+        sn = self.store.step(lr=lr_sparse * mult, clip_norm=t.sparse_clip_norm)
+        return dn, sn
+
+    def train_step(self, batch) -> StepResult:
+        """One micro-batch; runs the optimizers every ``gradient_accumulation_steps`` micro-batches."""
+
+        out = self.forward_backward(batch)
+        self.micro_index += 1
+        dn = sn = None
+        if self.micro_index % self.config.training.gradient_accumulation_steps == 0:
+            dn, sn = self.optimizer_step()
+        return StepResult(loss=out["loss"].detach(), logits=out.get("logits"), dense_grad_norm=dn,
+                          sparse_grad_norm=sn)
+
+    def step_from_host(self, host_batch, loss_out: torch.Tensor | None = None) -> StepResult:
+        """Public end-to-end step: copy a (pinned) host batch to the device, train, and copy
+        the loss back into ``loss_out`` (a pinned host scalar) without a host sync."""
+
+        if self.device.type == "cuda":
+            batch = host_batch.to(self.device, non_blocking=True)
+        else:
+            batch = host_batch
+        result = self.train_step(batch)
+        if loss_out is not None:
+            loss_out.copy_(result.loss.reshape(loss_out.shape), non_blocking=True)
+        return result
+
+    @torch.no_grad()
+    def predict_logits(self, batch) -> torch.Tensor:
+        out = self.model(batch, task_scale=self.task_scale(batch))
+        return out["logits"].detach()
