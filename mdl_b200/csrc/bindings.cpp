@@ -94,10 +94,9 @@ template <typename T>
 const T* dptr(const at::Tensor& t) { return t.defined() && t.numel() ? reinterpret_cast<const T*>(t.data_ptr()) : nullptr; }
 
 mdl::EmbPlan make_plan(const std::vector<at::Tensor>& meta, const std::vector<int64_t>& slabs,
-                       const std::vector<int64_t>& grad_slabs, const std::vector<int64_t>& flags,
-                       const std::vector<int64_t>& touched, const std::vector<int64_t>& counts, int64_t touched_cap,
-                       int64_t rank, const at::Tensor& ids, const at::Tensor& id_offsets,
-                       const std::optional<at::Tensor>& dense, int64_t dense_ld, const std::optional<at::Tensor>& err) {
+                       const std::vector<int64_t>& grad_slabs, const std::vector<int64_t>& flags, int64_t rank,
+                       const at::Tensor& ids, const at::Tensor& id_offsets, const std::optional<at::Tensor>& dense,
+                       int64_t dense_ld, const std::optional<at::Tensor>& err, int64_t max_vec) {
   // meta order (all device tensors):
   //  0 f_chunk_prefix(i64) 1 f_bag_prefix(i64) 2 f_table(i32) 3 f_pool(i32) 4 f_hash(i32) 5 f_buckets(i64)
   //  6 f_width(i32) 7 f_lanes(i32) 8 f_out_base(i64) 9 f_out_ld(i64) 10 f_out_col(i32) 11 f_slice(i32)
@@ -109,6 +108,7 @@ mdl::EmbPlan make_plan(const std::vector<at::Tensor>& meta, const std::vector<in
   p.world = static_cast<int>(slabs.size());
   TORCH_CHECK(p.world >= 1 && p.world <= mdl::kMaxWorld, "world size out of range");
   p.rank = static_cast<int>(rank);
+  p.max_vec = static_cast<int>(max_vec);
   p.f_chunk_prefix = dptr<long long>(meta[0]);
   p.f_bag_prefix = dptr<long long>(meta[1]);
   p.f_table = dptr<int>(meta[2]);
@@ -133,11 +133,8 @@ mdl::EmbPlan make_plan(const std::vector<at::Tensor>& meta, const std::vector<in
   for (int r = 0; r < p.world; ++r) {
     p.slabs[r] = reinterpret_cast<float*>(slabs[r]);
     if (r < static_cast<int>(grad_slabs.size())) p.grad_slabs[r] = reinterpret_cast<float*>(grad_slabs[r]);
-    if (r < static_cast<int>(flags.size())) p.flags[r] = reinterpret_cast<unsigned*>(flags[r]);
-    if (r < static_cast<int>(touched.size())) p.touched[r] = reinterpret_cast<long long*>(touched[r]);
-    if (r < static_cast<int>(counts.size())) p.touched_count[r] = reinterpret_cast<int*>(counts[r]);
+    if (r < static_cast<int>(flags.size())) p.flags[r] = reinterpret_cast<unsigned char*>(flags[r]);
   }
-  p.touched_cap = touched_cap;
   p.ids = dptr<long long>(ids);
   p.id_offsets = dptr<long long>(id_offsets);
   p.dense = dense.has_value() ? dptr<float>(*dense) : nullptr;
@@ -148,40 +145,41 @@ mdl::EmbPlan make_plan(const std::vector<at::Tensor>& meta, const std::vector<in
 
 void emb_forward(const std::vector<at::Tensor>& meta, const std::vector<int64_t>& slabs, int64_t rank,
                  const at::Tensor& ids, const at::Tensor& id_offsets, const std::optional<at::Tensor>& dense,
-                 int64_t dense_ld, const at::Tensor& out, int64_t total_chunks, const std::optional<at::Tensor>& err) {
+                 int64_t dense_ld, const at::Tensor& out, int64_t total_chunks, const std::optional<at::Tensor>& err,
+                 int64_t max_vec) {
   c10::cuda::CUDAGuard guard(out.device());
   TORCH_CHECK(out.scalar_type() == at::kBFloat16, "embedding output must be bf16");
-  mdl::EmbPlan p = make_plan(meta, slabs, {}, {}, {}, {}, 0, rank, ids, id_offsets, dense, dense_ld, err);
+  mdl::EmbPlan p = make_plan(meta, slabs, {}, {}, rank, ids, id_offsets, dense, dense_ld, err, max_vec);
   p.out = out.data_ptr();
   check(mdl::emb_pool_forward(p, total_chunks, stream_of(out)), "emb_pool_forward");
   g_launches += 1;
 }
 
 void emb_backward(const std::vector<at::Tensor>& meta, const std::vector<int64_t>& slabs,
-                  const std::vector<int64_t>& grad_slabs, const std::vector<int64_t>& flags,
-                  const std::vector<int64_t>& touched, const std::vector<int64_t>& counts, int64_t touched_cap,
-                  int64_t rank, const at::Tensor& ids, const at::Tensor& id_offsets, const at::Tensor& grad_out,
-                  int64_t total_chunks, const std::optional<at::Tensor>& err) {
+                  const std::vector<int64_t>& grad_slabs, const std::vector<int64_t>& flags, int64_t rank,
+                  const at::Tensor& ids, const at::Tensor& id_offsets, const at::Tensor& grad_out,
+                  int64_t total_chunks, const std::optional<at::Tensor>& err, int64_t max_vec) {
   c10::cuda::CUDAGuard guard(grad_out.device());
   TORCH_CHECK(grad_out.scalar_type() == at::kBFloat16, "embedding grad must be bf16");
-  mdl::EmbPlan p = make_plan(meta, slabs, grad_slabs, flags, touched, counts, touched_cap, rank, ids, id_offsets,
-                             std::nullopt, 0, err);
+  mdl::EmbPlan p = make_plan(meta, slabs, grad_slabs, flags, rank, ids, id_offsets, std::nullopt, 0, err, max_vec);
   check(mdl::emb_pool_backward(p, grad_out.data_ptr(), total_chunks, stream_of(grad_out)), "emb_pool_backward");
   g_launches += 1;
 }
 
 mdl::AdagradArgs adagrad_args(const at::Tensor& slab, const at::Tensor& grad_slab, const at::Tensor& acc,
-                              const at::Tensor& flags, const at::Tensor& touched, const at::Tensor& count,
-                              const at::Tensor& t_base, const at::Tensor& t_row_base, const at::Tensor& t_dim,
-                              double lr, double eps, double grad_scale, const std::optional<at::Tensor>& clip,
-                              const std::optional<at::Tensor>& err) {
+                              const at::Tensor& flags, int64_t total_rows, const at::Tensor& t_base,
+                              const at::Tensor& t_row_base, const at::Tensor& t_dim, double lr, double eps,
+                              double grad_scale, const std::optional<at::Tensor>& clip,
+                              const std::optional<at::Tensor>& err, int64_t max_dim) {
+  TORCH_CHECK(flags.scalar_type() == at::kByte && flags.numel() >= (total_rows + 511) / 512 * 512,
+              "flags must be uint8 padded to a multiple of 512 rows");
   mdl::AdagradArgs a;
   a.slab = ptr<float>(slab);
   a.grad_slab = ptr<float>(grad_slab);
   a.acc = ptr<float>(acc);
-  a.flags = ptr<unsigned>(flags);
-  a.touched = ptr<const long long>(touched);
-  a.touched_count = ptr<int>(count);
+  a.flags = ptr<unsigned char>(flags);
+  a.total_rows = total_rows;
+  a.num_tables = static_cast<int>(t_base.numel());
   a.t_base = ptr<const long long>(t_base);
   a.t_row_base = ptr<const long long>(t_row_base);
   a.t_dim = ptr<const int>(t_dim);
@@ -189,28 +187,28 @@ mdl::AdagradArgs adagrad_args(const at::Tensor& slab, const at::Tensor& grad_sla
   a.eps = static_cast<float>(eps);
   a.grad_scale = static_cast<float>(grad_scale);
   a.clip_scale = optr<const float>(clip);
-  a.cap = touched.numel();
+  a.max_dim = static_cast<int>(max_dim);
   a.err = optr<int>(err);
   return a;
 }
 
 void adagrad_apply(const at::Tensor& slab, const at::Tensor& grad_slab, const at::Tensor& acc, const at::Tensor& flags,
-                   const at::Tensor& touched, const at::Tensor& count, const at::Tensor& t_base,
-                   const at::Tensor& t_row_base, const at::Tensor& t_dim, double lr, double eps, double grad_scale,
-                   const std::optional<at::Tensor>& clip, const std::optional<at::Tensor>& err) {
+                   int64_t total_rows, const at::Tensor& t_base, const at::Tensor& t_row_base,
+                   const at::Tensor& t_dim, double lr, double eps, double grad_scale,
+                   const std::optional<at::Tensor>& clip, const std::optional<at::Tensor>& err, int64_t max_dim) {
   c10::cuda::CUDAGuard guard(slab.device());
-  auto a = adagrad_args(slab, grad_slab, acc, flags, touched, count, t_base, t_row_base, t_dim, lr, eps, grad_scale,
-                        clip, err);
+  auto a = adagrad_args(slab, grad_slab, acc, flags, total_rows, t_base, t_row_base, t_dim, lr, eps, grad_scale,
+                        clip, err, max_dim);
   check(mdl::rowwise_adagrad_apply(a, stream_of(slab)), "rowwise_adagrad_apply");
   g_launches += 1;
 }
 
-void touched_sqnorm(const at::Tensor& grad_slab, const at::Tensor& touched, const at::Tensor& count,
+void touched_sqnorm(const at::Tensor& grad_slab, const at::Tensor& flags, int64_t total_rows,
                     const at::Tensor& t_base, const at::Tensor& t_row_base, const at::Tensor& t_dim, double grad_scale,
                     const at::Tensor& out) {
   c10::cuda::CUDAGuard guard(grad_slab.device());
-  mdl::AdagradArgs a = adagrad_args(grad_slab, grad_slab, grad_slab, grad_slab, touched, count, t_base, t_row_base,
-                                    t_dim, 0.0, 1.0, grad_scale, std::nullopt, std::nullopt);
+  mdl::AdagradArgs a = adagrad_args(grad_slab, grad_slab, grad_slab, flags, total_rows, t_base, t_row_base, t_dim,
+                                    0.0, 1.0, grad_scale, std::nullopt, std::nullopt, 1024);
   check(mdl::touched_grad_sqnorm(a, ptr<float>(out), stream_of(grad_slab)), "touched_grad_sqnorm");
   g_launches += 1;
 }

@@ -18,9 +18,9 @@
 //
 // The backward pushes each id's gradient into the owner's fp32 grad slab with
 // vector reductions (red.add.v4.f32, system scope when peers are involved) and
-// records each newly touched row once in the owner's fixed-capacity touched
-// list (overflow is reported through the error word). After a device-side
-// barrier the owner applies row-wise Adagrad to exactly those rows.
+// marks the row in the owner's touched-row byte flags (a plain store: no
+// atomic counter, no capacity limit). After a device-side barrier the owner
+// scans its flags and applies row-wise Adagrad to exactly those rows.
 #include "common.cuh"
 #include "embedding.h"
 
@@ -28,7 +28,6 @@ namespace mdl {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kMaxVec = 8;  // float4 vectors per lane -> width <= 32 * lanes... see f_lanes
 
 __device__ __forceinline__ long long find_feature(const long long* prefix, int nf, long long w) {
   int lo = 0, hi = nf;  // find f with prefix[f] <= w < prefix[f+1]
@@ -119,14 +118,20 @@ __device__ __forceinline__ BagCtx bag_of_lane(const EmbPlan& p) {
 
 __device__ __forceinline__ void route(const EmbPlan& p, int t, long long id, int& owner, long long& row) {
   if (__ldg(p.t_mode + t) == 0) {
-    owner = static_cast<int>((id + __ldg(p.t_cyc + t)) % p.world);
-    row = id / p.world;
+    if (p.world == 1) {
+      owner = 0;
+      row = id;
+    } else {
+      owner = static_cast<int>((id + __ldg(p.t_cyc + t)) % p.world);
+      row = id / p.world;
+    }
   } else {
     owner = __ldg(p.t_owner + t);
     row = id;
   }
 }
 
+template <int NV>  // float4 vectors per lane: width <= 4 * lanes * NV
 __global__ void __launch_bounds__(kThreads) emb_pool_fwd_kernel(const EmbPlan p, long long total_chunks) {
   const long long warp = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
   if (warp >= total_chunks) return;
@@ -136,15 +141,15 @@ __global__ void __launch_bounds__(kThreads) emb_pool_fwd_kernel(const EmbPlan p,
   const int width = __ldg(p.f_width + f);
   const int t = __ldg(p.f_table + f);
   const int pool = __ldg(p.f_pool + f);
-  float acc[kMaxVec][4];
+  float acc[NV][4];
 #pragma unroll
-  for (int i = 0; i < kMaxVec; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  for (int i = 0; i < NV; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
   const int stride_cols = 4 * b.lanes;
   int count = 0;
   if (t < 0) {
     const float* src = p.dense + b.bag_local * p.dense_ld + __ldg(p.f_dense_col + f);
 #pragma unroll
-    for (int i = 0; i < kMaxVec; ++i) {
+    for (int i = 0; i < NV; ++i) {
       const int col = b.sl * 4 + i * stride_cols;
       if (col < width)
         for (int j = 0; j < 4; ++j) acc[i][j] = (col + j < width) ? __ldg(src + col + j) : 0.f;
@@ -170,7 +175,7 @@ __global__ void __launch_bounds__(kThreads) emb_pool_fwd_kernel(const EmbPlan p,
       route(p, t, id, owner, row);
       const float* src = p.slabs[owner] + tbase + row * dim;
 #pragma unroll
-      for (int i = 0; i < kMaxVec; ++i) {
+      for (int i = 0; i < NV; ++i) {
         const int col = b.sl * 4 + i * stride_cols;
         if (col < dim) {
           const float4 v = *reinterpret_cast<const float4*>(src + col);
@@ -183,7 +188,7 @@ __global__ void __launch_bounds__(kThreads) emb_pool_fwd_kernel(const EmbPlan p,
     if (pool == 1 && count > 0) {
       const float inv = 1.f / static_cast<float>(count);
 #pragma unroll
-      for (int i = 0; i < kMaxVec; ++i)
+      for (int i = 0; i < NV; ++i)
         for (int j = 0; j < 4; ++j) acc[i][j] *= inv;
     }
   }
@@ -192,13 +197,13 @@ __global__ void __launch_bounds__(kThreads) emb_pool_fwd_kernel(const EmbPlan p,
   const int c0 = __ldg(p.f_out_col + f);
   const int slice = __ldg(p.f_slice + f), sstride = __ldg(p.f_slice_stride + f);
 #pragma unroll
-  for (int i = 0; i < kMaxVec; ++i) {
+  for (int i = 0; i < NV; ++i) {
     const int col = b.sl * 4 + i * stride_cols;
     if (col < width) store4_bf16(out, row_off, c0 + col, slice, sstride, min(4, width - col), acc[i]);
   }
 }
 
-template <bool SYS>
+template <bool SYS, int NV>
 __global__ void __launch_bounds__(kThreads)
     emb_pool_bwd_kernel(const EmbPlan p, const __nv_bfloat16* __restrict__ grad_out, long long total_chunks) {
   const long long warp = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
@@ -228,13 +233,13 @@ __global__ void __launch_bounds__(kThreads)
     scale = 1.f / static_cast<float>(count);
   }
   const int stride_cols = 4 * b.lanes;
-  float g[kMaxVec][4];
+  float g[NV][4];
   const long long row_off = b.bag_local * __ldg(p.f_out_ld + f);
   const int c0 = __ldg(p.f_out_col + f);
   const int slice = __ldg(p.f_slice + f), sstride = __ldg(p.f_slice_stride + f);
   const __nv_bfloat16* gbase = grad_out + __ldg(p.f_out_base + f);
 #pragma unroll
-  for (int i = 0; i < kMaxVec; ++i) {
+  for (int i = 0; i < NV; ++i) {
     const int col = b.sl * 4 + i * stride_cols;
     if (col < dim) {
       load4_bf16(gbase, row_off, c0 + col, slice, sstride, min(4, dim - col), g[i]);
@@ -249,42 +254,70 @@ __global__ void __launch_bounds__(kThreads)
     route(p, t, id, owner, row);
     float* dst = p.grad_slabs[owner] + tbase + row * dim;
 #pragma unroll
-    for (int i = 0; i < kMaxVec; ++i) {
+    for (int i = 0; i < NV; ++i) {
       const int col = b.sl * 4 + i * stride_cols;
       if (col < dim) red_add4<SYS>(dst + col, g[i]);
     }
-    if (b.sl == 0) {
-      const long long rs = rbase + row;
-      unsigned prev;
-      if (SYS) prev = atomicExch_system(p.flags[owner] + rs, 1u);
-      else prev = atomicExch(p.flags[owner] + rs, 1u);
-      if (prev == 0u) {
-        const int idx = SYS ? atomicAdd_system(p.touched_count[owner], 1) : atomicAdd(p.touched_count[owner], 1);
-        if (idx < p.touched_cap) p.touched[owner][idx] = (static_cast<long long>(t) << 40) | row;
-        else record_error(p.err, MDL_ERR_CAPACITY);
-      }
-    }
+    // Mark the row touched: an idempotent byte store (no atomic, no shared counter).
+    if (b.sl == 0) *reinterpret_cast<volatile unsigned char*>(p.flags[owner] + rbase + row) = 1;
     if (pool == 0) break;
   }
 }
 
+// Walk the touched-row byte flags of this rank in warp-sized chunks of 512 rows
+// (each lane tests 16 flags with one 16-byte load) and call `fn(rs)` with the
+// whole warp for every touched row-space index, in ballot order.
+template <typename F>
+__device__ __forceinline__ void for_each_touched(const AdagradArgs& a, F&& fn) {
+  const int lane = threadIdx.x & 31;
+  const long long nwarps = static_cast<long long>(gridDim.x) * (blockDim.x / 32);
+  const long long nchunks = (a.total_rows + 511) / 512;
+  for (long long chunk = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; chunk < nchunks;
+       chunk += nwarps) {
+    const uint4 f = *reinterpret_cast<const uint4*>(a.flags + chunk * 512 + lane * 16);
+    unsigned mask = 0;
+    const unsigned words[4] = {f.x, f.y, f.z, f.w};
+#pragma unroll
+    for (int w = 0; w < 4; ++w)
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if ((words[w] >> (8 * k)) & 0xffu) mask |= 1u << (4 * w + k);
+    while (true) {
+      const unsigned ballot = __ballot_sync(0xffffffffu, mask != 0);
+      if (ballot == 0) break;
+      const int src = __ffs(ballot) - 1;
+      const unsigned m = __shfl_sync(0xffffffffu, mask, src);
+      const int bit = __ffs(m) - 1;
+      if (lane == src) mask &= ~(1u << bit);
+      fn(chunk * 512 + src * 16 + bit);
+    }
+  }
+}
+
+// Table of a row-space index (warp-uniform binary search over t_row_base).
+__device__ __forceinline__ int table_of_row(const AdagradArgs& a, long long rs) {
+  int lo = 0, hi = a.num_tables;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (__ldg(a.t_row_base + mid) <= rs) lo = mid; else hi = mid;
+  }
+  return lo;
+}
+
+template <int NV>  // dim <= 128 * NV
 __global__ void __launch_bounds__(kThreads) rowwise_adagrad_kernel(const AdagradArgs a) {
   const int lane = threadIdx.x & 31;
-  const long long warps = static_cast<long long>(gridDim.x) * (kThreads / 32);
-  const long long n = min(static_cast<long long>(*a.touched_count), a.cap);
   const float clip = a.clip_scale != nullptr ? *a.clip_scale : 1.f;
   const float gscale = a.grad_scale * clip;
-  for (long long e = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5; e < n; e += warps) {
-    const long long packed = a.touched[e];
-    const int t = static_cast<int>(packed >> 40);
-    const long long row = packed & ((1ll << 40) - 1);
+  for_each_touched(a, [&](long long rs) {
+    const int t = table_of_row(a, rs);
+    const long long row = rs - __ldg(a.t_row_base + t);
     const int dim = __ldg(a.t_dim + t);
     const long long base = __ldg(a.t_base + t) + row * dim;
-    const long long rs = __ldg(a.t_row_base + t) + row;
-    float g[kMaxVec][4];
+    float g[NV][4];
     float sq = 0.f;
 #pragma unroll
-    for (int i = 0; i < kMaxVec; ++i) {
+    for (int i = 0; i < NV; ++i) {
       const int col = lane * 4 + i * 128;
       if (col < dim) {
         const float4 v = *reinterpret_cast<const float4*>(a.grad_slab + base + col);
@@ -297,12 +330,12 @@ __global__ void __launch_bounds__(kThreads) rowwise_adagrad_kernel(const Adagrad
     if (lane == 0) {
       acc = a.acc[rs] + sq / static_cast<float>(dim);
       a.acc[rs] = acc;
-      a.flags[rs] = 0u;
+      a.flags[rs] = 0;
     }
     acc = __shfl_sync(0xffffffffu, acc, 0);
     const float step = a.lr / (sqrtf(acc) + a.eps);
 #pragma unroll
-    for (int i = 0; i < kMaxVec; ++i) {
+    for (int i = 0; i < NV; ++i) {
       const int col = lane * 4 + i * 128;
       if (col < dim) {
         float4* w = reinterpret_cast<float4*>(a.slab + base + col);
@@ -312,36 +345,45 @@ __global__ void __launch_bounds__(kThreads) rowwise_adagrad_kernel(const Adagrad
         *reinterpret_cast<float4*>(a.grad_slab + base + col) = make_float4(0.f, 0.f, 0.f, 0.f);
       }
     }
-  }
+  });
 }
 
 __global__ void __launch_bounds__(kThreads) touched_sqnorm_kernel(const AdagradArgs a, float* out_sq) {
   const int lane = threadIdx.x & 31;
-  const long long warps = static_cast<long long>(gridDim.x) * (kThreads / 32);
-  const long long n = min(static_cast<long long>(*a.touched_count), a.cap);
   float sq = 0.f;
-  for (long long e = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5; e < n; e += warps) {
-    const long long packed = a.touched[e];
-    const int t = static_cast<int>(packed >> 40);
-    const long long row = packed & ((1ll << 40) - 1);
+  for_each_touched(a, [&](long long rs) {
+    const int t = table_of_row(a, rs);
+    const long long row = rs - __ldg(a.t_row_base + t);
     const int dim = __ldg(a.t_dim + t);
     const long long base = __ldg(a.t_base + t) + row * dim;
     for (int col = lane * 4; col < dim; col += 128) {
       const float4 v = *reinterpret_cast<const float4*>(a.grad_slab + base + col);
       sq += (v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w) * a.grad_scale * a.grad_scale;
     }
-  }
+  });
   sq = warp_sum(sq);
   if (lane == 0) atomicAdd(out_sq, sq);
 }
 
 int blocks_for(long long warps) { return static_cast<int>((warps * 32 + kThreads - 1) / kThreads); }
 
+int scan_grid(long long total_rows) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long want = blocks_for((total_rows + 511) / 512);
+  return static_cast<int>(want < sms * 8 ? (want > 0 ? want : 1) : sms * 8);
+}
+
 }  // namespace
 
 cudaError_t emb_pool_forward(const EmbPlan& plan, long long total_chunks, cudaStream_t stream) {
   if (total_chunks <= 0) return cudaSuccess;
-  emb_pool_fwd_kernel<<<blocks_for(total_chunks), kThreads, 0, stream>>>(plan, total_chunks);
+  const int grid = blocks_for(total_chunks);
+  if (plan.max_vec <= 1) emb_pool_fwd_kernel<1><<<grid, kThreads, 0, stream>>>(plan, total_chunks);
+  else if (plan.max_vec <= 2) emb_pool_fwd_kernel<2><<<grid, kThreads, 0, stream>>>(plan, total_chunks);
+  else if (plan.max_vec <= 4) emb_pool_fwd_kernel<4><<<grid, kThreads, 0, stream>>>(plan, total_chunks);
+  else emb_pool_fwd_kernel<8><<<grid, kThreads, 0, stream>>>(plan, total_chunks);
   return cudaGetLastError();
 }
 
@@ -349,34 +391,31 @@ cudaError_t emb_pool_backward(const EmbPlan& plan, const void* grad_out, long lo
                               cudaStream_t stream) {
   if (total_chunks <= 0) return cudaSuccess;
   const auto* g = reinterpret_cast<const __nv_bfloat16*>(grad_out);
-  if (plan.world > 1)
-    emb_pool_bwd_kernel<true><<<blocks_for(total_chunks), kThreads, 0, stream>>>(plan, g, total_chunks);
-  else
-    emb_pool_bwd_kernel<false><<<blocks_for(total_chunks), kThreads, 0, stream>>>(plan, g, total_chunks);
+  const int grid = blocks_for(total_chunks);
+#define MDL_BWD(SYS, NV) emb_pool_bwd_kernel<SYS, NV><<<grid, kThreads, 0, stream>>>(plan, g, total_chunks)
+  const int nv = plan.max_vec <= 1 ? 1 : plan.max_vec <= 2 ? 2 : plan.max_vec <= 4 ? 4 : 8;
+  if (plan.world > 1) {
+    if (nv == 1) MDL_BWD(true, 1); else if (nv == 2) MDL_BWD(true, 2); else if (nv == 4) MDL_BWD(true, 4); else MDL_BWD(true, 8);
+  } else {
+    if (nv == 1) MDL_BWD(false, 1); else if (nv == 2) MDL_BWD(false, 2); else if (nv == 4) MDL_BWD(false, 4); else MDL_BWD(false, 8);
+  }
+#undef MDL_BWD
   return cudaGetLastError();
 }
 
 cudaError_t rowwise_adagrad_apply(const AdagradArgs& a, cudaStream_t stream) {
-  if (a.cap <= 0) return cudaSuccess;
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const long long want = blocks_for(a.cap);
-  const int grid = static_cast<int>(want < sms * 8 ? want : sms * 8);
-  rowwise_adagrad_kernel<<<grid, kThreads, 0, stream>>>(a);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
-  return cudaMemsetAsync(a.touched_count, 0, sizeof(int), stream);
+  if (a.total_rows <= 0) return cudaSuccess;
+  const int grid = scan_grid(a.total_rows);
+  if (a.max_dim <= 128) rowwise_adagrad_kernel<1><<<grid, kThreads, 0, stream>>>(a);
+  else if (a.max_dim <= 256) rowwise_adagrad_kernel<2><<<grid, kThreads, 0, stream>>>(a);
+  else if (a.max_dim <= 512) rowwise_adagrad_kernel<4><<<grid, kThreads, 0, stream>>>(a);
+  else rowwise_adagrad_kernel<8><<<grid, kThreads, 0, stream>>>(a);
+  return cudaGetLastError();
 }
 
 cudaError_t touched_grad_sqnorm(const AdagradArgs& a, float* out_sq, cudaStream_t stream) {
-  if (a.cap <= 0) return cudaSuccess;
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const long long want = blocks_for(a.cap);
-  const int grid = static_cast<int>(want < sms * 8 ? want : sms * 8);
-  touched_sqnorm_kernel<<<grid, kThreads, 0, stream>>>(a, out_sq);
+  if (a.total_rows <= 0) return cudaSuccess;
+  touched_sqnorm_kernel<<<scan_grid(a.total_rows), kThreads, 0, stream>>>(a, out_sq);
   return cudaGetLastError();
 }
 

@@ -18,6 +18,7 @@ struct EmbPlan {
   int num_features = 0;
   int world = 1;
   int rank = 0;
+  int max_vec = 8;  // max over features of ceil(width / (4 * lanes)) (selects the kernel variant)
   // work list: feature f owns warp-chunks [f_chunk_prefix[f], f_chunk_prefix[f+1])
   const long long* f_chunk_prefix = nullptr;  // [F+1]
   const long long* f_bag_prefix = nullptr;    // [F+1] first global bag of feature f
@@ -29,7 +30,7 @@ struct EmbPlan {
   const int* f_hash = nullptr;         // 0 ids used as-is, 1 pre_hashed low bits (+1)
   const long long* f_buckets = nullptr;// pre_hashed bucket count (power of two)
   const int* f_width = nullptr;        // output width (embedding dim or dense width)
-  const int* f_lanes = nullptr;        // lanes per bag (power of two, width <= 4*lanes*iters)
+  const int* f_lanes = nullptr;        // lanes per bag (power of two)
   const long long* f_out_base = nullptr;  // element offset of the feature's output matrix
   const long long* f_out_ld = nullptr;    // row stride of that matrix (elements)
   const int* f_out_col = nullptr;      // first logical column of the feature
@@ -47,10 +48,7 @@ struct EmbPlan {
   // peer-visible buffers, one pointer per rank (index = rank)
   float* slabs[kMaxWorld] = {};
   float* grad_slabs[kMaxWorld] = {};
-  unsigned* flags[kMaxWorld] = {};
-  long long* touched[kMaxWorld] = {};
-  int* touched_count[kMaxWorld] = {};
-  long long touched_cap = 0;
+  unsigned char* flags[kMaxWorld] = {};  // touched-row byte flags, indexed by row space
   // dense inputs (fp32 [rows, dense_ld]) and the pooled output (bf16)
   const float* dense = nullptr;
   long long dense_ld = 0;
@@ -68,21 +66,23 @@ cudaError_t emb_pool_backward(const EmbPlan& plan, const void* grad_out, long lo
 
 // Row-wise Adagrad over this rank's touched rows (reference optim.py:31-62):
 //   g = grad * grad_scale * clip_scale[0]; acc += mean(g^2); w -= lr * g / (sqrt(acc) + eps)
-// then zero the grad rows, clear the flags and reset the touched count.
+// then zero the grad rows and clear the flags. Touched rows are found by a
+// scan of the byte flags (16 per lane per load), so the backward needs no
+// shared counter and there is no capacity limit.
 struct AdagradArgs {
-  float* slab;
-  float* grad_slab;
-  float* acc;            // fp32 [row space]
-  unsigned* flags;
-  const long long* touched;
-  int* touched_count;
-  const long long* t_base;
-  const long long* t_row_base;
-  const int* t_dim;
-  float lr, eps, grad_scale;
-  const float* clip_scale;  // optional device scalar (nullptr = 1)
-  long long cap;
-  int* err;
+  float* slab = nullptr;
+  float* grad_slab = nullptr;
+  float* acc = nullptr;              // fp32 [row space]
+  unsigned char* flags = nullptr;    // [row space, padded to a multiple of 512]
+  long long total_rows = 0;
+  int num_tables = 0;
+  const long long* t_base = nullptr;
+  const long long* t_row_base = nullptr;
+  const int* t_dim = nullptr;
+  float lr = 0.f, eps = 1e-10f, grad_scale = 1.f;
+  const float* clip_scale = nullptr;  // optional device scalar (nullptr = 1)
+  int max_dim = 1024;                 // widest table (selects the kernel variant)
+  int* err = nullptr;
 };
 cudaError_t rowwise_adagrad_apply(const AdagradArgs& a, cudaStream_t stream);
 

@@ -7,11 +7,11 @@
 // these as cuBLAS strided-batched GEMMs through torch.bmm
 // (src/modules/mlp.py:187-207, PerTokenLinear src/modules/mlp.py:30-42).
 //
-// Roles inside one CTA (320 threads, one CTA per SM):
+// Roles inside one CTA (576 threads, one CTA per SM):
 //   warp 0      : TMA producer (one lane) filling a STAGES-deep smem ring
 //   warp 1      : MMA issuer (one lane) + TMEM allocator
-//   warps 2..9  : epilogue; warp w reads TMEM lane quarter (w % 4) and one
-//                 half (128 columns) of the 256-column accumulator
+//   warps 2..17 : epilogue; warp w reads TMEM lane quarter (w % 4) and one
+//                 quarter (64 columns) of the 256-column accumulator
 // The accumulator is double-buffered in TMEM (2 x 256 fp32 columns) so the
 // epilogue of tile i overlaps the main loop of tile i+1.
 #include <cudaTypedefs.h>
@@ -31,7 +31,7 @@ constexpr int STAGES = 4;
 constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KB
 constexpr int B_STAGE_BYTES = BN * BK * 2;  // 32 KB
 constexpr int TMEM_COLS = 2 * BN;           // double-buffered accumulator
-constexpr int NUM_EPI_WARPS = 8;                 // two warps per TMEM lane quarter
+constexpr int NUM_EPI_WARPS = 16;                // four warps per TMEM lane quarter
 constexpr int NUM_THREADS = 64 + NUM_EPI_WARPS * 32;
 constexpr int MN_CHUNK_BYTES = BK * 128;    // one 64-wide MN chunk of BK rows (MN-major)
 constexpr int SMEM_BYTES =
@@ -231,7 +231,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;            // TMEM lane quarter this warp may read
-    const int half = (warp - 2) / 4;         // which 128-column half of the tile
+    const int cgroup = (warp - 2) / 4;       // which 64-column group of the tile
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -243,7 +243,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int nb = rem - mb * n_tiles;
       const int row = mb * BM + quarter * 32 + lane;
       const bool row_ok = row < ep.M;
-      for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 32) {
+      for (int c0 = cgroup * (BN / 4); c0 < (cgroup + 1) * (BN / 4); c0 += 32) {
         const int col0 = nb * BN + c0;
         if (col0 >= ep.N) break;  // warp-uniform
         float v[32];

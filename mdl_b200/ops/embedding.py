@@ -2,7 +2,7 @@
 
 ``EmbeddingStore`` keeps the local shard of every table of a model in one fp32
 *slab* per rank (plus the fp32 gradient slab, the row-wise Adagrad
-accumulator, touched-row flags and a fixed-capacity touched list). On CUDA
+accumulator and one touched-row byte flag per local row). On CUDA
 with ``world > 1`` those buffers are exported over CUDA IPC and every rank maps
 its peers' buffers, so the lookup kernel loads rows straight from the owner's
 HBM over NVLink and the backward kernel reduces gradients straight into the
@@ -62,7 +62,7 @@ class EmbeddingStore:
 
     def __init__(self, tables: Sequence[tuple[str, int, int]], plan: EmbeddingShardingPlan, *, rank: int,
                  world: int, device: torch.device, init_std: float = 0.02, lr: float = 0.01, eps: float = 1e-10,
-                 initial_accumulator_value: float = 0.1, touched_capacity: int | None = None,
+                 initial_accumulator_value: float = 0.1,
                  process_group=None, base_seed: int | None = None) -> None:
         self.rank = rank
         self.world = world
@@ -84,7 +84,6 @@ class EmbeddingStore:
             rows += local
         self.total_elems = max(elem, 4)
         self.total_rows = max(rows, 1)
-        self.touched_capacity = int(touched_capacity or self.total_rows)
         self._peer_handles: list = []
         self._alloc()
         self.reset_parameters(init_std, base_seed)
@@ -95,6 +94,7 @@ class EmbeddingStore:
     # ------------------------------------------------------------ storage
     def _alloc(self) -> None:
         dev = self.device
+        flag_len = (self.total_rows + 511) // 512 * 512  # the Adagrad scan reads 512 flags per warp
         if dev.type == "cuda" and self.world > 1:
             from ..parallel import symm
 
@@ -102,9 +102,7 @@ class EmbeddingStore:
                 {
                     "slab": (self.total_elems, torch.float32),
                     "grad": (self.total_elems, torch.float32),
-                    "flags": (self.total_rows, torch.int32),
-                    "touched": (self.touched_capacity, torch.int64),
-                    "count": (4, torch.int32),
+                    "flags": (flag_len, torch.uint8),
                 },
                 device=dev,
                 process_group=self.process_group,
@@ -112,19 +110,15 @@ class EmbeddingStore:
             self.slab = self._symm.local("slab")
             self.grad = self._symm.local("grad")
             self.flags = self._symm.local("flags")
-            self.touched = self._symm.local("touched")
-            self.count = self._symm.local("count")
             self.grad.zero_()
             self.flags.zero_()
-            self.count.zero_()
+            torch.cuda.synchronize(dev)
             self._symm.barrier_host()
         else:
             self._symm = None
             self.slab = torch.empty(self.total_elems, dtype=torch.float32, device=dev)
             self.grad = torch.zeros(self.total_elems, dtype=torch.float32, device=dev)
-            self.flags = torch.zeros(self.total_rows, dtype=torch.int32, device=dev)
-            self.touched = torch.zeros(self.touched_capacity, dtype=torch.int64, device=dev)
-            self.count = torch.zeros(4, dtype=torch.int32, device=dev)
+            self.flags = torch.zeros(flag_len, dtype=torch.uint8, device=dev)
         self.acc = torch.empty(self.total_rows, dtype=torch.float32, device=dev)
         # CPU path: dense gradient accumulation per table (sparse rows tracked by a mask)
         self._cpu_touched = torch.zeros(self.total_rows, dtype=torch.bool) if dev.type != "cuda" else None
@@ -182,8 +176,7 @@ class EmbeddingStore:
     def peer_ptrs(self, name: str) -> list[int]:
         if self._symm is not None:
             return self._symm.peer_ptrs(name)
-        return [getattr(self, {"slab": "slab", "grad": "grad", "flags": "flags", "touched": "touched",
-                               "count": "count"}[name]).data_ptr()]
+        return [getattr(self, name).data_ptr()]
 
     # ------------------------------------------------------------ optimizer
     @torch.no_grad()
@@ -205,16 +198,18 @@ class EmbeddingStore:
         norm = None
         if clip_norm is not None:
             sq = torch.zeros(1, dtype=torch.float32, device=self.device)
-            ext().touched_sqnorm(self.grad, self.touched, self.count, m["t_base"], m["t_row_base"], m["t_dim"],
+            ext().touched_sqnorm(self.grad, self.flags, self.total_rows, m["t_base"], m["t_row_base"], m["t_dim"],
                                  grad_scale, sq)
-            if self.world > 1:
+            if self._symm is not None:
+                self._symm.allreduce_small(sq)
+            elif self.world > 1:
                 dist.all_reduce(sq, group=self.process_group)
             clip = torch.empty(1, dtype=torch.float32, device=self.device)
             ext().clip_factor(sq, float(clip_norm), clip)
             norm = sq.sqrt()
-        ext().adagrad_apply(self.slab, self.grad, self.acc, self.flags, self.touched, self.count, m["t_base"],
+        ext().adagrad_apply(self.slab, self.grad, self.acc, self.flags, self.total_rows, m["t_base"],
                             m["t_row_base"], m["t_dim"], float(lr), float(self.eps), grad_scale, clip,
-                            error_word(self.device))
+                            error_word(self.device), max((t.dim for t in self.layouts), default=4))
         if self._symm is not None:
             self._symm.barrier()  # updated rows visible before any peer reads them
         return norm
@@ -345,7 +340,8 @@ class LookupPlan:
             i32([f.dense_col for f in self.features]),
             tm["t_base"], tm["t_row_base"], tm["t_dim"], tm["t_mode"], tm["t_cyc"], tm["t_owner"], tm["t_rows"],
         ]
-        result = (meta, chunk_prefix[-1])
+        max_vec = max([(f.width + 4 * ln - 1) // (4 * ln) for f, ln in zip(self.features, lanes_list)] or [1])
+        result = (meta, chunk_prefix[-1], max_vec)
         self._meta[key] = result
         return result
 
@@ -496,12 +492,12 @@ class _FusedLookup(torch.autograd.Function):
         ctx.store, ctx.plan, ctx.rows = store, plan, rows
         ctx.save_for_backward(ids, offsets)
         if ids.is_cuda:
-            meta, chunks = plan.device_meta(store, rows)
+            meta, chunks, max_vec = plan.device_meta(store, rows)
             out = torch.empty(rows, plan.out_ld, dtype=torch.bfloat16, device=ids.device)
             if plan.slice_k and plan.out_ld != plan.out_width:
                 out.zero_()  # padding columns of the per-token slices must read as zero
             ext().emb_forward(meta, store.peer_ptrs("slab"), store.rank, ids, offsets, dense,
-                              plan.dense_width, out, chunks, error_word(ids.device))
+                              plan.dense_width, out, chunks, error_word(ids.device), max_vec)
             return out
         return lookup_reference(store, plan, ids, offsets, dense, rows, out_dtype=torch.float32)
 
@@ -510,11 +506,10 @@ class _FusedLookup(torch.autograd.Function):
         ids, offsets = ctx.saved_tensors
         store, plan, rows = ctx.store, ctx.plan, ctx.rows
         if ids.is_cuda:
-            meta, chunks = plan.device_meta(store, rows)
+            meta, chunks, max_vec = plan.device_meta(store, rows)
             g = grad_out if grad_out.dtype == torch.bfloat16 else grad_out.to(torch.bfloat16)
             ext().emb_backward(meta, store.peer_ptrs("slab"), store.peer_ptrs("grad"), store.peer_ptrs("flags"),
-                               store.peer_ptrs("touched"), store.peer_ptrs("count"), store.touched_capacity,
-                               store.rank, ids, offsets, g.contiguous(), chunks, error_word(ids.device))
+                               store.rank, ids, offsets, g.contiguous(), chunks, error_word(ids.device), max_vec)
         else:
             backward_reference(store, plan, ids, offsets, grad_out, rows)
         return (None,) * 7
