@@ -431,3 +431,92 @@ cudaError_t rmsnorm_bwd(const RMSArgs& a, cudaStream_t stream) {
 }
 
 }  // namespace mdl
+
+// ---------------------------------------------------------------------------
+// LayerNorm backward for callers that cannot allocate (see norm_noalloc.h):
+// the per-CTA partial sums live in a fixed file-scope device array instead of
+// a caller-provided buffer. Builds on mdl::layernorm_bwd unchanged.
+#include <cstdio>
+#include <mutex>
+
+#include "norm_noalloc.h"
+
+namespace {
+
+constexpr long long kNoAllocScratchFloats = MDL_LN_BWD_NOALLOC_SCRATCH_BYTES / sizeof(float);
+static __device__ __align__(256) float g_ln_bwd_noalloc_scratch[kNoAllocScratchFloats];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+float* g_noalloc_scratch_ptr[kNoAllocMaxDevices] = {};
+thread_local char g_noalloc_message[256] = "";
+
+int noalloc_reject(const char* msg) {
+  std::snprintf(g_noalloc_message, sizeof(g_noalloc_message), "%s", msg);
+  return -1;
+}
+
+// Device address of the scratch array on the current device, looked up once per
+// device (host code only holds a stand-in for the symbol, never its address).
+cudaError_t noalloc_scratch(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_ln_bwd_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    g_noalloc_scratch_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_scratch_ptr[dev];
+  return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" const char* mdl_noalloc_last_error(void) { return g_noalloc_message; }
+
+extern "C" int mdl_layernorm_bwd_noalloc(const void* dy, const void* dy_bcast, float bcast_scale, const void* a,
+                                         const void* b, const float* mean, const float* rstd, const float* gamma,
+                                         void* dx, void* dx2, float* dgamma, float* dbeta, int B, int T, int D,
+                                         int mix, cudaStream_t stream) {
+  g_noalloc_message[0] = '\0';
+  if (B < 0 || T <= 0 || D <= 0 || D % 8 != 0 || D > 2048)
+    return noalloc_reject("mdl_layernorm_bwd_noalloc: need B >= 0, T >= 1 and D a multiple of 8 in [8, 2048]");
+  if (mix && (D % T != 0 || (D / T) % 8 != 0))
+    return noalloc_reject("mdl_layernorm_bwd_noalloc: token mixing needs D / T to be a multiple of 8");
+  if (dy == nullptr && dy_bcast == nullptr)
+    return noalloc_reject("mdl_layernorm_bwd_noalloc: one of dy / dy_bcast is required");
+  const long long per_cta = 2LL * D;  // gamma and beta partial sums of one CTA
+  const long long max_grid = kNoAllocScratchFloats / per_cta;
+  if (max_grid < 1) return noalloc_reject("mdl_layernorm_bwd_noalloc: D exceeds the 2 MiB scratch array");
+  if (B == 0) return 0;
+  float* scratch = nullptr;
+  cudaError_t e = noalloc_scratch(&scratch);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  int grid = mdl::layernorm_bwd_grid(B);
+  if (grid > max_grid) grid = static_cast<int>(max_grid);
+  mdl::LNBwdArgs args;
+  args.dy = dy;
+  args.dy_bcast = dy_bcast;
+  args.bcast_scale = bcast_scale;
+  args.a = a;
+  args.b = b;
+  args.mean = mean;
+  args.rstd = rstd;
+  args.gamma = gamma;
+  args.dx = dx;
+  args.dx2 = dx2;
+  args.partials = scratch;
+  args.dgamma = dgamma;
+  args.dbeta = dbeta;
+  args.B = B;
+  args.T = T;
+  args.D = D;
+  args.mix = mix ? 1 : 0;
+  args.grid = grid;
+  e = mdl::layernorm_bwd(args, stream);
+  return e == cudaSuccess ? 0 : static_cast<int>(e);
+}
