@@ -1,0 +1,244 @@
+"""Reference arm of ``bench.py``: the unmodified reference trained on the same workload.
+
+The reference (``wcrmu/MDL``) is installed, unmodified, under ``baseline/_ref`` (package
+``src``). Everything on the timed path is the reference's own code: its config loader
+(``src.config.load_app_config``), model factory run on the destination device
+(``src.train._build_model_on_device`` -> ``src.model.build_model``), parameter
+classification and DDP preparation (``_classify_model_parameters``,
+``_prepare_forward_model``, incl. its CUDA-graph backbone prewarm), optimizers
+(``_build_dense_optimizer`` RMSprop, ``src.optim.ShardedRowWiseAdagrad``), autocast
+context and loss (``_autocast_context``, ``_loss_terms_from_batch``), and its batch
+container / H2D helpers (``src.dataloader.FeatureBatch``, ``pin_feature_batch``,
+``move_feature_batch``). The step body mirrors the reference hot loop
+(``src/train.py:6996-7190``): zero_grad -> autocast forward + loss -> backward ->
+optimizer steps.
+
+The workload is BASELINE config 2 built by ``mdl_b200.data.baseline_configs`` with two
+adjustments the reference needs: bag pooling ``mean`` (it has no ``sum``; same cost) and
+its production ``runtime.cuda_graph_backbone: true``. Synthetic batches come from the
+same generator as our arm and are converted to the reference's ``FeatureBatch``.
+"""
+
+from __future__ import annotations
+
+import copy
+import os
+import sys
+import tempfile
+
+import torch
+import torch.distributed as dist
+import yaml
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REF = os.path.join(HERE, "_ref")
+
+
+def _import_reference():
+    if not os.path.isdir(os.path.join(REF, "src")):
+        raise RuntimeError("reference not installed under baseline/_ref")
+    if REF not in sys.path:
+        sys.path.insert(0, REF)
+    import src.config as rconfig  # noqa: F401
+    import src.dataloader as rdata  # noqa: F401
+    import src.train as rtrain  # noqa: F401
+    from src import optim as roptim  # noqa: F401
+
+    return rconfig, rdata, rtrain, roptim
+
+
+def reference_mapping(mapping: dict, cuda_graphs: bool) -> dict:
+    """Adapt a benchmark mapping to what the reference supports (see module docstring)."""
+
+    m = copy.deepcopy(mapping)
+    for f in m.get("features", []):
+        if f.get("pooling") == "sum":
+            f["pooling"] = "mean"
+    m.setdefault("vocab_strategy", {"defaults": {}, "features": {}})
+    m["runtime"]["cuda_graph_backbone"] = bool(cuda_graphs)
+    m["runtime"]["distributed"] = "none"
+    m["runtime"].pop("kernel_backend", None)
+    m["training"].pop("comm", None)
+    return m
+
+
+def to_feature_batch(rdata, packed, plan, device=None):
+    """Our PackedBatch -> the reference's FeatureBatch (features dict keyed by name)."""
+
+    rows = packed.rows
+    ids = packed.ids
+    off = packed.offsets
+    features = {}
+    for fi, f in enumerate(plan.features):
+        if f.table is None:
+            features[f.name] = packed.dense[:, f.dense_col:f.dense_col + f.width]
+            continue
+        beg = int(off[fi * rows])
+        end = int(off[(fi + 1) * rows])
+        flat = ids[beg:end]
+        if f.pooling == 0:
+            features[f.name] = flat.clone()
+        else:
+            lengths = (off[fi * rows + 1:(fi + 1) * rows + 1] - off[fi * rows:(fi + 1) * rows]).clone()
+            features[f.name] = {"values": flat.clone(), "lengths": lengths}
+    batch = rdata.FeatureBatch(features=features, labels=packed.labels.clone(), label_mask=None,
+                               scenario_id=torch.zeros(rows, dtype=torch.long), group_id=[])
+    if device is not None:
+        batch = rdata.move_feature_batch(batch, device)
+    return batch
+
+
+class ReferenceTrainer:
+    """Builds the reference model + optimizers and runs its training step."""
+
+    def __init__(self, mapping: dict, *, device: torch.device, rank: int, world: int, local: int,
+                 cuda_graphs: bool = True) -> None:
+        rconfig, rdata, rtrain, roptim = _import_reference()
+        self.rdata, self.rtrain = rdata, rtrain
+        ref_map = reference_mapping(mapping, cuda_graphs and device.type == "cuda")
+        with tempfile.NamedTemporaryFile("w", suffix=".yaml", delete=False) as fh:
+            yaml.safe_dump(ref_map, fh)
+            path = fh.name
+        self.config = rconfig.load_app_config(path)
+        os.unlink(path)
+        self.device = device
+        self.context = rtrain.DistributedContext(enabled=world > 1, rank=rank, local_rank=local, world_size=world,
+                                                 device=device)
+        base = rtrain._build_model_on_device(self.config, {}, device)
+        groups = rtrain._classify_model_parameters(base)
+        ignored = (*groups.sparse_sync, *groups.sharded_ddp_ignore)
+        self.model = rtrain._prepare_forward_model(self.config, base, self.context, ignored)
+        self.base = base
+        t = self.config.training
+        self.optimizers = []
+        dense = list(groups.dense_optimizer)
+        if dense:
+            self.optimizers.append(rtrain._build_dense_optimizer(dense, self.config, device))
+        sharded = list(groups.sharded_optimizer)
+        if sharded:
+            lr = t.lr_sparse or t.lr_dense
+            self.optimizers.append(roptim.ShardedRowWiseAdagrad(
+                sharded, lr=lr, lr_decay=t.adagrad_lr_decay, weight_decay=t.adagrad_weight_decay,
+                initial_accumulator_value=t.adagrad_initial_accumulator_value, eps=t.adagrad_eps))
+        if list(groups.embedding_optimizer):
+            raise RuntimeError("benchmark workload expects sharded embeddings only")
+
+    def step(self, batch) -> torch.Tensor:
+        rt = self.rtrain
+        for opt in self.optimizers:
+            opt.zero_grad(set_to_none=True)
+        with rt._autocast_context(self.config, self.device):
+            output = self.model(batch.features, batch.scenario_id)
+            loss, _num, _den = rt._loss_terms_from_batch(
+                output, batch, moe_loss_weight=self.config.model.sparse_moe_loss_weight,
+                loss_reduction=self.config.training.loss_reduction, task_loss_weights=None, rank_active=True,
+                active_rank_count=self.context.world_size)
+        loss.backward()
+        for opt in self.optimizers:
+            opt.step()
+        return loss.detach()
+
+
+def run(args, rank: int, world: int, local: int) -> dict:
+    from mdl_b200.data.baseline_configs import baseline_config
+    from mdl_b200.data.synthetic import BatchPool, SyntheticGenerator
+    from mdl_b200.models.features import FeatureEncoder  # noqa: F401  (plan only, no tables on this path)
+    from mdl_b200.ops.embedding import LookupFeature, LookupPlan, POOL_MEAN, POOL_NONE, POOL_SUM
+    from mdl_b200.utils.clocks import ClockSampler
+
+    device = torch.device("cuda", local)
+    mapping, spec = baseline_config(2, batch=args.batch)
+    torch.manual_seed(1234)
+    trainer = ReferenceTrainer(mapping, device=device, rank=rank, world=world, local=local,
+                               cuda_graphs=not getattr(args, "ref_no_graphs", False))
+    # a lookup plan of the same feature order, only to drive the shared synthetic generator
+    feats, col = [], 0
+    for f in mapping["features"]:
+        if f["kind"] == "dense":
+            feats.append(LookupFeature(f["name"], None, width=f["dimension"], out_col=col, dense_col=0))
+            col += f["dimension"]
+        else:
+            pool = {"none": POOL_NONE, "mean": POOL_MEAN, "sum": POOL_SUM}[f.get("pooling", "none")]
+            feats.append(LookupFeature(f["name"], f["name"], pooling=pool, width=f["embedding_dim"], out_col=col))
+            col += f["embedding_dim"]
+    plan = LookupPlan(feats, out_width=col, dense_width=spec.dense_width)
+    gen = SyntheticGenerator(plan, spec, rank=rank)
+    pool = BatchPool(gen, args.batch, count=args.pool, pin=False)
+    rd = trainer.rdata
+    dev_batches = [to_feature_batch(rd, b, plan, device) for b in pool.batches]
+    host_batches = [rd.pin_feature_batch(to_feature_batch(rd, b, plan)) for b in pool.batches]
+    torch.cuda.synchronize(device)
+
+    for i in range(args.warmup):
+        trainer.step(dev_batches[i % len(dev_batches)])
+    torch.cuda.synchronize(device)
+
+    props = torch.cuda.get_device_properties(device)
+    sampler = ClockSampler(f"GPU-{props.uuid}" if getattr(props, "uuid", None) else local).start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(args.steps):
+        trainer.step(dev_batches[i % len(dev_batches)])
+    end.record()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    ms = _max(start.elapsed_time(end), world)
+
+    loss_host = torch.zeros(args.steps, dtype=torch.float32, pin_memory=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for i in range(args.steps):
+        batch = rd.move_feature_batch(host_batches[i % len(host_batches)], device, non_blocking=True)
+        loss = trainer.step(batch)
+        loss_host[i:i + 1].copy_(loss.reshape(1).float(), non_blocking=True)
+    e2.record()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    ms_e2e = _max(s2.elapsed_time(e2), world)
+    rows_total = args.batch * world * args.steps
+    h2d = pool.batches[0].nbytes()
+    return {
+        "impl": "reference",
+        "metric": "train samples/sec",
+        "value": round(rows_total / (ms / 1000.0), 1),
+        "unit": "samples/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (same generator and seeds as the ours arm); random-init weights",
+        "config": {
+            "model": "rankmixer (BASELINE config 2) on the unmodified reference; bag pooling mean (no sum in the "
+                     "reference); cuda_graph_backbone=" + str(bool(trainer.config.runtime.cuda_graph_backbone)),
+            "global_batch": args.batch * world,
+            "seq_len": None,
+            "parallelism": f"ddp{world}+sharded-embeddings{world}",
+            "l2": "inputs larger than L2 (same batches as the ours arm)",
+        },
+        "clocks": clocks,
+        "e2e": {"value": round(rows_total / (ms_e2e / 1000.0), 1), "unit": "samples/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": 4},
+        "gpu_launches": 0,
+        "final_loss": float(loss_host[-1]),
+    }
+
+
+def _max(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())

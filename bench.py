@@ -158,9 +158,16 @@ def run_ours(args) -> dict:
 
 
 def run_reference(args) -> dict:
-    from baseline import reference_harness
+    """The unmodified reference on the same workload (see baseline/reference_harness.py)."""
 
-    return reference_harness.run(args)
+    try:
+        from baseline import reference_harness
+
+        reference_harness._import_reference()
+    except Exception as error:  # not installed / not importable: report, do not fail the driver
+        return {"impl": "reference", "unavailable": f"reference not importable: {error}"}
+    rank, world, local = _dist_setup(args)
+    return reference_harness.run(args, rank, world, local)
 
 
 def main(argv=None) -> int:
@@ -171,6 +178,7 @@ def main(argv=None) -> int:
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--batch", type=int, default=2048, help="rows per GPU")
     p.add_argument("--pool", type=int, default=4, help="distinct pinned host batches rotated per step")
+    p.add_argument("--ref-no-graphs", action="store_true", help="reference arm: disable its CUDA-graph backbone")
     args = p.parse_args(argv)
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

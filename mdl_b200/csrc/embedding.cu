@@ -348,6 +348,60 @@ __global__ void __launch_bounds__(kThreads) rowwise_adagrad_kernel(const Adagrad
   });
 }
 
+// Thread-per-row variant for narrow tables (dim <= 128): each thread tests 16
+// flags with one coalesced 16-byte load and updates its own touched rows, so
+// all touched rows of a warp are in flight at once. Table row bases are staged
+// in shared memory for the row -> table search.
+__global__ void __launch_bounds__(kThreads) rowwise_adagrad_thread_kernel(const AdagradArgs a) {
+  extern __shared__ long long s_rb[];
+  const bool staged = a.num_tables <= 4096;
+  if (staged)
+    for (int i = threadIdx.x; i < a.num_tables; i += blockDim.x) s_rb[i] = __ldg(a.t_row_base + i);
+  __syncthreads();
+  const float clip = a.clip_scale != nullptr ? *a.clip_scale : 1.f;
+  const float gscale = a.grad_scale * clip;
+  const long long n16 = (a.total_rows + 15) / 16;
+  uint4* flags16 = reinterpret_cast<uint4*>(a.flags);
+  for (long long c = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; c < n16;
+       c += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const uint4 f = flags16[c];
+    if ((f.x | f.y | f.z | f.w) == 0u) continue;
+    const unsigned words[4] = {f.x, f.y, f.z, f.w};
+    for (int k = 0; k < 16; ++k) {
+      if (((words[k >> 2] >> (8 * (k & 3))) & 0xffu) == 0u) continue;
+      const long long rs = c * 16 + k;
+      int lo = 0, hi = a.num_tables;
+      while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        const long long v = staged ? s_rb[mid] : __ldg(a.t_row_base + mid);
+        if (v <= rs) lo = mid; else hi = mid;
+      }
+      const int t = lo;
+      const long long row = rs - (staged ? s_rb[t] : __ldg(a.t_row_base + t));
+      const int dim = __ldg(a.t_dim + t);
+      const long long base = __ldg(a.t_base + t) + row * dim;
+      float sq = 0.f;
+      for (int col = 0; col < dim; col += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(a.grad_slab + base + col);
+        sq += (v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w) * gscale * gscale;
+      }
+      const float acc = a.acc[rs] + sq / static_cast<float>(dim);
+      a.acc[rs] = acc;
+      const float step = a.lr / (sqrtf(acc) + a.eps);
+      for (int col = 0; col < dim; col += 4) {
+        float4* gp = reinterpret_cast<float4*>(a.grad_slab + base + col);
+        const float4 g = *gp;
+        float4* w = reinterpret_cast<float4*>(a.slab + base + col);
+        float4 v = *w;
+        v.x -= step * g.x * gscale; v.y -= step * g.y * gscale; v.z -= step * g.z * gscale; v.w -= step * g.w * gscale;
+        *w = v;
+        *gp = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    flags16[c] = make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
 __global__ void __launch_bounds__(kThreads) touched_sqnorm_kernel(const AdagradArgs a, float* out_sq) {
   const int lane = threadIdx.x & 31;
   float sq = 0.f;
@@ -406,6 +460,16 @@ cudaError_t emb_pool_backward(const EmbPlan& plan, const void* grad_out, long lo
 cudaError_t rowwise_adagrad_apply(const AdagradArgs& a, cudaStream_t stream) {
   if (a.total_rows <= 0) return cudaSuccess;
   const int grid = scan_grid(a.total_rows);
+  if (a.max_dim <= 128) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long long want = ((a.total_rows + 15) / 16 + kThreads - 1) / kThreads;
+    const int tgrid = static_cast<int>(want < sms * 8 ? (want > 0 ? want : 1) : sms * 8);
+    const size_t smem = a.num_tables <= 4096 ? static_cast<size_t>(a.num_tables) * sizeof(long long) : 0;
+    rowwise_adagrad_thread_kernel<<<tgrid, kThreads, smem, stream>>>(a);
+    return cudaGetLastError();
+  }
   if (a.max_dim <= 128) rowwise_adagrad_kernel<1><<<grid, kThreads, 0, stream>>>(a);
   else if (a.max_dim <= 256) rowwise_adagrad_kernel<2><<<grid, kThreads, 0, stream>>>(a);
   else if (a.max_dim <= 512) rowwise_adagrad_kernel<4><<<grid, kThreads, 0, stream>>>(a);

@@ -84,9 +84,11 @@ def _config2_features(num_fields: int = 300, seed: int = 0) -> tuple[list[dict],
     for i in range(num_fields):
         name = f"f{i:03d}"
         is_multi = i in multi
-        feats.append({"name": name, "kind": "categorical", "source": name, "embedding_dim": 64,
-                      "encoding": {"type": "identity", "max_id": vocabs[i]},
-                      "pooling": "sum" if is_multi else "none", "max_length": 20 if is_multi else 1})
+        feat = {"name": name, "kind": "categorical", "source": name, "embedding_dim": 64,
+                "encoding": {"type": "identity", "max_id": vocabs[i]}, "pooling": "sum" if is_multi else "none"}
+        if is_multi:
+            feat["max_length"] = 20
+        feats.append(feat)
         fields[name] = FieldSpec(vocab=vocabs[i], multi_hot=is_multi, min_len=1, max_len=20 if is_multi else 1)
     feats.append({"name": "dense", "kind": "dense", "source": "dense", "dimension": 64, "presence": False})
     return feats, fields
