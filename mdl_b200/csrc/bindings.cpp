@@ -101,8 +101,8 @@ mdl::EmbPlan make_plan(const std::vector<at::Tensor>& meta, const std::vector<in
   //  0 f_chunk_prefix(i64) 1 f_bag_prefix(i64) 2 f_table(i32) 3 f_pool(i32) 4 f_hash(i32) 5 f_buckets(i64)
   //  6 f_width(i32) 7 f_lanes(i32) 8 f_out_base(i64) 9 f_out_ld(i64) 10 f_out_col(i32) 11 f_slice(i32)
   //  12 f_slice_stride(i32) 13 f_dense_col(i32) 14 t_base(i64) 15 t_row_base(i64) 16 t_dim(i32) 17 t_mode(i32)
-  //  18 t_cyc(i32) 19 t_owner(i32) 20 t_rows(i64)
-  TORCH_CHECK(meta.size() == 21, "embedding plan needs 21 metadata tensors");
+  //  18 t_cyc(i32) 19 t_owner(i32) 20 t_rows(i64) 21 t_base_all(i64 [W*T]) 22 t_row_base_all(i64 [W*T])
+  TORCH_CHECK(meta.size() == 23, "embedding plan needs 23 metadata tensors");
   mdl::EmbPlan p;
   p.num_features = static_cast<int>(meta[2].numel());
   p.world = static_cast<int>(slabs.size());
@@ -130,6 +130,10 @@ mdl::EmbPlan make_plan(const std::vector<at::Tensor>& meta, const std::vector<in
   p.t_cyc = dptr<int>(meta[18]);
   p.t_owner = dptr<int>(meta[19]);
   p.t_rows = dptr<long long>(meta[20]);
+  p.num_tables = static_cast<int>(meta[14].numel());
+  p.t_base_all = dptr<long long>(meta[21]);
+  p.t_row_base_all = dptr<long long>(meta[22]);
+  TORCH_CHECK(meta[21].numel() == static_cast<int64_t>(p.num_tables) * p.world, "t_base_all must be [world * T]");
   for (int r = 0; r < p.world; ++r) {
     p.slabs[r] = reinterpret_cast<float*>(slabs[r]);
     if (r < static_cast<int>(grad_slabs.size())) p.grad_slabs[r] = reinterpret_cast<float*>(grad_slabs[r]);

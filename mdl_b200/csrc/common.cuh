@@ -99,7 +99,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* desc) {
 }
 
 // 3D tiled TMA load into this CTA's shared memory, completion on `bar`.
-// No multicast: every CTA fetches its own tiles.
+// Every CTA fetches its own tiles; nothing is shared across a cluster.
 __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* desc, uint64_t* bar,
                                             int c0, int c1, int c2) {
   asm volatile(

@@ -159,7 +159,7 @@ __global__ void __launch_bounds__(kThreads) emb_pool_fwd_kernel(const EmbPlan p,
     const int hmode = __ldg(p.f_hash + f);
     const long long buckets = __ldg(p.f_buckets + f);
     const long long rows = __ldg(p.t_rows + t);
-    const long long tbase = __ldg(p.t_base + t);
+    // the element base of the table differs per rank: use the OWNER's layout (t_base_all[owner][t])
     const int dim = __ldg(p.t_dim + t);
     const long long beg = __ldg(p.id_offsets + b.gbag);
     const long long end = __ldg(p.id_offsets + b.gbag + 1);
@@ -173,7 +173,7 @@ __global__ void __launch_bounds__(kThreads) emb_pool_fwd_kernel(const EmbPlan p,
       int owner;
       long long row;
       route(p, t, id, owner, row);
-      const float* src = p.slabs[owner] + tbase + row * dim;
+      const float* src = p.slabs[owner] + __ldg(p.t_base_all + owner * p.num_tables + t) + row * dim;
 #pragma unroll
       for (int i = 0; i < NV; ++i) {
         const int col = b.sl * 4 + i * stride_cols;
@@ -217,8 +217,6 @@ __global__ void __launch_bounds__(kThreads)
   const int hmode = __ldg(p.f_hash + f);
   const long long buckets = __ldg(p.f_buckets + f);
   const long long rows = __ldg(p.t_rows + t);
-  const long long tbase = __ldg(p.t_base + t);
-  const long long rbase = __ldg(p.t_row_base + t);
   const int dim = __ldg(p.t_dim + t);
   const long long beg = __ldg(p.id_offsets + b.gbag);
   const long long end = __ldg(p.id_offsets + b.gbag + 1);
@@ -252,14 +250,15 @@ __global__ void __launch_bounds__(kThreads)
     int owner;
     long long row;
     route(p, t, id, owner, row);
-    float* dst = p.grad_slabs[owner] + tbase + row * dim;
+    float* dst = p.grad_slabs[owner] + __ldg(p.t_base_all + owner * p.num_tables + t) + row * dim;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const int col = b.sl * 4 + i * stride_cols;
       if (col < dim) red_add4<SYS>(dst + col, g[i]);
     }
     // Mark the row touched: an idempotent byte store (no atomic, no shared counter).
-    if (b.sl == 0) *reinterpret_cast<volatile unsigned char*>(p.flags[owner] + rbase + row) = 1;
+    if (b.sl == 0)
+      *reinterpret_cast<volatile unsigned char*>(p.flags[owner] + __ldg(p.t_row_base_all + owner * p.num_tables + t) + row) = 1;
     if (pool == 0) break;
   }
 }

@@ -45,6 +45,10 @@ struct EmbPlan {
   const int* t_cyc = nullptr;          // row-wise cyclic offset
   const int* t_owner = nullptr;        // table-wise owner rank
   const long long* t_rows = nullptr;   // global row count (bounds check)
+  // layouts of EVERY rank (local row counts differ per rank): [world * num_tables]
+  int num_tables = 0;
+  const long long* t_base_all = nullptr;      // t_base_all[r * T + t]: element base of table t in rank r's slab
+  const long long* t_row_base_all = nullptr;  // t_row_base_all[r * T + t]: its row-space base on rank r
   // peer-visible buffers, one pointer per rank (index = rank)
   float* slabs[kMaxWorld] = {};
   float* grad_slabs[kMaxWorld] = {};

@@ -121,6 +121,27 @@ class PackedBatch:
         dst._flat[1].copy_(self._flat[1], non_blocking=non_blocking)
         return dst
 
+    def slice_rows(self, start: int, stop: int, num_features: int) -> "PackedBatch":
+        """Rows ``[start, stop)`` as a new packed batch (host tensors; ids re-based per feature)."""
+
+        rows = self.rows
+        n = stop - start
+        off = self.offsets.cpu()
+        ids = self.ids.cpu()
+        id_parts, len_parts = [], []
+        for f in range(num_features):
+            seg = off[f * rows + start:f * rows + stop + 1]
+            id_parts.append(ids[int(seg[0]):int(seg[-1])])
+            len_parts.append(seg[1:] - seg[:-1])
+        offsets = torch.zeros(num_features * n + 1, dtype=torch.int64)
+        if len_parts:
+            offsets[1:] = torch.cumsum(torch.cat(len_parts), 0)
+        cut = lambda t: None if t is None else t.cpu()[start:stop].clone()
+        seqs = {name: {k: v.cpu()[start:stop].clone() for k, v in seq.items()} for name, seq in self.sequences.items()}
+        return PackedBatch.pack(torch.cat(id_parts) if id_parts else torch.zeros(0, dtype=torch.int64), offsets,
+                                cut(self.dense), cut(self.labels), cut(self.label_mask), cut(self.scenario_id), n,
+                                seqs)
+
     def pin_memory(self) -> "PackedBatch":
         if self._flat and self._flat[0].is_pinned():
             return self

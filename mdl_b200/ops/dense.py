@@ -196,6 +196,23 @@ class DenseParams:
         self.grad.zero_()
         return norm
 
+    @torch.no_grad()
+    def gather_master(self) -> torch.Tensor:
+        """The full fp32 master vector on every rank.
+
+        With the fused NVLink update each rank keeps the authoritative fp32 copy of
+        its own slice only (peers receive the bf16 shadow, plus fp32 for the
+        non-GEMM parameters); this all-gathers the owned slices.
+        """
+
+        if self._symm is None or self.world == 1:
+            return self.master
+        chunk = self.total // self.world
+        mine = self.master[self.rank * chunk:(self.rank + 1) * chunk].contiguous()
+        full = torch.empty_like(self.master)
+        dist.all_gather_into_tensor(full, mine, group=self.group)
+        return full
+
     def state_dict(self) -> dict:
         return {
             "params": {n: self.master[self.offsets[n]:self.offsets[n] + p.numel()].view_as(p).detach().cpu().clone()

@@ -84,12 +84,35 @@ class EmbeddingStore:
             rows += local
         self.total_elems = max(elem, 4)
         self.total_rows = max(rows, 1)
+        # Every rank's layout (local row counts differ per rank): kernels that reach a
+        # peer's slab must use the OWNER's table bases.
+        self.base_all: list[list[int]] = []
+        self.row_base_all: list[list[int]] = []
+        for r in range(world):
+            e = rw = 0
+            bases, rbases = [], []
+            for name, num, dim in tables:
+                local = plan.tables[name].local_rows(int(num), r)
+                bases.append(e)
+                rbases.append(rw)
+                e += ((local * int(dim) + 3) // 4) * 4
+                rw += local
+            self.base_all.append(bases)
+            self.row_base_all.append(rbases)
         self._peer_handles: list = []
         self._alloc()
         self.reset_parameters(init_std, base_seed)
         self.acc.fill_(initial_accumulator_value)
         self._meta_cache: dict = {}
         self.step_count = 0
+        self.sync_peers()
+
+    def sync_peers(self) -> None:
+        """Make this rank's table writes visible before any peer reads them (W > 1 on CUDA)."""
+
+        if self._symm is not None:
+            torch.cuda.synchronize(self.device)
+            self._symm.barrier_host()
 
     # ------------------------------------------------------------ storage
     def _alloc(self) -> None:
@@ -169,6 +192,10 @@ class EmbeddingStore:
                 "t_cyc": torch.tensor([t.spec.cyclic_offset for t in L] or [0], dtype=torch.int32, device=dev),
                 "t_owner": torch.tensor([t.spec.table_owner or 0 for t in L] or [0], dtype=torch.int32, device=dev),
                 "t_rows": torch.tensor([t.num_embeddings for t in L] or [1], dtype=torch.int64, device=dev),
+                "t_base_all": torch.tensor([b for r in self.base_all for b in r] or [0] * self.world,
+                                           dtype=torch.int64, device=dev),
+                "t_row_base_all": torch.tensor([b for r in self.row_base_all for b in r] or [0] * self.world,
+                                               dtype=torch.int64, device=dev),
             }
             self._meta_cache[key] = meta
         return meta
@@ -339,6 +366,7 @@ class LookupPlan:
             i32([self.slice_stride] * F),
             i32([f.dense_col for f in self.features]),
             tm["t_base"], tm["t_row_base"], tm["t_dim"], tm["t_mode"], tm["t_cyc"], tm["t_owner"], tm["t_rows"],
+            tm["t_base_all"], tm["t_row_base_all"],
         ]
         max_vec = max([(f.width + 4 * ln - 1) // (4 * ln) for f, ln in zip(self.features, lanes_list)] or [1])
         result = (meta, chunk_prefix[-1], max_vec)
