@@ -34,6 +34,11 @@ if ROOT not in sys.path:
 
 BASELINE_VALUE = None  # BASELINE.md publishes no B200 number for this workload
 METRIC = "train samples/sec"
+MODEL_DESC = {
+    2: "rankmixer (BASELINE config 2: 300 fields, ~200M x 64 fp32 rows, T=16 D=768 L=2 FFNx4, 2 heads)",
+    3: "mdl_rankmixer (BASELINE config 3: config-2 features + 5 scenes x 4 scenario tokens + global, "
+       "3 task tokens, FiLM scene bias, T=16 D=768 L=2 FFNx4, 3 heads)",
+}
 
 
 def _dist_setup(args):
@@ -73,13 +78,13 @@ def run_ours(args) -> dict:
 
     rank, world, local = _dist_setup(args)
     device = torch.device("cuda", local)
-    mapping, spec = baseline_config(2, batch=args.batch)
+    mapping, spec = baseline_config(args.config, batch=args.batch)
     cfg = app_config_from_mapping(mapping)
     torch.manual_seed(1234)
     pg = dist.group.WORLD if world > 1 else None
     model = build_model(cfg, device=device, rank=rank, world=world, process_group=pg, base_seed=1234)
     trainer = Trainer(cfg, model, device=device, rank=rank, world=world, process_group=pg)
-    gen = SyntheticGenerator(model.encoder.plan, spec, rank=rank)
+    gen = SyntheticGenerator(model.encoder.batch_plan, spec, rank=rank)
     pool = BatchPool(gen, args.batch, count=args.pool, pin=True)
     dev_batches = [b.to(device) for b in pool.batches]
     torch.cuda.synchronize(device)
@@ -141,7 +146,7 @@ def run_ours(args) -> dict:
         "dtype": "bf16",
         "data": "synthetic (seeded Zipf(1.05) ids, N(0,1) dense, labels from a hidden model); random-init weights",
         "config": {
-            "model": "rankmixer (BASELINE config 2: 300 fields, ~200M x 64 fp32 rows, T=16 D=768 L=2 FFNx4, 2 heads)",
+            "model": MODEL_DESC[args.config],
             "global_batch": args.batch * world,
             "seq_len": None,
             "parallelism": f"dp{world}+emb-rowwise/tablewise-mp{world}",
@@ -160,6 +165,8 @@ def run_ours(args) -> dict:
 def run_reference(args) -> dict:
     """The unmodified reference on the same workload (see baseline/reference_harness.py)."""
 
+    if args.config != 2:
+        return {"impl": "reference", "unavailable": f"reference arm is wired for workload 2 only (asked {args.config})"}
     try:
         from baseline import reference_harness
 
@@ -177,6 +184,8 @@ def main(argv=None) -> int:
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--batch", type=int, default=2048, help="rows per GPU")
+    p.add_argument("--config", type=int, default=2, choices=sorted(MODEL_DESC),
+                   help="BASELINE workload (2: RankMixer headline, 3: MDL)")
     p.add_argument("--pool", type=int, default=4, help="distinct pinned host batches rotated per step")
     p.add_argument("--ref-no-graphs", action="store_true", help="reference arm: disable its CUDA-graph backbone")
     args = p.parse_args(argv)

@@ -28,6 +28,12 @@ class ResolvedDomainToken:
     scenario_index: int | None
     important_inputs: tuple[str, ...]
     prior_inputs: tuple[str, ...]
+    inputs: tuple[str, ...] = ()
+
+    def resolved_inputs(self) -> list[str]:
+        """Projector inputs in order: direct, important, prior (duplicates dropped)."""
+
+        return list(dict.fromkeys((*self.inputs, *self.important_inputs, *self.prior_inputs)))
 
 
 @dataclass(frozen=True)
@@ -83,8 +89,12 @@ def sequence_output_dim(config: AppConfig, sequence: SequenceConfig) -> int:
 
 
 def tokenizable_input_names(config: AppConfig) -> tuple[str, ...]:
-    names = [f.name for f in config.features]
-    names += [s.name for s in config.sequences if s.encoder != "raw"]
+    """Inputs that become feature tokens by default: embedding scope ``feature`` or ``shared``
+    (scenario/task-scope inputs only feed MDL domain tokens; reference ``src/config.py:3730-3744``)."""
+
+    keep = ("feature", "shared")
+    names = [f.name for f in config.features if f.embedding_scope in keep]
+    names += [s.name for s in config.sequences if s.encoder != "raw" and s.embedding_scope in keep]
     return tuple(names)
 
 
@@ -123,6 +133,7 @@ def resolve_tokenization(config: AppConfig) -> ResolvedTokenization:
                     scenario_index=index,
                     important_inputs=tuple(spec.important_inputs) if spec else tuple(tok.scenario_token_inputs),
                     prior_inputs=tuple(spec.prior_inputs) if spec else (),
+                    inputs=tuple(spec.inputs) if spec else (),
                 )
             )
     if config.model.use_global_scenario_token:
@@ -134,6 +145,7 @@ def resolve_tokenization(config: AppConfig) -> ResolvedTokenization:
                 scenario_index=None,
                 important_inputs=tuple(spec.important_inputs) if spec else tuple(tok.scenario_token_inputs),
                 prior_inputs=tuple(spec.prior_inputs) if spec else (),
+                inputs=tuple(spec.inputs) if spec else (),
             )
         )
     task_by_name = {t.name: t for t in tok.task_tokens}
@@ -145,6 +157,7 @@ def resolve_tokenization(config: AppConfig) -> ResolvedTokenization:
             important_inputs=tuple(task_by_name[task].important_inputs) if task in task_by_name
             else tuple(tok.task_token_inputs),
             prior_inputs=tuple(task_by_name[task].prior_inputs) if task in task_by_name else (),
+            inputs=tuple(task_by_name[task].inputs) if task in task_by_name else (),
         )
         for task in config.task_names
     )

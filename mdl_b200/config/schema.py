@@ -136,8 +136,11 @@ def build_dataclass(cls: type, mapping: Mapping[str, Any], path: str = "") -> An
     unknown = sorted(set(mapping) - names)
     if unknown:
         raise ConfigError(f"{path or cls.__name__}: unknown key(s) {unknown}")
+    legacy = getattr(cls, "_legacy_values", {})
     kwargs = {}
     for key, value in mapping.items():
+        if key in legacy and isinstance(value, str):
+            value = legacy[key].get(value, value)
         kwargs[key] = _convert(hints[key], value, f"{path}.{key}" if path else key)
     try:
         return cls(**kwargs)
@@ -352,6 +355,7 @@ class TokenGroupConfig:
 @_frozen
 class DomainTokenConfig:
     name: str
+    inputs: tuple[str, ...] = ()
     important_inputs: tuple[str, ...] = ()
     prior_inputs: tuple[str, ...] = ()
 
@@ -413,6 +417,9 @@ class RuntimeConfig:
 # -------------------------------------------------------------------- model
 @_frozen
 class ModelConfig:
+    # old spellings accepted by the reference loader (src/config.py:2558-2564)
+    _legacy_values = {"mdl_feature_interaction": {"paper": "direct_ffn", "rankmixer_full": "residual_ffn"}}
+
     name: Literal["rankmixer", "mdl_rankmixer", "onetrans", "mdl_onetrans", "mixformer", "mdl_mixformer", "longer"]
     embedding_dim: int = 32
     token_dim: int = 768
@@ -430,7 +437,7 @@ class ModelConfig:
     use_global_scenario_token: bool = True
     use_task_feature_interaction: bool = True
     use_scenario_feature_interaction: bool = True
-    mdl_feature_interaction: Literal["residual_ffn", "attention", "rankmixer"] = "residual_ffn"
+    mdl_feature_interaction: Literal["direct_ffn", "residual_ffn"] = "residual_ffn"
     mdl_token_state: Literal["coupled", "split"] = "coupled"
     scene_feature_bias: Literal["none", "additive", "film"] = "none"
     tokens_per_scenario: int = 1

@@ -102,7 +102,8 @@ mdl::EmbPlan make_plan(const std::vector<at::Tensor>& meta, const std::vector<in
   //  6 f_width(i32) 7 f_lanes(i32) 8 f_out_base(i64) 9 f_out_ld(i64) 10 f_out_col(i32) 11 f_slice(i32)
   //  12 f_slice_stride(i32) 13 f_dense_col(i32) 14 t_base(i64) 15 t_row_base(i64) 16 t_dim(i32) 17 t_mode(i32)
   //  18 t_cyc(i32) 19 t_owner(i32) 20 t_rows(i64) 21 t_base_all(i64 [W*T]) 22 t_row_base_all(i64 [W*T])
-  TORCH_CHECK(meta.size() == 23, "embedding plan needs 23 metadata tensors");
+  //  23 f_src_bag(i64)
+  TORCH_CHECK(meta.size() == 24, "embedding plan needs 24 metadata tensors");
   mdl::EmbPlan p;
   p.num_features = static_cast<int>(meta[2].numel());
   p.world = static_cast<int>(slabs.size());
@@ -133,6 +134,8 @@ mdl::EmbPlan make_plan(const std::vector<at::Tensor>& meta, const std::vector<in
   p.num_tables = static_cast<int>(meta[14].numel());
   p.t_base_all = dptr<long long>(meta[21]);
   p.t_row_base_all = dptr<long long>(meta[22]);
+  p.f_src_bag = dptr<long long>(meta[23]);
+  TORCH_CHECK(meta[23].numel() == p.num_features, "f_src_bag must have one entry per feature");
   TORCH_CHECK(meta[21].numel() == static_cast<int64_t>(p.num_tables) * p.world, "t_base_all must be [world * T]");
   for (int r = 0; r < p.world; ++r) {
     p.slabs[r] = reinterpret_cast<float*>(slabs[r]);
@@ -507,6 +510,62 @@ void small_allreduce(const std::vector<int64_t>& bufs, const at::Tensor& out, in
   g_launches += 1;
 }
 
+
+// ------------------------------------------------------------------ attention
+mdl::SmallAttnArgs small_attn_args(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
+                                   const at::Tensor& lse, const std::optional<at::Tensor>& key_valid, int64_t B,
+                                   int64_t Nq, int64_t Nk, int64_t H, int64_t hd, double scale) {
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && k.scalar_type() == at::kBFloat16 && v.scalar_type() == at::kBFloat16,
+              "attention operands must be bf16");
+  TORCH_CHECK(q.dim() == 3 && k.dim() == 3 && v.dim() == 3 && o.dim() == 3, "attention tensors are [B, N, D]");
+  TORCH_CHECK(q.stride(2) == 1 && k.stride(2) == 1 && v.stride(2) == 1 && o.stride(2) == 1, "last dim contiguous");
+  TORCH_CHECK(k.stride(0) == v.stride(0) && k.stride(1) == v.stride(1), "K and V must share strides");
+  mdl::SmallAttnArgs a;
+  a.q = q.data_ptr();
+  a.k = k.data_ptr();
+  a.v = v.data_ptr();
+  a.o = o.data_ptr();
+  a.lse = ptr<float>(lse);
+  a.key_valid = optr<const int>(key_valid);
+  a.ldq = q.stride(1);
+  a.ldk = k.stride(1);
+  a.ldo = o.stride(1);
+  a.bsq = q.stride(0);
+  a.bsk = k.stride(0);
+  a.bso = o.stride(0);
+  a.B = static_cast<int>(B);
+  a.Nq = static_cast<int>(Nq);
+  a.Nk = static_cast<int>(Nk);
+  a.H = static_cast<int>(H);
+  a.hd = static_cast<int>(hd);
+  a.scale = static_cast<float>(scale);
+  return a;
+}
+
+void small_attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
+                    const at::Tensor& lse, const std::optional<at::Tensor>& key_valid, int64_t H, double scale) {
+  c10::cuda::CUDAGuard guard(q.device());
+  auto a = small_attn_args(q, k, v, o, lse, key_valid, q.size(0), q.size(1), k.size(1), H, q.size(2) / H, scale);
+  check(mdl::small_attention_fwd(a, stream_of(q)), "small_attention_fwd");
+  g_launches += 1;
+}
+
+void small_attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
+                    const at::Tensor& lse, const std::optional<at::Tensor>& key_valid, const at::Tensor& dout,
+                    const at::Tensor& dq, const at::Tensor& dk, const at::Tensor& dv, int64_t H, double scale) {
+  c10::cuda::CUDAGuard guard(q.device());
+  auto a = small_attn_args(q, k, v, o, lse, key_valid, q.size(0), q.size(1), k.size(1), H, q.size(2) / H, scale);
+  TORCH_CHECK(dout.stride(1) == o.stride(1) && dout.stride(0) == o.stride(0), "dO must share O's strides");
+  TORCH_CHECK(dq.stride(1) == q.stride(1) && dk.stride(1) == k.stride(1) && dv.stride(1) == k.stride(1),
+              "gradients must share their input's strides");
+  a.dout = dout.data_ptr();
+  a.dq = dq.data_ptr();
+  a.dk = dk.data_ptr();
+  a.dv = dv.data_ptr();
+  check(mdl::small_attention_bwd(a, stream_of(q)), "small_attention_bwd");
+  g_launches += 1;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -546,4 +605,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dense_sync", &dense_sync);
   m.def("small_allreduce", &small_allreduce);
   m.def("launch_count", &launch_count);
+  m.def("small_attn_fwd", &small_attn_fwd);
+  m.def("small_attn_bwd", &small_attn_bwd);
 }

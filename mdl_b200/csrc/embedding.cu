@@ -112,7 +112,7 @@ __device__ __forceinline__ BagCtx bag_of_lane(const EmbPlan& p) {
   b.bag_local = chunk * bags_per_warp + sub;
   const long long n_bags = __ldg(p.f_bag_prefix + b.f + 1) - __ldg(p.f_bag_prefix + b.f);
   b.active = b.bag_local < n_bags;
-  b.gbag = __ldg(p.f_bag_prefix + b.f) + b.bag_local;
+  b.gbag = __ldg(p.f_src_bag + b.f) + b.bag_local;
   return b;
 }
 

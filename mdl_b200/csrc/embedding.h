@@ -21,7 +21,9 @@ struct EmbPlan {
   int max_vec = 8;  // max over features of ceil(width / (4 * lanes)) (selects the kernel variant)
   // work list: feature f owns warp-chunks [f_chunk_prefix[f], f_chunk_prefix[f+1])
   const long long* f_chunk_prefix = nullptr;  // [F+1]
-  const long long* f_bag_prefix = nullptr;    // [F+1] first global bag of feature f
+  const long long* f_bag_prefix = nullptr;    // [F+1] prefix of bag counts (work split)
+  const long long* f_src_bag = nullptr;       // [F] first CSR bag of feature f's ids in the batch (several plan
+                                              // features may read one batch feature)
   const long long* id_offsets = nullptr;      // [total_bags+1] CSR offsets into ids
   const long long* ids = nullptr;             // raw ids (int64)
   // per feature

@@ -1,6 +1,7 @@
 // Umbrella header: host entry points of every mdl_b200 kernel family.
 #pragma once
 
+#include "attention.h"
 #include "comm.h"
 #include "embedding.h"
 #include "gemm.h"

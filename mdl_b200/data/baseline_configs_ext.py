@@ -1,0 +1,68 @@
+"""Benchmark workloads 3-5 (MDL, OneTrans, LONGER/STCA) as reference-schema configs.
+
+Workload 3, MDL on the RankMixer backbone of workload 2:
+
+* the 300 fields + 64 dense features of workload 2 form the feature tokens
+  (T=16, D=768, 2 layers, FFN x4);
+* a scene id uniform over 5 scenes (``scene_id``, embedding scope
+  ``scenario``) feeds the scenario tokens: 4 tokens per scene plus the global
+  token (``tokens_per_scenario: 4``);
+* one prior feature per task (``prior_<task>``, scope ``task``) feeds each
+  task token;
+* scene-conditioned feature bias (FiLM on the feature tokens);
+* click / like / finish heads at positive rates 0.08 / 0.02 / 0.3, whose
+  ground truth depends on the scene;
+* batch 2048 per GPU, bf16.
+"""
+
+from __future__ import annotations
+
+import copy
+
+from .baseline_configs import _config2_features, _rankmixer_common
+from .synthetic import FieldSpec, SyntheticSpec
+
+MDL_TASKS = {"click": 0.08, "like": 0.02, "finish": 0.3}
+MDL_SCENES = 5
+
+
+def config3(num_fields: int = 300, batch: int = 2048, tokens_per_scenario: int = 4,
+            scene_feature_bias: str = "film") -> tuple[dict, SyntheticSpec]:
+    tasks = dict(MDL_TASKS)
+    m = _rankmixer_common("mdl_rankmixer", tasks, batch, "bf16", "cuda")
+    feats, fields = _config2_features(num_fields)
+    feats = copy.deepcopy(feats)
+    scenes = [f"scene{i}" for i in range(MDL_SCENES)]
+    feats.append({"name": "scene_id", "kind": "categorical", "source": "scene_id", "embedding_dim": 64,
+                  "embedding_scope": "scenario", "encoding": {"type": "identity", "max_id": MDL_SCENES}})
+    fields["scene_id"] = FieldSpec(vocab=MDL_SCENES)
+    for task in tasks:
+        name = f"prior_{task}"
+        feats.append({"name": name, "kind": "categorical", "source": name, "embedding_dim": 64,
+                      "embedding_scope": "task", "encoding": {"type": "identity", "max_id": 1000}})
+        fields[name] = FieldSpec(vocab=1000)
+    m["features"] = feats
+    m["scenarios"] = {"names": scenes, "source": "scene_id"}
+    m["tokenization"] = {
+        "feature_tokenizer": "rankmixer",
+        "num_feature_tokens": 16,
+        "scenario_tokens": [{"name": s, "important_inputs": ["scene_id"]} for s in scenes]
+        + [{"name": "global", "important_inputs": ["scene_id"]}],
+        "task_tokens": [{"name": t, "important_inputs": [f"prior_{t}"]} for t in tasks],
+    }
+    m["model"].update({"embedding_dim": 64, "token_dim": 768, "num_layers": 2, "num_heads": 12, "hidden_dim": 3072,
+                       "task_head_hidden_dim": 1536, "ffn_activation": "gelu", "use_task_tokens": True,
+                       "use_scenario_tokens": True, "use_global_scenario_token": True,
+                       "tokens_per_scenario": tokens_per_scenario, "scene_feature_bias": scene_feature_bias,
+                       "mdl_feature_interaction": "residual_ffn", "mdl_token_state": "coupled"})
+    m["training"].update({"lr_dense": 1e-4, "lr_sparse": 0.05, "dense_optimizer": "rmsprop", "lr_warmup_steps": 1000,
+                          "rmsprop_alpha": 0.99999, "adagrad_initial_accumulator_value": 0.0})
+    spec = SyntheticSpec(fields=fields, dense_width=64, task_rates=list(tasks.values()), zipf_s=1.05, seed=0,
+                         num_scenarios=MDL_SCENES, scene_field="scene_id", scene_effect=0.5)
+    return m, spec
+
+
+def config(n: int, **kw) -> tuple[dict, SyntheticSpec]:
+    if n == 3:
+        return config3(**kw)
+    raise ValueError(f"no benchmark workload {n}")

@@ -9,9 +9,10 @@ parity run uses generated data of the configured shape:
 * multi-hot bags with uniform lengths in ``[min_len, max_len]``;
 * dense features ``N(0, 1)``;
 * labels ``Bernoulli`` drawn from a hidden ground-truth logit (a fixed random
-  score per (field, id), averaged over bags, plus a dense projection), shifted
-  per task so the positive rate matches the configured one. A model can
-  therefore learn something, and AUC comparisons are meaningful.
+  score per (field, id), averaged over bags, plus a dense projection, plus for
+  multi-scene specs a per-(scene, task) offset and gain), shifted per task so
+  the positive rate matches the configured one. A model can therefore learn
+  something, and AUC comparisons are meaningful.
 
 Generation is vectorised numpy; ``BatchPool`` pre-generates a few distinct
 batches in pinned host memory for the timed loops.
@@ -46,6 +47,8 @@ class SyntheticSpec:
     zipf_s: float | None = 1.05      # None -> uniform ids
     num_scenarios: int = 1
     seed: int = 0
+    scene_field: str | None = None   # categorical field whose id is the scene id + 1
+    scene_effect: float = 0.0        # strength of the per-(scene, task) part of the ground truth
 
 
 def zipf_ids(rng: np.random.Generator, n: int, vocab: int, s: float | None, scramble: int) -> np.ndarray:
@@ -93,12 +96,18 @@ class SyntheticGenerator:
         self.dense_proj = self.truth_rng.normal(0.0, 1.0, size=(max(spec.dense_width, 1), len(spec.task_rates)))
         self.task_mix = self.truth_rng.normal(0.0, 1.0, size=(len(spec.task_rates),))
         self.task_bias = None
+        ns, nt = max(1, spec.num_scenarios), len(spec.task_rates)
+        self.scene_offset = self.truth_rng.normal(0.0, 1.0, size=(ns, nt)) * spec.scene_effect
+        self.scene_gain = 1.0 + 0.5 * spec.scene_effect * self.truth_rng.normal(0.0, 1.0, size=(ns, nt))
 
-    def _truth_logits(self, per_field_scores: np.ndarray, dense: np.ndarray) -> np.ndarray:
+    def _truth_logits(self, per_field_scores: np.ndarray, dense: np.ndarray, scen: np.ndarray) -> np.ndarray:
         nf = max(1, per_field_scores.shape[1])
         base = per_field_scores.sum(axis=1, keepdims=True) * (2.0 / math.sqrt(nf))
         dense_part = dense @ self.dense_proj[: dense.shape[1]] * (0.5 / math.sqrt(max(1, dense.shape[1])))
-        return base * (1.0 + 0.3 * self.task_mix[None, :]) + dense_part
+        logits = base * (1.0 + 0.3 * self.task_mix[None, :]) + dense_part
+        if self.spec.scene_effect:
+            logits = logits * self.scene_gain[scen] + self.scene_offset[scen]
+        return logits
 
     def _calibrate(self, logits: np.ndarray) -> np.ndarray:
         if self.task_bias is None:
@@ -122,9 +131,14 @@ class SyntheticGenerator:
         ids_parts = []
         lengths_parts = []
         scores = []
+        scen = rng.integers(0, max(1, spec.num_scenarios), size=rows, dtype=np.int64)
         for f in self.plan.features:
             if f.table is None:
                 lengths_parts.append(np.zeros(rows, dtype=np.int64))
+                continue
+            if f.name == spec.scene_field:
+                ids_parts.append(scen + 1)
+                lengths_parts.append(np.ones(rows, dtype=np.int64))
                 continue
             fs = spec.fields[f.name]
             if fs.multi_hot:
@@ -142,13 +156,12 @@ class SyntheticGenerator:
         dense = rng.standard_normal((rows, spec.dense_width)).astype(np.float32) if spec.dense_width else \
             np.zeros((rows, 0), dtype=np.float32)
         per_field = np.stack(scores, axis=1) if scores else np.zeros((rows, 0))
-        logits = self._calibrate(self._truth_logits(per_field, dense.astype(np.float64)))
+        logits = self._calibrate(self._truth_logits(per_field, dense.astype(np.float64), scen))
         probs = 1.0 / (1.0 + np.exp(-logits))
         labels = (rng.random(probs.shape) < probs).astype(np.float32)
         offsets = np.zeros(len(self.plan.features) * rows + 1, dtype=np.int64)
         np.cumsum(np.concatenate(lengths_parts), out=offsets[1:])
         ids_all = np.concatenate(ids_parts) if ids_parts else np.zeros(0, dtype=np.int64)
-        scen = rng.integers(0, spec.num_scenarios, size=rows, dtype=np.int64)
         return PackedBatch.pack(torch.from_numpy(ids_all), torch.from_numpy(offsets),
                                 torch.from_numpy(dense) if spec.dense_width else None, torch.from_numpy(labels), None,
                                 torch.from_numpy(scen), rows, pin=pin)

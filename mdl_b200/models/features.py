@@ -58,30 +58,57 @@ class ScalarInputs:
 
 
 class FeatureEncoder:
-    """Builds the tables + lookup plan of a config's scalar token inputs."""
+    """Builds the tables + lookup plans of a config's scalar inputs.
+
+    * ``plan``: the feature-token inputs, concatenated (optionally cut into
+      per-token slices padded to 8 columns for the RankMixer tokenizer);
+    * ``domain_plan`` (when ``domain_tokens`` is given): the inputs of each MDL
+      domain token, token ``t`` at columns ``[t * domain_k_pad, ...)`` of a
+      ``[rows, n_tokens * domain_k_pad]`` matrix (an input read by several
+      tokens is looked up once per token);
+    * ``batch_plan``: the batch layout (CSR order of the ids and column order
+      of the dense matrix) that both plans read: the feature-token inputs,
+      then the inputs used only by domain tokens.
+    """
 
     def __init__(self, config: AppConfig, *, device: torch.device, rank: int = 0, world: int = 1,
                  process_group=None, vocab_sizes: dict[str, int] | None = None, input_names: list[str] | None = None,
-                 slice_tokens: int = 0, base_seed: int | None = None) -> None:
+                 slice_tokens: int = 0, base_seed: int | None = None,
+                 domain_tokens: list[list[str]] | None = None) -> None:
         self.config = config
         by_name = {f.name: f for f in config.features}
         names = list(input_names if input_names is not None else config.resolved.tokenization.feature_token_inputs)
         names = [n for n in names if n in by_name]
         self.inputs = names
+        domain_tokens = [list(t) for t in (domain_tokens or [])]
+        for tok in domain_tokens:
+            missing = [n for n in tok if n not in by_name]
+            if missing:
+                raise ValueError(f"domain token inputs reference unknown features: {missing}")
+        batch_names = list(names)
+        for tok in domain_tokens:
+            for n in tok:
+                if n not in batch_names:
+                    batch_names.append(n)
+        self.batch_names = batch_names
+        src_of = {n: i for i, n in enumerate(batch_names)}
         tables: dict[str, tuple[int, int]] = {}
-        features: list[LookupFeature] = []
-        col = 0
-        dense_col = 0
-        dense_names = []
-        for name in names:
+        dense_col_of: dict[str, int] = {}
+        dense_names: list[str] = []
+        dense_total = 0
+        for name in batch_names:
+            f = by_name[name]
+            if f.kind == "dense":
+                dense_col_of[name] = dense_total
+                dense_names.append(name)
+                dense_total += int(f.dimension) + (1 if f.presence else 0)
+
+        def make(name: str, out_col: int) -> LookupFeature:
             f = by_name[name]
             if f.kind == "dense":
                 width = int(f.dimension) + (1 if f.presence else 0)
-                features.append(LookupFeature(name, None, width=width, out_col=col, dense_col=dense_col))
-                dense_names.append(name)
-                dense_col += width
-                col += width
-                continue
+                return LookupFeature(name, None, width=width, out_col=out_col, dense_col=dense_col_of[name],
+                                     src=src_of[name])
             tname = table_name_of(config, name)
             owner = by_name.get(tname, f)
             dim = int(owner.embedding_dim or config.model.embedding_dim)
@@ -93,11 +120,17 @@ class FeatureEncoder:
             enc = f.encoding
             hmode = HASH_PREHASHED if (enc is not None and enc.type == "pre_hashed" and self._device_hash) else HASH_NONE
             buckets = int(enc.num_buckets or 0) if enc is not None else 0
-            features.append(LookupFeature(name, tname, pooling=pool, hash_mode=hmode, buckets=buckets, width=dim,
-                                          out_col=col))
-            col += dim
-        self.table_shapes = tables
-        self.scalar = ScalarInputs(names, [f.width for f in features], col, dense_names, dense_col)
+            return LookupFeature(name, tname, pooling=pool, hash_mode=hmode, buckets=buckets, width=dim,
+                                 out_col=out_col, src=src_of[name])
+
+        features: list[LookupFeature] = []
+        col = 0
+        for name in names:
+            lf = make(name, col)
+            features.append(lf)
+            col += lf.width
+        self.scalar = ScalarInputs(names, [f.width for f in features], col, [n for n in names if n in dense_col_of],
+                                   dense_total)
         slice_k = 0
         slice_stride = 0
         if slice_tokens:
@@ -106,10 +139,35 @@ class FeatureEncoder:
             slice_stride = (slice_k + 7) // 8 * 8
         self.slice_tokens = slice_tokens
         self.plan = LookupPlan(features, out_width=col, slice_k=slice_k, slice_stride=slice_stride,
-                               dense_width=dense_col)
+                               dense_width=dense_total)
+        # MDL domain-token inputs
+        self.domain_plan = None
+        self.domain_widths: list[int] = []
+        self.domain_k_pad = 0
+        if domain_tokens:
+            dfeats: list[list[LookupFeature]] = []
+            for tok in domain_tokens:
+                row, c = [], 0
+                for name in tok:
+                    lf = make(name, c)
+                    row.append(lf)
+                    c += lf.width
+                dfeats.append(row)
+                self.domain_widths.append(c)
+            kp = (max(self.domain_widths) + 7) // 8 * 8
+            self.domain_k_pad = kp
+            flat = []
+            for t, row in enumerate(dfeats):
+                for lf in row:
+                    lf.out_col += t * kp
+                    flat.append(lf)
+            self.domain_plan = LookupPlan(flat, out_width=len(domain_tokens) * kp, dense_width=dense_total,
+                                          zero_fill=any(w != kp for w in self.domain_widths))
+        self.batch_plan = LookupPlan([make(n, 0) for n in batch_names], out_width=0, dense_width=dense_total)
         train = config.training
         specs = [EmbeddingTableSpec(n, r, d, 4 if train.embedding_weight_dtype == "fp32" else 2)
                  for n, (r, d) in sorted(tables.items())]
+        self.table_shapes = tables
         self.shard_plan = plan_embedding_shards(
             specs, world_size=world, strategy=train.embedding_sharding.strategy,
             table_wise_max_rows=train.embedding_sharding.table_wise_max_rows,

@@ -1,0 +1,348 @@
+"""MDL multi-domain ranker on a RankMixer backbone (``model.name: mdl_rankmixer``).
+
+Reference: ``MDLRankMixerModel`` (``src/model.py:7543-7967``), ``MDLRankMixerBlock``
+(:7418-7465), domain interaction (:6953-7228), readout (:7238-7416),
+``DomainTokenProjector`` (:4469-4498), ``SceneFeatureBias`` (:4501-4547),
+``ScenarioTower`` (:6914-6950), ``DomainAwareAttention`` /
+``RankMixerDomainInteraction`` / ``masked_scenario_pool`` / ``DomainFusedModule``
+(``src/modules/attention.py:366-512, 719-789``).
+
+Per sample the model carries three token sets through ``L`` blocks:
+
+* feature tokens ``[B, T, D]``: the RankMixer tokenizer and blocks (token
+  mixing + LayerNorm + per-token FFN, with the second residual + LayerNorm for
+  ``mdl_feature_interaction: residual_ffn``);
+* scenario tokens ``[B, Ns, D]``: ``tokens_per_scenario`` tokens per scene plus
+  an optional global token, built by per-token MLPs (``Linear -> act ->
+  Linear -> ReLU``) from their configured inputs;
+* task tokens ``[B, ntask, D]``, built the same way.
+
+In every block each domain token set reads the feature tokens with
+domain-aware attention (per-token FFN projections of queries, keys and values;
+``few_query_attention``), task tokens add the masked mean of the active
+scene's tokens (DomainFused), and both sets pass a per-token FFN with a
+residual. The task heads read one task token each.
+
+Execution on CUDA: the embedding lookup writes the tokenizer input and the
+domain-token inputs (two lookups over one batch), every per-token MLP/FFN is a
+grouped tcgen05 GEMM pair, attention is the few-query kernel, the RankMixer
+block is the fused block, heads + BCE are one grouped GEMM and one kernel. On
+CPU the same modules run their PyTorch definitions.
+
+``tokens_per_scenario`` (default 1, the reference layout) generalises the
+scenario tokens: scene ``s`` owns tokens ``[s * k, (s + 1) * k)`` and every
+pooling over "the active scene" averages its ``k`` tokens.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from ..config.schema import AppConfig
+from ..ops.layers import DomainAwareAttention, Linear, PerTokenFFN, gemm_param
+from .features import FeatureEncoder
+from .heads import TaskHeads
+from .rankmixer import token_mix
+
+
+def _kaiming_uniform_(t: torch.Tensor, fan_in: int) -> None:
+    bound = 1.0 / math.sqrt(max(1, fan_in))
+    nn.init.uniform_(t, -bound, bound)
+
+
+def scenario_mask_from_ids(scenario_id: torch.Tensor, num_scenarios: int) -> torch.Tensor:
+    """``[B]`` integer ids -> one-hot ``[B, S]`` float; a ``[B, S]`` mask passes through
+    (reference ``_scenario_mask_from_ids`` ``src/model.py:414-480``, without the
+    per-step validation sync)."""
+
+    if scenario_id.dim() == 2:
+        if scenario_id.size(1) != num_scenarios:
+            raise ValueError(f"scenario mask width must be {num_scenarios}, got {scenario_id.size(1)}")
+        return scenario_id.float()
+    if scenario_id.dim() != 1:
+        raise ValueError("scenario_id must have shape [batch] or [batch, num_scenarios]")
+    return F.one_hot(scenario_id.long().clamp(0, num_scenarios - 1), num_scenarios).float()
+
+
+class RankMixerDomainInteraction(nn.Module):
+    """Ablation of domain-aware attention: RankMixer mixing over ``[feature; domain]``
+    tokens, zero-padded to a width divisible by the token count, residual +
+    LayerNorm, domain outputs cropped back (``src/modules/attention.py:366-422``)."""
+
+    def __init__(self, token_dim: int, num_domain_tokens: int, num_feature_tokens: int, device=None) -> None:
+        super().__init__()
+        self.token_dim = token_dim
+        self.num_feature_tokens = num_feature_tokens
+        self.num_tokens = num_feature_tokens + num_domain_tokens
+        self.mixing_dim = math.ceil(token_dim / self.num_tokens) * self.num_tokens
+        self.norm = nn.LayerNorm(self.mixing_dim, device=device)
+
+    def forward(self, domain_tokens: torch.Tensor, feature_tokens: torch.Tensor) -> torch.Tensor:
+        tokens = torch.cat([feature_tokens, domain_tokens.to(feature_tokens.dtype)], dim=1)
+        if self.mixing_dim != self.token_dim:
+            tokens = F.pad(tokens, (0, self.mixing_dim - self.token_dim))
+        mixed = token_mix(tokens) + tokens
+        out = F.layer_norm(mixed.float(), (self.mixing_dim,), self.norm.weight, self.norm.bias, self.norm.eps)
+        return out.to(tokens.dtype)[:, self.num_feature_tokens:, :self.token_dim]
+
+
+class MDLRankMixerModel(nn.Module):
+    def __init__(self, config: AppConfig, *, device: torch.device, rank: int = 0, world: int = 1,
+                 process_group=None, vocab_sizes: dict[str, int] | None = None, base_seed: int | None = None) -> None:
+        super().__init__()
+        self.config = config
+        mc = config.model
+        res = config.resolved.tokenization
+        dev = torch.device(device)
+        self.T = int(res.feature_token_count)
+        self.D = int(mc.token_dim)
+        self.H = int(mc.hidden_dim)
+        self.L = int(mc.num_layers)
+        self.tasks = list(config.task_names)
+        self.ntask = len(self.tasks)
+        self.S = len(config.scenarios.names)
+        self.tps = max(1, int(mc.tokens_per_scenario))
+        self.heads_n = int(mc.num_heads)
+        self.act = mc.ffn_activation
+        self.ffn_relu = mc.ffn_activation == "relu"
+        self.use_scen = bool(mc.use_scenario_tokens)
+        self.use_task = bool(mc.use_task_tokens)
+        self.use_global = bool(mc.use_global_scenario_token) and self.use_scen
+        self.split = mc.mdl_token_state == "split"
+        self.residual_ffn = mc.mdl_feature_interaction == "residual_ffn"
+        self.ln_eps = 1e-5
+        T, D, H = self.T, self.D, self.H
+        if D % T:
+            raise ValueError("mdl_rankmixer requires token_dim divisible by the feature token count")
+        if D % self.heads_n:
+            raise ValueError("token_dim must be divisible by num_heads")
+        if mc.rankmixer_ffn_type != "dense":
+            raise NotImplementedError("mdl_rankmixer implements the dense per-token FFN")
+        if self.split and not (self.use_scen or self.use_task):
+            raise ValueError("model.mdl_token_state=split requires task or scenario tokens")
+        scen_specs = [s for s in res.scenario_token_specs
+                      if self.use_scen and (s.kind != "global" or self.use_global)]
+        task_specs = list(res.task_token_specs) if self.use_task else []
+        self.Ns, self.Nt = len(scen_specs), len(task_specs)
+        dom_inputs = [s.resolved_inputs() for s in scen_specs + task_specs]
+        for spec, inputs in zip(scen_specs + task_specs, dom_inputs):
+            if not inputs:
+                raise ValueError(f"domain token {spec.name!r} has no inputs")
+        self.encoder = FeatureEncoder(config, device=dev, rank=rank, world=world, process_group=process_group,
+                                      vocab_sizes=vocab_sizes, slice_tokens=T, base_seed=base_seed,
+                                      domain_tokens=dom_inputs or None)
+        self.K = self.encoder.slice_k
+        self.Kpad = self.encoder.slice_stride
+        Kd = self.encoder.domain_k_pad
+        self.Kd = Kd
+        # feature tokenizer: T per-token linear maps of the concatenated inputs
+        self.tok_weight = gemm_param(torch.zeros(T, D, self.Kpad, device=dev))
+        self.tok_bias = nn.Parameter(torch.empty(T, D, device=dev))
+        for t in range(T):
+            _kaiming_uniform_(self.tok_weight.data[t, :, :self.K], self.K)
+            _kaiming_uniform_(self.tok_bias.data[t], self.K)
+        # domain-token projectors (reference DomainTokenProjector: Linear -> act -> Linear -> ReLU)
+        widths = self.encoder.domain_widths
+        self.scenario_projector = None
+        self.task_projector = None
+        if self.Ns:
+            self.scenario_projector = PerTokenFFN(self.Ns, Kd, H, self.act, output_relu=True, device=dev, out_dim=D)
+            self.scenario_projector.restrict_inputs(widths[:self.Ns])
+        if self.Nt:
+            self.task_projector = PerTokenFFN(self.Nt, Kd, H, self.act, output_relu=True, device=dev, out_dim=D)
+            self.task_projector.restrict_inputs(widths[self.Ns:])
+        std = float(mc.init_std)
+        self.scenario_readout_seed = (nn.Parameter(torch.randn(1, self.Ns, D, device=dev) * std)
+                                      if self.split and self.Ns else None)
+        self.task_readout_seed = (nn.Parameter(torch.randn(1, self.Nt, D, device=dev) * std)
+                                  if self.split and self.Nt else None)
+        self.blocks = nn.ModuleList(self._make_block(dev) for _ in range(self.L))
+        self.scene_feature_bias = None
+        if mc.scene_feature_bias != "none":
+            if not self.use_scen:
+                raise ValueError("scene_feature_bias needs scenario tokens")
+            out = D if mc.scene_feature_bias == "additive" else 2 * D
+            self.scene_feature_bias = Linear(D, out, device=dev)
+            nn.init.zeros_(self.scene_feature_bias.weight)
+            nn.init.zeros_(self.scene_feature_bias.bias)
+        self.scene_bias_mode = mc.scene_feature_bias
+        # scenario tower ablation (no scenario tokens): one MLP per scene over the pooled feature state
+        self.scenario_tower = (PerTokenFFN(self.S, D, H, self.act, device=dev) if not self.use_scen else None)
+        Hh = int(mc.task_head_hidden_dim or mc.hidden_dim)
+        self.heads = TaskHeads(self.ntask, D, Hh, mc.task_head_activation, device=dev)
+
+    def _make_block(self, dev) -> nn.Module:
+        mc = self.config.model
+        T, D, H = self.T, self.D, self.H
+        blk = nn.Module()
+        blk.ln1_weight = nn.Parameter(torch.ones(D, device=dev))
+        blk.ln1_bias = nn.Parameter(torch.zeros(D, device=dev))
+        blk.w_in = gemm_param(torch.empty(T, H, D, device=dev))
+        blk.b_in = nn.Parameter(torch.empty(T, H, device=dev))
+        blk.w_out = gemm_param(torch.empty(T, D, H, device=dev))
+        blk.b_out = nn.Parameter(torch.empty(T, D, device=dev))
+        for t in range(T):
+            _kaiming_uniform_(blk.w_in.data[t], D)
+            _kaiming_uniform_(blk.b_in.data[t], D)
+            _kaiming_uniform_(blk.w_out.data[t], H)
+            _kaiming_uniform_(blk.b_out.data[t], H)
+        if self.residual_ffn:
+            blk.ln2_weight = nn.Parameter(torch.ones(D, device=dev))
+            blk.ln2_bias = nn.Parameter(torch.zeros(D, device=dev))
+        blk.scenario_attention = blk.scenario_rankmixer = blk.scenario_ffn = None
+        blk.task_attention = blk.task_rankmixer = blk.task_ffn = None
+        if self.Ns:
+            if mc.use_scenario_feature_interaction:
+                blk.scenario_attention = DomainAwareAttention(D, self.heads_n, self.Ns, T, H, self.act, device=dev)
+            else:
+                blk.scenario_rankmixer = RankMixerDomainInteraction(D, self.Ns, T, device=dev)
+            blk.scenario_ffn = PerTokenFFN(self.Ns, D, H, self.act, device=dev)
+        if self.Nt:
+            if mc.use_task_feature_interaction:
+                blk.task_attention = DomainAwareAttention(D, self.heads_n, self.Nt, T, H, self.act, device=dev)
+            else:
+                blk.task_rankmixer = RankMixerDomainInteraction(D, self.Nt, T, device=dev)
+            blk.task_ffn = PerTokenFFN(self.Nt, D, H, self.act, device=dev)
+        return blk
+
+    # ------------------------------------------------------------------ params
+    def gemm_param_names(self) -> set[str]:
+        return {n for n, p in self.named_parameters() if getattr(p, "_mdl_gemm", False)}
+
+    @property
+    def store(self):
+        return self.encoder.store
+
+    # ------------------------------------------------------------------ pieces
+    def _cuda(self, batch) -> bool:
+        return batch.ids.is_cuda and self.config.runtime.kernel_backend == "native"
+
+    def _tokenize(self, x0: torch.Tensor, B: int, cuda: bool) -> torch.Tensor:
+        if cuda:
+            from ..ops.fused import PerTokenLinearFn
+
+            return PerTokenLinearFn.apply(x0, self.tok_weight, self.tok_bias, self.T, self.K, self.Kpad)
+        xin = x0.float().view(B, self.T, self.Kpad)[:, :, :self.K]
+        return torch.einsum("btk,tdk->btd", xin, self.tok_weight[:, :, :self.K]) + self.tok_bias.unsqueeze(0)
+
+    def _feature_block(self, blk, x: torch.Tensor, cuda: bool) -> torch.Tensor:
+        D = self.D
+        if cuda and not self.ffn_relu:
+            from ..ops.fused import MixLayerNormFn, RankMixerBlockFn
+            from ..ops.layers import PerTokenFFNFn
+
+            if self.residual_ffn:
+                return RankMixerBlockFn.apply(x, blk.ln1_weight, blk.ln1_bias, blk.w_in, blk.b_in, blk.w_out,
+                                              blk.b_out, blk.ln2_weight, blk.ln2_bias, self.ln_eps)
+            m = MixLayerNormFn.apply(x, blk.ln1_weight, blk.ln1_bias, self.ln_eps)
+            return PerTokenFFNFn.apply(m, blk.w_in, blk.b_in, blk.w_out, blk.b_out, False)
+        act_fn = F.relu if self.ffn_relu else F.gelu
+        xf = x.float()
+        m = F.layer_norm(token_mix(xf) + xf, (D,), blk.ln1_weight, blk.ln1_bias, self.ln_eps)
+        h = act_fn(torch.einsum("btd,thd->bth", m, blk.w_in) + blk.b_in.unsqueeze(0))
+        f = torch.einsum("bth,tdh->btd", h, blk.w_out) + blk.b_out.unsqueeze(0)
+        if not self.residual_ffn:
+            return f.to(x.dtype)
+        return F.layer_norm(f + m, (D,), blk.ln2_weight, blk.ln2_bias, self.ln_eps).to(x.dtype)
+
+    def _scene_weights(self, mask: torch.Tensor, include_global: bool) -> torch.Tensor:
+        """``[B, Ns]`` weights of the masked mean over the active scene's tokens (and the
+        global token when ``include_global``); reference ``masked_scenario_pool``."""
+
+        w = mask.repeat_interleave(self.tps, dim=1)
+        if self.use_global:
+            g = torch.full_like(w[:, :1], 1.0 if include_global else 0.0)
+            w = torch.cat([w, g], dim=1)
+        return w / w.sum(dim=1, keepdim=True).clamp_min(1.0)
+
+    @staticmethod
+    def _pool(tokens: torch.Tensor, weights: torch.Tensor) -> torch.Tensor:
+        return torch.einsum("bn,bnd->bd", weights.to(tokens.dtype), tokens)
+
+    @staticmethod
+    def _interact(domain: torch.Tensor, feature: torch.Tensor, attention, rankmixer) -> torch.Tensor:
+        if attention is not None:
+            return domain + attention(domain, feature).to(domain.dtype)
+        return rankmixer(domain, feature)
+
+    # ------------------------------------------------------------------ forward
+    def forward(self, batch, task_scale: torch.Tensor | None = None) -> dict[str, torch.Tensor]:
+        from ..ops.embedding import fused_lookup
+
+        B = batch.rows
+        cuda = self._cuda(batch)
+        anchor = torch.zeros(0, device=batch.ids.device, requires_grad=True)
+        enc = self.encoder
+        x0 = fused_lookup(self.store, enc.plan, batch.ids, batch.offsets, batch.dense, B, anchor)
+        x = self._tokenize(x0, B, cuda)
+        dt = x.dtype
+        mask = scenario_mask_from_ids(batch.scenario_id, self.S).to(x.device)
+        s_prompt = t_prompt = None
+        if enc.domain_plan is not None:
+            d0 = fused_lookup(self.store, enc.domain_plan, batch.ids, batch.offsets, batch.dense, B, anchor)
+            dom = d0.view(B, self.Ns + self.Nt, self.Kd)
+            if not cuda:
+                dom = dom.float()
+            if self.Ns:
+                s_prompt = self.scenario_projector(dom[:, :self.Ns]).to(dt)
+            if self.Nt:
+                t_prompt = self.task_projector(dom[:, self.Ns:]).to(dt)
+        s = t = None
+        if s_prompt is not None:
+            s = s_prompt if self.scenario_readout_seed is None else \
+                self.scenario_readout_seed.to(dt).expand(B, -1, -1)
+        if t_prompt is not None:
+            t = t_prompt if self.task_readout_seed is None else self.task_readout_seed.to(dt).expand(B, -1, -1)
+        if self.scene_feature_bias is not None:
+            w = self._scene_weights(mask, include_global=False)
+            scene = self._pool(s_prompt, w)
+            params = self.scene_feature_bias(scene).to(dt)
+            if self.scene_bias_mode == "additive":
+                x = x + params.unsqueeze(1)
+            else:
+                gamma, beta = params.chunk(2, dim=-1)
+                x = (1.0 + gamma).unsqueeze(1) * x + beta.unsqueeze(1)
+        w_fused = self._scene_weights(mask, include_global=self.use_global) if (s is not None) else None
+        for blk in self.blocks:
+            x = self._feature_block(blk, x, cuda)
+            s_hat = None
+            if s is not None:
+                if self.split:
+                    q = s_prompt + s
+                    s_hat = s + blk.scenario_attention(q, x).to(dt)
+                else:
+                    s_hat = self._interact(s, x, blk.scenario_attention, blk.scenario_rankmixer)
+                s = s_hat + blk.scenario_ffn(s_hat).to(dt)
+            if t is not None:
+                if self.split:
+                    q = t_prompt + t
+                    t_hat = t + blk.task_attention(q, x).to(dt)
+                else:
+                    t_hat = self._interact(t, x, blk.task_attention, blk.task_rankmixer)
+                if s_hat is not None:
+                    t_hat = t_hat + self._pool(s_hat, w_fused).unsqueeze(1)
+                t = t_hat + blk.task_ffn(t_hat).to(dt)
+        # readout (reference _mdl_logits src/model.py:7375-7415)
+        context = None
+        if not self.use_scen:
+            pooled = x.mean(dim=1)
+            states = self.scenario_tower(pooled.unsqueeze(1).expand(B, self.S, self.D).contiguous()).to(dt)
+            wm = mask / mask.sum(dim=1, keepdim=True).clamp_min(1.0)
+            context = self._pool(states, wm)
+        elif not self.use_task:
+            context = self._pool(s, self._scene_weights(mask, include_global=self.use_global))
+        if self.use_task:
+            pred = t if context is None else t + context.unsqueeze(1)
+        else:
+            v = x.mean(dim=1)
+            if context is not None:
+                v = v + context
+            pred = v.unsqueeze(1).expand(B, self.ntask, self.D).contiguous()
+        if task_scale is None:
+            task_scale = torch.full((self.ntask,), 1.0 / max(1, B), device=x.device)
+        labels = batch.labels
+        return self.heads(pred, labels, batch.label_mask, task_scale)

@@ -47,7 +47,7 @@ class DenseParams:
         self.weight_decay, self.rmsprop_alpha = weight_decay, rmsprop_alpha
         self.comm = comm
         named = list(named_params)
-        bf16_names = set(bf16_names or ())
+        bf16_names = set(bf16_names or ()) | {n for n, p in named if getattr(p, "_mdl_gemm", False)}
         ordered = [x for x in named if x[0] in bf16_names] + [x for x in named if x[0] not in bf16_names]
         self.names = [n for n, _ in ordered]
         self.params = {n: p for n, p in ordered}
@@ -71,8 +71,9 @@ class DenseParams:
                 o = self.offsets[name]
                 self.master[o:o + p.numel()].copy_(p.detach().flatten().to(self.device, torch.float32))
                 p.data = self.master[o:o + p.numel()].view_as(p)
-                if self.device.type != "cuda":
-                    p.grad = self.grad[o:o + p.numel()].view_as(p)
+                # autograd accumulates plain-PyTorch gradients straight into the flat buffer;
+                # fused nodes write the same memory through _mdl_grad
+                p.grad = self.grad[o:o + p.numel()].view_as(p)
                 p._mdl_grad = self.grad[o:o + p.numel()].view_as(p)
                 if self.shadow is not None:
                     p._mdl_shadow = self.shadow[o:o + p.numel()].view_as(p)

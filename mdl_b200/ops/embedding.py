@@ -300,6 +300,7 @@ class LookupFeature:
     width: int = 0
     out_col: int = 0
     dense_col: int = 0
+    src: int = -1              # feature index in the batch CSR (-1: the feature's own plan index)
 
 
 @dataclass
@@ -316,6 +317,7 @@ class LookupPlan:
     slice_k: int = 0
     slice_stride: int = 0
     dense_width: int = 0
+    zero_fill: bool = False      # output has columns no feature writes (must read as zero)
     _meta: dict = field(default_factory=dict)
 
     @property
@@ -323,6 +325,16 @@ class LookupPlan:
         if self.slice_k:
             return (self.out_width + self.slice_k - 1) // self.slice_k * self.slice_stride
         return self.out_width
+
+    def src_of(self, i: int) -> int:
+        s = self.features[i].src
+        return i if s < 0 else s
+
+    @property
+    def num_src(self) -> int:
+        """Batch features (CSR blocks) the plan reads."""
+
+        return max((self.src_of(i) for i, f in enumerate(self.features) if f.table is not None), default=-1) + 1
 
     def phys_col(self, c: int) -> int:
         return (c // self.slice_k) * self.slice_stride + c % self.slice_k if self.slice_k else c
@@ -367,6 +379,7 @@ class LookupPlan:
             i32([f.dense_col for f in self.features]),
             tm["t_base"], tm["t_row_base"], tm["t_dim"], tm["t_mode"], tm["t_cyc"], tm["t_owner"], tm["t_rows"],
             tm["t_base_all"], tm["t_row_base_all"],
+            i64([self.src_of(i) * rows for i in range(F)]),
         ]
         max_vec = max([(f.width + 4 * ln - 1) // (4 * ln) for f, ln in zip(self.features, lanes_list)] or [1])
         result = (meta, chunk_prefix[-1], max_vec)
@@ -457,7 +470,8 @@ def lookup_reference(store: EmbeddingStore, plan: LookupPlan, ids: torch.Tensor,
         if f.table is None:
             logical[:, f.out_col:f.out_col + f.width] = dense[:, f.dense_col:f.dense_col + f.width].float().cpu()
             continue
-        beg = offsets[fi * rows:(fi + 1) * rows + 1].cpu()
+        si = plan.src_of(fi)
+        beg = offsets[si * rows:(si + 1) * rows + 1].cpu()
         lengths = beg[1:] - beg[:-1]
         flat = ids[int(beg[0]):int(beg[-1])].cpu()
         flat = _hash_ids(flat, f)
@@ -491,7 +505,8 @@ def backward_reference(store: EmbeddingStore, plan: LookupPlan, ids: torch.Tenso
     for fi, f in enumerate(plan.features):
         if f.table is None:
             continue
-        beg = offsets[fi * rows:(fi + 1) * rows + 1].cpu()
+        si = plan.src_of(fi)
+        beg = offsets[si * rows:(si + 1) * rows + 1].cpu()
         lengths = beg[1:] - beg[:-1]
         flat = _hash_ids(ids[int(beg[0]):int(beg[-1])].cpu(), f)
         bag = torch.repeat_interleave(torch.arange(rows), lengths)
@@ -519,10 +534,12 @@ class _FusedLookup(torch.autograd.Function):
     def forward(ctx, anchor, store, plan, ids, offsets, dense, rows):
         ctx.store, ctx.plan, ctx.rows = store, plan, rows
         ctx.save_for_backward(ids, offsets)
+        if plan.num_src * rows + 1 > offsets.numel():
+            raise ValueError(f"lookup plan reads {plan.num_src} batch features; offsets hold {offsets.numel()}")
         if ids.is_cuda:
             meta, chunks, max_vec = plan.device_meta(store, rows)
             out = torch.empty(rows, plan.out_ld, dtype=torch.bfloat16, device=ids.device)
-            if plan.slice_k and plan.out_ld != plan.out_width:
+            if plan.zero_fill or (plan.slice_k and plan.out_ld != plan.out_width):
                 out.zero_()  # padding columns of the per-token slices must read as zero
             ext().emb_forward(meta, store.peer_ptrs("slab"), store.rank, ids, offsets, dense,
                               plan.dense_width, out, chunks, error_word(ids.device), max_vec)

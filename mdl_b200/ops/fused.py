@@ -199,3 +199,34 @@ class HeadsBCEFn(torch.autograd.Function):
               b_mn=True, ldc=D, alpha=1.0 / T)
         dx = dpooled.unsqueeze(1).expand(B, T, D)
         return dx, None, None, None, None, None, None, None, None
+
+
+# ----------------------------------------------------------------------------- token mixing + LayerNorm
+class MixLayerNormFn(torch.autograd.Function):
+    """``LayerNorm(token_mix(x) + x)`` over ``[B, T, D]`` as one kernel each way
+    (the first half of a RankMixer block, reference ``src/model.py:6663``)."""
+
+    @staticmethod
+    def forward(ctx, x, g, b, eps):
+        B, T, D = x.shape
+        x = x.contiguous()
+        m = torch.empty_like(x)
+        mean = torch.empty(B * T, dtype=torch.float32, device=x.device)
+        rstd = torch.empty_like(mean)
+        ext().ln_fwd(x, None, g, b, m, mean, rstd, B, T, D, True, eps)
+        ctx.save_for_backward(x, mean, rstd)
+        ctx.params = (g, b)
+        return m
+
+    @staticmethod
+    def backward(ctx, dm):
+        x, mean, rstd = ctx.saved_tensors
+        g, b = ctx.params
+        B, T, D = x.shape
+        C = ext()
+        grid = C.ln_bwd_grid(B)
+        partials = torch.empty(grid, 2 * D, dtype=torch.float32, device=x.device)
+        dx = torch.empty_like(x)
+        C.ln_bwd(dm.contiguous().to(torch.bfloat16), None, 1.0, x, None, mean, rstd, g, dx, None, partials, _grad(g),
+                 _grad(b), B, T, D, True, grid)
+        return dx, None, None, None

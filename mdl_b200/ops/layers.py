@@ -1,0 +1,277 @@
+"""Reusable layers with a fused sm_100a path (CUDA) and a PyTorch path (CPU).
+
+* ``Linear``: ``y = x W^T + b`` as one tcgen05 GEMM; backward = two GEMMs plus a
+  column-sum for the bias (reference: ``nn.Linear`` under autocast).
+* ``PerTokenFFN``: N independent two-layer FFNs over ``[B, N, D]`` as two grouped
+  GEMMs, bias + GELU/ReLU fused in the first epilogue, the activation derivative
+  fused in the backward dgrad epilogue (reference ``PerTokenFFN`` /
+  ``StackedPerTokenFFN`` ``src/modules/mlp.py:53-207``).
+* ``few_query_attention``: multi-head attention of a few query tokens over a few
+  key tokens per sample, one CTA per (sample, head) (reference
+  ``DomainAwareAttention`` ``src/modules/attention.py:425-512``).
+
+GEMM weights carry ``_mdl_gemm = True``: ``DenseParams`` keeps a bf16 shadow for
+them. Fused nodes write parameter gradients into the flat gradient buffer
+(``param._mdl_grad``) and return no gradient for the parameter.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from ._ext import ext
+from .gemm import ACT_DGELU, ACT_DRELU, ACT_GELU, ACT_RELU, bgemm
+
+
+def _shadow(p):
+    s = getattr(p, "_mdl_shadow", None)
+    if s is None:
+        raise RuntimeError("parameter has no bf16 shadow (not registered in DenseParams)")
+    return s
+
+
+def _grad(p):
+    g = getattr(p, "_mdl_grad", None)
+    if g is None:
+        raise RuntimeError("parameter has no flat gradient view (not registered in DenseParams)")
+    return g
+
+
+def gemm_param(t: torch.Tensor) -> nn.Parameter:
+    p = nn.Parameter(t)
+    p._mdl_gemm = True
+    return p
+
+
+def _kaiming_uniform_(t: torch.Tensor, fan_in: int) -> None:
+    bound = 1.0 / math.sqrt(max(1, fan_in))
+    nn.init.uniform_(t, -bound, bound)
+
+
+# ============================================================================ Linear
+class LinearFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, bias):
+        M, K = x.shape
+        N = weight.shape[0]
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
+        bgemm(x, _shadow(weight), out, M=M, N=N, K=K, lda=x.stride(0), ldb=K, ldc=N, bias=bias)
+        ctx.save_for_backward(x)
+        ctx.params = (weight, bias)
+        return out
+
+    @staticmethod
+    def backward(ctx, dy):
+        (x,) = ctx.saved_tensors
+        weight, bias = ctx.params
+        M, K = x.shape
+        N = weight.shape[0]
+        dy = dy.contiguous().to(torch.bfloat16)
+        bgemm(dy, x, _grad(weight), M=N, N=K, K=M, lda=N, a_mn=True, ldb=x.stride(0), b_mn=True, ldc=K,
+              accumulate=True)
+        if bias is not None:
+            ext().colsum(dy, _grad(bias), 1, M, N, N, 0, 1.0)
+        dx = None
+        if ctx.needs_input_grad[0]:
+            dx = torch.empty(M, K, dtype=torch.bfloat16, device=x.device)
+            bgemm(dy, _shadow(weight), dx, M=M, N=K, K=N, lda=N, ldb=K, b_mn=True, ldc=K)
+        return dx, None, None
+
+
+class Linear(nn.Module):
+    """``nn.Linear`` layout (``weight [out, in]``) with the fused GEMM on CUDA."""
+
+    def __init__(self, in_features: int, out_features: int, bias: bool = True, device=None) -> None:
+        super().__init__()
+        self.in_features, self.out_features = in_features, out_features
+        self.weight = gemm_param(torch.empty(out_features, in_features, device=device))
+        self.bias = nn.Parameter(torch.empty(out_features, device=device)) if bias else None
+        _kaiming_uniform_(self.weight.data, in_features)
+        if self.bias is not None:
+            _kaiming_uniform_(self.bias.data, in_features)
+
+    def _fusable(self, x: torch.Tensor) -> bool:
+        return (x.is_cuda and hasattr(self.weight, "_mdl_shadow") and self.in_features % 8 == 0
+                and self.out_features % 8 == 0 and x.dim() == 2 and x.stride(-1) == 1 and x.stride(0) % 8 == 0)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self._fusable(x):
+            return LinearFn.apply(x.to(torch.bfloat16), self.weight, self.bias)
+        if x.is_cuda:
+            w = getattr(self.weight, "_mdl_shadow", None)
+            # narrow layers (e.g. width-1 outputs) below the TMA alignment: bf16 autocast-equivalent math
+            return F.linear(x.to(torch.bfloat16), self.weight.to(torch.bfloat16),
+                            None if self.bias is None else self.bias.to(torch.bfloat16))
+        return F.linear(x, self.weight, self.bias)
+
+
+# ============================================================================ PerTokenFFN
+class PerTokenFFNFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w_in, b_in, w_out, b_out, relu):
+        B, N, D = x.shape
+        H = w_in.shape[1]
+        Do = w_out.shape[1]
+        dev = x.device
+        # a token-strided view (e.g. some tokens of a wider [B, N', D] matrix) is read in place
+        if not (x.stride(2) == 1 and x.stride(1) == D and x.stride(0) % 8 == 0 and x.data_ptr() % 16 == 0):
+            x = x.contiguous()
+        lda = x.stride(0)
+        act = torch.empty(N, B, H, dtype=torch.bfloat16, device=dev)
+        if relu:
+            pre = None
+            bgemm(x, _shadow(w_in), act, M=B, N=H, K=D, G=N, lda=lda, gsA=D, ldb=D, gsB=H * D, ldc=H, gsC=B * H,
+                  bias=b_in, gs_bias=H, act=ACT_RELU)
+        else:
+            pre = torch.empty_like(act)
+            bgemm(x, _shadow(w_in), pre, M=B, N=H, K=D, G=N, lda=lda, gsA=D, ldb=D, gsB=H * D, ldc=H, gsC=B * H,
+                  out2=act, bias=b_in, gs_bias=H, act=ACT_GELU)
+        y = torch.empty(B, N, Do, dtype=torch.bfloat16, device=dev)
+        bgemm(act, _shadow(w_out), y, M=B, N=Do, K=H, G=N, lda=H, gsA=B * H, ldb=H, gsB=Do * H, ldc=N * Do, gsC=Do,
+              bias=b_out, gs_bias=Do)
+        ctx.save_for_backward(x, act, pre if pre is not None else act)
+        ctx.meta = (w_in, b_in, w_out, b_out, bool(relu))
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, act, pre = ctx.saved_tensors
+        w_in, b_in, w_out, b_out, relu = ctx.meta
+        B, N, D = x.shape
+        H = w_in.shape[1]
+        Do = w_out.shape[1]
+        dy = dy.contiguous().to(torch.bfloat16)
+        C = ext()
+        C.colsum(dy, _grad(b_out), N, B, Do, N * Do, Do, 1.0)
+        dpre = torch.empty_like(act)
+        bgemm(dy, _shadow(w_out), dpre, M=B, N=H, K=Do, G=N, lda=N * Do, gsA=Do, ldb=H, gsB=Do * H, b_mn=True,
+              ldc=H, gsC=B * H, aux=pre, ld_aux=H, gs_aux=B * H, colsum=_grad(b_in), gs_colsum=H,
+              act=ACT_DRELU if relu else ACT_DGELU)
+        bgemm(dy, act, _grad(w_out), M=Do, N=H, K=B, G=N, lda=N * Do, gsA=Do, a_mn=True, ldb=H, gsB=B * H,
+              b_mn=True, ldc=H, gsC=Do * H, accumulate=True)
+        bgemm(dpre, x, _grad(w_in), M=H, N=D, K=B, G=N, lda=H, gsA=B * H, a_mn=True, ldb=x.stride(0), gsB=D,
+              b_mn=True, ldc=D, gsC=H * D, accumulate=True)
+        dx = None
+        if ctx.needs_input_grad[0]:
+            dx = torch.empty(B, N, D, dtype=torch.bfloat16, device=x.device)
+            bgemm(dpre, _shadow(w_in), dx, M=B, N=D, K=H, G=N, lda=H, gsA=B * H, ldb=D, gsB=H * D, b_mn=True,
+                  ldc=N * D, gsC=D)
+        return dx, None, None, None, None, None
+
+
+class PerTokenFFN(nn.Module):
+    """N independent ``Linear(D,H) -> act -> Linear(H,D)`` networks over ``[B, N, D]``.
+
+    Parameter layout follows the reference ``StackedPerTokenFFN``
+    (``input_weight [N,H,D]``, ``input_bias [N,H]``, ``output_weight [N,D,H]``,
+    ``output_bias [N,D]``).
+    """
+
+    def __init__(self, num_tokens: int, token_dim: int, hidden_dim: int, activation: str = "gelu",
+                 output_relu: bool = False, device=None, out_dim: int | None = None) -> None:
+        super().__init__()
+        N, D, H = num_tokens, token_dim, hidden_dim
+        Do = out_dim or token_dim
+        self.num_tokens, self.token_dim, self.hidden_dim, self.out_dim = N, D, H, Do
+        self.relu = activation == "relu"
+        self.output_relu = output_relu
+        self.input_weight = gemm_param(torch.empty(N, H, D, device=device))
+        self.input_bias = nn.Parameter(torch.empty(N, H, device=device))
+        self.output_weight = gemm_param(torch.empty(N, Do, H, device=device))
+        self.output_bias = nn.Parameter(torch.empty(N, Do, device=device))
+        for t in range(N):
+            _kaiming_uniform_(self.input_weight.data[t], D)
+            _kaiming_uniform_(self.input_bias.data[t], D)
+            _kaiming_uniform_(self.output_weight.data[t], H)
+            _kaiming_uniform_(self.output_bias.data[t], H)
+
+    @torch.no_grad()
+    def restrict_inputs(self, widths: list[int]) -> None:
+        """Token ``t`` reads only its first ``widths[t]`` input columns: the rest of its
+        input weight is zero (and stays zero: those inputs are zero padding), and the
+        first layer is initialised with fan-in ``widths[t]``."""
+
+        for t, w in enumerate(widths):
+            self.input_weight[t].zero_()
+            _kaiming_uniform_(self.input_weight[t, :, :w], w)
+            _kaiming_uniform_(self.input_bias[t], w)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if x.is_cuda and hasattr(self.input_weight, "_mdl_shadow") and self.token_dim % 8 == 0 \
+                and self.hidden_dim % 8 == 0 and self.out_dim % 8 == 0:
+            y = PerTokenFFNFn.apply(x.to(torch.bfloat16), self.input_weight, self.input_bias, self.output_weight,
+                                    self.output_bias, self.relu)
+        else:
+            act = F.relu if self.relu else F.gelu
+            h = act(torch.einsum("bnd,nhd->bnh", x, self.input_weight) + self.input_bias.unsqueeze(0))
+            y = torch.einsum("bnh,ndh->bnd", h, self.output_weight) + self.output_bias.unsqueeze(0)
+        return F.relu(y) if self.output_relu else y
+
+
+# ============================================================================ attention
+class FewQueryAttentionFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, heads, key_valid):
+        B, Nq, D = q.shape
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        o = torch.empty_like(q)
+        lse = torch.empty(B, heads, Nq, dtype=torch.float32, device=q.device)
+        scale = 1.0 / math.sqrt(D // heads)
+        ext().small_attn_fwd(q, k, v, o, lse, key_valid, heads, scale)
+        ctx.save_for_backward(q, k, v, o, lse, key_valid if key_valid is not None else lse.new_empty(0))
+        ctx.meta = (heads, scale, key_valid is not None)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, o, lse, kv = ctx.saved_tensors
+        heads, scale, has_kv = ctx.meta
+        do = do.contiguous().to(torch.bfloat16)
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        ext().small_attn_bwd(q, k, v, o, lse, kv if has_kv else None, do, dq, dk, dv, heads, scale)
+        return dq, dk, dv, None, None
+
+
+def few_query_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int,
+                        key_valid: torch.Tensor | None = None) -> torch.Tensor:
+    """``softmax(Q K^T / sqrt(hd)) V`` per head for ``q [B,Nq,D]``, ``k, v [B,Nk,D]``."""
+
+    B, Nq, D = q.shape
+    Nk = k.shape[1]
+    if q.is_cuda and Nq <= 64 and Nk <= 64 and (D // heads) <= 128:
+        return FewQueryAttentionFn.apply(q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16), heads,
+                                         None if key_valid is None else key_valid.to(torch.int32))
+    hd = D // heads
+    qh = q.view(B, Nq, heads, hd).transpose(1, 2)
+    kh = k.view(B, Nk, heads, hd).transpose(1, 2)
+    vh = v.view(B, Nk, heads, hd).transpose(1, 2)
+    mask = None
+    if key_valid is not None:
+        mask = (torch.arange(Nk, device=q.device).view(1, 1, 1, Nk) < key_valid.view(B, 1, 1, 1))
+    out = F.scaled_dot_product_attention(qh, kh, vh, attn_mask=mask)
+    return out.transpose(1, 2).reshape(B, Nq, D)
+
+
+class DomainAwareAttention(nn.Module):
+    """Domain tokens (queries through a per-token FFN) attend to feature tokens
+    (keys/values through per-token FFNs); reference ``src/modules/attention.py:425-512``."""
+
+    def __init__(self, token_dim: int, num_heads: int, num_domain_tokens: int, num_feature_tokens: int,
+                 hidden_dim: int, activation: str = "gelu", device=None) -> None:
+        super().__init__()
+        if token_dim % num_heads:
+            raise ValueError("token_dim must be divisible by num_heads")
+        self.num_heads = num_heads
+        self.query_projection = PerTokenFFN(num_domain_tokens, token_dim, hidden_dim, activation, device=device)
+        self.key_projection = PerTokenFFN(num_feature_tokens, token_dim, hidden_dim, activation, device=device)
+        self.value_projection = PerTokenFFN(num_feature_tokens, token_dim, hidden_dim, activation, device=device)
+
+    def forward(self, domain_tokens: torch.Tensor, feature_tokens: torch.Tensor) -> torch.Tensor:
+        q = self.query_projection(domain_tokens)
+        k = self.key_projection(feature_tokens)
+        v = self.value_projection(feature_tokens)
+        return few_query_attention(q, k, v, self.num_heads)

@@ -129,8 +129,8 @@ def _run_parity_body(rank: int, world: int, device_type: str, out_path: str, opt
         load_full_tables(model.store)
         model.store.sync_peers()
         trainer = Trainer(cfg, model, device=device, rank=rank, world=world, process_group=dist.group.WORLD)
-        F = len(model.encoder.plan.features)
-        union = SyntheticGenerator(model.encoder.plan, spec, rank=0).batch(B * world)
+        F = len(model.encoder.batch_plan.features)
+        union = SyntheticGenerator(model.encoder.batch_plan, spec, rank=0).batch(B * world)
         local = union.slice_rows(rank * B, (rank + 1) * B, F)
         batch = local.to(device) if device.type == "cuda" else local
         out = trainer.forward_backward(batch)

@@ -216,7 +216,7 @@ def test_rankmixer_cuda_step_matches_cpu_reference():
     gpu_model.store.slab.copy_(cpu_model.store.slab)
     cpu_tr = Trainer(cfg, cpu_model, device=torch.device("cpu"))
     gpu_tr = Trainer(cfg, gpu_model, device=torch.device("cuda"))
-    gen = SyntheticGenerator(cpu_model.encoder.plan, spec)
+    gen = SyntheticGenerator(cpu_model.encoder.batch_plan, spec)
     batch = gen.batch(256)
     out_c = cpu_tr.forward_backward(batch)
     out_g = gpu_tr.forward_backward(batch.to("cuda"))
