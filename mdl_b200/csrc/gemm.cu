@@ -14,6 +14,12 @@
 //                 quarter (64 columns) of the 256-column accumulator
 // The accumulator is double-buffered in TMEM (2 x 256 fp32 columns) so the
 // epilogue of tile i overlaps the main loop of tile i+1.
+//
+// Epilogue data path: tcgen05.ld gives each lane one ROW of a 32x32 chunk, so
+// direct stores would touch 32 rows per instruction. Each warp instead stages
+// its chunk in shared memory (fp32, 36-float pitch: conflict-free 16-byte
+// accesses) and writes it back four rows x 128 bytes per instruction; the aux
+// operand of the activation-derivative epilogues is read the same way.
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -27,15 +33,19 @@ namespace {
 constexpr int BM = 128;
 constexpr int BN = 256;
 constexpr int BK = 64;   // 64 bf16 = 128 bytes = one swizzle row
-constexpr int STAGES = 4;
+constexpr int STAGES = 3;
 constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KB
 constexpr int B_STAGE_BYTES = BN * BK * 2;  // 32 KB
 constexpr int TMEM_COLS = 2 * BN;           // double-buffered accumulator
 constexpr int NUM_EPI_WARPS = 16;                // four warps per TMEM lane quarter
 constexpr int NUM_THREADS = 64 + NUM_EPI_WARPS * 32;
 constexpr int MN_CHUNK_BYTES = BK * 128;    // one 64-wide MN chunk of BK rows (MN-major)
+constexpr int EPI_PITCH = 36;               // floats per staged row (32 + 4 pad)
+constexpr int EPI_WARP_FLOATS = 32 * EPI_PITCH;
+constexpr int EPI_BYTES = NUM_EPI_WARPS * EPI_WARP_FLOATS * 4;  // 72 KB
 constexpr int SMEM_BYTES =
-    1024 + STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + (2 * STAGES + 4) * 8 + 16;
+    1024 + STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + EPI_BYTES + (2 * STAGES + 4) * 8 + 16;
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 
 struct EpiParams {
   void* out;
@@ -59,32 +69,14 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-__device__ __forceinline__ void unpack_bf16x8(const uint4& u, float* f) {
-  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    float2 t = __bfloat1622float2(h[i]);
-    f[2 * i] = t.x;
-    f[2 * i + 1] = t.y;
-  }
-}
+// Epilogue kinds (compile-time, so each instantiation carries only its own path).
+constexpr int EPI_PLAIN = 0;     // bf16 out, optional bias / ReLU / column sums
+constexpr int EPI_GELU = 1;      // bf16 pre-activation + bf16 GELU(pre)
+constexpr int EPI_AUX = 2;       // bf16 out scaled by GELU'(aux) or ReLU'(aux), optional column sums
+constexpr int EPI_ACC_BF16 = 3;  // bf16 out += result
+constexpr int EPI_F32 = 4;       // fp32 out (= or +=)
 
-// Reduce v[0..31] across the 32 lanes so that lane l ends with the column-l sum
-// in v[0] (recursive halving, 31 shuffles).
-__device__ __forceinline__ void warp_transpose_reduce32(float* v, int lane) {
-#pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) {
-    const bool upper = (lane & o) != 0;
-#pragma unroll
-    for (int i = 0; i < o; ++i) {
-      const float send = upper ? v[i] : v[i + o];
-      const float keep = upper ? v[i + o] : v[i];
-      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-    }
-  }
-}
-
-template <bool A_MN, bool B_MN>
+template <bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB, const EpiParams ep) {
@@ -93,7 +85,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_STAGE_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * B_STAGE_BYTES);
+  float* sEpi = reinterpret_cast<float*>(sB + STAGES * B_STAGE_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sEpi + NUM_EPI_WARPS * EPI_WARP_FLOATS);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
   uint64_t* tfull = bars + 2 * STAGES;
@@ -230,8 +223,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    // Per 32x32 chunk: tcgen05.ld (lane = row) -> stage in smem -> write-back where
+    // lane l owns columns 4*(l%8)..+3 of rows it*4 + l/8 (it = 0..7): bias,
+    // activation, accumulate and column sums act on 4 consecutive columns, and
+    // every global access is a coalesced 4-row x 128/64-byte pattern.
+    constexpr bool kF32 = EPI == EPI_F32;
+    constexpr bool kGelu = EPI == EPI_GELU;
+    constexpr bool kAux = EPI == EPI_AUX;
+    const bool accumulate = EPI == EPI_ACC_BF16 || (kF32 && ep.accumulate);
+    const bool relu = EPI == EPI_PLAIN && ep.act == GEMM_ACT_RELU;
     const int quarter = warp & 3;            // TMEM lane quarter this warp may read
     const int cgroup = (warp - 2) / 4;       // which 64-column group of the tile
+    float* stg = sEpi + (warp - 2) * EPI_WARP_FLOATS;
+    const int q = lane & 7;                  // 4-column group in the chunk (write-back)
+    const int rsub = lane >> 3;              // row within each 4-row step (write-back)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -241,122 +246,170 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int rem = tile - g * tiles_per_group;
       const int mb = rem / n_tiles;
       const int nb = rem - mb * n_tiles;
-      const int row = mb * BM + quarter * 32 + lane;
-      const bool row_ok = row < ep.M;
+      const int row0 = mb * BM + quarter * 32;  // first row of this warp's 32-row slab
       for (int c0 = cgroup * (BN / 4); c0 < (cgroup + 1) * (BN / 4); c0 += 32) {
         const int col0 = nb * BN + c0;
         if (col0 >= ep.N) break;  // warp-uniform
-        float v[32];
-        tmem_ld_32x32b_x32(
-            tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN + c0),
-            v);
-        const bool full_chunk = col0 + 32 <= ep.N;
+        const int gcol = col0 + q * 4;
+        const bool col_vec = gcol + 4 <= ep.N;
+        const int ncols = col_vec ? 4 : max(0, ep.N - gcol);
+        constexpr bool need_aux = kAux;
+        // Global reads of the chunk (aux or old output) run PF rows ahead: rows 0..PF-1 are
+        // requested before the TMEM load, row r+PF as soon as row r is consumed.
+        const bool need_read = need_aux || accumulate;
+        constexpr int PF = kF32 ? 2 : 4;  // rows in flight (fp32 rows need 4 registers each)
+        uint4 pf[PF];
+        auto prefetch = [&](int it) -> uint4 {
+          uint4 r4 = make_uint4(0u, 0u, 0u, 0u);
+          const int grow = row0 + it * 4 + rsub;
+          if (grow < ep.M && col_vec) {
+            if constexpr (need_aux) {
+              const uint2 a2 = __ldg(reinterpret_cast<const uint2*>(ep.aux + g * ep.gs_aux +
+                                                                   static_cast<long long>(grow) * ep.ld_aux + gcol));
+              r4 = make_uint4(a2.x, a2.y, 0u, 0u);
+            } else if (accumulate) {
+              const long long off = g * ep.gsC + static_cast<long long>(grow) * ep.ldc + gcol;
+              if (kF32) {
+                r4 = *reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(ep.out) + off);
+              } else {
+                const uint2 o = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(ep.out) + off);
+                r4 = make_uint4(o.x, o.y, 0u, 0u);
+              }
+            }
+          }
+          return r4;
+        };
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] *= ep.alpha;
-        if (ep.bias != nullptr) {
-          const float* bp = ep.bias + g * ep.gs_bias + col0;
+        for (int it = 0; it < PF; ++it) pf[it] = need_read ? prefetch(it) : make_uint4(0u, 0u, 0u, 0u);
+        float4 bias4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (ep.bias != nullptr && ncols > 0) {
+          const float* bp = ep.bias + g * ep.gs_bias + gcol;
+          if (col_vec && ((reinterpret_cast<uintptr_t>(bp) & 15) == 0)) {
+            bias4 = __ldg(reinterpret_cast<const float4*>(bp));
+          } else {
+            float b4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (full_chunk || col0 + i < ep.N) v[i] += __ldg(bp + i);
+            for (int e = 0; e < 4; ++e)
+              if (e < ncols) b4[e] = __ldg(bp + e);
+            bias4 = make_float4(b4[0], b4[1], b4[2], b4[3]);
+          }
         }
-        if (ep.act == GEMM_ACT_DGELU || ep.act == GEMM_ACT_DRELU) {
-          if (row_ok) {
-            const __nv_bfloat16* ap = ep.aux + g * ep.gs_aux + static_cast<long long>(row) * ep.ld_aux + col0;
-            float a[32];
-            if (full_chunk) {
-              const uint4* ap4 = reinterpret_cast<const uint4*>(ap);
+        {
+          float v[32];
+          tmem_ld_32x32b_x32(
+              tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN + c0), v);
 #pragma unroll
-              for (int q = 0; q < 4; ++q) unpack_bf16x8(__ldg(ap4 + q), a + 8 * q);
-            } else {
+          for (int k = 0; k < 8; ++k)
+            reinterpret_cast<float4*>(stg + lane * EPI_PITCH)[k] =
+                make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+        }
+        __syncwarp();
+        float csum[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-              for (int i = 0; i < 32; ++i) a[i] = (col0 + i < ep.N) ? __bfloat162float(ap[i]) : 0.f;
+        for (int it = 0; it < 8; ++it) {
+          const int r = it * 4 + rsub;
+          const int grow = row0 + r;
+          const uint4 cur = pf[it % PF];
+          if (it + PF < 8 && need_read) pf[it % PF] = prefetch(it + PF);
+          if (grow >= ep.M || ncols == 0) continue;
+          const float4 s4 = reinterpret_cast<const float4*>(stg + r * EPI_PITCH)[q];
+          float t[4] = {s4.x * ep.alpha + bias4.x, s4.y * ep.alpha + bias4.y, s4.z * ep.alpha + bias4.z,
+                        s4.w * ep.alpha + bias4.w};
+          const long long off = g * ep.gsC + static_cast<long long>(grow) * ep.ldc + gcol;
+          if constexpr (need_aux) {
+            uint32_t abits[4] = {cur.x & 0xFFFFu, cur.x >> 16, cur.y & 0xFFFFu, cur.y >> 16};
+            if (!col_vec) {
+              const __nv_bfloat16* ap = ep.aux + g * ep.gs_aux + static_cast<long long>(grow) * ep.ld_aux + gcol;
+#pragma unroll
+              for (int e = 0; e < 4; ++e) abits[e] = e < ncols ? __bfloat16_as_ushort(ap[e]) : 0u;
             }
             if (ep.act == GEMM_ACT_DGELU) {
 #pragma unroll
-              for (int i = 0; i < 32; ++i) v[i] *= gelu_erf_grad(a[i]);
+              for (int e = 0; e < 4; ++e) t[e] *= gelu_grad_fast(bf16_bits_to_float(abits[e]));
             } else {
 #pragma unroll
-              for (int i = 0; i < 32; ++i) v[i] = a[i] > 0.f ? v[i] : 0.f;
+              for (int e = 0; e < 4; ++e) t[e] = bf16_bits_to_float(abits[e]) > 0.f ? t[e] : 0.f;
             }
+          } else if (relu) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) t[e] = fmaxf(t[e], 0.f);
           }
-        }
-        if (ep.act == GEMM_ACT_RELU) {
+          if (ep.colsum != nullptr) {  // column sums of the product (before any accumulate)
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = fmaxf(v[i], 0.f);
-        }
-        if (row_ok) {
-          const long long off = g * ep.gsC + static_cast<long long>(row) * ep.ldc + col0;
-          if (ep.out_fp32) {
+            for (int e = 0; e < 4; ++e) csum[e] += t[e];
+          }
+          if (kF32) {
             float* op = reinterpret_cast<float*>(ep.out) + off;
-            if (full_chunk) {
-              float4* op4 = reinterpret_cast<float4*>(op);
-#pragma unroll
-              for (int q = 0; q < 8; ++q) {
-                float4 t = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-                if (ep.accumulate) {
-                  const float4 o = op4[q];
-                  t.x += o.x; t.y += o.y; t.z += o.z; t.w += o.w;
-                }
-                op4[q] = t;
+            if (col_vec) {
+              float4 o4 = make_float4(t[0], t[1], t[2], t[3]);
+              if (accumulate) {
+                const uint4 o = need_aux ? *reinterpret_cast<const uint4*>(op) : cur;
+                o4.x += __uint_as_float(o.x);
+                o4.y += __uint_as_float(o.y);
+                o4.z += __uint_as_float(o.z);
+                o4.w += __uint_as_float(o.w);
               }
+              *reinterpret_cast<float4*>(op) = o4;
             } else {
-              for (int i = 0; i < 32; ++i)
-                if (col0 + i < ep.N) op[i] = ep.accumulate ? op[i] + v[i] : v[i];
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                if (e < ncols) op[e] = accumulate ? op[e] + t[e] : t[e];
             }
           } else {
             __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(ep.out) + off;
-            __nv_bfloat16* op2 = ep.out2 != nullptr ? ep.out2 + off : nullptr;
-            if (full_chunk) {
-              uint4* o4 = reinterpret_cast<uint4*>(op);
-              if (ep.accumulate) {
+            if (accumulate) {
+              if (col_vec) {
+                const uint2 o = need_aux ? *reinterpret_cast<const uint2*>(op) : make_uint2(cur.x, cur.y);
+                t[0] += bf16_bits_to_float(o.x & 0xFFFFu);
+                t[1] += bf16_bits_to_float(o.x >> 16);
+                t[2] += bf16_bits_to_float(o.y & 0xFFFFu);
+                t[3] += bf16_bits_to_float(o.y >> 16);
+              } else {
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                  float old[8];
-                  unpack_bf16x8(o4[q], old);
-#pragma unroll
-                  for (int e = 0; e < 8; ++e) v[8 * q + e] += old[e];
-                }
+                for (int e = 0; e < 4; ++e)
+                  if (e < ncols) t[e] += __bfloat162float(op[e]);
               }
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                uint4 t;
-                t.x = pack_bf16x2(v[8 * q + 0], v[8 * q + 1]);
-                t.y = pack_bf16x2(v[8 * q + 2], v[8 * q + 3]);
-                t.z = pack_bf16x2(v[8 * q + 4], v[8 * q + 5]);
-                t.w = pack_bf16x2(v[8 * q + 6], v[8 * q + 7]);
-                o4[q] = t;
-              }
-              if (ep.act == GEMM_ACT_GELU) {
-                uint4* o24 = reinterpret_cast<uint4*>(op2);
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                  uint4 t;
-                  t.x = pack_bf16x2(gelu_erf(v[8 * q + 0]), gelu_erf(v[8 * q + 1]));
-                  t.y = pack_bf16x2(gelu_erf(v[8 * q + 2]), gelu_erf(v[8 * q + 3]));
-                  t.z = pack_bf16x2(gelu_erf(v[8 * q + 4]), gelu_erf(v[8 * q + 5]));
-                  t.w = pack_bf16x2(gelu_erf(v[8 * q + 6]), gelu_erf(v[8 * q + 7]));
-                  o24[q] = t;
-                }
-              }
+            }
+            const uint32_t p01 = pack_bf16x2(t[0], t[1]), p23 = pack_bf16x2(t[2], t[3]);
+            if (col_vec) {
+              *reinterpret_cast<uint2*>(op) = make_uint2(p01, p23);
             } else {
-              for (int i = 0; i < 32; ++i) {
-                if (col0 + i < ep.N) {
-                  if (ep.accumulate) v[i] += __bfloat162float(op[i]);
-                  op[i] = __float2bfloat16_rn(v[i]);
-                  if (ep.act == GEMM_ACT_GELU) op2[i] = __float2bfloat16_rn(gelu_erf(v[i]));
-                }
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                if (e < ncols) op[e] = __float2bfloat16_rn(t[e]);
+            }
+            if constexpr (kGelu) {
+              // GELU of the stored (bf16) pre-activation
+              const float a0 = gelu_fast(bf16_bits_to_float(p01 & 0xFFFFu));
+              const float a1 = gelu_fast(bf16_bits_to_float(p01 >> 16));
+              const float a2 = gelu_fast(bf16_bits_to_float(p23 & 0xFFFFu));
+              const float a3 = gelu_fast(bf16_bits_to_float(p23 >> 16));
+              if (col_vec) {
+                *reinterpret_cast<uint2*>(ep.out2 + off) = make_uint2(pack_bf16x2(a0, a1), pack_bf16x2(a2, a3));
+              } else {
+                const float av[4] = {a0, a1, a2, a3};
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                  if (e < ncols) ep.out2[off + e] = __float2bfloat16_rn(av[e]);
               }
             }
           }
         }
         if (ep.colsum != nullptr) {
-          // Column sums of what this epilogue produced (gelu output excluded).
+          // lanes q, q+8, q+16, q+24 hold the same four columns: reduce, then lanes 0..7 add
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (!row_ok) v[i] = 0.f;
-          warp_transpose_reduce32(v, lane);
-          if (col0 + lane < ep.N) atomicAdd(ep.colsum + g * ep.gs_colsum + col0 + lane, v[0]);
+          for (int e = 0; e < 4; ++e) {
+            csum[e] += __shfl_xor_sync(0xffffffffu, csum[e], 8);
+            csum[e] += __shfl_xor_sync(0xffffffffu, csum[e], 16);
+          }
+          if (rsub == 0) {
+            float* cp = ep.colsum + g * ep.gs_colsum + gcol;
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              if (e < ncols) atomicAdd(cp + e, csum[e]);
+          }
         }
+        __syncwarp();
       }
       tc_fence_before();
       __syncwarp();
@@ -413,10 +466,10 @@ int num_sms() {
   return n;
 }
 
-template <bool A_MN, bool B_MN>
-cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const EpiParams& ep, int grid,
-                   cudaStream_t stream) {
-  auto kern = gemm_tcgen05_kernel<A_MN, B_MN>;
+template <bool A_MN, bool B_MN, int EPI>
+cudaError_t launch_kind(const CUtensorMap& ta, const CUtensorMap& tb, const EpiParams& ep, int grid,
+                        cudaStream_t stream) {
+  auto kern = gemm_tcgen05_kernel<A_MN, B_MN, EPI>;
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
@@ -425,6 +478,28 @@ cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const EpiParams
   }
   kern<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ta, tb, ep);
   return cudaGetLastError();
+}
+
+template <bool A_MN, bool B_MN>
+cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const EpiParams& ep, int epi, int grid,
+                   cudaStream_t stream) {
+  switch (epi) {
+    case EPI_PLAIN: return launch_kind<A_MN, B_MN, EPI_PLAIN>(ta, tb, ep, grid, stream);
+    case EPI_GELU: return launch_kind<A_MN, B_MN, EPI_GELU>(ta, tb, ep, grid, stream);
+    case EPI_AUX: return launch_kind<A_MN, B_MN, EPI_AUX>(ta, tb, ep, grid, stream);
+    case EPI_ACC_BF16: return launch_kind<A_MN, B_MN, EPI_ACC_BF16>(ta, tb, ep, grid, stream);
+    default: return launch_kind<A_MN, B_MN, EPI_F32>(ta, tb, ep, grid, stream);
+  }
+}
+
+// Epilogue kind of a call; -1 for a combination no kernel implements.
+int epilogue_kind(const GemmArgs& a) {
+  const bool aux_act = a.act == GEMM_ACT_DGELU || a.act == GEMM_ACT_DRELU;
+  if (a.out_fp32) return (a.act == GEMM_ACT_NONE && a.out2 == nullptr && a.colsum == nullptr) ? EPI_F32 : -1;
+  if (a.act == GEMM_ACT_GELU) return (!a.accumulate && a.out2 != nullptr) ? EPI_GELU : -1;
+  if (aux_act) return (!a.accumulate && a.aux != nullptr) ? EPI_AUX : -1;
+  if (a.accumulate) return a.act == GEMM_ACT_NONE ? EPI_ACC_BF16 : -1;
+  return EPI_PLAIN;
 }
 
 }  // namespace
@@ -436,6 +511,14 @@ cudaError_t gemm_bf16_tcgen05(const GemmArgs& a, cudaStream_t stream) {
     return cudaErrorInvalidValue;
   if (!a.out_fp32 && (a.ldc % 8)) return cudaErrorInvalidValue;
   if (a.out_fp32 && (a.ldc % 4)) return cudaErrorInvalidValue;
+  // vector epilogue stores: 16 bytes (fp32) / 8 bytes (bf16) per lane; aux read 16 bytes per lane
+  if (a.G > 1 && (a.gsC % 4)) return cudaErrorInvalidValue;
+  if (reinterpret_cast<uintptr_t>(a.out) & (a.out_fp32 ? 15 : 7)) return cudaErrorInvalidValue;
+  if (a.out2 != nullptr && (reinterpret_cast<uintptr_t>(a.out2) & 7)) return cudaErrorInvalidValue;
+  if (a.aux != nullptr && ((a.ld_aux % 8) || (a.G > 1 && (a.gs_aux % 8)) || (reinterpret_cast<uintptr_t>(a.aux) & 15)))
+    return cudaErrorInvalidValue;
+  const int epi = epilogue_kind(a);
+  if (epi < 0) return cudaErrorInvalidValue;
   CUtensorMap ta, tb;
   bool ok;
   if (!a.a_mn_major)
@@ -476,11 +559,11 @@ cudaError_t gemm_bf16_tcgen05(const GemmArgs& a, cudaStream_t stream) {
   if (a.max_ctas > 0 && a.max_ctas < grid) grid = a.max_ctas;
   if (tiles < grid) grid = static_cast<int>(tiles);
   if (a.a_mn_major) {
-    return a.b_mn_major ? launch<true, true>(ta, tb, ep, grid, stream)
-                        : launch<true, false>(ta, tb, ep, grid, stream);
+    return a.b_mn_major ? launch<true, true>(ta, tb, ep, epi, grid, stream)
+                        : launch<true, false>(ta, tb, ep, epi, grid, stream);
   }
-  return a.b_mn_major ? launch<false, true>(ta, tb, ep, grid, stream)
-                      : launch<false, false>(ta, tb, ep, grid, stream);
+  return a.b_mn_major ? launch<false, true>(ta, tb, ep, epi, grid, stream)
+                      : launch<false, false>(ta, tb, ep, epi, grid, stream);
 }
 
 }  // namespace mdl
