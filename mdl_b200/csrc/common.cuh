@@ -233,6 +233,19 @@ __device__ __forceinline__ float gelu_fast(float x) {
   return gelu_erf_tail(x);
 }
 
+// GELU(x) and, when `want_grad`, GELU'(x) sharing one evaluation of Phi.
+__device__ __forceinline__ void gelu_and_grad_fast(float x, float& g, float& dg, bool want_grad) {
+  if (fabsf(x) <= 3.f) {
+    const float u = x * x;
+    const float p = phi_minus_half_over_x(u);
+    g = x * fmaf(x, p, 0.5f);
+    dg = want_grad ? fmaf(x, p + kInvSqrt2Pi * __expf(-0.5f * u), 0.5f) : 0.f;
+  } else {
+    g = gelu_erf_tail(x);
+    dg = want_grad ? gelu_erf_grad_tail(x) : 0.f;
+  }
+}
+
 __device__ __forceinline__ float gelu_grad_fast(float x) {
   if (fabsf(x) <= 3.f) {
     const float u = x * x;

@@ -71,8 +71,8 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
 
 // Epilogue kinds (compile-time, so each instantiation carries only its own path).
 constexpr int EPI_PLAIN = 0;     // bf16 out, optional bias / ReLU / column sums
-constexpr int EPI_GELU = 1;      // bf16 pre-activation + bf16 GELU(pre)
-constexpr int EPI_AUX = 2;       // bf16 out scaled by GELU'(aux) or ReLU'(aux), optional column sums
+constexpr int EPI_GELU = 1;      // bf16 pre-activation (or GELU'(pre)) + bf16 GELU(pre)
+constexpr int EPI_AUX = 2;       // bf16 out scaled by GELU'(aux), ReLU'(aux) or aux; optional column sums
 constexpr int EPI_ACC_BF16 = 3;  // bf16 out += result
 constexpr int EPI_F32 = 4;       // fp32 out (= or +=)
 
@@ -232,6 +232,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     constexpr bool kAux = EPI == EPI_AUX;
     const bool accumulate = EPI == EPI_ACC_BF16 || (kF32 && ep.accumulate);
     const bool relu = EPI == EPI_PLAIN && ep.act == GEMM_ACT_RELU;
+    const bool affine = ep.alpha != 1.f || ep.bias != nullptr;
+    const bool store_grad = kGelu && ep.act == GEMM_ACT_GELU_GRAD;
     const int quarter = warp & 3;            // TMEM lane quarter this warp may read
     const int cgroup = (warp - 2) / 4;       // which 64-column group of the tile
     float* stg = sEpi + (warp - 2) * EPI_WARP_FLOATS;
@@ -313,8 +315,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (it + PF < 8 && need_read) pf[it % PF] = prefetch(it + PF);
           if (grow >= ep.M || ncols == 0) continue;
           const float4 s4 = reinterpret_cast<const float4*>(stg + r * EPI_PITCH)[q];
-          float t[4] = {s4.x * ep.alpha + bias4.x, s4.y * ep.alpha + bias4.y, s4.z * ep.alpha + bias4.z,
-                        s4.w * ep.alpha + bias4.w};
+          float t[4] = {s4.x, s4.y, s4.z, s4.w};
+          if (affine) {
+            t[0] = fmaf(t[0], ep.alpha, bias4.x);
+            t[1] = fmaf(t[1], ep.alpha, bias4.y);
+            t[2] = fmaf(t[2], ep.alpha, bias4.z);
+            t[3] = fmaf(t[3], ep.alpha, bias4.w);
+          }
           const long long off = g * ep.gsC + static_cast<long long>(grow) * ep.ldc + gcol;
           if constexpr (need_aux) {
             uint32_t abits[4] = {cur.x & 0xFFFFu, cur.x >> 16, cur.y & 0xFFFFu, cur.y >> 16};
@@ -323,7 +330,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
               for (int e = 0; e < 4; ++e) abits[e] = e < ncols ? __bfloat16_as_ushort(ap[e]) : 0u;
             }
-            if (ep.act == GEMM_ACT_DGELU) {
+            if (ep.act == GEMM_ACT_DMUL) {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) t[e] *= bf16_bits_to_float(abits[e]);
+            } else if (ep.act == GEMM_ACT_DGELU) {
 #pragma unroll
               for (int e = 0; e < 4; ++e) t[e] *= gelu_grad_fast(bf16_bits_to_float(abits[e]));
             } else {
@@ -371,19 +381,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               }
             }
             const uint32_t p01 = pack_bf16x2(t[0], t[1]), p23 = pack_bf16x2(t[2], t[3]);
-            if (col_vec) {
-              *reinterpret_cast<uint2*>(op) = make_uint2(p01, p23);
-            } else {
-#pragma unroll
-              for (int e = 0; e < 4; ++e)
-                if (e < ncols) op[e] = __float2bfloat16_rn(t[e]);
-            }
             if constexpr (kGelu) {
-              // GELU of the stored (bf16) pre-activation
-              const float a0 = gelu_fast(bf16_bits_to_float(p01 & 0xFFFFu));
-              const float a1 = gelu_fast(bf16_bits_to_float(p01 >> 16));
-              const float a2 = gelu_fast(bf16_bits_to_float(p23 & 0xFFFFu));
-              const float a3 = gelu_fast(bf16_bits_to_float(p23 >> 16));
+              // GELU (and optionally GELU') of the bf16 pre-activation
+              const float x[4] = {bf16_bits_to_float(p01 & 0xFFFFu), bf16_bits_to_float(p01 >> 16),
+                                  bf16_bits_to_float(p23 & 0xFFFFu), bf16_bits_to_float(p23 >> 16)};
+              float a[4], d[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) gelu_and_grad_fast(x[e], a[e], d[e], store_grad);
+              const uint32_t o01 = store_grad ? pack_bf16x2(d[0], d[1]) : p01;
+              const uint32_t o23 = store_grad ? pack_bf16x2(d[2], d[3]) : p23;
+              if (col_vec) {
+                *reinterpret_cast<uint2*>(op) = make_uint2(o01, o23);
+              } else {
+                const float ov[4] = {store_grad ? d[0] : t[0], store_grad ? d[1] : t[1], store_grad ? d[2] : t[2],
+                                     store_grad ? d[3] : t[3]};
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                  if (e < ncols) op[e] = __float2bfloat16_rn(ov[e]);
+              }
+              const float a0 = a[0], a1 = a[1], a2 = a[2], a3 = a[3];
               if (col_vec) {
                 *reinterpret_cast<uint2*>(ep.out2 + off) = make_uint2(pack_bf16x2(a0, a1), pack_bf16x2(a2, a3));
               } else {
@@ -391,6 +407,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
                 for (int e = 0; e < 4; ++e)
                   if (e < ncols) ep.out2[off + e] = __float2bfloat16_rn(av[e]);
+              }
+            } else {
+              if (col_vec) {
+                *reinterpret_cast<uint2*>(op) = make_uint2(p01, p23);
+              } else {
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                  if (e < ncols) op[e] = __float2bfloat16_rn(t[e]);
               }
             }
           }
@@ -494,9 +518,10 @@ cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const EpiParams
 
 // Epilogue kind of a call; -1 for a combination no kernel implements.
 int epilogue_kind(const GemmArgs& a) {
-  const bool aux_act = a.act == GEMM_ACT_DGELU || a.act == GEMM_ACT_DRELU;
+  const bool aux_act = a.act == GEMM_ACT_DGELU || a.act == GEMM_ACT_DRELU || a.act == GEMM_ACT_DMUL;
   if (a.out_fp32) return (a.act == GEMM_ACT_NONE && a.out2 == nullptr && a.colsum == nullptr) ? EPI_F32 : -1;
-  if (a.act == GEMM_ACT_GELU) return (!a.accumulate && a.out2 != nullptr) ? EPI_GELU : -1;
+  if (a.act == GEMM_ACT_GELU || a.act == GEMM_ACT_GELU_GRAD)
+    return (!a.accumulate && a.out2 != nullptr) ? EPI_GELU : -1;
   if (aux_act) return (!a.accumulate && a.aux != nullptr) ? EPI_AUX : -1;
   if (a.accumulate) return a.act == GEMM_ACT_NONE ? EPI_ACC_BF16 : -1;
   return EPI_PLAIN;

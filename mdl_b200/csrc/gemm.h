@@ -13,6 +13,9 @@ enum GemmAct : int {
   GEMM_ACT_DGELU = 2,  // out = acc * gelu'(aux)
   GEMM_ACT_RELU = 3,   // out = relu(acc)
   GEMM_ACT_DRELU = 4,  // out = acc * (aux > 0)
+  // GELU pair that saves the derivative instead of the pre-activation:
+  GEMM_ACT_GELU_GRAD = 5,  // x = bf16(acc): out = gelu'(x), out2 = gelu(x)
+  GEMM_ACT_DMUL = 6,       // out = acc * aux (aux = the saved derivative)
 };
 
 // C[g] = epilogue(alpha * A[g] @ B[g]^T) for g in [0, G).

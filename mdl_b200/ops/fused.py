@@ -26,7 +26,7 @@ from __future__ import annotations
 import torch
 
 from ._ext import ext
-from .gemm import ACT_DGELU, ACT_GELU, ACT_NONE, bgemm
+from .gemm import ACT_DMUL, ACT_GELU, ACT_GELU_GRAD, ACT_NONE, bgemm
 
 
 def _shadow(p: torch.Tensor) -> torch.Tensor:
@@ -96,7 +96,7 @@ class RankMixerBlockFn(torch.autograd.Function):
         pre = torch.empty(T, B, H, dtype=torch.bfloat16, device=dev)
         act = torch.empty_like(pre)
         bgemm(m, _shadow(w_in), pre, M=B, N=H, K=D, G=T, lda=T * D, gsA=D, ldb=D, gsB=H * D, ldc=H, gsC=B * H,
-              out2=act, bias=b_in, gs_bias=H, act=ACT_GELU)
+              out2=act, bias=b_in, gs_bias=H, act=ACT_GELU_GRAD)  # pre <- gelu'(pre-activation)
         f = torch.empty_like(x)
         bgemm(act, _shadow(w_out), f, M=B, N=D, K=H, G=T, lda=H, gsA=B * H, ldb=H, gsB=D * H, ldc=T * D, gsC=D,
               bias=b_out, gs_bias=D)
@@ -132,7 +132,7 @@ class RankMixerBlockFn(torch.autograd.Function):
         # dPre = (df_t @ W_out[t]) * gelu'(pre);  colsum -> d b_in
         dpre = torch.empty_like(pre)
         bgemm(df, _shadow(w_out), dpre, M=B, N=H, K=D, G=T, lda=T * D, gsA=D, ldb=H, gsB=D * H, b_mn=True, ldc=H,
-              gsC=B * H, aux=pre, ld_aux=H, gs_aux=B * H, colsum=_grad(b_in), gs_colsum=H, act=ACT_DGELU)
+              gsC=B * H, aux=pre, ld_aux=H, gs_aux=B * H, colsum=_grad(b_in), gs_colsum=H, act=ACT_DMUL)
         # dW_out[t] += df_t^T @ act_t
         bgemm(df, act, _grad(w_out), M=D, N=H, K=B, G=T, lda=T * D, gsA=D, a_mn=True, ldb=H, gsB=B * H, b_mn=True,
               ldc=H, gsC=D * H, accumulate=True)

@@ -1,4 +1,4 @@
-"""Batched GEMM with fused epilogues (bias, GELU / dGELU, ReLU, column sums).
+"""Batched GEMM with fused epilogues (bias, GELU / GELU-with-derivative / dGELU, ReLU, column sums).
 
 On CUDA tensors this calls the persistent tcgen05 kernel in ``csrc/gemm.cu``;
 on CPU tensors it evaluates the same contract with PyTorch in fp32, which is
@@ -28,6 +28,8 @@ ACT_GELU = 1
 ACT_DGELU = 2
 ACT_RELU = 3
 ACT_DRELU = 4
+ACT_GELU_GRAD = 5  # x = bf16(acc): out = gelu'(x), out2 = gelu(x)  (saves the derivative for the backward)
+ACT_DMUL = 6       # out = acc * aux
 
 
 def _view(t: torch.Tensor, g: int, rows: int, cols: int, gs: int, ld: int, mn_major: bool) -> torch.Tensor:
@@ -87,13 +89,17 @@ def bgemm(
     acc = torch.bmm(av, bv.transpose(1, 2)) * alpha
     if bias is not None:
         acc = acc + bias.as_strided((G, 1, N), (gs_bias, 0, 1)).float()
-    if act in (ACT_DGELU, ACT_DRELU):
+    if act in (ACT_DGELU, ACT_DRELU, ACT_DMUL):
         auxv = aux.as_strided((G, M, N), (gs_aux, ld_aux, 1)).float()
-        acc = acc * (gelu_grad(auxv) if act == ACT_DGELU else (auxv > 0).float())
+        acc = acc * {ACT_DGELU: gelu_grad, ACT_DRELU: lambda a: (a > 0).float(), ACT_DMUL: lambda a: a}[act](auxv)
     if act == ACT_RELU:
         acc = F.relu(acc)
     outv = out.as_strided((G, M, N), (gsC, ldc, 1))
-    if accumulate:
+    if act == ACT_GELU_GRAD:
+        x = acc.to(torch.bfloat16).float()
+        outv.copy_(gelu_grad(x).to(out.dtype))
+        out2.as_strided((G, M, N), (gsC, ldc, 1)).copy_(F.gelu(x).to(out2.dtype))
+    elif accumulate:
         outv.copy_(outv.float() + acc)
     else:
         outv.copy_(acc.to(out.dtype))

@@ -24,7 +24,7 @@ import torch.nn.functional as F
 from torch import nn
 
 from ._ext import ext
-from .gemm import ACT_DGELU, ACT_DRELU, ACT_GELU, ACT_RELU, bgemm
+from .gemm import ACT_DMUL, ACT_DRELU, ACT_GELU_GRAD, ACT_RELU, bgemm
 
 
 def _shadow(p):
@@ -127,9 +127,9 @@ class PerTokenFFNFn(torch.autograd.Function):
             bgemm(x, _shadow(w_in), act, M=B, N=H, K=D, G=N, lda=lda, gsA=D, ldb=D, gsB=H * D, ldc=H, gsC=B * H,
                   bias=b_in, gs_bias=H, act=ACT_RELU)
         else:
-            pre = torch.empty_like(act)
+            pre = torch.empty_like(act)  # holds gelu'(pre-activation)
             bgemm(x, _shadow(w_in), pre, M=B, N=H, K=D, G=N, lda=lda, gsA=D, ldb=D, gsB=H * D, ldc=H, gsC=B * H,
-                  out2=act, bias=b_in, gs_bias=H, act=ACT_GELU)
+                  out2=act, bias=b_in, gs_bias=H, act=ACT_GELU_GRAD)
         y = torch.empty(B, N, Do, dtype=torch.bfloat16, device=dev)
         bgemm(act, _shadow(w_out), y, M=B, N=Do, K=H, G=N, lda=H, gsA=B * H, ldb=H, gsB=Do * H, ldc=N * Do, gsC=Do,
               bias=b_out, gs_bias=Do)
@@ -150,7 +150,7 @@ class PerTokenFFNFn(torch.autograd.Function):
         dpre = torch.empty_like(act)
         bgemm(dy, _shadow(w_out), dpre, M=B, N=H, K=Do, G=N, lda=N * Do, gsA=Do, ldb=H, gsB=Do * H, b_mn=True,
               ldc=H, gsC=B * H, aux=pre, ld_aux=H, gs_aux=B * H, colsum=_grad(b_in), gs_colsum=H,
-              act=ACT_DRELU if relu else ACT_DGELU)
+              act=ACT_DRELU if relu else ACT_DMUL)
         bgemm(dy, act, _grad(w_out), M=Do, N=H, K=B, G=N, lda=N * Do, gsA=Do, a_mn=True, ldb=H, gsB=B * H,
               b_mn=True, ldc=H, gsC=Do * H, accumulate=True)
         bgemm(dpre, x, _grad(w_in), M=H, N=D, K=B, G=N, lda=H, gsA=B * H, a_mn=True, ldb=x.stride(0), gsB=D,

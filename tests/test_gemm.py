@@ -58,7 +58,8 @@ def test_gemm_tcgen05_layouts(a_mn, b_mn, shape):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("act", [G.ACT_NONE, G.ACT_GELU, G.ACT_DGELU, G.ACT_RELU])
+@pytest.mark.parametrize("act", [G.ACT_NONE, G.ACT_GELU, G.ACT_DGELU, G.ACT_RELU, G.ACT_DRELU, G.ACT_GELU_GRAD,
+                                 G.ACT_DMUL])
 def test_gemm_tcgen05_epilogues(act):
     M, N, K, Gn = 384, 512, 256, 2
     a, lda, gsA, b, ldb, gsB = _operands(M, N, K, Gn, False, True, "cuda")
@@ -78,7 +79,7 @@ def test_gemm_tcgen05_epilogues(act):
             colsum=ref_cs, gs_colsum=N, act=act, alpha=0.5)
     torch.cuda.synchronize()
     torch.testing.assert_close(out.cpu().float(), ref_out.float(), atol=0.05, rtol=0.02)
-    if act == G.ACT_GELU:
+    if act in (G.ACT_GELU, G.ACT_GELU_GRAD):
         torch.testing.assert_close(out2.cpu().float(), ref_out2.float(), atol=0.05, rtol=0.02)
     torch.testing.assert_close(colsum.cpu(), ref_cs, atol=0.5, rtol=0.02)
 
