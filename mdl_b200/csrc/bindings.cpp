@@ -199,23 +199,48 @@ mdl::AdagradArgs adagrad_args(const at::Tensor& slab, const at::Tensor& grad_sla
   return a;
 }
 
+void set_list(mdl::AdagradArgs& a, const std::optional<at::Tensor>& list, const std::optional<at::Tensor>& count) {
+  if (list.has_value() != count.has_value()) TORCH_CHECK(false, "touched list and count go together");
+  if (!list.has_value()) return;
+  TORCH_CHECK(list->scalar_type() == at::kInt && list->numel() >= a.total_rows, "touched list: int32 [total_rows]");
+  TORCH_CHECK(count->scalar_type() == at::kInt && count->numel() >= 1, "touched count: int32 [1]");
+  a.list = reinterpret_cast<unsigned*>(list->data_ptr());
+  a.count = reinterpret_cast<unsigned*>(count->data_ptr());
+}
+
 void adagrad_apply(const at::Tensor& slab, const at::Tensor& grad_slab, const at::Tensor& acc, const at::Tensor& flags,
                    int64_t total_rows, const at::Tensor& t_base, const at::Tensor& t_row_base,
                    const at::Tensor& t_dim, double lr, double eps, double grad_scale,
-                   const std::optional<at::Tensor>& clip, const std::optional<at::Tensor>& err, int64_t max_dim) {
+                   const std::optional<at::Tensor>& clip, const std::optional<at::Tensor>& err, int64_t max_dim,
+                   const std::optional<at::Tensor>& list, const std::optional<at::Tensor>& count) {
   c10::cuda::CUDAGuard guard(slab.device());
   auto a = adagrad_args(slab, grad_slab, acc, flags, total_rows, t_base, t_row_base, t_dim, lr, eps, grad_scale,
                         clip, err, max_dim);
+  set_list(a, list, count);
   check(mdl::rowwise_adagrad_apply(a, stream_of(slab)), "rowwise_adagrad_apply");
+  g_launches += 1;
+}
+
+void compact_touched(const at::Tensor& flags, int64_t total_rows, const at::Tensor& list, const at::Tensor& count) {
+  c10::cuda::CUDAGuard guard(flags.device());
+  TORCH_CHECK(flags.scalar_type() == at::kByte && flags.numel() >= (total_rows + 511) / 512 * 512,
+              "flags must be uint8 padded to a multiple of 512 rows");
+  mdl::AdagradArgs a;
+  a.flags = ptr<unsigned char>(flags);
+  a.total_rows = total_rows;
+  set_list(a, list, count);
+  check(mdl::compact_touched(a, stream_of(flags)), "compact_touched");
   g_launches += 1;
 }
 
 void touched_sqnorm(const at::Tensor& grad_slab, const at::Tensor& flags, int64_t total_rows,
                     const at::Tensor& t_base, const at::Tensor& t_row_base, const at::Tensor& t_dim, double grad_scale,
-                    const at::Tensor& out) {
+                    const at::Tensor& out, const std::optional<at::Tensor>& list,
+                    const std::optional<at::Tensor>& count, int64_t max_dim) {
   c10::cuda::CUDAGuard guard(grad_slab.device());
   mdl::AdagradArgs a = adagrad_args(grad_slab, grad_slab, grad_slab, flags, total_rows, t_base, t_row_base, t_dim,
-                                    0.0, 1.0, grad_scale, std::nullopt, std::nullopt, 1024);
+                                    0.0, 1.0, grad_scale, std::nullopt, std::nullopt, max_dim);
+  set_list(a, list, count);
   check(mdl::touched_grad_sqnorm(a, ptr<float>(out), stream_of(grad_slab)), "touched_grad_sqnorm");
   g_launches += 1;
 }
@@ -582,6 +607,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("emb_backward", &emb_backward);
   m.def("adagrad_apply", &adagrad_apply);
   m.def("touched_sqnorm", &touched_sqnorm);
+  m.def("compact_touched", &compact_touched);
   m.def("ln_fwd", &ln_fwd);
   m.def("ln_bwd_grid", &ln_bwd_grid);
   m.def("ln_bwd", &ln_bwd);

@@ -401,6 +401,154 @@ __global__ void __launch_bounds__(kThreads) rowwise_adagrad_thread_kernel(const 
   }
 }
 
+// ---- touched-row list: compaction, then a coalesced update per row ----------
+__global__ void __launch_bounds__(kThreads) compact_touched_kernel(const AdagradArgs a) {
+  __shared__ unsigned s_warp[kThreads / 32];
+  __shared__ unsigned s_base;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const long long n16 = (a.total_rows + 15) / 16;
+  uint4* flags16 = reinterpret_cast<uint4*>(a.flags);
+  for (long long base = static_cast<long long>(blockIdx.x) * blockDim.x; base < n16;
+       base += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long c = base + threadIdx.x;
+    uint4 f = make_uint4(0u, 0u, 0u, 0u);
+    if (c < n16) f = flags16[c];
+    // one bit per touched row of this thread's 16
+    unsigned bits = 0;
+    const unsigned words[4] = {f.x, f.y, f.z, f.w};
+#pragma unroll
+    for (int w = 0; w < 4; ++w)
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if ((words[w] >> (8 * k)) & 0xffu) bits |= 1u << (4 * w + k);
+    const unsigned n = __popc(bits);
+    // block-wide exclusive prefix sum of n
+    unsigned incl = n;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane == 31) s_warp[warp] = incl;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      unsigned tot = 0;
+      for (int w = 0; w < kThreads / 32; ++w) {
+        const unsigned x = s_warp[w];
+        s_warp[w] = tot;
+        tot += x;
+      }
+      s_base = tot ? atomicAdd(a.count, tot) : 0u;
+    }
+    __syncthreads();
+    unsigned pos = s_base + s_warp[warp] + incl - n;
+    while (bits) {
+      const int k = __ffs(bits) - 1;
+      bits &= bits - 1;
+      a.list[pos++] = static_cast<unsigned>(c * 16 + k);
+    }
+    if (n) flags16[c] = make_uint4(0u, 0u, 0u, 0u);
+    __syncthreads();  // s_warp / s_base are rewritten by the next iteration
+  }
+}
+
+// Row of table t for a row-space index: binary search over the table row bases
+// (staged in shared memory when they fit).
+__device__ __forceinline__ int table_of(const long long* rb, int num_tables, long long rs) {
+  int lo = 0, hi = num_tables;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (rb[mid] <= rs) lo = mid; else hi = mid;
+  }
+  return lo;
+}
+
+// G lanes per row (G in {8, 16, 32}), NV float4 per lane: dim <= 4 * G * NV.
+template <int G, int NV, bool NORM>
+__global__ void __launch_bounds__(kThreads) adagrad_list_kernel(const AdagradArgs a, float* out_sq) {
+  extern __shared__ long long s_rb[];
+  const bool staged = a.num_tables <= 4096;
+  if (staged)
+    for (int i = threadIdx.x; i < a.num_tables; i += blockDim.x) s_rb[i] = __ldg(a.t_row_base + i);
+  __syncthreads();
+  const long long* rb = staged ? s_rb : a.t_row_base;
+  const float clip = (!NORM && a.clip_scale != nullptr) ? *a.clip_scale : 1.f;
+  const float gscale = a.grad_scale * clip;
+  const unsigned n = *a.count;
+  const int sub = threadIdx.x % G;
+  constexpr int RPW = 32 / G;  // rows per warp per iteration
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x / 32);
+  float sq_total = 0.f;
+  // Warp-uniform trip count: every lane reaches the group shuffles.
+  for (long long i0 = ((static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5) * RPW; i0 < n;
+       i0 += warps * RPW) {
+    const long long i = i0 + (threadIdx.x & 31) / G;
+    const bool valid = i < n;
+    long long rs = 0, base = 0;
+    int dim = 0;
+    if (valid) {
+      rs = a.list[i];
+      const int t = table_of(rb, a.num_tables, rs);
+      dim = __ldg(a.t_dim + t);
+      base = __ldg(a.t_base + t) + (rs - rb[t]) * dim;
+    }
+    float4 g[NV];
+    float sq = 0.f;
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const int col = (sub + v * G) * 4;
+      g[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (col < dim) {
+        const float4 x = *reinterpret_cast<const float4*>(a.grad_slab + base + col);
+        g[v] = make_float4(x.x * gscale, x.y * gscale, x.z * gscale, x.w * gscale);
+        sq += g[v].x * g[v].x + g[v].y * g[v].y + g[v].z * g[v].z + g[v].w * g[v].w;
+      }
+    }
+#pragma unroll
+    for (int o = G / 2; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o, G);
+    if (!valid) continue;
+    if (NORM) {
+      if (sub == 0) sq_total += sq;
+      continue;
+    }
+    const float acc = a.acc[rs] + sq / static_cast<float>(dim);
+    const float step = a.lr / (sqrtf(acc) + a.eps);
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const int col = (sub + v * G) * 4;
+      if (col < dim) {
+        float4* w = reinterpret_cast<float4*>(a.slab + base + col);
+        float4 x = *w;
+        x.x -= step * g[v].x; x.y -= step * g[v].y; x.z -= step * g[v].z; x.w -= step * g[v].w;
+        *w = x;
+        *reinterpret_cast<float4*>(a.grad_slab + base + col) = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    if (sub == 0) a.acc[rs] = acc;
+  }
+  if (NORM) {
+    sq_total = warp_sum(sq_total);
+    if ((threadIdx.x & 31) == 0 && sq_total != 0.f) atomicAdd(out_sq, sq_total);
+  }
+}
+
+template <bool NORM>
+cudaError_t launch_list(const AdagradArgs& a, float* out_sq, cudaStream_t stream) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int grid = sms * 8;
+  const size_t smem = a.num_tables <= 4096 ? static_cast<size_t>(a.num_tables) * sizeof(long long) : 0;
+  if (a.max_dim <= 32) adagrad_list_kernel<8, 1, NORM><<<grid, kThreads, smem, stream>>>(a, out_sq);
+  else if (a.max_dim <= 64) adagrad_list_kernel<16, 1, NORM><<<grid, kThreads, smem, stream>>>(a, out_sq);
+  else if (a.max_dim <= 128) adagrad_list_kernel<32, 1, NORM><<<grid, kThreads, smem, stream>>>(a, out_sq);
+  else if (a.max_dim <= 256) adagrad_list_kernel<32, 2, NORM><<<grid, kThreads, smem, stream>>>(a, out_sq);
+  else if (a.max_dim <= 512) adagrad_list_kernel<32, 4, NORM><<<grid, kThreads, smem, stream>>>(a, out_sq);
+  else if (a.max_dim <= 1024) adagrad_list_kernel<32, 8, NORM><<<grid, kThreads, smem, stream>>>(a, out_sq);
+  else return cudaErrorInvalidValue;
+  return cudaGetLastError();
+}
+
 __global__ void __launch_bounds__(kThreads) touched_sqnorm_kernel(const AdagradArgs a, float* out_sq) {
   const int lane = threadIdx.x & 31;
   float sq = 0.f;
@@ -456,8 +604,24 @@ cudaError_t emb_pool_backward(const EmbPlan& plan, const void* grad_out, long lo
   return cudaGetLastError();
 }
 
+cudaError_t compact_touched(const AdagradArgs& a, cudaStream_t stream) {
+  if (a.list == nullptr || a.count == nullptr) return cudaErrorInvalidValue;
+  if (a.total_rows >= (1LL << 32)) return cudaErrorInvalidValue;  // list entries are 32-bit
+  cudaError_t e = cudaMemsetAsync(a.count, 0, sizeof(unsigned), stream);
+  if (e != cudaSuccess) return e;
+  if (a.total_rows <= 0) return cudaSuccess;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long want = ((a.total_rows + 15) / 16 + kThreads - 1) / kThreads;
+  const int grid = static_cast<int>(want < sms * 8 ? (want > 0 ? want : 1) : sms * 8);
+  compact_touched_kernel<<<grid, kThreads, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
 cudaError_t rowwise_adagrad_apply(const AdagradArgs& a, cudaStream_t stream) {
   if (a.total_rows <= 0) return cudaSuccess;
+  if (a.list != nullptr) return launch_list<false>(a, nullptr, stream);
   const int grid = scan_grid(a.total_rows);
   if (a.max_dim <= 128) {
     int dev = 0, sms = 148;
@@ -478,6 +642,7 @@ cudaError_t rowwise_adagrad_apply(const AdagradArgs& a, cudaStream_t stream) {
 
 cudaError_t touched_grad_sqnorm(const AdagradArgs& a, float* out_sq, cudaStream_t stream) {
   if (a.total_rows <= 0) return cudaSuccess;
+  if (a.list != nullptr) return launch_list<true>(a, out_sq, stream);
   touched_sqnorm_kernel<<<scan_grid(a.total_rows), kThreads, 0, stream>>>(a, out_sq);
   return cudaGetLastError();
 }

@@ -89,8 +89,18 @@ struct AdagradArgs {
   const float* clip_scale = nullptr;  // optional device scalar (nullptr = 1)
   int max_dim = 1024;                 // widest table (selects the kernel variant)
   int* err = nullptr;
+  // Touched-row list (row-space indices, capacity total_rows) written by
+  // compact_touched. When set, the update and the norm walk the list instead of
+  // scanning the flags.
+  unsigned* list = nullptr;
+  unsigned* count = nullptr;
 };
 cudaError_t rowwise_adagrad_apply(const AdagradArgs& a, cudaStream_t stream);
+
+// Collect the touched rows into a.list / a.count (any order) and clear their
+// flags. One 16-byte flag load per thread, a block-wide prefix sum and one
+// atomic per block.
+cudaError_t compact_touched(const AdagradArgs& a, cudaStream_t stream);
 
 // Sum of squared (scaled) gradients over the touched rows (for global sparse clipping).
 cudaError_t touched_grad_sqnorm(const AdagradArgs& a, float* out_sq, cudaStream_t stream);

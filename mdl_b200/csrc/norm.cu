@@ -33,6 +33,19 @@ __device__ __forceinline__ void store8(__nv_bfloat16* p, const float* v) {
   *reinterpret_cast<uint4*>(p) = u;
 }
 
+// 8 consecutive fp32 values (32-byte aligned), or `fill` when p is null.
+__device__ __forceinline__ void load_f8(const float* p, int c, float* v, float fill) {
+  if (p == nullptr) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = fill;
+    return;
+  }
+  const float4 x = __ldg(reinterpret_cast<const float4*>(p + c));
+  const float4 y = __ldg(reinterpret_cast<const float4*>(p + c + 4));
+  v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+  v[4] = y.x; v[5] = y.y; v[6] = y.z; v[7] = y.w;
+}
+
 // Pre-norm value of row (b, i): mix(a)+a or a+b, 8 elements at column c.
 template <bool MIX>
 __device__ __forceinline__ void load_v(const __nv_bfloat16* a, const __nv_bfloat16* bsrc, long long b, int i,
@@ -94,13 +107,11 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const LNFwdArgs p) {
   for (int k = 0; k < NCH; ++k) {
     const int c = (lane + 32 * k) * 8;
     if (c < p.D) {
-      float o[8];
+      float o[8], g[8], bt[8];
+      load_f8(p.gamma, c, g, 1.f);
+      load_f8(p.beta, c, bt, 0.f);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float g = p.gamma ? __ldg(p.gamma + c + e) : 1.f;
-        const float bt = p.beta ? __ldg(p.beta + c + e) : 0.f;
-        o[e] = (v[k][e] - mean) * rstd * g + bt;
-      }
+      for (int e = 0; e < 8; ++e) o[e] = (v[k][e] - mean) * rstd * g[e] + bt[e];
       store8(out + c, o);
     }
   }
@@ -152,11 +163,12 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const LNBwdArgs p) {
 #pragma unroll
           for (int e = 0; e < 8; ++e) g[k][e] *= p.bcast_scale;
         }
+        float gm[8];
+        load_f8(p.gamma, c, gm, 1.f);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           xh[k][e] = (xh[k][e] - mean) * rstd;
-          const float gm = p.gamma ? __ldg(p.gamma + c + e) : 1.f;
-          gy[k][e] = g[k][e] * gm;
+          gy[k][e] = g[k][e] * gm[e];
           s1 += gy[k][e];
           s2 += gy[k][e] * xh[k][e];
         }
@@ -187,9 +199,11 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const LNBwdArgs p) {
 #pragma unroll
         for (int k = 0; k < NCH; ++k) {
           const int c = (lane + 32 * k) * 8;
-          if (c < D)
-#pragma unroll
-            for (int e = 0; e < 8; ++e) sm[i * D + c + e] = dv[k][e];
+          if (c < D) {
+            float4* d = reinterpret_cast<float4*>(sm + i * D + c);
+            d[0] = make_float4(dv[k][0], dv[k][1], dv[k][2], dv[k][3]);
+            d[1] = make_float4(dv[k][4], dv[k][5], dv[k][6], dv[k][7]);
+          }
         }
       }
       __syncthreads();
@@ -201,9 +215,11 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const LNBwdArgs p) {
           if (c < D) {
             const int j = c / dh;
             const int w = c - j * dh;
-            float o[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) o[e] = sm[i * D + c + e] + sm[j * D + i * dh + w + e];
+            const float4* d0 = reinterpret_cast<const float4*>(sm + i * D + c);
+            const float4* d1 = reinterpret_cast<const float4*>(sm + j * D + i * dh + w);
+            const float4 x0 = d0[0], x1 = d0[1], y0 = d1[0], y1 = d1[1];
+            const float o[8] = {x0.x + y0.x, x0.y + y0.y, x0.z + y0.z, x0.w + y0.w,
+                                x1.x + y1.x, x1.y + y1.y, x1.z + y1.z, x1.w + y1.w};
             store8(dx + r * D + c, o);
             if (dx2 != nullptr) store8(dx2 + r * D + c, o);
           }
@@ -248,15 +264,37 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const LNBwdArgs p) {
   }
 }
 
-__global__ void ln_partials_reduce_kernel(const float* partials, int grid, int D, float* dgamma, float* dbeta) {
-  const int col = blockIdx.x * blockDim.x + threadIdx.x;
-  if (col >= 2 * D) return;
+// Column sums of `partials` [grid, 2D] into dgamma (first D) / dbeta (last D).
+// Block = 32 columns x 8 warps; warp w sums rows w, w+8, ... (coalesced 128-byte
+// rows), then the 8 warp sums are added in a fixed order (deterministic).
+__global__ void __launch_bounds__(256) ln_partials_reduce_kernel(const float* partials, int grid, int D,
+                                                                 float* dgamma, float* dbeta) {
+  __shared__ float red[8][33];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int col = blockIdx.x * 32 + lane;
   float s = 0.f;
-  for (int g = 0; g < grid; ++g) s += partials[static_cast<long long>(g) * 2 * D + col];
-  if (col < D) {
-    if (dgamma) dgamma[col] += s;
-  } else if (dbeta) {
-    dbeta[col - D] += s;
+  if (col < 2 * D) {
+    int g = warp;
+    for (; g + 24 < grid; g += 32) {
+      const float a0 = partials[static_cast<long long>(g) * 2 * D + col];
+      const float a1 = partials[static_cast<long long>(g + 8) * 2 * D + col];
+      const float a2 = partials[static_cast<long long>(g + 16) * 2 * D + col];
+      const float a3 = partials[static_cast<long long>(g + 24) * 2 * D + col];
+      s += (a0 + a1) + (a2 + a3);
+    }
+    for (; g < grid; g += 8) s += partials[static_cast<long long>(g) * 2 * D + col];
+  }
+  red[warp][lane] = s;
+  __syncthreads();
+  if (warp == 0 && col < 2 * D) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += red[w][lane];
+    if (col < D) {
+      if (dgamma) dgamma[col] += t;
+    } else if (dbeta) {
+      dbeta[col - D] += t;
+    }
   }
 }
 
@@ -284,9 +322,10 @@ __global__ void __launch_bounds__(256) rms_fwd_kernel(const RMSArgs p) {
   for (int k = 0; k < NCH; ++k) {
     const int c = (lane + 32 * k) * 8;
     if (c < p.D) {
-      float o[8];
+      float o[8], w[8];
+      load_f8(p.weight, c, w, 1.f);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] = v[k][e] * rstd * (p.weight ? __ldg(p.weight + c + e) : 1.f);
+      for (int e = 0; e < 8; ++e) o[e] = v[k][e] * rstd * w[e];
       store8(out + c, o);
     }
   }
@@ -314,10 +353,11 @@ __global__ void __launch_bounds__(256) rms_bwd_kernel(const RMSArgs p) {
       if (c < p.D) {
         load8(x + c, xv[k]);
         load8(dy + c, gv[k]);
+        float w[8];
+        load_f8(p.weight, c, w, 1.f);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const float w = p.weight ? __ldg(p.weight + c + e) : 1.f;
-          s += gv[k][e] * w * xv[k][e];
+          s += gv[k][e] * w[e] * xv[k][e];
           dw[k][e] += gv[k][e] * xv[k][e] * rstd;
         }
       }
@@ -328,12 +368,10 @@ __global__ void __launch_bounds__(256) rms_bwd_kernel(const RMSArgs p) {
     for (int k = 0; k < NCH; ++k) {
       const int c = (lane + 32 * k) * 8;
       if (c < p.D) {
-        float o[8];
+        float o[8], w[8];
+        load_f8(p.weight, c, w, 1.f);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float w = p.weight ? __ldg(p.weight + c + e) : 1.f;
-          o[e] = rstd * (gv[k][e] * w - xv[k][e] * rstd * rstd * s);
-        }
+        for (int e = 0; e < 8; ++e) o[e] = rstd * (gv[k][e] * w[e] - xv[k][e] * rstd * rstd * s);
         store8(dx + c, o);
       }
     }
@@ -381,7 +419,7 @@ cudaError_t layernorm_fwd(const LNFwdArgs& a, cudaStream_t stream) {
 }
 
 int layernorm_bwd_grid(int B) {
-  const int cap = sm_count() * 2;
+  const int cap = sm_count() * 4;  // 4 resident CTAs per SM (48 KB of staging each at D=768, T=16)
   return B < cap ? (B > 0 ? B : 1) : cap;
 }
 
@@ -405,7 +443,7 @@ cudaError_t layernorm_bwd(const LNBwdArgs& a, cudaStream_t stream) {
 #undef LNB
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  ln_partials_reduce_kernel<<<(2 * a.D + 255) / 256, 256, 0, stream>>>(a.partials, grid, a.D, a.dgamma, a.dbeta);
+  ln_partials_reduce_kernel<<<(2 * a.D + 31) / 32, 256, 0, stream>>>(a.partials, grid, a.D, a.dgamma, a.dbeta);
   return cudaGetLastError();
 }
 

@@ -143,6 +143,11 @@ class EmbeddingStore:
             self.grad = torch.zeros(self.total_elems, dtype=torch.float32, device=dev)
             self.flags = torch.zeros(flag_len, dtype=torch.uint8, device=dev)
         self.acc = torch.empty(self.total_rows, dtype=torch.float32, device=dev)
+        # touched-row list rebuilt every step from the flags (CUDA): the update then walks
+        # only those rows, each with coalesced 16-byte lanes
+        self.touched_list = (torch.empty(max(self.total_rows, 1), dtype=torch.int32, device=dev)
+                             if dev.type == "cuda" else None)
+        self.touched_count = torch.zeros(1, dtype=torch.int32, device=dev) if dev.type == "cuda" else None
         # CPU path: dense gradient accumulation per table (sparse rows tracked by a mask)
         self._cpu_touched = torch.zeros(self.total_rows, dtype=torch.bool) if dev.type != "cuda" else None
 
@@ -223,10 +228,13 @@ class EmbeddingStore:
             self._symm.barrier()  # every rank finished pushing gradients
         clip = None
         norm = None
+        max_dim = max((t.dim for t in self.layouts), default=4)
+        C = ext()
+        C.compact_touched(self.flags, self.total_rows, self.touched_list, self.touched_count)
         if clip_norm is not None:
             sq = torch.zeros(1, dtype=torch.float32, device=self.device)
-            ext().touched_sqnorm(self.grad, self.flags, self.total_rows, m["t_base"], m["t_row_base"], m["t_dim"],
-                                 grad_scale, sq)
+            C.touched_sqnorm(self.grad, self.flags, self.total_rows, m["t_base"], m["t_row_base"], m["t_dim"],
+                             grad_scale, sq, self.touched_list, self.touched_count, max_dim)
             if self._symm is not None:
                 self._symm.allreduce_small(sq)
             elif self.world > 1:
@@ -234,9 +242,9 @@ class EmbeddingStore:
             clip = torch.empty(1, dtype=torch.float32, device=self.device)
             ext().clip_factor(sq, float(clip_norm), clip)
             norm = sq.sqrt()
-        ext().adagrad_apply(self.slab, self.grad, self.acc, self.flags, self.total_rows, m["t_base"],
-                            m["t_row_base"], m["t_dim"], float(lr), float(self.eps), grad_scale, clip,
-                            error_word(self.device), max((t.dim for t in self.layouts), default=4))
+        C.adagrad_apply(self.slab, self.grad, self.acc, self.flags, self.total_rows, m["t_base"], m["t_row_base"],
+                        m["t_dim"], float(lr), float(self.eps), grad_scale, clip, error_word(self.device), max_dim,
+                        self.touched_list, self.touched_count)
         if self._symm is not None:
             self._symm.barrier()  # updated rows visible before any peer reads them
         return norm

@@ -237,3 +237,21 @@ def test_rankmixer_cuda_step_matches_cpu_reference():
     ref = cpu_model.store.grad
     got = gpu_model.store.grad.cpu()
     assert ((ref - got).abs().max() / (ref.abs().max() + 1e-9)) < 0.08
+
+
+@pytest.mark.parametrize("rows,frac", [(1000, 0.3), (100003, 0.01), (5_000_017, 0.001)])
+def test_compact_touched_lists_every_flagged_row(rows, frac):
+    flags = torch.zeros((rows + 511) // 512 * 512, dtype=torch.uint8, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(0)
+    hit = torch.rand(rows, device="cuda", generator=g) < frac
+    flags[:rows][hit] = 1
+    lst = torch.empty(rows, dtype=torch.int32, device="cuda")
+    cnt = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ext().compact_touched(flags, rows, lst, cnt)
+    torch.cuda.synchronize()
+    n = int(cnt.item())
+    assert n == int(hit.sum().item())
+    got = torch.sort(lst[:n].long()).values
+    want = hit.nonzero().flatten()
+    assert torch.equal(got, want)
+    assert int(flags.sum().item()) == 0
