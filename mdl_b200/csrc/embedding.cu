@@ -50,36 +50,6 @@ __device__ __forceinline__ long long phys_col(int c, int slice, int stride) {
   return slice > 0 ? static_cast<long long>(c / slice) * stride + (c % slice) : c;
 }
 
-__device__ __forceinline__ void store4_bf16(__nv_bfloat16* out, long long row_off, int c, int slice, int stride,
-                                            int valid, const float* v) {
-  const long long p0 = phys_col(c, slice, stride);
-  const bool contiguous = slice <= 0 || (c / slice) == ((c + 3) / slice);
-  if (valid == 4 && contiguous && ((row_off + p0) & 3) == 0) {
-    __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]);
-    __nv_bfloat162 b = __floats2bfloat162_rn(v[2], v[3]);
-    uint2 u;
-    u.x = *reinterpret_cast<uint32_t*>(&a);
-    u.y = *reinterpret_cast<uint32_t*>(&b);
-    *reinterpret_cast<uint2*>(out + row_off + p0) = u;
-  } else {
-    for (int j = 0; j < valid; ++j) out[row_off + phys_col(c + j, slice, stride)] = __float2bfloat16_rn(v[j]);
-  }
-}
-
-__device__ __forceinline__ void load4_bf16(const __nv_bfloat16* g, long long row_off, int c, int slice, int stride,
-                                           int valid, float* v) {
-  const long long p0 = phys_col(c, slice, stride);
-  const bool contiguous = slice <= 0 || (c / slice) == ((c + 3) / slice);
-  if (valid == 4 && contiguous && ((row_off + p0) & 3) == 0) {
-    const uint2 u = *reinterpret_cast<const uint2*>(g + row_off + p0);
-    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
-    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
-    v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
-  } else {
-    for (int j = 0; j < 4; ++j) v[j] = j < valid ? __bfloat162float(g[row_off + phys_col(c + j, slice, stride)]) : 0.f;
-  }
-}
-
 template <bool SYS>
 __device__ __forceinline__ void red_add4(float* dst, const float* v) {
   if (SYS) {
@@ -93,173 +63,353 @@ __device__ __forceinline__ void red_add4(float* dst, const float* v) {
   }
 }
 
-struct BagCtx {
-  int f, lanes, sl;
-  long long bag_local, gbag;
-  bool active;
+constexpr int kChunkBags = 32;  // bags per warp work item (all 32 lanes hold one bag's offsets)
+
+// Everything a warp needs about its work item, loaded once per warp.
+struct Chunk {
+  int f = 0, t = -1, pool = 0, hmode = 0, width = 0, dim = 0, lanes = 1, lg = 0;
+  long long buckets = 1, rows = 0;
+  long long first = 0;  // first bag (sample row) of the chunk within the feature
+  int nb = 0;           // bags in the chunk (<= 32)
+  long long g0 = 0;     // CSR index of the chunk's first bag
+  // output columns: logical c0 + col -> physical p0 + col (+ delta past `split`)
+  long long out_base = 0, out_ld = 0;
+  int p0 = 0, split = 1 << 30, delta = 0;
+  bool general = false;  // more than one slice boundary inside the feature: per-column mapping
+  int c0 = 0, slice = 0, sstride = 0;
+  const float* tbl = nullptr;  // this rank's shard of the table (single-rank fast path)
+  float* gtbl = nullptr;       // ... and of its gradient
+  unsigned char* ftbl = nullptr;  // ... and of its touched flags
 };
 
-__device__ __forceinline__ BagCtx bag_of_lane(const EmbPlan& p) {
-  BagCtx b;
-  const long long warp = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  b.f = static_cast<int>(find_feature(p.f_chunk_prefix, p.num_features, warp));
-  b.lanes = __ldg(p.f_lanes + b.f);
-  const int bags_per_warp = 32 / b.lanes;
-  const long long chunk = warp - __ldg(p.f_chunk_prefix + b.f);
-  const int sub = lane / b.lanes;
-  b.sl = lane % b.lanes;
-  b.bag_local = chunk * bags_per_warp + sub;
-  const long long n_bags = __ldg(p.f_bag_prefix + b.f + 1) - __ldg(p.f_bag_prefix + b.f);
-  b.active = b.bag_local < n_bags;
-  b.gbag = __ldg(p.f_src_bag + b.f) + b.bag_local;
-  return b;
+__device__ __forceinline__ Chunk load_chunk(const EmbPlan& p, long long warp) {
+  Chunk c;
+  c.f = static_cast<int>(find_feature(p.f_chunk_prefix, p.num_features, warp));
+  const int f = c.f;
+  c.t = __ldg(p.f_table + f);
+  c.pool = __ldg(p.f_pool + f);
+  c.hmode = __ldg(p.f_hash + f);
+  c.buckets = __ldg(p.f_buckets + f);
+  c.width = __ldg(p.f_width + f);
+  c.lanes = __ldg(p.f_lanes + f);
+  c.lg = __ffs(c.lanes) - 1;
+  if (c.t >= 0) {
+    c.rows = __ldg(p.t_rows + c.t);
+    c.dim = __ldg(p.t_dim + c.t);
+    const long long tb = __ldg(p.t_base_all + p.rank * p.num_tables + c.t);
+    c.tbl = p.slabs[p.rank] + tb;
+    if (p.grad_slabs[p.rank] != nullptr) c.gtbl = p.grad_slabs[p.rank] + tb;
+    if (p.flags[p.rank] != nullptr) c.ftbl = p.flags[p.rank] + __ldg(p.t_row_base_all + p.rank * p.num_tables + c.t);
+  }
+  c.first = (warp - __ldg(p.f_chunk_prefix + f)) * kChunkBags;
+  const long long n_bags = __ldg(p.f_bag_prefix + f + 1) - __ldg(p.f_bag_prefix + f);
+  const long long left = n_bags - c.first;
+  c.nb = static_cast<int>(left < kChunkBags ? (left > 0 ? left : 0) : kChunkBags);
+  c.g0 = __ldg(p.f_src_bag + f) + c.first;
+  c.out_base = __ldg(p.f_out_base + f);
+  c.out_ld = __ldg(p.f_out_ld + f);
+  c.c0 = __ldg(p.f_out_col + f);
+  c.slice = __ldg(p.f_slice + f);
+  c.sstride = __ldg(p.f_slice_stride + f);
+  if (c.slice > 0) {
+    const int r = c.c0 % c.slice;
+    c.p0 = (c.c0 / c.slice) * c.sstride + r;
+    c.split = c.slice - r;
+    c.delta = c.sstride - c.slice;
+    c.general = c.width > c.split + c.slice;
+  } else {
+    c.p0 = c.c0;
+  }
+  return c;
 }
 
-__device__ __forceinline__ void route(const EmbPlan& p, int t, long long id, int& owner, long long& row) {
-  if (__ldg(p.t_mode + t) == 0) {
-    if (p.world == 1) {
-      owner = 0;
-      row = id;
-    } else {
-      owner = static_cast<int>((id + __ldg(p.t_cyc + t)) % p.world);
-      row = id / p.world;
-    }
+// Physical output column of feature column `col`.
+__device__ __forceinline__ long long out_col(const Chunk& c, int col) {
+  if (c.general) return phys_col(c.c0 + col, c.slice, c.sstride);
+  return c.p0 + col + (col >= c.split ? c.delta : 0);
+}
+
+__device__ __forceinline__ void store4(const Chunk& c, __nv_bfloat16* out, long long row_off, int col, int valid,
+                                       const float* v) {
+  const long long p0 = out_col(c, col);
+  const bool contiguous = !c.general && ((col < c.split) == (col + 3 < c.split));
+  if (valid == 4 && contiguous && ((row_off + p0) & 3) == 0) {
+    const __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]);
+    const __nv_bfloat162 b = __floats2bfloat162_rn(v[2], v[3]);
+    uint2 u;
+    u.x = *reinterpret_cast<const uint32_t*>(&a);
+    u.y = *reinterpret_cast<const uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(out + row_off + p0) = u;
   } else {
-    owner = __ldg(p.t_owner + t);
-    row = id;
+    for (int j = 0; j < valid; ++j) out[row_off + out_col(c, col + j)] = __float2bfloat16_rn(v[j]);
   }
 }
 
-template <int NV>  // float4 vectors per lane: width <= 4 * lanes * NV
-__global__ void __launch_bounds__(kThreads) emb_pool_fwd_kernel(const EmbPlan p, long long total_chunks) {
+__device__ __forceinline__ void load4(const Chunk& c, const __nv_bfloat16* g, long long row_off, int col, int valid,
+                                      float* v) {
+  const long long p0 = out_col(c, col);
+  const bool contiguous = !c.general && ((col < c.split) == (col + 3 < c.split));
+  if (valid == 4 && contiguous && ((row_off + p0) & 3) == 0) {
+    const uint2 u = *reinterpret_cast<const uint2*>(g + row_off + p0);
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+    v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+  } else {
+    for (int j = 0; j < 4; ++j) v[j] = j < valid ? __bfloat162float(g[row_off + out_col(c, col + j)]) : 0.f;
+  }
+}
+
+__device__ __forceinline__ void route(const EmbPlan& p, int t, long long id, int& owner, long long& row) {
+  if (__ldg(p.t_mode + t) != 0) {
+    owner = __ldg(p.t_owner + t);
+    row = id;
+  } else if (p.world == 1) {
+    owner = 0;
+    row = id;
+  } else {
+    const long long cyc = __ldg(p.t_cyc + t);
+    if (id < (1LL << 31) && cyc < (1LL << 31)) {  // 32-bit division is several times cheaper
+      const unsigned w = static_cast<unsigned>(p.world);
+      owner = static_cast<int>((static_cast<unsigned>(id) + static_cast<unsigned>(cyc)) % w);
+      row = static_cast<long long>(static_cast<unsigned>(id) / w);
+    } else {
+      owner = static_cast<int>((id + cyc) % p.world);
+      row = id / p.world;
+    }
+  }
+}
+
+// CSR range [beg, end) of bag `lane` of the chunk (lanes >= nb get an empty range).
+__device__ __forceinline__ void bag_ranges(const EmbPlan& p, const Chunk& c, int lane, long long& beg,
+                                           long long& end) {
+  beg = lane < c.nb ? __ldg(p.id_offsets + c.g0 + lane) : 0;
+  end = __shfl_down_sync(0xffffffffu, beg, 1);
+  if (lane == c.nb - 1) end = __ldg(p.id_offsets + c.g0 + c.nb);
+  if (lane >= c.nb) end = beg;
+}
+
+// First valid id of the bag (single-valued features), 0 when none; records bad ids.
+__device__ __forceinline__ long long first_valid(const EmbPlan& p, const Chunk& c, long long beg, long long end) {
+  for (long long q = beg; q < end; ++q) {
+    const long long id = hash_id(__ldg(p.ids + q), c.hmode, c.buckets);
+    if (id <= 0) continue;  // null / padding
+    if (id >= c.rows) {
+      record_error(p.err, MDL_ERR_BAD_INDEX);
+      continue;
+    }
+    return id;
+  }
+  return 0;
+}
+
+// Source row of `id`: the local shard directly when this is the only rank
+// (64-bit IMAD on an unsigned id), else the owner's slab (peer memory).
+template <bool LOCAL>
+__device__ __forceinline__ const float* row_src(const EmbPlan& p, const Chunk& c, long long id) {
+  if (LOCAL) return c.tbl + static_cast<unsigned long long>(id) * static_cast<unsigned>(c.dim);
+  int owner;
+  long long row;
+  route(p, c.t, id, owner, row);
+  return p.slabs[owner] + __ldg(p.t_base_all + owner * p.num_tables + c.t) + row * c.dim;
+}
+
+template <int NV, bool LOCAL>  // float4 vectors per lane: width <= 4 * lanes * NV
+__global__ void __launch_bounds__(kThreads, NV <= 2 ? 4 : 2) emb_pool_fwd_kernel(const EmbPlan p, long long total_chunks) {
   const long long warp = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
   if (warp >= total_chunks) return;
-  const BagCtx b = bag_of_lane(p);
-  if (!b.active) return;
-  const int f = b.f;
-  const int width = __ldg(p.f_width + f);
-  const int t = __ldg(p.f_table + f);
-  const int pool = __ldg(p.f_pool + f);
-  float acc[NV][4];
-#pragma unroll
-  for (int i = 0; i < NV; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-  const int stride_cols = 4 * b.lanes;
-  int count = 0;
-  if (t < 0) {
-    const float* src = p.dense + b.bag_local * p.dense_ld + __ldg(p.f_dense_col + f);
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int col = b.sl * 4 + i * stride_cols;
-      if (col < width)
-        for (int j = 0; j < 4; ++j) acc[i][j] = (col + j < width) ? __ldg(src + col + j) : 0.f;
-    }
-    count = 1;
-  } else {
-    const int hmode = __ldg(p.f_hash + f);
-    const long long buckets = __ldg(p.f_buckets + f);
-    const long long rows = __ldg(p.t_rows + t);
-    // the element base of the table differs per rank: use the OWNER's layout (t_base_all[owner][t])
-    const int dim = __ldg(p.t_dim + t);
-    const long long beg = __ldg(p.id_offsets + b.gbag);
-    const long long end = __ldg(p.id_offsets + b.gbag + 1);
-    for (long long q = beg; q < end; ++q) {
-      const long long id = hash_id(__ldg(p.ids + q), hmode, buckets);
-      if (id <= 0) continue;  // padding id 0 contributes nothing (null policy "exclude")
-      if (id >= rows) {
-        record_error(p.err, MDL_ERR_BAD_INDEX);
-        continue;
-      }
-      int owner;
-      long long row;
-      route(p, t, id, owner, row);
-      const float* src = p.slabs[owner] + __ldg(p.t_base_all + owner * p.num_tables + t) + row * dim;
+  const int lane = threadIdx.x & 31;
+  const Chunk c = load_chunk(p, warp);
+  if (c.nb <= 0) return;
+  const int sub = lane >> c.lg, sl = lane & (c.lanes - 1);
+  const int bps = 32 >> c.lg;  // bags per step
+  const int stride_cols = 4 * c.lanes;
+  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out) + c.out_base;
+  if (c.t < 0) {  // dense input columns
+    const int dcol = __ldg(p.f_dense_col + c.f);
+    for (int s = 0; s * bps < c.nb; ++s) {
+      const int bag = s * bps + sub;
+      if (bag >= c.nb) continue;
+      const long long brow = c.first + bag;
+      const float* src = p.dense + brow * p.dense_ld + dcol;
 #pragma unroll
       for (int i = 0; i < NV; ++i) {
-        const int col = b.sl * 4 + i * stride_cols;
-        if (col < dim) {
-          const float4 v = *reinterpret_cast<const float4*>(src + col);
-          acc[i][0] += v.x; acc[i][1] += v.y; acc[i][2] += v.z; acc[i][3] += v.w;
+        const int col = sl * 4 + i * stride_cols;
+        if (col < c.width) {
+          float v[4];
+          for (int j = 0; j < 4; ++j) v[j] = (col + j < c.width) ? __ldg(src + col + j) : 0.f;
+          store4(c, out, brow * c.out_ld, col, min(4, c.width - col), v);
         }
       }
-      ++count;
-      if (pool == 0) break;  // single-valued feature: first non-null id only
     }
-    if (pool == 1 && count > 0) {
+    return;
+  }
+  long long beg, end;
+  bag_ranges(p, c, lane, beg, end);
+  if (c.pool == 0) {
+    // one id per bag, found by the bag's own lane; lane groups then fetch the rows
+    const long long my_id = first_valid(p, c, beg, end);
+    for (int s0 = 0; s0 * bps < c.nb; s0 += 2) {
+      float v[2][NV][4];
+      long long brow[2];
+      bool ok[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int bag = (s0 + u) * bps + sub;
+        const long long id = __shfl_sync(0xffffffffu, my_id, bag & 31);
+        ok[u] = bag < c.nb;
+        brow[u] = c.first + bag;
+        const float* src = (ok[u] && id > 0) ? row_src<LOCAL>(p, c, id) : nullptr;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          const int col = sl * 4 + i * stride_cols;
+          float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (src != nullptr && col < c.dim) x = *reinterpret_cast<const float4*>(src + col);
+          v[u][i][0] = x.x; v[u][i][1] = x.y; v[u][i][2] = x.z; v[u][i][3] = x.w;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        if (!ok[u]) continue;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          const int col = sl * 4 + i * stride_cols;
+          if (col < c.width) store4(c, out, brow[u] * c.out_ld, col, min(4, c.width - col), v[u][i]);
+        }
+      }
+    }
+    return;
+  }
+  // bags (sum / mean): each lane group walks its bag four ids at a time
+  for (int s = 0; s * bps < c.nb; ++s) {
+    const int bag = s * bps + sub;
+    const long long qb = __shfl_sync(0xffffffffu, beg, bag & 31);
+    const long long qe = __shfl_sync(0xffffffffu, end, bag & 31);
+    if (bag >= c.nb) continue;
+    float acc[NV][4];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+    int count = 0;
+    for (long long q = qb; q < qe; q += 4) {
+      long long id[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) id[u] = q + u < qe ? hash_id(__ldg(p.ids + q + u), c.hmode, c.buckets) : 0;
+      float4 x[4][NV];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const bool bad = id[u] >= c.rows;
+        if (bad) record_error(p.err, MDL_ERR_BAD_INDEX);
+        const float* src = nullptr;
+        if (id[u] > 0 && !bad) {
+          src = row_src<LOCAL>(p, c, id[u]);
+          ++count;
+        }
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          const int col = sl * 4 + i * stride_cols;
+          x[u][i] = (src != nullptr && col < c.dim) ? *reinterpret_cast<const float4*>(src + col)
+                                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          acc[i][0] += x[u][i].x; acc[i][1] += x[u][i].y; acc[i][2] += x[u][i].z; acc[i][3] += x[u][i].w;
+        }
+    }
+    if (c.pool == 1 && count > 0) {
       const float inv = 1.f / static_cast<float>(count);
 #pragma unroll
       for (int i = 0; i < NV; ++i)
         for (int j = 0; j < 4; ++j) acc[i][j] *= inv;
     }
-  }
-  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out) + __ldg(p.f_out_base + f);
-  const long long row_off = b.bag_local * __ldg(p.f_out_ld + f);
-  const int c0 = __ldg(p.f_out_col + f);
-  const int slice = __ldg(p.f_slice + f), sstride = __ldg(p.f_slice_stride + f);
+    const long long brow = c.first + bag;
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int col = b.sl * 4 + i * stride_cols;
-    if (col < width) store4_bf16(out, row_off, c0 + col, slice, sstride, min(4, width - col), acc[i]);
+    for (int i = 0; i < NV; ++i) {
+      const int col = sl * 4 + i * stride_cols;
+      if (col < c.width) store4(c, out, brow * c.out_ld, col, min(4, c.width - col), acc[i]);
+    }
   }
 }
 
-template <bool SYS, int NV>
-__global__ void __launch_bounds__(kThreads)
+template <bool SYS, int NV, bool LOCAL>
+__global__ void __launch_bounds__(kThreads, NV <= 2 ? 4 : 2)
     emb_pool_bwd_kernel(const EmbPlan p, const __nv_bfloat16* __restrict__ grad_out, long long total_chunks) {
   const long long warp = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
   if (warp >= total_chunks) return;
-  const BagCtx b = bag_of_lane(p);
-  if (!b.active) return;
-  const int f = b.f;
-  const int t = __ldg(p.f_table + f);
-  if (t < 0) return;  // dense inputs have no trainable table
-  const int pool = __ldg(p.f_pool + f);
-  const int hmode = __ldg(p.f_hash + f);
-  const long long buckets = __ldg(p.f_buckets + f);
-  const long long rows = __ldg(p.t_rows + t);
-  const int dim = __ldg(p.t_dim + t);
-  const long long beg = __ldg(p.id_offsets + b.gbag);
-  const long long end = __ldg(p.id_offsets + b.gbag + 1);
-  float scale = 1.f;
-  if (pool == 1) {
-    int count = 0;
+  const int lane = threadIdx.x & 31;
+  const Chunk c = load_chunk(p, warp);
+  if (c.nb <= 0 || c.t < 0) return;  // dense inputs have no trainable table
+  const int sub = lane >> c.lg, sl = lane & (c.lanes - 1);
+  const int bps = 32 >> c.lg;
+  const int stride_cols = 4 * c.lanes;
+  const __nv_bfloat16* gbase = grad_out + c.out_base;
+  long long beg, end;
+  bag_ranges(p, c, lane, beg, end);
+  // per bag (own lane): the single id (pool none) or the valid-id count (mean)
+  long long my_id = 0;
+  int my_count = 0;
+  if (c.pool == 0) {
+    my_id = first_valid(p, c, beg, end);
+  } else if (c.pool == 1) {
     for (long long q = beg; q < end; ++q) {
-      const long long id = hash_id(__ldg(p.ids + q), hmode, buckets);
-      if (id > 0 && id < rows) ++count;
-    }
-    if (count == 0) return;
-    scale = 1.f / static_cast<float>(count);
-  }
-  const int stride_cols = 4 * b.lanes;
-  float g[NV][4];
-  const long long row_off = b.bag_local * __ldg(p.f_out_ld + f);
-  const int c0 = __ldg(p.f_out_col + f);
-  const int slice = __ldg(p.f_slice + f), sstride = __ldg(p.f_slice_stride + f);
-  const __nv_bfloat16* gbase = grad_out + __ldg(p.f_out_base + f);
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int col = b.sl * 4 + i * stride_cols;
-    if (col < dim) {
-      load4_bf16(gbase, row_off, c0 + col, slice, sstride, min(4, dim - col), g[i]);
-      for (int j = 0; j < 4; ++j) g[i][j] *= scale;
+      const long long id = hash_id(__ldg(p.ids + q), c.hmode, c.buckets);
+      if (id > 0 && id < c.rows) ++my_count;
     }
   }
-  for (long long q = beg; q < end; ++q) {
-    const long long id = hash_id(__ldg(p.ids + q), hmode, buckets);
-    if (id <= 0 || id >= rows) continue;
-    int owner;
-    long long row;
-    route(p, t, id, owner, row);
-    float* dst = p.grad_slabs[owner] + __ldg(p.t_base_all + owner * p.num_tables + t) + row * dim;
+  for (int s = 0; s * bps < c.nb; ++s) {
+    const int bag = s * bps + sub;
+    const long long qb = __shfl_sync(0xffffffffu, beg, bag & 31);
+    const long long qe = __shfl_sync(0xffffffffu, end, bag & 31);
+    const long long one = __shfl_sync(0xffffffffu, my_id, bag & 31);
+    const int cnt = __shfl_sync(0xffffffffu, my_count, bag & 31);
+    if (bag >= c.nb) continue;
+    if (c.pool == 0 && one <= 0) continue;
+    if (c.pool == 1 && cnt == 0) continue;
+    const float scale = c.pool == 1 ? 1.f / static_cast<float>(cnt) : 1.f;
+    const long long brow = c.first + bag;
+    float g[NV][4];
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      const int col = b.sl * 4 + i * stride_cols;
-      if (col < dim) red_add4<SYS>(dst + col, g[i]);
+      const int col = sl * 4 + i * stride_cols;
+      if (col < c.dim) {
+        load4(c, gbase, brow * c.out_ld, col, min(4, c.dim - col), g[i]);
+        for (int j = 0; j < 4; ++j) g[i][j] *= scale;
+      }
     }
-    // Mark the row touched: an idempotent byte store (no atomic, no shared counter).
-    if (b.sl == 0)
-      *reinterpret_cast<volatile unsigned char*>(p.flags[owner] + __ldg(p.t_row_base_all + owner * p.num_tables + t) + row) = 1;
-    if (pool == 0) break;
+    auto push = [&](long long id) {
+      float* dst;
+      unsigned char* flag;
+      if (LOCAL) {
+        dst = c.gtbl + static_cast<unsigned long long>(id) * static_cast<unsigned>(c.dim);
+        flag = c.ftbl + id;
+      } else {
+        int owner;
+        long long row;
+        route(p, c.t, id, owner, row);
+        dst = p.grad_slabs[owner] + __ldg(p.t_base_all + owner * p.num_tables + c.t) + row * c.dim;
+        flag = p.flags[owner] + __ldg(p.t_row_base_all + owner * p.num_tables + c.t) + row;
+      }
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int col = sl * 4 + i * stride_cols;
+        if (col < c.dim) red_add4<SYS>(dst + col, g[i]);
+      }
+      // Mark the row touched: an idempotent byte store (no atomic, no shared counter).
+      if (sl == 0) *reinterpret_cast<volatile unsigned char*>(flag) = 1;
+    };
+    if (c.pool == 0) {
+      push(one);
+      continue;
+    }
+    for (long long q = qb; q < qe; q += 4) {
+      long long id[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) id[u] = q + u < qe ? hash_id(__ldg(p.ids + q + u), c.hmode, c.buckets) : 0;
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (id[u] > 0 && id[u] < c.rows) push(id[u]);
+    }
   }
 }
 
@@ -581,10 +731,13 @@ int scan_grid(long long total_rows) {
 cudaError_t emb_pool_forward(const EmbPlan& plan, long long total_chunks, cudaStream_t stream) {
   if (total_chunks <= 0) return cudaSuccess;
   const int grid = blocks_for(total_chunks);
-  if (plan.max_vec <= 1) emb_pool_fwd_kernel<1><<<grid, kThreads, 0, stream>>>(plan, total_chunks);
-  else if (plan.max_vec <= 2) emb_pool_fwd_kernel<2><<<grid, kThreads, 0, stream>>>(plan, total_chunks);
-  else if (plan.max_vec <= 4) emb_pool_fwd_kernel<4><<<grid, kThreads, 0, stream>>>(plan, total_chunks);
-  else emb_pool_fwd_kernel<8><<<grid, kThreads, 0, stream>>>(plan, total_chunks);
+  const bool local = plan.world == 1;
+#define MDL_FWD(NV)                                                                        \
+  if (local) emb_pool_fwd_kernel<NV, true><<<grid, kThreads, 0, stream>>>(plan, total_chunks); \
+  else emb_pool_fwd_kernel<NV, false><<<grid, kThreads, 0, stream>>>(plan, total_chunks);
+  if (plan.max_vec <= 1) { MDL_FWD(1) } else if (plan.max_vec <= 2) { MDL_FWD(2) }
+  else if (plan.max_vec <= 4) { MDL_FWD(4) } else { MDL_FWD(8) }
+#undef MDL_FWD
   return cudaGetLastError();
 }
 
@@ -593,12 +746,14 @@ cudaError_t emb_pool_backward(const EmbPlan& plan, const void* grad_out, long lo
   if (total_chunks <= 0) return cudaSuccess;
   const auto* g = reinterpret_cast<const __nv_bfloat16*>(grad_out);
   const int grid = blocks_for(total_chunks);
-#define MDL_BWD(SYS, NV) emb_pool_bwd_kernel<SYS, NV><<<grid, kThreads, 0, stream>>>(plan, g, total_chunks)
+#define MDL_BWD(SYS, NV, L) emb_pool_bwd_kernel<SYS, NV, L><<<grid, kThreads, 0, stream>>>(plan, g, total_chunks)
   const int nv = plan.max_vec <= 1 ? 1 : plan.max_vec <= 2 ? 2 : plan.max_vec <= 4 ? 4 : 8;
   if (plan.world > 1) {
-    if (nv == 1) MDL_BWD(true, 1); else if (nv == 2) MDL_BWD(true, 2); else if (nv == 4) MDL_BWD(true, 4); else MDL_BWD(true, 8);
+    if (nv == 1) MDL_BWD(true, 1, false); else if (nv == 2) MDL_BWD(true, 2, false);
+    else if (nv == 4) MDL_BWD(true, 4, false); else MDL_BWD(true, 8, false);
   } else {
-    if (nv == 1) MDL_BWD(false, 1); else if (nv == 2) MDL_BWD(false, 2); else if (nv == 4) MDL_BWD(false, 4); else MDL_BWD(false, 8);
+    if (nv == 1) MDL_BWD(false, 1, true); else if (nv == 2) MDL_BWD(false, 2, true);
+    else if (nv == 4) MDL_BWD(false, 4, true); else MDL_BWD(false, 8, true);
   }
 #undef MDL_BWD
   return cudaGetLastError();

@@ -364,8 +364,8 @@ class LookupPlan:
             if f.width > 4 * lanes * 8:
                 raise ValueError(f"feature {f.name}: width {f.width} exceeds the lookup kernel limit")
             lanes_list.append(lanes)
-            bags_per_warp = 32 // lanes
-            chunk_prefix.append(chunk_prefix[-1] + (rows + bags_per_warp - 1) // bags_per_warp)
+            # one warp per chunk of 32 bags of one feature (csrc/embedding.cu kChunkBags)
+            chunk_prefix.append(chunk_prefix[-1] + (rows + 31) // 32)
             bag_prefix.append(bag_prefix[-1] + rows)
         tm = store.table_meta()
         i32 = lambda xs: torch.tensor(xs, dtype=torch.int32, device=dev)
