@@ -173,6 +173,60 @@ void emb_backward(const std::vector<at::Tensor>& meta, const std::vector<int64_t
   g_launches += 1;
 }
 
+mdl::OwnerArgs owner_args(const std::vector<int64_t>& req_ids, const std::vector<int64_t>& req_offsets, int world) {
+  TORCH_CHECK(static_cast<int>(req_ids.size()) == world && static_cast<int>(req_offsets.size()) == world,
+              "one staged ids/offsets pointer per rank");
+  mdl::OwnerArgs o;
+  for (int r = 0; r < world; ++r) {
+    o.req_ids[r] = reinterpret_cast<const long long*>(req_ids[r]);
+    o.req_offsets[r] = reinterpret_cast<const long long*>(req_offsets[r]);
+  }
+  return o;
+}
+
+// Owner-push lookup: this rank gathers the rows it owns for every requester's bags
+// and adds the pooled partials into each requester's fp32 accumulator.
+void emb_owner_forward(const std::vector<at::Tensor>& meta, const std::vector<int64_t>& slabs, int64_t rank,
+                       const at::Tensor& ids, const at::Tensor& id_offsets, const std::vector<int64_t>& req_ids,
+                       const std::vector<int64_t>& req_offsets, const std::vector<int64_t>& req_acc,
+                       const std::optional<at::Tensor>& dense, int64_t dense_ld, int64_t total_chunks,
+                       const std::optional<at::Tensor>& err, int64_t max_vec) {
+  c10::cuda::CUDAGuard guard(ids.device());
+  mdl::EmbPlan p = make_plan(meta, slabs, {}, {}, rank, ids, id_offsets, std::nullopt, 0, err, max_vec);
+  mdl::OwnerArgs o = owner_args(req_ids, req_offsets, p.world);
+  TORCH_CHECK(static_cast<int>(req_acc.size()) == p.world, "one accumulator pointer per rank");
+  for (int r = 0; r < p.world; ++r) o.req_acc[r] = reinterpret_cast<float*>(req_acc[r]);
+  if (dense.has_value()) {
+    TORCH_CHECK(dense->scalar_type() == at::kFloat, "dense inputs must be fp32");
+    o.dense = dense->data_ptr<float>();
+    o.dense_ld = dense_ld;
+  }
+  check(mdl::emb_owner_forward(p, o, total_chunks, stream_of(ids)), "emb_owner_forward");
+  g_launches += 1;
+}
+
+void emb_owner_backward(const std::vector<at::Tensor>& meta, const std::vector<int64_t>& slabs,
+                        const std::vector<int64_t>& grad_slabs, const std::vector<int64_t>& flags, int64_t rank,
+                        const at::Tensor& ids, const at::Tensor& id_offsets, const std::vector<int64_t>& req_ids,
+                        const std::vector<int64_t>& req_offsets, const std::vector<int64_t>& req_grad,
+                        int64_t total_chunks, const std::optional<at::Tensor>& err, int64_t max_vec) {
+  c10::cuda::CUDAGuard guard(ids.device());
+  mdl::EmbPlan p = make_plan(meta, slabs, grad_slabs, flags, rank, ids, id_offsets, std::nullopt, 0, err, max_vec);
+  mdl::OwnerArgs o = owner_args(req_ids, req_offsets, p.world);
+  TORCH_CHECK(static_cast<int>(req_grad.size()) == p.world, "one staged gradient pointer per rank");
+  for (int r = 0; r < p.world; ++r) o.req_grad[r] = reinterpret_cast<const void*>(req_grad[r]);
+  check(mdl::emb_owner_backward(p, o, total_chunks, stream_of(ids)), "emb_owner_backward");
+  g_launches += 1;
+}
+
+void emb_acc_to_bf16(const at::Tensor& acc, const at::Tensor& out) {
+  c10::cuda::CUDAGuard guard(acc.device());
+  TORCH_CHECK(acc.scalar_type() == at::kFloat && out.scalar_type() == at::kBFloat16, "fp32 -> bf16");
+  TORCH_CHECK(acc.numel() >= out.numel() && out.is_contiguous(), "accumulator smaller than the output");
+  check(mdl::emb_acc_to_bf16(acc.data_ptr<float>(), out.data_ptr(), out.numel(), stream_of(out)), "emb_acc_to_bf16");
+  g_launches += 1;
+}
+
 mdl::AdagradArgs adagrad_args(const at::Tensor& slab, const at::Tensor& grad_slab, const at::Tensor& acc,
                               const at::Tensor& flags, int64_t total_rows, const at::Tensor& t_base,
                               const at::Tensor& t_row_base, const at::Tensor& t_dim, double lr, double eps,
@@ -605,6 +659,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
 
   m.def("emb_forward", &emb_forward);
   m.def("emb_backward", &emb_backward);
+  m.def("emb_owner_forward", &emb_owner_forward);
+  m.def("emb_owner_backward", &emb_owner_backward);
+  m.def("emb_acc_to_bf16", &emb_acc_to_bf16);
   m.def("adagrad_apply", &adagrad_apply);
   m.def("touched_sqnorm", &touched_sqnorm);
   m.def("compact_touched", &compact_touched);

@@ -180,18 +180,19 @@ __device__ __forceinline__ void route(const EmbPlan& p, int t, long long id, int
 }
 
 // CSR range [beg, end) of bag `lane` of the chunk (lanes >= nb get an empty range).
-__device__ __forceinline__ void bag_ranges(const EmbPlan& p, const Chunk& c, int lane, long long& beg,
+__device__ __forceinline__ void bag_ranges(const long long* offs, const Chunk& c, int lane, long long& beg,
                                            long long& end) {
-  beg = lane < c.nb ? __ldg(p.id_offsets + c.g0 + lane) : 0;
+  beg = lane < c.nb ? offs[c.g0 + lane] : 0;
   end = __shfl_down_sync(0xffffffffu, beg, 1);
-  if (lane == c.nb - 1) end = __ldg(p.id_offsets + c.g0 + c.nb);
+  if (lane == c.nb - 1) end = offs[c.g0 + c.nb];
   if (lane >= c.nb) end = beg;
 }
 
 // First valid id of the bag (single-valued features), 0 when none; records bad ids.
-__device__ __forceinline__ long long first_valid(const EmbPlan& p, const Chunk& c, long long beg, long long end) {
+__device__ __forceinline__ long long first_valid(const EmbPlan& p, const long long* ids, const Chunk& c,
+                                                 long long beg, long long end) {
   for (long long q = beg; q < end; ++q) {
-    const long long id = hash_id(__ldg(p.ids + q), c.hmode, c.buckets);
+    const long long id = hash_id(ids[q], c.hmode, c.buckets);
     if (id <= 0) continue;  // null / padding
     if (id >= c.rows) {
       record_error(p.err, MDL_ERR_BAD_INDEX);
@@ -244,10 +245,10 @@ __global__ void __launch_bounds__(kThreads, NV <= 2 ? 4 : 2) emb_pool_fwd_kernel
     return;
   }
   long long beg, end;
-  bag_ranges(p, c, lane, beg, end);
+  bag_ranges(p.id_offsets, c, lane, beg, end);
   if (c.pool == 0) {
     // one id per bag, found by the bag's own lane; lane groups then fetch the rows
-    const long long my_id = first_valid(p, c, beg, end);
+    const long long my_id = first_valid(p, p.ids, c, beg, end);
     for (int s0 = 0; s0 * bps < c.nb; s0 += 2) {
       float v[2][NV][4];
       long long brow[2];
@@ -345,12 +346,12 @@ __global__ void __launch_bounds__(kThreads, NV <= 2 ? 4 : 2)
   const int stride_cols = 4 * c.lanes;
   const __nv_bfloat16* gbase = grad_out + c.out_base;
   long long beg, end;
-  bag_ranges(p, c, lane, beg, end);
+  bag_ranges(p.id_offsets, c, lane, beg, end);
   // per bag (own lane): the single id (pool none) or the valid-id count (mean)
   long long my_id = 0;
   int my_count = 0;
   if (c.pool == 0) {
-    my_id = first_valid(p, c, beg, end);
+    my_id = first_valid(p, p.ids, c, beg, end);
   } else if (c.pool == 1) {
     for (long long q = beg; q < end; ++q) {
       const long long id = hash_id(__ldg(p.ids + q), c.hmode, c.buckets);
@@ -410,6 +411,228 @@ __global__ void __launch_bounds__(kThreads, NV <= 2 ? 4 : 2)
       for (int u = 0; u < 4; ++u)
         if (id[u] > 0 && id[u] < c.rows) push(id[u]);
     }
+  }
+}
+
+// ---- owner-push kernels (multi-rank) -----------------------------------------
+__device__ __forceinline__ bool owns(const EmbPlan& p, int t, long long id, long long& row) {
+  int owner;
+  route(p, t, id, owner, row);
+  return owner == p.rank;
+}
+
+// acc[row_off + phys(col .. col+3)] (+)= v
+template <bool ADD>
+__device__ __forceinline__ void acc_write4(const Chunk& c, float* acc, long long row_off, int col, int valid,
+                                           const float* v) {
+  const long long p0 = out_col(c, col);
+  const bool contiguous = !c.general && ((col < c.split) == (col + 3 < c.split));
+  if (valid == 4 && contiguous && ((row_off + p0) & 3) == 0) {
+    if (ADD) red_add4<true>(acc + row_off + p0, v);
+    else *reinterpret_cast<float4*>(acc + row_off + p0) = make_float4(v[0], v[1], v[2], v[3]);
+  } else {
+    for (int j = 0; j < valid; ++j) {
+      float* d = acc + row_off + out_col(c, col + j);
+      if (ADD) atomicAdd(d, v[j]);
+      else *d = v[j];
+    }
+  }
+}
+
+template <int NV>
+__global__ void __launch_bounds__(kThreads, NV <= 2 ? 4 : 2)
+    emb_owner_fwd_kernel(const EmbPlan p, const OwnerArgs o, long long total_chunks) {
+  const long long gw = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+  if (gw >= total_chunks * p.world) return;
+  const int r = static_cast<int>(gw / total_chunks);  // requester
+  const int lane = threadIdx.x & 31;
+  const Chunk c = load_chunk(p, gw - r * total_chunks);
+  if (c.nb <= 0) return;
+  const int sub = lane >> c.lg, sl = lane & (c.lanes - 1);
+  const int bps = 32 >> c.lg;
+  const int stride_cols = 4 * c.lanes;
+  float* acc = o.req_acc[r] + c.out_base;
+  if (c.t < 0) {  // dense inputs: written by their own rank
+    if (r != p.rank) return;
+    const int dcol = __ldg(p.f_dense_col + c.f);
+    for (int s = 0; s * bps < c.nb; ++s) {
+      const int bag = s * bps + sub;
+      if (bag >= c.nb) continue;
+      const long long brow = c.first + bag;
+      const float* src = o.dense + brow * o.dense_ld + dcol;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int col = sl * 4 + i * stride_cols;
+        if (col < c.width) {
+          float v[4];
+          for (int j = 0; j < 4; ++j) v[j] = (col + j < c.width) ? __ldg(src + col + j) : 0.f;
+          acc_write4<false>(c, acc, brow * c.out_ld, col, min(4, c.width - col), v);
+        }
+      }
+    }
+    return;
+  }
+  if (__ldg(p.t_mode + c.t) != 0 && __ldg(p.t_owner + c.t) != p.rank) return;  // whole table elsewhere
+  const long long* ids = o.req_ids[r];
+  long long beg, end;
+  bag_ranges(o.req_offsets[r], c, lane, beg, end);
+  if (c.pool == 0) {
+    const long long my_id = first_valid(p, ids, c, beg, end);
+    for (int s = 0; s * bps < c.nb; ++s) {
+      const int bag = s * bps + sub;
+      const long long id = __shfl_sync(0xffffffffu, my_id, bag & 31);
+      long long row;
+      if (bag >= c.nb || id <= 0 || !owns(p, c.t, id, row)) continue;
+      const float* src = c.tbl + row * c.dim;
+      const long long brow = c.first + bag;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int col = sl * 4 + i * stride_cols;
+        if (col < c.width) {
+          const float4 x = *reinterpret_cast<const float4*>(src + col);
+          const float v[4] = {x.x, x.y, x.z, x.w};
+          acc_write4<false>(c, acc, brow * c.out_ld, col, min(4, c.width - col), v);  // single contributor
+        }
+      }
+    }
+    return;
+  }
+  for (int s = 0; s * bps < c.nb; ++s) {
+    const int bag = s * bps + sub;
+    const long long qb = __shfl_sync(0xffffffffu, beg, bag & 31);
+    const long long qe = __shfl_sync(0xffffffffu, end, bag & 31);
+    if (bag >= c.nb) continue;
+    float sum[NV][4];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) sum[i][0] = sum[i][1] = sum[i][2] = sum[i][3] = 0.f;
+    int all = 0, mine = 0;
+    for (long long q = qb; q < qe; q += 4) {
+      long long id[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) id[u] = q + u < qe ? hash_id(ids[q + u], c.hmode, c.buckets) : 0;
+      float4 x[4][NV];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const bool valid = id[u] > 0 && id[u] < c.rows;
+        long long row = 0;
+        const bool own = valid && owns(p, c.t, id[u], row);
+        all += valid ? 1 : 0;
+        mine += own ? 1 : 0;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          const int col = sl * 4 + i * stride_cols;
+          x[u][i] = (own && col < c.dim) ? *reinterpret_cast<const float4*>(c.tbl + row * c.dim + col)
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          sum[i][0] += x[u][i].x; sum[i][1] += x[u][i].y; sum[i][2] += x[u][i].z; sum[i][3] += x[u][i].w;
+        }
+    }
+    if (mine == 0) continue;
+    const float scale = c.pool == 1 ? 1.f / static_cast<float>(all) : 1.f;
+    const long long brow = c.first + bag;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int col = sl * 4 + i * stride_cols;
+      if (col < c.width) {
+        const float v[4] = {sum[i][0] * scale, sum[i][1] * scale, sum[i][2] * scale, sum[i][3] * scale};
+        acc_write4<true>(c, acc, brow * c.out_ld, col, min(4, c.width - col), v);
+      }
+    }
+  }
+}
+
+template <int NV>
+__global__ void __launch_bounds__(kThreads, NV <= 2 ? 4 : 2)
+    emb_owner_bwd_kernel(const EmbPlan p, const OwnerArgs o, long long total_chunks) {
+  const long long gw = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+  if (gw >= total_chunks * p.world) return;
+  const int r = static_cast<int>(gw / total_chunks);
+  const int lane = threadIdx.x & 31;
+  const Chunk c = load_chunk(p, gw - r * total_chunks);
+  if (c.nb <= 0 || c.t < 0) return;
+  if (__ldg(p.t_mode + c.t) != 0 && __ldg(p.t_owner + c.t) != p.rank) return;
+  const int sub = lane >> c.lg, sl = lane & (c.lanes - 1);
+  const int bps = 32 >> c.lg;
+  const int stride_cols = 4 * c.lanes;
+  const __nv_bfloat16* gbase = reinterpret_cast<const __nv_bfloat16*>(o.req_grad[r]) + c.out_base;
+  const long long* ids = o.req_ids[r];
+  long long beg, end;
+  bag_ranges(o.req_offsets[r], c, lane, beg, end);
+  long long my_id = 0;
+  if (c.pool == 0) my_id = first_valid(p, ids, c, beg, end);
+  for (int s = 0; s * bps < c.nb; ++s) {
+    const int bag = s * bps + sub;
+    const long long qb = __shfl_sync(0xffffffffu, beg, bag & 31);
+    const long long qe = __shfl_sync(0xffffffffu, end, bag & 31);
+    const long long one = __shfl_sync(0xffffffffu, my_id, bag & 31);
+    if (bag >= c.nb) continue;
+    long long row = 0;
+    int all = 1;
+    if (c.pool == 0) {
+      if (one <= 0 || !owns(p, c.t, one, row)) continue;
+    } else {
+      all = 0;
+      int mine = 0;
+      for (long long q = qb; q < qe; ++q) {
+        const long long id = hash_id(ids[q], c.hmode, c.buckets);
+        if (id > 0 && id < c.rows) {
+          ++all;
+          long long rr;
+          mine += owns(p, c.t, id, rr) ? 1 : 0;
+        }
+      }
+      if (mine == 0) continue;
+    }
+    const float scale = c.pool == 1 ? 1.f / static_cast<float>(all) : 1.f;
+    const long long brow = c.first + bag;
+    float g[NV][4];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int col = sl * 4 + i * stride_cols;
+      if (col < c.dim) {
+        load4(c, gbase, brow * c.out_ld, col, min(4, c.dim - col), g[i]);
+        for (int j = 0; j < 4; ++j) g[i][j] *= scale;
+      }
+    }
+    auto push = [&](long long lrow) {
+      float* dst = c.gtbl + lrow * c.dim;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int col = sl * 4 + i * stride_cols;
+        if (col < c.dim) red_add4<false>(dst + col, g[i]);
+      }
+      if (sl == 0) *reinterpret_cast<volatile unsigned char*>(c.ftbl + lrow) = 1;
+    };
+    if (c.pool == 0) {
+      push(row);
+      continue;
+    }
+    for (long long q = qb; q < qe; ++q) {
+      const long long id = hash_id(ids[q], c.hmode, c.buckets);
+      long long rr;
+      if (id > 0 && id < c.rows && owns(p, c.t, id, rr)) push(rr);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) acc_to_bf16_kernel(const float* __restrict__ acc, __nv_bfloat16* out,
+                                                               long long n8) {
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const float4 a = reinterpret_cast<const float4*>(acc)[2 * i];
+    const float4 b = reinterpret_cast<const float4*>(acc)[2 * i + 1];
+    uint4 u;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+    h[0] = __floats2bfloat162_rn(a.x, a.y);
+    h[1] = __floats2bfloat162_rn(a.z, a.w);
+    h[2] = __floats2bfloat162_rn(b.x, b.y);
+    h[3] = __floats2bfloat162_rn(b.z, b.w);
+    reinterpret_cast<uint4*>(out)[i] = u;
   }
 }
 
@@ -756,6 +979,46 @@ cudaError_t emb_pool_backward(const EmbPlan& plan, const void* grad_out, long lo
     else if (nv == 4) MDL_BWD(false, 4, true); else MDL_BWD(false, 8, true);
   }
 #undef MDL_BWD
+  return cudaGetLastError();
+}
+
+cudaError_t emb_owner_forward(const EmbPlan& plan, const OwnerArgs& o, long long total_chunks, cudaStream_t stream) {
+  if (total_chunks <= 0) return cudaSuccess;
+  for (int r = 0; r < plan.world; ++r)
+    if (o.req_ids[r] == nullptr || o.req_offsets[r] == nullptr || o.req_acc[r] == nullptr) return cudaErrorInvalidValue;
+  const int grid = blocks_for(total_chunks * plan.world);
+  if (plan.max_vec <= 1) emb_owner_fwd_kernel<1><<<grid, kThreads, 0, stream>>>(plan, o, total_chunks);
+  else if (plan.max_vec <= 2) emb_owner_fwd_kernel<2><<<grid, kThreads, 0, stream>>>(plan, o, total_chunks);
+  else if (plan.max_vec <= 4) emb_owner_fwd_kernel<4><<<grid, kThreads, 0, stream>>>(plan, o, total_chunks);
+  else emb_owner_fwd_kernel<8><<<grid, kThreads, 0, stream>>>(plan, o, total_chunks);
+  return cudaGetLastError();
+}
+
+cudaError_t emb_owner_backward(const EmbPlan& plan, const OwnerArgs& o, long long total_chunks,
+                               cudaStream_t stream) {
+  if (total_chunks <= 0) return cudaSuccess;
+  for (int r = 0; r < plan.world; ++r)
+    if (o.req_ids[r] == nullptr || o.req_offsets[r] == nullptr || o.req_grad[r] == nullptr) return cudaErrorInvalidValue;
+  if (plan.grad_slabs[plan.rank] == nullptr || plan.flags[plan.rank] == nullptr) return cudaErrorInvalidValue;
+  const int grid = blocks_for(total_chunks * plan.world);
+  if (plan.max_vec <= 1) emb_owner_bwd_kernel<1><<<grid, kThreads, 0, stream>>>(plan, o, total_chunks);
+  else if (plan.max_vec <= 2) emb_owner_bwd_kernel<2><<<grid, kThreads, 0, stream>>>(plan, o, total_chunks);
+  else if (plan.max_vec <= 4) emb_owner_bwd_kernel<4><<<grid, kThreads, 0, stream>>>(plan, o, total_chunks);
+  else emb_owner_bwd_kernel<8><<<grid, kThreads, 0, stream>>>(plan, o, total_chunks);
+  return cudaGetLastError();
+}
+
+cudaError_t emb_acc_to_bf16(const float* acc, void* out, long long n, cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  if ((n % 8) || (reinterpret_cast<uintptr_t>(acc) & 15) || (reinterpret_cast<uintptr_t>(out) & 15))
+    return cudaErrorInvalidValue;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long n8 = n / 8;
+  const long long want = (n8 + kThreads - 1) / kThreads;
+  const int grid = static_cast<int>(want < sms * 16 ? want : sms * 16);
+  acc_to_bf16_kernel<<<grid, kThreads, 0, stream>>>(acc, reinterpret_cast<__nv_bfloat16*>(out), n8);
   return cudaGetLastError();
 }
 

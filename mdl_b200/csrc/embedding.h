@@ -70,6 +70,34 @@ cudaError_t emb_pool_forward(const EmbPlan& plan, long long total_chunks, cudaSt
 cudaError_t emb_pool_backward(const EmbPlan& plan, const void* grad_out, long long total_chunks,
                               cudaStream_t stream);
 
+// ---- multi-rank lookup, owner side ("owner-push") -------------------------
+// With several ranks the random row traffic stays in each owner's local HBM and
+// only pooled vectors cross NVLink:
+//   forward : every rank stages its batch ids/offsets in peer-visible memory;
+//             owner o walks the bags of EVERY requester r, sums the rows it owns
+//             (local gathers), scales by the bag's global valid-id count (mean)
+//             and adds the partial into r's fp32 accumulator [rows, out_ld] with
+//             vector reductions over NVLink (a plain store when it is the single
+//             contributor: the first valid id of a single-valued feature);
+//             dense inputs are copied by their own rank. r then converts its
+//             accumulator to the bf16 output.
+//   backward: r stages d(out) in peer-visible memory; owner o reads the bf16
+//             gradient slice of each bag it holds ids of (NVLink) and adds it
+//             into its LOCAL grad slab rows, marking them touched.
+// Remote accesses are contiguous 128-256 byte runs of small staging buffers.
+struct OwnerArgs {
+  const long long* req_ids[kMaxWorld] = {};      // each requester's staged ids
+  const long long* req_offsets[kMaxWorld] = {};  // ... and CSR offsets
+  float* req_acc[kMaxWorld] = {};                // forward: each requester's fp32 accumulator
+  const void* req_grad[kMaxWorld] = {};          // backward: each requester's bf16 d(out)
+  const float* dense = nullptr;                  // this rank's dense inputs (forward)
+  long long dense_ld = 0;
+};
+cudaError_t emb_owner_forward(const EmbPlan& plan, const OwnerArgs& o, long long total_chunks, cudaStream_t stream);
+cudaError_t emb_owner_backward(const EmbPlan& plan, const OwnerArgs& o, long long total_chunks, cudaStream_t stream);
+// out[i] = bf16(acc[i]) for i < n (n a multiple of 8, 16-byte aligned buffers)
+cudaError_t emb_acc_to_bf16(const float* acc, void* out, long long n, cudaStream_t stream);
+
 // Row-wise Adagrad over this rank's touched rows (reference optim.py:31-62):
 //   g = grad * grad_scale * clip_scale[0]; acc += mean(g^2); w -= lr * g / (sqrt(acc) + eps)
 // then zero the grad rows and clear the flags. Touched rows are found by a

@@ -148,6 +148,7 @@ class EmbeddingStore:
         self.touched_list = (torch.empty(max(self.total_rows, 1), dtype=torch.int32, device=dev)
                              if dev.type == "cuda" else None)
         self.touched_count = torch.zeros(1, dtype=torch.int32, device=dev) if dev.type == "cuda" else None
+        self._exchanges: dict = {}  # multi-rank lookup staging per (plan, rows)
         # CPU path: dense gradient accumulation per table (sparse rows tracked by a mask)
         self._cpu_touched = torch.zeros(self.total_rows, dtype=torch.bool) if dev.type != "cuda" else None
 
@@ -537,6 +538,43 @@ def backward_reference(store: EmbeddingStore, plan: LookupPlan, ids: torch.Tenso
 
 
 # ====================================================================== autograd op
+class _Exchange:
+    """Peer-visible staging of one lookup plan's traffic across ranks (CUDA, world > 1).
+
+    Holds each rank's batch ids/offsets, the fp32 accumulator the owners add pooled
+    partials into, and the bf16 output gradient the owners read back. Capacities
+    are agreed on once (collectively) from the first batch: twice the largest id
+    count of any rank.
+    """
+
+    def __init__(self, store: "EmbeddingStore", plan: "LookupPlan", rows: int, n_ids: int, n_offsets: int) -> None:
+        from ..parallel.symm import SymmetricBuffers
+
+        dev = store.device
+        t = torch.tensor([n_ids, n_offsets, rows, -rows], dtype=torch.int64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=store.process_group)
+        if int(t[2]) != -int(t[3]):
+            raise ValueError("every rank must look up the same number of rows per step")
+        self.rows = rows
+        self.cap_ids = 2 * int(t[0]) + 4096
+        self.cap_offsets = int(t[1])
+        self.n_out = (rows * plan.out_ld + 7) // 8 * 8
+        self.symm = SymmetricBuffers({"ids": (self.cap_ids, torch.int64), "offsets": (self.cap_offsets, torch.int64),
+                                      "acc": (self.n_out, torch.float32), "grad": (self.n_out, torch.bfloat16)},
+                                     device=dev, process_group=store.process_group)
+        self.ids = self.symm.local("ids")
+        self.offsets = self.symm.local("offsets")
+        self.acc = self.symm.local("acc")
+        self.grad = self.symm.local("grad")
+
+    def stage(self, ids: torch.Tensor, offsets: torch.Tensor) -> None:
+        if ids.numel() > self.cap_ids or offsets.numel() > self.cap_offsets:
+            raise RuntimeError(f"batch holds {ids.numel()} ids / {offsets.numel()} offsets; the lookup exchange "
+                               f"was sized for {self.cap_ids} / {self.cap_offsets}")
+        self.ids[:ids.numel()].copy_(ids)
+        self.offsets[:offsets.numel()].copy_(offsets)
+
+
 class _FusedLookup(torch.autograd.Function):
     @staticmethod
     def forward(ctx, anchor, store, plan, ids, offsets, dense, rows):
@@ -544,6 +582,8 @@ class _FusedLookup(torch.autograd.Function):
         ctx.save_for_backward(ids, offsets)
         if plan.num_src * rows + 1 > offsets.numel():
             raise ValueError(f"lookup plan reads {plan.num_src} batch features; offsets hold {offsets.numel()}")
+        if ids.is_cuda and store.world > 1:
+            return _owner_forward(store, plan, ids, offsets, dense, rows)
         if ids.is_cuda:
             meta, chunks, max_vec = plan.device_meta(store, rows)
             out = torch.empty(rows, plan.out_ld, dtype=torch.bfloat16, device=ids.device)
@@ -558,7 +598,9 @@ class _FusedLookup(torch.autograd.Function):
     def backward(ctx, grad_out):
         ids, offsets = ctx.saved_tensors
         store, plan, rows = ctx.store, ctx.plan, ctx.rows
-        if ids.is_cuda:
+        if ids.is_cuda and store.world > 1:
+            _owner_backward(store, plan, ids, offsets, grad_out, rows)
+        elif ids.is_cuda:
             meta, chunks, max_vec = plan.device_meta(store, rows)
             g = grad_out if grad_out.dtype == torch.bfloat16 else grad_out.to(torch.bfloat16)
             ext().emb_backward(meta, store.peer_ptrs("slab"), store.peer_ptrs("grad"), store.peer_ptrs("flags"),
@@ -566,6 +608,49 @@ class _FusedLookup(torch.autograd.Function):
         else:
             backward_reference(store, plan, ids, offsets, grad_out, rows)
         return (None,) * 7
+
+
+def _exchange(store: EmbeddingStore, plan: LookupPlan, ids: torch.Tensor, offsets: torch.Tensor,
+              rows: int) -> _Exchange:
+    key = (id(plan), rows)
+    ex = store._exchanges.get(key)
+    if ex is None:
+        ex = _Exchange(store, plan, rows, ids.numel(), offsets.numel())
+        store._exchanges[key] = ex
+    return ex
+
+
+def _owner_forward(store, plan, ids, offsets, dense, rows):
+    """Multi-rank lookup: owners push pooled partials into each requester's accumulator."""
+
+    C = ext()
+    ex = _exchange(store, plan, ids, offsets, rows)
+    ex.stage(ids, offsets)
+    ex.acc.zero_()
+    meta, chunks, max_vec = plan.device_meta(store, rows)
+    ex.symm.barrier()  # every rank's ids staged, every accumulator zeroed
+    C.emb_owner_forward(meta, store.peer_ptrs("slab"), store.rank, ex.ids, ex.offsets, ex.symm.peer_ptrs("ids"),
+                        ex.symm.peer_ptrs("offsets"), ex.symm.peer_ptrs("acc"), dense, plan.dense_width, chunks,
+                        error_word(ids.device), max_vec)
+    ex.symm.barrier()  # every owner's partials have landed
+    out = torch.empty(rows, plan.out_ld, dtype=torch.bfloat16, device=ids.device)
+    C.emb_acc_to_bf16(ex.acc, out)
+    return out
+
+
+def _owner_backward(store, plan, ids, offsets, grad_out, rows):
+    """Multi-rank gradient: owners pull each requester's d(out) slices into their own grad rows."""
+
+    C = ext()
+    ex = _exchange(store, plan, ids, offsets, rows)
+    g = grad_out if grad_out.dtype == torch.bfloat16 else grad_out.to(torch.bfloat16)
+    ex.grad[:g.numel()].copy_(g.reshape(-1))
+    meta, chunks, max_vec = plan.device_meta(store, rows)
+    ex.symm.barrier()  # every requester's gradient staged
+    C.emb_owner_backward(meta, store.peer_ptrs("slab"), store.peer_ptrs("grad"), store.peer_ptrs("flags"), store.rank,
+                         ex.ids, ex.offsets, ex.symm.peer_ptrs("ids"), ex.symm.peer_ptrs("offsets"),
+                         ex.symm.peer_ptrs("grad"), chunks, error_word(ids.device), max_vec)
+    ex.symm.barrier()  # staged ids / gradients may be overwritten after this point
 
 
 def fused_lookup(store: EmbeddingStore, plan: LookupPlan, ids: torch.Tensor, offsets: torch.Tensor,
