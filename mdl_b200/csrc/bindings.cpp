@@ -102,8 +102,8 @@ mdl::EmbPlan make_plan(const std::vector<at::Tensor>& meta, const std::vector<in
   //  6 f_width(i32) 7 f_lanes(i32) 8 f_out_base(i64) 9 f_out_ld(i64) 10 f_out_col(i32) 11 f_slice(i32)
   //  12 f_slice_stride(i32) 13 f_dense_col(i32) 14 t_base(i64) 15 t_row_base(i64) 16 t_dim(i32) 17 t_mode(i32)
   //  18 t_cyc(i32) 19 t_owner(i32) 20 t_rows(i64) 21 t_base_all(i64 [W*T]) 22 t_row_base_all(i64 [W*T])
-  //  23 f_src_bag(i64)
-  TORCH_CHECK(meta.size() == 24, "embedding plan needs 24 metadata tensors");
+  //  23 f_src_bag(i64) 24 f_phys0(i32) 25 f_split(i32)
+  TORCH_CHECK(meta.size() == 26, "embedding plan needs 26 metadata tensors");
   mdl::EmbPlan p;
   p.num_features = static_cast<int>(meta[2].numel());
   p.world = static_cast<int>(slabs.size());
@@ -135,6 +135,8 @@ mdl::EmbPlan make_plan(const std::vector<at::Tensor>& meta, const std::vector<in
   p.t_base_all = dptr<long long>(meta[21]);
   p.t_row_base_all = dptr<long long>(meta[22]);
   p.f_src_bag = dptr<long long>(meta[23]);
+  p.f_phys0 = dptr<int>(meta[24]);
+  p.f_split = dptr<int>(meta[25]);
   TORCH_CHECK(meta[23].numel() == p.num_features, "f_src_bag must have one entry per feature");
   TORCH_CHECK(meta[21].numel() == static_cast<int64_t>(p.num_tables) * p.world, "t_base_all must be [world * T]");
   for (int r = 0; r < p.world; ++r) {
@@ -173,49 +175,72 @@ void emb_backward(const std::vector<at::Tensor>& meta, const std::vector<int64_t
   g_launches += 1;
 }
 
-mdl::OwnerArgs owner_args(const std::vector<int64_t>& req_ids, const std::vector<int64_t>& req_offsets, int world) {
-  TORCH_CHECK(static_cast<int>(req_ids.size()) == world && static_cast<int>(req_offsets.size()) == world,
-              "one staged ids/offsets pointer per rank");
+mdl::OwnerArgs owner_args(const std::vector<int64_t>& bundles, const std::vector<int64_t>& rows,
+                          const std::vector<int64_t>& counts, int64_t cap_bundles, int64_t cap_rows, int world) {
+  TORCH_CHECK(static_cast<int>(bundles.size()) == world && static_cast<int>(rows.size()) == world &&
+                  static_cast<int>(counts.size()) == world,
+              "one bundle, row-list and count pointer per rank");
   mdl::OwnerArgs o;
   for (int r = 0; r < world; ++r) {
-    o.req_ids[r] = reinterpret_cast<const long long*>(req_ids[r]);
-    o.req_offsets[r] = reinterpret_cast<const long long*>(req_offsets[r]);
+    o.bundles[r] = reinterpret_cast<mdl::RouteBundle*>(bundles[r]);
+    o.rows[r] = reinterpret_cast<int*>(rows[r]);
+    o.counts[r] = reinterpret_cast<int*>(counts[r]);
   }
+  o.cap_bundles = cap_bundles;
+  o.cap_rows = cap_rows;
   return o;
 }
 
-// Owner-push lookup: this rank gathers the rows it owns for every requester's bags
-// and adds the pooled partials into each requester's fp32 accumulator.
-void emb_owner_forward(const std::vector<at::Tensor>& meta, const std::vector<int64_t>& slabs, int64_t rank,
-                       const at::Tensor& ids, const at::Tensor& id_offsets, const std::vector<int64_t>& req_ids,
-                       const std::vector<int64_t>& req_offsets, const std::vector<int64_t>& req_acc,
-                       const std::optional<at::Tensor>& dense, int64_t dense_ld, int64_t total_chunks,
-                       const std::optional<at::Tensor>& err, int64_t max_vec) {
+// Route pass: this rank's contributing ids -> entries in their owners' segments;
+// dense inputs -> this rank's accumulator.
+void emb_route(const std::vector<at::Tensor>& meta, const std::vector<int64_t>& slabs, int64_t rank,
+               const at::Tensor& ids, const at::Tensor& id_offsets, const std::vector<int64_t>& bundles,
+               const std::vector<int64_t>& rows, const std::vector<int64_t>& counts, int64_t cap_bundles,
+               int64_t cap_rows, const at::Tensor& acc,
+               const std::optional<at::Tensor>& dense, int64_t dense_ld, int64_t total_chunks,
+               const std::optional<at::Tensor>& err, int64_t max_vec) {
   c10::cuda::CUDAGuard guard(ids.device());
   mdl::EmbPlan p = make_plan(meta, slabs, {}, {}, rank, ids, id_offsets, std::nullopt, 0, err, max_vec);
-  mdl::OwnerArgs o = owner_args(req_ids, req_offsets, p.world);
-  TORCH_CHECK(static_cast<int>(req_acc.size()) == p.world, "one accumulator pointer per rank");
-  for (int r = 0; r < p.world; ++r) o.req_acc[r] = reinterpret_cast<float*>(req_acc[r]);
+  mdl::OwnerArgs o = owner_args(bundles, rows, counts, cap_bundles, cap_rows, p.world);
+  TORCH_CHECK(acc.scalar_type() == at::kFloat, "accumulator must be fp32");
+  o.acc[p.rank] = acc.data_ptr<float>();
   if (dense.has_value()) {
     TORCH_CHECK(dense->scalar_type() == at::kFloat, "dense inputs must be fp32");
     o.dense = dense->data_ptr<float>();
     o.dense_ld = dense_ld;
   }
-  check(mdl::emb_owner_forward(p, o, total_chunks, stream_of(ids)), "emb_owner_forward");
+  check(mdl::emb_route(p, o, total_chunks, stream_of(ids)), "emb_route");
+  g_launches += 1;
+}
+
+void emb_owner_forward(const std::vector<at::Tensor>& meta, const std::vector<int64_t>& slabs, int64_t rank,
+                       const at::Tensor& ids, const at::Tensor& id_offsets, const std::vector<int64_t>& bundles,
+                       const std::vector<int64_t>& rows, const std::vector<int64_t>& counts, int64_t cap_bundles,
+                       int64_t cap_rows, const std::vector<int64_t>& accs,
+                       int64_t max_dim, const std::optional<at::Tensor>& err) {
+  c10::cuda::CUDAGuard guard(ids.device());
+  mdl::EmbPlan p = make_plan(meta, slabs, {}, {}, rank, ids, id_offsets, std::nullopt, 0, err, 1);
+  p.max_dim = static_cast<int>(max_dim);
+  mdl::OwnerArgs o = owner_args(bundles, rows, counts, cap_bundles, cap_rows, p.world);
+  TORCH_CHECK(static_cast<int>(accs.size()) == p.world, "one accumulator pointer per rank");
+  for (int r = 0; r < p.world; ++r) o.acc[r] = reinterpret_cast<float*>(accs[r]);
+  check(mdl::emb_owner_forward(p, o, stream_of(ids)), "emb_owner_forward");
   g_launches += 1;
 }
 
 void emb_owner_backward(const std::vector<at::Tensor>& meta, const std::vector<int64_t>& slabs,
                         const std::vector<int64_t>& grad_slabs, const std::vector<int64_t>& flags, int64_t rank,
-                        const at::Tensor& ids, const at::Tensor& id_offsets, const std::vector<int64_t>& req_ids,
-                        const std::vector<int64_t>& req_offsets, const std::vector<int64_t>& req_grad,
-                        int64_t total_chunks, const std::optional<at::Tensor>& err, int64_t max_vec) {
+                        const at::Tensor& ids, const at::Tensor& id_offsets, const std::vector<int64_t>& bundles,
+                        const std::vector<int64_t>& rows, const std::vector<int64_t>& counts, int64_t cap_bundles,
+                        int64_t cap_rows, const std::vector<int64_t>& grads,
+                        int64_t max_dim, const std::optional<at::Tensor>& err) {
   c10::cuda::CUDAGuard guard(ids.device());
-  mdl::EmbPlan p = make_plan(meta, slabs, grad_slabs, flags, rank, ids, id_offsets, std::nullopt, 0, err, max_vec);
-  mdl::OwnerArgs o = owner_args(req_ids, req_offsets, p.world);
-  TORCH_CHECK(static_cast<int>(req_grad.size()) == p.world, "one staged gradient pointer per rank");
-  for (int r = 0; r < p.world; ++r) o.req_grad[r] = reinterpret_cast<const void*>(req_grad[r]);
-  check(mdl::emb_owner_backward(p, o, total_chunks, stream_of(ids)), "emb_owner_backward");
+  mdl::EmbPlan p = make_plan(meta, slabs, grad_slabs, flags, rank, ids, id_offsets, std::nullopt, 0, err, 1);
+  p.max_dim = static_cast<int>(max_dim);
+  mdl::OwnerArgs o = owner_args(bundles, rows, counts, cap_bundles, cap_rows, p.world);
+  TORCH_CHECK(static_cast<int>(grads.size()) == p.world, "one staged gradient pointer per rank");
+  for (int r = 0; r < p.world; ++r) o.grad[r] = reinterpret_cast<const void*>(grads[r]);
+  check(mdl::emb_owner_backward(p, o, stream_of(ids)), "emb_owner_backward");
   g_launches += 1;
 }
 
@@ -659,6 +684,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
 
   m.def("emb_forward", &emb_forward);
   m.def("emb_backward", &emb_backward);
+  m.def("emb_route", &emb_route);
   m.def("emb_owner_forward", &emb_owner_forward);
   m.def("emb_owner_backward", &emb_owner_backward);
   m.def("emb_acc_to_bf16", &emb_acc_to_bf16);

@@ -415,207 +415,284 @@ __global__ void __launch_bounds__(kThreads, NV <= 2 ? 4 : 2)
 }
 
 // ---- owner-push kernels (multi-rank) -----------------------------------------
-__device__ __forceinline__ bool owns(const EmbPlan& p, int t, long long id, long long& row) {
-  int owner;
-  route(p, t, id, owner, row);
-  return owner == p.rank;
+// Physical output column of column `col` of feature f (host-computed phys0/split;
+// split < 0 marks a feature that crosses several token slices).
+__device__ __forceinline__ long long feat_col(const EmbPlan& p, int f, int col) {
+  const int split = __ldg(p.f_split + f);
+  if (split < 0) return phys_col(__ldg(p.f_out_col + f) + col, __ldg(p.f_slice + f), __ldg(p.f_slice_stride + f));
+  return __ldg(p.f_phys0 + f) + col + (col >= split ? __ldg(p.f_slice_stride + f) - __ldg(p.f_slice + f) : 0);
 }
 
-// acc[row_off + phys(col .. col+3)] (+)= v
-template <bool ADD>
-__device__ __forceinline__ void acc_write4(const Chunk& c, float* acc, long long row_off, int col, int valid,
-                                           const float* v) {
-  const long long p0 = out_col(c, col);
-  const bool contiguous = !c.general && ((col < c.split) == (col + 3 < c.split));
-  if (valid == 4 && contiguous && ((row_off + p0) & 3) == 0) {
-    if (ADD) red_add4<true>(acc + row_off + p0, v);
-    else *reinterpret_cast<float4*>(acc + row_off + p0) = make_float4(v[0], v[1], v[2], v[3]);
-  } else {
-    for (int j = 0; j < valid; ++j) {
-      float* d = acc + row_off + out_col(c, col + j);
-      if (ADD) atomicAdd(d, v[j]);
-      else *d = v[j];
-    }
-  }
+__device__ __forceinline__ bool feat_vec4(const EmbPlan& p, int f, int col, long long addr) {
+  const int split = __ldg(p.f_split + f);
+  return split >= 0 && ((col < split) == (col + 3 < split)) && (addr & 3) == 0;
 }
 
-template <int NV>
-__global__ void __launch_bounds__(kThreads, NV <= 2 ? 4 : 2)
-    emb_owner_fwd_kernel(const EmbPlan p, const OwnerArgs o, long long total_chunks) {
-  const long long gw = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
-  if (gw >= total_chunks * p.world) return;
-  const int r = static_cast<int>(gw / total_chunks);  // requester
+// Route pass of this rank: lane = bag. Per (bag, owner) one bundle; rows of
+// multi-row bundles go to the owner's row list, contiguous per bundle.
+__global__ void __launch_bounds__(kThreads) emb_route_kernel(const EmbPlan p, const OwnerArgs o,
+                                                            long long total_chunks) {
+  const long long warp = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+  if (warp >= total_chunks) return;
   const int lane = threadIdx.x & 31;
-  const Chunk c = load_chunk(p, gw - r * total_chunks);
+  const Chunk c = load_chunk(p, warp);
   if (c.nb <= 0) return;
-  const int sub = lane >> c.lg, sl = lane & (c.lanes - 1);
-  const int bps = 32 >> c.lg;
-  const int stride_cols = 4 * c.lanes;
-  float* acc = o.req_acc[r] + c.out_base;
-  if (c.t < 0) {  // dense inputs: written by their own rank
-    if (r != p.rank) return;
+  if (c.t < 0) {  // dense inputs: copied into this rank's own accumulator
+    float* acc = o.acc[p.rank] + c.out_base;
     const int dcol = __ldg(p.f_dense_col + c.f);
+    const int sub = lane >> c.lg, sl = lane & (c.lanes - 1);
+    const int bps = 32 >> c.lg;
     for (int s = 0; s * bps < c.nb; ++s) {
       const int bag = s * bps + sub;
       if (bag >= c.nb) continue;
       const long long brow = c.first + bag;
       const float* src = o.dense + brow * o.dense_ld + dcol;
-#pragma unroll
-      for (int i = 0; i < NV; ++i) {
-        const int col = sl * 4 + i * stride_cols;
-        if (col < c.width) {
-          float v[4];
-          for (int j = 0; j < 4; ++j) v[j] = (col + j < c.width) ? __ldg(src + col + j) : 0.f;
-          acc_write4<false>(c, acc, brow * c.out_ld, col, min(4, c.width - col), v);
-        }
-      }
+      for (int col = sl * 4; col < c.width; col += 4 * c.lanes)
+        for (int j = 0; j < 4 && col + j < c.width; ++j)
+          acc[brow * c.out_ld + out_col(c, col + j)] = __ldg(src + col + j);
     }
     return;
   }
-  if (__ldg(p.t_mode + c.t) != 0 && __ldg(p.t_owner + c.t) != p.rank) return;  // whole table elsewhere
-  const long long* ids = o.req_ids[r];
+  const int W = p.world;
   long long beg, end;
-  bag_ranges(o.req_offsets[r], c, lane, beg, end);
+  bag_ranges(p.id_offsets, c, lane, beg, end);
+  // per owner: rows of this lane's bag and the last one seen (registers: the owner
+  // index is only ever compared against compile-time constants)
+  int cnt[kMaxWorld], last[kMaxWorld];
+#pragma unroll
+  for (int j = 0; j < kMaxWorld; ++j) cnt[j] = last[j] = 0;
+  int valid = 0;
+  auto note = [&](long long id) {
+    int owner;
+    long long row;
+    route(p, c.t, id, owner, row);
+#pragma unroll
+    for (int j = 0; j < kMaxWorld; ++j) {
+      if (j == owner) {
+        ++cnt[j];
+        last[j] = static_cast<int>(row);
+      }
+    }
+    ++valid;
+  };
   if (c.pool == 0) {
-    const long long my_id = first_valid(p, ids, c, beg, end);
-    for (int s = 0; s * bps < c.nb; ++s) {
-      const int bag = s * bps + sub;
-      const long long id = __shfl_sync(0xffffffffu, my_id, bag & 31);
-      long long row;
-      if (bag >= c.nb || id <= 0 || !owns(p, c.t, id, row)) continue;
-      const float* src = c.tbl + row * c.dim;
-      const long long brow = c.first + bag;
-#pragma unroll
-      for (int i = 0; i < NV; ++i) {
-        const int col = sl * 4 + i * stride_cols;
-        if (col < c.width) {
-          const float4 x = *reinterpret_cast<const float4*>(src + col);
-          const float v[4] = {x.x, x.y, x.z, x.w};
-          acc_write4<false>(c, acc, brow * c.out_ld, col, min(4, c.width - col), v);  // single contributor
-        }
+    const long long id = first_valid(p, p.ids, c, beg, end);
+    if (id > 0) note(id);
+  } else {
+    for (long long q = beg; q < end; ++q) {
+      const long long id = hash_id(__ldg(p.ids + q), c.hmode, c.buckets);
+      if (id <= 0) continue;
+      if (id >= c.rows) {
+        record_error(p.err, MDL_ERR_BAD_INDEX);
+        continue;
       }
+      note(id);
     }
-    return;
   }
-  for (int s = 0; s * bps < c.nb; ++s) {
-    const int bag = s * bps + sub;
-    const long long qb = __shfl_sync(0xffffffffu, beg, bag & 31);
-    const long long qe = __shfl_sync(0xffffffffu, end, bag & 31);
-    if (bag >= c.nb) continue;
-    float sum[NV][4];
+  const float scale = (c.pool == 1 && valid > 0) ? 1.f / static_cast<float>(valid) : 1.f;
+  // allocate bundles and row-list slots owner by owner (warp-aggregated atomics)
+  int row_start[kMaxWorld];
+  bool need_rows = false;
+  const unsigned lt = (1u << lane) - 1u;
 #pragma unroll
-    for (int i = 0; i < NV; ++i) sum[i][0] = sum[i][1] = sum[i][2] = sum[i][3] = 0.f;
-    int all = 0, mine = 0;
-    for (long long q = qb; q < qe; q += 4) {
-      long long id[4];
+  for (int j = 0; j < kMaxWorld; ++j) {
+    row_start[j] = 0;
+    if (j >= W) continue;
+    const int k = cnt[j];
+    const unsigned want = __ballot_sync(0xffffffffu, k > 0);
+    if (want == 0) continue;
+    const int multi = k > 1 ? k : 0;  // rows that go to the row list
+    int incl = multi;
 #pragma unroll
-      for (int u = 0; u < 4; ++u) id[u] = q + u < qe ? hash_id(ids[q + u], c.hmode, c.buckets) : 0;
-      float4 x[4][NV];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const bool valid = id[u] > 0 && id[u] < c.rows;
-        long long row = 0;
-        const bool own = valid && owns(p, c.t, id[u], row);
-        all += valid ? 1 : 0;
-        mine += own ? 1 : 0;
-#pragma unroll
-        for (int i = 0; i < NV; ++i) {
-          const int col = sl * 4 + i * stride_cols;
-          x[u][i] = (own && col < c.dim) ? *reinterpret_cast<const float4*>(c.tbl + row * c.dim + col)
-                                         : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-#pragma unroll
-        for (int i = 0; i < NV; ++i) {
-          sum[i][0] += x[u][i].x; sum[i][1] += x[u][i].y; sum[i][2] += x[u][i].z; sum[i][3] += x[u][i].w;
-        }
+    for (int d = 1; d < 32; d <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl += y;
     }
-    if (mine == 0) continue;
-    const float scale = c.pool == 1 ? 1.f / static_cast<float>(all) : 1.f;
-    const long long brow = c.first + bag;
+    const int total_rows = __shfl_sync(0xffffffffu, incl, 31);
+    int bbase = 0, rbase = 0;
+    if (lane == 0) {
+      bbase = atomicAdd(o.counts[p.rank] + 2 * j, __popc(want));
+      if (total_rows > 0) rbase = atomicAdd(o.counts[p.rank] + 2 * j + 1, total_rows);
+    }
+    bbase = __shfl_sync(0xffffffffu, bbase, 0);
+    rbase = __shfl_sync(0xffffffffu, rbase, 0);
+    if (k > 0) {
+      const long long bi = bbase + __popc(want & lt);
+      row_start[j] = rbase + incl - multi;
+      if (bi < o.cap_bundles && (multi == 0 || row_start[j] + multi <= o.cap_rows)) {
+        RouteBundle b;
+        b.bag = static_cast<int>(c.first + lane);
+        b.f_count = c.f | (k << 16);
+        b.row = k == 1 ? last[j] : row_start[j];
+        b.scale = scale;
+        o.bundles[p.rank][j * o.cap_bundles + bi] = b;
+        need_rows |= multi > 0;
+      } else {
+        record_error(p.err, MDL_ERR_CAPACITY);
+        cnt[j] = 0;  // nothing of this bag reaches owner j
+      }
+    }
+  }
+  if (!need_rows) return;
+  // second pass: rows of multi-row bundles, in bag order
+  int fill[kMaxWorld];
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int col = sl * 4 + i * stride_cols;
-      if (col < c.width) {
-        const float v[4] = {sum[i][0] * scale, sum[i][1] * scale, sum[i][2] * scale, sum[i][3] * scale};
-        acc_write4<true>(c, acc, brow * c.out_ld, col, min(4, c.width - col), v);
+  for (int j = 0; j < kMaxWorld; ++j) fill[j] = 0;
+  for (long long q = beg; q < end; ++q) {
+    const long long id = hash_id(__ldg(p.ids + q), c.hmode, c.buckets);
+    if (id <= 0 || id >= c.rows) continue;
+    int owner;
+    long long row;
+    route(p, c.t, id, owner, row);
+#pragma unroll
+    for (int j = 0; j < kMaxWorld; ++j) {
+      if (j == owner && cnt[j] > 1) {
+        o.rows[p.rank][j * o.cap_rows + row_start[j] + fill[j]] = static_cast<int>(row);
+        ++fill[j];
       }
     }
   }
 }
 
+// Owner side, forward: one group of 16 lanes per bundle (two in flight): gather and
+// sum the bundle's rows from the local shard, scale, add the pooled vector into the
+// requester's accumulator.
 template <int NV>
-__global__ void __launch_bounds__(kThreads, NV <= 2 ? 4 : 2)
-    emb_owner_bwd_kernel(const EmbPlan p, const OwnerArgs o, long long total_chunks) {
-  const long long gw = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
-  if (gw >= total_chunks * p.world) return;
-  const int r = static_cast<int>(gw / total_chunks);
-  const int lane = threadIdx.x & 31;
-  const Chunk c = load_chunk(p, gw - r * total_chunks);
-  if (c.nb <= 0 || c.t < 0) return;
-  if (__ldg(p.t_mode + c.t) != 0 && __ldg(p.t_owner + c.t) != p.rank) return;
-  const int sub = lane >> c.lg, sl = lane & (c.lanes - 1);
-  const int bps = 32 >> c.lg;
-  const int stride_cols = 4 * c.lanes;
-  const __nv_bfloat16* gbase = reinterpret_cast<const __nv_bfloat16*>(o.req_grad[r]) + c.out_base;
-  const long long* ids = o.req_ids[r];
-  long long beg, end;
-  bag_ranges(o.req_offsets[r], c, lane, beg, end);
-  long long my_id = 0;
-  if (c.pool == 0) my_id = first_valid(p, ids, c, beg, end);
-  for (int s = 0; s * bps < c.nb; ++s) {
-    const int bag = s * bps + sub;
-    const long long qb = __shfl_sync(0xffffffffu, beg, bag & 31);
-    const long long qe = __shfl_sync(0xffffffffu, end, bag & 31);
-    const long long one = __shfl_sync(0xffffffffu, my_id, bag & 31);
-    if (bag >= c.nb) continue;
-    long long row = 0;
-    int all = 1;
-    if (c.pool == 0) {
-      if (one <= 0 || !owns(p, c.t, one, row)) continue;
-    } else {
-      all = 0;
-      int mine = 0;
-      for (long long q = qb; q < qe; ++q) {
-        const long long id = hash_id(ids[q], c.hmode, c.buckets);
-        if (id > 0 && id < c.rows) {
-          ++all;
-          long long rr;
-          mine += owns(p, c.t, id, rr) ? 1 : 0;
+__global__ void __launch_bounds__(kThreads) emb_owner_fwd_kernel(const EmbPlan p, const OwnerArgs o) {
+  constexpr int G = 16;
+  const int sub = threadIdx.x % G;
+  const long long gid = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) / G;
+  const long long ngroups = static_cast<long long>(gridDim.x) * kThreads / G;
+  const float* slab = p.slabs[p.rank];
+  for (int r = 0; r < p.world; ++r) {
+    const long long n = min(static_cast<long long>(o.counts[r][2 * p.rank]), o.cap_bundles);
+    const RouteBundle* seg = o.bundles[r] + p.rank * o.cap_bundles;
+    const int* rl = o.rows[r] + p.rank * o.cap_rows;
+    float* acc = o.acc[r];
+    for (long long e0 = gid; e0 < n; e0 += 2 * ngroups) {
+      RouteBundle bd[2];
+      bool ok[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const long long e = e0 + u * ngroups;
+        ok[u] = e < n;
+        if (ok[u]) bd[u] = seg[e];
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        if (!ok[u]) continue;
+        const int f = bd[u].f_count & 0xffff, k = bd[u].f_count >> 16;
+        const int t = __ldg(p.f_table + f);
+        const int dim = __ldg(p.t_dim + t);
+        const float* tbl = slab + __ldg(p.t_base_all + p.rank * p.num_tables + t);
+        float sum[NV][4];
+#pragma unroll
+        for (int i = 0; i < NV; ++i) sum[i][0] = sum[i][1] = sum[i][2] = sum[i][3] = 0.f;
+        for (int q = 0; q < k; q += 4) {
+          int rows[4];
+#pragma unroll
+          for (int v = 0; v < 4; ++v) rows[v] = q + v < k ? (k == 1 ? bd[u].row : rl[bd[u].row + q + v]) : -1;
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            if (rows[v] < 0) continue;
+            const float* src = tbl + static_cast<long long>(rows[v]) * dim;
+#pragma unroll
+            for (int i = 0; i < NV; ++i) {
+              const int col = (sub + i * G) * 4;
+              if (col < dim) {
+                const float4 x = *reinterpret_cast<const float4*>(src + col);
+                sum[i][0] += x.x; sum[i][1] += x.y; sum[i][2] += x.z; sum[i][3] += x.w;
+              }
+            }
+          }
+        }
+        const long long row_off = __ldg(p.f_out_base + f) + static_cast<long long>(bd[u].bag) * __ldg(p.f_out_ld + f);
+        const int width = __ldg(p.f_width + f);
+        const float sc = bd[u].scale;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          const int col = (sub + i * G) * 4;
+          if (col >= width) continue;
+          const float v[4] = {sum[i][0] * sc, sum[i][1] * sc, sum[i][2] * sc, sum[i][3] * sc};
+          const long long a = row_off + feat_col(p, f, col);
+          if (col + 4 <= width && feat_vec4(p, f, col, a)) {
+            red_add4<true>(acc + a, v);
+          } else {
+            for (int j = 0; j < 4 && col + j < width; ++j) atomicAdd(acc + row_off + feat_col(p, f, col + j), v[j]);
+          }
         }
       }
-      if (mine == 0) continue;
     }
-    const float scale = c.pool == 1 ? 1.f / static_cast<float>(all) : 1.f;
-    const long long brow = c.first + bag;
-    float g[NV][4];
+  }
+}
+
+// Owner side, backward: per bundle read the requester's bf16 gradient slice of the
+// bag once and add it into every row of the bundle (local), marking them touched.
+template <int NV>
+__global__ void __launch_bounds__(kThreads) emb_owner_bwd_kernel(const EmbPlan p, const OwnerArgs o) {
+  constexpr int G = 16;
+  const int sub = threadIdx.x % G;
+  const long long gid = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) / G;
+  const long long ngroups = static_cast<long long>(gridDim.x) * kThreads / G;
+  float* gslab = p.grad_slabs[p.rank];
+  unsigned char* flags = p.flags[p.rank];
+  for (int r = 0; r < p.world; ++r) {
+    const long long n = min(static_cast<long long>(o.counts[r][2 * p.rank]), o.cap_bundles);
+    const RouteBundle* seg = o.bundles[r] + p.rank * o.cap_bundles;
+    const int* rl = o.rows[r] + p.rank * o.cap_rows;
+    const __nv_bfloat16* grad = reinterpret_cast<const __nv_bfloat16*>(o.grad[r]);
+    for (long long e0 = gid; e0 < n; e0 += 2 * ngroups) {
+      RouteBundle bd[2];
+      bool ok[2];
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int col = sl * 4 + i * stride_cols;
-      if (col < c.dim) {
-        load4(c, gbase, brow * c.out_ld, col, min(4, c.dim - col), g[i]);
-        for (int j = 0; j < 4; ++j) g[i][j] *= scale;
+      for (int u = 0; u < 2; ++u) {
+        const long long e = e0 + u * ngroups;
+        ok[u] = e < n;
+        if (ok[u]) bd[u] = seg[e];
       }
-    }
-    auto push = [&](long long lrow) {
-      float* dst = c.gtbl + lrow * c.dim;
+      float g[2][NV][4];
 #pragma unroll
-      for (int i = 0; i < NV; ++i) {
-        const int col = sl * 4 + i * stride_cols;
-        if (col < c.dim) red_add4<false>(dst + col, g[i]);
+      for (int u = 0; u < 2; ++u) {
+        if (!ok[u]) continue;
+        const int f = bd[u].f_count & 0xffff;
+        const long long row_off = __ldg(p.f_out_base + f) + static_cast<long long>(bd[u].bag) * __ldg(p.f_out_ld + f);
+        const int width = __ldg(p.f_width + f);
+        const float sc = bd[u].scale;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          const int col = (sub + i * G) * 4;
+          g[u][i][0] = g[u][i][1] = g[u][i][2] = g[u][i][3] = 0.f;
+          if (col >= width) continue;
+          const long long a = row_off + feat_col(p, f, col);
+          if (col + 4 <= width && feat_vec4(p, f, col, a)) {
+            const uint2 w = *reinterpret_cast<const uint2*>(grad + a);
+            const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.x));
+            const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.y));
+            g[u][i][0] = lo.x * sc; g[u][i][1] = lo.y * sc; g[u][i][2] = hi.x * sc; g[u][i][3] = hi.y * sc;
+          } else {
+            for (int j = 0; j < 4 && col + j < width; ++j)
+              g[u][i][j] = __bfloat162float(grad[row_off + feat_col(p, f, col + j)]) * sc;
+          }
+        }
       }
-      if (sl == 0) *reinterpret_cast<volatile unsigned char*>(c.ftbl + lrow) = 1;
-    };
-    if (c.pool == 0) {
-      push(row);
-      continue;
-    }
-    for (long long q = qb; q < qe; ++q) {
-      const long long id = hash_id(ids[q], c.hmode, c.buckets);
-      long long rr;
-      if (id > 0 && id < c.rows && owns(p, c.t, id, rr)) push(rr);
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        if (!ok[u]) continue;
+        const int f = bd[u].f_count & 0xffff, k = bd[u].f_count >> 16;
+        const int t = __ldg(p.f_table + f);
+        const int dim = __ldg(p.t_dim + t);
+        float* tbl = gslab + __ldg(p.t_base_all + p.rank * p.num_tables + t);
+        unsigned char* ftbl = flags + __ldg(p.t_row_base_all + p.rank * p.num_tables + t);
+        for (int q = 0; q < k; ++q) {
+          const long long row = k == 1 ? bd[u].row : rl[bd[u].row + q];
+#pragma unroll
+          for (int i = 0; i < NV; ++i) {
+            const int col = (sub + i * G) * 4;
+            if (col < dim) red_add4<false>(tbl + row * dim + col, g[u][i]);
+          }
+          if (sub == 0) *reinterpret_cast<volatile unsigned char*>(ftbl + row) = 1;
+        }
+      }
     }
   }
 }
@@ -982,29 +1059,52 @@ cudaError_t emb_pool_backward(const EmbPlan& plan, const void* grad_out, long lo
   return cudaGetLastError();
 }
 
-cudaError_t emb_owner_forward(const EmbPlan& plan, const OwnerArgs& o, long long total_chunks, cudaStream_t stream) {
-  if (total_chunks <= 0) return cudaSuccess;
+int owner_grid() {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms * 8;
+}
+
+bool owner_args_ok(const EmbPlan& plan, const OwnerArgs& o) {
+  if (o.cap_bundles <= 0 || o.cap_rows <= 0) return false;
   for (int r = 0; r < plan.world; ++r)
-    if (o.req_ids[r] == nullptr || o.req_offsets[r] == nullptr || o.req_acc[r] == nullptr) return cudaErrorInvalidValue;
-  const int grid = blocks_for(total_chunks * plan.world);
-  if (plan.max_vec <= 1) emb_owner_fwd_kernel<1><<<grid, kThreads, 0, stream>>>(plan, o, total_chunks);
-  else if (plan.max_vec <= 2) emb_owner_fwd_kernel<2><<<grid, kThreads, 0, stream>>>(plan, o, total_chunks);
-  else if (plan.max_vec <= 4) emb_owner_fwd_kernel<4><<<grid, kThreads, 0, stream>>>(plan, o, total_chunks);
-  else emb_owner_fwd_kernel<8><<<grid, kThreads, 0, stream>>>(plan, o, total_chunks);
+    if (o.bundles[r] == nullptr || o.rows[r] == nullptr || o.counts[r] == nullptr) return false;
+  return true;
+}
+
+cudaError_t emb_route(const EmbPlan& plan, const OwnerArgs& o, long long total_chunks, cudaStream_t stream) {
+  if (total_chunks <= 0) return cudaSuccess;
+  if (!owner_args_ok(plan, o) || o.acc[plan.rank] == nullptr) return cudaErrorInvalidValue;
+  emb_route_kernel<<<blocks_for(total_chunks), kThreads, 0, stream>>>(plan, o, total_chunks);
   return cudaGetLastError();
 }
 
-cudaError_t emb_owner_backward(const EmbPlan& plan, const OwnerArgs& o, long long total_chunks,
-                               cudaStream_t stream) {
-  if (total_chunks <= 0) return cudaSuccess;
+cudaError_t emb_owner_forward(const EmbPlan& plan, const OwnerArgs& o, cudaStream_t stream) {
+  if (!owner_args_ok(plan, o)) return cudaErrorInvalidValue;
   for (int r = 0; r < plan.world; ++r)
-    if (o.req_ids[r] == nullptr || o.req_offsets[r] == nullptr || o.req_grad[r] == nullptr) return cudaErrorInvalidValue;
+    if (o.acc[r] == nullptr) return cudaErrorInvalidValue;
+  const int grid = owner_grid();
+  // NV float4 per lane of a 16-lane group: table dims <= 64 * NV
+  if (plan.max_dim <= 64) emb_owner_fwd_kernel<1><<<grid, kThreads, 0, stream>>>(plan, o);
+  else if (plan.max_dim <= 128) emb_owner_fwd_kernel<2><<<grid, kThreads, 0, stream>>>(plan, o);
+  else if (plan.max_dim <= 256) emb_owner_fwd_kernel<4><<<grid, kThreads, 0, stream>>>(plan, o);
+  else if (plan.max_dim <= 512) emb_owner_fwd_kernel<8><<<grid, kThreads, 0, stream>>>(plan, o);
+  else return cudaErrorInvalidValue;
+  return cudaGetLastError();
+}
+
+cudaError_t emb_owner_backward(const EmbPlan& plan, const OwnerArgs& o, cudaStream_t stream) {
+  if (!owner_args_ok(plan, o)) return cudaErrorInvalidValue;
+  for (int r = 0; r < plan.world; ++r)
+    if (o.grad[r] == nullptr) return cudaErrorInvalidValue;
   if (plan.grad_slabs[plan.rank] == nullptr || plan.flags[plan.rank] == nullptr) return cudaErrorInvalidValue;
-  const int grid = blocks_for(total_chunks * plan.world);
-  if (plan.max_vec <= 1) emb_owner_bwd_kernel<1><<<grid, kThreads, 0, stream>>>(plan, o, total_chunks);
-  else if (plan.max_vec <= 2) emb_owner_bwd_kernel<2><<<grid, kThreads, 0, stream>>>(plan, o, total_chunks);
-  else if (plan.max_vec <= 4) emb_owner_bwd_kernel<4><<<grid, kThreads, 0, stream>>>(plan, o, total_chunks);
-  else emb_owner_bwd_kernel<8><<<grid, kThreads, 0, stream>>>(plan, o, total_chunks);
+  const int grid = owner_grid();
+  if (plan.max_dim <= 64) emb_owner_bwd_kernel<1><<<grid, kThreads, 0, stream>>>(plan, o);
+  else if (plan.max_dim <= 128) emb_owner_bwd_kernel<2><<<grid, kThreads, 0, stream>>>(plan, o);
+  else if (plan.max_dim <= 256) emb_owner_bwd_kernel<4><<<grid, kThreads, 0, stream>>>(plan, o);
+  else if (plan.max_dim <= 512) emb_owner_bwd_kernel<8><<<grid, kThreads, 0, stream>>>(plan, o);
+  else return cudaErrorInvalidValue;
   return cudaGetLastError();
 }
 

@@ -39,6 +39,9 @@ struct EmbPlan {
   const int* f_slice = nullptr;        // per-feature column map: phys = (c/slice)*stride + c%slice (0 = identity)
   const int* f_slice_stride = nullptr;
   const int* f_dense_col = nullptr;    // dense features: first column in `dense`
+  const int* f_phys0 = nullptr;        // physical column of the feature's first column
+  const int* f_split = nullptr;        // columns before the next slice boundary (-1: several boundaries)
+  int max_dim = 0;                     // widest table of the plan (owner-push kernels)
   // per table
   const long long* t_base = nullptr;
   const long long* t_row_base = nullptr;
@@ -70,31 +73,43 @@ cudaError_t emb_pool_forward(const EmbPlan& plan, long long total_chunks, cudaSt
 cudaError_t emb_pool_backward(const EmbPlan& plan, const void* grad_out, long long total_chunks,
                               cudaStream_t stream);
 
-// ---- multi-rank lookup, owner side ("owner-push") -------------------------
+// ---- multi-rank lookup ("owner-push") ----------------------------------------
 // With several ranks the random row traffic stays in each owner's local HBM and
-// only pooled vectors cross NVLink:
-//   forward : every rank stages its batch ids/offsets in peer-visible memory;
-//             owner o walks the bags of EVERY requester r, sums the rows it owns
-//             (local gathers), scales by the bag's global valid-id count (mean)
-//             and adds the partial into r's fp32 accumulator [rows, out_ld] with
-//             vector reductions over NVLink (a plain store when it is the single
-//             contributor: the first valid id of a single-valued feature);
-//             dense inputs are copied by their own rank. r then converts its
-//             accumulator to the bf16 output.
+// only contiguous staging buffers are read or written over NVLink:
+//   route   : each rank walks its own bags once. For every (bag, owner) pair
+//             with contributing ids it appends a bundle {bag, feature, count,
+//             scale} to the owner's segment and the ids' owner-local rows to the
+//             owner's row list (a single row is kept in the bundle itself).
+//             Dense inputs go straight into the rank's own accumulator.
+//   forward : owner o reads its bundles from every rank r, gathers and sums the
+//             bundle's rows from its local shard, scales, and adds ONE pooled
+//             vector per bundle into r's fp32 accumulator [rows, out_ld] (vector
+//             reductions over NVLink); r then converts it to the bf16 output.
 //   backward: r stages d(out) in peer-visible memory; owner o reads the bf16
-//             gradient slice of each bag it holds ids of (NVLink) and adds it
-//             into its LOCAL grad slab rows, marking them touched.
-// Remote accesses are contiguous 128-256 byte runs of small staging buffers.
+//             gradient slice of each bundle's bag once and adds it into the
+//             bundle's LOCAL grad rows, marking them touched.
+// An owner's work is the ids it owns, whatever the number of ranks; NVLink
+// carries one vector per (bag, owner) in each direction.
+struct RouteBundle {
+  int bag;        // sample row within the batch
+  int f_count;    // plan feature | (number of rows << 16)
+  int row;        // the row itself when count == 1, else the first index in the row list
+  float scale;    // 1 (sum / single id) or 1 / valid ids of the bag (mean)
+};
 struct OwnerArgs {
-  const long long* req_ids[kMaxWorld] = {};      // each requester's staged ids
-  const long long* req_offsets[kMaxWorld] = {};  // ... and CSR offsets
-  float* req_acc[kMaxWorld] = {};                // forward: each requester's fp32 accumulator
-  const void* req_grad[kMaxWorld] = {};          // backward: each requester's bf16 d(out)
-  const float* dense = nullptr;                  // this rank's dense inputs (forward)
+  RouteBundle* bundles[kMaxWorld] = {};  // rank r's bundles: [world][cap_bundles]
+  int* rows[kMaxWorld] = {};             // rank r's row lists: [world][cap_rows]
+  int* counts[kMaxWorld] = {};           // rank r's [world][2]: bundles, rows per owner
+  long long cap_bundles = 0, cap_rows = 0;
+  float* acc[kMaxWorld] = {};            // forward: each rank's fp32 accumulator
+  const void* grad[kMaxWorld] = {};      // backward: each rank's bf16 d(out)
+  const float* dense = nullptr;          // this rank's dense inputs (route pass)
   long long dense_ld = 0;
 };
-cudaError_t emb_owner_forward(const EmbPlan& plan, const OwnerArgs& o, long long total_chunks, cudaStream_t stream);
-cudaError_t emb_owner_backward(const EmbPlan& plan, const OwnerArgs& o, long long total_chunks, cudaStream_t stream);
+// route pass of this rank (its counts and accumulator zeroed beforehand)
+cudaError_t emb_route(const EmbPlan& plan, const OwnerArgs& o, long long total_chunks, cudaStream_t stream);
+cudaError_t emb_owner_forward(const EmbPlan& plan, const OwnerArgs& o, cudaStream_t stream);
+cudaError_t emb_owner_backward(const EmbPlan& plan, const OwnerArgs& o, cudaStream_t stream);
 // out[i] = bf16(acc[i]) for i < n (n a multiple of 8, 16-byte aligned buffers)
 cudaError_t emb_acc_to_bf16(const float* acc, void* out, long long n, cudaStream_t stream);
 

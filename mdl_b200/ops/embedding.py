@@ -148,7 +148,8 @@ class EmbeddingStore:
         self.touched_list = (torch.empty(max(self.total_rows, 1), dtype=torch.int32, device=dev)
                              if dev.type == "cuda" else None)
         self.touched_count = torch.zeros(1, dtype=torch.int32, device=dev) if dev.type == "cuda" else None
-        self._exchanges: dict = {}  # multi-rank lookup staging per (plan, rows)
+        self._exchanges: dict = {}  # multi-rank lookup staging per plan
+        self.max_dim = max((t.dim for t in self.layouts), default=4)
         # CPU path: dense gradient accumulation per table (sparse rows tracked by a mask)
         self._cpu_touched = torch.zeros(self.total_rows, dtype=torch.bool) if dev.type != "cuda" else None
 
@@ -335,6 +336,14 @@ class LookupPlan:
             return (self.out_width + self.slice_k - 1) // self.slice_k * self.slice_stride
         return self.out_width
 
+    def _split(self, f: "LookupFeature") -> int:
+        """Columns of ``f`` before its next slice boundary (-1: it crosses more than one)."""
+
+        if not self.slice_k:
+            return 1 << 30
+        split = self.slice_k - f.out_col % self.slice_k
+        return split if f.width <= split + self.slice_k else -1
+
     def src_of(self, i: int) -> int:
         s = self.features[i].src
         return i if s < 0 else s
@@ -389,6 +398,8 @@ class LookupPlan:
             tm["t_base"], tm["t_row_base"], tm["t_dim"], tm["t_mode"], tm["t_cyc"], tm["t_owner"], tm["t_rows"],
             tm["t_base_all"], tm["t_row_base_all"],
             i64([self.src_of(i) * rows for i in range(F)]),
+            i32([self.phys_col(f.out_col) for f in self.features]),
+            i32([self._split(f) for f in self.features]),
         ]
         max_vec = max([(f.width + 4 * ln - 1) // (4 * ln) for f, ln in zip(self.features, lanes_list)] or [1])
         result = (meta, chunk_prefix[-1], max_vec)
@@ -541,38 +552,39 @@ def backward_reference(store: EmbeddingStore, plan: LookupPlan, ids: torch.Tenso
 class _Exchange:
     """Peer-visible staging of one lookup plan's traffic across ranks (CUDA, world > 1).
 
-    Holds each rank's batch ids/offsets, the fp32 accumulator the owners add pooled
-    partials into, and the bf16 output gradient the owners read back. Capacities
-    are agreed on once (collectively) from the first batch: twice the largest id
-    count of any rank.
+    Holds this rank's routed bundles (per owner: at most one per bag and
+    feature), the owner-local row lists of multi-row bundles, their counts, the
+    fp32 accumulator owners add pooled rows into, and the bf16 output gradient
+    owners read back. Sizes are agreed on once (collectively) from the first
+    batch; row lists hold twice the largest id count of any rank.
     """
 
-    def __init__(self, store: "EmbeddingStore", plan: "LookupPlan", rows: int, n_ids: int, n_offsets: int) -> None:
+    def __init__(self, store: "EmbeddingStore", plan: "LookupPlan", rows: int, n_ids: int) -> None:
         from ..parallel.symm import SymmetricBuffers
 
         dev = store.device
-        t = torch.tensor([n_ids, n_offsets, rows, -rows], dtype=torch.int64, device=dev)
+        t = torch.tensor([n_ids, rows], dtype=torch.int64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=store.process_group)
-        if int(t[2]) != -int(t[3]):
-            raise ValueError("every rank must look up the same number of rows per step")
-        self.rows = rows
-        self.cap_ids = 2 * int(t[0]) + 4096
-        self.cap_offsets = int(t[1])
-        self.n_out = (rows * plan.out_ld + 7) // 8 * 8
-        self.symm = SymmetricBuffers({"ids": (self.cap_ids, torch.int64), "offsets": (self.cap_offsets, torch.int64),
+        if max((lay.local_rows for lay in store.layouts), default=0) >= 2 ** 31:
+            raise ValueError("owner-push lookup keeps 32-bit local row indices")
+        if len(plan.features) >= 2 ** 16:
+            raise ValueError("owner-push lookup packs the feature index in 16 bits")
+        W = store.world
+        self.rows_cap = int(t[1])
+        self.cap_bundles = max(1, len(plan.features) * self.rows_cap)
+        self.cap_rows = 2 * int(t[0]) + 4096
+        self.n_out = (self.rows_cap * plan.out_ld + 7) // 8 * 8
+        self.symm = SymmetricBuffers({"bundles": (W * self.cap_bundles * 4, torch.int32),
+                                      "rows": (W * self.cap_rows, torch.int32), "counts": (16, torch.int32),
                                       "acc": (self.n_out, torch.float32), "grad": (self.n_out, torch.bfloat16)},
                                      device=dev, process_group=store.process_group)
-        self.ids = self.symm.local("ids")
-        self.offsets = self.symm.local("offsets")
+        self.counts = self.symm.local("counts")
         self.acc = self.symm.local("acc")
         self.grad = self.symm.local("grad")
 
-    def stage(self, ids: torch.Tensor, offsets: torch.Tensor) -> None:
-        if ids.numel() > self.cap_ids or offsets.numel() > self.cap_offsets:
-            raise RuntimeError(f"batch holds {ids.numel()} ids / {offsets.numel()} offsets; the lookup exchange "
-                               f"was sized for {self.cap_ids} / {self.cap_offsets}")
-        self.ids[:ids.numel()].copy_(ids)
-        self.offsets[:offsets.numel()].copy_(offsets)
+    def ptrs(self) -> tuple[list[int], list[int], list[int], int, int]:
+        s = self.symm
+        return s.peer_ptrs("bundles"), s.peer_ptrs("rows"), s.peer_ptrs("counts"), self.cap_bundles, self.cap_rows
 
 
 class _FusedLookup(torch.autograd.Function):
@@ -610,29 +622,33 @@ class _FusedLookup(torch.autograd.Function):
         return (None,) * 7
 
 
-def _exchange(store: EmbeddingStore, plan: LookupPlan, ids: torch.Tensor, offsets: torch.Tensor,
-              rows: int) -> _Exchange:
-    key = (id(plan), rows)
-    ex = store._exchanges.get(key)
+def _exchange(store: EmbeddingStore, plan: LookupPlan, ids: torch.Tensor, rows: int) -> _Exchange:
+    ex = store._exchanges.get(id(plan))
     if ex is None:
-        ex = _Exchange(store, plan, rows, ids.numel(), offsets.numel())
-        store._exchanges[key] = ex
+        ex = _Exchange(store, plan, rows, ids.numel())
+        store._exchanges[id(plan)] = ex
+    if rows > ex.rows_cap or ids.numel() > ex.cap_rows:
+        raise RuntimeError(f"batch of {rows} rows / {ids.numel()} ids exceeds the lookup exchange sized for "
+                           f"{ex.rows_cap} rows / {ex.cap_rows} ids")
     return ex
 
 
 def _owner_forward(store, plan, ids, offsets, dense, rows):
-    """Multi-rank lookup: owners push pooled partials into each requester's accumulator."""
+    """Multi-rank lookup: route (bag, owner) bundles, owners push pooled vectors back."""
 
     C = ext()
-    ex = _exchange(store, plan, ids, offsets, rows)
-    ex.stage(ids, offsets)
-    ex.acc.zero_()
+    ex = _exchange(store, plan, ids, rows)
     meta, chunks, max_vec = plan.device_meta(store, rows)
-    ex.symm.barrier()  # every rank's ids staged, every accumulator zeroed
-    C.emb_owner_forward(meta, store.peer_ptrs("slab"), store.rank, ex.ids, ex.offsets, ex.symm.peer_ptrs("ids"),
-                        ex.symm.peer_ptrs("offsets"), ex.symm.peer_ptrs("acc"), dense, plan.dense_width, chunks,
-                        error_word(ids.device), max_vec)
-    ex.symm.barrier()  # every owner's partials have landed
+    err = error_word(ids.device)
+    ex.counts.zero_()
+    ex.acc[:rows * plan.out_ld].zero_()
+    bundles, row_lists, counts, capb, capr = ex.ptrs()
+    C.emb_route(meta, store.peer_ptrs("slab"), store.rank, ids, offsets, bundles, row_lists, counts, capb, capr,
+                ex.acc, dense, plan.dense_width, chunks, err, max_vec)
+    ex.symm.barrier()  # every rank's bundles routed, every accumulator zeroed
+    C.emb_owner_forward(meta, store.peer_ptrs("slab"), store.rank, ids, offsets, bundles, row_lists, counts, capb,
+                        capr, ex.symm.peer_ptrs("acc"), store.max_dim, err)
+    ex.symm.barrier()  # every owner's vectors have landed
     out = torch.empty(rows, plan.out_ld, dtype=torch.bfloat16, device=ids.device)
     C.emb_acc_to_bf16(ex.acc, out)
     return out
@@ -642,15 +658,16 @@ def _owner_backward(store, plan, ids, offsets, grad_out, rows):
     """Multi-rank gradient: owners pull each requester's d(out) slices into their own grad rows."""
 
     C = ext()
-    ex = _exchange(store, plan, ids, offsets, rows)
+    ex = _exchange(store, plan, ids, rows)
+    meta, chunks, max_vec = plan.device_meta(store, rows)
     g = grad_out if grad_out.dtype == torch.bfloat16 else grad_out.to(torch.bfloat16)
     ex.grad[:g.numel()].copy_(g.reshape(-1))
-    meta, chunks, max_vec = plan.device_meta(store, rows)
+    bundles, row_lists, counts, capb, capr = ex.ptrs()
     ex.symm.barrier()  # every requester's gradient staged
     C.emb_owner_backward(meta, store.peer_ptrs("slab"), store.peer_ptrs("grad"), store.peer_ptrs("flags"), store.rank,
-                         ex.ids, ex.offsets, ex.symm.peer_ptrs("ids"), ex.symm.peer_ptrs("offsets"),
-                         ex.symm.peer_ptrs("grad"), chunks, error_word(ids.device), max_vec)
-    ex.symm.barrier()  # staged ids / gradients may be overwritten after this point
+                         ids, offsets, bundles, row_lists, counts, capb, capr, ex.symm.peer_ptrs("grad"),
+                         store.max_dim, error_word(ids.device))
+    ex.symm.barrier()  # bundles / staged gradients may be overwritten after this point
 
 
 def fused_lookup(store: EmbeddingStore, plan: LookupPlan, ids: torch.Tensor, offsets: torch.Tensor,
