@@ -481,18 +481,23 @@ mdl::OptimArgs optim_args(const at::Tensor& param, const at::Tensor& grad, const
 
 void adam(const at::Tensor& param, const at::Tensor& grad, const at::Tensor& m, const at::Tensor& v,
           const std::optional<at::Tensor>& shadow, double lr, double beta1, double beta2, double eps, double wd,
-          double bc1, double bc2, double grad_scale, const std::optional<at::Tensor>& clip) {
+          double bc1, double bc2, double grad_scale, const std::optional<at::Tensor>& clip, bool zero_grad,
+          int64_t max_blocks) {
   c10::cuda::CUDAGuard guard(param.device());
   auto a = optim_args(param, grad, m, v, shadow, lr, beta1, beta2, eps, wd, bc1, bc2, 0.0, grad_scale, clip);
+  a.zero_grad = zero_grad;
+  a.max_blocks = static_cast<int>(max_blocks);
   check(mdl::adam_step(a, stream_of(param)), "adam_step");
   g_launches += 1;
 }
 
 void rmsprop(const at::Tensor& param, const at::Tensor& grad, const at::Tensor& sq,
              const std::optional<at::Tensor>& shadow, double lr, double alpha, double eps, double wd,
-             double grad_scale, const std::optional<at::Tensor>& clip) {
+             double grad_scale, const std::optional<at::Tensor>& clip, bool zero_grad, int64_t max_blocks) {
   c10::cuda::CUDAGuard guard(param.device());
   auto a = optim_args(param, grad, sq, std::nullopt, shadow, lr, 0.0, 0.0, eps, wd, 1.0, 1.0, alpha, grad_scale, clip);
+  a.zero_grad = zero_grad;
+  a.max_blocks = static_cast<int>(max_blocks);
   check(mdl::rmsprop_step(a, stream_of(param)), "rmsprop_step");
   g_launches += 1;
 }
@@ -572,7 +577,7 @@ void dense_sync(const std::vector<int64_t>& grads, const std::vector<int64_t>& p
                 int64_t begin, int64_t end, int64_t fp32_from, int64_t rank, int64_t optimizer, double lr,
                 double beta1, double beta2, double eps, double wd, double bc1, double bc2, double alpha,
                 double grad_scale, const std::optional<at::Tensor>& clip, const std::optional<at::Tensor>& sqnorm_out,
-                int64_t phase) {
+                int64_t phase, int64_t max_blocks) {
   c10::cuda::CUDAGuard guard(state1.device());
   mdl::DenseSyncArgs a;
   a.world = static_cast<int>(grads.size());
@@ -601,6 +606,7 @@ void dense_sync(const std::vector<int64_t>& grads, const std::vector<int64_t>& p
   a.clip = optr<const float>(clip);
   a.sqnorm_out = optr<float>(sqnorm_out);
   a.phase = static_cast<int>(phase);
+  a.max_blocks = static_cast<int>(max_blocks);
   check(mdl::dense_sync_update(a, stream_of(state1)), "dense_sync_update");
   g_launches += 1;
 }

@@ -188,6 +188,7 @@ cudaError_t dense_sync_update(const DenseSyncArgs& a, cudaStream_t stream) {
   const long long per_rank_vec = (a.end - a.begin) / a.world / 4 + 1;
   long long blocks = (per_rank_vec + 255) / 256;
   if (blocks > sms * 4) blocks = sms * 4;
+  if (a.max_blocks > 0 && blocks > a.max_blocks) blocks = a.max_blocks;
   if (blocks < 1) blocks = 1;
   dense_sync_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(a, p);
   return cudaGetLastError();

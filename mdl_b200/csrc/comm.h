@@ -49,6 +49,7 @@ struct DenseSyncArgs {
   const float* clip = nullptr;
   float* sqnorm_out = nullptr;     // phase "norm": sum of squares of the reduced slice
   int phase = 0;                   // 0: fused update, 1: only reduce -> local grad slice + sqnorm
+  int max_blocks = 0;              // grid cap (0: fill the GPU) when running beside other kernels
 };
 cudaError_t dense_sync_update(const DenseSyncArgs& a, cudaStream_t stream);
 

@@ -138,38 +138,64 @@ __global__ void __launch_bounds__(256) head_bce_kernel(const HeadArgs p) {
 
 __device__ __forceinline__ float clip_of(const float* clip) { return clip ? *clip : 1.f; }
 
-__global__ void adam_kernel(const OptimArgs a) {
+// One optimizer element update; ALGO 0 = Adam, 1 = RMSprop.
+template <int ALGO>
+__device__ __forceinline__ float opt_elem(const OptimArgs& a, float g, float p, float& s1, float& s2, float step_size,
+                                          float bc2_sqrt) {
+  if (a.weight_decay != 0.f) g += a.weight_decay * p;
+  if (ALGO == 0) {
+    s1 = a.beta1 * s1 + (1.f - a.beta1) * g;
+    s2 = a.beta2 * s2 + (1.f - a.beta2) * g * g;
+    return p - step_size * s1 / (sqrtf(s2) / bc2_sqrt + a.eps);
+  }
+  s1 = a.alpha * s1 + (1.f - a.alpha) * g * g;
+  return p - a.lr * g / (sqrtf(s1) + a.eps);
+}
+
+// Vectorised (4 elements per thread and iteration) when n and every buffer allow it.
+template <int ALGO>
+__global__ void __launch_bounds__(256) optim_kernel(const OptimArgs a) {
   const float gs = a.grad_scale * clip_of(a.clip);
   const float step_size = a.lr / a.bias_correction1;
   const float bc2_sqrt = sqrtf(a.bias_correction2);
   __nv_bfloat16* sh = reinterpret_cast<__nv_bfloat16*>(a.shadow);
-  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < a.n;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    float g = a.grad[i] * gs;
-    float p = a.param[i];
-    if (a.weight_decay != 0.f) g += a.weight_decay * p;
-    const float m = a.beta1 * a.state1[i] + (1.f - a.beta1) * g;
-    const float v = a.beta2 * a.state2[i] + (1.f - a.beta2) * g * g;
-    a.state1[i] = m;
-    a.state2[i] = v;
-    p -= step_size * m / (sqrtf(v) / bc2_sqrt + a.eps);
-    a.param[i] = p;
-    if (sh) sh[i] = __float2bfloat16_rn(p);
+  float* grad = const_cast<float*>(a.grad);
+  const long long n4 = a.n / 4;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long v = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; v < n4; v += stride) {
+    const long long i = v * 4;
+    const float4 g4 = *reinterpret_cast<const float4*>(grad + i);
+    const float4 p4 = *reinterpret_cast<const float4*>(a.param + i);
+    const float4 s14 = *reinterpret_cast<const float4*>(a.state1 + i);
+    float4 s24 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (ALGO == 0) s24 = *reinterpret_cast<const float4*>(a.state2 + i);
+    float g[4] = {g4.x * gs, g4.y * gs, g4.z * gs, g4.w * gs};
+    float p[4] = {p4.x, p4.y, p4.z, p4.w};
+    float s1[4] = {s14.x, s14.y, s14.z, s14.w};
+    float s2[4] = {s24.x, s24.y, s24.z, s24.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) p[k] = opt_elem<ALGO>(a, g[k], p[k], s1[k], s2[k], step_size, bc2_sqrt);
+    *reinterpret_cast<float4*>(a.param + i) = make_float4(p[0], p[1], p[2], p[3]);
+    *reinterpret_cast<float4*>(a.state1 + i) = make_float4(s1[0], s1[1], s1[2], s1[3]);
+    if (ALGO == 0) *reinterpret_cast<float4*>(a.state2 + i) = make_float4(s2[0], s2[1], s2[2], s2[3]);
+    if (a.zero_grad) *reinterpret_cast<float4*>(grad + i) = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (sh) {
+      const __nv_bfloat162 h0 = __floats2bfloat162_rn(p[0], p[1]);
+      const __nv_bfloat162 h1 = __floats2bfloat162_rn(p[2], p[3]);
+      uint2 u;
+      u.x = *reinterpret_cast<const uint32_t*>(&h0);
+      u.y = *reinterpret_cast<const uint32_t*>(&h1);
+      *reinterpret_cast<uint2*>(sh + i) = u;
+    }
   }
-}
-
-__global__ void rmsprop_kernel(const OptimArgs a) {
-  const float gs = a.grad_scale * clip_of(a.clip);
-  __nv_bfloat16* sh = reinterpret_cast<__nv_bfloat16*>(a.shadow);
-  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < a.n;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    float g = a.grad[i] * gs;
-    float p = a.param[i];
-    if (a.weight_decay != 0.f) g += a.weight_decay * p;
-    const float v = a.alpha * a.state1[i] + (1.f - a.alpha) * g * g;
-    a.state1[i] = v;
-    p -= a.lr * g / (sqrtf(v) + a.eps);
+  // tail
+  for (long long i = n4 * 4 + static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < a.n; i += stride) {
+    float s1 = a.state1[i], s2 = ALGO == 0 ? a.state2[i] : 0.f;
+    const float p = opt_elem<ALGO>(a, grad[i] * gs, a.param[i], s1, s2, step_size, bc2_sqrt);
     a.param[i] = p;
+    a.state1[i] = s1;
+    if (ALGO == 0) a.state2[i] = s2;
+    if (a.zero_grad) grad[i] = 0.f;
     if (sh) sh[i] = __float2bfloat16_rn(p);
   }
 }
@@ -238,15 +264,30 @@ cudaError_t head_bce(const HeadArgs& a, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+namespace {
+bool optim_aligned(const OptimArgs& a) {
+  auto al = [](const void* p, uintptr_t m) { return (reinterpret_cast<uintptr_t>(p) & m) == 0; };
+  return al(a.param, 15) && al(a.grad, 15) && al(a.state1, 15) && (a.state2 == nullptr || al(a.state2, 15)) &&
+         (a.shadow == nullptr || al(a.shadow, 7));
+}
+int optim_grid(const OptimArgs& a) {
+  int g = grid_for((a.n + 3) / 4);
+  if (a.max_blocks > 0 && g > a.max_blocks) g = a.max_blocks;
+  return g;
+}
+}  // namespace
+
 cudaError_t adam_step(const OptimArgs& a, cudaStream_t stream) {
   if (a.n == 0) return cudaSuccess;
-  adam_kernel<<<grid_for(a.n), 256, 0, stream>>>(a);
+  if (!optim_aligned(a)) return cudaErrorInvalidValue;
+  optim_kernel<0><<<optim_grid(a), 256, 0, stream>>>(a);
   return cudaGetLastError();
 }
 
 cudaError_t rmsprop_step(const OptimArgs& a, cudaStream_t stream) {
   if (a.n == 0) return cudaSuccess;
-  rmsprop_kernel<<<grid_for(a.n), 256, 0, stream>>>(a);
+  if (!optim_aligned(a)) return cudaErrorInvalidValue;
+  optim_kernel<1><<<optim_grid(a), 256, 0, stream>>>(a);
   return cudaGetLastError();
 }
 

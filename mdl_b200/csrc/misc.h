@@ -53,6 +53,8 @@ struct OptimArgs {
   float alpha = 0.99f;      // RMSprop smoothing
   float grad_scale = 1.f;
   const float* clip = nullptr;
+  bool zero_grad = false;   // write 0 to the gradient after reading it (fused zero_grad)
+  int max_blocks = 0;       // cap on the grid (0: enough to fill the GPU) for runs beside other kernels
 };
 cudaError_t adam_step(const OptimArgs& a, cudaStream_t stream);
 cudaError_t rmsprop_step(const OptimArgs& a, cudaStream_t stream);

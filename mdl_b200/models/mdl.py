@@ -213,6 +213,16 @@ class MDLRankMixerModel(nn.Module):
     def gemm_param_names(self) -> set[str]:
         return {n for n, p in self.named_parameters() if getattr(p, "_mdl_gemm", False)}
 
+    def dense_buckets(self) -> list[list[str]]:
+        """Parameter groups in the order their gradients become final in the backward
+        (heads, last block, ..., first block; the rest finishes last)."""
+
+        names = [n for n, _ in self.named_parameters()]
+        groups = [[n for n in names if n.startswith("heads.")]]
+        for i in reversed(range(self.L)):
+            groups.append([n for n in names if n.startswith(f"blocks.{i}.")])
+        return groups
+
     @property
     def store(self):
         return self.encoder.store
@@ -307,7 +317,11 @@ class MDLRankMixerModel(nn.Module):
                 gamma, beta = params.chunk(2, dim=-1)
                 x = (1.0 + gamma).unsqueeze(1) * x + beta.unsqueeze(1)
         w_fused = self._scene_weights(mask, include_global=self.use_global) if (s is not None) else None
-        for blk in self.blocks:
+        from ..ops.dense import grad_ready
+
+        hooks = getattr(self, "dense_hooks", None) if cuda else None
+        for i, blk in enumerate(self.blocks):
+            x = grad_ready(x, hooks, self.L - i)  # block i's gradients are final once d(x_in) is
             x = self._feature_block(blk, x, cuda)
             s_hat = None
             if s is not None:
@@ -345,4 +359,5 @@ class MDLRankMixerModel(nn.Module):
         if task_scale is None:
             task_scale = torch.full((self.ntask,), 1.0 / max(1, B), device=x.device)
         labels = batch.labels
+        pred = grad_ready(pred, hooks, 0)
         return self.heads(pred, labels, batch.label_mask, task_scale)

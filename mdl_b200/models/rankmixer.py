@@ -112,6 +112,14 @@ class RankMixerModel(nn.Module):
             names |= {f"blocks.{i}.w_in", f"blocks.{i}.w_out"}
         return names
 
+    def dense_buckets(self) -> list[list[str]]:
+        """Parameter groups in the order their gradients become final in the backward."""
+
+        heads = ["head_w1", "head_b1", "head_w2", "head_b2"]
+        blocks = [[f"blocks.{i}.{n}" for n in ("w_in", "b_in", "w_out", "b_out", "ln1_weight", "ln1_bias",
+                                               "ln2_weight", "ln2_bias")] for i in reversed(range(self.L))]
+        return [heads, *blocks, ["tok_weight", "tok_bias"]]
+
     @property
     def store(self):
         return self.encoder.store
@@ -133,10 +141,16 @@ class RankMixerModel(nn.Module):
 
         if self.ffn_relu:
             raise NotImplementedError("fused RankMixer block implements the gelu FFN (reference default)")
+        from ..ops.dense import grad_ready
+
+        hooks = getattr(self, "dense_hooks", None)  # bucket k final -> its update starts (see dense_buckets)
+        x0 = grad_ready(x0, hooks, self.L + 1)
         x = PerTokenLinearFn.apply(x0, self.tok_weight, self.tok_bias, self.T, self.K, self.Kpad)
-        for blk in self.blocks:
+        for i, blk in enumerate(self.blocks):
+            x = grad_ready(x, hooks, self.L - i)
             x = RankMixerBlockFn.apply(x, blk.ln1_weight, blk.ln1_bias, blk.w_in, blk.b_in, blk.w_out, blk.b_out,
                                        blk.ln2_weight, blk.ln2_bias, self.ln_eps)
+        x = grad_ready(x, hooks, 0)
         if task_scale is None:
             task_scale = torch.full((self.ntask,), 1.0 / max(1, batch.rows), device=x.device)
         loss, logits = HeadsBCEFn.apply(x, self.head_w1, self.head_b1, self.head_w2, self.head_b2, batch.labels,

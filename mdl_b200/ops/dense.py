@@ -10,9 +10,20 @@ master and shadow buffers are symmetric (IPC-mapped by every peer) and the
 update is the fused NVLink reduce-scatter / optimizer / all-gather kernel
 (``csrc/comm.cu``), bucket by bucket.
 
-Layout: parameters whose consumers read the bf16 shadow (GEMM weights) come
-first, parameters read as fp32 (norm scales, biases, head vectors) after
-``fp32_from``; each parameter starts on a 32-element boundary.
+Layout: parameters are grouped into *buckets* in the order their gradients
+become final in the backward (a model lists them: heads, last block, ...,
+first block, tokenizer; everything else forms a last bucket). Within a bucket
+the parameters whose consumers read the bf16 shadow (GEMM weights) come first
+and the ones read as fp32 (norm scales, biases, head vectors) after the
+bucket's ``fp32_from``; every parameter starts on a 32-element boundary and
+every bucket on a multiple of 32 x world.
+
+Overlap: between ``begin_step`` and ``step`` the model calls
+``bucket_ready(k)`` as soon as bucket k's gradients are final (a ``GradReady``
+node in the autograd graph); the bucket's update (with one rank: the
+optimizer, fused with zeroing the gradient; with several: barrier + fused
+reduce-scatter / optimizer / all-gather) is then issued on a side stream, so it
+runs under the rest of the backward.
 
 Reference counterpart: DDP (``src/train.py:5276-5328``) + RMSprop
 (``src/train.py:4826-4893``) + dense clipping (``src/train.py:5745-5775``).
@@ -21,6 +32,7 @@ Reference counterpart: DDP (``src/train.py:5276-5328``) + RMSprop
 from __future__ import annotations
 
 import math
+import os
 from typing import Iterable
 
 import torch
@@ -40,7 +52,8 @@ class DenseParams:
     def __init__(self, named_params: Iterable[tuple[str, nn.Parameter]], *, device: torch.device,
                  bf16_names: set[str] | None = None, world: int = 1, rank: int = 0, process_group=None,
                  optimizer: str = "adam", lr: float = 1e-3, betas=(0.9, 0.999), eps: float = 1e-8,
-                 weight_decay: float = 0.0, rmsprop_alpha: float = 0.99, comm: str = "fused") -> None:
+                 weight_decay: float = 0.0, rmsprop_alpha: float = 0.99, comm: str = "fused",
+                 buckets: list[list[str]] | None = None, overlap: bool = False) -> None:
         self.device = torch.device(device)
         self.world, self.rank, self.group = world, rank, process_group
         self.optimizer, self.lr, self.betas, self.eps = optimizer, lr, betas, eps
@@ -48,26 +61,44 @@ class DenseParams:
         self.comm = comm
         named = list(named_params)
         bf16_names = set(bf16_names or ()) | {n for n, p in named if getattr(p, "_mdl_gemm", False)}
-        ordered = [x for x in named if x[0] in bf16_names] + [x for x in named if x[0] not in bf16_names]
-        self.names = [n for n, _ in ordered]
-        self.params = {n: p for n, p in ordered}
+        by_name = {n: p for n, p in named}
+        groups: list[list[str]] = []
+        seen: set[str] = set()
+        for names in buckets or []:
+            grp = [n for n in names if n in by_name and n not in seen]
+            seen.update(grp)
+            if grp:
+                groups.append(grp)
+        rest = [n for n, _ in named if n not in seen]
+        if rest:
+            groups.append(rest)
+        self.names: list[str] = []
+        self.params: dict[str, nn.Parameter] = {}
         self.offsets: dict[str, int] = {}
+        self.buckets: list[tuple[int, int, int]] = []  # (begin, end, fp32_from)
+        self.bucket_of: dict[str, int] = {}
         off = 0
-        self.fp32_from = 0
-        for i, (name, p) in enumerate(ordered):
-            if name not in bf16_names and self.fp32_from == 0 and i > 0 and ordered[i - 1][0] in bf16_names:
-                self.fp32_from = off
-            self.offsets[name] = off
-            off += _round(p.numel())
-        if not any(n in bf16_names for n in self.names):
-            self.fp32_from = 0
-        elif all(n in bf16_names for n in self.names):
-            self.fp32_from = off
-        self.total = _round(max(off, ALIGN), ALIGN * max(1, world))
-        self.fp32_from = min(self.fp32_from, self.total)
+        for k, grp in enumerate(groups):
+            begin = off
+            ordered = [n for n in grp if n in bf16_names] + [n for n in grp if n not in bf16_names]
+            fp32_from = None
+            for n in ordered:
+                if n not in bf16_names and fp32_from is None:
+                    fp32_from = off
+                self.names.append(n)
+                self.params[n] = by_name[n]
+                self.offsets[n] = off
+                self.bucket_of[n] = k
+                off += _round(by_name[n].numel())
+            off = _round(max(off, begin + ALIGN), ALIGN * max(1, world))
+            self.buckets.append((begin, off, off if fp32_from is None else fp32_from))
+        self.total = max(off, ALIGN * max(1, world))
+        # single-range view used by callers of the whole buffer
+        self.fp32_from = self.buckets[0][2] if len(self.buckets) == 1 else 0
         self._alloc()
         with torch.no_grad():
-            for name, p in ordered:
+            for name in self.names:
+                p = self.params[name]
                 o = self.offsets[name]
                 self.master[o:o + p.numel()].copy_(p.detach().flatten().to(self.device, torch.float32))
                 p.data = self.master[o:o + p.numel()].view_as(p)
@@ -80,6 +111,15 @@ class DenseParams:
         if self.shadow is not None:
             self.refresh_shadow()
         self.step_count = 0
+        # Measured on B200 (RankMixer workload, 1 and 2 GPUs): a side-stream update competes with the
+        # backward's kernels for SMs and memory bandwidth and the step gets slower (1 GPU 4.62 -> 5.53
+        # ms, 2 GPUs 5.08 -> 5.64 ms), so it is opt-in (MDL_B200_DENSE_OVERLAP=1 or overlap=True).
+        env = os.environ.get("MDL_B200_DENSE_OVERLAP")
+        on = overlap if env is None else env != "0"
+        self.overlap = on and self.device.type == "cuda"
+        self._active = False
+        self._launched: list[bool] = [False] * len(self.buckets)
+        self._side = torch.cuda.Stream(device=self.device) if self.device.type == "cuda" else None
 
     def _alloc(self) -> None:
         dev = self.device
@@ -119,19 +159,87 @@ class DenseParams:
             self.refresh_shadow()
 
     # ------------------------------------------------------------------ step
+    def _hyper(self, lr: float) -> dict:
+        b1, b2 = self.betas
+        t = self.step_count
+        return dict(lr=lr, b1=b1, b2=b2, bc1=1.0 - b1 ** t, bc2=1.0 - b2 ** t, opt=0 if self.optimizer == "adam" else 1)
+
+    def begin_step(self, lr: float | None = None, clip_norm: float | None = None) -> bool:
+        """Open an optimizer step whose bucket updates may start during the backward.
+
+        Returns whether overlapping is on (CUDA and no global clipping: the clip factor
+        needs every gradient before any update)."""
+
+        self._active = False
+        if not self.overlap or clip_norm is not None:
+            return False
+        self.step_count += 1
+        self._h = self._hyper(self.lr if lr is None else lr)
+        self._launched = [False] * len(self.buckets)
+        self._active = True
+        return True
+
+    def bucket_ready(self, k: int) -> None:
+        """Bucket k's gradients are final: issue its update on the side stream."""
+
+        if not self._active or self._launched[k]:
+            return
+        self._launched[k] = True
+        cur = torch.cuda.current_stream(self.device)
+        self._side.wait_stream(cur)
+        with torch.cuda.stream(self._side):
+            self._update_bucket(k, self._h, max_blocks=self._side_blocks())
+
+    def _side_blocks(self) -> int:
+        # a few SMs' worth of 256-thread blocks: enough in flight for NVLink, little HBM pressure
+        env = os.environ.get("MDL_B200_SIDE_BLOCKS")
+        return int(env) if env else 0
+
+    def _update_bucket(self, k: int, h: dict, max_blocks: int = 0) -> None:
+        C = ext()
+        begin, end, fp32_from = self.buckets[k]
+        scale = 1.0 / self.world
+        if self._symm is not None:
+            sym = self._symm
+            sym.barrier()  # every rank's gradients of this bucket are final
+            C.dense_sync(sym.peer_ptrs("grad"), sym.peer_ptrs("master"), sym.peer_ptrs("shadow"), self.state1,
+                         self.state2, begin, end, fp32_from, self.rank, h["opt"], h["lr"], h["b1"], h["b2"], self.eps,
+                         self.weight_decay, h["bc1"], h["bc2"], self.rmsprop_alpha, scale, None, None, 0, max_blocks)
+            return
+        sl = slice(begin, end)
+        shadow = None if self.shadow is None else self.shadow[sl]
+        if h["opt"] == 0:
+            C.adam(self.master[sl], self.grad[sl], self.state1[sl], self.state2[sl], shadow, h["lr"], h["b1"],
+                   h["b2"], self.eps, self.weight_decay, h["bc1"], h["bc2"], scale, None, True, max_blocks)
+        else:
+            C.rmsprop(self.master[sl], self.grad[sl], self.state1[sl], shadow, h["lr"], self.rmsprop_alpha, self.eps,
+                      self.weight_decay, scale, None, True, max_blocks)
+
     @torch.no_grad()
     def step(self, lr: float | None = None, clip_norm: float | None = None) -> torch.Tensor | None:
-        """Average gradients over ranks and apply the optimizer. Returns the grad norm if clipping."""
+        """Average gradients over ranks and apply the optimizer. Returns the grad norm if clipping.
 
+        After ``begin_step`` this only issues the buckets the backward did not report
+        and joins the side stream."""
+
+        if self._active:
+            self._active = False
+            cur = torch.cuda.current_stream(self.device)
+            self._side.wait_stream(cur)
+            with torch.cuda.stream(self._side):
+                for k, done in enumerate(self._launched):
+                    if not done:
+                        self._update_bucket(k, self._h, max_blocks=0)
+                if self._symm is not None:
+                    self._symm.barrier()  # no rank reads this rank's gradients any more
+                    self.grad.zero_()
+            cur.wait_stream(self._side)
+            return None
         lr = self.lr if lr is None else lr
         self.step_count += 1
-        t = self.step_count
-        b1, b2 = self.betas
-        bc1 = 1.0 - b1 ** t
-        bc2 = 1.0 - b2 ** t
-        opt = 0 if self.optimizer == "adam" else 1
+        h = self._hyper(lr)
         if self.device.type != "cuda":
-            return self._cpu_step(lr, clip_norm, bc1, bc2)
+            return self._cpu_step(lr, clip_norm, h["bc1"], h["bc2"])
         C = ext()
         scale = 1.0 / self.world
         norm = None
@@ -141,17 +249,20 @@ class DenseParams:
             clip = None
             if clip_norm is not None:
                 self._sq.zero_()
-                C.dense_sync(sym.peer_ptrs("grad"), sym.peer_ptrs("master"), sym.peer_ptrs("shadow"), self.state1,
-                             self.state2, 0, self.total, self.fp32_from, self.rank, opt, lr, b1, b2, self.eps,
-                             self.weight_decay, bc1, bc2, self.rmsprop_alpha, scale, None, self._sq, 1)
+                for begin, end, fp32_from in self.buckets:
+                    C.dense_sync(sym.peer_ptrs("grad"), sym.peer_ptrs("master"), sym.peer_ptrs("shadow"), self.state1,
+                                 self.state2, begin, end, fp32_from, self.rank, h["opt"], lr, h["b1"], h["b2"],
+                                 self.eps, self.weight_decay, h["bc1"], h["bc2"], self.rmsprop_alpha, scale, None,
+                                 self._sq, 1, 0)
                 sym.allreduce_small(self._sq)
                 C.clip_factor(self._sq, float(clip_norm), self._clip)
                 norm = self._sq.sqrt()
                 clip = self._clip
-            C.dense_sync(sym.peer_ptrs("grad"), sym.peer_ptrs("master"), sym.peer_ptrs("shadow"), self.state1,
-                         self.state2, 0, self.total, self.fp32_from, self.rank, opt, lr, b1, b2, self.eps,
-                         self.weight_decay, bc1, bc2, self.rmsprop_alpha, scale, clip, None,
-                         2 if clip_norm is not None else 0)
+            for begin, end, fp32_from in self.buckets:
+                C.dense_sync(sym.peer_ptrs("grad"), sym.peer_ptrs("master"), sym.peer_ptrs("shadow"), self.state1,
+                             self.state2, begin, end, fp32_from, self.rank, h["opt"], lr, h["b1"], h["b2"], self.eps,
+                             self.weight_decay, h["bc1"], h["bc2"], self.rmsprop_alpha, scale, clip, None,
+                             2 if clip_norm is not None else 0, 0)
             sym.barrier()
             self.grad.zero_()
             return norm
@@ -164,13 +275,12 @@ class DenseParams:
             C.clip_factor(self._sq, float(clip_norm), self._clip)
             clip = self._clip
             norm = self._sq.sqrt()
-        if opt == 0:
-            C.adam(self.master, self.grad, self.state1, self.state2, self.shadow, lr, b1, b2, self.eps,
-                   self.weight_decay, bc1, bc2, scale, clip)
+        if h["opt"] == 0:
+            C.adam(self.master, self.grad, self.state1, self.state2, self.shadow, lr, h["b1"], h["b2"], self.eps,
+                   self.weight_decay, h["bc1"], h["bc2"], scale, clip, True, 0)
         else:
             C.rmsprop(self.master, self.grad, self.state1, self.shadow, lr, self.rmsprop_alpha, self.eps,
-                      self.weight_decay, scale, clip)
-        self.grad.zero_()
+                      self.weight_decay, scale, clip, True, 0)
         return norm
 
     def _cpu_step(self, lr, clip_norm, bc1, bc2):
@@ -236,3 +346,27 @@ class DenseParams:
                     self.state2.copy_(state["state2"].to(self.state2.device))
             self.step_count = int(state.get("step", 0))
         self.refresh_shadow()
+
+
+class GradReadyFn(torch.autograd.Function):
+    """Identity whose backward tells ``DenseParams`` that bucket ``k`` is final.
+
+    Placed on the input of a module: autograd reaches this node's backward only
+    after the module's backward (which wrote its parameter gradients) has run.
+    """
+
+    @staticmethod
+    def forward(ctx, x, dense, k):
+        ctx.dense, ctx.k = dense, k
+        return x.view_as(x)
+
+    @staticmethod
+    def backward(ctx, g):
+        ctx.dense.bucket_ready(ctx.k)
+        return g, None, None
+
+
+def grad_ready(x: torch.Tensor, dense: "DenseParams | None", k: int) -> torch.Tensor:
+    if dense is None or not x.requires_grad:
+        return x
+    return GradReadyFn.apply(x, dense, k)

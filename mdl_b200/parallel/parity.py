@@ -164,12 +164,18 @@ def _run_parity_body(rank: int, world: int, device_type: str, out_path: str, opt
             ref_tables = gather_tables(ref_model.store, "weight")
 
             def rel(a, b):
-                n = min(a.numel(), b.numel())  # flat buffers differ only in tail padding (multiple of 32 * W)
+                n = min(a.numel(), b.numel())
                 a, b = a.flatten()[:n], b.flatten()[:n]
                 return float((a - b).abs().max() / (b.abs().max() + 1e-12))
 
-            n_used = max(o + p.numel() for o, p in zip(ref.dense.offsets.values(), ref.dense.params.values()))
-            master, ref_master = master[:n_used], ref_master[:n_used]
+            def by_name(dense, flat):
+                # flat layouts differ with the world size (bucket padding): compare parameter by parameter
+                return torch.cat([flat[dense.offsets[n]:dense.offsets[n] + dense.params[n].numel()]
+                                  for n in sorted(dense.offsets)])
+
+            grads_dense = by_name(trainer.dense, grads_dense.float().cpu())
+            ref_grads = by_name(ref.dense, ref_grads)
+            master, ref_master = by_name(trainer.dense, master), by_name(ref.dense, ref_master)
 
             result = {
                 "loss": float(loss) / world, "ref_loss": float(rout["loss"].detach()),

@@ -60,12 +60,15 @@ class Trainer:
         self.device = torch.device(device)
         self.rank, self.world, self.group = rank, world, process_group
         t = config.training
+        buckets = model.dense_buckets() if hasattr(model, "dense_buckets") else None
         self.dense = DenseParams(
             model.named_parameters(), device=self.device, bf16_names=model.gemm_param_names(), world=world,
             rank=rank, process_group=process_group, optimizer=t.dense_optimizer, lr=t.lr_dense,
             betas=(t.adam_beta1, t.adam_beta2), eps=t.adam_eps if t.dense_optimizer == "adam" else 1e-8,
-            weight_decay=t.weight_decay, rmsprop_alpha=t.rmsprop_alpha, comm=t.comm)
+            weight_decay=t.weight_decay, rmsprop_alpha=t.rmsprop_alpha, comm=t.comm, buckets=buckets)
         self.dense.broadcast_from_rank0()
+        # the model reports finished gradient buckets during the backward (overlapped updates)
+        model.dense_hooks = self.dense
         self.store = model.store
         names = list(config.task_names)
         self.task_weights = torch.tensor([float(t.task_loss_weights.get(n, 1.0)) for n in names],
@@ -96,22 +99,35 @@ class Trainer:
         out["loss"].backward()
         return out
 
+    def _lrs(self, step: int) -> tuple[float, float]:
+        t = self.config.training
+        mult = lr_multiplier(self.config, step)
+        lr_sparse = t.lr_sparse if t.lr_sparse is not None else t.lr_dense
+        return t.lr_dense * mult, lr_sparse * mult
+
     def optimizer_step(self) -> tuple[torch.Tensor | None, torch.Tensor | None]:
         self.step_index += 1
         t = self.config.training
-        mult = lr_multiplier(self.config, self.step_index)
-        lr_sparse = t.lr_sparse if t.lr_sparse is not None else t.lr_dense
-        dn = self.dense.step(lr=t.lr_dense * mult, clip_norm=t.dense_clip_norm)
-        sn = self.store.step(lr=lr_sparse * mult, clip_norm=t.sparse_clip_norm)
+        lr_dense, lr_sparse = self._lrs(self.step_index)
+        dn = self.dense.step(lr=lr_dense, clip_norm=t.dense_clip_norm)
+        sn = self.store.step(lr=lr_sparse, clip_norm=t.sparse_clip_norm)
         return dn, sn
 
     def train_step(self, batch) -> StepResult:
-        """One micro-batch; runs the optimizers every ``gradient_accumulation_steps`` micro-batches."""
+        """One micro-batch; runs the optimizers every ``gradient_accumulation_steps`` micro-batches.
 
+        On the last micro-batch of a step the dense update is opened before the
+        backward, so buckets whose gradients are final update while the rest of
+        the backward runs."""
+
+        t = self.config.training
+        final = (self.micro_index + 1) % t.gradient_accumulation_steps == 0
+        if final:
+            self.dense.begin_step(lr=self._lrs(self.step_index + 1)[0], clip_norm=t.dense_clip_norm)
         out = self.forward_backward(batch)
         self.micro_index += 1
         dn = sn = None
-        if self.micro_index % self.config.training.gradient_accumulation_steps == 0:
+        if final:
             dn, sn = self.optimizer_step()
         return StepResult(loss=out["loss"].detach(), logits=out.get("logits"), dense_grad_norm=dn,
                           sparse_grad_norm=sn)
