@@ -308,31 +308,42 @@ class DenseParams:
         return norm
 
     @torch.no_grad()
-    def gather_master(self) -> torch.Tensor:
-        """The full fp32 master vector on every rank.
+    def gather(self, buf: torch.Tensor) -> torch.Tensor:
+        """``buf`` (master or optimizer state) complete on every rank.
 
-        With the fused NVLink update each rank keeps the authoritative fp32 copy of
-        its own slice only (peers receive the bf16 shadow, plus fp32 for the
-        non-GEMM parameters); this all-gathers the owned slices.
+        With the fused NVLink update rank r keeps the authoritative values of its
+        slice ``[begin + r * c, begin + (r + 1) * c)`` of every bucket only (peers
+        receive the bf16 shadow, plus fp32 for the non-GEMM parameters); this
+        all-gathers the owned slices bucket by bucket.
         """
 
         if self._symm is None or self.world == 1:
-            return self.master
-        chunk = self.total // self.world
-        mine = self.master[self.rank * chunk:(self.rank + 1) * chunk].contiguous()
-        full = torch.empty_like(self.master)
-        dist.all_gather_into_tensor(full, mine, group=self.group)
+            return buf
+        full = torch.empty_like(buf)
+        for begin, end, _ in self.buckets:
+            c = (end - begin) // self.world
+            mine = buf[begin + self.rank * c:begin + (self.rank + 1) * c].contiguous()
+            dist.all_gather_into_tensor(full[begin:end], mine, group=self.group)
         return full
 
+    def gather_master(self) -> torch.Tensor:
+        """The full fp32 master vector on every rank (see ``gather``)."""
+
+        return self.gather(self.master)
+
     def state_dict(self) -> dict:
-        return {
-            "params": {n: self.master[self.offsets[n]:self.offsets[n] + p.numel()].view_as(p).detach().cpu().clone()
-                       for n, p in self.params.items()},
-            "state1": self.state1.detach().cpu().clone(),
-            "state2": None if self.state2 is None else self.state2.detach().cpu().clone(),
-            "step": self.step_count,
-            "names": list(self.names),
-        }
+        """Parameters by name and optimizer state by name (collective when the update is sharded)."""
+
+        master = self.gather(self.master).detach().cpu()
+        s1 = self.gather(self.state1).detach().cpu()
+        s2 = None if self.state2 is None else self.gather(self.state2).detach().cpu()
+
+        def by_name(buf):
+            return {n: buf[self.offsets[n]:self.offsets[n] + p.numel()].view_as(p).clone()
+                    for n, p in self.params.items()}
+
+        return {"params": by_name(master), "state1": by_name(s1), "state2": None if s2 is None else by_name(s2),
+                "step": self.step_count, "optimizer": self.optimizer}
 
     def load_state_dict(self, state: dict) -> None:
         with torch.no_grad():
@@ -340,11 +351,16 @@ class DenseParams:
                 if n in self.params:
                     o = self.offsets[n]
                     self.master[o:o + v.numel()].copy_(v.flatten().to(self.master.device))
-            if state.get("names") == self.names:
-                self.state1.copy_(state["state1"].to(self.state1.device))
-                if self.state2 is not None and state.get("state2") is not None:
-                    self.state2.copy_(state["state2"].to(self.state2.device))
-            self.step_count = int(state.get("step", 0))
+            for key, buf in (("state1", self.state1), ("state2", self.state2)):
+                saved = state.get(key)
+                if buf is None or not isinstance(saved, dict):
+                    continue
+                for n, v in saved.items():
+                    if n in self.params:
+                        o = self.offsets[n]
+                        buf[o:o + v.numel()].copy_(v.flatten().to(buf.device))
+            if "step" in state:
+                self.step_count = int(state["step"])
         self.refresh_shadow()
 
 
