@@ -1,0 +1,491 @@
+"""Flat Parquet input pipeline: discovery, rank sharding, encodings, tensorization, prefetch.
+
+Counterparts in the reference: input discovery and schema checks
+(``src/dataloader.py:2326-2460``), the Parquet scanner with row-group LPT
+sharding, column pruning and threaded prefetch (``:2809``, ``:3232-4045``),
+tensorization into one batch per step (``:9200-9600``), categorical encodings
+(``src/features.py:150-365``), the pinned host pool and coalesced H2D
+(``src/train.py:2923-3108``, ``src/dataloader.py:11586-11790``) and the device
+prefetch iterator on a side stream (``src/train.py:4547-4713``).
+
+One sample per Parquet row (``data.train.format: flat_parquet``). A categorical
+feature's column holds a scalar or a list (a bag); a dense feature's column a
+scalar or a fixed-length list. Batches come out as ``PackedBatch`` in the CSR
+order of a lookup plan's batch layout (``FeatureEncoder.batch_plan``), with all
+int64 leaves in one pinned buffer and all fp32 leaves in another.
+"""
+
+from __future__ import annotations
+
+import glob
+import os
+import queue
+import threading
+from dataclasses import dataclass
+from hashlib import sha256
+from typing import Any, Iterator, Sequence
+
+import numpy as np
+import torch
+
+from .batch import PackedBatch
+
+
+def _pa():
+    import pyarrow as pa
+    import pyarrow.parquet as pq
+
+    return pa, pq
+
+
+# ------------------------------------------------------------------ discovery
+def discover_parquet_inputs(inputs: Sequence[str]) -> list[str]:
+    """Expand globs and directories (recursively) into a sorted list of Parquet files."""
+
+    out: list[str] = []
+    for item in inputs:
+        if any(ch in item for ch in "*?["):
+            out.extend(p for p in glob.glob(item, recursive=True) if os.path.isfile(p))
+        elif os.path.isdir(item):
+            for root, _dirs, files in os.walk(item):
+                out.extend(os.path.join(root, f) for f in files if f.endswith(".parquet"))
+        elif os.path.isfile(item):
+            out.append(item)
+        else:
+            raise FileNotFoundError(f"no Parquet input at {item!r}")
+    return sorted(dict.fromkeys(out))
+
+
+def validate_matching_schemas(paths: Sequence[str], required: Sequence[str]) -> None:
+    """Every file has every required column, with one type per column across files."""
+
+    _, pq = _pa()
+    seen: dict[str, Any] = {}
+    for p in paths:
+        schema = pq.read_schema(p)
+        names = set(schema.names)
+        missing = [c for c in required if c not in names]
+        if missing:
+            raise ValueError(f"{p}: missing columns {missing}")
+        for c in required:
+            t = schema.field(c).type
+            if c in seen and seen[c] != t:
+                raise ValueError(f"column {c!r} has type {seen[c]} in one file and {t} in {p}")
+            seen[c] = t
+
+
+@dataclass(frozen=True)
+class RowGroupRef:
+    path: str
+    index: int
+    rows: int
+
+
+def plan_row_groups(paths: Sequence[str], rank: int, world: int, unit: str = "row_group") -> list[RowGroupRef]:
+    """Deterministic shard of the input across ranks: longest-processing-time over rows
+    (largest units first, ties to the lowest rank), in file order within a rank."""
+
+    _, pq = _pa()
+    units: list[tuple[int, int, RowGroupRef]] = []
+    order = 0
+    for p in paths:
+        meta = pq.ParquetFile(p).metadata
+        if unit == "file":
+            units.append((meta.num_rows, order, RowGroupRef(p, -1, meta.num_rows)))
+            order += 1
+            continue
+        for g in range(meta.num_row_groups):
+            units.append((meta.row_group(g).num_rows, order, RowGroupRef(p, g, meta.row_group(g).num_rows)))
+            order += 1
+    load = [0] * world
+    mine: list[tuple[int, RowGroupRef]] = []
+    for rows, o, ref in sorted(units, key=lambda u: (-u[0], u[1])):
+        r = min(range(world), key=lambda i: (load[i], i))
+        load[r] += rows
+        if r == rank:
+            mine.append((o, ref))
+    return [ref for _, ref in sorted(mine, key=lambda x: x[0])]
+
+
+# ------------------------------------------------------------------ encodings
+def stable_hash_bucket(value: Any, num_buckets: int, salt: str | None = None) -> int:
+    """``sha256("<salt>:<value>")`` low 8 bytes (little-endian) mod n, plus 1 (0 is padding)."""
+
+    prefix = "" if salt is None else f"{salt}:"
+    return int.from_bytes(sha256((prefix + str(value)).encode("utf-8")).digest()[:8], "little") % num_buckets + 1
+
+
+class CategoricalEncoder:
+    """Raw column values -> table ids (0 = padding / null / out of vocabulary)."""
+
+    def __init__(self, feature, vocab: dict[str, int] | None = None) -> None:
+        enc = feature.encoding
+        self.name = feature.name
+        self.type = enc.type if enc is not None else "identity"
+        self.enc = enc
+        self.vocab = vocab
+        if self.type in ("vocab", "shared_vocab") and vocab is None:
+            raise ValueError(f"feature {feature.name!r}: vocab encoding needs a fitted vocabulary")
+        if self.type == "pre_hashed":
+            n = int(enc.num_buckets or 0)
+            if n <= 0 or n & (n - 1):
+                raise ValueError(f"feature {feature.name!r}: pre_hashed needs a power-of-two num_buckets")
+
+    def encode(self, values: np.ndarray) -> np.ndarray:
+        """``values``: 1-D object/int array with None for nulls."""
+
+        n = len(values)
+        if n == 0:
+            return np.zeros(0, dtype=np.int64)
+        enc = self.enc
+        if self.type == "identity":
+            mask = np.array([v is not None for v in values]) if values.dtype == object else np.ones(n, bool)
+            out = np.zeros(n, dtype=np.int64)
+            out[mask] = values[mask].astype(np.int64)
+            max_id = int(enc.max_id) if enc is not None and enc.max_id else None
+            if max_id is not None:
+                bad = out > max_id
+                if bad.any():
+                    policy = enc.out_of_range
+                    if policy == "error":
+                        raise ValueError(f"feature {self.name!r}: ids above max_id {max_id}")
+                    out[bad] = max_id if policy == "clip" else 0
+            out[out < 0] = 0
+            return out
+        if self.type == "pre_hashed":
+            mask = np.array([v is not None for v in values]) if values.dtype == object else np.ones(n, bool)
+            nb = np.uint64(int(enc.num_buckets))
+            raw = np.zeros(n, dtype=np.int64)
+            raw[mask] = values[mask].astype(np.int64)
+            out = (raw.view(np.uint64) & (nb - np.uint64(1))).astype(np.int64) + 1
+            out[~mask] = 0
+            return out
+        # hash / vocab: map each distinct value once
+        keys = np.array(["" if v is None else str(v) for v in values], dtype=object)
+        nulls = np.array([v is None for v in values])
+        uniq, inv = np.unique(keys, return_inverse=True)
+        if self.type == "hash":
+            nbk, salt = int(enc.num_buckets), enc.salt
+            mapped = np.array([stable_hash_bucket(u, nbk, salt) for u in uniq], dtype=np.int64)
+        else:
+            mapped = np.array([self.vocab.get(u, 0) for u in uniq], dtype=np.int64)
+        out = mapped[inv]
+        out[nulls] = 0
+        return out
+
+
+def fit_vocabs(config, paths: Sequence[str], out_dir: str) -> dict[str, str]:
+    """Count values of every ``vocab``-encoded feature and write ``value, id, count`` Parquet
+    artifacts (ids by descending count then value, from 1; ``min_count`` / ``max_size``)."""
+
+    pa, pq = _pa()
+    from collections import Counter
+
+    feats = [f for f in config.features if f.kind == "categorical" and f.encoding is not None
+             and f.encoding.type == "vocab"]
+    counters = {f.name: Counter() for f in feats}
+    for p in paths:
+        cols = list(dict.fromkeys(f.source or f.name for f in feats))
+        table = pq.read_table(p, columns=cols)
+        for f in feats:
+            col = table.column(f.source or f.name).to_pylist()
+            for v in col:
+                if isinstance(v, list):
+                    counters[f.name].update(str(x) for x in v if x is not None)
+                elif v is not None:
+                    counters[f.name][str(v)] += 1
+    os.makedirs(out_dir, exist_ok=True)
+    written = {}
+    for f in feats:
+        min_count = f.encoding.min_count or 1
+        cands = sorted(((v, c) for v, c in counters[f.name].items() if c >= min_count), key=lambda x: (-x[1], x[0]))
+        if f.encoding.max_size is not None:
+            cands = cands[:f.encoding.max_size]
+        path = os.path.join(out_dir, f.encoding.artifact or f"{f.name}.vocab.parquet")
+        pq.write_table(pa.table({"value": [v for v, _ in cands], "id": list(range(1, len(cands) + 1)),
+                                 "count": [c for _, c in cands]}), path)
+        written[f.name] = path
+    return written
+
+
+def load_vocab_map(path: str) -> dict[str, int]:
+    _, pq = _pa()
+    t = pq.read_table(path)
+    return {str(v): int(i) for v, i in zip(t["value"].to_pylist(), t["id"].to_pylist())}
+
+
+# ------------------------------------------------------------------ tensorization
+class Tensorizer:
+    """Arrow table (one sample per row) -> ``PackedBatch`` for a batch layout."""
+
+    def __init__(self, config, batch_plan, *, split: str = "train", vocab_maps: dict[str, dict] | None = None):
+        self.config = config
+        self.plan = batch_plan
+        by_name = {f.name: f for f in config.features}
+        self.features = [by_name[lf.name] for lf in batch_plan.features]
+        vocab_maps = vocab_maps or {}
+        self.encoders = {}
+        for f in self.features:
+            if f.kind != "categorical":
+                continue
+            enc = f.encoding
+            share = enc.share_with if enc is not None and enc.type == "shared_vocab" else None
+            self.encoders[f.name] = CategoricalEncoder(f, vocab_maps.get(share or f.name))
+        sp = getattr(config.data, split) or config.data.train
+        self.labels = dict(sp.labels)
+        self.label_masks = dict(sp.label_masks)
+        self.tasks = list(config.task_names)
+        self.dense_width = batch_plan.dense_width
+        sc = config.scenarios
+        self.scene_source = sc.source
+        self.scene_index = {str(n): i for i, n in enumerate(sc.names)}
+        self.scene_encoding = sc.source_encoding
+
+    def columns(self) -> list[str]:
+        cols = [f.source or f.name for f in self.features]
+        cols += [self.labels.get(t, t) for t in self.tasks if self.labels.get(t, t)]
+        cols += list(self.label_masks.values())
+        if self.scene_source:
+            cols.append(self.scene_source)
+        return list(dict.fromkeys(cols))
+
+    def _bag(self, f, col) -> tuple[np.ndarray, np.ndarray]:
+        """(flat raw values, lengths) of one categorical column; scalars are bags of one."""
+
+        py = col.to_pylist()
+        rows = len(py)
+        lengths = np.zeros(rows, dtype=np.int64)
+        flat: list = []
+        cap = f.max_length
+        for i, v in enumerate(py):
+            if isinstance(v, list):
+                if cap is not None and len(v) > cap:
+                    v = v[-cap:] if f.truncation == "tail" else v[:cap]
+                flat.extend(v)
+                lengths[i] = len(v)
+            else:
+                flat.append(v)
+                lengths[i] = 1
+        return np.array(flat, dtype=object), lengths
+
+    def _dense(self, f, col) -> np.ndarray:
+        py = col.to_pylist()
+        dim = int(f.dimension)
+        out = np.zeros((len(py), dim + (1 if f.presence else 0)), dtype=np.float32)
+        for i, v in enumerate(py):
+            if v is None:
+                continue
+            vals = v if isinstance(v, list) else [v]
+            vals = [0.0 if x is None else float(x) for x in vals[:dim]]
+            out[i, :len(vals)] = vals
+            if f.presence:
+                out[i, dim] = 1.0
+        return out
+
+    def __call__(self, table, pin: bool = False) -> PackedBatch:
+        rows = table.num_rows
+        ids_parts, len_parts = [], []
+        dense = np.zeros((rows, self.dense_width), dtype=np.float32)
+        for lf, f in zip(self.plan.features, self.features):
+            col = table.column(f.source or f.name)
+            if f.kind == "dense":
+                d = self._dense(f, col)
+                dense[:, lf.dense_col:lf.dense_col + d.shape[1]] = d
+                len_parts.append(np.zeros(rows, dtype=np.int64))
+                continue
+            flat, lengths = self._bag(f, col)
+            ids_parts.append(self.encoders[f.name].encode(flat))
+            len_parts.append(lengths)
+        offsets = np.zeros(len(self.plan.features) * rows + 1, dtype=np.int64)
+        np.cumsum(np.concatenate(len_parts) if len_parts else np.zeros(0, np.int64), out=offsets[1:])
+        ids = np.concatenate(ids_parts) if ids_parts else np.zeros(0, dtype=np.int64)
+        labels = np.zeros((rows, len(self.tasks)), dtype=np.float32)
+        mask = np.ones((rows, len(self.tasks)), dtype=np.float32)
+        any_mask = False
+        for t, task in enumerate(self.tasks):
+            name = self.labels.get(task, task)
+            if name not in table.column_names:
+                mask[:, t] = 0.0
+                any_mask = True
+                continue
+            vals = table.column(name).to_pylist()
+            for i, v in enumerate(vals):
+                if v is None:
+                    mask[i, t] = 0.0
+                    any_mask = True
+                else:
+                    labels[i, t] = float(v)
+            mname = self.label_masks.get(task)
+            if mname and mname in table.column_names:
+                mv = np.array([0.0 if v is None else float(v) for v in table.column(mname).to_pylist()], np.float32)
+                mask[:, t] *= mv
+                any_mask = True
+        scen = np.zeros(rows, dtype=np.int64)
+        if self.scene_source and self.scene_source in table.column_names:
+            vals = table.column(self.scene_source).to_pylist()
+            if self.scene_encoding == "index":
+                scen = np.array([0 if v is None else int(v) for v in vals], dtype=np.int64)
+            else:
+                scen = np.array([self.scene_index.get(str(v), 0) for v in vals], dtype=np.int64)
+        return PackedBatch.pack(torch.from_numpy(ids), torch.from_numpy(offsets),
+                                torch.from_numpy(dense) if self.dense_width else None, torch.from_numpy(labels),
+                                torch.from_numpy(mask) if any_mask else None, torch.from_numpy(scen), rows, pin=pin)
+
+
+# ------------------------------------------------------------------ iteration
+class ParquetBatchIterator:
+    """This rank's batches: its row groups (``plan_row_groups``) read with column pruning,
+    optionally shuffled through a row buffer, cut into ``batch_size`` rows and tensorized,
+    ``prefetch`` batches ahead on a background thread. ``position`` counts the row groups
+    consumed (the data cursor of a checkpoint)."""
+
+    def __init__(self, paths: Sequence[str], tensorizer: Tensorizer, batch_size: int, *, rank: int = 0,
+                 world: int = 1, shard_unit: str = "row_group", shuffle_rows: int = 0, seed: int = 0,
+                 drop_last: bool = True, prefetch: int = 2, pin: bool = False, start_position: int = 0,
+                 loop: bool = False) -> None:
+        self.refs = plan_row_groups(paths, rank, world, shard_unit)
+        self.tz = tensorizer
+        self.batch_size = batch_size
+        self.shuffle_rows = shuffle_rows
+        self.rng = np.random.default_rng([seed, rank])
+        self.drop_last = drop_last
+        self.prefetch = max(1, prefetch)
+        self.pin = pin
+        self.position = start_position
+        self.loop = loop
+        self._q: queue.Queue = queue.Queue(maxsize=self.prefetch)
+        self._thread: threading.Thread | None = None
+        self._stop = threading.Event()
+
+    def _tables(self):
+        pa, pq = _pa()
+        cols = self.tz.columns()
+        while True:
+            while self.position < len(self.refs):
+                ref = self.refs[self.position]
+                f = pq.ParquetFile(ref.path)
+                present = [c for c in cols if c in f.schema_arrow.names]
+                t = f.read(columns=present) if ref.index < 0 else f.read_row_group(ref.index, columns=present)
+                self.position += 1
+                yield t
+            if not self.loop or not self.refs:
+                return
+            self.position = 0
+
+    def _batches(self):
+        pa, _ = _pa()
+        buf = None
+        for t in self._tables():
+            buf = t if buf is None else pa.concat_tables([buf, t])
+            need = max(self.batch_size, self.shuffle_rows)
+            while buf.num_rows >= need:
+                if self.shuffle_rows:
+                    idx = self.rng.permutation(buf.num_rows)
+                    buf = buf.take(pa.array(idx))
+                yield self.tz(buf.slice(0, self.batch_size), pin=self.pin)
+                buf = buf.slice(self.batch_size)
+        while buf is not None and buf.num_rows >= self.batch_size:
+            yield self.tz(buf.slice(0, self.batch_size), pin=self.pin)
+            buf = buf.slice(self.batch_size)
+        if buf is not None and buf.num_rows and not self.drop_last:
+            yield self.tz(buf, pin=self.pin)
+
+    def _worker(self):
+        try:
+            for b in self._batches():
+                while not self._stop.is_set():
+                    try:
+                        self._q.put(b, timeout=0.1)
+                        break
+                    except queue.Full:
+                        continue
+                if self._stop.is_set():
+                    return
+            self._q.put(StopIteration())
+        except BaseException as error:  # surfaced to the consumer
+            self._q.put(error)
+
+    def __iter__(self) -> Iterator[PackedBatch]:
+        self._stop.clear()
+        self._thread = threading.Thread(target=self._worker, daemon=True)
+        self._thread.start()
+        while True:
+            item = self._q.get()
+            if isinstance(item, StopIteration):
+                return
+            if isinstance(item, BaseException):
+                raise item
+            yield item
+
+    def close(self) -> None:
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=5)
+
+
+class DevicePrefetcher:
+    """Copies batch k+1 host->device on a side CUDA stream while step k runs; the consumer's
+    stream waits on an event and the tensors are recorded on it (no host sync)."""
+
+    def __init__(self, batches, device: torch.device) -> None:
+        self.it = iter(batches)
+        self.device = torch.device(device)
+        self.stream = torch.cuda.Stream(device=self.device)
+        self._next = None
+        self._preload()
+
+    def _preload(self) -> None:
+        try:
+            host = next(self.it)
+        except StopIteration:
+            self._next = None
+            return
+        with torch.cuda.stream(self.stream):
+            dev = host.to(self.device, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(self.stream)
+        self._next = (dev, ev, host)
+
+    def __iter__(self):
+        return self
+
+    def __next__(self) -> PackedBatch:
+        if self._next is None:
+            raise StopIteration
+        dev, ev, _host = self._next
+        cur = torch.cuda.current_stream(self.device)
+        cur.wait_event(ev)
+        for t in dev._flat:
+            t.record_stream(cur)
+        self._preload()
+        return dev
+
+
+def write_synthetic_parquet(path: str, batch: PackedBatch, batch_plan, config, rows_per_group: int = 1024) -> None:
+    """Write a ``PackedBatch`` as a flat Parquet file (test data / mock inputs): one column per
+    feature (scalar ids for single-valued, lists for bags, lists for dense), one per label,
+    and the scene column when the config has one."""
+
+    pa, pq = _pa()
+    rows = batch.rows
+    by_name = {f.name: f for f in config.features}
+    cols: dict[str, Any] = {}
+    offs = batch.offsets.numpy()
+    ids = batch.ids.numpy()
+    for fi, lf in enumerate(batch_plan.features):
+        f = by_name[lf.name]
+        if lf.table is None:
+            d = batch.dense.numpy()[:, lf.dense_col:lf.dense_col + int(f.dimension)]
+            cols[f.source or f.name] = pa.array([list(map(float, r)) for r in d], type=pa.list_(pa.float32()))
+            continue
+        seg = [ids[offs[fi * rows + i]:offs[fi * rows + i + 1]].tolist() for i in range(rows)]
+        if f.pooling == "none" and all(len(s) == 1 for s in seg):
+            cols[f.source or f.name] = pa.array([s[0] for s in seg], type=pa.int64())
+        else:
+            cols[f.source or f.name] = pa.array(seg, type=pa.list_(pa.int64()))
+    sp = config.data.train
+    for t, task in enumerate(config.task_names):
+        cols[sp.labels.get(task, task)] = pa.array(batch.labels.numpy()[:, t].astype(np.float32))
+    if config.scenarios.source and config.scenarios.source not in cols:
+        cols[config.scenarios.source] = pa.array(batch.scenario_id.numpy().astype(np.int64))
+    pq.write_table(pa.table(cols), path, row_group_size=rows_per_group)
