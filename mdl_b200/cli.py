@@ -1,0 +1,461 @@
+"""Command line: ``python -m mdl_b200 <command> --config CONFIG.yaml ...``.
+
+Commands (reference CLI ``src/main.py:1232-1430``): ``validate-config``,
+``plan-shards``, ``profile``, ``fit-vocab``, ``check-checkpoint-store``,
+``train``, ``benchmark``, ``evaluate``, ``predict``, plus
+``make-synthetic-parquet`` (mock input files of a benchmark workload).
+
+``--set section.key=value`` overrides any config value (YAML-parsed value).
+With ``--nproc-per-node N`` (N > 1) ``train`` / ``benchmark`` / ``evaluate``
+re-launch themselves under ``torch.distributed.run`` (one process per GPU,
+rendezvous on 127.0.0.1). Training data comes from ``data.train.inputs``
+(flat Parquet) or, with ``--synthetic`` or no inputs, from the seeded synthetic
+generator in the shapes of the config.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import subprocess
+import sys
+import time
+
+import yaml
+
+
+# ------------------------------------------------------------------ config
+def _set_path(mapping: dict, dotted: str, value) -> None:
+    keys = dotted.split(".")
+    cur = mapping
+    for k in keys[:-1]:
+        cur = cur.setdefault(k, {})
+    cur[keys[-1]] = value
+
+
+def load_cli_config(args):
+    from .config import app_config_from_mapping, load_config_mapping
+    from .data.baseline_configs import baseline_config
+
+    if getattr(args, "benchmark_config", None):
+        mapping, _ = baseline_config(int(args.benchmark_config))
+    else:
+        mapping = load_config_mapping(args.config)
+    for item in getattr(args, "set", None) or []:
+        key, _, raw = item.partition("=")
+        _set_path(mapping, key.strip(), yaml.safe_load(raw))
+    return app_config_from_mapping(mapping)
+
+
+def _add_config(p, required=True):
+    g = p.add_mutually_exclusive_group(required=required)
+    g.add_argument("--config", help="YAML config")
+    g.add_argument("--benchmark-config", type=int, help="one of the benchmark workloads (1-5)")
+    p.add_argument("--set", action="append", default=[], metavar="KEY=VALUE", help="config override")
+
+
+# ------------------------------------------------------------------ runtime
+def _launched_world() -> tuple[int, int, int]:
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+def _relaunch(args, argv) -> int | None:
+    n = getattr(args, "nproc_per_node", None) or 1
+    if n <= 1 or "LOCAL_RANK" in os.environ:
+        return None
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n}",
+           "--master-addr=127.0.0.1", f"--master-port={args.master_port}", "-m", "mdl_b200", *argv]
+    return subprocess.call(cmd)
+
+
+def _setup_runtime(config):
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = _launched_world()
+    use_cuda = torch.cuda.is_available() and config.runtime.device != "cpu"
+    device = torch.device("cuda", local) if use_cuda else torch.device("cpu")
+    if use_cuda:
+        torch.cuda.set_device(device)
+    if world > 1 and not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        kw = {"device_id": device} if use_cuda else {}
+        dist.init_process_group("nccl" if use_cuda else "gloo", timeout=datetime.timedelta(minutes=10), **kw)
+    return rank, world, device
+
+
+def _build(config, rank, world, device, seed=1234):
+    import torch
+    import torch.distributed as dist
+
+    from .models.factory import build_model
+    from .train.trainer import Trainer
+
+    torch.manual_seed(seed)
+    pg = dist.group.WORLD if world > 1 else None
+    vocab_sizes = None
+    model = build_model(config, device=device, rank=rank, world=world, process_group=pg, vocab_sizes=vocab_sizes,
+                        base_seed=seed)
+    trainer = Trainer(config, model, device=device, rank=rank, world=world, process_group=pg)
+    return model, trainer
+
+
+def _batches(config, model, rank, world, *, split="train", synthetic=False, batch=None, loop=True):
+    from .data.parquet import ParquetBatchIterator, Tensorizer, discover_parquet_inputs
+    from .data.synthetic import SyntheticGenerator, synthetic_spec_from_config
+
+    rows = batch or config.training.batch_size
+    sp = getattr(config.data, split) or config.data.train
+    if not synthetic and sp.inputs:
+        paths = discover_parquet_inputs(sp.inputs)
+        r = sp.reader
+        return ParquetBatchIterator(paths, Tensorizer(config, model.encoder.batch_plan, split=split), rows, rank=rank,
+                                    world=world, shard_unit=r.shard_unit, shuffle_rows=r.shuffle_buffer_rows,
+                                    seed=r.shuffle_seed, prefetch=r.prefetch_batches, loop=loop and split == "train",
+                                    pin=r.pin_memory)
+    gen = SyntheticGenerator(model.encoder.batch_plan, synthetic_spec_from_config(config, model.encoder.batch_plan),
+                             rank=rank)
+
+    def forever():
+        while True:
+            yield gen.batch(rows)
+
+    return forever()
+
+
+# ------------------------------------------------------------------ commands
+def cmd_validate(args) -> int:
+    cfg = load_cli_config(args)
+    res = cfg.resolved.tokenization
+    print(json.dumps({"valid": True, "model": cfg.model.name, "features": len(cfg.features),
+                      "feature_token_inputs": len(res.feature_token_inputs),
+                      "feature_tokens": res.feature_token_count, "scenario_tokens": len(res.scenario_token_specs),
+                      "task_tokens": len(res.task_token_specs), "tasks": list(cfg.task_names)}))
+    return 0
+
+
+def cmd_plan_shards(args) -> int:
+    from .models.features import FeatureEncoder
+    import torch
+
+    cfg = load_cli_config(args)
+    enc = FeatureEncoder.__new__(FeatureEncoder)  # plan only: no tables are allocated
+    from .parallel.sharding import EmbeddingTableSpec, plan_embedding_shards
+    from .models.features import categorical_size, table_name_of
+
+    by_name = {f.name: f for f in cfg.features}
+    tables = {}
+    for f in cfg.features:
+        if f.kind != "categorical":
+            continue
+        t = table_name_of(cfg, f.name)
+        owner = by_name.get(t, f)
+        tables[t] = (categorical_size(owner), int(owner.embedding_dim or cfg.model.embedding_dim))
+    specs = [EmbeddingTableSpec(n, r, d) for n, (r, d) in sorted(tables.items())]
+    plan = plan_embedding_shards(specs, world_size=args.world, strategy=cfg.training.embedding_sharding.strategy,
+                                 table_wise_max_rows=cfg.training.embedding_sharding.table_wise_max_rows)
+    load = [0] * args.world
+    for s in specs:
+        sp = plan.tables[s.name]
+        for r in range(args.world):
+            load[r] += sp.local_rows(s.num_embeddings, r) * s.embedding_dim * 4
+    print(json.dumps({"world": args.world, "fingerprint": plan.fingerprint,
+                      "row_wise": sum(1 for s in plan.tables.values() if s.strategy == "row_wise"),
+                      "table_wise": sum(1 for s in plan.tables.values() if s.strategy == "table_wise"),
+                      "bytes_per_rank": load}))
+    del enc, torch
+    return 0
+
+
+def cmd_profile(args) -> int:
+    import numpy as np
+
+    cfg = load_cli_config(args)
+    rank, world, device = 0, 1, "cpu"
+    from .models.factory import build_model
+
+    model = build_model(cfg, device="cpu", base_seed=0)
+    it = _batches(cfg, model, rank, world, split=args.split, synthetic=args.synthetic, loop=False)
+    stats = {"batches": 0, "rows": 0, "ids": 0}
+    for i, b in enumerate(it):
+        if i >= args.max_batches:
+            break
+        stats["batches"] += 1
+        stats["rows"] += b.rows
+        stats["ids"] += int(b.ids.numel())
+        if b.labels is not None:
+            stats.setdefault("label_sum", np.zeros(b.labels.shape[1]))
+            stats["label_sum"] += b.labels.sum(0).numpy()
+    if "label_sum" in stats:
+        stats["label_rate"] = (stats.pop("label_sum") / max(1, stats["rows"])).tolist()
+    stats["ids_per_row"] = stats["ids"] / max(1, stats["rows"])
+    print(json.dumps(stats))
+    return 0
+
+
+def cmd_fit_vocab(args) -> int:
+    from .data.parquet import discover_parquet_inputs, fit_vocabs
+
+    cfg = load_cli_config(args)
+    out = fit_vocabs(cfg, discover_parquet_inputs(args.inputs or cfg.data.train.inputs), args.out)
+    print(json.dumps(out))
+    return 0
+
+
+def cmd_check_store(args) -> int:
+    from .checkpoint import latest_committed_checkpoint, open_checkpoint_store
+
+    store = open_checkpoint_store(args.checkpoint_dir)
+    payload = os.urandom(args.probe_mib * 2 ** 20)
+    t0 = time.time()
+    store.write_bytes(payload, "_probe")
+    ok = store.read_bytes("_probe") == payload
+    store.remove_tree("_probe")
+    latest = latest_committed_checkpoint(store)
+    print(json.dumps({"store": store.root_uri, "round_trip_ok": ok, "seconds": round(time.time() - t0, 3),
+                      "resume_from": None if latest is None else latest.directory}))
+    return 0 if ok else 1
+
+
+def cmd_train(args, argv) -> int:
+    rc = _relaunch(args, argv)
+    if rc is not None:
+        return rc
+    import torch
+
+    from .checkpoint import load_training_checkpoint, open_checkpoint_store, save_training_checkpoint
+    from .train.watchdog import StepWatchdog, abort_on_cuda_oom
+
+    cfg = load_cli_config(args)
+    rank, world, device = _setup_runtime(cfg)
+    model, trainer = _build(cfg, rank, world, device)
+    run = open_checkpoint_store(args.checkpoint_dir) if args.checkpoint_dir else None
+    start = 0
+    if run is not None:
+        state = load_training_checkpoint(cfg, trainer, run, args.resume)
+        if state is not None:
+            start = state.step
+    batches = iter(_batches(cfg, model, rank, world, synthetic=args.synthetic))
+    dog = StepWatchdog(cfg.training.step_watchdog_sec if args.watchdog_sec is None else args.watchdog_sec).start()
+    t0 = time.time()
+    last = None
+    step = start
+    try:
+        while step < args.max_steps:
+            batch = next(batches)
+            if device.type == "cuda":
+                batch = batch.to(device, non_blocking=True)
+            res = abort_on_cuda_oom(trainer.train_step, batch)
+            step = trainer.step_index
+            dog.beat("step", step)
+            if step % args.log_every == 0 and rank == 0:
+                last = float(res.loss)
+                print(json.dumps({"step": step, "loss": last, "elapsed_s": round(time.time() - t0, 2)}), flush=True)
+            if run is not None and args.save_every and step % args.save_every == 0:
+                save_training_checkpoint(cfg, trainer, run, step, keep_last=args.keep_last)
+    finally:
+        dog.stop()
+    if run is not None:
+        save_training_checkpoint(cfg, trainer, run, step, keep_last=args.keep_last)
+    if device.type == "cuda":
+        torch.cuda.synchronize(device)
+    if rank == 0:
+        print(json.dumps({"done": True, "steps": step, "seconds": round(time.time() - t0, 2)}), flush=True)
+    return 0
+
+
+def cmd_benchmark(args, argv) -> int:
+    rc = _relaunch(args, argv)
+    if rc is not None:
+        return rc
+    import torch
+    import torch.distributed as dist
+
+    cfg = load_cli_config(args)
+    rank, world, device = _setup_runtime(cfg)
+    model, trainer = _build(cfg, rank, world, device)
+    it = _batches(cfg, model, rank, world, synthetic=True)
+    pool = [next(it) for _ in range(3)]
+    dev = [b.to(device) for b in pool] if device.type == "cuda" else pool
+    for i in range(args.warmup):
+        trainer.train_step(dev[i % 3])
+    sync = torch.cuda.synchronize if device.type == "cuda" else (lambda *a: None)
+    sync(device) if device.type == "cuda" else None
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    if device.type == "cuda":
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+    for i in range(args.steps):
+        trainer.train_step(dev[i % 3])
+    if device.type == "cuda":
+        e1.record()
+        torch.cuda.synchronize(device)
+        ms = e0.elapsed_time(e1)
+    else:
+        ms = (time.perf_counter() - t0) * 1e3
+    t = torch.tensor([ms], dtype=torch.float64, device=device if device.type == "cuda" else "cpu")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t)
+    rows = cfg.training.batch_size * world * args.steps
+    if rank == 0:
+        print(json.dumps({"metric": "train samples/sec", "value": round(rows / (ms / 1e3), 1), "n_gpus": world,
+                          "ms_per_step": round(ms / args.steps, 4), "model": cfg.model.name,
+                          "global_batch": cfg.training.batch_size * world}), flush=True)
+    return 0
+
+
+def _eval_setup(args, argv):
+    from .checkpoint import load_model_checkpoint, open_checkpoint_store
+    from .checkpoint.training import MODEL_SUBDIR, resolve_resume_checkpoint
+
+    cfg = load_cli_config(args)
+    rank, world, device = _setup_runtime(cfg)
+    model, trainer = _build(cfg, rank, world, device)
+    if args.checkpoint:
+        store = open_checkpoint_store(args.checkpoint)
+        if store.exists("manifest.json"):
+            load_model_checkpoint(cfg, trainer, store)
+        else:
+            ck = resolve_resume_checkpoint(store, "latest")
+            if ck is None:
+                raise FileNotFoundError(f"no committed checkpoint under {args.checkpoint}")
+            load_model_checkpoint(cfg, trainer, store.child(ck.directory, MODEL_SUBDIR))
+    split = "test" if cfg.data.test is not None and cfg.data.test.inputs else "train"
+    it = _batches(cfg, model, rank, world, split=split, synthetic=args.synthetic, loop=False)
+
+    def limited():
+        for i, b in enumerate(it):
+            if i >= args.max_batches:
+                return
+            yield b
+
+    return cfg, rank, trainer, limited()
+
+
+def cmd_evaluate(args, argv) -> int:
+    rc = _relaunch(args, argv)
+    if rc is not None:
+        return rc
+    from .train.evaluate import evaluate
+
+    cfg, rank, trainer, batches = _eval_setup(args, argv)
+    res = evaluate(trainer, batches)
+    if rank == 0:
+        print(json.dumps(res, default=str), flush=True)
+    return 0
+
+
+def cmd_predict(args, argv) -> int:
+    from .train.evaluate import predict
+
+    cfg, rank, trainer, batches = _eval_setup(args, argv)
+    probs = predict(trainer, batches, args.output if rank == 0 else None)
+    if rank == 0:
+        print(json.dumps({"rows": int(probs.shape[0]), "output": args.output}), flush=True)
+    return 0
+
+
+def cmd_make_synthetic(args) -> int:
+    from .config import app_config_from_mapping
+    from .data.baseline_configs import baseline_config, scaled_config
+    from .data.parquet import write_synthetic_parquet
+    from .data.synthetic import SyntheticGenerator
+    from .models.factory import build_model
+
+    mapping, spec = (scaled_config(args.benchmark, args.scale) if args.scale != 1.0
+                     else baseline_config(args.benchmark))
+    mapping["runtime"]["device"] = "cpu"
+    cfg = app_config_from_mapping(mapping)
+    model = build_model(cfg, device="cpu", base_seed=0)
+    gen = SyntheticGenerator(model.encoder.batch_plan, spec)
+    os.makedirs(args.out, exist_ok=True)
+    for i in range(args.files):
+        write_synthetic_parquet(os.path.join(args.out, f"part-{i:05d}.parquet"), gen.batch(args.rows),
+                                model.encoder.batch_plan, cfg)
+    print(json.dumps({"files": args.files, "rows_per_file": args.rows, "out": args.out}))
+    return 0
+
+
+def build_parser() -> argparse.ArgumentParser:
+    ap = argparse.ArgumentParser(prog="python -m mdl_b200", description=__doc__,
+                                 formatter_class=argparse.RawDescriptionHelpFormatter)
+    sub = ap.add_subparsers(dest="command", required=True)
+    p = sub.add_parser("validate-config")
+    _add_config(p)
+    p = sub.add_parser("plan-shards")
+    _add_config(p)
+    p.add_argument("--world", type=int, default=8)
+    p = sub.add_parser("profile")
+    _add_config(p)
+    p.add_argument("--split", choices=["train", "test"], default="train")
+    p.add_argument("--max-batches", type=int, default=10)
+    p.add_argument("--synthetic", action="store_true")
+    p = sub.add_parser("fit-vocab")
+    _add_config(p)
+    p.add_argument("--inputs", nargs="*")
+    p.add_argument("--out", required=True)
+    p = sub.add_parser("check-checkpoint-store")
+    p.add_argument("--checkpoint-dir", required=True)
+    p.add_argument("--probe-mib", type=int, default=8)
+    for name in ("train", "benchmark", "evaluate", "predict"):
+        p = sub.add_parser(name)
+        _add_config(p)
+        p.add_argument("--nproc-per-node", type=int, default=1)
+        p.add_argument("--master-port", type=int, default=29533)
+        p.add_argument("--synthetic", action="store_true")
+        if name == "train":
+            p.add_argument("--max-steps", type=int, default=100)
+            p.add_argument("--checkpoint-dir")
+            p.add_argument("--resume", default="auto")
+            p.add_argument("--save-every", type=int, default=0)
+            p.add_argument("--keep-last", type=int, default=3)
+            p.add_argument("--log-every", type=int, default=10)
+            p.add_argument("--watchdog-sec", type=float, default=None)
+        if name == "benchmark":
+            p.add_argument("--steps", type=int, default=20)
+            p.add_argument("--warmup", type=int, default=5)
+        if name in ("evaluate", "predict"):
+            p.add_argument("--checkpoint")
+            p.add_argument("--max-batches", type=int, default=10)
+        if name == "predict":
+            p.add_argument("--output", required=True)
+    p = sub.add_parser("make-synthetic-parquet")
+    p.add_argument("--benchmark", type=int, default=1)
+    p.add_argument("--scale", type=float, default=1.0)
+    p.add_argument("--files", type=int, default=2)
+    p.add_argument("--rows", type=int, default=1024)
+    p.add_argument("--out", required=True)
+    return ap
+
+
+def main(argv=None) -> int:
+    argv = list(sys.argv[1:] if argv is None else argv)
+    args = build_parser().parse_args(argv)
+    cmd = args.command
+    if cmd == "validate-config":
+        return cmd_validate(args)
+    if cmd == "plan-shards":
+        return cmd_plan_shards(args)
+    if cmd == "profile":
+        return cmd_profile(args)
+    if cmd == "fit-vocab":
+        return cmd_fit_vocab(args)
+    if cmd == "check-checkpoint-store":
+        return cmd_check_store(args)
+    if cmd == "train":
+        return cmd_train(args, argv)
+    if cmd == "benchmark":
+        return cmd_benchmark(args, argv)
+    if cmd == "evaluate":
+        return cmd_evaluate(args, argv)
+    if cmd == "predict":
+        return cmd_predict(args, argv)
+    if cmd == "make-synthetic-parquet":
+        return cmd_make_synthetic(args)
+    raise SystemExit(f"unknown command {cmd}")

@@ -178,3 +178,28 @@ class BatchPool:
         b = self.batches[self.i % len(self.batches)]
         self.i += 1
         return b
+
+
+def synthetic_spec_from_config(config, batch_plan, *, zipf_s: float | None = 1.05, seed: int = 0,
+                               task_rate: float = 0.1) -> SyntheticSpec:
+    """A ``SyntheticSpec`` for any config: every categorical input of the batch layout draws
+    ids over its table (``max_id`` / ``num_buckets``; ``vocab`` features over a
+    1000-entry vocabulary), bags draw lengths in [1, max_length or 8]."""
+
+    by_name = {f.name: f for f in config.features}
+    fields = {}
+    for lf in batch_plan.features:
+        if lf.table is None:
+            continue
+        f = by_name[lf.name]
+        enc = f.encoding
+        vocab = 1000
+        if enc is not None and enc.max_id:
+            vocab = int(enc.max_id)
+        elif enc is not None and enc.num_buckets:
+            vocab = int(enc.num_buckets)
+        multi = f.pooling != "none"
+        fields[f.name] = FieldSpec(vocab=vocab, multi_hot=multi, min_len=1, max_len=(f.max_length or 8) if multi else 1)
+    return SyntheticSpec(fields=fields, dense_width=batch_plan.dense_width,
+                         task_rates=[task_rate] * len(config.task_names), zipf_s=zipf_s,
+                         num_scenarios=len(config.scenarios.names), seed=seed)
