@@ -191,6 +191,7 @@ def cmd_profile(args) -> int:
             stats["label_sum"] += b.labels.sum(0).numpy()
     if "label_sum" in stats:
         stats["label_rate"] = (stats.pop("label_sum") / max(1, stats["rows"])).tolist()
+    _close(it)
     stats["ids_per_row"] = stats["ids"] / max(1, stats["rows"])
     print(json.dumps(stats))
     return 0
@@ -238,7 +239,8 @@ def cmd_train(args, argv) -> int:
         state = load_training_checkpoint(cfg, trainer, run, args.resume)
         if state is not None:
             start = state.step
-    batches = iter(_batches(cfg, model, rank, world, synthetic=args.synthetic))
+    source = _batches(cfg, model, rank, world, synthetic=args.synthetic)
+    batches = iter(source)
     dog = StepWatchdog(cfg.training.step_watchdog_sec if args.watchdog_sec is None else args.watchdog_sec).start()
     t0 = time.time()
     last = None
@@ -258,6 +260,7 @@ def cmd_train(args, argv) -> int:
                 save_training_checkpoint(cfg, trainer, run, step, keep_last=args.keep_last)
     finally:
         dog.stop()
+        _close(source)
     if run is not None:
         save_training_checkpoint(cfg, trainer, run, step, keep_last=args.keep_last)
     if device.type == "cuda":
@@ -310,6 +313,12 @@ def cmd_benchmark(args, argv) -> int:
     return 0
 
 
+def _close(it) -> None:
+    close = getattr(it, "close", None)
+    if close is not None:
+        close()
+
+
 def _eval_setup(args, argv):
     from .checkpoint import load_model_checkpoint, open_checkpoint_store
     from .checkpoint.training import MODEL_SUBDIR, resolve_resume_checkpoint
@@ -330,10 +339,13 @@ def _eval_setup(args, argv):
     it = _batches(cfg, model, rank, world, split=split, synthetic=args.synthetic, loop=False)
 
     def limited():
-        for i, b in enumerate(it):
-            if i >= args.max_batches:
-                return
-            yield b
+        try:
+            for i, b in enumerate(it):
+                if i >= args.max_batches:
+                    return
+                yield b
+        finally:
+            _close(it)
 
     return cfg, rank, trainer, limited()
 

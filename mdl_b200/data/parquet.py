@@ -360,8 +360,8 @@ class ParquetBatchIterator:
     def _tables(self):
         pa, pq = _pa()
         cols = self.tz.columns()
-        while True:
-            while self.position < len(self.refs):
+        while not self._stop.is_set():
+            while self.position < len(self.refs) and not self._stop.is_set():
                 ref = self.refs[self.position]
                 f = pq.ParquetFile(ref.path)
                 present = [c for c in cols if c in f.schema_arrow.names]
@@ -419,8 +419,13 @@ class ParquetBatchIterator:
 
     def close(self) -> None:
         self._stop.set()
-        if self._thread is not None:
-            self._thread.join(timeout=5)
+        while self._thread is not None and self._thread.is_alive():
+            try:  # unblock a producer waiting on a full queue
+                self._q.get_nowait()
+            except queue.Empty:
+                pass
+            self._thread.join(timeout=0.1)
+        self._thread = None
 
 
 class DevicePrefetcher:
