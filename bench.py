@@ -38,7 +38,11 @@ MODEL_DESC = {
     2: "rankmixer (BASELINE config 2: 300 fields, ~200M x 64 fp32 rows, T=16 D=768 L=2 FFNx4, 2 heads)",
     3: "mdl_rankmixer (BASELINE config 3: config-2 features + 5 scenes x 4 scenario tokens + global, "
        "3 task tokens, FiLM scene bias, T=16 D=768 L=2 FFNx4, 3 heads)",
+    4: "onetrans (BASELINE config 4: 512-event sequence of item + 4 side ids, 32 NS tokens from the config-2 "
+       "fields, d=256 8 heads FFN 1024, 6 layers, causal, pyramid halving every 2 layers, click head)",
 }
+DEFAULT_BATCH = {2: 2048, 3: 2048, 4: 1024}
+SEQ_LEN = {4: 512}
 
 
 def _dist_setup(args):
@@ -78,6 +82,8 @@ def run_ours(args) -> dict:
 
     rank, world, local = _dist_setup(args)
     device = torch.device("cuda", local)
+    if args.batch is None:
+        args.batch = DEFAULT_BATCH[args.config]
     mapping, spec = baseline_config(args.config, batch=args.batch)
     cfg = app_config_from_mapping(mapping)
     torch.manual_seed(1234)
@@ -148,7 +154,7 @@ def run_ours(args) -> dict:
         "config": {
             "model": MODEL_DESC[args.config],
             "global_batch": args.batch * world,
-            "seq_len": None,
+            "seq_len": SEQ_LEN.get(args.config),
             "parallelism": f"dp{world}+emb-rowwise/tablewise-mp{world}",
             "dense_params": n_params,
             "embedding_rows": sum(t.num_embeddings for t in model.store.layouts),
@@ -167,6 +173,8 @@ def run_reference(args) -> dict:
 
     if args.config != 2:
         return {"impl": "reference", "unavailable": f"reference arm is wired for workload 2 only (asked {args.config})"}
+    if args.batch is None:
+        args.batch = DEFAULT_BATCH[args.config]
     try:
         from baseline import reference_harness
 
@@ -183,9 +191,9 @@ def main(argv=None) -> int:
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--batch", type=int, default=2048, help="rows per GPU")
+    p.add_argument("--batch", type=int, default=None, help="rows per GPU (default: the workload's)")
     p.add_argument("--config", type=int, default=2, choices=sorted(MODEL_DESC),
-                   help="BASELINE workload (2: RankMixer headline, 3: MDL)")
+                   help="BASELINE workload (2: RankMixer headline, 3: MDL, 4: OneTrans)")
     p.add_argument("--pool", type=int, default=4, help="distinct pinned host batches rotated per step")
     p.add_argument("--ref-no-graphs", action="store_true", help="reference arm: disable its CUDA-graph backbone")
     args = p.parse_args(argv)

@@ -43,7 +43,7 @@ void gemm(const at::Tensor& A, int64_t lda, int64_t gsA, bool a_mn, const at::Te
           const std::optional<at::Tensor>& bias, int64_t gs_bias, const std::optional<at::Tensor>& aux,
           int64_t ld_aux, int64_t gs_aux, const std::optional<at::Tensor>& colsum, int64_t gs_colsum,
           int64_t act, double alpha, bool accumulate, const std::optional<at::Tensor>& err,
-          int64_t max_ctas) {
+          int64_t max_ctas, int64_t KG, int64_t ksA, int64_t ksB) {
   require_cuda(A, "A");
   require_cuda(B, "B");
   require_cuda(out, "out");
@@ -67,6 +67,9 @@ void gemm(const at::Tensor& A, int64_t lda, int64_t gsA, bool a_mn, const at::Te
   a.N = static_cast<int>(N);
   a.K = static_cast<int>(K);
   a.G = static_cast<int>(G);
+  a.KG = static_cast<int>(KG);
+  a.ksA = ksA;
+  a.ksB = ksB;
   a.out = out.data_ptr();
   a.ldc = ldc;
   a.gsC = gsC;
@@ -393,7 +396,8 @@ void rms_fwd(const at::Tensor& x, const std::optional<at::Tensor>& w, const at::
 }
 
 void rms_bwd(const at::Tensor& x, const std::optional<at::Tensor>& w, const at::Tensor& rstd, const at::Tensor& dy,
-             const at::Tensor& dx, const std::optional<at::Tensor>& dw, int64_t rows, int64_t D) {
+             const at::Tensor& dx, const std::optional<at::Tensor>& dw, int64_t rows, int64_t D,
+             const std::optional<at::Tensor>& dres, int64_t res_period, int64_t res_tail) {
   c10::cuda::CUDAGuard guard(x.device());
   mdl::RMSArgs p;
   p.x = x.data_ptr();
@@ -404,6 +408,9 @@ void rms_bwd(const at::Tensor& x, const std::optional<at::Tensor>& w, const at::
   p.dweight = optr<float>(dw);
   p.rows = rows;
   p.D = static_cast<int>(D);
+  p.dres = optr(dres);
+  p.res_period = static_cast<int>(res_period);
+  p.res_tail = static_cast<int>(res_tail);
   check(mdl::rmsnorm_bwd(p, stream_of(x)), "rmsnorm_bwd");
   g_launches += 1;
 }
@@ -418,11 +425,11 @@ void token_mean(const at::Tensor& x, const at::Tensor& out, int64_t B, int64_t T
 }
 
 void colsum(const at::Tensor& x, const at::Tensor& out, int64_t G, int64_t M, int64_t N, int64_t ld, int64_t gs,
-            double scale) {
+            double scale, int64_t gs_out) {
   c10::cuda::CUDAGuard guard(x.device());
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && out.scalar_type() == at::kFloat, "colsum: bf16 in, fp32 out");
   check(mdl::colsum_bf16(x.data_ptr(), ptr<float>(out), static_cast<int>(G), M, static_cast<int>(N), ld, gs,
-                         static_cast<float>(scale), stream_of(x)),
+                         static_cast<float>(scale), stream_of(x), gs_out),
         "colsum_bf16");
   g_launches += 1;
 }
@@ -676,6 +683,84 @@ void small_attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& 
   g_launches += 1;
 }
 
+void position_add(const at::Tensor& x, const at::Tensor& pos, const at::Tensor& kstart, int64_t B, int64_t L,
+                  int64_t D) {
+  c10::cuda::CUDAGuard guard(x.device());
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && pos.scalar_type() == at::kFloat && kstart.scalar_type() == at::kInt,
+              "position_add: bf16 x, fp32 pos, int32 kstart");
+  TORCH_CHECK(x.numel() >= B * L * D && kstart.numel() >= B, "position_add: sizes");
+  check(mdl::position_add(x.data_ptr(), pos.data_ptr<float>(), kstart.data_ptr<int>(), static_cast<int>(B),
+                          static_cast<int>(L), static_cast<int>(D), stream_of(x)),
+        "position_add");
+  g_launches += 1;
+}
+
+void position_grad(const at::Tensor& dx, const at::Tensor& dpos, const at::Tensor& kstart, int64_t B, int64_t L,
+                   int64_t D) {
+  c10::cuda::CUDAGuard guard(dx.device());
+  TORCH_CHECK(dx.scalar_type() == at::kBFloat16 && dpos.scalar_type() == at::kFloat && kstart.scalar_type() == at::kInt,
+              "position_grad: bf16 dx, fp32 dpos, int32 kstart");
+  TORCH_CHECK(dpos.numel() >= L * D, "position_grad: dpos holds fewer than L positions");
+  check(mdl::position_grad(dx.data_ptr(), dpos.data_ptr<float>(), kstart.data_ptr<int>(), static_cast<int>(B),
+                           static_cast<int>(L), static_cast<int>(D), stream_of(dx)),
+        "position_grad");
+  g_launches += 1;
+}
+
+// ------------------------------------------------------------------ flash attention
+mdl::FmhaArgs fmha_args(const at::Tensor& qkv, const at::Tensor& kstart, const at::Tensor& out, const at::Tensor& lse,
+                        int64_t H, int64_t Lq, bool causal, double scale, const std::optional<at::Tensor>& err) {
+  require_cuda(qkv, "qkv");
+  TORCH_CHECK(qkv.scalar_type() == at::kBFloat16 && qkv.dim() == 3 && qkv.is_contiguous(), "qkv must be [B, Lk, 3D] bf16");
+  TORCH_CHECK(kstart.scalar_type() == at::kInt && kstart.numel() == qkv.size(0), "kstart must be int32 [B]");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous(), "out must be contiguous bf16");
+  TORCH_CHECK(lse.scalar_type() == at::kFloat && lse.is_contiguous(), "lse must be contiguous fp32");
+  mdl::FmhaArgs a;
+  a.qkv = qkv.data_ptr();
+  a.kstart = kstart.data_ptr<int>();
+  a.out = out.data_ptr();
+  a.lse = lse.data_ptr<float>();
+  a.B = static_cast<int>(qkv.size(0));
+  a.Lk = static_cast<int>(qkv.size(1));
+  a.H = static_cast<int>(H);
+  a.hd = static_cast<int>(qkv.size(2) / 3 / H);
+  a.Lq = static_cast<int>(Lq);
+  a.causal = causal;
+  a.scale = static_cast<float>(scale);
+  a.err = optr<int>(err);
+  TORCH_CHECK(qkv.size(2) == 3 * H * a.hd, "qkv width must be 3 * H * head_dim");
+  TORCH_CHECK(out.numel() == static_cast<int64_t>(a.B) * Lq * H * a.hd, "out must be [B, Lq, D]");
+  TORCH_CHECK(lse.numel() == static_cast<int64_t>(a.B) * H * Lq, "lse must be [B, H, Lq]");
+  return a;
+}
+
+void fmha_fwd(const at::Tensor& qkv, const at::Tensor& kstart, const at::Tensor& out, const at::Tensor& lse, int64_t H,
+              int64_t Lq, bool causal, double scale, const std::optional<at::Tensor>& err) {
+  c10::cuda::CUDAGuard guard(qkv.device());
+  auto a = fmha_args(qkv, kstart, out, lse, H, Lq, causal, scale, err);
+  check(mdl::fmha_fwd(a, stream_of(qkv)), "fmha_fwd");
+  g_launches += 1;
+}
+
+void fmha_bwd(const at::Tensor& qkv, const at::Tensor& kstart, const at::Tensor& out, const at::Tensor& lse,
+              const at::Tensor& dout, const at::Tensor& dqkv, const at::Tensor& dq_acc, const at::Tensor& dsum,
+              int64_t H, int64_t Lq, bool causal, double scale, const std::optional<at::Tensor>& err) {
+  c10::cuda::CUDAGuard guard(qkv.device());
+  auto a = fmha_args(qkv, kstart, out, lse, H, Lq, causal, scale, err);
+  TORCH_CHECK(dout.scalar_type() == at::kBFloat16 && dout.is_contiguous() && dout.numel() == out.numel(),
+              "dout must be contiguous bf16 like out");
+  TORCH_CHECK(dqkv.scalar_type() == at::kBFloat16 && dqkv.is_contiguous() && dqkv.numel() == qkv.numel(),
+              "dqkv must be contiguous bf16 like qkv");
+  TORCH_CHECK(dq_acc.scalar_type() == at::kFloat && dq_acc.numel() >= out.numel(), "dq_acc must be fp32 [B, Lq, D]");
+  TORCH_CHECK(dsum.scalar_type() == at::kFloat && dsum.numel() >= lse.numel(), "dsum must be fp32 [B, H, Lq]");
+  a.dout = dout.data_ptr();
+  a.dqkv = dqkv.data_ptr();
+  a.dq_acc = dq_acc.data_ptr<float>();
+  a.dsum = dsum.data_ptr<float>();
+  check(mdl::fmha_bwd(a, stream_of(qkv)), "fmha_bwd");
+  g_launches += 3;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -686,7 +771,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("bias") = py::none(), py::arg("gs_bias") = 0, py::arg("aux") = py::none(), py::arg("ld_aux") = 0,
         py::arg("gs_aux") = 0, py::arg("colsum") = py::none(), py::arg("gs_colsum") = 0, py::arg("act") = 0,
         py::arg("alpha") = 1.0, py::arg("accumulate") = false, py::arg("err") = py::none(),
-        py::arg("max_ctas") = 0);
+        py::arg("max_ctas") = 0, py::arg("KG") = 1, py::arg("ksA") = 0, py::arg("ksB") = 0);
 
   m.def("emb_forward", &emb_forward);
   m.def("emb_backward", &emb_backward);
@@ -701,9 +786,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ln_bwd_grid", &ln_bwd_grid);
   m.def("ln_bwd", &ln_bwd);
   m.def("rms_fwd", &rms_fwd);
-  m.def("rms_bwd", &rms_bwd);
+  m.def("rms_bwd", &rms_bwd, py::arg("x"), py::arg("w"), py::arg("rstd"), py::arg("dy"), py::arg("dx"), py::arg("dw"),
+        py::arg("rows"), py::arg("D"), py::arg("dres") = py::none(), py::arg("res_period") = 0,
+        py::arg("res_tail") = 0);
   m.def("token_mean", &token_mean);
-  m.def("colsum", &colsum);
+  m.def("colsum", &colsum, py::arg("x"), py::arg("out"), py::arg("G"), py::arg("M"), py::arg("N"), py::arg("ld"),
+        py::arg("gs"), py::arg("scale"), py::arg("gs_out") = -1);
   m.def("head_bce", &head_bce);
   m.def("adam", &adam);
   m.def("rmsprop", &rmsprop);
@@ -722,4 +810,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("launch_count", &launch_count);
   m.def("small_attn_fwd", &small_attn_fwd);
   m.def("small_attn_bwd", &small_attn_bwd);
+  m.def("fmha_fwd", &fmha_fwd);
+  m.def("position_add", &position_add);
+  m.def("position_grad", &position_grad);
+  m.def("fmha_bwd", &fmha_bwd);
 }

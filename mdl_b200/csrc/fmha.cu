@@ -1,0 +1,819 @@
+// Flash attention for sm_100a on the 5th-generation tensor cores: scores and
+// products in TMEM (tcgen05.mma), operands staged by TMA with 128-byte swizzle,
+// softmax in registers, one warp-specialised CTA per tile.
+//
+// Serves the OneTrans mixed causal attention (queries = the pyramid-pruned
+// suffix of the [S; NS] token sequence, bottom-right causal, prefix padding
+// given as a per-sample first valid key; reference
+// MixedCausalAttention.attend_causal_suffix src/model.py:5617-5695, which
+// packs the valid tokens and calls flash_attn_varlen_func,
+// src/attention.py:103-162). Padding is never packed away here: a sample's
+// prefix of invalid keys is skipped a whole 128-key tile at a time and masked
+// inside the boundary tile.
+//
+// Tiling. Query and key tiles are 128 token rows aligned to the END of the
+// sequence (tile t = rows Lk-128(t+1) .. Lk-128t-1), so query tile i meets key
+// tile i on the diagonal (the only tile with a causal mask) and key tiles
+// t > i in full. Rows before the first token read as zeros (TMA fill).
+//
+// Forward (320 threads, 1 CTA/SM, 512 TMEM columns): one CTA = one sample,
+// one pair of heads (head_dim 32: one 128-byte swizzled row of Q/K/V holds
+// both heads), one query tile.
+//   warp 0      TMA: Q once, then K/V tiles into a 2-stage ring
+//   warp 1      MMA: S_h = Q_h K_h^T (M=128, N=128, K=32) into TMEM,
+//               then PV_h = P_h V (M=128, N=64, K=128) into a TMEM double buffer
+//   warps 2-5   softmax of head 0, warps 6-9 head 1: thread = query row;
+//               online max / sum in base 2, P as bf16 into swizzled smem; the
+//               PV of tile j-1 is folded into the register accumulator while
+//               the tensor core works on tile j.
+// Backward (320 threads): one CTA = one sample, one head, one key tile; it
+// walks the query tiles that see those keys:
+//   S^T = K Q^T and dP^T = V dO^T (thread = key row), P^T = exp2(S^T*c - lse),
+//   dS^T = P^T (dP^T - D) * scale, dV += P^T dO, dK += dS^T Q (accumulated in
+//   TMEM), dQ_tile = dS K (same smem dS^T read as an MN-major operand) added
+//   to an fp32 buffer with vector reductions.
+//
+// Every wait is bounded (error word + abort flag) and every role drains what
+// it has in flight before the CTA exits.
+#include <cudaTypedefs.h>
+
+#include <math_constants.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "fmha.h"
+
+namespace mdl {
+namespace {
+
+constexpr int HD = 32;
+constexpr int TILE = 128;
+constexpr int TILE_BYTES = TILE * 128;  // 128 rows x 128 bytes (64 bf16 = two heads)
+constexpr int P_BYTES = 2 * TILE_BYTES; // 128 x 128 bf16 as two 64-column swizzled blocks
+constexpr int NUM_THREADS = 320;
+constexpr int TMEM_COLS = 512;
+constexpr float kLog2e = 1.4426950408889634f;
+
+// forward smem: Q | K[2] | V[2] | P[2] | barriers
+constexpr int F_SMEM = 1024 + TILE_BYTES * 5 + 2 * P_BYTES + 256;
+// backward smem: K | V | Q[2] | dO[2] | P^T | dS^T | lse[2][128] | D[2][128] | barriers
+constexpr int B_SMEM = 1024 + TILE_BYTES * 6 + 2 * P_BYTES + 4 * TILE * 4 + 256;
+static_assert(F_SMEM <= 232448 && B_SMEM <= 232448, "shared memory budget");
+
+struct Params {
+  void* out;
+  float* lse;
+  const int* kstart;
+  float* dq_acc;
+  const float* dsum;
+  void* dqkv;
+  int B, H, Lk, Lq, D, causal;
+  float scale, scale2;
+  int* err;
+};
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~static_cast<uintptr_t>(1023));
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float lg2(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void st_smem_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// 32 consecutive fp32 TMEM columns of this thread's lane, no wait.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
+        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
+        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// K-major operand, 128-byte swizzle: `k_bytes` selects the 16-element K step inside the row.
+__device__ __forceinline__ uint64_t desc_k(uint32_t base, uint32_t k_bytes) {
+  return make_smem_desc(base + k_bytes, 16, 1024);
+}
+// 128 x 128 operand stored as two 64-column K-major blocks: K step s (16 columns).
+__device__ __forceinline__ uint64_t desc_k128(uint32_t base, int s) {
+  return make_smem_desc(base + (s >> 2) * TILE_BYTES + (s & 3) * 32, 16, 1024);
+}
+// MN-major operand (rows = K, 64 contiguous MN elements per 128-byte row; a
+// second 64-wide MN block TILE_BYTES further): K step s = 16 rows.
+__device__ __forceinline__ uint64_t desc_mn(uint32_t base, int s) {
+  return make_smem_desc(base + s * 2048, TILE_BYTES, 1024);
+}
+
+// Byte offset of 16-byte chunk `c` (0..15) of row `r` in a 128 x 128 bf16 block pair.
+__device__ __forceinline__ uint32_t swz_off(int r, int c) {
+  return (c >> 3) * TILE_BYTES + r * 128 + (((c & 7) ^ (r & 7)) << 4);
+}
+
+__device__ __forceinline__ void red_add_v4(float* dst, float a, float b, float c, float d) {
+  asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(dst), "f"(a), "f"(b), "f"(c),
+               "f"(d)
+               : "memory");
+}
+
+// ============================================================================ forward
+__global__ void __maxnreg__(200)
+    fmha_fwd_kernel(const __grid_constant__ CUtensorMap tm, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + TILE_BYTES;
+  uint8_t* sV = sK + 2 * TILE_BYTES;
+  uint8_t* sP = sV + 2 * TILE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * P_BYTES);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;     // [2]
+  uint64_t* kv_empty = bars + 3;    // [2]
+  uint64_t* s_full = bars + 5;      // [2 heads]
+  uint64_t* s_empty = bars + 7;     // [2]
+  uint64_t* p_full = bars + 9;      // [2]
+  uint64_t* p_empty = bars + 11;    // [2]
+  uint64_t* pv_full = bars + 13;    // [head*2 + buf]
+  uint64_t* pv_empty = bars + 17;   // [head*2 + buf]
+  uint64_t* done = bars + 21;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 22);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int HP = p.H >> 1;
+  const int hp = blockIdx.x % HP;
+  const int rest = blockIdx.x / HP;
+  const int b = rest % p.B;
+  const int i = rest / p.B;  // query tile (0 = last 128 rows)
+  const int h0 = hp * 2;
+  const int Lk = p.Lk;
+  const int kst = min(max(p.kstart[b], 0), Lk);
+  const int tmax = (Lk - kst + TILE - 1) / TILE - 1;
+  const int t0 = p.causal ? i : 0;
+  const int n = max(0, tmax - t0 + 1);  // key tiles this CTA visits
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_empty[s], 4);
+      mbar_init(&p_full[s], 4);
+      mbar_init(&p_empty[s], 1);
+    }
+    for (int s = 0; s < 4; ++s) {
+      mbar_init(&pv_full[s], 1);
+      mbar_init(&pv_empty[s], 4);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0 && n > 0) {
+      tma_prefetch_desc(&tm);
+      mbar_arrive_expect_tx(q_full, TILE_BYTES);
+      tma_load_3d(sQ, &tm, q_full, h0 * HD, Lk - TILE * (i + 1), b);
+      int issued = 0;
+      for (int j = 0; j < n; ++j) {
+        const int st = j & 1;
+        if (j >= 2 && !mbar_wait(&kv_empty[st], ((j >> 1) - 1) & 1, p.err, abort_flag)) break;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * TILE_BYTES);
+        const int y = Lk - TILE * (t0 + j + 1);
+        tma_load_3d(sK + st * TILE_BYTES, &tm, &kv_full[st], p.D + h0 * HD, y, b);
+        tma_load_3d(sV + st * TILE_BYTES, &tm, &kv_full[st], 2 * p.D + h0 * HD, y, b);
+        issued = j + 1;
+      }
+      // every copy into this CTA's smem has landed before the CTA may exit
+      mbar_wait(q_full, 0, nullptr, nullptr);
+      for (int j = max(0, issued - 2); j < issued; ++j) mbar_wait(&kv_full[j & 1], (j >> 1) & 1, nullptr, nullptr);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && n > 0) {
+      constexpr uint32_t idesc_s = make_idesc_bf16(TILE, TILE, false, false);
+      constexpr uint32_t idesc_pv = make_idesc_bf16(TILE, 64, false, true);
+      const uint32_t q_base = smem_u32(sQ);
+      const uint32_t k_base = smem_u32(sK);
+      const uint32_t v_base = smem_u32(sV);
+      const uint32_t p_base = smem_u32(sP);
+      bool ok = mbar_wait(q_full, 0, p.err, abort_flag) && mbar_wait(&kv_full[0], 0, p.err, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        for (int hl = 0; hl < 2; ++hl) {
+          for (int ks = 0; ks < 2; ++ks)
+            tc_mma_bf16(tmem + hl * 256, desc_k(q_base, hl * 64 + ks * 32), desc_k(k_base, hl * 64 + ks * 32),
+                        idesc_s, ks);
+          tc_commit(&s_full[hl]);
+        }
+      }
+      for (int j = 0; j < n && ok; ++j) {
+        if (j + 1 < n) {
+          const int st1 = (j + 1) & 1;
+          if (!mbar_wait(&kv_full[st1], ((j + 1) >> 1) & 1, p.err, abort_flag)) break;
+          for (int hl = 0; hl < 2 && ok; ++hl) {
+            if (!mbar_wait(&s_empty[hl], j & 1, p.err, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            for (int ks = 0; ks < 2; ++ks)
+              tc_mma_bf16(tmem + hl * 256, desc_k(q_base, hl * 64 + ks * 32),
+                          desc_k(k_base + st1 * TILE_BYTES, hl * 64 + ks * 32), idesc_s, ks);
+            tc_commit(&s_full[hl]);
+          }
+          if (!ok) break;
+        }
+        const int st = j & 1;
+        for (int hl = 0; hl < 2 && ok; ++hl) {
+          if (!mbar_wait(&p_full[hl], j & 1, p.err, abort_flag) ||
+              (j >= 2 && !mbar_wait(&pv_empty[hl * 2 + st], ((j >> 1) - 1) & 1, p.err, abort_flag))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = tmem + hl * 256 + 128 + st * 64;
+          for (int ks = 0; ks < 8; ++ks)
+            tc_mma_bf16(d, desc_k128(p_base + hl * P_BYTES, ks), desc_mn(v_base + st * TILE_BYTES, ks), idesc_pv,
+                        ks);
+          tc_commit(&pv_full[hl * 2 + st]);
+          tc_commit(&p_empty[hl]);
+        }
+        tc_commit(&kv_empty[st]);
+      }
+      // all MMAs have finished before TMEM is released
+      tc_commit(done);
+      mbar_wait(done, 0, nullptr, nullptr);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int hl = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int qrow = Lk - TILE * (i + 1) + r;
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + hl * 256;
+    const uint32_t p_base = smem_u32(sP + hl * P_BYTES);
+    float m = -CUDART_INF_F, l = 0.f, alpha_prev = 1.f;
+    float o[HD];
+#pragma unroll
+    for (int d = 0; d < HD; ++d) o[d] = 0.f;
+    bool ok = true;
+    auto fold_pv = [&](int jj) -> bool {
+      const int buf = jj & 1;
+      if (!mbar_wait(&pv_full[hl * 2 + buf], (jj >> 1) & 1, p.err, abort_flag)) return false;
+      tc_fence_after();
+      uint32_t pv[HD];
+      tmem_ld32(t_lane + 128 + buf * 64 + hl * HD, pv);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&pv_empty[hl * 2 + buf]);
+#pragma unroll
+      for (int d = 0; d < HD; ++d) o[d] = fmaf(o[d], alpha_prev, __uint_as_float(pv[d]));
+      return true;
+    };
+    for (int j = 0; j < n; ++j) {
+      const int t = t0 + j;
+      const int kbase = Lk - TILE * (t + 1);
+      if (!mbar_wait(&s_full[hl], j & 1, p.err, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sr[TILE];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(t_lane + c * 32, sr + c * 32);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[hl]);
+      const int lo = kst - kbase;                        // columns < lo are padding
+      const int hi = (p.causal && t == i) ? r : TILE - 1;  // columns > hi are in the future
+      if (lo > 0 || hi < TILE - 1) {
+#pragma unroll
+        for (int c = 0; c < TILE; ++c)
+          if (c < lo || c > hi) sr[c] = __float_as_uint(-CUDART_INF_F);
+      }
+      float mx = -CUDART_INF_F;
+#pragma unroll
+      for (int c = 0; c < TILE; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
+      const float m_new = fmaxf(m, mx * p.scale2);
+      const float m_use = m_new == -CUDART_INF_F ? 0.f : m_new;
+      const float alpha = ex2(m - m_use);
+      if (j > 0 && !mbar_wait(&p_empty[hl], (j - 1) & 1, p.err, abort_flag)) {
+        ok = false;
+        break;
+      }
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        float e[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          e[k] = ex2(fmaf(__uint_as_float(sr[c * 8 + k]), p.scale2, -m_use));
+          sum += e[k];
+        }
+        st_smem_v4(p_base + swz_off(r, c), pack2(e[0], e[1]), pack2(e[2], e[3]), pack2(e[4], e[5]),
+                   pack2(e[6], e[7]));
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[hl]);
+      l = fmaf(l, alpha, sum);
+      m = m_new;
+      if (j > 0 && !fold_pv(j - 1)) {
+        ok = false;
+        break;
+      }
+      alpha_prev = alpha;
+    }
+    if (ok && n > 0) ok = fold_pv(n - 1);
+    if (ok) {
+      const int qi = qrow - (Lk - p.Lq);
+      const int h = h0 + hl;
+      if (qi >= 0) {
+        const bool valid = qrow >= kst && l > 0.f;
+        const float inv = valid ? 1.f / l : 0.f;
+        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) +
+                                              (static_cast<long long>(b) * p.Lq + qi) * p.D + h * HD);
+#pragma unroll
+        for (int c = 0; c < HD / 8; ++c)
+          dst[c] = make_uint4(pack2(o[c * 8] * inv, o[c * 8 + 1] * inv), pack2(o[c * 8 + 2] * inv, o[c * 8 + 3] * inv),
+                              pack2(o[c * 8 + 4] * inv, o[c * 8 + 5] * inv), pack2(o[c * 8 + 6] * inv, o[c * 8 + 7] * inv));
+        p.lse[(static_cast<long long>(b) * p.H + h) * p.Lq + qi] = valid ? m + lg2(l) : CUDART_INF_F;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// ============================================================================ backward
+// D[b,h,q] = sum_d dO*O over the head; zero the dQ accumulator row.
+__global__ void __launch_bounds__(256) fmha_bwd_pre_kernel(const __nv_bfloat16* __restrict__ out,
+                                                           const __nv_bfloat16* __restrict__ dout,
+                                                           float* __restrict__ dsum, float* __restrict__ dq_acc,
+                                                           int B, int Lq, int H, int D) {
+  const long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= static_cast<long long>(B) * Lq) return;
+  const int b = static_cast<int>(row / Lq);
+  const int q = static_cast<int>(row - static_cast<long long>(b) * Lq);
+  for (int base = 0; base < D; base += 256) {  // warp-uniform trip count (shuffles below)
+    const int c = base + lane * 8;
+    const bool active = c < D;
+    float acc = 0.f;
+    if (active) {
+      const uint4 ov = *reinterpret_cast<const uint4*>(out + row * D + c);
+      const uint4 gv = *reinterpret_cast<const uint4*>(dout + row * D + c);
+      const uint32_t* o32 = reinterpret_cast<const uint32_t*>(&ov);
+      const uint32_t* g32 = reinterpret_cast<const uint32_t*>(&gv);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        acc = fmaf(bf16_bits_to_float(o32[k] & 0xFFFFu), bf16_bits_to_float(g32[k] & 0xFFFFu), acc);
+        acc = fmaf(bf16_bits_to_float(o32[k] >> 16), bf16_bits_to_float(g32[k] >> 16), acc);
+      }
+      *reinterpret_cast<float4*>(dq_acc + row * D + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+      *reinterpret_cast<float4*>(dq_acc + row * D + c + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    // four lanes hold one head (32 elements)
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    if (active && (lane & 3) == 0) dsum[(static_cast<long long>(b) * H + c / HD) * Lq + q] = acc;
+  }
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    fmha_bwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap tm_do,
+                    const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + TILE_BYTES;
+  uint8_t* sQ = sV + TILE_BYTES;        // [2]
+  uint8_t* sdO = sQ + 2 * TILE_BYTES;   // [2]
+  uint8_t* sPT = sdO + 2 * TILE_BYTES;
+  uint8_t* sdST = sPT + P_BYTES;
+  float* sLse = reinterpret_cast<float*>(sdST + P_BYTES);  // [2][128]
+  float* sDs = sLse + 2 * TILE;                            // [2][128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDs + 2 * TILE);
+  uint64_t* kv_full = bars;
+  uint64_t* qd_full = bars + 1;    // [2]
+  uint64_t* qd_empty = bars + 3;   // [2]
+  uint64_t* st_full = bars + 5;
+  uint64_t* st_empty = bars + 6;
+  uint64_t* pds_full = bars + 7;
+  uint64_t* pds_empty = bars + 8;
+  uint64_t* dq_full = bars + 9;
+  uint64_t* dq_empty = bars + 10;
+  uint64_t* dkv_full = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int Lk = p.Lk;
+  const int nkt = (Lk + TILE - 1) / TILE;
+  const int h = blockIdx.x % p.H;
+  const int rest = blockIdx.x / p.H;
+  const int b = rest % p.B;
+  const int t = nkt - 1 - rest / p.B;  // key tile; the oldest (most query tiles) launch first
+  const int kbase = Lk - TILE * (t + 1);
+  const int kst = min(max(p.kstart[b], 0), Lk);
+  const int qlo = max(kst, Lk - p.Lq);  // first row that is a query with a visible key
+  const int nq = (p.Lq + TILE - 1) / TILE;
+  int imax = p.causal ? min(t, nq - 1) : nq - 1;
+  imax = min(imax, (Lk - 1 - qlo) / TILE);
+  const int n = (kbase + TILE - 1 >= kst && qlo < Lk) ? max(0, imax + 1) : 0;  // query tiles visited
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&qd_full[s], 33);
+      mbar_init(&qd_empty[s], 1);
+    }
+    mbar_init(st_full, 1);
+    mbar_init(st_empty, 8);
+    mbar_init(pds_full, 8);
+    mbar_init(pds_empty, 1);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_empty, 8);
+    mbar_init(dkv_full, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (n > 0) {
+      if (lane == 0) {
+        tma_prefetch_desc(&tm);
+        tma_prefetch_desc(&tm_do);
+        mbar_arrive_expect_tx(kv_full, 2 * TILE_BYTES);
+        tma_load_3d(sK, &tm, kv_full, p.D + h * HD, kbase, b);
+        tma_load_3d(sV, &tm, kv_full, 2 * p.D + h * HD, kbase, b);
+      }
+      int issued = 0;
+      for (int j = 0; j < n; ++j) {
+        const int st = j & 1;
+        if (j >= 2 && !mbar_wait(&qd_empty[st], ((j >> 1) - 1) & 1, p.err, abort_flag)) break;
+        const int qrow0 = Lk - TILE * (j + 1);  // token row of query column 0
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&qd_full[st], 2 * TILE_BYTES);
+          tma_load_3d(sQ + st * TILE_BYTES, &tm, &qd_full[st], h * HD, qrow0, b);
+          tma_load_3d(sdO + st * TILE_BYTES, &tm_do, &qd_full[st], h * HD, qrow0 - (Lk - p.Lq), b);
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int c = lane * 4 + e;
+          const int qi = qrow0 + c - (Lk - p.Lq);
+          const bool real = qi >= 0 && qrow0 + c >= qlo;
+          const long long off = (static_cast<long long>(b) * p.H + h) * p.Lq + qi;
+          sLse[st * TILE + c] = real ? p.lse[off] : CUDART_INF_F;
+          sDs[st * TILE + c] = real ? p.dsum[off] : 0.f;
+        }
+        mbar_arrive(&qd_full[st]);
+        issued = j + 1;
+      }
+      if (lane == 0) {
+        mbar_wait(kv_full, 0, nullptr, nullptr);
+        for (int j = max(0, issued - 2); j < issued; ++j)
+          mbar_wait(&qd_full[j & 1], (j >> 1) & 1, nullptr, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && n > 0) {
+      constexpr uint32_t idesc_s = make_idesc_bf16(TILE, TILE, false, false);
+      constexpr uint32_t idesc_kv = make_idesc_bf16(TILE, 64, false, true);
+      constexpr uint32_t idesc_q = make_idesc_bf16(TILE, 64, true, true);
+      const uint32_t k_base = smem_u32(sK), v_base = smem_u32(sV);
+      const uint32_t pt_base = smem_u32(sPT), ds_base = smem_u32(sdST);
+      bool ok = mbar_wait(kv_full, 0, p.err, abort_flag);
+      for (int j = 0; j < n && ok; ++j) {
+        const int st = j & 1;
+        const uint32_t q_base = smem_u32(sQ + st * TILE_BYTES);
+        const uint32_t do_base = smem_u32(sdO + st * TILE_BYTES);
+        if (!mbar_wait(&qd_full[st], (j >> 1) & 1, p.err, abort_flag) ||
+            (j > 0 && !mbar_wait(st_empty, (j - 1) & 1, p.err, abort_flag)))
+          break;
+        tc_fence_after();
+        for (int ks = 0; ks < 2; ++ks) {
+          tc_mma_bf16(tmem, desc_k(k_base, ks * 32), desc_k(q_base, ks * 32), idesc_s, ks);
+          tc_mma_bf16(tmem + 128, desc_k(v_base, ks * 32), desc_k(do_base, ks * 32), idesc_s, ks);
+        }
+        tc_commit(st_full);
+        if (!mbar_wait(pds_full, j & 1, p.err, abort_flag)) break;
+        tc_fence_after();
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint32_t acc = (j > 0 || ks > 0) ? 1u : 0u;
+          tc_mma_bf16(tmem + 256, desc_k128(pt_base, ks), desc_mn(do_base, ks), idesc_kv, acc);
+          tc_mma_bf16(tmem + 320, desc_k128(ds_base, ks), desc_mn(q_base, ks), idesc_kv, acc);
+        }
+        if (j > 0 && !mbar_wait(dq_empty, (j - 1) & 1, p.err, abort_flag)) break;
+        tc_fence_after();
+        for (int ks = 0; ks < 8; ++ks)
+          tc_mma_bf16(tmem + 384, desc_mn(ds_base, ks), desc_mn(k_base, ks), idesc_q, ks);
+        tc_commit(dq_full);
+        tc_commit(pds_empty);
+        tc_commit(&qd_empty[st]);
+      }
+      tc_commit(dkv_full);
+      mbar_wait(dkv_full, 0, nullptr, nullptr);
+    }
+  } else {
+    // ------------------------------------------------------------ compute
+    const int wg = (warp - 2) >> 2;  // query columns [64*wg, 64*wg + 64)
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int krow = kbase + r;
+    const bool key_ok = krow >= kst;
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const uint32_t pt_base = smem_u32(sPT), ds_base = smem_u32(sdST);
+    bool ok = true;
+    auto drain_dq = [&](int jj) -> bool {
+      if (!mbar_wait(dq_full, jj & 1, p.err, abort_flag)) return false;
+      tc_fence_after();
+      uint32_t g[16];
+      tmem_ld16(t_lane + 384 + wg * 16, g);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_empty);
+      const int qrow = Lk - TILE * (jj + 1) + r;  // TMEM lane = query column of tile jj
+      if (qrow >= qlo) {
+        float* dst = p.dq_acc + (static_cast<long long>(b) * p.Lq + (qrow - (Lk - p.Lq))) * p.D + h * HD + wg * 16;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          red_add_v4(dst + c * 4, __uint_as_float(g[c * 4]), __uint_as_float(g[c * 4 + 1]),
+                     __uint_as_float(g[c * 4 + 2]), __uint_as_float(g[c * 4 + 3]));
+      }
+      return true;
+    };
+    for (int j = 0; j < n; ++j) {
+      const int st = j & 1;
+      const int qrow0 = Lk - TILE * (j + 1);
+      if (!mbar_wait(&qd_full[st], (j >> 1) & 1, p.err, abort_flag) ||
+          !mbar_wait(st_full, j & 1, p.err, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t s[64], dp[64];
+      tmem_ld32(t_lane + wg * 64, s);
+      tmem_ld32(t_lane + wg * 64 + 32, s + 32);
+      tmem_ld32(t_lane + 128 + wg * 64, dp);
+      tmem_ld32(t_lane + 128 + wg * 64 + 32, dp + 32);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(st_empty);
+      if (j > 0 && !mbar_wait(pds_empty, (j - 1) & 1, p.err, abort_flag)) {
+        ok = false;
+        break;
+      }
+      const float* lse = sLse + st * TILE + wg * 64;
+      const float* dsv = sDs + st * TILE + wg * 64;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        float pe[8], de[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int qc = c * 8 + k;
+          const int qrow = qrow0 + wg * 64 + qc;
+          const bool vis = key_ok && (!p.causal || krow <= qrow);
+          const float pv = vis ? ex2(fmaf(__uint_as_float(s[qc]), p.scale2, -lse[qc])) : 0.f;
+          pe[k] = pv;
+          de[k] = pv * (__uint_as_float(dp[qc]) - dsv[qc]) * p.scale;
+        }
+        const uint32_t off = swz_off(r, wg * 8 + c);
+        st_smem_v4(pt_base + off, pack2(pe[0], pe[1]), pack2(pe[2], pe[3]), pack2(pe[4], pe[5]), pack2(pe[6], pe[7]));
+        st_smem_v4(ds_base + off, pack2(de[0], de[1]), pack2(de[2], de[3]), pack2(de[4], de[5]), pack2(de[6], de[7]));
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pds_full);
+      if (j > 0 && !drain_dq(j - 1)) {
+        ok = false;
+        break;
+      }
+    }
+    if (ok && n > 0) ok = drain_dq(n - 1);
+    // dK (warpgroup 1) and dV (warpgroup 0) of this key tile
+    if (ok && krow >= 0) {
+      float g[HD];
+      if (n > 0) {
+        if (!mbar_wait(dkv_full, 0, p.err, abort_flag)) {
+          ok = false;
+        } else {
+          tc_fence_after();
+          uint32_t gr[HD];
+          tmem_ld32(t_lane + (wg == 0 ? 256 : 320), gr);
+          tmem_wait_ld();
+#pragma unroll
+          for (int d = 0; d < HD; ++d) g[d] = key_ok ? __uint_as_float(gr[d]) : 0.f;
+        }
+      } else {
+#pragma unroll
+        for (int d = 0; d < HD; ++d) g[d] = 0.f;
+      }
+      if (ok) {
+        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.dqkv) +
+                                              (static_cast<long long>(b) * Lk + krow) * 3 * p.D +
+                                              (wg == 0 ? 2 * p.D : p.D) + h * HD);
+#pragma unroll
+        for (int c = 0; c < HD / 8; ++c)
+          dst[c] = make_uint4(pack2(g[c * 8], g[c * 8 + 1]), pack2(g[c * 8 + 2], g[c * 8 + 3]),
+                              pack2(g[c * 8 + 4], g[c * 8 + 5]), pack2(g[c * 8 + 6], g[c * 8 + 7]));
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// dqkv[:, :, 0:D] = bf16(dQ) on query rows, 0 elsewhere (8 elements per thread).
+__global__ void __launch_bounds__(256) fmha_bwd_post_kernel(const float* __restrict__ dq_acc,
+                                                            __nv_bfloat16* __restrict__ dqkv, int B, int Lk,
+                                                            int Lq, int D) {
+  const long long idx = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
+  const long long total = static_cast<long long>(B) * Lk * D;
+  if (idx >= total) return;
+  const long long row = idx / D;
+  const int c = static_cast<int>(idx - row * D);
+  const int b = static_cast<int>(row / Lk);
+  const int k = static_cast<int>(row - static_cast<long long>(b) * Lk);
+  const int qi = k - (Lk - Lq);
+  uint4 v = make_uint4(0u, 0u, 0u, 0u);
+  if (qi >= 0) {
+    const float* src = dq_acc + (static_cast<long long>(b) * Lq + qi) * D + c;
+    const float4 a = *reinterpret_cast<const float4*>(src);
+    const float4 e = *reinterpret_cast<const float4*>(src + 4);
+    v = make_uint4(pack2(a.x, a.y), pack2(a.z, a.w), pack2(e.x, e.y), pack2(e.z, e.w));
+  }
+  *reinterpret_cast<uint4*>(dqkv + row * 3 * D + c) = v;
+}
+
+// ------------------------------------------------------------------ host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// [B, L, W] bf16 rows (row stride W), box 64 x 128 x 1, 128-byte swizzle.
+bool encode_rows(CUtensorMap* map, const void* base, uint64_t W, uint64_t L, uint64_t B) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[3] = {W, L, B};
+  cuuint64_t strides[2] = {W * 2, L * W * 2};
+  cuuint32_t box[3] = {64, TILE, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+Params make_params(const FmhaArgs& a) {
+  Params p;
+  p.out = a.out;
+  p.lse = a.lse;
+  p.kstart = a.kstart;
+  p.dq_acc = a.dq_acc;
+  p.dsum = a.dsum;
+  p.dqkv = a.dqkv;
+  p.B = a.B;
+  p.H = a.H;
+  p.Lk = a.Lk;
+  p.Lq = a.Lq;
+  p.D = a.H * HD;
+  p.causal = a.causal ? 1 : 0;
+  p.scale = a.scale > 0.f ? a.scale : 1.f / sqrtf(static_cast<float>(HD));
+  p.scale2 = p.scale * kLog2e;
+  p.err = a.err;
+  return p;
+}
+
+bool shapes_ok(const FmhaArgs& a) {
+  return a.hd == HD && a.B > 0 && a.H > 0 && a.Lq > 0 && a.Lq <= a.Lk && a.kstart != nullptr &&
+         (reinterpret_cast<uintptr_t>(a.qkv) & 15) == 0;
+}
+
+}  // namespace
+
+cudaError_t fmha_fwd(const FmhaArgs& a, cudaStream_t stream) {
+  if (!shapes_ok(a) || (a.H & 1) || a.out == nullptr || a.lse == nullptr ||
+      (reinterpret_cast<uintptr_t>(a.out) & 15))
+    return cudaErrorInvalidValue;
+  const Params p = make_params(a);
+  CUtensorMap tm;
+  if (!encode_rows(&tm, a.qkv, 3ull * p.D, a.Lk, a.B)) return cudaErrorInvalidValue;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(fmha_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, F_SMEM);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  const long long grid = static_cast<long long>(a.H / 2) * a.B * ((a.Lq + TILE - 1) / TILE);
+  if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
+  fmha_fwd_kernel<<<static_cast<unsigned>(grid), NUM_THREADS, F_SMEM, stream>>>(tm, p);
+  return cudaGetLastError();
+}
+
+cudaError_t fmha_bwd(const FmhaArgs& a, cudaStream_t stream) {
+  if (!shapes_ok(a) || a.out == nullptr || a.lse == nullptr || a.dout == nullptr || a.dqkv == nullptr ||
+      a.dq_acc == nullptr || a.dsum == nullptr || (reinterpret_cast<uintptr_t>(a.dout) & 15) ||
+      (reinterpret_cast<uintptr_t>(a.dqkv) & 15) || (reinterpret_cast<uintptr_t>(a.dq_acc) & 15))
+    return cudaErrorInvalidValue;
+  const Params p = make_params(a);
+  CUtensorMap tm, tm_do;
+  if (!encode_rows(&tm, a.qkv, 3ull * p.D, a.Lk, a.B) || !encode_rows(&tm_do, a.dout, p.D, a.Lq, a.B))
+    return cudaErrorInvalidValue;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(fmha_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, B_SMEM);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  const long long rows = static_cast<long long>(a.B) * a.Lq;
+  fmha_bwd_pre_kernel<<<static_cast<unsigned>((rows * 32 + 255) / 256), 256, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(a.out), reinterpret_cast<const __nv_bfloat16*>(a.dout), a.dsum,
+      a.dq_acc, a.B, a.Lq, a.H, p.D);
+  const long long grid = static_cast<long long>(a.H) * a.B * ((a.Lk + TILE - 1) / TILE);
+  fmha_bwd_kernel<<<static_cast<unsigned>(grid), NUM_THREADS, B_SMEM, stream>>>(tm, tm_do, p);
+  const long long vec = static_cast<long long>(a.B) * a.Lk * p.D / 8;
+  fmha_bwd_post_kernel<<<static_cast<unsigned>((vec + 255) / 256), 256, 0, stream>>>(
+      a.dq_acc, reinterpret_cast<__nv_bfloat16*>(a.dqkv), a.B, a.Lk, a.Lq, p.D);
+  return cudaGetLastError();
+}
+
+}  // namespace mdl

@@ -1,0 +1,42 @@
+// Host interface of the tcgen05 flash attention used by the OneTrans and
+// LONGER backbones.
+#pragma once
+
+#include <cuda_runtime.h>
+
+namespace mdl {
+
+// Multi-head attention of a query SUFFIX over the keys of the same token
+// sequence, with bottom-right causality and a per-sample valid-key start
+// (reference MixedCausalAttention.attend_causal_suffix src/model.py:5617-5695
+// over flash_attn_varlen_func):
+//
+//   qkv   [B, Lk, 3*D] bf16: per token Q | K | V, D = H * 32 (head h at h*32)
+//   the queries are the last Lq tokens (rows Lk-Lq .. Lk-1) of each sample
+//   key j is visible to query row p iff kstart[b] <= j and (!causal or j <= p)
+//   out   [B, Lq, D] bf16, rows whose query has no visible key are zero
+//   lse   [B, H, Lq] fp32: base-2 log-sum-exp of the scaled scores (+inf for
+//         rows without a visible key), saved for the backward
+//
+// Backward: dqkv [B, Lk, 3*D] bf16 (every element written; Q rows that are not
+// queries get zero), workspaces dq_acc fp32 [B, Lq, D] and dsum fp32 [B, H, Lq].
+// head_dim is 32; H must be even for the forward (two heads per CTA).
+struct FmhaArgs {
+  const void* qkv = nullptr;
+  void* out = nullptr;
+  float* lse = nullptr;
+  const int* kstart = nullptr;  // int32 [B]
+  const void* dout = nullptr;   // bf16 [B, Lq, D]
+  void* dqkv = nullptr;
+  float* dq_acc = nullptr;
+  float* dsum = nullptr;
+  int B = 0, H = 0, Lk = 0, Lq = 0, hd = 32;
+  bool causal = true;
+  float scale = 0.f;            // softmax scale (1/sqrt(hd) when 0)
+  int* err = nullptr;
+};
+
+cudaError_t fmha_fwd(const FmhaArgs& a, cudaStream_t stream);
+cudaError_t fmha_bwd(const FmhaArgs& a, cudaStream_t stream);
+
+}  // namespace mdl

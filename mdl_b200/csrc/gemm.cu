@@ -61,6 +61,8 @@ struct EpiParams {
   int act;
   float alpha;
   int M, N, K, G;
+  int KG;                  // K-range groups (G == 1 when KG > 1)
+  int a_shared, b_shared;  // operand shared by every group (batch stride 0)
   int* err;
 };
 
@@ -72,7 +74,7 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
 // Epilogue kinds (compile-time, so each instantiation carries only its own path).
 constexpr int EPI_PLAIN = 0;     // bf16 out, optional bias / ReLU / column sums
 constexpr int EPI_GELU = 1;      // bf16 pre-activation (or GELU'(pre)) + bf16 GELU(pre)
-constexpr int EPI_AUX = 2;       // bf16 out scaled by GELU'(aux), ReLU'(aux) or aux; optional column sums
+constexpr int EPI_AUX = 2;       // bf16 out scaled by GELU'(aux), ReLU'(aux) or aux, or plus aux; optional column sums
 constexpr int EPI_ACC_BF16 = 3;  // bf16 out += result
 constexpr int EPI_F32 = 4;       // fp32 out (= or +=)
 
@@ -100,7 +102,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int n_tiles = (ep.N + BN - 1) / BN;
   const int tiles_per_group = m_tiles * n_tiles;
   const int num_tiles = tiles_per_group * ep.G;
-  const int k_blocks = (ep.K + BK - 1) / BK;
+  const int kb_per_range = (ep.K + BK - 1) / BK;
+  const int k_blocks = kb_per_range * ep.KG;
 
   if (threadIdx.x == 0) {
 #pragma unroll
@@ -143,22 +146,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             break;
           }
           mbar_arrive_expect_tx(&full[stage], A_STAGE_BYTES + B_STAGE_BYTES);
-          const int k0 = kb * BK;
+          // third map coordinate: the batch group, or the K range when KG > 1
+          const int kr = ep.KG > 1 ? kb / kb_per_range : 0;
+          const int k0 = (kb - kr * kb_per_range) * BK;
+          const int za = ep.KG > 1 ? kr : (ep.a_shared ? 0 : g);
+          const int zb = ep.KG > 1 ? kr : (ep.b_shared ? 0 : g);
           uint8_t* a_dst = sA + stage * A_STAGE_BYTES;
           uint8_t* b_dst = sB + stage * B_STAGE_BYTES;
           if (!A_MN) {
-            tma_load_3d(a_dst, &tmA, &full[stage], k0, mb * BM, g);
+            tma_load_3d(a_dst, &tmA, &full[stage], k0, mb * BM, za);
           } else {
 #pragma unroll
             for (int c = 0; c < BM / 64; ++c)
-              tma_load_3d(a_dst + c * MN_CHUNK_BYTES, &tmA, &full[stage], mb * BM + c * 64, k0, g);
+              tma_load_3d(a_dst + c * MN_CHUNK_BYTES, &tmA, &full[stage], mb * BM + c * 64, k0, za);
           }
           if (!B_MN) {
-            tma_load_3d(b_dst, &tmB, &full[stage], k0, nb * BN, g);
+            tma_load_3d(b_dst, &tmB, &full[stage], k0, nb * BN, zb);
           } else {
 #pragma unroll
             for (int c = 0; c < BN / 64; ++c)
-              tma_load_3d(b_dst + c * MN_CHUNK_BYTES, &tmB, &full[stage], nb * BN + c * 64, k0, g);
+              tma_load_3d(b_dst + c * MN_CHUNK_BYTES, &tmB, &full[stage], nb * BN + c * 64, k0, zb);
           }
           ++issued;
           if (++stage == STAGES) {
@@ -333,6 +340,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             if (ep.act == GEMM_ACT_DMUL) {
 #pragma unroll
               for (int e = 0; e < 4; ++e) t[e] *= bf16_bits_to_float(abits[e]);
+            } else if (ep.act == GEMM_ACT_ADD) {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) t[e] += bf16_bits_to_float(abits[e]);
             } else if (ep.act == GEMM_ACT_DGELU) {
 #pragma unroll
               for (int e = 0; e < 4; ++e) t[e] *= gelu_grad_fast(bf16_bits_to_float(abits[e]));
@@ -518,7 +528,8 @@ cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const EpiParams
 
 // Epilogue kind of a call; -1 for a combination no kernel implements.
 int epilogue_kind(const GemmArgs& a) {
-  const bool aux_act = a.act == GEMM_ACT_DGELU || a.act == GEMM_ACT_DRELU || a.act == GEMM_ACT_DMUL;
+  const bool aux_act =
+      a.act == GEMM_ACT_DGELU || a.act == GEMM_ACT_DRELU || a.act == GEMM_ACT_DMUL || a.act == GEMM_ACT_ADD;
   if (a.out_fp32) return (a.act == GEMM_ACT_NONE && a.out2 == nullptr && a.colsum == nullptr) ? EPI_F32 : -1;
   if (a.act == GEMM_ACT_GELU || a.act == GEMM_ACT_GELU_GRAD)
     return (!a.accumulate && a.out2 != nullptr) ? EPI_GELU : -1;
@@ -530,7 +541,9 @@ int epilogue_kind(const GemmArgs& a) {
 }  // namespace
 
 cudaError_t gemm_bf16_tcgen05(const GemmArgs& a, cudaStream_t stream) {
-  if (a.M <= 0 || a.N <= 0 || a.K <= 0 || a.G <= 0) return cudaSuccess;
+  if (a.M <= 0 || a.N <= 0 || a.K <= 0 || a.G <= 0 || a.KG <= 0) return cudaSuccess;
+  if (a.KG > 1 && (a.G != 1 || (a.ksA % 8) || (a.ksB % 8) || a.ksA <= 0 || a.ksB <= 0))
+    return cudaErrorInvalidValue;
   if ((a.lda % 8) || (a.ldb % 8) || (a.G > 1 && ((a.gsA % 8) || (a.gsB % 8))) ||
       (reinterpret_cast<uintptr_t>(a.A) & 15) || (reinterpret_cast<uintptr_t>(a.B) & 15))
     return cudaErrorInvalidValue;
@@ -546,15 +559,22 @@ cudaError_t gemm_bf16_tcgen05(const GemmArgs& a, cudaStream_t stream) {
   if (epi < 0) return cudaErrorInvalidValue;
   CUtensorMap ta, tb;
   bool ok;
+  // third map dimension: K ranges (KG > 1), batch groups, or 1 for a shared operand
+  const bool a_shared = a.G > 1 && a.gsA == 0;
+  const bool b_shared = a.G > 1 && a.gsB == 0;
+  const uint64_t za = a.KG > 1 ? a.KG : (a_shared ? 1 : a.G);
+  const uint64_t zb = a.KG > 1 ? a.KG : (b_shared ? 1 : a.G);
+  const long long sa = a.KG > 1 ? a.ksA : a.gsA;
+  const long long sb = a.KG > 1 ? a.ksB : a.gsB;
   if (!a.a_mn_major)
-    ok = encode_map(&ta, a.A, a.K, a.M, a.G, a.lda, a.gsA, BM);
+    ok = encode_map(&ta, a.A, a.K, a.M, za, a.lda, sa, BM);
   else
-    ok = encode_map(&ta, a.A, a.M, a.K, a.G, a.lda, a.gsA, BK);
+    ok = encode_map(&ta, a.A, a.M, a.K, za, a.lda, sa, BK);
   if (!ok) return cudaErrorInvalidValue;
   if (!a.b_mn_major)
-    ok = encode_map(&tb, a.B, a.K, a.N, a.G, a.ldb, a.gsB, BN);
+    ok = encode_map(&tb, a.B, a.K, a.N, zb, a.ldb, sb, BN);
   else
-    ok = encode_map(&tb, a.B, a.N, a.K, a.G, a.ldb, a.gsB, BK);
+    ok = encode_map(&tb, a.B, a.N, a.K, zb, a.ldb, sb, BK);
   if (!ok) return cudaErrorInvalidValue;
 
   EpiParams ep;
@@ -577,6 +597,9 @@ cudaError_t gemm_bf16_tcgen05(const GemmArgs& a, cudaStream_t stream) {
   ep.N = a.N;
   ep.K = a.K;
   ep.G = a.G;
+  ep.KG = a.KG;
+  ep.a_shared = a_shared ? 1 : 0;
+  ep.b_shared = b_shared ? 1 : 0;
   ep.err = a.err;
   const long long tiles =
       static_cast<long long>((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN) * static_cast<long long>(a.G);

@@ -16,6 +16,7 @@ enum GemmAct : int {
   // GELU pair that saves the derivative instead of the pre-activation:
   GEMM_ACT_GELU_GRAD = 5,  // x = bf16(acc): out = gelu'(x), out2 = gelu(x)
   GEMM_ACT_DMUL = 6,       // out = acc * aux (aux = the saved derivative)
+  GEMM_ACT_ADD = 7,        // out = acc + aux (a fused residual add)
 };
 
 // C[g] = epilogue(alpha * A[g] @ B[g]^T) for g in [0, G).
@@ -24,6 +25,11 @@ enum GemmAct : int {
 //   B[g] is N x K: K-major -> B[n,k] at B + g*gsB + n*ldb + k
 //                  MN-major -> B[n,k] at B + g*gsB + k*ldb + n
 //   C[g] is M x N row-major: C[m,n] at out + g*gsC + m*ldc + n
+// A batch stride of 0 with G > 1 shares that operand across the batch (one
+// weight applied to every group). KG > 1 (with G == 1) sums KG products whose
+// K ranges lie ksA / ksB elements apart: C = sum_j A_j @ B_j^T, each A_j, B_j
+// of depth K (rows past K inside a range read as zeros), which is the weight
+// gradient of a weight shared by rows that are not uniformly strided.
 // A and B are bf16; C is bf16 or fp32. All leading dimensions and batch
 // strides must be multiples of 8 elements (16 bytes) and the base pointers
 // 16-byte aligned (TMA rule).
@@ -35,6 +41,8 @@ struct GemmArgs {
   long long ldb = 0, gsB = 0;
   bool b_mn_major = false;
   int M = 0, N = 0, K = 0, G = 1;
+  int KG = 1;                       // K-range groups summed into one output
+  long long ksA = 0, ksB = 0;       // element distance between K ranges
   // epilogue
   void* out = nullptr;
   long long ldc = 0, gsC = 0;

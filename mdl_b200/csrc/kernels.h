@@ -4,6 +4,7 @@
 #include "attention.h"
 #include "comm.h"
 #include "embedding.h"
+#include "fmha.h"
 #include "gemm.h"
 #include "misc.h"
 #include "norm.h"

@@ -56,7 +56,7 @@ __global__ void token_mean_kernel(const __nv_bfloat16* x, __nv_bfloat16* out, in
 
 // grid (ceil(N/256), G, splits); each thread sums a strided range of rows for one column
 __global__ void colsum_kernel(const __nv_bfloat16* x, float* out, long long M, int N, long long ld, long long gs,
-                              float scale) {
+                              long long gs_out, float scale) {
   const int n = blockIdx.x * blockDim.x + threadIdx.x;
   const int g = blockIdx.y;
   if (n >= N) return;
@@ -66,7 +66,7 @@ __global__ void colsum_kernel(const __nv_bfloat16* x, float* out, long long M, i
   const __nv_bfloat16* p = x + g * gs + n;
   float s = 0.f;
   for (long long m = m0; m < m1; ++m) s += __bfloat162float(p[m * ld]);
-  atomicAdd(out + static_cast<long long>(g) * N + n, s * scale);
+  atomicAdd(out + g * gs_out + n, s * scale);
 }
 
 // One warp per (b, task); H % 256 == 0 handled by 8-wide chunks per lane.
@@ -230,6 +230,78 @@ int grid_for(long long n) {
 
 }  // namespace
 
+__global__ void __launch_bounds__(256) position_add_kernel(__nv_bfloat16* x, const float* __restrict__ pos,
+                                                           const int* __restrict__ kstart, int B, int L, int D) {
+  const long long i = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
+  if (i >= static_cast<long long>(B) * L * D) return;
+  const long long row = i / D;
+  const int c = static_cast<int>(i - row * D);
+  const int b = static_cast<int>(row / L);
+  const int p = static_cast<int>(row - static_cast<long long>(b) * L) - kstart[b];
+  if (p < 0) return;
+  uint4* xp = reinterpret_cast<uint4*>(x + i);
+  uint4 v = *xp;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&v);
+  const float4 a = *reinterpret_cast<const float4*>(pos + static_cast<long long>(p) * D + c);
+  const float4 e = *reinterpret_cast<const float4*>(pos + static_cast<long long>(p) * D + c + 4);
+  const float add[8] = {a.x, a.y, a.z, a.w, e.x, e.y, e.z, e.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 f = __bfloat1622float2(h[k]);
+    h[k] = __floats2bfloat162_rn(f.x + add[2 * k], f.y + add[2 * k + 1]);
+  }
+  *xp = v;
+}
+
+// grid: (positions x D/8 threads, sample chunks); each thread sums its chunk of samples.
+constexpr int kPosChunk = 64;
+__global__ void __launch_bounds__(256) position_grad_kernel(const __nv_bfloat16* __restrict__ dx, float* dpos,
+                                                            const int* __restrict__ kstart, int B, int L, int D) {
+  const long long i = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
+  if (i >= static_cast<long long>(L) * D) return;
+  const int p = static_cast<int>(i / D);
+  const int c = static_cast<int>(i - static_cast<long long>(p) * D);
+  const int b0 = blockIdx.y * kPosChunk;
+  const int b1 = min(B, b0 + kPosChunk);
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  bool any = false;
+  for (int b = b0; b < b1; ++b) {
+    const int e = kstart[b] + p;
+    if (e >= L) continue;
+    any = true;
+    const uint4 v = *reinterpret_cast<const uint4*>(dx + (static_cast<long long>(b) * L + e) * D + c);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = __bfloat1622float2(h[k]);
+      acc[2 * k] += f.x;
+      acc[2 * k + 1] += f.y;
+    }
+  }
+  if (!any) return;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) atomicAdd(dpos + i + k, acc[k]);
+}
+
+cudaError_t position_add(void* x, const float* pos, const int* kstart, int B, int L, int D, cudaStream_t stream) {
+  if (D % 8 || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(pos) & 15))
+    return cudaErrorInvalidValue;
+  const long long vec = static_cast<long long>(B) * L * D / 8;
+  if (vec == 0) return cudaSuccess;
+  position_add_kernel<<<static_cast<unsigned>((vec + 255) / 256), 256, 0, stream>>>(
+      reinterpret_cast<__nv_bfloat16*>(x), pos, kstart, B, L, D);
+  return cudaGetLastError();
+}
+
+cudaError_t position_grad(const void* dx, float* dpos, const int* kstart, int B, int L, int D, cudaStream_t stream) {
+  if (D % 8 || (reinterpret_cast<uintptr_t>(dx) & 15)) return cudaErrorInvalidValue;
+  const long long vec = static_cast<long long>(L) * D / 8;
+  if (vec == 0 || B == 0) return cudaSuccess;
+  dim3 grid(static_cast<unsigned>((vec + 255) / 256), static_cast<unsigned>((B + kPosChunk - 1) / kPosChunk));
+  position_grad_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(dx), dpos, kstart, B, L, D);
+  return cudaGetLastError();
+}
+
 cudaError_t token_mean_fwd(const void* x, void* out, int B, int T, int D, cudaStream_t stream) {
   if (D % 8) return cudaErrorInvalidValue;
   const long long n = static_cast<long long>(B) * (D / 8);
@@ -240,7 +312,7 @@ cudaError_t token_mean_fwd(const void* x, void* out, int B, int T, int D, cudaSt
 }
 
 cudaError_t colsum_bf16(const void* x, float* out, int G, long long M, int N, long long ld, long long gs, float scale,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, long long gs_out) {
   if (G <= 0 || M <= 0 || N <= 0) return cudaSuccess;
   const int bx = (N + 255) / 256;
   long long splits = (static_cast<long long>(sms()) * 4) / (static_cast<long long>(bx) * G);
@@ -248,7 +320,8 @@ cudaError_t colsum_bf16(const void* x, float* out, int G, long long M, int N, lo
   if (splits > M) splits = M;
   if (splits > 65535) splits = 65535;
   dim3 grid(bx, G, static_cast<unsigned>(splits));
-  colsum_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(x), out, M, N, ld, gs, scale);
+  colsum_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(x), out, M, N, ld, gs,
+                                          gs_out < 0 ? N : gs_out, scale);
   return cudaGetLastError();
 }
 

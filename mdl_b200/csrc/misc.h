@@ -10,8 +10,17 @@ namespace mdl {
 cudaError_t token_mean_fwd(const void* x, void* out, int B, int T, int D, cudaStream_t stream);
 
 // out[g, n] += scale * sum_m x[g*gs + m*ld + n]  (bf16 x, fp32 out)
+// gs_out: element distance between the outputs of consecutive groups (-1: N;
+// 0: every group adds into the same N sums).
 cudaError_t colsum_bf16(const void* x, float* out, int G, long long M, int N, long long ld, long long gs,
-                        float scale, cudaStream_t stream);
+                        float scale, cudaStream_t stream, long long gs_out = -1);
+
+// Learned absolute positions over a prefix-padded token sequence (reference
+// OneTransBackbone._add_unified_position_embeddings src/model.py:6151-6179):
+//   x[b, e, :] += pos[e - kstart[b], :] for e >= kstart[b]      (bf16 x [B, L, D], fp32 pos)
+// and its gradient dpos[p, :] += sum_b dx[b, kstart[b] + p, :]. D % 8 == 0.
+cudaError_t position_add(void* x, const float* pos, const int* kstart, int B, int L, int D, cudaStream_t stream);
+cudaError_t position_grad(const void* dx, float* dpos, const int* kstart, int B, int L, int D, cudaStream_t stream);
 
 // Task heads, last layer + BCE (reference TaskHead src/model.py:869-882 and
 // _loss_terms_from_batch src/train.py:5890-6031), one launch for all tasks:

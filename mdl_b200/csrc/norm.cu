@@ -364,6 +364,16 @@ __global__ void __launch_bounds__(256) rms_bwd_kernel(const RMSArgs p) {
     }
     s = warp_sum(s) / p.D;
     auto* dx = reinterpret_cast<__nv_bfloat16*>(p.dx) + r * p.D;
+    const __nv_bfloat16* res = nullptr;
+    if (p.dres != nullptr) {
+      long long rr = r;
+      if (p.res_period > 0) {
+        const long long smp = r / p.res_period;
+        const int e = static_cast<int>(r - smp * p.res_period) - (p.res_period - p.res_tail);
+        rr = e >= 0 ? smp * p.res_tail + e : -1;
+      }
+      if (rr >= 0) res = reinterpret_cast<const __nv_bfloat16*>(p.dres) + rr * p.D;
+    }
 #pragma unroll
     for (int k = 0; k < NCH; ++k) {
       const int c = (lane + 32 * k) * 8;
@@ -372,6 +382,12 @@ __global__ void __launch_bounds__(256) rms_bwd_kernel(const RMSArgs p) {
         load_f8(p.weight, c, w, 1.f);
 #pragma unroll
         for (int e = 0; e < 8; ++e) o[e] = rstd * (gv[k][e] * w[e] - xv[k][e] * rstd * rstd * s);
+        if (res != nullptr) {
+          float rv[8];
+          load8(res + c, rv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o[e] += rv[e];
+        }
         store8(dx + c, o);
       }
     }

@@ -59,6 +59,11 @@ struct RMSArgs {
   const void* dy = nullptr;
   void* dx = nullptr;
   float* dweight = nullptr;  // fp32 [D] (+=)
+  // optional residual gradient added to dx: rows come in samples of res_period
+  // rows; the last res_tail rows of each sample add dres row (sample * res_tail
+  // + row - (res_period - res_tail)). res_period == 0: dres has dx's layout.
+  const void* dres = nullptr;
+  int res_period = 0, res_tail = 0;
   long long rows = 0;
   int D = 0;
   float eps = 1e-6f;

@@ -129,4 +129,12 @@ def scaled_config(n: int, scale: float, **kw) -> tuple[dict, SyntheticSpec]:
             enc["max_id"] = max(16, int(enc["max_id"] * scale))
     for name, fs in spec.fields.items():
         fs.vocab = max(16, int(fs.vocab * scale))
+    for seq in m.get("sequences", []):
+        for fl in seq.get("fields", []):
+            enc = fl.get("encoding")
+            if enc and enc.get("max_id"):
+                enc["max_id"] = max(16, int(enc["max_id"] * scale))
+    for ss in (spec.sequences or {}).values():
+        for fs in ss.fields.values():
+            fs.vocab = max(16, int(fs.vocab * scale))
     return m, spec

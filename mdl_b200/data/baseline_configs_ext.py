@@ -1,5 +1,16 @@
 """Benchmark workloads 3-5 (MDL, OneTrans, LONGER/STCA) as reference-schema configs.
 
+Workload 4, OneTrans:
+
+* one behaviour sequence of 512 events (``behavior``): item id Zipf over 1e7
+  plus 4 side ids over 1e5, all embedding dim 64, fused into S tokens by a
+  320 -> 1024 -> 256 projection MLP (one sequence group, so no SEP token);
+* 32 NS tokens from the 300 fields + 64 dense features of workload 2
+  (``auto_split``: one MLP from the concatenated inputs to 32 x 256);
+* d=256, 8 heads (head_dim 32), FFN 1024, 6 layers, causal attention, pyramid
+  that halves the queried S tokens every 2 layers (512, 256, 256, 128, 128, 64);
+* one click head (hidden 1024) at positive rate 0.05; batch 1024 per GPU, bf16.
+
 Workload 3, MDL on the RankMixer backbone of workload 2:
 
 * the 300 fields + 64 dense features of workload 2 form the feature tokens
@@ -20,7 +31,7 @@ from __future__ import annotations
 import copy
 
 from .baseline_configs import _config2_features, _rankmixer_common
-from .synthetic import FieldSpec, SyntheticSpec
+from .synthetic import FieldSpec, SequenceSpec, SyntheticSpec
 
 MDL_TASKS = {"click": 0.08, "like": 0.02, "finish": 0.3}
 MDL_SCENES = 5
@@ -62,7 +73,42 @@ def config3(num_fields: int = 300, batch: int = 2048, tokens_per_scenario: int =
     return m, spec
 
 
+def config4(num_fields: int = 300, batch: int = 1024, seq_len: int = 512, side_fields: int = 4,
+            item_vocab: int = 10_000_000, side_vocab: int = 100_000, num_layers: int = 6,
+            pyramid_schedule: str = "halve") -> tuple[dict, SyntheticSpec]:
+    tasks = {"click": 0.05}
+    m = _rankmixer_common("onetrans", tasks, batch, "bf16", "cuda")
+    feats, fields = _config2_features(num_fields)
+    m["features"] = copy.deepcopy(feats)
+    seq_fields = [{"name": "item_id", "kind": "categorical", "source": "behavior_item_id", "embedding_dim": 64,
+                   "encoding": {"type": "identity", "max_id": item_vocab}}]
+    seq_fields += [{"name": f"side{k}", "kind": "categorical", "source": f"behavior_side{k}", "embedding_dim": 64,
+                    "encoding": {"type": "identity", "max_id": side_vocab}} for k in range(side_fields)]
+    m["sequences"] = [{"name": "behavior", "fields": seq_fields, "max_length": seq_len, "encoder": "raw",
+                       "sequence_order": "oldest_to_newest", "truncation": "tail"}]
+    m["tokenization"] = {"feature_tokenizer": "auto_split", "num_feature_tokens": 32,
+                         "sequence_tokens": [{"name": "behavior", "inputs": ["behavior"]}]}
+    m["model"].update({"embedding_dim": 64, "token_dim": 256, "num_layers": num_layers, "num_heads": 8,
+                       "hidden_dim": 1024, "task_head_hidden_dim": 1024, "ffn_activation": "gelu",
+                       "ns_tokenizer": "auto_split", "num_ns_tokens": 32, "use_pyramid": True,
+                       "pyramid_schedule": pyramid_schedule, "pyramid_halve_every": 2, "pyramid_round_to": 32,
+                       "use_sep_tokens": True, "sequence_fusion": "intent_ordered",
+                       "max_position_embeddings": seq_len + 32, "use_task_tokens": False,
+                       "use_scenario_tokens": False, "use_global_scenario_token": False,
+                       "use_task_feature_interaction": False, "use_scenario_feature_interaction": False})
+    m["training"].update({"lr_dense": 1e-4, "lr_sparse": 0.05, "dense_optimizer": "rmsprop", "lr_warmup_steps": 1000,
+                          "rmsprop_alpha": 0.99999, "adagrad_initial_accumulator_value": 0.0})
+    seq = SequenceSpec(fields={"item_id": FieldSpec(vocab=item_vocab),
+                               **{f"side{k}": FieldSpec(vocab=side_vocab) for k in range(side_fields)}},
+                       max_len=seq_len)
+    spec = SyntheticSpec(fields=fields, dense_width=64, task_rates=list(tasks.values()), zipf_s=1.05, seed=0,
+                         sequences={"behavior": seq})
+    return m, spec
+
+
 def config(n: int, **kw) -> tuple[dict, SyntheticSpec]:
     if n == 3:
         return config3(**kw)
+    if n == 4:
+        return config4(**kw)
     raise ValueError(f"no benchmark workload {n}")

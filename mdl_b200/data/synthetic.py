@@ -40,6 +40,18 @@ class FieldSpec:
 
 
 @dataclass
+class SequenceSpec:
+    """A raw event sequence: per-event categorical fields (ids in [1, vocab]; the
+    first field carries the label signal), lengths uniform in [min_len, max_len],
+    left-padded to ``max_len`` with id 0."""
+
+    fields: dict[str, FieldSpec]
+    max_len: int
+    min_len: int | None = None       # None: every row is full length
+    dense_width: int = 0
+
+
+@dataclass
 class SyntheticSpec:
     fields: dict[str, FieldSpec]
     dense_width: int
@@ -49,6 +61,7 @@ class SyntheticSpec:
     seed: int = 0
     scene_field: str | None = None   # categorical field whose id is the scene id + 1
     scene_effect: float = 0.0        # strength of the per-(scene, task) part of the ground truth
+    sequences: dict[str, SequenceSpec] | None = None
 
 
 def zipf_ids(rng: np.random.Generator, n: int, vocab: int, s: float | None, scramble: int) -> np.ndarray:
@@ -155,6 +168,28 @@ class SyntheticGenerator:
             scores.append(per_row)
         dense = rng.standard_normal((rows, spec.dense_width)).astype(np.float32) if spec.dense_width else \
             np.zeros((rows, 0), dtype=np.float32)
+        sequences = {}
+        for name, ss in (spec.sequences or {}).items():
+            L = ss.max_len
+            lo = ss.min_len if ss.min_len is not None else L
+            lengths = rng.integers(lo, L + 1, size=rows, dtype=np.int64) if lo < L else np.full(rows, L, np.int64)
+            valid = np.arange(L)[None, :] >= (L - lengths)[:, None]          # prefix padding
+            ids = np.zeros((len(ss.fields), rows, L), dtype=np.int64)
+            for k, (fname, fs) in enumerate(ss.fields.items()):
+                key = f"{name}.{fname}"
+                if key not in self.scramble:
+                    self.scramble[key] = _coprime(fs.vocab, 7919 + k)
+                draw = zipf_ids(rng, rows * L, fs.vocab, spec.zipf_s, self.scramble[key]).reshape(rows, L)
+                ids[k] = np.where(valid, draw, 0)
+                if k == 0:  # mean score of the valid events of the first field
+                    sc = _id_score(ids[k].reshape(-1), int.from_bytes(sha256(key.encode()).digest()[:4], "little"))
+                    sc = (sc.reshape(rows, L) * valid).sum(1) / np.maximum(lengths, 1)
+                    scores.append(sc * 2.0)
+            seq = {"ids": torch.from_numpy(ids.reshape(len(ss.fields), rows * L)),
+                   "lengths": torch.from_numpy(lengths)}
+            if ss.dense_width:
+                seq["dense"] = torch.from_numpy(rng.standard_normal((rows * L, ss.dense_width)).astype(np.float32))
+            sequences[name] = seq
         per_field = np.stack(scores, axis=1) if scores else np.zeros((rows, 0))
         logits = self._calibrate(self._truth_logits(per_field, dense.astype(np.float64), scen))
         probs = 1.0 / (1.0 + np.exp(-logits))
@@ -164,7 +199,7 @@ class SyntheticGenerator:
         ids_all = np.concatenate(ids_parts) if ids_parts else np.zeros(0, dtype=np.int64)
         return PackedBatch.pack(torch.from_numpy(ids_all), torch.from_numpy(offsets),
                                 torch.from_numpy(dense) if spec.dense_width else None, torch.from_numpy(labels), None,
-                                torch.from_numpy(scen), rows, pin=pin)
+                                torch.from_numpy(scen), rows, sequences=sequences, pin=pin)
 
 
 class BatchPool:

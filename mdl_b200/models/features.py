@@ -74,7 +74,7 @@ class FeatureEncoder:
     def __init__(self, config: AppConfig, *, device: torch.device, rank: int = 0, world: int = 1,
                  process_group=None, vocab_sizes: dict[str, int] | None = None, input_names: list[str] | None = None,
                  slice_tokens: int = 0, base_seed: int | None = None,
-                 domain_tokens: list[list[str]] | None = None) -> None:
+                 domain_tokens: list[list[str]] | None = None, sequences: list | None = None) -> None:
         self.config = config
         by_name = {f.name: f for f in config.features}
         names = list(input_names if input_names is not None else config.resolved.tokenization.feature_token_inputs)
@@ -164,6 +164,46 @@ class FeatureEncoder:
             self.domain_plan = LookupPlan(flat, out_width=len(domain_tokens) * kp, dense_width=dense_total,
                                           zero_fill=any(w != kp for w in self.domain_widths))
         self.batch_plan = LookupPlan([make(n, 0) for n in batch_names], out_width=0, dense_width=dense_total)
+        # Raw event sequences (OneTrans S tokens): one plan per sequence whose rows are the
+        # events (rows * max_length), categorical fields first, then dense fields.
+        self.seq_plans: dict[str, LookupPlan] = {}
+        self.seq_fields: dict[str, list[str]] = {}
+        self.seq_dense_fields: dict[str, list[str]] = {}
+        self.seq_widths: dict[str, int] = {}
+        for seq in sequences or []:
+            cats = [fl for fl in seq.fields if fl.kind == "categorical"]
+            dens = [fl for fl in seq.fields if fl.kind == "dense"]
+            lfs: list[LookupFeature] = []
+            col = 0
+            for i, fl in enumerate(cats):
+                enc = fl.encoding
+                if enc is not None and enc.share_with and enc.share_embedding:
+                    tname = table_name_of(config, enc.share_with)
+                    owner = by_name.get(tname)
+                    if owner is None:
+                        raise ValueError(f"sequence field {seq.name}.{fl.name} shares unknown table {enc.share_with!r}")
+                else:
+                    tname, owner = f"{seq.name}.{fl.name}", fl
+                dim = int(owner.embedding_dim or config.model.embedding_dim)
+                rows = categorical_size(owner, vocab_sizes)
+                if tname in tables and tables[tname] != (rows, dim):
+                    raise ValueError(f"shared table {tname!r} used with different shapes")
+                tables[tname] = (rows, dim)
+                lfs.append(LookupFeature(f"{seq.name}.{fl.name}", tname, pooling=POOL_NONE, width=dim, out_col=col,
+                                         src=i))
+                col += dim
+            dcol = 0
+            for j, fl in enumerate(dens):
+                lfs.append(LookupFeature(f"{seq.name}.{fl.name}", None, width=int(fl.dimension), out_col=col,
+                                         dense_col=dcol, src=len(cats) + j))
+                col += int(fl.dimension)
+                dcol += int(fl.dimension)
+            pad = (col + 7) // 8 * 8  # 16-byte rows for the projection GEMM
+            self.seq_plans[seq.name] = LookupPlan(lfs, out_width=col, slice_k=col if pad != col else 0,
+                                                  slice_stride=pad if pad != col else 0, dense_width=dcol)
+            self.seq_fields[seq.name] = [fl.name for fl in cats]
+            self.seq_dense_fields[seq.name] = [fl.name for fl in dens]
+            self.seq_widths[seq.name] = col
         train = config.training
         specs = [EmbeddingTableSpec(n, r, d, 4 if train.embedding_weight_dtype == "fp32" else 2)
                  for n, (r, d) in sorted(tables.items())]

@@ -70,6 +70,53 @@ class TaskHeadsBCEFn(torch.autograd.Function):
         return dx, None, None, None, None, None, None, None, None
 
 
+class SharedInputHeadsBCEFn(torch.autograd.Function):
+    """Every task reads the same ``x [B, D]`` (row stride ``x.stride(0)``): the
+    first layers of all towers are one GEMM against the stacked ``w1``."""
+
+    @staticmethod
+    def forward(ctx, x, w1, b1, w2, b2, labels, mask, task_scale, relu):
+        B, D = x.shape
+        nt, Hh = w2.shape
+        dev = x.device
+        lda = x.stride(0)
+        pre = torch.empty(B, nt * Hh, dtype=torch.bfloat16, device=dev)
+        act = torch.empty_like(pre)
+        w1s = _shadow(w1).reshape(nt * Hh, D)
+        if relu:
+            bgemm(x, w1s, act, M=B, N=nt * Hh, K=D, lda=lda, ldb=D, ldc=nt * Hh, bias=b1.reshape(-1), act=ACT_RELU)
+            pre = act
+        else:
+            bgemm(x, w1s, pre, M=B, N=nt * Hh, K=D, lda=lda, ldb=D, ldc=nt * Hh, out2=act, bias=b1.reshape(-1),
+                  act=ACT_GELU)
+        logits = torch.empty(B, nt, dtype=torch.float32, device=dev)
+        loss = torch.zeros(1, dtype=torch.float32, device=dev)
+        ext().head_bce(act, pre, w2, b2, labels, mask, task_scale, logits, loss, None, None, None, B, nt, Hh,
+                       bool(relu))
+        ctx.save_for_backward(x, pre, act, labels, mask if mask is not None else labels.new_empty(0), task_scale)
+        ctx.meta = (w1, b1, w2, b2, relu, mask is not None)
+        ctx.mark_non_differentiable(logits)
+        return loss.reshape(()), logits
+
+    @staticmethod
+    def backward(ctx, dloss, _dlogits):
+        x, pre, act, labels, mask, task_scale = ctx.saved_tensors
+        w1, b1, w2, b2, relu, has_mask = ctx.meta
+        B, D = x.shape
+        nt, Hh = w2.shape
+        scale = task_scale * dloss.reshape(1).to(torch.float32)
+        dpre = torch.empty_like(act)
+        C = ext()
+        C.head_bce(act, pre, w2, b2, labels, mask if has_mask else None, scale, None, None, dpre, _grad(w2), _grad(b2),
+                   B, nt, Hh, bool(relu))
+        C.colsum(dpre, _grad(b1).reshape(-1), 1, B, nt * Hh, nt * Hh, 0, 1.0)
+        bgemm(dpre, x, _grad(w1).reshape(nt * Hh, D), M=nt * Hh, N=D, K=B, lda=nt * Hh, a_mn=True, ldb=x.stride(0),
+              b_mn=True, ldc=D, accumulate=True)
+        dx = torch.empty(B, D, dtype=torch.bfloat16, device=x.device)
+        bgemm(dpre, _shadow(w1).reshape(nt * Hh, D), dx, M=B, N=D, K=nt * Hh, lda=nt * Hh, ldb=D, b_mn=True, ldc=D)
+        return dx, None, None, None, None, None, None, None, None
+
+
 class TaskHeads(nn.Module):
     def __init__(self, num_tasks: int, input_dim: int, hidden_dim: int, activation: str = "gelu", device=None):
         super().__init__()
@@ -106,6 +153,19 @@ class TaskHeads(nn.Module):
                 bce = bce * mask.float()
             out["loss"] = (bce * task_scale.unsqueeze(0).to(bce.dtype)).sum()
         return out
+
+    def forward_shared(self, x: torch.Tensor, labels: torch.Tensor | None, mask: torch.Tensor | None,
+                       task_scale: torch.Tensor) -> dict[str, torch.Tensor]:
+        """``x [B, D]`` read by every task (reference default readout: the flattened
+        NS tokens feed each ``TaskHead``, ``src/model.py:7970-8022``)."""
+
+        if (x.is_cuda and labels is not None and hasattr(self.w1, "_mdl_shadow") and self.input_dim % 8 == 0
+                and self.hidden_dim % 8 == 0 and x.stride(1) == 1 and x.stride(0) % 8 == 0):
+            loss, logits = SharedInputHeadsBCEFn.apply(x.to(torch.bfloat16), self.w1, self.b1, self.w2, self.b2,
+                                                       labels.float(), None if mask is None else mask.float(),
+                                                       task_scale.float(), self.relu)
+            return {"loss": loss, "logits": logits}
+        return self.forward(x.unsqueeze(1).expand(-1, self.num_tasks, -1), labels, mask, task_scale)
 
     def reference_state_dict(self, prefix: str = "logit_layers") -> dict[str, torch.Tensor]:
         sd = {}

@@ -1,0 +1,550 @@
+"""OneTrans: one causal transformer over sequence (S) and non-sequence (NS) tokens.
+
+Reference: ``OneTransTokenizer`` ``src/model.py:4571-5296``, ``MixedCausalAttention``
+``:5479-5721``, ``MixedFFN`` ``:5724-5818``, ``OneTransBlock`` ``:5821-6071``,
+``OneTransBackbone`` ``:6097-6560``, ``OneTransModel`` ``:7970-8022``.
+
+Token sequence of one sample: ``[S_0 .. S_{L-1}, NS_0 .. NS_{N-1}]`` with the
+S tokens left-padded (a sample's valid events are its last ``len`` events; the
+first valid token index is ``kstart``).
+
+* S tokens: the embeddings of each event's fields (one lookup per field, rows =
+  events) through a ``Linear -> GELU -> Linear`` projection;
+* NS tokens (``auto_split``): the concatenated scalar inputs through one
+  ``Linear -> GELU -> Linear`` to ``N * d``;
+* learned absolute positions counted over valid tokens only (``e - kstart``),
+  added to valid tokens;
+* per layer (pre-RMSNorm): mixed causal attention -- shared Q/K/V weights for
+  S tokens, one weight set per NS token, a shared output projection -- over a
+  query suffix (the last ``q_l`` S tokens + all NS tokens, the pyramid), then a
+  mixed FFN (shared for S, per NS token), both residual;
+* readout: the final NS tokens flattened into the task heads.
+
+Layouts. The whole sequence of a sample lives in one ``[B, L + N, d]`` buffer
+(S rows then NS rows): shared-weight products run as GEMMs grouped over the
+batch with one weight (batch stride 0), per-token products as GEMMs grouped
+over the NS tokens, both writing straight into the buffer, and the weight
+gradient of a shared weight sums the per-sample row ranges inside one GEMM. The
+attention is the tcgen05 flash attention of ``ops/attention.py``.
+
+Pyramid schedules: ``linear`` is the reference's (``_layer_s_count``
+``src/model.py:6181-6198``); ``halve`` keeps ``initial >> ((l + 1) // k)`` S
+queries at layer ``l`` (halving every ``k`` layers), rounded like ``linear``.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from ..config.schema import AppConfig
+from ..ops._ext import error_word, ext
+from ..ops.attention import suffix_attention, suffix_attention_reference
+from ..ops.gemm import ACT_ADD, ACT_DMUL, ACT_GELU_GRAD, bgemm
+from ..ops.layers import _grad, _kaiming_uniform_, _shadow, gemm_param
+from .features import FeatureEncoder
+from .heads import TaskHeads
+
+
+# ----------------------------------------------------------------------------- schedule
+def pyramid_query_counts(config: AppConfig, initial_s: int, num_ns: int) -> list[int]:
+    """S tokens queried (and kept) by each layer."""
+
+    m = config.model
+    counts, cur = [], initial_s
+    for layer in range(m.num_layers):
+        if not m.use_pyramid or initial_s == 0:
+            counts.append(cur)
+            continue
+        final = m.final_s_tokens
+        if m.pyramid_schedule == "halve":
+            target = initial_s >> ((layer + 1) // max(1, m.pyramid_halve_every))
+            if final is not None:
+                target = max(min(final, initial_s), target)
+                if layer == m.num_layers - 1:
+                    target = min(final, initial_s)
+        else:
+            final = min(num_ns, initial_s) if final is None else min(final, initial_s)
+            if layer == m.num_layers - 1:
+                target = final
+            else:
+                progress = float(layer + 1) / float(m.num_layers)
+                target = round(initial_s - (initial_s - final) * progress)
+            if target > m.pyramid_round_to:
+                target = max(final, int(round(target / m.pyramid_round_to) * m.pyramid_round_to))
+        if m.pyramid_schedule == "halve" and m.pyramid_round_to < target < initial_s:
+            target = int(round(target / m.pyramid_round_to) * m.pyramid_round_to)
+        cur = max(0, min(cur, target))
+        counts.append(cur)
+    return counts
+
+
+def _off(t: torch.Tensor, n: int) -> torch.Tensor:
+    """Flat view of a contiguous tensor starting ``n`` elements in (a GEMM operand base)."""
+
+    return t.view(-1)[n:]
+
+
+# ----------------------------------------------------------------------------- mixed GEMMs
+def _mixed_fwd(x, L, s, K, w_s, b_s, w_ns, b_ns, out, Nout, act=0, out2=None, aux=None):
+    """``out [B, L, Nout] = x [B, L, K] W^T + b`` with W shared for rows < s and per token above."""
+
+    B = x.shape[0]
+    n = L - s
+    if s > 0:
+        bgemm(x, w_s, out, M=s, N=Nout, K=K, G=B, lda=K, gsA=L * K, ldb=K, gsB=0, ldc=Nout, gsC=L * Nout,
+              out2=out2, bias=b_s, gs_bias=0, aux=aux, ld_aux=Nout, gs_aux=L * Nout, act=act)
+    if n > 0:
+        bgemm(_off(x, s * K), w_ns, _off(out, s * Nout), M=B, N=Nout, K=K, G=n, lda=L * K, gsA=K, ldb=K,
+              gsB=Nout * K, ldc=L * Nout, gsC=Nout, out2=None if out2 is None else _off(out2, s * Nout),
+              bias=b_ns, gs_bias=Nout, aux=None if aux is None else _off(aux, s * Nout), ld_aux=L * Nout,
+              gs_aux=Nout, act=act)
+
+
+def _mixed_dgrad(dy, L, s, Nout, K, w_s, w_ns, dx, act=0, aux=None, colsum_s=None, colsum_ns=None):
+    """``dx [B, L, K] = dy [B, L, Nout] W`` (optionally times ``aux``, with column sums of the result)."""
+
+    B = dy.shape[0]
+    n = L - s
+    if s > 0:
+        bgemm(dy, w_s, dx, M=s, N=K, K=Nout, G=B, lda=Nout, gsA=L * Nout, ldb=K, gsB=0, b_mn=True, ldc=K,
+              gsC=L * K, aux=aux, ld_aux=K, gs_aux=L * K, act=act, colsum=colsum_s, gs_colsum=0)
+    if n > 0:
+        bgemm(_off(dy, s * Nout), w_ns, _off(dx, s * K), M=B, N=K, K=Nout, G=n, lda=L * Nout, gsA=Nout, ldb=K,
+              gsB=Nout * K, b_mn=True, ldc=L * K, gsC=K, aux=None if aux is None else _off(aux, s * K),
+              ld_aux=L * K, gs_aux=K, act=act, colsum=colsum_ns, gs_colsum=K)
+
+
+def _mixed_wgrad(dy, x, L, s, Nout, K, gw_s, gw_ns):
+    """``gw_s += sum over S rows of dy^T x``; ``gw_ns[t] += dy_t^T x_t`` (fp32 gradients)."""
+
+    B = dy.shape[0]
+    n = L - s
+    if s > 0:
+        bgemm(dy, x, gw_s, M=Nout, N=K, K=s, lda=Nout, a_mn=True, ldb=K, b_mn=True, ldc=K, accumulate=True,
+              kg=B, ksA=L * Nout, ksB=L * K)
+    if n > 0:
+        bgemm(_off(dy, s * Nout), _off(x, s * K), gw_ns, M=Nout, N=K, K=B, G=n, lda=L * Nout, gsA=Nout, a_mn=True,
+              ldb=L * K, gsB=K, b_mn=True, ldc=K, gsC=Nout * K, accumulate=True)
+
+
+def _mixed_bias_grad(dy, L, s, Nout, gb_s, gb_ns):
+    B = dy.shape[0]
+    n = L - s
+    C = ext()
+    if s > 0:
+        C.colsum(dy, gb_s, B, s, Nout, Nout, L * Nout, 1.0, 0)
+    if n > 0:
+        C.colsum(_off(dy, s * Nout), gb_ns, n, B, Nout, L * Nout, Nout, 1.0, Nout)
+
+
+# ----------------------------------------------------------------------------- fused layer
+class OneTransLayerFn(torch.autograd.Function):
+    """One OneTrans block on the CUDA path: ``X [B, Lk, d] -> Y [B, q + N, d]``."""
+
+    @staticmethod
+    def forward(ctx, X, kstart, layer, s_in, q, heads, eps):
+        C = ext()
+        B, Lk, D = X.shape
+        N = Lk - s_in
+        Lq = q + N
+        Hd = layer.hidden_dim
+        dev = X.device
+        X = X.contiguous()
+        xn = torch.empty_like(X)
+        rstd1 = torch.empty(B * Lk, dtype=torch.float32, device=dev)
+        C.rms_fwd(X, layer.norm1, xn, rstd1, B * Lk, D, eps)
+        qkv = torch.empty(B, Lk, 3 * D, dtype=torch.bfloat16, device=dev)
+        _mixed_fwd(xn, Lk, s_in, D, _shadow(layer.wqkv_s), layer.bqkv_s, _shadow(layer.wqkv_ns), layer.bqkv_ns, qkv,
+                   3 * D)
+        ks = kstart.to(torch.int32).contiguous()
+        att = torch.empty(B, Lq, D, dtype=torch.bfloat16, device=dev)
+        lse = torch.empty(B, heads, Lq, dtype=torch.float32, device=dev)
+        C.fmha_fwd(qkv, ks, att, lse, heads, Lq, True, 0.0, error_word(dev))
+        h = torch.empty(B, Lq, D, dtype=torch.bfloat16, device=dev)
+        # h = X[:, Lk-Lq:] + att W_o^T + b_o
+        bgemm(att, _shadow(layer.wo), h, M=Lq, N=D, K=D, G=B, lda=D, gsA=Lq * D, ldb=D, gsB=0, ldc=D, gsC=Lq * D,
+              bias=layer.bo, aux=_off(X, (Lk - Lq) * D), ld_aux=D, gs_aux=Lk * D, act=ACT_ADD)
+        hn = torch.empty_like(h)
+        rstd2 = torch.empty(B * Lq, dtype=torch.float32, device=dev)
+        C.rms_fwd(h, layer.norm2, hn, rstd2, B * Lq, D, eps)
+        ug = torch.empty(B, Lq, Hd, dtype=torch.bfloat16, device=dev)
+        u = torch.empty_like(ug)
+        _mixed_fwd(hn, Lq, q, D, _shadow(layer.w1_s), layer.b1_s, _shadow(layer.w1_ns), layer.b1_ns, ug, Hd,
+                   act=ACT_GELU_GRAD, out2=u)
+        Y = torch.empty(B, Lq, D, dtype=torch.bfloat16, device=dev)
+        _mixed_fwd(u, Lq, q, Hd, _shadow(layer.w2_s), layer.b2_s, _shadow(layer.w2_ns), layer.b2_ns, Y, D,
+                   act=ACT_ADD, aux=h)
+        ctx.save_for_backward(X, xn, rstd1, qkv, ks, att, lse, h, hn, rstd2, ug, u)
+        ctx.meta = (layer, s_in, q, heads)
+        return Y
+
+    @staticmethod
+    def backward(ctx, dY):
+        X, xn, rstd1, qkv, ks, att, lse, h, hn, rstd2, ug, u = ctx.saved_tensors
+        layer, s_in, q, heads = ctx.meta
+        C = ext()
+        B, Lk, D = X.shape
+        N = Lk - s_in
+        Lq = q + N
+        Hd = layer.hidden_dim
+        dev = X.device
+        dY = dY.to(torch.bfloat16).contiguous()
+        # ---- FFN
+        du = torch.empty(B, Lq, Hd, dtype=torch.bfloat16, device=dev)
+        _mixed_dgrad(dY, Lq, q, D, Hd, _shadow(layer.w2_s), _shadow(layer.w2_ns), du, act=ACT_DMUL, aux=ug,
+                     colsum_s=_grad(layer.b1_s), colsum_ns=_grad(layer.b1_ns))
+        _mixed_wgrad(dY, u, Lq, q, D, Hd, _grad(layer.w2_s), _grad(layer.w2_ns))
+        _mixed_bias_grad(dY, Lq, q, D, _grad(layer.b2_s), _grad(layer.b2_ns))
+        dhn = torch.empty(B, Lq, D, dtype=torch.bfloat16, device=dev)
+        _mixed_dgrad(du, Lq, q, Hd, D, _shadow(layer.w1_s), _shadow(layer.w1_ns), dhn)
+        _mixed_wgrad(du, hn, Lq, q, Hd, D, _grad(layer.w1_s), _grad(layer.w1_ns))
+        del du
+        dh = torch.empty_like(dhn)
+        C.rms_bwd(h, layer.norm2, rstd2, dhn, dh, _grad(layer.norm2), B * Lq, D, dres=dY)
+        # ---- attention output projection
+        datt = torch.empty_like(dh)
+        bgemm(dh, _shadow(layer.wo), datt, M=B * Lq, N=D, K=D, lda=D, ldb=D, b_mn=True, ldc=D)
+        bgemm(dh, att, _grad(layer.wo), M=D, N=D, K=B * Lq, lda=D, a_mn=True, ldb=D, b_mn=True, ldc=D,
+              accumulate=True)
+        C.colsum(dh, _grad(layer.bo), 1, B * Lq, D, D, 0, 1.0)
+        # ---- attention
+        dqkv = torch.empty_like(qkv)
+        dq_acc = torch.empty(B, Lq, D, dtype=torch.float32, device=dev)
+        dsum = torch.empty(B, heads, Lq, dtype=torch.float32, device=dev)
+        C.fmha_bwd(qkv, ks, att, lse, datt, dqkv, dq_acc, dsum, heads, Lq, True, 0.0, error_word(dev))
+        del dq_acc, dsum, datt
+        # ---- Q/K/V projections
+        dxn = torch.empty_like(X)
+        _mixed_dgrad(dqkv, Lk, s_in, 3 * D, D, _shadow(layer.wqkv_s), _shadow(layer.wqkv_ns), dxn)
+        _mixed_wgrad(dqkv, xn, Lk, s_in, 3 * D, D, _grad(layer.wqkv_s), _grad(layer.wqkv_ns))
+        _mixed_bias_grad(dqkv, Lk, s_in, 3 * D, _grad(layer.bqkv_s), _grad(layer.bqkv_ns))
+        dX = torch.empty_like(X)
+        C.rms_bwd(X, layer.norm1, rstd1, dxn, dX, _grad(layer.norm1), B * Lk, D, dres=dh, res_period=Lk,
+                  res_tail=Lq)
+        return dX, None, None, None, None, None, None
+
+
+class OneTransTokenizeFn(torch.autograd.Function):
+    """S tokens (event projection MLP) + NS tokens (auto_split MLP) + positions -> ``[B, L + N, d]``."""
+
+    @staticmethod
+    def forward(ctx, seq_in, ns_in, kstart, model, L):
+        C = ext()
+        B = ns_in.shape[0]
+        D, N, Hd = model.token_dim, model.num_ns, model.hidden_dim
+        Ks, Kn = seq_in.shape[1], ns_in.shape[1]
+        Lt = L + N
+        dev = ns_in.device
+        ug = torch.empty(B * L, Hd, dtype=torch.bfloat16, device=dev)
+        u = torch.empty_like(ug)
+        bgemm(seq_in, _shadow(model.seq_w1), ug, M=B * L, N=Hd, K=Ks, lda=seq_in.stride(0), ldb=Ks, ldc=Hd, out2=u,
+              bias=model.seq_b1, act=ACT_GELU_GRAD)
+        X0 = torch.empty(B, Lt, D, dtype=torch.bfloat16, device=dev)
+        bgemm(u, _shadow(model.seq_w2), X0, M=L, N=D, K=Hd, G=B, lda=Hd, gsA=L * Hd, ldb=Hd, gsB=0, ldc=D,
+              gsC=Lt * D, bias=model.seq_b2)
+        vg = torch.empty(B, Hd, dtype=torch.bfloat16, device=dev)
+        v = torch.empty_like(vg)
+        bgemm(ns_in, _shadow(model.ns_w1), vg, M=B, N=Hd, K=Kn, lda=ns_in.stride(0), ldb=Kn, ldc=Hd, out2=v,
+              bias=model.ns_b1, act=ACT_GELU_GRAD)
+        bgemm(v, _shadow(model.ns_w2), _off(X0, L * D), M=B, N=N * D, K=Hd, lda=Hd, ldb=Hd, ldc=Lt * D,
+              bias=model.ns_b2)
+        ks = kstart.to(torch.int32).contiguous()
+        C.position_add(X0, model.pos, ks, B, Lt, D)
+        ctx.save_for_backward(seq_in, ns_in, ks, ug, u, vg, v)
+        ctx.meta = (model, L)
+        return X0
+
+    @staticmethod
+    def backward(ctx, dX0):
+        seq_in, ns_in, ks, ug, u, vg, v = ctx.saved_tensors
+        model, L = ctx.meta
+        C = ext()
+        B = ns_in.shape[0]
+        D, N, Hd = model.token_dim, model.num_ns, model.hidden_dim
+        Ks, Kn = seq_in.shape[1], ns_in.shape[1]
+        Lt = L + N
+        dev = ns_in.device
+        dX0 = dX0.to(torch.bfloat16).contiguous()
+        C.position_grad(dX0, _grad(model.pos), ks, B, Lt, D)
+        # S: projection MLP over events
+        du = torch.empty(B * L, Hd, dtype=torch.bfloat16, device=dev)
+        bgemm(dX0, _shadow(model.seq_w2), du, M=L, N=Hd, K=D, G=B, lda=D, gsA=Lt * D, ldb=Hd, gsB=0, b_mn=True,
+              ldc=Hd, gsC=L * Hd, aux=ug, ld_aux=Hd, gs_aux=L * Hd, act=ACT_DMUL, colsum=_grad(model.seq_b1),
+              gs_colsum=0)
+        bgemm(dX0, u, _grad(model.seq_w2), M=D, N=Hd, K=L, lda=D, a_mn=True, ldb=Hd, b_mn=True, ldc=Hd,
+              accumulate=True, kg=B, ksA=Lt * D, ksB=L * Hd)
+        C.colsum(dX0, _grad(model.seq_b2), B, L, D, D, Lt * D, 1.0, 0)
+        bgemm(du, seq_in, _grad(model.seq_w1), M=Hd, N=Ks, K=B * L, lda=Hd, a_mn=True, ldb=seq_in.stride(0),
+              b_mn=True, ldc=Ks, accumulate=True)
+        dseq = torch.empty(B * L, Ks, dtype=torch.bfloat16, device=dev)
+        bgemm(du, _shadow(model.seq_w1), dseq, M=B * L, N=Ks, K=Hd, lda=Hd, ldb=Ks, b_mn=True, ldc=Ks)
+        del du
+        # NS: auto_split MLP
+        dns_tok = _off(dX0, L * D)
+        dv = torch.empty(B, Hd, dtype=torch.bfloat16, device=dev)
+        bgemm(dns_tok, _shadow(model.ns_w2), dv, M=B, N=Hd, K=N * D, lda=Lt * D, ldb=Hd, b_mn=True, ldc=Hd, aux=vg,
+              ld_aux=Hd, act=ACT_DMUL, colsum=_grad(model.ns_b1))
+        bgemm(dns_tok, v, _grad(model.ns_w2), M=N * D, N=Hd, K=B, lda=Lt * D, a_mn=True, ldb=Hd, b_mn=True, ldc=Hd,
+              accumulate=True)
+        C.colsum(dns_tok, _grad(model.ns_b2), 1, B, N * D, Lt * D, 0, 1.0)
+        bgemm(dv, ns_in, _grad(model.ns_w1), M=Hd, N=Kn, K=B, lda=Hd, a_mn=True, ldb=ns_in.stride(0), b_mn=True,
+              ldc=Kn, accumulate=True)
+        dns = torch.empty(B, Kn, dtype=torch.bfloat16, device=dev)
+        bgemm(dv, _shadow(model.ns_w1), dns, M=B, N=Kn, K=Hd, lda=Hd, ldb=Kn, b_mn=True, ldc=Kn)
+        return dseq, dns, None, None, None
+
+
+# ----------------------------------------------------------------------------- modules
+def _rms_reference(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    x = x.float()
+    return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w
+
+
+def _mixed_reference(x, s, w_s, b_s, w_ns, b_ns):
+    """fp32: rows < s with the shared weight, rows >= s with their own."""
+
+    ys = x[:, :s] @ w_s.t() + b_s
+    yn = torch.einsum("bnk,nok->bno", x[:, s:], w_ns) + b_ns.unsqueeze(0)
+    return torch.cat([ys, yn], dim=1)
+
+
+class OneTransLayer(nn.Module):
+    """Parameters of one block (reference ``OneTransBlock`` ``src/model.py:5821-5840``)."""
+
+    def __init__(self, token_dim: int, hidden_dim: int, num_ns: int, device=None) -> None:
+        super().__init__()
+        D, H, N = token_dim, hidden_dim, num_ns
+        self.token_dim, self.hidden_dim, self.num_ns = D, H, N
+        self.norm1 = nn.Parameter(torch.ones(D, device=device))
+        self.wqkv_s = gemm_param(torch.empty(3 * D, D, device=device))
+        self.bqkv_s = nn.Parameter(torch.empty(3 * D, device=device))
+        self.wqkv_ns = gemm_param(torch.empty(N, 3 * D, D, device=device))
+        self.bqkv_ns = nn.Parameter(torch.empty(N, 3 * D, device=device))
+        self.wo = gemm_param(torch.empty(D, D, device=device))
+        self.bo = nn.Parameter(torch.empty(D, device=device))
+        self.norm2 = nn.Parameter(torch.ones(D, device=device))
+        self.w1_s = gemm_param(torch.empty(H, D, device=device))
+        self.b1_s = nn.Parameter(torch.empty(H, device=device))
+        self.w1_ns = gemm_param(torch.empty(N, H, D, device=device))
+        self.b1_ns = nn.Parameter(torch.empty(N, H, device=device))
+        self.w2_s = gemm_param(torch.empty(D, H, device=device))
+        self.b2_s = nn.Parameter(torch.empty(D, device=device))
+        self.w2_ns = gemm_param(torch.empty(N, D, H, device=device))
+        self.b2_ns = nn.Parameter(torch.empty(N, D, device=device))
+        # nn.Linear's default init per projection (kaiming-uniform weight, bias U(+-1/sqrt(fan_in)))
+        for w, b, fan in ((self.wqkv_s, self.bqkv_s, D), (self.wo, self.bo, D), (self.w1_s, self.b1_s, D),
+                          (self.w2_s, self.b2_s, H)):
+            _kaiming_uniform_(w.data, fan)
+            _kaiming_uniform_(b.data, fan)
+        for w, b, fan in ((self.wqkv_ns, self.bqkv_ns, D), (self.w1_ns, self.b1_ns, D), (self.w2_ns, self.b2_ns, H)):
+            _kaiming_uniform_(w.data, fan)
+            _kaiming_uniform_(b.data, fan)
+
+    def forward_reference(self, X, kstart, s_in, q, heads, eps):
+        B, Lk, D = X.shape
+        N = Lk - s_in
+        Lq = q + N
+        xn = _rms_reference(X, self.norm1, eps)
+        qkv = _mixed_reference(xn, s_in, self.wqkv_s, self.bqkv_s, self.wqkv_ns, self.bqkv_ns)
+        att = suffix_attention_reference(qkv, kstart, heads, Lq)
+        h = X[:, Lk - Lq:].float() + att @ self.wo.t() + self.bo
+        hn = _rms_reference(h, self.norm2, eps)
+        u = F.gelu(_mixed_reference(hn, q, self.w1_s, self.b1_s, self.w1_ns, self.b1_ns))
+        return h + _mixed_reference(u, q, self.w2_s, self.b2_s, self.w2_ns, self.b2_ns)
+
+    def reference_state_dict(self, prefix: str) -> dict[str, torch.Tensor]:
+        D = self.token_dim
+        sd = {prefix + "norm_attention.weight": self.norm1, prefix + "norm_ffn.weight": self.norm2,
+              prefix + "attention.output.weight": self.wo, prefix + "attention.output.bias": self.bo,
+              prefix + "ffn.s_ffn.0.weight": self.w1_s, prefix + "ffn.s_ffn.0.bias": self.b1_s,
+              prefix + "ffn.s_ffn.2.weight": self.w2_s, prefix + "ffn.s_ffn.2.bias": self.b2_s}
+        for j, part in enumerate(("query", "key", "value")):
+            sd[prefix + f"attention.s_{part}.weight"] = self.wqkv_s[j * D:(j + 1) * D]
+            sd[prefix + f"attention.s_{part}.bias"] = self.bqkv_s[j * D:(j + 1) * D]
+            for n in range(self.num_ns):
+                sd[prefix + f"attention.ns_{part}.{n}.weight"] = self.wqkv_ns[n, j * D:(j + 1) * D]
+                sd[prefix + f"attention.ns_{part}.{n}.bias"] = self.bqkv_ns[n, j * D:(j + 1) * D]
+        for n in range(self.num_ns):
+            sd[prefix + f"ffn.ns_ffn.{n}.0.weight"] = self.w1_ns[n]
+            sd[prefix + f"ffn.ns_ffn.{n}.0.bias"] = self.b1_ns[n]
+            sd[prefix + f"ffn.ns_ffn.{n}.2.weight"] = self.w2_ns[n]
+            sd[prefix + f"ffn.ns_ffn.{n}.2.bias"] = self.b2_ns[n]
+        return {k: v.detach().clone() for k, v in sd.items()}
+
+
+class OneTransModel(nn.Module):
+    """OneTrans ranker (``model.name: onetrans``) with ``auto_split`` NS tokens and one
+    ``intent_ordered`` sequence group."""
+
+    def __init__(self, config: AppConfig, *, device: torch.device, rank: int = 0, world: int = 1, process_group=None,
+                 vocab_sizes: dict[str, int] | None = None, base_seed: int | None = None) -> None:
+        super().__init__()
+        m = config.model
+        if m.ns_tokenizer != "auto_split":
+            raise NotImplementedError(f"OneTrans ns_tokenizer {m.ns_tokenizer!r}: auto_split is implemented")
+        groups = config.resolved.tokenization.sequence_token_groups
+        seq_by_name = {s.name: s for s in config.sequences}
+        if len(groups) != 1 or len(groups[0].inputs) != 1 or groups[0].inputs[0] not in seq_by_name:
+            raise NotImplementedError("OneTrans: one sequence token group over one raw sequence is implemented")
+        if m.token_dim % m.num_heads or m.token_dim // m.num_heads != 32:
+            raise NotImplementedError("OneTrans attention kernels use head_dim 32")
+        self.config = config
+        self.seq = seq_by_name[groups[0].inputs[0]]
+        if not self.seq.max_length:
+            raise ValueError(f"sequence {self.seq.name!r} needs max_length")
+        self.L = int(self.seq.max_length)
+        ns_inputs = list(config.resolved.tokenization.feature_token_inputs)
+        self.encoder = FeatureEncoder(config, device=device, rank=rank, world=world, process_group=process_group,
+                                      vocab_sizes=vocab_sizes, input_names=ns_inputs, slice_tokens=1,
+                                      base_seed=base_seed, sequences=[self.seq])
+        D, Hd = int(m.token_dim), int(m.hidden_dim)
+        N = int(m.num_ns_tokens or max(1, len(ns_inputs)))
+        self.token_dim, self.hidden_dim, self.num_ns, self.heads = D, Hd, N, int(m.num_heads)
+        self.eps = 1e-6
+        seq_plan = self.encoder.seq_plans[self.seq.name]
+        self.Ks, self.Ks_log = seq_plan.out_ld, seq_plan.out_width
+        self.Kn, self.Kn_log = self.encoder.plan.out_ld, self.encoder.plan.out_width
+        self.seq_w1 = gemm_param(torch.zeros(Hd, self.Ks, device=device))
+        self.seq_b1 = nn.Parameter(torch.empty(Hd, device=device))
+        self.seq_w2 = gemm_param(torch.empty(D, Hd, device=device))
+        self.seq_b2 = nn.Parameter(torch.empty(D, device=device))
+        self.ns_w1 = gemm_param(torch.zeros(Hd, self.Kn, device=device))
+        self.ns_b1 = nn.Parameter(torch.empty(Hd, device=device))
+        self.ns_w2 = gemm_param(torch.empty(N * D, Hd, device=device))
+        self.ns_b2 = nn.Parameter(torch.empty(N * D, device=device))
+        _kaiming_uniform_(self.seq_w1.data[:, :self.Ks_log], self.Ks_log)  # padded input columns stay zero
+        _kaiming_uniform_(self.seq_b1.data, self.Ks_log)
+        _kaiming_uniform_(self.seq_w2.data, Hd)
+        _kaiming_uniform_(self.seq_b2.data, Hd)
+        _kaiming_uniform_(self.ns_w1.data[:, :self.Kn_log], self.Kn_log)
+        _kaiming_uniform_(self.ns_b1.data, self.Kn_log)
+        _kaiming_uniform_(self.ns_w2.data, Hd)
+        _kaiming_uniform_(self.ns_b2.data, Hd)
+        P = max(int(config.resolved.onetrans_max_position_embeddings), self.L + N)
+        self.pos = nn.Parameter(torch.empty(P, D, device=device).normal_(0.0, m.init_std))
+        self.layers = nn.ModuleList(OneTransLayer(D, Hd, N, device=device) for _ in range(m.num_layers))
+        self.query_counts = pyramid_query_counts(config, self.L, N)
+        self.ntask = len(config.task_names)
+        self.heads_mod = TaskHeads(self.ntask, N * D, int(m.task_head_hidden_dim or Hd), m.task_head_activation,
+                                   device=device)
+
+    # ------------------------------------------------------------------ params
+    def gemm_param_names(self) -> set[str]:
+        return {n for n, p in self.named_parameters() if getattr(p, "_mdl_gemm", False)}
+
+    def dense_buckets(self) -> list[list[str]]:
+        names = [n for n, _ in self.named_parameters()]
+        heads = [n for n in names if n.startswith("heads_mod.")]
+        layers = [[n for n in names if n.startswith(f"layers.{i}.")] for i in reversed(range(len(self.layers)))]
+        rest = [n for n in names if not n.startswith(("heads_mod.", "layers."))]
+        return [heads, *layers, rest]
+
+    @property
+    def store(self):
+        return self.encoder.store
+
+    # ------------------------------------------------------------------ inputs
+    def _seq_offsets(self, rows: int, device) -> torch.Tensor:
+        key = (rows, str(device))
+        cache = getattr(self, "_offsets_cache", None)
+        if cache is None or cache[0] != key:
+            n = len(self.encoder.seq_fields[self.seq.name]) * rows
+            cache = (key, torch.arange(n + 1, dtype=torch.int64, device=device))
+            self._offsets_cache = cache
+        return cache[1]
+
+    def _inputs(self, batch, anchor):
+        from ..ops.embedding import fused_lookup
+
+        seq = batch.sequences[self.seq.name]
+        B, L = batch.rows, self.L
+        lengths = seq["lengths"].to(torch.int64)
+        kstart = (L - lengths.clamp(0, L)).to(torch.int32)
+        plan = self.encoder.seq_plans[self.seq.name]
+        ids = seq["ids"].reshape(-1)
+        seq_in = fused_lookup(self.store, plan, ids, self._seq_offsets(B * L, ids.device), seq.get("dense"), B * L,
+                              anchor)
+        ns_in = fused_lookup(self.store, self.encoder.plan, batch.ids, batch.offsets, batch.dense, B, anchor)
+        return seq_in, ns_in, kstart
+
+    # ------------------------------------------------------------------ forward
+    def forward(self, batch, task_scale: torch.Tensor | None = None) -> dict[str, torch.Tensor]:
+        anchor = torch.zeros(0, device=batch.ids.device, requires_grad=True)
+        seq_in, ns_in, kstart = self._inputs(batch, anchor)
+        if task_scale is None:
+            task_scale = torch.full((self.ntask,), 1.0 / max(1, batch.rows), device=batch.ids.device)
+        if batch.ids.is_cuda and self.config.runtime.kernel_backend == "native":
+            return self._forward_cuda(seq_in, ns_in, kstart, batch, task_scale)
+        return self.forward_reference(seq_in, ns_in, kstart, batch, task_scale)
+
+    def _forward_cuda(self, seq_in, ns_in, kstart, batch, task_scale):
+        from ..ops.dense import grad_ready
+
+        hooks = getattr(self, "dense_hooks", None)
+        nl = len(self.layers)
+        seq_in = grad_ready(seq_in, hooks, nl + 1)
+        X = OneTransTokenizeFn.apply(seq_in, ns_in, kstart, self, self.L)
+        s_in, ks = self.L, kstart
+        for i, layer in enumerate(self.layers):
+            X = grad_ready(X, hooks, nl - i)
+            q = self.query_counts[i]
+            X = OneTransLayerFn.apply(X, ks, layer, s_in, q, self.heads, self.eps)
+            ks = (ks - (s_in - q)).clamp(min=0)
+            s_in = q
+        X = grad_ready(X, hooks, 0)
+        B, Lq, D = X.shape
+        readout = X[:, s_in:, :].reshape(B, self.num_ns * D)
+        return self.heads_mod.forward_shared(readout, batch.labels, batch.label_mask, task_scale)
+
+    def forward_reference(self, seq_in, ns_in, kstart, batch, task_scale=None):
+        """Plain PyTorch fp32 definition (CPU path and test oracle)."""
+
+        B, L, D, N = batch.rows, self.L, self.token_dim, self.num_ns
+        s = F.gelu(seq_in.float()[:, :self.Ks_log] @ self.seq_w1[:, :self.Ks_log].t() + self.seq_b1)
+        s = (s @ self.seq_w2.t() + self.seq_b2).view(B, L, D)
+        v = F.gelu(ns_in.float()[:, :self.Kn_log] @ self.ns_w1[:, :self.Kn_log].t() + self.ns_b1)
+        ns = (v @ self.ns_w2.t() + self.ns_b2).view(B, N, D)
+        X = torch.cat([s, ns], dim=1)
+        e = torch.arange(L + N, device=X.device)
+        ks = kstart.to(X.device).long()
+        valid = e.view(1, -1) >= ks.view(-1, 1)
+        pid = (e.view(1, -1) - ks.view(-1, 1)).clamp(min=0)
+        X = X + self.pos[pid] * valid.unsqueeze(-1)
+        s_in = L
+        for i, layer in enumerate(self.layers):
+            q = self.query_counts[i]
+            X = layer.forward_reference(X, ks, s_in, q, self.heads, self.eps)
+            ks = (ks - (s_in - q)).clamp(min=0)
+            s_in = q
+        readout = X[:, s_in:, :].reshape(B, N * D)
+        return self.heads_mod.forward_shared(readout, batch.labels, batch.label_mask, task_scale)
+
+    # ------------------------------------------------------------------ reference layout
+    def reference_state_dict(self) -> dict[str, torch.Tensor]:
+        """Dense weights under the reference's parameter names (``OneTransModel``)."""
+
+        p = "backbone."
+        sd = {p + "tokenizer.sequence_projectors.0.0.weight": self.seq_w1[:, :self.Ks_log],
+              p + "tokenizer.sequence_projectors.0.0.bias": self.seq_b1,
+              p + "tokenizer.sequence_projectors.0.2.weight": self.seq_w2,
+              p + "tokenizer.sequence_projectors.0.2.bias": self.seq_b2,
+              p + "tokenizer.auto_ns_projection.0.weight": self.ns_w1[:, :self.Kn_log],
+              p + "tokenizer.auto_ns_projection.0.bias": self.ns_b1,
+              p + "tokenizer.auto_ns_projection.2.weight": self.ns_w2,
+              p + "tokenizer.auto_ns_projection.2.bias": self.ns_b2,
+              p + "unified_position_embeddings.weight": self.pos}
+        sd = {k: v.detach().clone() for k, v in sd.items()}
+        for i, layer in enumerate(self.layers):
+            sd.update(layer.reference_state_dict(f"{p}blocks.{i}."))
+        sd.update(self.heads_mod.reference_state_dict())
+        return sd
+
+
+def build_onetrans(config: AppConfig, **kw):
+    if config.model.name == "onetrans":
+        return OneTransModel(config, **kw)
+    raise NotImplementedError("mdl_onetrans (OneTrans backbone with MDL domain blocks) is not built yet")

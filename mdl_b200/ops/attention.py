@@ -1,0 +1,89 @@
+"""Causal attention of a query suffix over its own token sequence.
+
+``suffix_attention(qkv, kstart, heads, lq)`` is the attention of the OneTrans
+mixed causal attention (reference ``MixedCausalAttention.attend_causal_suffix``
+``src/model.py:5617-5695``; flash-attn varlen with bottom-right causality over
+the packed valid tokens):
+
+* ``qkv [B, Lk, 3*D]``: per token Q | K | V (head ``h`` at columns
+  ``h*hd : (h+1)*hd`` of each part);
+* the queries are the last ``lq`` tokens; query row ``p`` (token index) sees
+  key ``j`` iff ``kstart[b] <= j <= p`` (``j <= p`` only when ``causal``);
+* padding is a per-sample prefix (``kstart``), which is how the reference lays
+  out valid tokens (valid S tokens at the end of the S block, NS tokens always
+  valid), so a query row before ``kstart`` has no visible key and outputs zero;
+* returns ``[B, lq, D]``.
+
+CUDA: the tcgen05 flash attention in ``csrc/fmha.cu`` (forward saves the
+base-2 log-sum-exp; backward writes ``dqkv`` in the input layout). CPU: the
+same contract in fp32 PyTorch, also the oracle of the GPU tests.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from ._ext import error_word, ext
+
+LOG2E = 1.4426950408889634
+
+
+def suffix_attention_reference(qkv: torch.Tensor, kstart: torch.Tensor, heads: int, lq: int, causal: bool = True,
+                               scale: float | None = None) -> torch.Tensor:
+    """fp32 PyTorch definition (differentiable)."""
+
+    B, Lk, W = qkv.shape
+    D = W // 3
+    hd = D // heads
+    scale = scale if scale else 1.0 / math.sqrt(hd)
+    x = qkv.float()
+    q = x[:, Lk - lq:, :D].reshape(B, lq, heads, hd).transpose(1, 2)
+    k = x[:, :, D:2 * D].reshape(B, Lk, heads, hd).transpose(1, 2)
+    v = x[:, :, 2 * D:].reshape(B, Lk, heads, hd).transpose(1, 2)
+    s = torch.matmul(q, k.transpose(-1, -2)) * scale                   # [B, H, lq, Lk]
+    kpos = torch.arange(Lk, device=qkv.device)
+    qpos = torch.arange(Lk - lq, Lk, device=qkv.device)
+    ks = kstart.to(qkv.device).long().view(B, 1, 1)
+    allowed = kpos.view(1, 1, Lk) >= ks
+    if causal:
+        allowed = allowed & (kpos.view(1, 1, Lk) <= qpos.view(1, lq, 1))
+    allowed = allowed & (qpos.view(1, lq, 1) >= ks)                      # padded queries output zero
+    s = s.masked_fill(~allowed.unsqueeze(1), float("-inf"))
+    p = torch.softmax(s, dim=-1)
+    p = torch.where(allowed.unsqueeze(1), p, torch.zeros_like(p))       # rows without a visible key
+    o = torch.matmul(p, v)                                              # [B, H, lq, hd]
+    return o.transpose(1, 2).reshape(B, lq, D)
+
+
+class SuffixAttentionFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv, kstart, heads, lq, causal):
+        B, Lk, W = qkv.shape
+        D = W // 3
+        qkv = qkv.contiguous()
+        ks = kstart.to(torch.int32).contiguous()
+        out = torch.empty(B, lq, D, dtype=torch.bfloat16, device=qkv.device)
+        lse = torch.empty(B, heads, lq, dtype=torch.float32, device=qkv.device)
+        ext().fmha_fwd(qkv, ks, out, lse, heads, lq, bool(causal), 0.0, error_word(qkv.device))
+        ctx.save_for_backward(qkv, ks, out, lse)
+        ctx.meta = (heads, lq, bool(causal))
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        qkv, ks, out, lse = ctx.saved_tensors
+        heads, lq, causal = ctx.meta
+        dout = dout.to(torch.bfloat16).contiguous()
+        dqkv = torch.empty_like(qkv)
+        dq_acc = torch.empty(out.shape, dtype=torch.float32, device=qkv.device)
+        dsum = torch.empty(lse.shape, dtype=torch.float32, device=qkv.device)
+        ext().fmha_bwd(qkv, ks, out, lse, dout, dqkv, dq_acc, dsum, heads, lq, causal, 0.0, error_word(qkv.device))
+        return dqkv, None, None, None, None
+
+
+def suffix_attention(qkv: torch.Tensor, kstart: torch.Tensor, heads: int, lq: int, causal: bool = True) -> torch.Tensor:
+    if qkv.is_cuda:
+        return SuffixAttentionFn.apply(qkv, kstart, heads, lq, causal)
+    return suffix_attention_reference(qkv, kstart, heads, lq, causal)

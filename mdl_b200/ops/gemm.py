@@ -30,6 +30,7 @@ ACT_RELU = 3
 ACT_DRELU = 4
 ACT_GELU_GRAD = 5  # x = bf16(acc): out = gelu'(x), out2 = gelu(x)  (saves the derivative for the backward)
 ACT_DMUL = 6       # out = acc * aux
+ACT_ADD = 7        # out = acc + aux (fused residual add)
 
 
 def _view(t: torch.Tensor, g: int, rows: int, cols: int, gs: int, ld: int, mn_major: bool) -> torch.Tensor:
@@ -74,24 +75,39 @@ def bgemm(
     act: int = ACT_NONE,
     alpha: float = 1.0,
     accumulate: bool = False,
+    kg: int = 1,
+    ksA: int = 0,
+    ksB: int = 0,
 ) -> torch.Tensor:
-    """``out[g] = epilogue(alpha * A[g] @ B[g]^T)``; see the module docstring."""
+    """``out[g] = epilogue(alpha * A[g] @ B[g]^T)``; see the module docstring.
+
+    ``gsA == 0`` / ``gsB == 0`` with ``G > 1`` shares that operand across groups;
+    ``kg > 1`` (``G == 1``) sums ``kg`` products over K ranges ``ksA`` / ``ksB``
+    elements apart.
+    """
 
     if out.is_cuda:
         ext().gemm(
             a, lda, gsA, a_mn, b, ldb, gsB, b_mn, M, N, K, G, out, ldc, gsC,
             out2, bias, gs_bias, aux, ld_aux, gs_aux, colsum, gs_colsum,
-            act, float(alpha), accumulate, error_word(out.device), 0,
+            act, float(alpha), accumulate, error_word(out.device), 0, kg, ksA, ksB,
         )
         return out
-    av = _view(a, G, M, K, gsA, lda, a_mn).float()
-    bv = _view(b, G, N, K, gsB, ldb, b_mn).float()
-    acc = torch.bmm(av, bv.transpose(1, 2)) * alpha
+    if kg > 1:
+        av = _view(a, kg, M, K, ksA, lda, a_mn).float()
+        bv = _view(b, kg, N, K, ksB, ldb, b_mn).float()
+        acc = torch.bmm(av, bv.transpose(1, 2)).sum(0, keepdim=True) * alpha
+    else:
+        av = _view(a, G, M, K, gsA, lda, a_mn).float()
+        bv = _view(b, G, N, K, gsB, ldb, b_mn).float()
+        acc = torch.bmm(av, bv.transpose(1, 2)) * alpha
     if bias is not None:
         acc = acc + bias.as_strided((G, 1, N), (gs_bias, 0, 1)).float()
     if act in (ACT_DGELU, ACT_DRELU, ACT_DMUL):
         auxv = aux.as_strided((G, M, N), (gs_aux, ld_aux, 1)).float()
         acc = acc * {ACT_DGELU: gelu_grad, ACT_DRELU: lambda a: (a > 0).float(), ACT_DMUL: lambda a: a}[act](auxv)
+    if act == ACT_ADD:
+        acc = acc + aux.as_strided((G, M, N), (gs_aux, ld_aux, 1)).float()
     if act == ACT_RELU:
         acc = F.relu(acc)
     outv = out.as_strided((G, M, N), (gsC, ldc, 1))

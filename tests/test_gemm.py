@@ -93,3 +93,45 @@ def test_gemm_tcgen05_accumulate_fp32():
     ref = _ref(a, b, M, N, K, 1, lda, gsA, True, ldb, gsB, True)[0] + 1.0
     torch.cuda.synchronize()
     torch.testing.assert_close(out, ref, atol=2e-2, rtol=1e-3)
+
+
+def _shared_and_krange(device):
+    """A shared weight over a batch of row groups, and the weight gradient that sums
+    per-sample row ranges (the OneTrans S-token products)."""
+
+    torch.manual_seed(1)
+    B, L, s, K, N = 3, 200, 136, 128, 320
+    x = torch.randn(B, L, K, device=device).bfloat16()
+    w = torch.randn(N, K, device=device).bfloat16()
+    out = torch.zeros(B, L, N, device=device, dtype=torch.float32)
+    G.bgemm(x, w, out, M=s, N=N, K=K, G=B, lda=K, gsA=L * K, ldb=K, gsB=0, ldc=N, gsC=L * N)
+    ref = torch.zeros(B, L, N, device=device)
+    ref[:, :s] = x[:, :s].float() @ w.float().t()
+    dy = torch.randn(B, L, N, device=device).bfloat16()
+    gw = torch.zeros(N, K, device=device)
+    G.bgemm(dy, x, gw, M=N, N=K, K=s, lda=N, a_mn=True, ldb=K, b_mn=True, ldc=K, accumulate=True, kg=B,
+            ksA=L * N, ksB=L * K)
+    gref = torch.einsum("bln,blk->nk", dy[:, :s].float(), x[:, :s].float())
+    aux = torch.randn(B, L, N, device=device).bfloat16()
+    add = torch.zeros(B, L, N, device=device, dtype=torch.bfloat16)
+    G.bgemm(x, w, add, M=s, N=N, K=K, G=B, lda=K, gsA=L * K, ldb=K, gsB=0, ldc=N, gsC=L * N, aux=aux, ld_aux=N,
+            gs_aux=L * N, act=G.ACT_ADD)
+    add_ref = torch.zeros(B, L, N, device=device)
+    add_ref[:, :s] = ref[:, :s] + aux[:, :s].float()
+    return out, ref, gw, gref, add, add_ref, K, s
+
+
+def test_gemm_shared_operand_and_k_ranges_cpu():
+    out, ref, gw, gref, add, add_ref, _, _ = _shared_and_krange("cpu")
+    torch.testing.assert_close(out, ref)
+    torch.testing.assert_close(gw, gref, atol=1e-3, rtol=1e-4)
+    torch.testing.assert_close(add.float(), add_ref, atol=0.05, rtol=0.01)
+
+
+@pytest.mark.gpu
+def test_gemm_shared_operand_and_k_ranges_tcgen05():
+    out, ref, gw, gref, add, add_ref, K, s = _shared_and_krange("cuda")
+    torch.cuda.synchronize()
+    torch.testing.assert_close(out, ref, atol=2e-3 * K ** 0.5, rtol=1e-3)
+    torch.testing.assert_close(gw, gref, atol=2e-3 * (3 * s) ** 0.5, rtol=1e-3)
+    torch.testing.assert_close(add.float(), add_ref, atol=0.1, rtol=0.02)

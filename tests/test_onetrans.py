@@ -1,0 +1,84 @@
+"""OneTrans model: pyramid schedule, CPU training, CUDA path against the fp32 CPU definition."""
+
+import pytest
+import torch
+
+from mdl_b200.config.loader import app_config_from_mapping
+from mdl_b200.data.baseline_configs import scaled_config
+from mdl_b200.data.synthetic import SyntheticGenerator
+from mdl_b200.models.factory import build_model
+from mdl_b200.models.onetrans import pyramid_query_counts
+from mdl_b200.ops._ext import check_error_word
+from mdl_b200.train.trainer import Trainer
+
+
+def _small(seq_len=40, layers=3, min_len=10, heads=2, schedule="halve"):
+    m, spec = scaled_config(4, 1e-4, num_fields=12, batch=64, seq_len=seq_len, num_layers=layers,
+                            pyramid_schedule=schedule)
+    m["model"].update({"hidden_dim": 128, "token_dim": 32 * heads, "num_heads": heads, "num_ns_tokens": 4,
+                       "task_head_hidden_dim": 64, "pyramid_round_to": 8})
+    m["training"].update({"lr_warmup_steps": 0, "dense_optimizer": "adam", "lr_dense": 1e-3})
+    spec.sequences["behavior"].min_len = min_len
+    return app_config_from_mapping(m), spec
+
+
+def test_pyramid_schedules():
+    cfg4, _ = scaled_config(4, 1e-3, num_fields=8, batch=8)
+    cfg = app_config_from_mapping(cfg4)
+    assert pyramid_query_counts(cfg, 512, 32) == [512, 256, 256, 128, 128, 64]
+    m, _ = scaled_config(4, 1e-3, num_fields=8, batch=8, pyramid_schedule="linear")
+    m["model"]["final_s_tokens"] = 12
+    cfg = app_config_from_mapping(m)
+    # the reference's linear schedule (src/model.py:6181-6198), rounded to 32
+    assert pyramid_query_counts(cfg, 512, 32) == [416, 352, 256, 192, 96, 12]
+
+
+def test_onetrans_cpu_trains():
+    cfg, spec = _small()
+    torch.manual_seed(0)
+    model = build_model(cfg, device="cpu", base_seed=1)
+    tr = Trainer(cfg, model, device=torch.device("cpu"))
+    gen = SyntheticGenerator(model.encoder.batch_plan, spec)
+    batch = gen.batch(64)
+    losses = [float(tr.train_step(batch).loss) for _ in range(8)]
+    assert losses[-1] < losses[0]
+
+
+def test_onetrans_reference_state_dict_names():
+    cfg, _ = _small()
+    model = build_model(cfg, device="cpu", base_seed=1)
+    sd = model.reference_state_dict()
+    assert "backbone.blocks.0.attention.ns_query.3.weight" in sd
+    assert sd["backbone.blocks.0.attention.s_key.weight"].shape == (64, 64)
+    assert "backbone.tokenizer.auto_ns_projection.2.bias" in sd
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("variant", [dict(), dict(seq_len=300, layers=4, min_len=50, heads=4)])
+def test_onetrans_cuda_step_matches_cpu_reference(variant):
+    cfg, spec = _small(**variant)
+    torch.manual_seed(0)
+    cpu_model = build_model(cfg, device="cpu", base_seed=1)
+    gpu_model = build_model(cfg, device="cuda", base_seed=1)
+    gpu_model.load_state_dict({k: v.cuda() for k, v in cpu_model.state_dict().items()})
+    gpu_model.store.slab.copy_(cpu_model.store.slab)
+    cpu_tr = Trainer(cfg, cpu_model, device=torch.device("cpu"))
+    gpu_tr = Trainer(cfg, gpu_model, device=torch.device("cuda"))
+    gen = SyntheticGenerator(cpu_model.encoder.batch_plan, spec)
+    batch = gen.batch(64)
+    out_c = cpu_tr.forward_backward(batch)
+    out_g = gpu_tr.forward_backward(batch.to("cuda"))
+    torch.cuda.synchronize()
+    check_error_word(0)
+    torch.testing.assert_close(out_g["logits"].cpu(), out_c["logits"].detach(), atol=6e-2, rtol=6e-2)
+    torch.testing.assert_close(out_g["loss"].cpu(), out_c["loss"].detach(), atol=3e-2, rtol=3e-2)
+    gc, gg = cpu_tr.dense.grad, gpu_tr.dense.grad.cpu()
+    for name in cpu_tr.dense.names:
+        o = cpu_tr.dense.offsets[name]
+        n = cpu_tr.dense.params[name].numel()
+        ref, got = gc[o:o + n], gg[o:o + n]
+        err = ((ref - got).norm() / (ref.norm() + 1e-9)).item()
+        assert err < 0.06, f"{name}: grad error {err:.3f}"
+    ref = cpu_model.store.grad
+    got = gpu_model.store.grad.cpu()
+    assert ((ref - got).norm() / (ref.norm() + 1e-9)) < 0.06
