@@ -738,7 +738,8 @@ void fmha_fwd(const at::Tensor& qkv, const at::Tensor& kstart, const at::Tensor&
               int64_t Lq, bool causal, double scale, const std::optional<at::Tensor>& err) {
   c10::cuda::CUDAGuard guard(qkv.device());
   auto a = fmha_args(qkv, kstart, out, lse, H, Lq, causal, scale, err);
-  check(mdl::fmha_fwd(a, stream_of(qkv)), "fmha_fwd");
+  cudaError_t e = mdl::fmha_fwd(a, stream_of(qkv));
+  if (e != cudaSuccess) throw std::runtime_error(std::string(mdl::fmha_last_error()) + ": " + cudaGetErrorString(e));
   g_launches += 1;
 }
 
@@ -757,7 +758,8 @@ void fmha_bwd(const at::Tensor& qkv, const at::Tensor& kstart, const at::Tensor&
   a.dqkv = dqkv.data_ptr();
   a.dq_acc = dq_acc.data_ptr<float>();
   a.dsum = dsum.data_ptr<float>();
-  check(mdl::fmha_bwd(a, stream_of(qkv)), "fmha_bwd");
+  cudaError_t e = mdl::fmha_bwd(a, stream_of(qkv));
+  if (e != cudaSuccess) throw std::runtime_error(std::string(mdl::fmha_last_error()) + ": " + cudaGetErrorString(e));
   g_launches += 3;
 }
 

@@ -35,6 +35,9 @@
 //
 // Every wait is bounded (error word + abort flag) and every role drains what
 // it has in flight before the CTA exits.
+//
+// Registers: the 10 warps of a CTA spread 3/3/2/2 over the four SM sub-
+// partitions, each with 16K registers, so a thread may hold at most 168.
 #include <cudaTypedefs.h>
 
 #include <math_constants.h>
@@ -46,6 +49,14 @@
 
 namespace mdl {
 namespace {
+
+void bind_context_once() {
+  thread_local bool bound = false;
+  if (!bound) {
+    cudaFree(nullptr);  // makes the device's primary context current on this thread
+    bound = true;
+  }
+}
 
 constexpr int HD = 32;
 constexpr int TILE = 128;
@@ -148,6 +159,13 @@ __device__ __forceinline__ uint32_t swz_off(int r, int c) {
   return (c >> 3) * TILE_BYTES + r * 128 + (((c & 7) ^ (r & 7)) << 4);
 }
 
+// A wait whose outcome is the same on every lane of the warp: the tcgen05.ld /
+// wait::ld that follow are .sync.aligned and must be executed by the whole warp.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag) {
+  const bool ok = mbar_wait(bar, parity, err, abort_flag);
+  return __all_sync(0xffffffffu, ok);
+}
+
 __device__ __forceinline__ void red_add_v4(float* dst, float a, float b, float c, float d) {
   asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(dst), "f"(a), "f"(b), "f"(c),
                "f"(d)
@@ -155,7 +173,7 @@ __device__ __forceinline__ void red_add_v4(float* dst, float a, float b, float c
 }
 
 // ============================================================================ forward
-__global__ void __maxnreg__(200)
+__global__ void __launch_bounds__(NUM_THREADS, 1)
     fmha_fwd_kernel(const __grid_constant__ CUtensorMap tm, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -308,7 +326,7 @@ __global__ void __maxnreg__(200)
     bool ok = true;
     auto fold_pv = [&](int jj) -> bool {
       const int buf = jj & 1;
-      if (!mbar_wait(&pv_full[hl * 2 + buf], (jj >> 1) & 1, p.err, abort_flag)) return false;
+      if (!warp_wait(&pv_full[hl * 2 + buf], (jj >> 1) & 1, p.err, abort_flag)) return false;
       tc_fence_after();
       uint32_t pv[HD];
       tmem_ld32(t_lane + 128 + buf * 64 + hl * HD, pv);
@@ -323,7 +341,7 @@ __global__ void __maxnreg__(200)
     for (int j = 0; j < n; ++j) {
       const int t = t0 + j;
       const int kbase = Lk - TILE * (t + 1);
-      if (!mbar_wait(&s_full[hl], j & 1, p.err, abort_flag)) {
+      if (!warp_wait(&s_full[hl], j & 1, p.err, abort_flag)) {
         ok = false;
         break;
       }
@@ -348,7 +366,7 @@ __global__ void __maxnreg__(200)
       const float m_new = fmaxf(m, mx * p.scale2);
       const float m_use = m_new == -CUDART_INF_F ? 0.f : m_new;
       const float alpha = ex2(m - m_use);
-      if (j > 0 && !mbar_wait(&p_empty[hl], (j - 1) & 1, p.err, abort_flag)) {
+      if (j > 0 && !warp_wait(&p_empty[hl], (j - 1) & 1, p.err, abort_flag)) {
         ok = false;
         break;
       }
@@ -590,7 +608,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t pt_base = smem_u32(sPT), ds_base = smem_u32(sdST);
     bool ok = true;
     auto drain_dq = [&](int jj) -> bool {
-      if (!mbar_wait(dq_full, jj & 1, p.err, abort_flag)) return false;
+      if (!warp_wait(dq_full, jj & 1, p.err, abort_flag)) return false;
       tc_fence_after();
       uint32_t g[16];
       tmem_ld16(t_lane + 384 + wg * 16, g);
@@ -611,8 +629,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int j = 0; j < n; ++j) {
       const int st = j & 1;
       const int qrow0 = Lk - TILE * (j + 1);
-      if (!mbar_wait(&qd_full[st], (j >> 1) & 1, p.err, abort_flag) ||
-          !mbar_wait(st_full, j & 1, p.err, abort_flag)) {
+      if (!warp_wait(&qd_full[st], (j >> 1) & 1, p.err, abort_flag) ||
+          !warp_wait(st_full, j & 1, p.err, abort_flag)) {
         ok = false;
         break;
       }
@@ -626,7 +644,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(st_empty);
-      if (j > 0 && !mbar_wait(pds_empty, (j - 1) & 1, p.err, abort_flag)) {
+      if (j > 0 && !warp_wait(pds_empty, (j - 1) & 1, p.err, abort_flag)) {
         ok = false;
         break;
       }
@@ -657,11 +675,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
     if (ok && n > 0) ok = drain_dq(n - 1);
-    // dK (warpgroup 1) and dV (warpgroup 0) of this key tile
-    if (ok && krow >= 0) {
+    // dK (warpgroup 1) and dV (warpgroup 0) of this key tile. The TMEM read is
+    // done by whole warps; only the store depends on the lane's key row.
+    if (ok) {
       float g[HD];
+#pragma unroll
+      for (int d = 0; d < HD; ++d) g[d] = 0.f;
       if (n > 0) {
-        if (!mbar_wait(dkv_full, 0, p.err, abort_flag)) {
+        if (!warp_wait(dkv_full, 0, p.err, abort_flag)) {
           ok = false;
         } else {
           tc_fence_after();
@@ -671,11 +692,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
           for (int d = 0; d < HD; ++d) g[d] = key_ok ? __uint_as_float(gr[d]) : 0.f;
         }
-      } else {
-#pragma unroll
-        for (int d = 0; d < HD; ++d) g[d] = 0.f;
       }
-      if (ok) {
+      if (ok && krow >= 0) {
         uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.dqkv) +
                                               (static_cast<long long>(b) * Lk + krow) * 3 * p.D +
                                               (wg == 0 ? 2 * p.D : p.D) + h * HD);
@@ -733,6 +751,9 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // [B, L, W] bf16 rows (row stride W), box 64 x 128 x 1, 128-byte swizzle.
 bool encode_rows(CUtensorMap* map, const void* base, uint64_t W, uint64_t L, uint64_t B) {
   auto fn = encode_fn();
+  // The encoder is a driver call: it needs this thread's context current (an
+  // autograd worker thread may not have made any runtime call yet).
+  bind_context_once();
   if (fn == nullptr) return false;
   cuuint64_t dims[3] = {W, L, B};
   cuuint64_t strides[2] = {W * 2, L * W * 2};
@@ -763,6 +784,14 @@ Params make_params(const FmhaArgs& a) {
   return p;
 }
 
+const char* g_reason = "";
+
+// Records why a host call failed (read back by fmha_last_error()).
+cudaError_t fail(const char* why, cudaError_t e) {
+  if (e != cudaSuccess) g_reason = why;
+  return e;
+}
+
 bool shapes_ok(const FmhaArgs& a) {
   return a.hd == HD && a.B > 0 && a.H > 0 && a.Lq > 0 && a.Lq <= a.Lk && a.kstart != nullptr &&
          (reinterpret_cast<uintptr_t>(a.qkv) & 15) == 0;
@@ -773,47 +802,53 @@ bool shapes_ok(const FmhaArgs& a) {
 cudaError_t fmha_fwd(const FmhaArgs& a, cudaStream_t stream) {
   if (!shapes_ok(a) || (a.H & 1) || a.out == nullptr || a.lse == nullptr ||
       (reinterpret_cast<uintptr_t>(a.out) & 15))
-    return cudaErrorInvalidValue;
+    return fail("fmha_fwd: bad shapes or pointers", cudaErrorInvalidValue);
   const Params p = make_params(a);
   CUtensorMap tm;
-  if (!encode_rows(&tm, a.qkv, 3ull * p.D, a.Lk, a.B)) return cudaErrorInvalidValue;
+  if (!encode_rows(&tm, a.qkv, 3ull * p.D, a.Lk, a.B)) return fail("fmha_fwd: qkv tensor map", cudaErrorInvalidValue);
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(fmha_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, F_SMEM);
-    if (e != cudaSuccess) return e;
+    if (e != cudaSuccess) return fail("fmha_fwd: smem attribute", e);
     configured = true;
   }
   const long long grid = static_cast<long long>(a.H / 2) * a.B * ((a.Lq + TILE - 1) / TILE);
-  if (grid > 0x7fffffffLL) return cudaErrorInvalidValue;
+  if (grid > 0x7fffffffLL) return fail("fmha_fwd: grid", cudaErrorInvalidValue);
   fmha_fwd_kernel<<<static_cast<unsigned>(grid), NUM_THREADS, F_SMEM, stream>>>(tm, p);
-  return cudaGetLastError();
+  return fail("fmha_fwd: launch", cudaGetLastError());
 }
 
 cudaError_t fmha_bwd(const FmhaArgs& a, cudaStream_t stream) {
   if (!shapes_ok(a) || a.out == nullptr || a.lse == nullptr || a.dout == nullptr || a.dqkv == nullptr ||
       a.dq_acc == nullptr || a.dsum == nullptr || (reinterpret_cast<uintptr_t>(a.dout) & 15) ||
       (reinterpret_cast<uintptr_t>(a.dqkv) & 15) || (reinterpret_cast<uintptr_t>(a.dq_acc) & 15))
-    return cudaErrorInvalidValue;
+    return fail("fmha_bwd: bad shapes or pointers", cudaErrorInvalidValue);
   const Params p = make_params(a);
   CUtensorMap tm, tm_do;
-  if (!encode_rows(&tm, a.qkv, 3ull * p.D, a.Lk, a.B) || !encode_rows(&tm_do, a.dout, p.D, a.Lq, a.B))
-    return cudaErrorInvalidValue;
+  if (!encode_rows(&tm, a.qkv, 3ull * p.D, a.Lk, a.B)) return fail("fmha_bwd: qkv tensor map", cudaErrorInvalidValue);
+  if (!encode_rows(&tm_do, a.dout, p.D, a.Lq, a.B)) return fail("fmha_bwd: dout tensor map", cudaErrorInvalidValue);
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(fmha_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, B_SMEM);
-    if (e != cudaSuccess) return e;
+    if (e != cudaSuccess) return fail("fmha_bwd: smem attribute", e);
     configured = true;
   }
   const long long rows = static_cast<long long>(a.B) * a.Lq;
   fmha_bwd_pre_kernel<<<static_cast<unsigned>((rows * 32 + 255) / 256), 256, 0, stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(a.out), reinterpret_cast<const __nv_bfloat16*>(a.dout), a.dsum,
       a.dq_acc, a.B, a.Lq, a.H, p.D);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail("fmha_bwd: pre-kernel launch", e);
   const long long grid = static_cast<long long>(a.H) * a.B * ((a.Lk + TILE - 1) / TILE);
   fmha_bwd_kernel<<<static_cast<unsigned>(grid), NUM_THREADS, B_SMEM, stream>>>(tm, tm_do, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return fail("fmha_bwd: main launch", e);
   const long long vec = static_cast<long long>(a.B) * a.Lk * p.D / 8;
   fmha_bwd_post_kernel<<<static_cast<unsigned>((vec + 255) / 256), 256, 0, stream>>>(
       a.dq_acc, reinterpret_cast<__nv_bfloat16*>(a.dqkv), a.B, a.Lk, a.Lq, p.D);
-  return cudaGetLastError();
+  return fail("fmha_bwd: post-kernel launch", cudaGetLastError());
 }
+
+const char* fmha_last_error() { return g_reason; }
 
 }  // namespace mdl

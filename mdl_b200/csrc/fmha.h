@@ -38,5 +38,7 @@ struct FmhaArgs {
 
 cudaError_t fmha_fwd(const FmhaArgs& a, cudaStream_t stream);
 cudaError_t fmha_bwd(const FmhaArgs& a, cudaStream_t stream);
+// Which step of the last failing fmha_* call failed.
+const char* fmha_last_error();
 
 }  // namespace mdl

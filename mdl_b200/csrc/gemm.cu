@@ -30,6 +30,14 @@
 namespace mdl {
 namespace {
 
+void bind_context_once() {
+  thread_local bool bound = false;
+  if (!bound) {
+    cudaFree(nullptr);  // makes the device's primary context current on this thread
+    bound = true;
+  }
+}
+
 constexpr int BM = 128;
 constexpr int BN = 256;
 constexpr int BK = 64;   // 64 bf16 = 128 bytes = one swizzle row
@@ -249,7 +257,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      if (!mbar_wait(&tfull[acc], acc_phase, ep.err, abort_flag)) break;
+      // warp-uniform outcome: the tcgen05.ld below must be executed by the whole warp
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, ep.err, abort_flag))) break;
       tc_fence_after();
       const int g = tile / tiles_per_group;
       const int rem = tile - g * tiles_per_group;
@@ -477,6 +486,9 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 bool encode_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t groups,
                 uint64_t outer_stride_elems, uint64_t group_stride_elems, uint32_t box_outer) {
   auto fn = get_encode_fn();
+  // The encoder is a driver call: it needs this thread's context current (an
+  // autograd worker thread may not have made any runtime call yet).
+  bind_context_once();
   if (fn == nullptr) return false;
   cuuint64_t dims[3] = {inner, outer, groups};
   uint64_t gstride = group_stride_elems * 2;
