@@ -22,6 +22,7 @@
 // operand of the activation-derivative epilogues is read the same way.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -70,6 +71,8 @@ struct EpiParams {
   float alpha;
   int M, N, K, G;
   int KG;                  // K-range groups (G == 1 when KG > 1)
+  int splits;              // K slices per output tile (> 1: fp32 output reduced with atomics)
+  int kb_per_split;
   int a_shared, b_shared;  // operand shared by every group (batch stride 0)
   int* err;
 };
@@ -110,6 +113,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int n_tiles = (ep.N + BN - 1) / BN;
   const int tiles_per_group = m_tiles * n_tiles;
   const int num_tiles = tiles_per_group * ep.G;
+  const int num_units = num_tiles * ep.splits;  // work unit = (output tile, K slice)
   const int kb_per_range = (ep.K + BK - 1) / BK;
   const int k_blocks = kb_per_range * ep.KG;
 
@@ -143,12 +147,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t phase = 0;
       int issued = 0;  // stages filled but possibly not yet consumed
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int unit = blockIdx.x; unit < num_units && ok; unit += gridDim.x) {
+        const int tile = unit / ep.splits;
+        const int kb0 = (unit - tile * ep.splits) * ep.kb_per_split;
+        const int kb1 = min(k_blocks, kb0 + ep.kb_per_split);
         const int g = tile / tiles_per_group;
         const int rem = tile - g * tiles_per_group;
         const int mb = rem / n_tiles;
         const int nb = rem - mb * n_tiles;
-        for (int kb = 0; kb < k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, ep.err, abort_flag)) {
             ok = false;
             break;
@@ -202,11 +209,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int unit = blockIdx.x; unit < num_units && ok; unit += gridDim.x) {
+        const int tile = unit / ep.splits;
+        const int kb0 = (unit - tile * ep.splits) * ep.kb_per_split;
+        const int kb1 = min(k_blocks, kb0 + ep.kb_per_split);
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, ep.err, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, ep.err, abort_flag)) {
             ok = false;
             break;
@@ -222,7 +232,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                                         : make_smem_desc(a_stage + kk * 32, 16, 1024);
             const uint64_t bdesc = B_MN ? make_smem_desc(b_stage + kk * 2048, MN_CHUNK_BYTES, 1024)
                                         : make_smem_desc(b_stage + kk * 32, 16, 1024);
-            tc_mma_bf16(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+            tc_mma_bf16(d_tmem, adesc, bdesc, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
           }
           tc_commit(&empty[stage]);
           if (++stage == STAGES) {
@@ -256,7 +266,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int rsub = lane >> 3;              // row within each 4-row step (write-back)
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    const bool atomic_out = ep.splits > 1;  // K slices of one tile add into the fp32 output
+    for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x) {
+      const int tile = unit / ep.splits;
       // warp-uniform outcome: the tcgen05.ld below must be executed by the whole warp
       if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, ep.err, abort_flag))) break;
       tc_fence_after();
@@ -274,7 +286,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         constexpr bool need_aux = kAux;
         // Global reads of the chunk (aux or old output) run PF rows ahead: rows 0..PF-1 are
         // requested before the TMEM load, row r+PF as soon as row r is consumed.
-        const bool need_read = need_aux || accumulate;
+        const bool need_read = need_aux || (accumulate && !atomic_out);
         constexpr int PF = kF32 ? 2 : 4;  // rows in flight (fp32 rows need 4 registers each)
         uint4 pf[PF];
         auto prefetch = [&](int it) -> uint4 {
@@ -367,7 +379,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
             for (int e = 0; e < 4; ++e) csum[e] += t[e];
           }
-          if (kF32) {
+          if (kF32 && atomic_out) {
+            float* op = reinterpret_cast<float*>(ep.out) + off;
+            if (col_vec) {
+              asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(op), "f"(t[0]), "f"(t[1]),
+                           "f"(t[2]), "f"(t[3])
+                           : "memory");
+            } else {
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                if (e < ncols) atomicAdd(op + e, t[e]);
+            }
+          } else if (kF32) {
             float* op = reinterpret_cast<float*>(ep.out) + off;
             if (col_vec) {
               float4 o4 = make_float4(t[0], t[1], t[2], t[3]);
@@ -615,9 +638,24 @@ cudaError_t gemm_bf16_tcgen05(const GemmArgs& a, cudaStream_t stream) {
   ep.err = a.err;
   const long long tiles =
       static_cast<long long>((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN) * static_cast<long long>(a.G);
+  // Split K across CTAs when the output has too few tiles to fill the GPU (weight
+  // gradients: a few output tiles over a K of many thousand rows). Only for an fp32
+  // output that is accumulated into, which the slices then add to atomically.
+  const int total_kb = ((a.K + BK - 1) / BK) * a.KG;
+  ep.splits = 1;
+  ep.kb_per_split = total_kb;
+  if (epi == EPI_F32 && a.accumulate && tiles * 2 <= num_sms() && total_kb >= 8) {
+    long long want = (num_sms() + tiles - 1) / tiles;
+    want = std::min<long long>(want, total_kb / 4);
+    if (want > 1) {
+      ep.kb_per_split = static_cast<int>((total_kb + want - 1) / want);
+      ep.splits = (total_kb + ep.kb_per_split - 1) / ep.kb_per_split;
+    }
+  }
+  const long long units = tiles * ep.splits;
   int grid = num_sms();
   if (a.max_ctas > 0 && a.max_ctas < grid) grid = a.max_ctas;
-  if (tiles < grid) grid = static_cast<int>(tiles);
+  if (units < grid) grid = static_cast<int>(units);
   if (a.a_mn_major) {
     return a.b_mn_major ? launch<true, true>(ta, tb, ep, epi, grid, stream)
                         : launch<true, false>(ta, tb, ep, epi, grid, stream);
