@@ -16,16 +16,15 @@
 // tile i on the diagonal (the only tile with a causal mask) and key tiles
 // t > i in full. Rows before the first token read as zeros (TMA fill).
 //
-// Forward (320 threads, 1 CTA/SM, 512 TMEM columns): one CTA = one sample,
-// one pair of heads (head_dim 32: one 128-byte swizzled row of Q/K/V holds
-// both heads), one query tile.
-//   warp 0      TMA: Q once, then K/V tiles into a 2-stage ring
-//   warp 1      MMA: S_h = Q_h K_h^T (M=128, N=128, K=32) into TMEM,
-//               then PV_h = P_h V (M=128, N=64, K=128) into a TMEM double buffer
-//   warps 2-5   softmax of head 0, warps 6-9 head 1: thread = query row;
-//               online max / sum in base 2, P as bf16 into swizzled smem; the
-//               PV of tile j-1 is folded into the register accumulator while
-//               the tensor core works on tile j.
+// Forward (192 threads, 2 CTAs/SM, 256 TMEM columns each): one CTA = one
+// sample, one head, one query tile. TMA boxes are 64 columns (one 128-byte
+// swizzled row) starting at the head, so the MMAs read the head's 32 columns.
+//   warp 0      TMA: Q once, K tiles into a 2-stage ring, V single-buffered
+//   warp 1      MMA: S = Q K^T (M=128, N=128, K=32) into TMEM, then
+//               PV = P V (M=128, N=64, K=128) into a TMEM double buffer
+//   warps 2-5   softmax: thread = query row; online max / sum in base 2, P as
+//               bf16 into swizzled smem; the PV of tile j-1 is folded into the
+//               register accumulator while the tensor core works on tile j.
 // Backward (320 threads): one CTA = one sample, one head, one key tile; it
 // walks the query tiles that see those keys:
 //   S^T = K Q^T and dP^T = V dO^T (thread = key row), P^T = exp2(S^T*c - lse),
@@ -36,8 +35,8 @@
 // Every wait is bounded (error word + abort flag) and every role drains what
 // it has in flight before the CTA exits.
 //
-// Registers: the 10 warps of a CTA spread 3/3/2/2 over the four SM sub-
-// partitions, each with 16K registers, so a thread may hold at most 168.
+// Registers: 10 warps (backward) or 2 x 6 warps (forward) spread at most 3 per
+// SM sub-partition, each with 16K registers, so a thread may hold at most 168.
 #include <cudaTypedefs.h>
 
 #include <math_constants.h>
@@ -66,8 +65,10 @@ constexpr int NUM_THREADS = 320;
 constexpr int TMEM_COLS = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 
-// forward smem: Q | K[2] | V[2] | P[2] | barriers
-constexpr int F_SMEM = 1024 + TILE_BYTES * 5 + 2 * P_BYTES + 256;
+// forward (one head per CTA, two CTAs per SM): Q | K[2] | V | P | barriers
+constexpr int F_THREADS = 192;
+constexpr int F_TMEM = 256;
+constexpr int F_SMEM = 1024 + TILE_BYTES * 4 + P_BYTES + 256;
 // backward smem: K | V | Q[2] | dO[2] | P^T | dS^T | lse[2][128] | D[2][128] | barriers
 constexpr int B_SMEM = 1024 + TILE_BYTES * 6 + 2 * P_BYTES + 4 * TILE * 4 + 256;
 static_assert(F_SMEM <= 232448 && B_SMEM <= 232448, "shared memory budget");
@@ -173,62 +174,63 @@ __device__ __forceinline__ void red_add_v4(float* dst, float a, float b, float c
 }
 
 // ============================================================================ forward
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __launch_bounds__(F_THREADS, 2)
     fmha_fwd_kernel(const __grid_constant__ CUtensorMap tm, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sQ = smem;
-  uint8_t* sK = sQ + TILE_BYTES;
+  uint8_t* sK = sQ + TILE_BYTES;      // [2]
   uint8_t* sV = sK + 2 * TILE_BYTES;
-  uint8_t* sP = sV + 2 * TILE_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * P_BYTES);
+  uint8_t* sP = sV + TILE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + P_BYTES);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;     // [2]
-  uint64_t* kv_empty = bars + 3;    // [2]
-  uint64_t* s_full = bars + 5;      // [2 heads]
-  uint64_t* s_empty = bars + 7;     // [2]
-  uint64_t* p_full = bars + 9;      // [2]
-  uint64_t* p_empty = bars + 11;    // [2]
-  uint64_t* pv_full = bars + 13;    // [head*2 + buf]
-  uint64_t* pv_empty = bars + 17;   // [head*2 + buf]
-  uint64_t* done = bars + 21;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 22);
+  uint64_t* k_full = bars + 1;      // [2]
+  uint64_t* k_empty = bars + 3;     // [2]
+  uint64_t* v_full = bars + 5;
+  uint64_t* v_empty = bars + 6;
+  uint64_t* s_full = bars + 7;
+  uint64_t* s_empty = bars + 8;
+  uint64_t* p_full = bars + 9;
+  uint64_t* p_empty = bars + 10;
+  uint64_t* pv_full = bars + 11;    // [2]
+  uint64_t* pv_empty = bars + 13;   // [2]
+  uint64_t* done = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int HP = p.H >> 1;
-  const int hp = blockIdx.x % HP;
-  const int rest = blockIdx.x / HP;
+  const int h = blockIdx.x % p.H;
+  const int rest = blockIdx.x / p.H;
   const int b = rest % p.B;
-  const int i = rest / p.B;  // query tile (0 = last 128 rows)
-  const int h0 = hp * 2;
+  const int i = rest / p.B;  // query tile (0 = last 128 rows), heaviest first
   const int Lk = p.Lk;
   const int kst = min(max(p.kstart[b], 0), Lk);
   const int tmax = (Lk - kst + TILE - 1) / TILE - 1;
   const int t0 = p.causal ? i : 0;
   const int n = max(0, tmax - t0 + 1);  // key tiles this CTA visits
+  const int xq = h * HD, xk = p.D + h * HD, xv = 2 * p.D + h * HD;  // head h at box column 0
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
-      mbar_init(&s_full[s], 1);
-      mbar_init(&s_empty[s], 4);
-      mbar_init(&p_full[s], 4);
-      mbar_init(&p_empty[s], 1);
-    }
-    for (int s = 0; s < 4; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
       mbar_init(&pv_full[s], 1);
       mbar_init(&pv_empty[s], 4);
     }
+    mbar_init(v_full, 1);
+    mbar_init(v_empty, 1);
+    mbar_init(s_full, 1);
+    mbar_init(s_empty, 4);
+    mbar_init(p_full, 4);
+    mbar_init(p_empty, 1);
     mbar_init(done, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_alloc(tmem_slot, F_TMEM);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -239,73 +241,73 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0) {
     if (lane == 0 && n > 0) {
       tma_prefetch_desc(&tm);
+      auto kv_row = [&](int j) { return Lk - TILE * (t0 + j + 1); };
       mbar_arrive_expect_tx(q_full, TILE_BYTES);
-      tma_load_3d(sQ, &tm, q_full, h0 * HD, Lk - TILE * (i + 1), b);
-      int issued = 0;
-      for (int j = 0; j < n; ++j) {
-        const int st = j & 1;
-        if (j >= 2 && !mbar_wait(&kv_empty[st], ((j >> 1) - 1) & 1, p.err, abort_flag)) break;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * TILE_BYTES);
-        const int y = Lk - TILE * (t0 + j + 1);
-        tma_load_3d(sK + st * TILE_BYTES, &tm, &kv_full[st], p.D + h0 * HD, y, b);
-        tma_load_3d(sV + st * TILE_BYTES, &tm, &kv_full[st], 2 * p.D + h0 * HD, y, b);
-        issued = j + 1;
+      tma_load_3d(sQ, &tm, q_full, xq, Lk - TILE * (i + 1), b);
+      mbar_arrive_expect_tx(&k_full[0], TILE_BYTES);
+      tma_load_3d(sK, &tm, &k_full[0], xk, kv_row(0), b);
+      mbar_arrive_expect_tx(v_full, TILE_BYTES);
+      tma_load_3d(sV, &tm, v_full, xv, kv_row(0), b);
+      int k_issued = 1, v_issued = 1;
+      if (n > 1) {
+        mbar_arrive_expect_tx(&k_full[1], TILE_BYTES);
+        tma_load_3d(sK + TILE_BYTES, &tm, &k_full[1], xk, kv_row(1), b);
+        k_issued = 2;
+      }
+      for (int j = 1; j < n; ++j) {
+        // V(j) once PV(j-1) has read V(j-1); K(j+1) once S(j-1) has read its stage
+        if (!mbar_wait(v_empty, (j - 1) & 1, p.err, abort_flag)) break;
+        mbar_arrive_expect_tx(v_full, TILE_BYTES);
+        tma_load_3d(sV, &tm, v_full, xv, kv_row(j), b);
+        v_issued = j + 1;
+        if (j + 1 < n) {
+          const int st = (j + 1) & 1;
+          if (!mbar_wait(&k_empty[st], ((j - 1) >> 1) & 1, p.err, abort_flag)) break;
+          mbar_arrive_expect_tx(&k_full[st], TILE_BYTES);
+          tma_load_3d(sK + st * TILE_BYTES, &tm, &k_full[st], xk, kv_row(j + 1), b);
+          k_issued = j + 2;
+        }
       }
       // every copy into this CTA's smem has landed before the CTA may exit
       mbar_wait(q_full, 0, nullptr, nullptr);
-      for (int j = max(0, issued - 2); j < issued; ++j) mbar_wait(&kv_full[j & 1], (j >> 1) & 1, nullptr, nullptr);
+      for (int j = max(0, k_issued - 2); j < k_issued; ++j) mbar_wait(&k_full[j & 1], (j >> 1) & 1, nullptr, nullptr);
+      mbar_wait(v_full, (v_issued - 1) & 1, nullptr, nullptr);
     }
   } else if (warp == 1) {
     if (lane == 0 && n > 0) {
       constexpr uint32_t idesc_s = make_idesc_bf16(TILE, TILE, false, false);
       constexpr uint32_t idesc_pv = make_idesc_bf16(TILE, 64, false, true);
-      const uint32_t q_base = smem_u32(sQ);
-      const uint32_t k_base = smem_u32(sK);
-      const uint32_t v_base = smem_u32(sV);
-      const uint32_t p_base = smem_u32(sP);
-      bool ok = mbar_wait(q_full, 0, p.err, abort_flag) && mbar_wait(&kv_full[0], 0, p.err, abort_flag);
+      const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV), p_base = smem_u32(sP);
+      auto issue_s = [&](int j) {
+        const uint32_t kb = k_base + (j & 1) * TILE_BYTES;
+        for (int ks = 0; ks < 2; ++ks)
+          tc_mma_bf16(tmem, desc_k(q_base, ks * 32), desc_k(kb, ks * 32), idesc_s, ks);
+        tc_commit(&k_empty[j & 1]);
+        tc_commit(s_full);
+      };
+      bool ok = mbar_wait(q_full, 0, p.err, abort_flag) && mbar_wait(&k_full[0], 0, p.err, abort_flag);
       if (ok) {
         tc_fence_after();
-        for (int hl = 0; hl < 2; ++hl) {
-          for (int ks = 0; ks < 2; ++ks)
-            tc_mma_bf16(tmem + hl * 256, desc_k(q_base, hl * 64 + ks * 32), desc_k(k_base, hl * 64 + ks * 32),
-                        idesc_s, ks);
-          tc_commit(&s_full[hl]);
-        }
+        issue_s(0);
       }
       for (int j = 0; j < n && ok; ++j) {
         if (j + 1 < n) {
-          const int st1 = (j + 1) & 1;
-          if (!mbar_wait(&kv_full[st1], ((j + 1) >> 1) & 1, p.err, abort_flag)) break;
-          for (int hl = 0; hl < 2 && ok; ++hl) {
-            if (!mbar_wait(&s_empty[hl], j & 1, p.err, abort_flag)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            for (int ks = 0; ks < 2; ++ks)
-              tc_mma_bf16(tmem + hl * 256, desc_k(q_base, hl * 64 + ks * 32),
-                          desc_k(k_base + st1 * TILE_BYTES, hl * 64 + ks * 32), idesc_s, ks);
-            tc_commit(&s_full[hl]);
-          }
-          if (!ok) break;
-        }
-        const int st = j & 1;
-        for (int hl = 0; hl < 2 && ok; ++hl) {
-          if (!mbar_wait(&p_full[hl], j & 1, p.err, abort_flag) ||
-              (j >= 2 && !mbar_wait(&pv_empty[hl * 2 + st], ((j >> 1) - 1) & 1, p.err, abort_flag))) {
-            ok = false;
+          if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, p.err, abort_flag) ||
+              !mbar_wait(s_empty, j & 1, p.err, abort_flag))
             break;
-          }
           tc_fence_after();
-          const uint32_t d = tmem + hl * 256 + 128 + st * 64;
-          for (int ks = 0; ks < 8; ++ks)
-            tc_mma_bf16(d, desc_k128(p_base + hl * P_BYTES, ks), desc_mn(v_base + st * TILE_BYTES, ks), idesc_pv,
-                        ks);
-          tc_commit(&pv_full[hl * 2 + st]);
-          tc_commit(&p_empty[hl]);
+          issue_s(j + 1);
         }
-        tc_commit(&kv_empty[st]);
+        const int buf = j & 1;
+        if (!mbar_wait(p_full, j & 1, p.err, abort_flag) || !mbar_wait(v_full, j & 1, p.err, abort_flag) ||
+            (j >= 2 && !mbar_wait(&pv_empty[buf], ((j >> 1) - 1) & 1, p.err, abort_flag)))
+          break;
+        tc_fence_after();
+        for (int ks = 0; ks < 8; ++ks)
+          tc_mma_bf16(tmem + 128 + buf * 64, desc_k128(p_base, ks), desc_mn(v_base, ks), idesc_pv, ks);
+        tc_commit(&pv_full[buf]);
+        tc_commit(p_empty);
+        tc_commit(v_empty);
       }
       // all MMAs have finished before TMEM is released
       tc_commit(done);
@@ -313,12 +315,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax
-    const int hl = (warp - 2) >> 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const int qrow = Lk - TILE * (i + 1) + r;
-    const uint32_t t_lane = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + hl * 256;
-    const uint32_t p_base = smem_u32(sP + hl * P_BYTES);
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const uint32_t p_base = smem_u32(sP);
     float m = -CUDART_INF_F, l = 0.f, alpha_prev = 1.f;
     float o[HD];
 #pragma unroll
@@ -326,14 +327,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     bool ok = true;
     auto fold_pv = [&](int jj) -> bool {
       const int buf = jj & 1;
-      if (!warp_wait(&pv_full[hl * 2 + buf], (jj >> 1) & 1, p.err, abort_flag)) return false;
+      if (!warp_wait(&pv_full[buf], (jj >> 1) & 1, p.err, abort_flag)) return false;
       tc_fence_after();
       uint32_t pv[HD];
-      tmem_ld32(t_lane + 128 + buf * 64 + hl * HD, pv);
+      tmem_ld32(t_lane + 128 + buf * 64, pv);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&pv_empty[hl * 2 + buf]);
+      if (lane == 0) mbar_arrive(&pv_empty[buf]);
 #pragma unroll
       for (int d = 0; d < HD; ++d) o[d] = fmaf(o[d], alpha_prev, __uint_as_float(pv[d]));
       return true;
@@ -341,7 +342,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int j = 0; j < n; ++j) {
       const int t = t0 + j;
       const int kbase = Lk - TILE * (t + 1);
-      if (!warp_wait(&s_full[hl], j & 1, p.err, abort_flag)) {
+      if (!warp_wait(s_full, j & 1, p.err, abort_flag)) {
         ok = false;
         break;
       }
@@ -352,8 +353,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s_empty[hl]);
-      const int lo = kst - kbase;                        // columns < lo are padding
+      if (lane == 0) mbar_arrive(s_empty);
+      const int lo = kst - kbase;                          // columns < lo are padding
       const int hi = (p.causal && t == i) ? r : TILE - 1;  // columns > hi are in the future
       if (lo > 0 || hi < TILE - 1) {
 #pragma unroll
@@ -366,7 +367,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const float m_new = fmaxf(m, mx * p.scale2);
       const float m_use = m_new == -CUDART_INF_F ? 0.f : m_new;
       const float alpha = ex2(m - m_use);
-      if (j > 0 && !warp_wait(&p_empty[hl], (j - 1) & 1, p.err, abort_flag)) {
+      if (j > 0 && !warp_wait(p_empty, (j - 1) & 1, p.err, abort_flag)) {
         ok = false;
         break;
       }
@@ -384,7 +385,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       fence_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[hl]);
+      if (lane == 0) mbar_arrive(p_full);
       l = fmaf(l, alpha, sum);
       m = m_new;
       if (j > 0 && !fold_pv(j - 1)) {
@@ -396,7 +397,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (ok && n > 0) ok = fold_pv(n - 1);
     if (ok) {
       const int qi = qrow - (Lk - p.Lq);
-      const int h = h0 + hl;
       if (qi >= 0) {
         const bool valid = qrow >= kst && l > 0.f;
         const float inv = valid ? 1.f / l : 0.f;
@@ -414,7 +414,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, TMEM_COLS);
+    tmem_dealloc(tmem, F_TMEM);
   }
 }
 
@@ -565,20 +565,29 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       constexpr uint32_t idesc_q = make_idesc_bf16(TILE, 64, true, true);
       const uint32_t k_base = smem_u32(sK), v_base = smem_u32(sV);
       const uint32_t pt_base = smem_u32(sPT), ds_base = smem_u32(sdST);
-      bool ok = mbar_wait(kv_full, 0, p.err, abort_flag);
-      for (int j = 0; j < n && ok; ++j) {
+      // S^T / dP^T of tile j+1 are issued as soon as the compute warps hold tile j in
+      // registers, so the tensor core works on them while tile j is being processed.
+      auto issue_s = [&](int j) -> bool {
         const int st = j & 1;
-        const uint32_t q_base = smem_u32(sQ + st * TILE_BYTES);
-        const uint32_t do_base = smem_u32(sdO + st * TILE_BYTES);
         if (!mbar_wait(&qd_full[st], (j >> 1) & 1, p.err, abort_flag) ||
             (j > 0 && !mbar_wait(st_empty, (j - 1) & 1, p.err, abort_flag)))
-          break;
+          return false;
         tc_fence_after();
+        const uint32_t q_base = smem_u32(sQ + st * TILE_BYTES);
+        const uint32_t do_base = smem_u32(sdO + st * TILE_BYTES);
         for (int ks = 0; ks < 2; ++ks) {
           tc_mma_bf16(tmem, desc_k(k_base, ks * 32), desc_k(q_base, ks * 32), idesc_s, ks);
           tc_mma_bf16(tmem + 128, desc_k(v_base, ks * 32), desc_k(do_base, ks * 32), idesc_s, ks);
         }
         tc_commit(st_full);
+        return true;
+      };
+      bool ok = mbar_wait(kv_full, 0, p.err, abort_flag) && issue_s(0);
+      for (int j = 0; j < n && ok; ++j) {
+        const int st = j & 1;
+        const uint32_t q_base = smem_u32(sQ + st * TILE_BYTES);
+        const uint32_t do_base = smem_u32(sdO + st * TILE_BYTES);
+        if (j + 1 < n && !issue_s(j + 1)) break;
         if (!mbar_wait(pds_full, j & 1, p.err, abort_flag)) break;
         tc_fence_after();
         for (int ks = 0; ks < 8; ++ks) {
@@ -800,7 +809,7 @@ bool shapes_ok(const FmhaArgs& a) {
 }  // namespace
 
 cudaError_t fmha_fwd(const FmhaArgs& a, cudaStream_t stream) {
-  if (!shapes_ok(a) || (a.H & 1) || a.out == nullptr || a.lse == nullptr ||
+  if (!shapes_ok(a) || a.out == nullptr || a.lse == nullptr ||
       (reinterpret_cast<uintptr_t>(a.out) & 15))
     return fail("fmha_fwd: bad shapes or pointers", cudaErrorInvalidValue);
   const Params p = make_params(a);
@@ -812,9 +821,9 @@ cudaError_t fmha_fwd(const FmhaArgs& a, cudaStream_t stream) {
     if (e != cudaSuccess) return fail("fmha_fwd: smem attribute", e);
     configured = true;
   }
-  const long long grid = static_cast<long long>(a.H / 2) * a.B * ((a.Lq + TILE - 1) / TILE);
+  const long long grid = static_cast<long long>(a.H) * a.B * ((a.Lq + TILE - 1) / TILE);
   if (grid > 0x7fffffffLL) return fail("fmha_fwd: grid", cudaErrorInvalidValue);
-  fmha_fwd_kernel<<<static_cast<unsigned>(grid), NUM_THREADS, F_SMEM, stream>>>(tm, p);
+  fmha_fwd_kernel<<<static_cast<unsigned>(grid), F_THREADS, F_SMEM, stream>>>(tm, p);
   return fail("fmha_fwd: launch", cudaGetLastError());
 }
 

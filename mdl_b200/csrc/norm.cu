@@ -332,73 +332,134 @@ __global__ void __launch_bounds__(256) rms_fwd_kernel(const RMSArgs p) {
   if (lane == 0 && p.rstd) p.rstd[r] = rstd;
 }
 
+// Row of the residual gradient added to dx row r (nullptr: none).
+__device__ __forceinline__ const __nv_bfloat16* rms_res_row(const RMSArgs& p, long long r) {
+  if (p.dres == nullptr) return nullptr;
+  long long rr = r;
+  if (p.res_period > 0) {
+    const long long smp = r / p.res_period;
+    const int e = static_cast<int>(r - smp * p.res_period) - (p.res_period - p.res_tail);
+    if (e < 0) return nullptr;
+    rr = smp * p.res_tail + e;
+  }
+  return reinterpret_cast<const __nv_bfloat16*>(p.dres) + rr * p.D;
+}
+
+// One warp per row, two independent rows in flight per warp; the weight
+// gradient is reduced over the block's warps in shared memory before one
+// atomic add per column and block.
 template <int NCH>
 __global__ void __launch_bounds__(256) rms_bwd_kernel(const RMSArgs p) {
+  constexpr int R = NCH <= 2 ? 2 : 1;  // rows in flight per warp (registers allow two for D <= 512)
+  __shared__ float sdw[8][256];
   const int lane = threadIdx.x & 31;
+  const int wib = threadIdx.x >> 5;
   const long long warps = static_cast<long long>(gridDim.x) * 8;
+  constexpr bool kKeepW = NCH <= 2;  // weights stay in registers for small D, reloaded otherwise
+  float wreg[kKeepW ? NCH : 1][8];
   float dw[NCH][8];
 #pragma unroll
-  for (int k = 0; k < NCH; ++k)
+  for (int k = 0; k < NCH; ++k) {
+    const int c = (lane + 32 * k) * 8;
+    if (kKeepW && c < p.D) load_f8(p.weight, c, wreg[kKeepW ? k : 0], 1.f);
 #pragma unroll
     for (int e = 0; e < 8; ++e) dw[k][e] = 0.f;
-  for (long long r = (static_cast<long long>(blockIdx.x) * 256 + threadIdx.x) >> 5; r < p.rows; r += warps) {
-    const auto* x = reinterpret_cast<const __nv_bfloat16*>(p.x) + r * p.D;
-    const auto* dy = reinterpret_cast<const __nv_bfloat16*>(p.dy) + r * p.D;
-    const float rstd = p.rstd[r];
-    float xv[NCH][8], gv[NCH][8];
-    float s = 0.f;
+  }
+  auto weights = [&](int k, int c, float* w) {
+    if constexpr (kKeepW) {
 #pragma unroll
-    for (int k = 0; k < NCH; ++k) {
-      const int c = (lane + 32 * k) * 8;
-      if (c < p.D) {
-        load8(x + c, xv[k]);
-        load8(dy + c, gv[k]);
-        float w[8];
-        load_f8(p.weight, c, w, 1.f);
+      for (int e = 0; e < 8; ++e) w[e] = wreg[kKeepW ? k : 0][e];
+    } else {
+      load_f8(p.weight, c, w, 1.f);
+    }
+  };
+  for (long long r0 = (static_cast<long long>(blockIdx.x) * 256 + threadIdx.x) >> 5; r0 < p.rows; r0 += R * warps) {
+    long long rr[R];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          s += gv[k][e] * w[e] * xv[k][e];
-          dw[k][e] += gv[k][e] * xv[k][e] * rstd;
+    for (int u = 0; u < R; ++u) rr[u] = r0 + u * warps;
+    float xv[R][NCH][8], gv[R][NCH][8], res[R][NCH][8];
+    float s[R], rstd[R];
+    bool has_res[R];
+#pragma unroll
+    for (int u = 0; u < R; ++u) {
+      s[u] = 0.f;
+      rstd[u] = 0.f;
+      has_res[u] = false;
+    }
+#pragma unroll
+    for (int u = 0; u < R; ++u) {
+      if (rr[u] >= p.rows) continue;
+      const auto* x = reinterpret_cast<const __nv_bfloat16*>(p.x) + rr[u] * p.D;
+      const auto* dy = reinterpret_cast<const __nv_bfloat16*>(p.dy) + rr[u] * p.D;
+      const __nv_bfloat16* rs = rms_res_row(p, rr[u]);
+      has_res[u] = rs != nullptr;
+      rstd[u] = p.rstd[rr[u]];
+#pragma unroll
+      for (int k = 0; k < NCH; ++k) {
+        const int c = (lane + 32 * k) * 8;
+        if (c < p.D) {
+          load8(x + c, xv[u][k]);
+          load8(dy + c, gv[u][k]);
+          if (rs != nullptr) load8(rs + c, res[u][k]);
         }
       }
     }
-    s = warp_sum(s) / p.D;
-    auto* dx = reinterpret_cast<__nv_bfloat16*>(p.dx) + r * p.D;
-    const __nv_bfloat16* res = nullptr;
-    if (p.dres != nullptr) {
-      long long rr = r;
-      if (p.res_period > 0) {
-        const long long smp = r / p.res_period;
-        const int e = static_cast<int>(r - smp * p.res_period) - (p.res_period - p.res_tail);
-        rr = e >= 0 ? smp * p.res_tail + e : -1;
+#pragma unroll
+    for (int u = 0; u < R; ++u) {
+      if (rr[u] >= p.rows) continue;
+#pragma unroll
+      for (int k = 0; k < NCH; ++k) {
+        const int c = (lane + 32 * k) * 8;
+        if (c < p.D) {
+          float w[8];
+          weights(k, c, w);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            s[u] += gv[u][k][e] * w[e] * xv[u][k][e];
+            dw[k][e] += gv[u][k][e] * xv[u][k][e] * rstd[u];
+          }
+        }
       }
-      if (rr >= 0) res = reinterpret_cast<const __nv_bfloat16*>(p.dres) + rr * p.D;
     }
 #pragma unroll
-    for (int k = 0; k < NCH; ++k) {
-      const int c = (lane + 32 * k) * 8;
-      if (c < p.D) {
-        float o[8], w[8];
-        load_f8(p.weight, c, w, 1.f);
+    for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-        for (int e = 0; e < 8; ++e) o[e] = rstd * (gv[k][e] * w[e] - xv[k][e] * rstd * rstd * s);
-        if (res != nullptr) {
-          float rv[8];
-          load8(res + c, rv);
+      for (int u = 0; u < R; ++u) s[u] += __shfl_xor_sync(0xffffffffu, s[u], o);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) o[e] += rv[e];
+    for (int u = 0; u < R; ++u) {
+      if (rr[u] >= p.rows) continue;
+      const float su = s[u] / p.D;
+      auto* dx = reinterpret_cast<__nv_bfloat16*>(p.dx) + rr[u] * p.D;
+#pragma unroll
+      for (int k = 0; k < NCH; ++k) {
+        const int c = (lane + 32 * k) * 8;
+        if (c < p.D) {
+          float o[8], w[8];
+          weights(k, c, w);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            o[e] = rstd[u] * (gv[u][k][e] * w[e] - xv[u][k][e] * rstd[u] * rstd[u] * su);
+            if (has_res[u]) o[e] += res[u][k][e];
+          }
+          store8(dx + c, o);
         }
-        store8(dx + c, o);
       }
     }
   }
   if (p.dweight) {
 #pragma unroll
-    for (int k = 0; k < NCH; ++k) {
-      const int c = (lane + 32 * k) * 8;
-      if (c < p.D)
+    for (int k = 0; k < NCH; ++k) {  // 256 columns at a time
 #pragma unroll
-        for (int e = 0; e < 8; ++e) atomicAdd(p.dweight + c + e, dw[k][e]);
+      for (int e = 0; e < 8; ++e) sdw[wib][lane * 8 + e] = dw[k][e];
+      __syncthreads();
+      const int c = k * 256 + threadIdx.x;
+      if (c < p.D) {
+        float t = 0.f;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) t += sdw[q][threadIdx.x];
+        atomicAdd(p.dweight + c, t);
+      }
+      __syncthreads();
     }
   }
 }
@@ -476,8 +537,8 @@ cudaError_t rmsnorm_fwd(const RMSArgs& a, cudaStream_t stream) {
 cudaError_t rmsnorm_bwd(const RMSArgs& a, cudaStream_t stream) {
   if (a.D % 8) return cudaErrorInvalidValue;
   if (a.rows == 0) return cudaSuccess;
-  long long want = (a.rows + 7) / 8;
-  const int grid = static_cast<int>(want < sm_count() * 4 ? want : sm_count() * 4);
+  long long want = (a.rows + 15) / 16;  // two rows per warp per step
+  const int grid = static_cast<int>(want < sm_count() * 8 ? want : sm_count() * 8);
 #define RMB(N) rms_bwd_kernel<N><<<grid, 256, 0, stream>>>(a);
   MDL_NCH_DISPATCH(a.D, RMB)
 #undef RMB

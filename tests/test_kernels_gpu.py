@@ -119,9 +119,10 @@ def test_layernorm_fused(mix, B, T, D):
     torch.testing.assert_close(db, bf.grad, atol=0.5, rtol=2e-2)
 
 
-def test_rmsnorm():
+@pytest.mark.parametrize("D", [256, 512, 1024])
+def test_rmsnorm(D):
     torch.manual_seed(0)
-    R, D = 300, 256
+    R = 300
     x = torch.randn(R, D, device="cuda").bfloat16()
     w = torch.randn(D, device="cuda")
     out = torch.empty_like(x)
@@ -140,6 +141,31 @@ def test_rmsnorm():
     torch.cuda.synchronize()
     torch.testing.assert_close(dx.float(), xf.grad, atol=5e-2, rtol=2e-2)
     torch.testing.assert_close(dw, wf.grad, atol=0.3, rtol=2e-2)
+
+
+def test_rmsnorm_backward_residual():
+    """dx += residual gradient: same layout, and the last `tail` rows of each sample."""
+
+    torch.manual_seed(1)
+    Bs, period, tail, D = 7, 50, 20, 256
+    R = Bs * period
+    x = torch.randn(R, D, device="cuda").bfloat16()
+    w = torch.randn(D, device="cuda")
+    out, rstd = torch.empty_like(x), torch.empty(R, device="cuda")
+    C = ext()
+    C.rms_fwd(x, w, out, rstd, R, D, 1e-6)
+    dy = torch.randn(R, D, device="cuda").bfloat16()
+    base = torch.empty_like(x)
+    C.rms_bwd(x, w, rstd, dy, base, None, R, D)
+    same = torch.randn(R, D, device="cuda").bfloat16()
+    dx = torch.empty_like(x)
+    C.rms_bwd(x, w, rstd, dy, dx, None, R, D, dres=same)
+    torch.testing.assert_close(dx.float(), base.float() + same.float(), atol=3e-2, rtol=1e-2)
+    part = torch.randn(Bs * tail, D, device="cuda").bfloat16()
+    C.rms_bwd(x, w, rstd, dy, dx, None, R, D, dres=part, res_period=period, res_tail=tail)
+    want = base.float().view(Bs, period, D).clone()
+    want[:, period - tail:] += part.float().view(Bs, tail, D)
+    torch.testing.assert_close(dx.float(), want.view(R, D), atol=3e-2, rtol=1e-2)
 
 
 def test_head_bce():
