@@ -19,7 +19,7 @@
 // Forward (192 threads, 2 CTAs/SM, 256 TMEM columns each): one CTA = one
 // sample, one head, one query tile. TMA boxes are 64 columns (one 128-byte
 // swizzled row) starting at the head, so the MMAs read the head's 32 columns.
-//   warp 0      TMA: Q once, K tiles into a 2-stage ring, V single-buffered
+//   warp 0      TMA: Q once, K and V tiles into 2-stage rings
 //   warp 1      MMA: S = Q K^T (M=128, N=128, K=32) into TMEM, then
 //               PV = P V (M=128, N=64, K=128) into a TMEM double buffer
 //   warps 2-5   softmax: thread = query row; online max / sum in base 2, P as
@@ -65,10 +65,13 @@ constexpr int NUM_THREADS = 320;
 constexpr int TMEM_COLS = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 
-// forward (one head per CTA, two CTAs per SM): Q | K[2] | V | P | barriers
+// forward (one head per CTA, two CTAs per SM): Q | K[2] | V[2] | P | barriers. Two
+// CTAs fit in the SM's shared memory only without alignment slack: the kernel
+// relies on the dynamic shared memory base being 1024-byte aligned (it is when
+// the kernel has no static shared memory) and checks it.
 constexpr int F_THREADS = 192;
 constexpr int F_TMEM = 256;
-constexpr int F_SMEM = 1024 + TILE_BYTES * 4 + P_BYTES + 256;
+constexpr int F_SMEM = TILE_BYTES * 5 + P_BYTES + 256;
 // backward smem: K | V | Q[2] | dO[2] | P^T | dS^T | lse[2][128] | D[2][128] | barriers
 constexpr int B_SMEM = 1024 + TILE_BYTES * 6 + 2 * P_BYTES + 4 * TILE * 4 + 256;
 static_assert(F_SMEM <= 232448 && B_SMEM <= 232448, "shared memory budget");
@@ -176,26 +179,29 @@ __device__ __forceinline__ void red_add_v4(float* dst, float a, float b, float c
 // ============================================================================ forward
 __global__ void __launch_bounds__(F_THREADS, 2)
     fmha_fwd_kernel(const __grid_constant__ CUtensorMap tm, const Params p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = align1024(smem_raw);
-  uint8_t* sQ = smem;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if (smem_u32(smem_raw) & 1023) {  // uniform across the CTA: nothing has been touched yet
+    if (threadIdx.x == 0) record_error(p.err, MDL_ERR_BAD_ARG);
+    return;
+  }
+  uint8_t* sQ = smem_raw;
   uint8_t* sK = sQ + TILE_BYTES;      // [2]
-  uint8_t* sV = sK + 2 * TILE_BYTES;
-  uint8_t* sP = sV + TILE_BYTES;
+  uint8_t* sV = sK + 2 * TILE_BYTES;  // [2]
+  uint8_t* sP = sV + 2 * TILE_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + P_BYTES);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;      // [2]
   uint64_t* k_empty = bars + 3;     // [2]
-  uint64_t* v_full = bars + 5;
-  uint64_t* v_empty = bars + 6;
-  uint64_t* s_full = bars + 7;
-  uint64_t* s_empty = bars + 8;
-  uint64_t* p_full = bars + 9;
-  uint64_t* p_empty = bars + 10;
-  uint64_t* pv_full = bars + 11;    // [2]
-  uint64_t* pv_empty = bars + 13;   // [2]
-  uint64_t* done = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* v_full = bars + 5;      // [2]
+  uint64_t* v_empty = bars + 7;     // [2]
+  uint64_t* s_full = bars + 9;
+  uint64_t* s_empty = bars + 10;
+  uint64_t* p_full = bars + 11;
+  uint64_t* p_empty = bars + 12;
+  uint64_t* pv_full = bars + 13;    // [2]
+  uint64_t* pv_empty = bars + 15;   // [2]
+  uint64_t* done = bars + 17;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -216,11 +222,11 @@ __global__ void __launch_bounds__(F_THREADS, 2)
     for (int s = 0; s < 2; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
       mbar_init(&pv_full[s], 1);
       mbar_init(&pv_empty[s], 4);
     }
-    mbar_init(v_full, 1);
-    mbar_init(v_empty, 1);
     mbar_init(s_full, 1);
     mbar_init(s_empty, 4);
     mbar_init(p_full, 4);
@@ -244,34 +250,23 @@ __global__ void __launch_bounds__(F_THREADS, 2)
       auto kv_row = [&](int j) { return Lk - TILE * (t0 + j + 1); };
       mbar_arrive_expect_tx(q_full, TILE_BYTES);
       tma_load_3d(sQ, &tm, q_full, xq, Lk - TILE * (i + 1), b);
-      mbar_arrive_expect_tx(&k_full[0], TILE_BYTES);
-      tma_load_3d(sK, &tm, &k_full[0], xk, kv_row(0), b);
-      mbar_arrive_expect_tx(v_full, TILE_BYTES);
-      tma_load_3d(sV, &tm, v_full, xv, kv_row(0), b);
-      int k_issued = 1, v_issued = 1;
-      if (n > 1) {
-        mbar_arrive_expect_tx(&k_full[1], TILE_BYTES);
-        tma_load_3d(sK + TILE_BYTES, &tm, &k_full[1], xk, kv_row(1), b);
-        k_issued = 2;
-      }
-      for (int j = 1; j < n; ++j) {
-        // V(j) once PV(j-1) has read V(j-1); K(j+1) once S(j-1) has read its stage
-        if (!mbar_wait(v_empty, (j - 1) & 1, p.err, abort_flag)) break;
-        mbar_arrive_expect_tx(v_full, TILE_BYTES);
-        tma_load_3d(sV, &tm, v_full, xv, kv_row(j), b);
+      // K and V tiles in 2-stage rings; stage j&1 is refilled once S(j-2) / PV(j-2) read it
+      int k_issued = 0, v_issued = 0;
+      for (int j = 0; j < n; ++j) {
+        const int st = j & 1;
+        if (j >= 2 && (!mbar_wait(&k_empty[st], ((j >> 1) - 1) & 1, p.err, abort_flag))) break;
+        mbar_arrive_expect_tx(&k_full[st], TILE_BYTES);
+        tma_load_3d(sK + st * TILE_BYTES, &tm, &k_full[st], xk, kv_row(j), b);
+        k_issued = j + 1;
+        if (j >= 2 && (!mbar_wait(&v_empty[st], ((j >> 1) - 1) & 1, p.err, abort_flag))) break;
+        mbar_arrive_expect_tx(&v_full[st], TILE_BYTES);
+        tma_load_3d(sV + st * TILE_BYTES, &tm, &v_full[st], xv, kv_row(j), b);
         v_issued = j + 1;
-        if (j + 1 < n) {
-          const int st = (j + 1) & 1;
-          if (!mbar_wait(&k_empty[st], ((j - 1) >> 1) & 1, p.err, abort_flag)) break;
-          mbar_arrive_expect_tx(&k_full[st], TILE_BYTES);
-          tma_load_3d(sK + st * TILE_BYTES, &tm, &k_full[st], xk, kv_row(j + 1), b);
-          k_issued = j + 2;
-        }
       }
       // every copy into this CTA's smem has landed before the CTA may exit
       mbar_wait(q_full, 0, nullptr, nullptr);
       for (int j = max(0, k_issued - 2); j < k_issued; ++j) mbar_wait(&k_full[j & 1], (j >> 1) & 1, nullptr, nullptr);
-      mbar_wait(v_full, (v_issued - 1) & 1, nullptr, nullptr);
+      for (int j = max(0, v_issued - 2); j < v_issued; ++j) mbar_wait(&v_full[j & 1], (j >> 1) & 1, nullptr, nullptr);
     }
   } else if (warp == 1) {
     if (lane == 0 && n > 0) {
@@ -299,15 +294,17 @@ __global__ void __launch_bounds__(F_THREADS, 2)
           issue_s(j + 1);
         }
         const int buf = j & 1;
-        if (!mbar_wait(p_full, j & 1, p.err, abort_flag) || !mbar_wait(v_full, j & 1, p.err, abort_flag) ||
+        if (!mbar_wait(p_full, j & 1, p.err, abort_flag) ||
+            !mbar_wait(&v_full[buf], (j >> 1) & 1, p.err, abort_flag) ||
             (j >= 2 && !mbar_wait(&pv_empty[buf], ((j >> 1) - 1) & 1, p.err, abort_flag)))
           break;
         tc_fence_after();
         for (int ks = 0; ks < 8; ++ks)
-          tc_mma_bf16(tmem + 128 + buf * 64, desc_k128(p_base, ks), desc_mn(v_base, ks), idesc_pv, ks);
+          tc_mma_bf16(tmem + 128 + buf * 64, desc_k128(p_base, ks), desc_mn(v_base + buf * TILE_BYTES, ks),
+                      idesc_pv, ks);
         tc_commit(&pv_full[buf]);
         tc_commit(p_empty);
-        tc_commit(v_empty);
+        tc_commit(&v_empty[buf]);
       }
       // all MMAs have finished before TMEM is released
       tc_commit(done);
