@@ -16,8 +16,8 @@
 // tile i on the diagonal (the only tile with a causal mask) and key tiles
 // t > i in full. Rows before the first token read as zeros (TMA fill).
 //
-// Forward (192 threads, 2 CTAs/SM, 256 TMEM columns each): one CTA = one
-// sample, one head, one query tile. TMA boxes are 64 columns (one 128-byte
+// Forward (192 threads, 2 persistent CTAs/SM, 256 TMEM columns each): a work
+// item = one sample, one head, one query tile. TMA boxes are 64 columns (one 128-byte
 // swizzled row) starting at the head, so the MMAs read the head's 32 columns.
 //   warp 0      TMA: Q once, K and V tiles into 2-stage rings
 //   warp 1      MMA: S = Q K^T (M=128, N=128, K=32) into TMEM, then
@@ -25,8 +25,8 @@
 //   warps 2-5   softmax: thread = query row; online max / sum in base 2, P as
 //               bf16 into swizzled smem; the PV of tile j-1 is folded into the
 //               register accumulator while the tensor core works on tile j.
-// Backward (320 threads): one CTA = one sample, one head, one key tile; it
-// walks the query tiles that see those keys:
+// Backward (320 threads, one persistent CTA per SM): a work item = one sample,
+// one head, one key tile; it walks the query tiles that see those keys:
 //   S^T = K Q^T and dP^T = V dO^T (thread = key row), P^T = exp2(S^T*c - lse),
 //   dS^T = P^T (dP^T - D) * scale, dV += P^T dO, dK += dS^T Q (accumulated in
 //   TMEM), dQ_tile = dS K (same smem dS^T read as an MN-major operand) added
@@ -41,6 +41,7 @@
 
 #include <math_constants.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -72,8 +73,8 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr int F_THREADS = 192;
 constexpr int F_TMEM = 256;
 constexpr int F_SMEM = TILE_BYTES * 5 + P_BYTES + 256;
-// backward smem: K | V | Q[2] | dO[2] | P^T | dS^T | lse[2][128] | D[2][128] | barriers
-constexpr int B_SMEM = 1024 + TILE_BYTES * 6 + 2 * P_BYTES + 4 * TILE * 4 + 256;
+// backward smem: K[2] | V[2] | Q[2] | dO[2] | P^T | dS^T | lse[2][128] | D[2][128] | barriers
+constexpr int B_SMEM = 1024 + TILE_BYTES * 8 + 2 * P_BYTES + 4 * TILE * 4 + 256;
 static_assert(F_SMEM <= 232448 && B_SMEM <= 232448, "shared memory budget");
 
 struct Params {
@@ -177,8 +178,30 @@ __device__ __forceinline__ void red_add_v4(float* dst, float a, float b, float c
 }
 
 // ============================================================================ forward
+// Work item = (sample, head, query tile); items are numbered heaviest first (query
+// tile 0 = the last 128 rows sees the most key tiles under causality).
+struct FwdItem {
+  int b, h, i, t0, n, kst;
+};
+
+__device__ __forceinline__ FwdItem fwd_item(const Params& p, int w) {
+  FwdItem it;
+  it.h = w % p.H;
+  const int rest = w / p.H;
+  it.b = rest % p.B;
+  it.i = rest / p.B;
+  it.kst = min(max(p.kstart[it.b], 0), p.Lk);
+  const int tmax = (p.Lk - it.kst + TILE - 1) / TILE - 1;
+  it.t0 = p.causal ? it.i : 0;
+  it.n = max(0, tmax - it.t0 + 1);  // key tiles visited
+  return it;
+}
+
+// Persistent: each CTA walks items blockIdx.x, +gridDim.x, ...; the K/V rings and
+// every barrier phase run on across items (global tile counter g), so the loads of
+// the next item overlap the softmax of the current one.
 __global__ void __launch_bounds__(F_THREADS, 2)
-    fmha_fwd_kernel(const __grid_constant__ CUtensorMap tm, const Params p) {
+    fmha_fwd_kernel(const __grid_constant__ CUtensorMap tm, const Params p, int num_items) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   if (smem_u32(smem_raw) & 1023) {  // uniform across the CTA: nothing has been touched yet
     if (threadIdx.x == 0) record_error(p.err, MDL_ERR_BAD_ARG);
@@ -190,35 +213,28 @@ __global__ void __launch_bounds__(F_THREADS, 2)
   uint8_t* sP = sV + 2 * TILE_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + P_BYTES);
   uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;      // [2]
-  uint64_t* k_empty = bars + 3;     // [2]
-  uint64_t* v_full = bars + 5;      // [2]
-  uint64_t* v_empty = bars + 7;     // [2]
-  uint64_t* s_full = bars + 9;
-  uint64_t* s_empty = bars + 10;
-  uint64_t* p_full = bars + 11;
-  uint64_t* p_empty = bars + 12;
-  uint64_t* pv_full = bars + 13;    // [2]
-  uint64_t* pv_empty = bars + 15;   // [2]
-  uint64_t* done = bars + 17;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  uint64_t* q_empty = bars + 1;
+  uint64_t* k_full = bars + 2;      // [2]
+  uint64_t* k_empty = bars + 4;     // [2]
+  uint64_t* v_full = bars + 6;      // [2]
+  uint64_t* v_empty = bars + 8;     // [2]
+  uint64_t* s_full = bars + 10;
+  uint64_t* s_empty = bars + 11;
+  uint64_t* p_full = bars + 12;
+  uint64_t* p_empty = bars + 13;
+  uint64_t* pv_full = bars + 14;    // [2]
+  uint64_t* pv_empty = bars + 16;   // [2]
+  uint64_t* done = bars + 18;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int h = blockIdx.x % p.H;
-  const int rest = blockIdx.x / p.H;
-  const int b = rest % p.B;
-  const int i = rest / p.B;  // query tile (0 = last 128 rows), heaviest first
   const int Lk = p.Lk;
-  const int kst = min(max(p.kstart[b], 0), Lk);
-  const int tmax = (Lk - kst + TILE - 1) / TILE - 1;
-  const int t0 = p.causal ? i : 0;
-  const int n = max(0, tmax - t0 + 1);  // key tiles this CTA visits
-  const int xq = h * HD, xk = p.D + h * HD, xv = 2 * p.D + h * HD;  // head h at box column 0
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
@@ -245,66 +261,90 @@ __global__ void __launch_bounds__(F_THREADS, 2)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0 && n > 0) {
+    if (lane == 0) {
       tma_prefetch_desc(&tm);
-      auto kv_row = [&](int j) { return Lk - TILE * (t0 + j + 1); };
-      mbar_arrive_expect_tx(q_full, TILE_BYTES);
-      tma_load_3d(sQ, &tm, q_full, xq, Lk - TILE * (i + 1), b);
-      // K and V tiles in 2-stage rings; stage j&1 is refilled once S(j-2) / PV(j-2) read it
+      int items = 0, g = 0;  // items with work, tiles issued (global)
       int k_issued = 0, v_issued = 0;
-      for (int j = 0; j < n; ++j) {
-        const int st = j & 1;
-        if (j >= 2 && (!mbar_wait(&k_empty[st], ((j >> 1) - 1) & 1, p.err, abort_flag))) break;
-        mbar_arrive_expect_tx(&k_full[st], TILE_BYTES);
-        tma_load_3d(sK + st * TILE_BYTES, &tm, &k_full[st], xk, kv_row(j), b);
-        k_issued = j + 1;
-        if (j >= 2 && (!mbar_wait(&v_empty[st], ((j >> 1) - 1) & 1, p.err, abort_flag))) break;
-        mbar_arrive_expect_tx(&v_full[st], TILE_BYTES);
-        tma_load_3d(sV + st * TILE_BYTES, &tm, &v_full[st], xv, kv_row(j), b);
-        v_issued = j + 1;
+      bool ok = true;
+      for (int w = blockIdx.x; w < num_items && ok; w += gridDim.x) {
+        const FwdItem it = fwd_item(p, w);
+        if (it.n == 0) continue;
+        if (items >= 1 && !mbar_wait(q_empty, (items - 1) & 1, p.err, abort_flag)) break;
+        mbar_arrive_expect_tx(q_full, TILE_BYTES);
+        tma_load_3d(sQ, &tm, q_full, it.h * HD, Lk - TILE * (it.i + 1), it.b);
+        ++items;
+        for (int j = 0; j < it.n; ++j, ++g) {
+          const int st = g & 1;
+          const int y = Lk - TILE * (it.t0 + j + 1);
+          if (g >= 2 && !mbar_wait(&k_empty[st], ((g >> 1) - 1) & 1, p.err, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&k_full[st], TILE_BYTES);
+          tma_load_3d(sK + st * TILE_BYTES, &tm, &k_full[st], p.D + it.h * HD, y, it.b);
+          k_issued = g + 1;
+          if (g >= 2 && !mbar_wait(&v_empty[st], ((g >> 1) - 1) & 1, p.err, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&v_full[st], TILE_BYTES);
+          tma_load_3d(sV + st * TILE_BYTES, &tm, &v_full[st], 2 * p.D + it.h * HD, y, it.b);
+          v_issued = g + 1;
+        }
       }
       // every copy into this CTA's smem has landed before the CTA may exit
-      mbar_wait(q_full, 0, nullptr, nullptr);
+      if (items > 0) mbar_wait(q_full, (items - 1) & 1, nullptr, nullptr);
       for (int j = max(0, k_issued - 2); j < k_issued; ++j) mbar_wait(&k_full[j & 1], (j >> 1) & 1, nullptr, nullptr);
       for (int j = max(0, v_issued - 2); j < v_issued; ++j) mbar_wait(&v_full[j & 1], (j >> 1) & 1, nullptr, nullptr);
     }
   } else if (warp == 1) {
-    if (lane == 0 && n > 0) {
+    if (lane == 0) {
       constexpr uint32_t idesc_s = make_idesc_bf16(TILE, TILE, false, false);
       constexpr uint32_t idesc_pv = make_idesc_bf16(TILE, 64, false, true);
       const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV), p_base = smem_u32(sP);
-      auto issue_s = [&](int j) {
-        const uint32_t kb = k_base + (j & 1) * TILE_BYTES;
+      bool ok = true;
+      int items = 0, g0 = 0;
+      // S(g) = Q K(g)^T; the item's last S releases Q
+      auto issue_s = [&](int g, bool last) -> bool {
+        if (!mbar_wait(&k_full[g & 1], (g >> 1) & 1, p.err, abort_flag) ||
+            (g > 0 && !mbar_wait(s_empty, (g - 1) & 1, p.err, abort_flag)))
+          return false;
+        tc_fence_after();
+        const uint32_t kb = k_base + (g & 1) * TILE_BYTES;
         for (int ks = 0; ks < 2; ++ks)
           tc_mma_bf16(tmem, desc_k(q_base, ks * 32), desc_k(kb, ks * 32), idesc_s, ks);
-        tc_commit(&k_empty[j & 1]);
+        tc_commit(&k_empty[g & 1]);
         tc_commit(s_full);
+        if (last) tc_commit(q_empty);
+        return true;
       };
-      bool ok = mbar_wait(q_full, 0, p.err, abort_flag) && mbar_wait(&k_full[0], 0, p.err, abort_flag);
-      if (ok) {
-        tc_fence_after();
-        issue_s(0);
-      }
-      for (int j = 0; j < n && ok; ++j) {
-        if (j + 1 < n) {
-          if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, p.err, abort_flag) ||
-              !mbar_wait(s_empty, j & 1, p.err, abort_flag))
+      for (int w = blockIdx.x; w < num_items && ok; w += gridDim.x) {
+        const FwdItem it = fwd_item(p, w);
+        if (it.n == 0) continue;
+        if (!mbar_wait(q_full, items & 1, p.err, abort_flag) || !issue_s(g0, it.n == 1)) break;
+        ++items;
+        for (int j = 0; j < it.n; ++j) {
+          const int g = g0 + j;
+          if (j + 1 < it.n && !issue_s(g + 1, j + 2 == it.n)) {
+            ok = false;
             break;
+          }
+          const int buf = g & 1;
+          if (!mbar_wait(p_full, g & 1, p.err, abort_flag) ||
+              !mbar_wait(&v_full[buf], (g >> 1) & 1, p.err, abort_flag) ||
+              (g >= 2 && !mbar_wait(&pv_empty[buf], ((g >> 1) - 1) & 1, p.err, abort_flag))) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
-          issue_s(j + 1);
+          for (int ks = 0; ks < 8; ++ks)
+            tc_mma_bf16(tmem + 128 + buf * 64, desc_k128(p_base, ks), desc_mn(v_base + buf * TILE_BYTES, ks),
+                        idesc_pv, ks);
+          tc_commit(&pv_full[buf]);
+          tc_commit(p_empty);
+          tc_commit(&v_empty[buf]);
         }
-        const int buf = j & 1;
-        if (!mbar_wait(p_full, j & 1, p.err, abort_flag) ||
-            !mbar_wait(&v_full[buf], (j >> 1) & 1, p.err, abort_flag) ||
-            (j >= 2 && !mbar_wait(&pv_empty[buf], ((j >> 1) - 1) & 1, p.err, abort_flag)))
-          break;
-        tc_fence_after();
-        for (int ks = 0; ks < 8; ++ks)
-          tc_mma_bf16(tmem + 128 + buf * 64, desc_k128(p_base, ks), desc_mn(v_base + buf * TILE_BYTES, ks),
-                      idesc_pv, ks);
-        tc_commit(&pv_full[buf]);
-        tc_commit(p_empty);
-        tc_commit(&v_empty[buf]);
+        g0 += it.n;
       }
       // all MMAs have finished before TMEM is released
       tc_commit(done);
@@ -314,96 +354,101 @@ __global__ void __launch_bounds__(F_THREADS, 2)
     // ------------------------------------------------------------ softmax
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
-    const int qrow = Lk - TILE * (i + 1) + r;
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     const uint32_t p_base = smem_u32(sP);
-    float m = -CUDART_INF_F, l = 0.f, alpha_prev = 1.f;
-    float o[HD];
-#pragma unroll
-    for (int d = 0; d < HD; ++d) o[d] = 0.f;
     bool ok = true;
-    auto fold_pv = [&](int jj) -> bool {
-      const int buf = jj & 1;
-      if (!warp_wait(&pv_full[buf], (jj >> 1) & 1, p.err, abort_flag)) return false;
-      tc_fence_after();
-      uint32_t pv[HD];
-      tmem_ld32(t_lane + 128 + buf * 64, pv);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&pv_empty[buf]);
+    int g0 = 0;
+    for (int w = blockIdx.x; w < num_items && ok; w += gridDim.x) {
+      const FwdItem it = fwd_item(p, w);
+      const int qrow = Lk - TILE * (it.i + 1) + r;
+      float m = -CUDART_INF_F, l = 0.f, alpha_prev = 1.f;
+      float o[HD];
 #pragma unroll
-      for (int d = 0; d < HD; ++d) o[d] = fmaf(o[d], alpha_prev, __uint_as_float(pv[d]));
-      return true;
-    };
-    for (int j = 0; j < n; ++j) {
-      const int t = t0 + j;
-      const int kbase = Lk - TILE * (t + 1);
-      if (!warp_wait(s_full, j & 1, p.err, abort_flag)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t sr[TILE];
+      for (int d = 0; d < HD; ++d) o[d] = 0.f;
+      auto fold_pv = [&](int gg) -> bool {
+        const int buf = gg & 1;
+        if (!warp_wait(&pv_full[buf], (gg >> 1) & 1, p.err, abort_flag)) return false;
+        tc_fence_after();
+        uint32_t pv[HD];
+        tmem_ld32(t_lane + 128 + buf * 64, pv);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&pv_empty[buf]);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(t_lane + c * 32, sr + c * 32);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(s_empty);
-      const int lo = kst - kbase;                          // columns < lo are padding
-      const int hi = (p.causal && t == i) ? r : TILE - 1;  // columns > hi are in the future
-      if (lo > 0 || hi < TILE - 1) {
-#pragma unroll
-        for (int c = 0; c < TILE; ++c)
-          if (c < lo || c > hi) sr[c] = __float_as_uint(-CUDART_INF_F);
-      }
-      float mx = -CUDART_INF_F;
-#pragma unroll
-      for (int c = 0; c < TILE; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
-      const float m_new = fmaxf(m, mx * p.scale2);
-      const float m_use = m_new == -CUDART_INF_F ? 0.f : m_new;
-      const float alpha = ex2(m - m_use);
-      if (j > 0 && !warp_wait(p_empty, (j - 1) & 1, p.err, abort_flag)) {
-        ok = false;
-        break;
-      }
-      float sum = 0.f;
-#pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        float e[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          e[k] = ex2(fmaf(__uint_as_float(sr[c * 8 + k]), p.scale2, -m_use));
-          sum += e[k];
+        for (int d = 0; d < HD; ++d) o[d] = fmaf(o[d], alpha_prev, __uint_as_float(pv[d]));
+        return true;
+      };
+      for (int j = 0; j < it.n; ++j) {
+        const int g = g0 + j;
+        const int t = it.t0 + j;
+        const int kbase = Lk - TILE * (t + 1);
+        if (!warp_wait(s_full, g & 1, p.err, abort_flag)) {
+          ok = false;
+          break;
         }
-        st_smem_v4(p_base + swz_off(r, c), pack2(e[0], e[1]), pack2(e[2], e[3]), pack2(e[4], e[5]),
-                   pack2(e[6], e[7]));
+        tc_fence_after();
+        uint32_t sr[TILE];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(t_lane + c * 32, sr + c * 32);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(s_empty);
+        const int lo = it.kst - kbase;                         // columns < lo are padding
+        const int hi = (p.causal && t == it.i) ? r : TILE - 1;  // columns > hi are in the future
+        if (lo > 0 || hi < TILE - 1) {
+#pragma unroll
+          for (int c = 0; c < TILE; ++c)
+            if (c < lo || c > hi) sr[c] = __float_as_uint(-CUDART_INF_F);
+        }
+        float mx = -CUDART_INF_F;
+#pragma unroll
+        for (int c = 0; c < TILE; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
+        const float m_new = fmaxf(m, mx * p.scale2);
+        const float m_use = m_new == -CUDART_INF_F ? 0.f : m_new;
+        const float alpha = ex2(m - m_use);
+        if (g > 0 && !warp_wait(p_empty, (g - 1) & 1, p.err, abort_flag)) {  // P(g-1) consumed
+          ok = false;
+          break;
+        }
+        float sum = 0.f;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          float e[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            e[k] = ex2(fmaf(__uint_as_float(sr[c * 8 + k]), p.scale2, -m_use));
+            sum += e[k];
+          }
+          st_smem_v4(p_base + swz_off(r, c), pack2(e[0], e[1]), pack2(e[2], e[3]), pack2(e[4], e[5]),
+                     pack2(e[6], e[7]));
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full);
+        l = fmaf(l, alpha, sum);
+        m = m_new;
+        if (j > 0 && !fold_pv(g - 1)) {
+          ok = false;
+          break;
+        }
+        alpha_prev = alpha;
       }
-      fence_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
-      l = fmaf(l, alpha, sum);
-      m = m_new;
-      if (j > 0 && !fold_pv(j - 1)) {
-        ok = false;
-        break;
-      }
-      alpha_prev = alpha;
-    }
-    if (ok && n > 0) ok = fold_pv(n - 1);
-    if (ok) {
+      if (ok && it.n > 0) ok = fold_pv(g0 + it.n - 1);
+      if (!ok) break;
+      g0 += it.n;
       const int qi = qrow - (Lk - p.Lq);
       if (qi >= 0) {
-        const bool valid = qrow >= kst && l > 0.f;
+        const bool valid = qrow >= it.kst && l > 0.f;
         const float inv = valid ? 1.f / l : 0.f;
         uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) +
-                                              (static_cast<long long>(b) * p.Lq + qi) * p.D + h * HD);
+                                              (static_cast<long long>(it.b) * p.Lq + qi) * p.D + it.h * HD);
 #pragma unroll
         for (int c = 0; c < HD / 8; ++c)
           dst[c] = make_uint4(pack2(o[c * 8] * inv, o[c * 8 + 1] * inv), pack2(o[c * 8 + 2] * inv, o[c * 8 + 3] * inv),
                               pack2(o[c * 8 + 4] * inv, o[c * 8 + 5] * inv), pack2(o[c * 8 + 6] * inv, o[c * 8 + 7] * inv));
-        p.lse[(static_cast<long long>(b) * p.H + h) * p.Lq + qi] = valid ? m + lg2(l) : CUDART_INF_F;
+        p.lse[(static_cast<long long>(it.b) * p.H + it.h) * p.Lq + qi] = valid ? m + lg2(l) : CUDART_INF_F;
       }
     }
   }
@@ -450,53 +495,70 @@ __global__ void __launch_bounds__(256) fmha_bwd_pre_kernel(const __nv_bfloat16* 
   }
 }
 
+// Work item = (sample, head, key tile); items with the most query tiles come first.
+struct BwdItem {
+  int b, h, kbase, kst, qlo, n;
+};
+
+__device__ __forceinline__ BwdItem bwd_item(const Params& p, int w) {
+  BwdItem it;
+  const int nkt = (p.Lk + TILE - 1) / TILE;
+  it.h = w % p.H;
+  const int rest = w / p.H;
+  it.b = rest % p.B;
+  const int t = nkt - 1 - rest / p.B;
+  it.kbase = p.Lk - TILE * (t + 1);
+  it.kst = min(max(p.kstart[it.b], 0), p.Lk);
+  it.qlo = max(it.kst, p.Lk - p.Lq);  // first row that is a query with a visible key
+  const int nq = (p.Lq + TILE - 1) / TILE;
+  int imax = p.causal ? min(t, nq - 1) : nq - 1;
+  imax = min(imax, (p.Lk - 1 - it.qlo) / TILE);
+  it.n = (it.kbase + TILE - 1 >= it.kst && it.qlo < p.Lk) ? max(0, imax + 1) : 0;  // query tiles visited
+  return it;
+}
+
+// Persistent: K/V of successive items in a 2-stage ring, Q/dO/lse/D of successive
+// query tiles in a 2-stage ring; barrier phases run on across items (item counter
+// for K/V and dK/dV, global query-tile counter for the rest).
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     fmha_bwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap tm_do,
-                    const Params p) {
+                    const Params p, int num_items) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint8_t* sK = smem;
-  uint8_t* sV = sK + TILE_BYTES;
-  uint8_t* sQ = sV + TILE_BYTES;        // [2]
+  uint8_t* sK = smem;                   // [2]
+  uint8_t* sV = sK + 2 * TILE_BYTES;    // [2]
+  uint8_t* sQ = sV + 2 * TILE_BYTES;    // [2]
   uint8_t* sdO = sQ + 2 * TILE_BYTES;   // [2]
   uint8_t* sPT = sdO + 2 * TILE_BYTES;
   uint8_t* sdST = sPT + P_BYTES;
   float* sLse = reinterpret_cast<float*>(sdST + P_BYTES);  // [2][128]
   float* sDs = sLse + 2 * TILE;                            // [2][128]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sDs + 2 * TILE);
-  uint64_t* kv_full = bars;
-  uint64_t* qd_full = bars + 1;    // [2]
-  uint64_t* qd_empty = bars + 3;   // [2]
-  uint64_t* st_full = bars + 5;
-  uint64_t* st_empty = bars + 6;
-  uint64_t* pds_full = bars + 7;
-  uint64_t* pds_empty = bars + 8;
-  uint64_t* dq_full = bars + 9;
-  uint64_t* dq_empty = bars + 10;
-  uint64_t* dkv_full = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* kv_full = bars;        // [2]
+  uint64_t* kv_empty = bars + 2;   // [2]
+  uint64_t* qd_full = bars + 4;    // [2]
+  uint64_t* qd_empty = bars + 6;   // [2]
+  uint64_t* st_full = bars + 8;
+  uint64_t* st_empty = bars + 9;
+  uint64_t* pds_full = bars + 10;
+  uint64_t* pds_empty = bars + 11;
+  uint64_t* dq_full = bars + 12;
+  uint64_t* dq_empty = bars + 13;
+  uint64_t* dkv_full = bars + 14;
+  uint64_t* dkv_empty = bars + 15;
+  uint64_t* done = bars + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int Lk = p.Lk;
-  const int nkt = (Lk + TILE - 1) / TILE;
-  const int h = blockIdx.x % p.H;
-  const int rest = blockIdx.x / p.H;
-  const int b = rest % p.B;
-  const int t = nkt - 1 - rest / p.B;  // key tile; the oldest (most query tiles) launch first
-  const int kbase = Lk - TILE * (t + 1);
-  const int kst = min(max(p.kstart[b], 0), Lk);
-  const int qlo = max(kst, Lk - p.Lq);  // first row that is a query with a visible key
-  const int nq = (p.Lq + TILE - 1) / TILE;
-  int imax = p.causal ? min(t, nq - 1) : nq - 1;
-  imax = min(imax, (Lk - 1 - qlo) / TILE);
-  const int n = (kbase + TILE - 1 >= kst && qlo < Lk) ? max(0, imax + 1) : 0;  // query tiles visited
 
   if (threadIdx.x == 0) {
-    mbar_init(kv_full, 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&qd_full[s], 33);
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+      mbar_init(&qd_full[s], 33);  // TMA bytes + the 32 lanes that stage lse / D
       mbar_init(&qd_empty[s], 1);
     }
     mbar_init(st_full, 1);
@@ -506,6 +568,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     mbar_init(dq_full, 1);
     mbar_init(dq_empty, 8);
     mbar_init(dkv_full, 1);
+    mbar_init(dkv_empty, 8);
+    mbar_init(done, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -519,194 +583,237 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    if (n > 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tm);
+      tma_prefetch_desc(&tm_do);
+    }
+    int items = 0, gq = 0, kv_issued = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < num_items && ok; w += gridDim.x) {
+      const BwdItem it = bwd_item(p, w);
+      if (it.n == 0) continue;
+      const int stk = items & 1;
       if (lane == 0) {
-        tma_prefetch_desc(&tm);
-        tma_prefetch_desc(&tm_do);
-        mbar_arrive_expect_tx(kv_full, 2 * TILE_BYTES);
-        tma_load_3d(sK, &tm, kv_full, p.D + h * HD, kbase, b);
-        tma_load_3d(sV, &tm, kv_full, 2 * p.D + h * HD, kbase, b);
+        if (items >= 2 && !mbar_wait(&kv_empty[stk], ((items >> 1) - 1) & 1, p.err, abort_flag)) ok = false;
+        if (ok) {
+          mbar_arrive_expect_tx(&kv_full[stk], 2 * TILE_BYTES);
+          tma_load_3d(sK + stk * TILE_BYTES, &tm, &kv_full[stk], p.D + it.h * HD, it.kbase, it.b);
+          tma_load_3d(sV + stk * TILE_BYTES, &tm, &kv_full[stk], 2 * p.D + it.h * HD, it.kbase, it.b);
+          kv_issued = items + 1;
+        }
       }
-      int issued = 0;
-      for (int j = 0; j < n; ++j) {
-        const int st = j & 1;
-        if (j >= 2 && !mbar_wait(&qd_empty[st], ((j >> 1) - 1) & 1, p.err, abort_flag)) break;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      ++items;
+      for (int j = 0; j < it.n; ++j, ++gq) {
+        const int st = gq & 1;
+        // parity of the previous use of this stage; a fresh barrier passes parity 1 at once
+        if (!warp_wait(&qd_empty[st], ((gq >> 1) + 1) & 1, p.err, abort_flag)) {
+          ok = false;
+          break;
+        }
         const int qrow0 = Lk - TILE * (j + 1);  // token row of query column 0
         if (lane == 0) {
           mbar_arrive_expect_tx(&qd_full[st], 2 * TILE_BYTES);
-          tma_load_3d(sQ + st * TILE_BYTES, &tm, &qd_full[st], h * HD, qrow0, b);
-          tma_load_3d(sdO + st * TILE_BYTES, &tm_do, &qd_full[st], h * HD, qrow0 - (Lk - p.Lq), b);
+          tma_load_3d(sQ + st * TILE_BYTES, &tm, &qd_full[st], it.h * HD, qrow0, it.b);
+          tma_load_3d(sdO + st * TILE_BYTES, &tm_do, &qd_full[st], it.h * HD, qrow0 - (Lk - p.Lq), it.b);
         }
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int c = lane * 4 + e;
           const int qi = qrow0 + c - (Lk - p.Lq);
-          const bool real = qi >= 0 && qrow0 + c >= qlo;
-          const long long off = (static_cast<long long>(b) * p.H + h) * p.Lq + qi;
+          const bool real = qi >= 0 && qrow0 + c >= it.qlo;
+          const long long off = (static_cast<long long>(it.b) * p.H + it.h) * p.Lq + qi;
           sLse[st * TILE + c] = real ? p.lse[off] : CUDART_INF_F;
           sDs[st * TILE + c] = real ? p.dsum[off] : 0.f;
         }
         mbar_arrive(&qd_full[st]);
-        issued = j + 1;
-      }
-      if (lane == 0) {
-        mbar_wait(kv_full, 0, nullptr, nullptr);
-        for (int j = max(0, issued - 2); j < issued; ++j)
-          mbar_wait(&qd_full[j & 1], (j >> 1) & 1, nullptr, nullptr);
       }
     }
+    if (lane == 0) {
+      for (int j = max(0, kv_issued - 2); j < kv_issued; ++j) mbar_wait(&kv_full[j & 1], (j >> 1) & 1, nullptr, nullptr);
+      for (int j = max(0, gq - 2); j < gq; ++j) mbar_wait(&qd_full[j & 1], (j >> 1) & 1, nullptr, nullptr);
+    }
   } else if (warp == 1) {
-    if (lane == 0 && n > 0) {
+    if (lane == 0) {
       constexpr uint32_t idesc_s = make_idesc_bf16(TILE, TILE, false, false);
       constexpr uint32_t idesc_kv = make_idesc_bf16(TILE, 64, false, true);
       constexpr uint32_t idesc_q = make_idesc_bf16(TILE, 64, true, true);
-      const uint32_t k_base = smem_u32(sK), v_base = smem_u32(sV);
       const uint32_t pt_base = smem_u32(sPT), ds_base = smem_u32(sdST);
-      // S^T / dP^T of tile j+1 are issued as soon as the compute warps hold tile j in
-      // registers, so the tensor core works on them while tile j is being processed.
-      auto issue_s = [&](int j) -> bool {
-        const int st = j & 1;
-        if (!mbar_wait(&qd_full[st], (j >> 1) & 1, p.err, abort_flag) ||
-            (j > 0 && !mbar_wait(st_empty, (j - 1) & 1, p.err, abort_flag)))
-          return false;
-        tc_fence_after();
-        const uint32_t q_base = smem_u32(sQ + st * TILE_BYTES);
-        const uint32_t do_base = smem_u32(sdO + st * TILE_BYTES);
-        for (int ks = 0; ks < 2; ++ks) {
-          tc_mma_bf16(tmem, desc_k(k_base, ks * 32), desc_k(q_base, ks * 32), idesc_s, ks);
-          tc_mma_bf16(tmem + 128, desc_k(v_base, ks * 32), desc_k(do_base, ks * 32), idesc_s, ks);
+      int items = 0, gq = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; w < num_items && ok; w += gridDim.x) {
+        const BwdItem it = bwd_item(p, w);
+        if (it.n == 0) continue;
+        const int stk = items & 1;
+        const uint32_t k_base = smem_u32(sK + stk * TILE_BYTES), v_base = smem_u32(sV + stk * TILE_BYTES);
+        if (!mbar_wait(&kv_full[stk], (items >> 1) & 1, p.err, abort_flag)) break;
+        // S^T / dP^T of query tile g, issued as soon as the compute warps hold tile g-1
+        auto issue_s = [&](int g) -> bool {
+          const int st = g & 1;
+          if (!mbar_wait(&qd_full[st], (g >> 1) & 1, p.err, abort_flag) ||
+              (g > 0 && !mbar_wait(st_empty, (g - 1) & 1, p.err, abort_flag)))
+            return false;
+          tc_fence_after();
+          const uint32_t q_base = smem_u32(sQ + st * TILE_BYTES);
+          const uint32_t do_base = smem_u32(sdO + st * TILE_BYTES);
+          for (int ks = 0; ks < 2; ++ks) {
+            tc_mma_bf16(tmem, desc_k(k_base, ks * 32), desc_k(q_base, ks * 32), idesc_s, ks);
+            tc_mma_bf16(tmem + 128, desc_k(v_base, ks * 32), desc_k(do_base, ks * 32), idesc_s, ks);
+          }
+          tc_commit(st_full);
+          return true;
+        };
+        if (!issue_s(gq)) break;
+        for (int j = 0; j < it.n; ++j) {
+          const int g = gq + j;
+          const int st = g & 1;
+          const uint32_t q_base = smem_u32(sQ + st * TILE_BYTES);
+          const uint32_t do_base = smem_u32(sdO + st * TILE_BYTES);
+          if ((j + 1 < it.n && !issue_s(g + 1)) || !mbar_wait(pds_full, g & 1, p.err, abort_flag) ||
+              (j == 0 && items >= 1 && !mbar_wait(dkv_empty, (items - 1) & 1, p.err, abort_flag))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint32_t acc = (j > 0 || ks > 0) ? 1u : 0u;
+            tc_mma_bf16(tmem + 256, desc_k128(pt_base, ks), desc_mn(do_base, ks), idesc_kv, acc);
+            tc_mma_bf16(tmem + 320, desc_k128(ds_base, ks), desc_mn(q_base, ks), idesc_kv, acc);
+          }
+          if (g > 0 && !mbar_wait(dq_empty, (g - 1) & 1, p.err, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          for (int ks = 0; ks < 8; ++ks)
+            tc_mma_bf16(tmem + 384, desc_mn(ds_base, ks), desc_mn(k_base, ks), idesc_q, ks);
+          tc_commit(dq_full);
+          tc_commit(pds_empty);
+          tc_commit(&qd_empty[st]);
         }
-        tc_commit(st_full);
-        return true;
-      };
-      bool ok = mbar_wait(kv_full, 0, p.err, abort_flag) && issue_s(0);
-      for (int j = 0; j < n && ok; ++j) {
-        const int st = j & 1;
-        const uint32_t q_base = smem_u32(sQ + st * TILE_BYTES);
-        const uint32_t do_base = smem_u32(sdO + st * TILE_BYTES);
-        if (j + 1 < n && !issue_s(j + 1)) break;
-        if (!mbar_wait(pds_full, j & 1, p.err, abort_flag)) break;
-        tc_fence_after();
-        for (int ks = 0; ks < 8; ++ks) {
-          const uint32_t acc = (j > 0 || ks > 0) ? 1u : 0u;
-          tc_mma_bf16(tmem + 256, desc_k128(pt_base, ks), desc_mn(do_base, ks), idesc_kv, acc);
-          tc_mma_bf16(tmem + 320, desc_k128(ds_base, ks), desc_mn(q_base, ks), idesc_kv, acc);
-        }
-        if (j > 0 && !mbar_wait(dq_empty, (j - 1) & 1, p.err, abort_flag)) break;
-        tc_fence_after();
-        for (int ks = 0; ks < 8; ++ks)
-          tc_mma_bf16(tmem + 384, desc_mn(ds_base, ks), desc_mn(k_base, ks), idesc_q, ks);
-        tc_commit(dq_full);
-        tc_commit(pds_empty);
-        tc_commit(&qd_empty[st]);
+        if (!ok) break;
+        tc_commit(dkv_full);
+        tc_commit(&kv_empty[stk]);
+        gq += it.n;
+        ++items;
       }
-      tc_commit(dkv_full);
-      mbar_wait(dkv_full, 0, nullptr, nullptr);
+      tc_commit(done);
+      mbar_wait(done, 0, nullptr, nullptr);
     }
   } else {
     // ------------------------------------------------------------ compute
     const int wg = (warp - 2) >> 2;  // query columns [64*wg, 64*wg + 64)
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
-    const int krow = kbase + r;
-    const bool key_ok = krow >= kst;
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     const uint32_t pt_base = smem_u32(sPT), ds_base = smem_u32(sdST);
     bool ok = true;
-    auto drain_dq = [&](int jj) -> bool {
-      if (!warp_wait(dq_full, jj & 1, p.err, abort_flag)) return false;
-      tc_fence_after();
-      uint32_t g[16];
-      tmem_ld16(t_lane + 384 + wg * 16, g);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(dq_empty);
-      const int qrow = Lk - TILE * (jj + 1) + r;  // TMEM lane = query column of tile jj
-      if (qrow >= qlo) {
-        float* dst = p.dq_acc + (static_cast<long long>(b) * p.Lq + (qrow - (Lk - p.Lq))) * p.D + h * HD + wg * 16;
+    int items = 0, gq = 0;
+    for (int w = blockIdx.x; w < num_items && ok; w += gridDim.x) {
+      const BwdItem it = bwd_item(p, w);
+      const int krow = it.kbase + r;
+      const bool key_ok = krow >= it.kst;
+      auto drain_dq = [&](int g, int j) -> bool {
+        if (!warp_wait(dq_full, g & 1, p.err, abort_flag)) return false;
+        tc_fence_after();
+        uint32_t gr[16];
+        tmem_ld16(t_lane + 384 + wg * 16, gr);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dq_empty);
+        const int qrow = Lk - TILE * (j + 1) + r;  // TMEM lane = query column of tile j
+        if (qrow >= it.qlo) {
+          float* dst = p.dq_acc + (static_cast<long long>(it.b) * p.Lq + (qrow - (Lk - p.Lq))) * p.D + it.h * HD +
+                       wg * 16;
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-          red_add_v4(dst + c * 4, __uint_as_float(g[c * 4]), __uint_as_float(g[c * 4 + 1]),
-                     __uint_as_float(g[c * 4 + 2]), __uint_as_float(g[c * 4 + 3]));
-      }
-      return true;
-    };
-    for (int j = 0; j < n; ++j) {
-      const int st = j & 1;
-      const int qrow0 = Lk - TILE * (j + 1);
-      if (!warp_wait(&qd_full[st], (j >> 1) & 1, p.err, abort_flag) ||
-          !warp_wait(st_full, j & 1, p.err, abort_flag)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t s[64], dp[64];
-      tmem_ld32(t_lane + wg * 64, s);
-      tmem_ld32(t_lane + wg * 64 + 32, s + 32);
-      tmem_ld32(t_lane + 128 + wg * 64, dp);
-      tmem_ld32(t_lane + 128 + wg * 64 + 32, dp + 32);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(st_empty);
-      if (j > 0 && !warp_wait(pds_empty, (j - 1) & 1, p.err, abort_flag)) {
-        ok = false;
-        break;
-      }
-      const float* lse = sLse + st * TILE + wg * 64;
-      const float* dsv = sDs + st * TILE + wg * 64;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        float pe[8], de[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int qc = c * 8 + k;
-          const int qrow = qrow0 + wg * 64 + qc;
-          const bool vis = key_ok && (!p.causal || krow <= qrow);
-          const float pv = vis ? ex2(fmaf(__uint_as_float(s[qc]), p.scale2, -lse[qc])) : 0.f;
-          pe[k] = pv;
-          de[k] = pv * (__uint_as_float(dp[qc]) - dsv[qc]) * p.scale;
+          for (int c = 0; c < 4; ++c)
+            red_add_v4(dst + c * 4, __uint_as_float(gr[c * 4]), __uint_as_float(gr[c * 4 + 1]),
+                       __uint_as_float(gr[c * 4 + 2]), __uint_as_float(gr[c * 4 + 3]));
         }
-        const uint32_t off = swz_off(r, wg * 8 + c);
-        st_smem_v4(pt_base + off, pack2(pe[0], pe[1]), pack2(pe[2], pe[3]), pack2(pe[4], pe[5]), pack2(pe[6], pe[7]));
-        st_smem_v4(ds_base + off, pack2(de[0], de[1]), pack2(de[2], de[3]), pack2(de[4], de[5]), pack2(de[6], de[7]));
-      }
-      fence_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(pds_full);
-      if (j > 0 && !drain_dq(j - 1)) {
-        ok = false;
-        break;
-      }
-    }
-    if (ok && n > 0) ok = drain_dq(n - 1);
-    // dK (warpgroup 1) and dV (warpgroup 0) of this key tile. The TMEM read is
-    // done by whole warps; only the store depends on the lane's key row.
-    if (ok) {
-      float g[HD];
-#pragma unroll
-      for (int d = 0; d < HD; ++d) g[d] = 0.f;
-      if (n > 0) {
-        if (!warp_wait(dkv_full, 0, p.err, abort_flag)) {
+        return true;
+      };
+      for (int j = 0; j < it.n; ++j) {
+        const int g = gq + j;
+        const int st = g & 1;
+        const int qrow0 = Lk - TILE * (j + 1);
+        if (!warp_wait(&qd_full[st], (g >> 1) & 1, p.err, abort_flag) || !warp_wait(st_full, g & 1, p.err, abort_flag)) {
           ok = false;
-        } else {
-          tc_fence_after();
-          uint32_t gr[HD];
-          tmem_ld32(t_lane + (wg == 0 ? 256 : 320), gr);
-          tmem_wait_ld();
+          break;
+        }
+        tc_fence_after();
+        uint32_t s[64], dp[64];
+        tmem_ld32(t_lane + wg * 64, s);
+        tmem_ld32(t_lane + wg * 64 + 32, s + 32);
+        tmem_ld32(t_lane + 128 + wg * 64, dp);
+        tmem_ld32(t_lane + 128 + wg * 64 + 32, dp + 32);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(st_empty);
+        if (g > 0 && !warp_wait(pds_empty, (g - 1) & 1, p.err, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const float* lse = sLse + st * TILE + wg * 64;
+        const float* dsv = sDs + st * TILE + wg * 64;
 #pragma unroll
-          for (int d = 0; d < HD; ++d) g[d] = key_ok ? __uint_as_float(gr[d]) : 0.f;
+        for (int c = 0; c < 8; ++c) {
+          float pe[8], de[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int qc = c * 8 + k;
+            const int qrow = qrow0 + wg * 64 + qc;
+            const bool vis = key_ok && (!p.causal || krow <= qrow);
+            const float pv = vis ? ex2(fmaf(__uint_as_float(s[qc]), p.scale2, -lse[qc])) : 0.f;
+            pe[k] = pv;
+            de[k] = pv * (__uint_as_float(dp[qc]) - dsv[qc]) * p.scale;
+          }
+          const uint32_t off = swz_off(r, wg * 8 + c);
+          st_smem_v4(pt_base + off, pack2(pe[0], pe[1]), pack2(pe[2], pe[3]), pack2(pe[4], pe[5]), pack2(pe[6], pe[7]));
+          st_smem_v4(ds_base + off, pack2(de[0], de[1]), pack2(de[2], de[3]), pack2(de[4], de[5]), pack2(de[6], de[7]));
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(pds_full);
+        if (j > 0 && !drain_dq(g - 1, j - 1)) {
+          ok = false;
+          break;
         }
       }
-      if (ok && krow >= 0) {
+      if (ok && it.n > 0) ok = drain_dq(gq + it.n - 1, it.n - 1);
+      if (!ok) break;
+      // dK (warpgroup 1) and dV (warpgroup 0) of this key tile. The TMEM read is
+      // done by whole warps; only the store depends on the lane's key row.
+      float gk[HD];
+#pragma unroll
+      for (int d = 0; d < HD; ++d) gk[d] = 0.f;
+      if (it.n > 0) {
+        if (!warp_wait(dkv_full, items & 1, p.err, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t gr[HD];
+        tmem_ld32(t_lane + (wg == 0 ? 256 : 320), gr);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dkv_empty);
+#pragma unroll
+        for (int d = 0; d < HD; ++d) gk[d] = key_ok ? __uint_as_float(gr[d]) : 0.f;
+        ++items;
+      }
+      gq += it.n;
+      if (krow >= 0) {
         uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.dqkv) +
-                                              (static_cast<long long>(b) * Lk + krow) * 3 * p.D +
-                                              (wg == 0 ? 2 * p.D : p.D) + h * HD);
+                                              (static_cast<long long>(it.b) * Lk + krow) * 3 * p.D +
+                                              (wg == 0 ? 2 * p.D : p.D) + it.h * HD);
 #pragma unroll
         for (int c = 0; c < HD / 8; ++c)
-          dst[c] = make_uint4(pack2(g[c * 8], g[c * 8 + 1]), pack2(g[c * 8 + 2], g[c * 8 + 3]),
-                              pack2(g[c * 8 + 4], g[c * 8 + 5]), pack2(g[c * 8 + 6], g[c * 8 + 7]));
+          dst[c] = make_uint4(pack2(gk[c * 8], gk[c * 8 + 1]), pack2(gk[c * 8 + 2], gk[c * 8 + 3]),
+                              pack2(gk[c * 8 + 4], gk[c * 8 + 5]), pack2(gk[c * 8 + 6], gk[c * 8 + 7]));
       }
     }
   }
@@ -792,6 +899,16 @@ Params make_params(const FmhaArgs& a) {
 
 const char* g_reason = "";
 
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
 // Records why a host call failed (read back by fmha_last_error()).
 cudaError_t fail(const char* why, cudaError_t e) {
   if (e != cudaSuccess) g_reason = why;
@@ -818,9 +935,10 @@ cudaError_t fmha_fwd(const FmhaArgs& a, cudaStream_t stream) {
     if (e != cudaSuccess) return fail("fmha_fwd: smem attribute", e);
     configured = true;
   }
-  const long long grid = static_cast<long long>(a.H) * a.B * ((a.Lq + TILE - 1) / TILE);
-  if (grid > 0x7fffffffLL) return fail("fmha_fwd: grid", cudaErrorInvalidValue);
-  fmha_fwd_kernel<<<static_cast<unsigned>(grid), F_THREADS, F_SMEM, stream>>>(tm, p);
+  const long long items = static_cast<long long>(a.H) * a.B * ((a.Lq + TILE - 1) / TILE);
+  if (items > 0x7fffffffLL) return fail("fmha_fwd: too many work items", cudaErrorInvalidValue);
+  const int grid = static_cast<int>(std::min<long long>(items, 2LL * num_sms()));
+  fmha_fwd_kernel<<<grid, F_THREADS, F_SMEM, stream>>>(tm, p, static_cast<int>(items));
   return fail("fmha_fwd: launch", cudaGetLastError());
 }
 
@@ -845,8 +963,10 @@ cudaError_t fmha_bwd(const FmhaArgs& a, cudaStream_t stream) {
       a.dq_acc, a.B, a.Lq, a.H, p.D);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail("fmha_bwd: pre-kernel launch", e);
-  const long long grid = static_cast<long long>(a.H) * a.B * ((a.Lk + TILE - 1) / TILE);
-  fmha_bwd_kernel<<<static_cast<unsigned>(grid), NUM_THREADS, B_SMEM, stream>>>(tm, tm_do, p);
+  const long long items = static_cast<long long>(a.H) * a.B * ((a.Lk + TILE - 1) / TILE);
+  if (items > 0x7fffffffLL) return fail("fmha_bwd: too many work items", cudaErrorInvalidValue);
+  const int grid = static_cast<int>(std::min<long long>(items, num_sms()));
+  fmha_bwd_kernel<<<grid, NUM_THREADS, B_SMEM, stream>>>(tm, tm_do, p, static_cast<int>(items));
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail("fmha_bwd: main launch", e);
   const long long vec = static_cast<long long>(a.B) * a.Lk * p.D / 8;
