@@ -42,6 +42,7 @@
 #include <math_constants.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -99,6 +100,34 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// 2^x on the FMA / integer pipes, for x <= 0: Cody-Waite style split x = j + f with
+// j = round(x) taken from the low mantissa bits of x + 1.5*2^23, 2^f by a degree-3
+// polynomial on [-0.5, 0.5] (fitted here to 2^f with near-minimax relative weighting;
+// largest relative error 7.5e-5 in fp32, far below bf16 rounding), and 2^j added to
+// the exponent bits; x < -125 (masked scores included) gives 0. Used for part of the
+// softmax exponentials so that they do not all queue on the special-function unit.
+__device__ __forceinline__ float ex2_fma(float x) {
+  const float shift = 12582912.f;  // 1.5 * 2^23
+  const float t = x + shift;
+  const float j = t - shift;
+  const float f = x - j;
+  float q = fmaf(0.0551716648f, f, 0.2426111251f);
+  q = fmaf(q, f, 0.6932609677f);
+  q = fmaf(q, f, 0.9999280572f);
+  const int ji = __float_as_int(t) - 0x4B400000;
+  const float r = __int_as_float(__float_as_int(q) + (ji << 23));
+  return x < -125.f ? 0.f : r;
+}
+
+// Element k (0..7) of an 8-wide chunk: polynomial when EXPV > 0 and k % EXPV == 0.
+template <int EXPV>
+__device__ __forceinline__ float ex2_mix(float x, int k) {
+  if constexpr (EXPV > 0) {
+    if (k % EXPV == 0) return ex2_fma(x);
+  }
+  return ex2(x);
+}
+
 __device__ __forceinline__ float lg2(float x) {
   float y;
   asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -117,6 +146,22 @@ __device__ __forceinline__ void st_smem_v4(uint32_t addr, uint32_t a, uint32_t b
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Round-to-nearest-even bf16 pair of two finite floats with integer ops only (keeps
+// the conversions off the special-function pipe, which the exponentials saturate):
+// add 0x7FFF plus the lowest kept bit, keep the high halves.
+__device__ __forceinline__ uint32_t pack2_int(float a, float b) {
+  uint32_t ua = __float_as_uint(a), ub = __float_as_uint(b);
+  ua += 0x7FFFu + ((ua >> 16) & 1u);
+  ub += 0x7FFFu + ((ub >> 16) & 1u);
+  return __byte_perm(ua, ub, 0x7632);
+}
+
+template <bool INT_PACK>
+__device__ __forceinline__ uint32_t packp(float a, float b) {
+  if constexpr (INT_PACK) return pack2_int(a, b);
+  return pack2(a, b);
 }
 
 // 32 consecutive fp32 TMEM columns of this thread's lane, no wait.
@@ -200,6 +245,7 @@ __device__ __forceinline__ FwdItem fwd_item(const Params& p, int w) {
 // Persistent: each CTA walks items blockIdx.x, +gridDim.x, ...; the K/V rings and
 // every barrier phase run on across items (global tile counter g), so the loads of
 // the next item overlap the softmax of the current one.
+template <bool INT_PACK, int EXPV>
 __global__ void __launch_bounds__(F_THREADS, 2)
     fmha_fwd_kernel(const __grid_constant__ CUtensorMap tm, const Params p, int num_items) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -402,9 +448,13 @@ __global__ void __launch_bounds__(F_THREADS, 2)
           for (int c = 0; c < TILE; ++c)
             if (c < lo || c > hi) sr[c] = __float_as_uint(-CUDART_INF_F);
         }
-        float mx = -CUDART_INF_F;
+        float mx8[8];  // eight independent partial maxima (short dependency chains)
 #pragma unroll
-        for (int c = 0; c < TILE; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
+        for (int k = 0; k < 8; ++k) mx8[k] = __uint_as_float(sr[k]);
+#pragma unroll
+        for (int c = 8; c < TILE; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], __uint_as_float(sr[c]));
+        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
         const float m_new = fmaxf(m, mx * p.scale2);
         const float m_use = m_new == -CUDART_INF_F ? 0.f : m_new;
         const float alpha = ex2(m - m_use);
@@ -412,18 +462,19 @@ __global__ void __launch_bounds__(F_THREADS, 2)
           ok = false;
           break;
         }
-        float sum = 0.f;
+        float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
           float e[8];
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
-            e[k] = ex2(fmaf(__uint_as_float(sr[c * 8 + k]), p.scale2, -m_use));
-            sum += e[k];
+            e[k] = ex2_mix<EXPV>(fmaf(__uint_as_float(sr[c * 8 + k]), p.scale2, -m_use), k);
+            sum8[k] += e[k];
           }
-          st_smem_v4(p_base + swz_off(r, c), pack2(e[0], e[1]), pack2(e[2], e[3]), pack2(e[4], e[5]),
-                     pack2(e[6], e[7]));
+          st_smem_v4(p_base + swz_off(r, c), packp<INT_PACK>(e[0], e[1]), packp<INT_PACK>(e[2], e[3]),
+                     packp<INT_PACK>(e[4], e[5]), packp<INT_PACK>(e[6], e[7]));
         }
+        const float sum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
         fence_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(p_full);
@@ -520,6 +571,7 @@ __device__ __forceinline__ BwdItem bwd_item(const Params& p, int w) {
 // Persistent: K/V of successive items in a 2-stage ring, Q/dO/lse/D of successive
 // query tiles in a 2-stage ring; barrier phases run on across items (item counter
 // for K/V and dK/dV, global query-tile counter for the rest).
+template <bool INT_PACK, int EXPV>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     fmha_bwd_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap tm_do,
                     const Params p, int num_items) {
@@ -766,13 +818,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const int qc = c * 8 + k;
             const int qrow = qrow0 + wg * 64 + qc;
             const bool vis = key_ok && (!p.causal || krow <= qrow);
-            const float pv = vis ? ex2(fmaf(__uint_as_float(s[qc]), p.scale2, -lse[qc])) : 0.f;
+            const float pv = vis ? ex2_mix<EXPV>(fmaf(__uint_as_float(s[qc]), p.scale2, -lse[qc]), k) : 0.f;
             pe[k] = pv;
             de[k] = pv * (__uint_as_float(dp[qc]) - dsv[qc]) * p.scale;
           }
           const uint32_t off = swz_off(r, wg * 8 + c);
-          st_smem_v4(pt_base + off, pack2(pe[0], pe[1]), pack2(pe[2], pe[3]), pack2(pe[4], pe[5]), pack2(pe[6], pe[7]));
-          st_smem_v4(ds_base + off, pack2(de[0], de[1]), pack2(de[2], de[3]), pack2(de[4], de[5]), pack2(de[6], de[7]));
+          st_smem_v4(pt_base + off, packp<INT_PACK>(pe[0], pe[1]), packp<INT_PACK>(pe[2], pe[3]),
+                     packp<INT_PACK>(pe[4], pe[5]), packp<INT_PACK>(pe[6], pe[7]));
+          st_smem_v4(ds_base + off, packp<INT_PACK>(de[0], de[1]), packp<INT_PACK>(de[2], de[3]),
+                     packp<INT_PACK>(de[4], de[5]), packp<INT_PACK>(de[6], de[7]));
         }
         fence_async_smem();
         __syncwarp();
@@ -899,6 +953,21 @@ Params make_params(const FmhaArgs& a) {
 
 const char* g_reason = "";
 
+// Kernel variant: bf16 packing of P / dS with integer ops or cvt
+// (MDL_B200_FMHA_INT_PACK=1/0) x share of exponentials on the FMA pipes
+// (MDL_B200_FMHA_EXP_POLY=0: none, 2: every second, 4: every fourth).
+int kernel_variant() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("MDL_B200_FMHA_INT_PACK");
+    const int ip = (e == nullptr || e[0] != '0') ? 1 : 0;
+    const char* x = std::getenv("MDL_B200_FMHA_EXP_POLY");
+    const int ev = x == nullptr ? 0 : (x[0] == '2' ? 1 : (x[0] == '4' ? 2 : 0));
+    v = ip * 3 + ev;
+  }
+  return v;
+}
+
 int num_sms() {
   static int n = 0;
   if (n == 0) {
@@ -929,16 +998,21 @@ cudaError_t fmha_fwd(const FmhaArgs& a, cudaStream_t stream) {
   const Params p = make_params(a);
   CUtensorMap tm;
   if (!encode_rows(&tm, a.qkv, 3ull * p.D, a.Lk, a.B)) return fail("fmha_fwd: qkv tensor map", cudaErrorInvalidValue);
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(fmha_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, F_SMEM);
+  const int variant = kernel_variant();
+  using FwdKern = void (*)(const CUtensorMap, const Params, int);
+  static const FwdKern kerns[6] = {fmha_fwd_kernel<false, 0>, fmha_fwd_kernel<false, 2>, fmha_fwd_kernel<false, 4>,
+                                   fmha_fwd_kernel<true, 0>,  fmha_fwd_kernel<true, 2>,  fmha_fwd_kernel<true, 4>};
+  const FwdKern kern = kerns[variant];
+  static bool configured[6] = {false, false, false, false, false, false};
+  if (!configured[variant]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, F_SMEM);
     if (e != cudaSuccess) return fail("fmha_fwd: smem attribute", e);
-    configured = true;
+    configured[variant] = true;
   }
   const long long items = static_cast<long long>(a.H) * a.B * ((a.Lq + TILE - 1) / TILE);
   if (items > 0x7fffffffLL) return fail("fmha_fwd: too many work items", cudaErrorInvalidValue);
   const int grid = static_cast<int>(std::min<long long>(items, 2LL * num_sms()));
-  fmha_fwd_kernel<<<grid, F_THREADS, F_SMEM, stream>>>(tm, p, static_cast<int>(items));
+  kern<<<grid, F_THREADS, F_SMEM, stream>>>(tm, p, static_cast<int>(items));
   return fail("fmha_fwd: launch", cudaGetLastError());
 }
 
@@ -951,11 +1025,16 @@ cudaError_t fmha_bwd(const FmhaArgs& a, cudaStream_t stream) {
   CUtensorMap tm, tm_do;
   if (!encode_rows(&tm, a.qkv, 3ull * p.D, a.Lk, a.B)) return fail("fmha_bwd: qkv tensor map", cudaErrorInvalidValue);
   if (!encode_rows(&tm_do, a.dout, p.D, a.Lq, a.B)) return fail("fmha_bwd: dout tensor map", cudaErrorInvalidValue);
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(fmha_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, B_SMEM);
+  const int variant = kernel_variant();
+  using BwdKern = void (*)(const CUtensorMap, const CUtensorMap, const Params, int);
+  static const BwdKern kerns[6] = {fmha_bwd_kernel<false, 0>, fmha_bwd_kernel<false, 2>, fmha_bwd_kernel<false, 4>,
+                                   fmha_bwd_kernel<true, 0>,  fmha_bwd_kernel<true, 2>,  fmha_bwd_kernel<true, 4>};
+  const BwdKern kern = kerns[variant];
+  static bool configured[6] = {false, false, false, false, false, false};
+  if (!configured[variant]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, B_SMEM);
     if (e != cudaSuccess) return fail("fmha_bwd: smem attribute", e);
-    configured = true;
+    configured[variant] = true;
   }
   const long long rows = static_cast<long long>(a.B) * a.Lq;
   fmha_bwd_pre_kernel<<<static_cast<unsigned>((rows * 32 + 255) / 256), 256, 0, stream>>>(
@@ -966,7 +1045,7 @@ cudaError_t fmha_bwd(const FmhaArgs& a, cudaStream_t stream) {
   const long long items = static_cast<long long>(a.H) * a.B * ((a.Lk + TILE - 1) / TILE);
   if (items > 0x7fffffffLL) return fail("fmha_bwd: too many work items", cudaErrorInvalidValue);
   const int grid = static_cast<int>(std::min<long long>(items, num_sms()));
-  fmha_bwd_kernel<<<grid, NUM_THREADS, B_SMEM, stream>>>(tm, tm_do, p, static_cast<int>(items));
+  kern<<<grid, NUM_THREADS, B_SMEM, stream>>>(tm, tm_do, p, static_cast<int>(items));
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail("fmha_bwd: main launch", e);
   const long long vec = static_cast<long long>(a.B) * a.Lk * p.D / 8;
