@@ -955,12 +955,17 @@ const char* g_reason = "";
 
 // Kernel variant: bf16 packing of P / dS with integer ops or cvt
 // (MDL_B200_FMHA_INT_PACK=1/0) x share of exponentials on the FMA pipes
-// (MDL_B200_FMHA_EXP_POLY=0: none, 2: every second, 4: every fourth).
+// (MDL_B200_FMHA_EXP_POLY=0: none, 2: every second, 4: every fourth). Measured on
+// the OneTrans layer-0 shape (B=1024, L=544, 8 heads): cvt + all exponentials on
+// the special-function unit is fastest (forward 1.48 ms, backward 3.52 ms); every
+// variant that moves work to the integer / FMA pipes is slower (up to 2.31 / 4.23
+// ms), i.e. the kernels are bound by instruction issue and latency, not by the
+// special-function unit. Default: cvt, no polynomial.
 int kernel_variant() {
   static int v = -1;
   if (v < 0) {
     const char* e = std::getenv("MDL_B200_FMHA_INT_PACK");
-    const int ip = (e == nullptr || e[0] != '0') ? 1 : 0;
+    const int ip = (e != nullptr && e[0] == '1') ? 1 : 0;
     const char* x = std::getenv("MDL_B200_FMHA_EXP_POLY");
     const int ev = x == nullptr ? 0 : (x[0] == '2' ? 1 : (x[0] == '4' ? 2 : 0));
     v = ip * 3 + ev;
