@@ -40,9 +40,11 @@ MODEL_DESC = {
        "3 task tokens, FiLM scene bias, T=16 D=768 L=2 FFNx4, 3 heads)",
     4: "onetrans (BASELINE config 4: 512-event sequence of item + 4 side ids, 32 NS tokens from the config-2 "
        "fields, d=256 8 heads FFN 1024, 6 layers, causal, pyramid halving every 2 layers, click head)",
+    5: "longer (BASELINE config 5: 100-2000 item ids padded to 2000, target-item global token, cross block to 256 "
+       "recent tokens + target, 2 self blocks d=256 8 heads, MixFormer-style head over 32 NS tokens, click head)",
 }
-DEFAULT_BATCH = {2: 2048, 3: 2048, 4: 1024}
-SEQ_LEN = {4: 512}
+DEFAULT_BATCH = {2: 2048, 3: 2048, 4: 1024, 5: 512}
+SEQ_LEN = {4: 512, 5: 2000}
 
 
 def _dist_setup(args):
@@ -193,7 +195,7 @@ def main(argv=None) -> int:
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--batch", type=int, default=None, help="rows per GPU (default: the workload's)")
     p.add_argument("--config", type=int, default=2, choices=sorted(MODEL_DESC),
-                   help="BASELINE workload (2: RankMixer headline, 3: MDL, 4: OneTrans)")
+                   help="BASELINE workload (2: RankMixer headline, 3: MDL, 4: OneTrans, 5: LONGER + MixFormer)")
     p.add_argument("--pool", type=int, default=4, help="distinct pinned host batches rotated per step")
     p.add_argument("--ref-no-graphs", action="store_true", help="reference arm: disable its CUDA-graph backbone")
     args = p.parse_args(argv)

@@ -709,7 +709,8 @@ void position_grad(const at::Tensor& dx, const at::Tensor& dpos, const at::Tenso
 
 // ------------------------------------------------------------------ flash attention
 mdl::FmhaArgs fmha_args(const at::Tensor& qkv, const at::Tensor& kstart, const at::Tensor& out, const at::Tensor& lse,
-                        int64_t H, int64_t Lq, bool causal, double scale, const std::optional<at::Tensor>& err) {
+                        int64_t H, int64_t Lq, bool causal, double scale, const std::optional<at::Tensor>& err,
+                        int64_t ktail) {
   require_cuda(qkv, "qkv");
   TORCH_CHECK(qkv.scalar_type() == at::kBFloat16 && qkv.dim() == 3 && qkv.is_contiguous(), "qkv must be [B, Lk, 3D] bf16");
   TORCH_CHECK(kstart.scalar_type() == at::kInt && kstart.numel() == qkv.size(0), "kstart must be int32 [B]");
@@ -726,6 +727,7 @@ mdl::FmhaArgs fmha_args(const at::Tensor& qkv, const at::Tensor& kstart, const a
   a.hd = static_cast<int>(qkv.size(2) / 3 / H);
   a.Lq = static_cast<int>(Lq);
   a.causal = causal;
+  a.ktail = static_cast<int>(ktail);
   a.scale = static_cast<float>(scale);
   a.err = optr<int>(err);
   TORCH_CHECK(qkv.size(2) == 3 * H * a.hd, "qkv width must be 3 * H * head_dim");
@@ -735,9 +737,9 @@ mdl::FmhaArgs fmha_args(const at::Tensor& qkv, const at::Tensor& kstart, const a
 }
 
 void fmha_fwd(const at::Tensor& qkv, const at::Tensor& kstart, const at::Tensor& out, const at::Tensor& lse, int64_t H,
-              int64_t Lq, bool causal, double scale, const std::optional<at::Tensor>& err) {
+              int64_t Lq, bool causal, double scale, const std::optional<at::Tensor>& err, int64_t ktail) {
   c10::cuda::CUDAGuard guard(qkv.device());
-  auto a = fmha_args(qkv, kstart, out, lse, H, Lq, causal, scale, err);
+  auto a = fmha_args(qkv, kstart, out, lse, H, Lq, causal, scale, err, ktail);
   cudaError_t e = mdl::fmha_fwd(a, stream_of(qkv));
   if (e != cudaSuccess) throw std::runtime_error(std::string(mdl::fmha_last_error()) + ": " + cudaGetErrorString(e));
   g_launches += 1;
@@ -745,9 +747,10 @@ void fmha_fwd(const at::Tensor& qkv, const at::Tensor& kstart, const at::Tensor&
 
 void fmha_bwd(const at::Tensor& qkv, const at::Tensor& kstart, const at::Tensor& out, const at::Tensor& lse,
               const at::Tensor& dout, const at::Tensor& dqkv, const at::Tensor& dq_acc, const at::Tensor& dsum,
-              int64_t H, int64_t Lq, bool causal, double scale, const std::optional<at::Tensor>& err) {
+              int64_t H, int64_t Lq, bool causal, double scale, const std::optional<at::Tensor>& err,
+              int64_t ktail) {
   c10::cuda::CUDAGuard guard(qkv.device());
-  auto a = fmha_args(qkv, kstart, out, lse, H, Lq, causal, scale, err);
+  auto a = fmha_args(qkv, kstart, out, lse, H, Lq, causal, scale, err, ktail);
   TORCH_CHECK(dout.scalar_type() == at::kBFloat16 && dout.is_contiguous() && dout.numel() == out.numel(),
               "dout must be contiguous bf16 like out");
   TORCH_CHECK(dqkv.scalar_type() == at::kBFloat16 && dqkv.is_contiguous() && dqkv.numel() == qkv.numel(),
@@ -812,8 +815,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("launch_count", &launch_count);
   m.def("small_attn_fwd", &small_attn_fwd);
   m.def("small_attn_bwd", &small_attn_bwd);
-  m.def("fmha_fwd", &fmha_fwd);
+  m.def("fmha_fwd", &fmha_fwd, py::arg("qkv"), py::arg("kstart"), py::arg("out"), py::arg("lse"), py::arg("H"),
+        py::arg("Lq"), py::arg("causal"), py::arg("scale"), py::arg("err") = py::none(), py::arg("ktail") = 0);
   m.def("position_add", &position_add);
   m.def("position_grad", &position_grad);
-  m.def("fmha_bwd", &fmha_bwd);
+  m.def("fmha_bwd", &fmha_bwd, py::arg("qkv"), py::arg("kstart"), py::arg("out"), py::arg("lse"), py::arg("dout"),
+        py::arg("dqkv"), py::arg("dq_acc"), py::arg("dsum"), py::arg("H"), py::arg("Lq"), py::arg("causal"),
+        py::arg("scale"), py::arg("err") = py::none(), py::arg("ktail") = 0);
 }

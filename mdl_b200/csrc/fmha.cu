@@ -86,6 +86,7 @@ struct Params {
   const float* dsum;
   void* dqkv;
   int B, H, Lk, Lq, D, causal;
+  int ktail;  // the last ktail tokens see and are seen by every token (causal only)
   float scale, scale2;
   int* err;
 };
@@ -226,7 +227,7 @@ __device__ __forceinline__ void red_add_v4(float* dst, float a, float b, float c
 // Work item = (sample, head, query tile); items are numbered heaviest first (query
 // tile 0 = the last 128 rows sees the most key tiles under causality).
 struct FwdItem {
-  int b, h, i, t0, n, kst;
+  int b, h, i, t0, n, kst, extra0;
 };
 
 __device__ __forceinline__ FwdItem fwd_item(const Params& p, int w) {
@@ -238,8 +239,16 @@ __device__ __forceinline__ FwdItem fwd_item(const Params& p, int w) {
   it.kst = min(max(p.kstart[it.b], 0), p.Lk);
   const int tmax = (p.Lk - it.kst + TILE - 1) / TILE - 1;
   it.t0 = p.causal ? it.i : 0;
-  it.n = max(0, tmax - it.t0 + 1);  // key tiles visited
+  // trailing always-visible tokens live in key tile 0, which a causal query tile
+  // i > 0 would otherwise skip: visit it first
+  it.extra0 = (p.causal && p.ktail > 0 && it.i > 0 && tmax >= 0) ? 1 : 0;
+  it.n = max(0, tmax - it.t0 + 1) + it.extra0;  // key tiles visited
   return it;
+}
+
+// Key tile of the j-th visited tile of an item.
+__device__ __forceinline__ int fwd_tile(const FwdItem& it, int j) {
+  return it.extra0 ? (j == 0 ? 0 : it.t0 + j - 1) : it.t0 + j;
 }
 
 // Persistent: each CTA walks items blockIdx.x, +gridDim.x, ...; the K/V rings and
@@ -321,7 +330,7 @@ __global__ void __launch_bounds__(F_THREADS, 2)
         ++items;
         for (int j = 0; j < it.n; ++j, ++g) {
           const int st = g & 1;
-          const int y = Lk - TILE * (it.t0 + j + 1);
+          const int y = Lk - TILE * (fwd_tile(it, j) + 1);
           if (g >= 2 && !mbar_wait(&k_empty[st], ((g >> 1) - 1) & 1, p.err, abort_flag)) {
             ok = false;
             break;
@@ -427,7 +436,7 @@ __global__ void __launch_bounds__(F_THREADS, 2)
       };
       for (int j = 0; j < it.n; ++j) {
         const int g = g0 + j;
-        const int t = it.t0 + j;
+        const int t = fwd_tile(it, j);
         const int kbase = Lk - TILE * (t + 1);
         if (!warp_wait(s_full, g & 1, p.err, abort_flag)) {
           ok = false;
@@ -441,12 +450,17 @@ __global__ void __launch_bounds__(F_THREADS, 2)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(s_empty);
-        const int lo = it.kst - kbase;                         // columns < lo are padding
-        const int hi = (p.causal && t == it.i) ? r : TILE - 1;  // columns > hi are in the future
-        if (lo > 0 || hi < TILE - 1) {
+        // padding, the diagonal tile and the tile of the trailing tokens need a per-column mask
+        const int tail0 = Lk - p.ktail;
+        const bool special = it.kst > kbase || (p.causal && (t == it.i || (p.ktail > 0 && t == 0)));
+        if (special) {
+          const bool q_tail = qrow >= tail0;
 #pragma unroll
-          for (int c = 0; c < TILE; ++c)
-            if (c < lo || c > hi) sr[c] = __float_as_uint(-CUDART_INF_F);
+          for (int c = 0; c < TILE; ++c) {
+            const int jj = kbase + c;
+            const bool vis = jj >= it.kst && (!p.causal || jj <= qrow || jj >= tail0 || q_tail);
+            if (!vis) sr[c] = __float_as_uint(-CUDART_INF_F);
+          }
         }
         float mx8[8];  // eight independent partial maxima (short dependency chains)
 #pragma unroll
@@ -562,7 +576,8 @@ __device__ __forceinline__ BwdItem bwd_item(const Params& p, int w) {
   it.kst = min(max(p.kstart[it.b], 0), p.Lk);
   it.qlo = max(it.kst, p.Lk - p.Lq);  // first row that is a query with a visible key
   const int nq = (p.Lq + TILE - 1) / TILE;
-  int imax = p.causal ? min(t, nq - 1) : nq - 1;
+  // key tile 0 holds the trailing always-visible tokens: every query tile sees it
+  int imax = (p.causal && !(p.ktail > 0 && t == 0)) ? min(t, nq - 1) : nq - 1;
   imax = min(imax, (p.Lk - 1 - it.qlo) / TILE);
   it.n = (it.kbase + TILE - 1 >= it.kst && it.qlo < p.Lk) ? max(0, imax + 1) : 0;  // query tiles visited
   return it;
@@ -817,7 +832,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           for (int k = 0; k < 8; ++k) {
             const int qc = c * 8 + k;
             const int qrow = qrow0 + wg * 64 + qc;
-            const bool vis = key_ok && (!p.causal || krow <= qrow);
+            // qrow >= qlo also drops rows that are not queries (their Q may be any finite value)
+            const bool vis = key_ok && qrow >= it.qlo &&
+                             (!p.causal || krow <= qrow || krow >= Lk - p.ktail || qrow >= Lk - p.ktail);
             const float pv = vis ? ex2_mix<EXPV>(fmaf(__uint_as_float(s[qc]), p.scale2, -lse[qc]), k) : 0.f;
             pe[k] = pv;
             de[k] = pv * (__uint_as_float(dp[qc]) - dsv[qc]) * p.scale;
@@ -945,6 +962,7 @@ Params make_params(const FmhaArgs& a) {
   p.Lq = a.Lq;
   p.D = a.H * HD;
   p.causal = a.causal ? 1 : 0;
+  p.ktail = a.causal ? a.ktail : 0;
   p.scale = a.scale > 0.f ? a.scale : 1.f / sqrtf(static_cast<float>(HD));
   p.scale2 = p.scale * kLog2e;
   p.err = a.err;
@@ -990,7 +1008,8 @@ cudaError_t fail(const char* why, cudaError_t e) {
 }
 
 bool shapes_ok(const FmhaArgs& a) {
-  return a.hd == HD && a.B > 0 && a.H > 0 && a.Lq > 0 && a.Lq <= a.Lk && a.kstart != nullptr &&
+  return a.hd == HD && a.B > 0 && a.H > 0 && a.Lq > 0 && a.Lq <= a.Lk && a.kstart != nullptr && a.ktail >= 0 &&
+         a.ktail <= TILE && a.ktail <= a.Lq &&
          (reinterpret_cast<uintptr_t>(a.qkv) & 15) == 0;
 }
 

@@ -13,13 +13,16 @@ namespace mdl {
 //
 //   qkv   [B, Lk, 3*D] bf16: per token Q | K | V, D = H * 32 (head h at h*32)
 //   the queries are the last Lq tokens (rows Lk-Lq .. Lk-1) of each sample
-//   key j is visible to query row p iff kstart[b] <= j and (!causal or j <= p)
+//   key j is visible to query row p iff kstart[b] <= j and (!causal or j <= p or
+//   j >= Lk - ktail or p >= Lk - ktail)
 //   out   [B, Lq, D] bf16, rows whose query has no visible key are zero
 //   lse   [B, H, Lq] fp32: base-2 log-sum-exp of the scaled scores (+inf for
 //         rows without a visible key), saved for the backward
 //
 // Backward: dqkv [B, Lk, 3*D] bf16 (every element written; Q rows that are not
 // queries get zero), workspaces dq_acc fp32 [B, Lq, D] and dsum fp32 [B, H, Lq].
+// Q of rows that are not queries is read (query tiles are 128 rows aligned to the
+// end) but must only be finite: rows [max(0, Lk - 128*ceil(Lq/128)), Lk - Lq).
 // head_dim is 32; H must be even for the forward (two heads per CTA).
 struct FmhaArgs {
   const void* qkv = nullptr;
@@ -32,6 +35,9 @@ struct FmhaArgs {
   float* dsum = nullptr;
   int B = 0, H = 0, Lk = 0, Lq = 0, hd = 32;
   bool causal = true;
+  // With causal: the last ktail tokens (<= 128, all queries) see every key and are
+  // seen by every query (LONGER's global tokens placed after the sequence).
+  int ktail = 0;
   float scale = 0.f;            // softmax scale (1/sqrt(hd) when 0)
   int* err = nullptr;
 };

@@ -106,9 +106,52 @@ def config4(num_fields: int = 300, batch: int = 1024, seq_len: int = 512, side_f
     return m, spec
 
 
+def config5(num_fields: int = 300, batch: int = 512, seq_len: int = 2000, min_len: int = 100,
+            item_vocab: int = 10_000_000, query_tokens: int = 256, self_layers: int = 2, d: int = 256, heads: int = 8,
+            sequence_head: str = "mixformer", ns_tokens: int = 32) -> tuple[dict, SyntheticSpec]:
+    """Workload 5, LONGER: a behaviour sequence of 100-2000 item ids (padded to 2000,
+    shared 64-dim item table with the target item), target-item global token, cross
+    block to the last 256 events + the target, 2 self blocks (d=256, 8 heads), then a
+    MixFormer-style head over 32 NS tokens from the workload-2 fields (or flattened
+    LONGER tokens with ``sequence_head="none"``); click head, batch 512 per GPU."""
+
+    tasks = {"click": 0.05}
+    m = _rankmixer_common("longer", tasks, batch, "bf16", "cuda")
+    feats, fields = _config2_features(num_fields)
+    feats = copy.deepcopy(feats)
+    feats.append({"name": "target_item", "kind": "categorical", "source": "target_item", "embedding_dim": 64,
+                  "encoding": {"type": "identity", "max_id": item_vocab}})
+    fields["target_item"] = FieldSpec(vocab=item_vocab)
+    m["features"] = feats
+    m["sequences"] = [{"name": "behavior", "max_length": seq_len, "encoder": "longer",
+                       "sequence_order": "oldest_to_newest", "truncation": "tail",
+                       "fields": [{"name": "item_id", "kind": "categorical", "source": "behavior_item_id",
+                                   "embedding_dim": 64,
+                                   "encoding": {"type": "identity", "max_id": item_vocab, "share_with": "target_item",
+                                                "share_embedding": True}}],
+                       "target_inputs": ["target_item"], "longer_dim": d, "longer_num_heads": heads,
+                       "longer_hidden_dim": 4 * d, "longer_query_tokens": query_tokens,
+                       "longer_self_layers": self_layers, "longer_token_merge": 1,
+                       "longer_candidate_global_tokens": 1}]
+    m["tokenization"] = {"feature_tokenizer": "auto_split", "num_feature_tokens": ns_tokens,
+                         "feature_token_inputs": [f["name"] for f in feats if f["name"] != "target_item"]}
+    m["model"].update({"embedding_dim": 64, "token_dim": 64, "num_heads": 2, "hidden_dim": 256,
+                       "task_head_hidden_dim": 1024, "ffn_activation": "gelu", "sequence_head": sequence_head,
+                       "num_layers": 1, "num_ns_tokens": ns_tokens, "use_task_tokens": False,
+                       "use_scenario_tokens": False, "use_global_scenario_token": False})
+    m["training"].update({"lr_dense": 1e-4, "lr_sparse": 0.05, "dense_optimizer": "rmsprop", "lr_warmup_steps": 1000,
+                          "rmsprop_alpha": 0.99999, "adagrad_initial_accumulator_value": 0.0})
+    seq = SequenceSpec(fields={"item_id": FieldSpec(vocab=item_vocab)}, max_len=seq_len, min_len=min_len)
+    spec = SyntheticSpec(fields=fields, dense_width=64, task_rates=list(tasks.values()), zipf_s=1.05, seed=0,
+                         sequences={"behavior": seq})
+    return m, spec
+
+
 def config(n: int, **kw) -> tuple[dict, SyntheticSpec]:
     if n == 3:
         return config3(**kw)
     if n == 4:
         return config4(**kw)
+    if n == 5:
+        return config5(**kw)
     raise ValueError(f"no benchmark workload {n}")

@@ -1,0 +1,241 @@
+"""MixFormer: feature heads that read one long behaviour sequence through cross attention.
+
+Reference: ``src/modules/mixformer.py`` (``MixFormerRMSNorm`` :28, ``DenseSwiGLUFFN`` :56,
+``StackedPerHeadSwiGLUFFN`` :82-115, ``MixFormerHeadMixing`` :118-174,
+``MixFormerQueryMixer`` :177, ``MixFormerOutputFusion`` :203,
+``MixFormerCrossAttention`` :226-784, ``MixFormerBlock`` :787-845) and
+``MixFormerModel`` ``src/model.py:8473-8578``.
+
+Block (``N`` heads of width ``D``, sequence width ``N * D``):
+
+* Query Mixer: ``x + HeadMixing(RMSNorm(x))`` (parameter-free transpose of the
+  ``[N, N, D/N]`` chunks), then ``+ SwiGLU_n(RMSNorm(.))`` per head;
+* Cross Attention: ``hist = s + SwiGLU(RMSNorm(s))`` viewed ``[L, N, D]``; head
+  ``n`` is one full-width query: ``q' = RMSNorm(x_n) W_k[n]``,
+  ``w = softmax(q' . hist[:, n] / sqrt(D))`` over valid events,
+  ``x_n + (sum_l w_l hist[l, n]) W_v[n]^T`` (the reordered form: no length-sized
+  K/V are materialised);
+* Output Fusion: ``x + SwiGLU_n(RMSNorm(x))``.
+
+The SwiGLU networks (per head and the sequence one) are grouped tcgen05 GEMMs
+(``ops.layers.SwiGLUFn``); RMSNorm runs on the CUDA kernel.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from ..ops.layers import gemm_param, rms_norm, swiglu
+
+
+def _kaiming_uniform_a5_(t: torch.Tensor) -> None:
+    """``nn.init.kaiming_uniform_(a=sqrt(5))`` on each [out, in] slice (nn.Linear's default)."""
+
+    for i in range(t.shape[0]):
+        nn.init.kaiming_uniform_(t[i], a=math.sqrt(5))
+
+
+class SwiGLUStack(nn.Module):
+    """``N`` bias-free SwiGLU FFNs; ``w_ug`` stacks each head's up and gate weights."""
+
+    def __init__(self, num: int, dim: int, hidden: int, device=None) -> None:
+        super().__init__()
+        self.num, self.dim, self.hidden = num, dim, hidden
+        self.w_ug = gemm_param(torch.empty(num, 2 * hidden, dim, device=device))
+        self.w_o = gemm_param(torch.empty(num, dim, hidden, device=device))
+        _kaiming_uniform_a5_(self.w_ug.data[:, :hidden])
+        _kaiming_uniform_a5_(self.w_ug.data[:, hidden:])
+        _kaiming_uniform_a5_(self.w_o.data)
+
+    def forward(self, x: torch.Tensor, native: bool) -> torch.Tensor:
+        return swiglu(x, self.w_ug, self.w_o, native)
+
+
+def head_mixing(x: torch.Tensor) -> torch.Tensor:
+    """``[B, N, D] -> [B, N, N, D/N] -> transpose(1, 2) -> [B, N, D]``."""
+
+    B, N, D = x.shape
+    return x.reshape(B, N, N, D // N).transpose(1, 2).reshape(B, N, D)
+
+
+class MixFormerBlock(nn.Module):
+    def __init__(self, num_heads: int, dim: int, hidden: int, seq_hidden: int, device=None) -> None:
+        super().__init__()
+        if dim % num_heads:
+            raise ValueError("MixFormer head width must be divisible by the head count")
+        N, D = num_heads, dim
+        self.N, self.D = N, D
+        self.qm_norm = nn.Parameter(torch.ones(D, device=device))
+        self.qm_ffn_norm = nn.Parameter(torch.ones(D, device=device))
+        self.qm_ffn = SwiGLUStack(N, D, hidden, device=device)
+        self.seq_norm = nn.Parameter(torch.ones(N * D, device=device))
+        self.seq_ffn = SwiGLUStack(1, N * D, seq_hidden, device=device)
+        self.key_weight = nn.Parameter(torch.empty(N, D, D, device=device))
+        self.value_weight = nn.Parameter(torch.empty(N, D, D, device=device))
+        for n in range(N):
+            nn.init.xavier_uniform_(self.key_weight.data[n])
+            nn.init.xavier_uniform_(self.value_weight.data[n])
+        self.q_norm = nn.Parameter(torch.ones(D, device=device))
+        self.of_norm = nn.Parameter(torch.ones(D, device=device))
+        self.of_ffn = SwiGLUStack(N, D, hidden, device=device)
+
+    def history(self, seq: torch.Tensor, native: bool) -> torch.Tensor:
+        """``s + SwiGLU(RMSNorm(s))`` viewed ``[B, L, N, D]``."""
+
+        B, L, W = seq.shape
+        flat = seq.reshape(B * L, 1, W)
+        h = flat + self.seq_ffn(rms_norm(flat, self.seq_norm, native=native), native)
+        return h.view(B, L, self.N, self.D)
+
+    def forward(self, x: torch.Tensor, seq: torch.Tensor, valid: torch.Tensor, native: bool) -> torch.Tensor:
+        """``x [B, N, D]`` heads, ``seq [B, L, N*D]``, ``valid [B, L]`` -> ``[B, N, D]``."""
+
+        # Query Mixer
+        x = x + head_mixing(rms_norm(x, self.qm_norm, native=native))
+        x = x + self.qm_ffn(rms_norm(x, self.qm_ffn_norm, native=native), native)
+        # Cross Attention (reordered single-query form)
+        hist = self.history(seq, native)
+        qn = rms_norm(x, self.q_norm, native=native).float()
+        sq = torch.einsum("bno,noi->bni", qn, self.key_weight)                 # q' = q W_k
+        scores = torch.einsum("bni,blni->bnl", sq, hist.float()) / math.sqrt(self.D)
+        mask = valid.bool().unsqueeze(1)
+        scores = scores.masked_fill(~mask, float("-inf"))
+        w = torch.nan_to_num(torch.softmax(scores, dim=-1)) * mask
+        ctx = torch.einsum("bnl,blni->bni", w, hist.float())
+        x = x + torch.einsum("bni,noi->bno", ctx, self.value_weight).to(x.dtype)
+        # Output Fusion
+        return x + self.of_ffn(rms_norm(x, self.of_norm, native=native), native)
+
+    def reference_state_dict(self, prefix: str) -> dict[str, torch.Tensor]:
+        H = self.qm_ffn.hidden
+        Hs = self.seq_ffn.hidden
+        sd = {prefix + "query_mixer.input_norm.weight": self.qm_norm,
+              prefix + "query_mixer.ffn_norm.weight": self.qm_ffn_norm,
+              prefix + "query_mixer.ffn.up_weight": self.qm_ffn.w_ug[:, :H],
+              prefix + "query_mixer.ffn.gate_weight": self.qm_ffn.w_ug[:, H:],
+              prefix + "query_mixer.ffn.output_weight": self.qm_ffn.w_o,
+              prefix + "cross_attention.sequence_norm.weight": self.seq_norm,
+              prefix + "cross_attention.sequence_ffn.up_projection.weight": self.seq_ffn.w_ug[0, :Hs],
+              prefix + "cross_attention.sequence_ffn.gate_projection.weight": self.seq_ffn.w_ug[0, Hs:],
+              prefix + "cross_attention.sequence_ffn.output_projection.weight": self.seq_ffn.w_o[0],
+              prefix + "cross_attention.key_weight": self.key_weight,
+              prefix + "cross_attention.value_weight": self.value_weight,
+              prefix + "cross_attention.query_norm.weight": self.q_norm,
+              prefix + "output_fusion.norm.weight": self.of_norm,
+              prefix + "output_fusion.ffn.up_weight": self.of_ffn.w_ug[:, :H],
+              prefix + "output_fusion.ffn.gate_weight": self.of_ffn.w_ug[:, H:],
+              prefix + "output_fusion.ffn.output_weight": self.of_ffn.w_o}
+        return {k: v.detach().clone() for k, v in sd.items()}
+
+
+class MixFormerHead(nn.Module):
+    """Feature heads (an ``auto_split`` MLP of the scalar inputs to ``N x D``) that read
+    a token sequence ``[B, L, W]`` (projected to ``N * D``) through MixFormer blocks;
+    the heads are flattened for the task heads."""
+
+    def __init__(self, k_in: int, k_log: int, seq_width: int, num_heads: int, dim: int, hidden: int, seq_hidden: int,
+                 layers: int, device=None) -> None:
+        super().__init__()
+        from .longer import _MLP  # deferred: longer imports this module
+
+        self.N, self.D = num_heads, dim
+        self.feature_mlp = _MLP(k_in, k_log, hidden, num_heads * dim, device=device)
+        self.seq_proj = gemm_param(torch.empty(num_heads * dim, seq_width, device=device))
+        nn.init.kaiming_uniform_(self.seq_proj.data, a=math.sqrt(5))
+        self.blocks = nn.ModuleList(MixFormerBlock(num_heads, dim, hidden, seq_hidden, device=device)
+                                    for _ in range(layers))
+        self.output_dim = num_heads * dim
+
+    def forward(self, feat_in: torch.Tensor, seq: torch.Tensor, valid: torch.Tensor, native: bool) -> torch.Tensor:
+        B, L, W = seq.shape
+        x = self.feature_mlp(feat_in, native).view(B, self.N, self.D)
+        if native:
+            from ..ops.layers import LinearFn
+
+            s = LinearFn.apply(seq.reshape(B * L, W).to(torch.bfloat16), self.seq_proj, None).view(B, L, -1)
+        else:
+            s = (seq.float().reshape(B * L, W) @ self.seq_proj.t()).view(B, L, self.N * self.D)
+        for blk in self.blocks:
+            x = blk(x, s, valid, native)
+        return x.reshape(B, self.N * self.D)
+
+
+class MixFormerModel(nn.Module):
+    """``model.name: mixformer``: ``num_ns_tokens`` (or the feature-token count) feature
+    heads of width ``token_dim`` from the scalar inputs (``auto_split`` MLP), one raw
+    behaviour sequence whose events (field embeddings through a step MLP) form the
+    ``N * token_dim`` sequence, ``num_layers`` MixFormer blocks, flattened heads ->
+    task heads (reference ``MixFormerModel`` ``src/model.py:8473-8578``)."""
+
+    def __init__(self, config, *, device: torch.device, rank: int = 0, world: int = 1, process_group=None,
+                 vocab_sizes: dict[str, int] | None = None, base_seed: int | None = None) -> None:
+        super().__init__()
+        from .features import FeatureEncoder
+        from .heads import TaskHeads
+        from .longer import _MLP
+
+        m = config.model
+        raw = [s for s in config.sequences if s.encoder == "raw"]
+        if len(raw) != 1 or not raw[0].max_length:
+            raise NotImplementedError("MixFormer: one raw sequence with max_length is implemented")
+        self.config = config
+        self.seq = raw[0]
+        by_name = {f.name: f for f in config.features}
+        ns_inputs = [n for n in config.resolved.tokenization.feature_token_inputs if n in by_name]
+        self.encoder = FeatureEncoder(config, device=device, rank=rank, world=world, process_group=process_group,
+                                      vocab_sizes=vocab_sizes, input_names=ns_inputs, slice_tokens=1,
+                                      base_seed=base_seed, sequences=[self.seq])
+        N = int(m.num_ns_tokens or config.resolved.tokenization.feature_token_count)
+        Dh = int(m.token_dim)
+        self.N, self.D, self.L = N, Dh, int(self.seq.max_length)
+        plan = self.encoder.seq_plans[self.seq.name]
+        self.step = _MLP(plan.out_ld, plan.out_width, int(m.hidden_dim), N * Dh, device=device)
+        self.mixer = MixFormerHead(self.encoder.plan.out_ld, self.encoder.plan.out_width, N * Dh, N, Dh,
+                                   int(m.hidden_dim), int(m.hidden_dim), max(1, int(m.num_layers)), device=device)
+        self.ntask = len(config.task_names)
+        self.heads_mod = TaskHeads(self.ntask, N * Dh, int(m.task_head_hidden_dim or 4 * Dh), m.task_head_activation,
+                                   device=device)
+
+    def gemm_param_names(self) -> set[str]:
+        return {n for n, p in self.named_parameters() if getattr(p, "_mdl_gemm", False)}
+
+    def dense_buckets(self) -> list[list[str]]:
+        names = [n for n, _ in self.named_parameters()]
+        return [[n for n in names if n.startswith("heads_mod.")], [n for n in names if not n.startswith("heads_mod.")]]
+
+    @property
+    def store(self):
+        return self.encoder.store
+
+    def forward(self, batch, task_scale: torch.Tensor | None = None) -> dict[str, torch.Tensor]:
+        from ..ops.embedding import fused_lookup
+
+        native = batch.ids.is_cuda and self.config.runtime.kernel_backend == "native"
+        anchor = torch.zeros(0, device=batch.ids.device, requires_grad=True)
+        seq = batch.sequences[self.seq.name]
+        B, L = batch.rows, self.L
+        ids = seq["ids"].reshape(-1)
+        n = len(self.encoder.seq_fields[self.seq.name]) * B * L
+        offsets = torch.arange(n + 1, dtype=torch.int64, device=ids.device)
+        seq_in = fused_lookup(self.store, self.encoder.seq_plans[self.seq.name], ids, offsets, seq.get("dense"), B * L,
+                              anchor)
+        feat_in = fused_lookup(self.store, self.encoder.plan, batch.ids, batch.offsets, batch.dense, B, anchor)
+        tokens = self.step(seq_in, native).view(B, L, self.N * self.D)
+        lengths = seq["lengths"]
+        e = torch.arange(L, device=tokens.device)
+        valid = e.view(1, -1) >= (L - lengths.clamp(0, L)).view(-1, 1)
+        # the head's sequence projection sees the already N*D-wide event tokens
+        readout = self.mixer(feat_in, tokens, valid, native)
+        if task_scale is None:
+            task_scale = torch.full((self.ntask,), 1.0 / max(1, B), device=readout.device)
+        return self.heads_mod.forward_shared(readout, batch.labels, batch.label_mask, task_scale)
+
+
+def build_mixformer(config, **kw):
+    if config.model.name == "mixformer":
+        return MixFormerModel(config, **kw)
+    raise NotImplementedError("mdl_mixformer (MixFormer with MDL scenario routing) is not built yet")

@@ -163,7 +163,7 @@ class OneTransLayerFn(torch.autograd.Function):
         ks = kstart.to(torch.int32).contiguous()
         att = torch.empty(B, Lq, D, dtype=torch.bfloat16, device=dev)
         lse = torch.empty(B, heads, Lq, dtype=torch.float32, device=dev)
-        C.fmha_fwd(qkv, ks, att, lse, heads, Lq, True, 0.0, error_word(dev))
+        C.fmha_fwd(qkv, ks, att, lse, heads, Lq, True, 0.0, error_word(dev), 0)
         h = torch.empty(B, Lq, D, dtype=torch.bfloat16, device=dev)
         # h = X[:, Lk-Lq:] + att W_o^T + b_o
         bgemm(att, _shadow(layer.wo), h, M=Lq, N=D, K=D, G=B, lda=D, gsA=Lq * D, ldb=D, gsB=0, ldc=D, gsC=Lq * D,
@@ -215,7 +215,7 @@ class OneTransLayerFn(torch.autograd.Function):
         dqkv = torch.empty_like(qkv)
         dq_acc = torch.empty(B, Lq, D, dtype=torch.float32, device=dev)
         dsum = torch.empty(B, heads, Lq, dtype=torch.float32, device=dev)
-        C.fmha_bwd(qkv, ks, att, lse, datt, dqkv, dq_acc, dsum, heads, Lq, True, 0.0, error_word(dev))
+        C.fmha_bwd(qkv, ks, att, lse, datt, dqkv, dq_acc, dsum, heads, Lq, True, 0.0, error_word(dev), 0)
         del dq_acc, dsum, datt
         # ---- Q/K/V projections
         dxn = torch.empty_like(X)

@@ -12,6 +12,11 @@ the packed valid tokens):
 * padding is a per-sample prefix (``kstart``), which is how the reference lays
   out valid tokens (valid S tokens at the end of the S block, NS tokens always
   valid), so a query row before ``kstart`` has no visible key and outputs zero;
+* ``ktail`` (causal only): the last ``ktail`` tokens see every key and are seen
+  by every query -- LONGER's mixed visibility (``mixed_allowed_mask``
+  ``src/model.py:1110-1158``: global tokens see everything, recent queries are
+  bottom-right causal and see the globals) with the globals placed after the
+  sequence instead of before it;
 * returns ``[B, lq, D]``.
 
 CUDA: the tcgen05 flash attention in ``csrc/fmha.cu`` (forward saves the
@@ -31,7 +36,7 @@ LOG2E = 1.4426950408889634
 
 
 def suffix_attention_reference(qkv: torch.Tensor, kstart: torch.Tensor, heads: int, lq: int, causal: bool = True,
-                               scale: float | None = None) -> torch.Tensor:
+                               scale: float | None = None, ktail: int = 0) -> torch.Tensor:
     """fp32 PyTorch definition (differentiable)."""
 
     B, Lk, W = qkv.shape
@@ -48,7 +53,9 @@ def suffix_attention_reference(qkv: torch.Tensor, kstart: torch.Tensor, heads: i
     ks = kstart.to(qkv.device).long().view(B, 1, 1)
     allowed = kpos.view(1, 1, Lk) >= ks
     if causal:
-        allowed = allowed & (kpos.view(1, 1, Lk) <= qpos.view(1, lq, 1))
+        tail0 = Lk - ktail
+        allowed = allowed & ((kpos.view(1, 1, Lk) <= qpos.view(1, lq, 1)) | (kpos.view(1, 1, Lk) >= tail0)
+                             | (qpos.view(1, lq, 1) >= tail0))
     allowed = allowed & (qpos.view(1, lq, 1) >= ks)                      # padded queries output zero
     s = s.masked_fill(~allowed.unsqueeze(1), float("-inf"))
     p = torch.softmax(s, dim=-1)
@@ -59,31 +66,33 @@ def suffix_attention_reference(qkv: torch.Tensor, kstart: torch.Tensor, heads: i
 
 class SuffixAttentionFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, qkv, kstart, heads, lq, causal):
+    def forward(ctx, qkv, kstart, heads, lq, causal, ktail=0):
         B, Lk, W = qkv.shape
         D = W // 3
         qkv = qkv.contiguous()
         ks = kstart.to(torch.int32).contiguous()
         out = torch.empty(B, lq, D, dtype=torch.bfloat16, device=qkv.device)
         lse = torch.empty(B, heads, lq, dtype=torch.float32, device=qkv.device)
-        ext().fmha_fwd(qkv, ks, out, lse, heads, lq, bool(causal), 0.0, error_word(qkv.device))
+        ext().fmha_fwd(qkv, ks, out, lse, heads, lq, bool(causal), 0.0, error_word(qkv.device), int(ktail))
         ctx.save_for_backward(qkv, ks, out, lse)
-        ctx.meta = (heads, lq, bool(causal))
+        ctx.meta = (heads, lq, bool(causal), int(ktail))
         return out
 
     @staticmethod
     def backward(ctx, dout):
         qkv, ks, out, lse = ctx.saved_tensors
-        heads, lq, causal = ctx.meta
+        heads, lq, causal, ktail = ctx.meta
         dout = dout.to(torch.bfloat16).contiguous()
         dqkv = torch.empty_like(qkv)
         dq_acc = torch.empty(out.shape, dtype=torch.float32, device=qkv.device)
         dsum = torch.empty(lse.shape, dtype=torch.float32, device=qkv.device)
-        ext().fmha_bwd(qkv, ks, out, lse, dout, dqkv, dq_acc, dsum, heads, lq, causal, 0.0, error_word(qkv.device))
-        return dqkv, None, None, None, None
+        ext().fmha_bwd(qkv, ks, out, lse, dout, dqkv, dq_acc, dsum, heads, lq, causal, 0.0, error_word(qkv.device),
+                       ktail)
+        return dqkv, None, None, None, None, None
 
 
-def suffix_attention(qkv: torch.Tensor, kstart: torch.Tensor, heads: int, lq: int, causal: bool = True) -> torch.Tensor:
+def suffix_attention(qkv: torch.Tensor, kstart: torch.Tensor, heads: int, lq: int, causal: bool = True,
+                     ktail: int = 0) -> torch.Tensor:
     if qkv.is_cuda:
-        return SuffixAttentionFn.apply(qkv, kstart, heads, lq, causal)
-    return suffix_attention_reference(qkv, kstart, heads, lq, causal)
+        return SuffixAttentionFn.apply(qkv, kstart, heads, lq, causal, ktail)
+    return suffix_attention_reference(qkv, kstart, heads, lq, causal, ktail=ktail)

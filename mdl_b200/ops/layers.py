@@ -275,3 +275,97 @@ class DomainAwareAttention(nn.Module):
         k = self.key_projection(feature_tokens)
         v = self.value_projection(feature_tokens)
         return few_query_attention(q, k, v, self.num_heads)
+
+
+# ============================================================================ RMSNorm, SwiGLU
+class RMSNormFn(torch.autograd.Function):
+    """``x * rsqrt(mean(x^2) + eps) * w`` over the last dim of a contiguous bf16 tensor
+    (fp32 statistics; reference ``RMSNorm`` ``src/model.py:4550-4568``,
+    ``MixFormerRMSNorm`` ``src/modules/mixformer.py:28-53``)."""
+
+    @staticmethod
+    def forward(ctx, x, w, eps):
+        D = x.shape[-1]
+        x = x.contiguous().to(torch.bfloat16)
+        rows = x.numel() // D
+        out = torch.empty_like(x)
+        rstd = torch.empty(rows, dtype=torch.float32, device=x.device)
+        ext().rms_fwd(x, w, out, rstd, rows, D, eps)
+        ctx.save_for_backward(x, rstd)
+        ctx.w = w
+        return out
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, rstd = ctx.saved_tensors
+        D = x.shape[-1]
+        dx = torch.empty_like(x)
+        ext().rms_bwd(x, ctx.w, rstd, dy.contiguous().to(torch.bfloat16), dx, _grad(ctx.w), x.numel() // D, D)
+        return dx, None, None
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6, native: bool = False) -> torch.Tensor:
+    if native:
+        return RMSNormFn.apply(x, w, eps)
+    xf = x.float()
+    return xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w
+
+
+class SwiGLUFn(torch.autograd.Function):
+    """N independent bias-free SwiGLU networks ``W_o (W_u x * silu(W_g x))`` over
+    ``x [B, N, D]`` as grouped tcgen05 GEMMs (``w_ug [N, 2H, D]`` = up rows then gate
+    rows, ``w_o [N, D, H]``); reference ``StackedPerHeadSwiGLUFFN`` /
+    ``DenseSwiGLUFFN`` ``src/modules/mixformer.py:56-115``."""
+
+    @staticmethod
+    def forward(ctx, x, w_ug, w_o):
+        B, N, D = x.shape
+        H = w_o.shape[2]
+        dev = x.device
+        if not (x.stride(2) == 1 and x.stride(1) == D and x.stride(0) % 8 == 0 and x.data_ptr() % 16 == 0):
+            x = x.contiguous()
+        x = x.to(torch.bfloat16)
+        lda = x.stride(0)
+        ug = torch.empty(N, B, 2 * H, dtype=torch.bfloat16, device=dev)
+        bgemm(x, _shadow(w_ug), ug, M=B, N=2 * H, K=D, G=N, lda=lda, gsA=D, ldb=D, gsB=2 * H * D, ldc=2 * H,
+              gsC=B * 2 * H)
+        u, g = ug[..., :H], ug[..., H:]
+        h = (u.float() * F.silu(g.float())).to(torch.bfloat16)
+        y = torch.empty(B, N, D, dtype=torch.bfloat16, device=dev)
+        bgemm(h, _shadow(w_o), y, M=B, N=D, K=H, G=N, lda=H, gsA=B * H, ldb=H, gsB=D * H, ldc=N * D, gsC=D)
+        ctx.save_for_backward(x, ug, h)
+        ctx.params = (w_ug, w_o)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, ug, h = ctx.saved_tensors
+        w_ug, w_o = ctx.params
+        B, N, D = x.shape
+        H = w_o.shape[2]
+        dy = dy.contiguous().to(torch.bfloat16)
+        dh = torch.empty(N, B, H, dtype=torch.bfloat16, device=x.device)
+        bgemm(dy, _shadow(w_o), dh, M=B, N=H, K=D, G=N, lda=N * D, gsA=D, ldb=H, gsB=D * H, b_mn=True, ldc=H,
+              gsC=B * H)
+        bgemm(dy, h, _grad(w_o), M=D, N=H, K=B, G=N, lda=N * D, gsA=D, a_mn=True, ldb=H, gsB=B * H, b_mn=True, ldc=H,
+              gsC=D * H, accumulate=True)
+        u, g = ug[..., :H].float(), ug[..., H:].float()
+        sg = torch.sigmoid(g)
+        dhf = dh.float()
+        dug = torch.cat([dhf * g * sg, dhf * u * sg * (1.0 + g * (1.0 - sg))], dim=-1).to(torch.bfloat16)
+        bgemm(dug, x, _grad(w_ug), M=2 * H, N=D, K=B, G=N, lda=2 * H, gsA=B * 2 * H, a_mn=True, ldb=x.stride(0),
+              gsB=D, b_mn=True, ldc=D, gsC=2 * H * D, accumulate=True)
+        dx = torch.empty(B, N, D, dtype=torch.bfloat16, device=x.device)
+        bgemm(dug, _shadow(w_ug), dx, M=B, N=D, K=2 * H, G=N, lda=2 * H, gsA=B * 2 * H, ldb=D, gsB=2 * H * D,
+              b_mn=True, ldc=N * D, gsC=D)
+        return dx, None, None
+
+
+def swiglu(x: torch.Tensor, w_ug: torch.Tensor, w_o: torch.Tensor, native: bool = False) -> torch.Tensor:
+    """``x [B, N, D]`` through N SwiGLU networks (one when N == 1)."""
+
+    if native:
+        return SwiGLUFn.apply(x, w_ug, w_o)
+    H = w_o.shape[2]
+    ug = torch.einsum("bnd,nhd->bnh", x.float(), w_ug)
+    return torch.einsum("bnh,ndh->bnd", ug[..., :H] * F.silu(ug[..., H:]), w_o)

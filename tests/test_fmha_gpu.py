@@ -16,6 +16,38 @@ def _case(B, Lk, Lq, H, kstart, causal, device, seed=0):
     return qkv, ks, dout
 
 
+def test_suffix_attention_ktail_matches_longer_mask():
+    """Globals after the sequence with ktail == globals before it with the reference's
+    mixed mask (globals see all keys; recent queries are causal and see the globals)."""
+
+    torch.manual_seed(0)
+    B, L, G, R, H = 2, 30, 3, 10, 2
+    D = 32 * H
+    qkv = torch.randn(B, L + G, 3 * D)
+    ks = torch.tensor([0, 7])
+    out = suffix_attention_reference(qkv, ks, H, R + G, True, ktail=G)
+    # reference layout: [globals; sequence], queries [globals; last R], mixed mask
+    ref_qkv = torch.cat([qkv[:, L:], qkv[:, :L]], dim=1)
+    hd = 32
+    q = ref_qkv[:, :, :D].reshape(B, L + G, H, hd).transpose(1, 2)
+    k = ref_qkv[:, :, D:2 * D].reshape(B, L + G, H, hd).transpose(1, 2)
+    v = ref_qkv[:, :, 2 * D:].reshape(B, L + G, H, hd).transpose(1, 2)
+    qi = torch.cat([torch.arange(G), torch.arange(L + G - R, L + G)])
+    kpos = torch.arange(L + G)
+    key_valid = (kpos.view(1, -1) < G) | (kpos.view(1, -1) >= G + ks.view(-1, 1))
+    glob = key_valid.unsqueeze(1).expand(B, G, L + G)
+    rec = key_valid.unsqueeze(1) & (kpos.view(1, 1, -1) <= torch.arange(L + G - R, L + G).view(1, R, 1))
+    rec = rec & (torch.arange(L + G - R, L + G).view(1, R, 1) >= G + ks.view(-1, 1, 1))
+    allowed = torch.cat([glob, rec], dim=1)
+    s = (q[:, :, qi] @ k.transpose(-1, -2)) / hd ** 0.5
+    s = s.masked_fill(~allowed.unsqueeze(1), float("-inf"))
+    p = torch.nan_to_num(torch.softmax(s, -1))
+    o = (p @ v).transpose(1, 2).reshape(B, G + R, D)
+    # ours: queries [last R sequence tokens; globals]
+    torch.testing.assert_close(out[:, R:], o[:, :G], atol=1e-5, rtol=1e-4)
+    torch.testing.assert_close(out[:, :R], o[:, G:], atol=1e-5, rtol=1e-4)
+
+
 def test_suffix_attention_reference_matches_loop():
     B, Lk, Lq, H = 2, 20, 9, 2
     qkv, ks, _ = _case(B, Lk, Lq, H, [0, 6], True, "cpu")
@@ -44,20 +76,23 @@ CASES = [
     (2, 160, 96, 8, [0, 150], True),        # last layers (queries before kstart output zero)
     (2, 300, 300, 2, [5, 129], False),      # non-causal
     (1, 64, 40, 4, [0], True),              # shorter than one tile
+    (2, 300, 280, 8, [0, 120], True, 1),    # LONGER cross block: 1 trailing global token
+    (2, 433, 300, 4, [7, 200], True, 24),   # 24 trailing globals, padded prefixes
 ]
 
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("case", CASES)
 def test_fmha_forward_backward(case):
-    B, Lk, Lq, H, kstart, causal = case
+    B, Lk, Lq, H, kstart, causal = case[:6]
+    ktail = case[6] if len(case) > 6 else 0
     qkv, ks, dout = _case(B, Lk, Lq, H, kstart, causal, "cuda")
     q1 = qkv.clone().requires_grad_(True)
-    out = suffix_attention(q1, ks, H, Lq, causal)
+    out = suffix_attention(q1, ks, H, Lq, causal, ktail)
     out.backward(dout)
     torch.cuda.synchronize()
     q2 = qkv.float().clone().requires_grad_(True)
-    ref = suffix_attention_reference(q2, ks, H, Lq, causal)
+    ref = suffix_attention_reference(q2, ks, H, Lq, causal, ktail=ktail)
     ref.backward(dout.float())
     err = (out.float() - ref).abs().max().item()
     assert err < 2e-2, f"forward max error {err}"
