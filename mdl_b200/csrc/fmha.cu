@@ -44,6 +44,7 @@
 #include <algorithm>
 #include <cstdlib>
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 #include "fmha.h"
@@ -451,9 +452,16 @@ __global__ void __launch_bounds__(F_THREADS, 2)
         __syncwarp();
         if (lane == 0) mbar_arrive(s_empty);
         // padding, the diagonal tile and the tile of the trailing tokens need a per-column mask
-        const int tail0 = Lk - p.ktail;
-        const bool special = it.kst > kbase || (p.causal && (t == it.i || (p.ktail > 0 && t == 0)));
-        if (special) {
+        if (p.ktail == 0) {
+          const int lo = it.kst - kbase;                         // columns < lo are padding
+          const int hi = (p.causal && t == it.i) ? r : TILE - 1;  // columns > hi are in the future
+          if (lo > 0 || hi < TILE - 1) {
+#pragma unroll
+            for (int c = 0; c < TILE; ++c)
+              if (c < lo || c > hi) sr[c] = __float_as_uint(-CUDART_INF_F);
+          }
+        } else if (it.kst > kbase || (p.causal && (t == it.i || t == 0))) {
+          const int tail0 = Lk - p.ktail;
           const bool q_tail = qrow >= tail0;
 #pragma unroll
           for (int c = 0; c < TILE; ++c) {
@@ -825,26 +833,40 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         const float* lse = sLse + st * TILE + wg * 64;
         const float* dsv = sDs + st * TILE + wg * 64;
+        // Whole tile visible to this lane's key (every column a real query, no causal
+        // or padding cut): the common case skips the per-element visibility test.
+        const int qcol0 = qrow0 + wg * 64;
+        const bool full = key_ok && qcol0 >= it.qlo && (!p.causal || krow <= qcol0);
+        auto tile = [&](auto full_tag) {
+          constexpr bool kFull = decltype(full_tag)::value;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          float pe[8], de[8];
+          for (int c = 0; c < 8; ++c) {
+            float pe[8], de[8];
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const int qc = c * 8 + k;
-            const int qrow = qrow0 + wg * 64 + qc;
-            // qrow >= qlo also drops rows that are not queries (their Q may be any finite value)
-            const bool vis = key_ok && qrow >= it.qlo &&
-                             (!p.causal || krow <= qrow || krow >= Lk - p.ktail || qrow >= Lk - p.ktail);
-            const float pv = vis ? ex2_mix<EXPV>(fmaf(__uint_as_float(s[qc]), p.scale2, -lse[qc]), k) : 0.f;
-            pe[k] = pv;
-            de[k] = pv * (__uint_as_float(dp[qc]) - dsv[qc]) * p.scale;
+            for (int k = 0; k < 8; ++k) {
+              const int qc = c * 8 + k;
+              bool vis = true;
+              if constexpr (!kFull) {
+                const int qrow = qcol0 + qc;
+                // qrow >= qlo also drops rows that are not queries (their Q may be any finite value)
+                vis = key_ok && qrow >= it.qlo &&
+                      (!p.causal || krow <= qrow || krow >= Lk - p.ktail || qrow >= Lk - p.ktail);
+              }
+              const float pv = vis ? ex2_mix<EXPV>(fmaf(__uint_as_float(s[qc]), p.scale2, -lse[qc]), k) : 0.f;
+              pe[k] = pv;
+              de[k] = pv * (__uint_as_float(dp[qc]) - dsv[qc]) * p.scale;
+            }
+            const uint32_t off = swz_off(r, wg * 8 + c);
+            st_smem_v4(pt_base + off, packp<INT_PACK>(pe[0], pe[1]), packp<INT_PACK>(pe[2], pe[3]),
+                       packp<INT_PACK>(pe[4], pe[5]), packp<INT_PACK>(pe[6], pe[7]));
+            st_smem_v4(ds_base + off, packp<INT_PACK>(de[0], de[1]), packp<INT_PACK>(de[2], de[3]),
+                       packp<INT_PACK>(de[4], de[5]), packp<INT_PACK>(de[6], de[7]));
           }
-          const uint32_t off = swz_off(r, wg * 8 + c);
-          st_smem_v4(pt_base + off, packp<INT_PACK>(pe[0], pe[1]), packp<INT_PACK>(pe[2], pe[3]),
-                     packp<INT_PACK>(pe[4], pe[5]), packp<INT_PACK>(pe[6], pe[7]));
-          st_smem_v4(ds_base + off, packp<INT_PACK>(de[0], de[1]), packp<INT_PACK>(de[2], de[3]),
-                     packp<INT_PACK>(de[4], de[5]), packp<INT_PACK>(de[6], de[7]));
-        }
+        };
+        if (full)
+          tile(std::true_type{});
+        else
+          tile(std::false_type{});
         fence_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(pds_full);
