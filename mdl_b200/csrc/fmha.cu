@@ -42,6 +42,7 @@
 #include <math_constants.h>
 
 #include <algorithm>
+#include <climits>
 #include <cstdlib>
 #include <mutex>
 #include <type_traits>
@@ -833,40 +834,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         const float* lse = sLse + st * TILE + wg * 64;
         const float* dsv = sDs + st * TILE + wg * 64;
-        // Whole tile visible to this lane's key (every column a real query, no causal
-        // or padding cut): the common case skips the per-element visibility test.
+        // The query columns this lane's key is visible to are one range qc >= cmin:
+        // real queries (row >= qlo) that are not before the key (causal), where a
+        // trailing always-visible key or query lifts the causal cut.
         const int qcol0 = qrow0 + wg * 64;
-        const bool full = key_ok && qcol0 >= it.qlo && (!p.causal || krow <= qcol0);
-        auto tile = [&](auto full_tag) {
-          constexpr bool kFull = decltype(full_tag)::value;
+        int cmin = it.qlo - qcol0;
+        if (p.causal) {
+          const int tail0 = Lk - p.ktail;
+          const int causal_min = krow >= tail0 ? INT_MIN / 2 : min(krow, tail0) - qcol0;
+          cmin = max(cmin, causal_min);
+        }
+        if (!key_ok) cmin = INT_MAX / 2;
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            float pe[8], de[8];
+        for (int c = 0; c < 8; ++c) {
+          float pe[8], de[8];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const int qc = c * 8 + k;
-              bool vis = true;
-              if constexpr (!kFull) {
-                const int qrow = qcol0 + qc;
-                // qrow >= qlo also drops rows that are not queries (their Q may be any finite value)
-                vis = key_ok && qrow >= it.qlo &&
-                      (!p.causal || krow <= qrow || krow >= Lk - p.ktail || qrow >= Lk - p.ktail);
-              }
-              const float pv = vis ? ex2_mix<EXPV>(fmaf(__uint_as_float(s[qc]), p.scale2, -lse[qc]), k) : 0.f;
-              pe[k] = pv;
-              de[k] = pv * (__uint_as_float(dp[qc]) - dsv[qc]) * p.scale;
-            }
-            const uint32_t off = swz_off(r, wg * 8 + c);
-            st_smem_v4(pt_base + off, packp<INT_PACK>(pe[0], pe[1]), packp<INT_PACK>(pe[2], pe[3]),
-                       packp<INT_PACK>(pe[4], pe[5]), packp<INT_PACK>(pe[6], pe[7]));
-            st_smem_v4(ds_base + off, packp<INT_PACK>(de[0], de[1]), packp<INT_PACK>(de[2], de[3]),
-                       packp<INT_PACK>(de[4], de[5]), packp<INT_PACK>(de[6], de[7]));
+          for (int k = 0; k < 8; ++k) {
+            const int qc = c * 8 + k;
+            const float pv = qc >= cmin ? ex2_mix<EXPV>(fmaf(__uint_as_float(s[qc]), p.scale2, -lse[qc]), k) : 0.f;
+            pe[k] = pv;
+            de[k] = pv * (__uint_as_float(dp[qc]) - dsv[qc]) * p.scale;
           }
-        };
-        if (full)
-          tile(std::true_type{});
-        else
-          tile(std::false_type{});
+          const uint32_t off = swz_off(r, wg * 8 + c);
+          st_smem_v4(pt_base + off, packp<INT_PACK>(pe[0], pe[1]), packp<INT_PACK>(pe[2], pe[3]),
+                     packp<INT_PACK>(pe[4], pe[5]), packp<INT_PACK>(pe[6], pe[7]));
+          st_smem_v4(ds_base + off, packp<INT_PACK>(de[0], de[1]), packp<INT_PACK>(de[2], de[3]),
+                     packp<INT_PACK>(de[4], de[5]), packp<INT_PACK>(de[6], de[7]));
+        }
         fence_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(pds_full);
