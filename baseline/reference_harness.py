@@ -13,10 +13,15 @@ container / H2D helpers (``src.dataloader.FeatureBatch``, ``pin_feature_batch``,
 (``src/train.py:6996-7190``): zero_grad -> autocast forward + loss -> backward ->
 optimizer steps.
 
-The workload is BASELINE config 2 built by ``mdl_b200.data.baseline_configs`` with two
-adjustments the reference needs: bag pooling ``mean`` (it has no ``sum``; same cost) and
-its production ``runtime.cuda_graph_backbone: true``. Synthetic batches come from the
-same generator as our arm and are converted to the reference's ``FeatureBatch``.
+The workload is a BASELINE config built by ``mdl_b200.data.baseline_configs`` with the
+adjustments the reference needs: bag pooling ``mean`` (it has no ``sum``; same cost), its
+production ``runtime.cuda_graph_backbone: true`` (RankMixer), and for OneTrans (config 4)
+its only pyramid schedule, ``linear`` with ``final_s_tokens: 32`` (queried S tokens per
+layer 448, 352, 256, 192, 128, 32 against 512, 256, 256, 128, 128, 64 for halving -- 5%
+more query work; run our arm with ``--pyramid linear`` for the like-for-like pair).
+Synthetic batches come from the same generator as our arm and are converted to the
+reference's ``FeatureBatch`` (sequences as ``{"fields": {name: [B, L]}, "lengths": [B]}``
+payloads with the valid events first, as its dataloader delivers them).
 """
 
 from __future__ import annotations
@@ -54,6 +59,11 @@ def reference_mapping(mapping: dict, cuda_graphs: bool) -> dict:
     for f in m.get("features", []):
         if f.get("pooling") == "sum":
             f["pooling"] = "mean"
+    model = m.get("model", {})
+    if model.pop("pyramid_schedule", "linear") != "linear":
+        model["final_s_tokens"] = 32
+    model.pop("pyramid_halve_every", None)
+    model.pop("sequence_head", None)
     m.setdefault("vocab_strategy", {"defaults": {}, "features": {}})
     m["runtime"]["cuda_graph_backbone"] = bool(cuda_graphs)
     m["runtime"]["distributed"] = "none"
@@ -62,8 +72,12 @@ def reference_mapping(mapping: dict, cuda_graphs: bool) -> dict:
     return m
 
 
-def to_feature_batch(rdata, packed, plan, device=None):
-    """Our PackedBatch -> the reference's FeatureBatch (features dict keyed by name)."""
+def to_feature_batch(rdata, packed, plan, device=None, sequences=None):
+    """Our PackedBatch -> the reference's FeatureBatch (features dict keyed by name).
+
+    ``sequences``: ``{name: [field names]}`` of the raw sequences in the batch; ours are
+    right-aligned (padding first), the reference's payloads carry the valid events first.
+    """
 
     rows = packed.rows
     ids = packed.ids
@@ -81,6 +95,17 @@ def to_feature_batch(rdata, packed, plan, device=None):
         else:
             lengths = (off[fi * rows + 1:(fi + 1) * rows + 1] - off[fi * rows:(fi + 1) * rows]).clone()
             features[f.name] = {"values": flat.clone(), "lengths": lengths}
+    for name, field_names in (sequences or {}).items():
+        seq = packed.sequences[name]
+        lengths = seq["lengths"].long()
+        L = seq["ids"].shape[1] // rows
+        ids = seq["ids"].view(len(field_names), rows, L)
+        # left-align: event e of the valid suffix moves to position e
+        pos = (torch.arange(L).view(1, L) + (L - lengths).view(rows, 1)).clamp(max=L - 1)
+        keep = torch.arange(L).view(1, L) < lengths.view(rows, 1)
+        fields = {fn: torch.where(keep, ids[k].gather(1, pos), torch.zeros_like(ids[k])) for k, fn in
+                  enumerate(field_names)}
+        features[name] = {"fields": fields, "lengths": lengths.clone()}
     batch = rdata.FeatureBatch(features=features, labels=packed.labels.clone(), label_mask=None,
                                scenario_id=torch.zeros(rows, dtype=torch.long), group_id=[])
     if device is not None:
@@ -120,8 +145,16 @@ class ReferenceTrainer:
             self.optimizers.append(roptim.ShardedRowWiseAdagrad(
                 sharded, lr=lr, lr_decay=t.adagrad_lr_decay, weight_decay=t.adagrad_weight_decay,
                 initial_accumulator_value=t.adagrad_initial_accumulator_value, eps=t.adagrad_eps))
-        if list(groups.embedding_optimizer):
-            raise RuntimeError("benchmark workload expects sharded embeddings only")
+        replicated = list(groups.embedding_optimizer)
+        if replicated:
+            # small tables the reference replicates (src/train.py:6619-6630); their
+            # cross-rank sparse sync is not reproduced here, so one rank only
+            if world > 1:
+                raise RuntimeError("replicated embedding tables with more than one rank are not wired here")
+            self.optimizers.append(torch.optim.Adagrad(
+                replicated, lr=t.lr_sparse or t.lr_dense, lr_decay=t.adagrad_lr_decay,
+                weight_decay=t.adagrad_weight_decay,
+                initial_accumulator_value=t.adagrad_initial_accumulator_value, eps=t.adagrad_eps))
 
     def step(self, batch) -> torch.Tensor:
         rt = self.rtrain
@@ -147,7 +180,7 @@ def run(args, rank: int, world: int, local: int) -> dict:
     from mdl_b200.utils.clocks import ClockSampler
 
     device = torch.device("cuda", local)
-    mapping, spec = baseline_config(2, batch=args.batch)
+    mapping, spec = baseline_config(args.config, batch=args.batch)
     torch.manual_seed(1234)
     trainer = ReferenceTrainer(mapping, device=device, rank=rank, world=world, local=local,
                                cuda_graphs=not getattr(args, "ref_no_graphs", False))
@@ -165,8 +198,9 @@ def run(args, rank: int, world: int, local: int) -> dict:
     gen = SyntheticGenerator(plan, spec, rank=rank)
     pool = BatchPool(gen, args.batch, count=args.pool, pin=False)
     rd = trainer.rdata
-    dev_batches = [to_feature_batch(rd, b, plan, device) for b in pool.batches]
-    host_batches = [rd.pin_feature_batch(to_feature_batch(rd, b, plan)) for b in pool.batches]
+    seqs = {s["name"]: [fl["name"] for fl in s["fields"]] for s in mapping.get("sequences", [])}
+    dev_batches = [to_feature_batch(rd, b, plan, device, seqs) for b in pool.batches]
+    host_batches = [rd.pin_feature_batch(to_feature_batch(rd, b, plan, None, seqs)) for b in pool.batches]
     torch.cuda.synchronize(device)
 
     for i in range(args.warmup):
@@ -221,10 +255,13 @@ def run(args, rank: int, world: int, local: int) -> dict:
         "dtype": "bf16",
         "data": "synthetic (same generator and seeds as the ours arm); random-init weights",
         "config": {
-            "model": "rankmixer (BASELINE config 2) on the unmodified reference; bag pooling mean (no sum in the "
-                     "reference); cuda_graph_backbone=" + str(bool(trainer.config.runtime.cuda_graph_backbone)),
+            "model": f"{trainer.config.model.name} (BASELINE config {args.config}) on the unmodified reference; bag "
+                     "pooling mean (no sum in the reference); cuda_graph_backbone="
+                     + str(bool(trainer.config.runtime.cuda_graph_backbone))
+                     + (f"; pyramid linear, final_s_tokens={trainer.config.model.final_s_tokens}"
+                        if trainer.config.model.name == "onetrans" else ""),
             "global_batch": args.batch * world,
-            "seq_len": None,
+            "seq_len": (mapping.get("sequences") or [{}])[0].get("max_length"),
             "parallelism": f"ddp{world}+sharded-embeddings{world}",
             "l2": "inputs larger than L2 (same batches as the ours arm)",
         },

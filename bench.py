@@ -87,6 +87,10 @@ def run_ours(args) -> dict:
     if args.batch is None:
         args.batch = DEFAULT_BATCH[args.config]
     mapping, spec = baseline_config(args.config, batch=args.batch)
+    if args.pyramid and args.config == 4:
+        mapping["model"]["pyramid_schedule"] = args.pyramid
+        if args.pyramid == "linear":
+            mapping["model"]["final_s_tokens"] = 32
     cfg = app_config_from_mapping(mapping)
     torch.manual_seed(1234)
     pg = dist.group.WORLD if world > 1 else None
@@ -173,8 +177,11 @@ def run_ours(args) -> dict:
 def run_reference(args) -> dict:
     """The unmodified reference on the same workload (see baseline/reference_harness.py)."""
 
-    if args.config != 2:
-        return {"impl": "reference", "unavailable": f"reference arm is wired for workload 2 only (asked {args.config})"}
+    if args.config not in (2, 4):
+        return {"impl": "reference", "unavailable": f"reference arm is wired for workloads 2 and 4 (asked {args.config}); "
+                                                     "workload 3 needs MDL priors the harness does not build, workload 5 "
+                                                     "combines LONGER with a MixFormer head, which the reference has no "
+                                                     "model for"}
     if args.batch is None:
         args.batch = DEFAULT_BATCH[args.config]
     try:
@@ -197,6 +204,8 @@ def main(argv=None) -> int:
     p.add_argument("--config", type=int, default=2, choices=sorted(MODEL_DESC),
                    help="BASELINE workload (2: RankMixer headline, 3: MDL, 4: OneTrans, 5: LONGER + MixFormer)")
     p.add_argument("--pool", type=int, default=4, help="distinct pinned host batches rotated per step")
+    p.add_argument("--pyramid", choices=["halve", "linear"], default=None,
+                   help="workload 4: pyramid schedule (linear = the reference's, final_s_tokens 32)")
     p.add_argument("--ref-no-graphs", action="store_true", help="reference arm: disable its CUDA-graph backbone")
     args = p.parse_args(argv)
     if args.warmup < 3:
