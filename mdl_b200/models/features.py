@@ -78,6 +78,10 @@ class FeatureEncoder:
         self.config = config
         by_name = {f.name: f for f in config.features}
         names = list(input_names if input_names is not None else config.resolved.tokenization.feature_token_inputs)
+        seq_by_name = {s.name: s for s in config.sequences}
+        # encoded-sequence inputs (STCA summaries) occupy columns after the looked-up
+        # features; the model adds their values into those columns after the lookup
+        extra = [seq_by_name[n] for n in names if n in seq_by_name and seq_by_name[n].encoder == "stca"]
         names = [n for n in names if n in by_name]
         self.inputs = names
         domain_tokens = [list(t) for t in (domain_tokens or [])]
@@ -131,6 +135,10 @@ class FeatureEncoder:
             col += lf.width
         self.scalar = ScalarInputs(names, [f.width for f in features], col, [n for n in names if n in dense_col_of],
                                    dense_total)
+        self.extra_inputs: list[tuple[str, int, int]] = []  # (sequence, first logical column, width)
+        for seq in extra:
+            self.extra_inputs.append((seq.name, col, int(seq.stca_dim)))
+            col += int(seq.stca_dim)
         slice_k = 0
         slice_stride = 0
         if slice_tokens:
@@ -139,7 +147,7 @@ class FeatureEncoder:
             slice_stride = (slice_k + 7) // 8 * 8
         self.slice_tokens = slice_tokens
         self.plan = LookupPlan(features, out_width=col, slice_k=slice_k, slice_stride=slice_stride,
-                               dense_width=dense_total)
+                               dense_width=dense_total, zero_fill=bool(self.extra_inputs))
         # MDL domain-token inputs
         self.domain_plan = None
         self.domain_widths: list[int] = []

@@ -63,8 +63,36 @@ class RankMixerModel(nn.Module):
         self.ffn_relu = mc.ffn_activation == "relu"
         if self.D % self.T:
             raise ValueError("rankmixer requires token_dim divisible by the feature token count")
+        by_name = {f.name: f for f in config.features}
+        stca_seqs = [s for s in config.sequences if s.encoder == "stca" and s.name in res.feature_token_inputs]
+        stca_targets = [[n for n in s.target_inputs if n in by_name] for s in stca_seqs]
         self.encoder = FeatureEncoder(config, device=device, rank=rank, world=world, process_group=process_group,
-                                      vocab_sizes=vocab_sizes, slice_tokens=self.T, base_seed=base_seed)
+                                      vocab_sizes=vocab_sizes, slice_tokens=self.T, base_seed=base_seed,
+                                      sequences=stca_seqs or None,
+                                      domain_tokens=[t for t in stca_targets if t] or None)
+        self.stca = nn.ModuleDict()
+        self._stca_meta = {}
+        if stca_seqs:
+            from .longer import _MLP
+            from .stca import STCAEncoder
+
+            plan = self.encoder.plan
+            kp = self.encoder.domain_k_pad
+            ti = 0
+            for seq, tgt, (name, c0, w) in zip(stca_seqs, stca_targets, self.encoder.extra_inputs):
+                if not tgt:
+                    raise ValueError(f"STCA sequence {seq.name!r} needs target_inputs")
+                d = int(seq.stca_dim)
+                sp = self.encoder.seq_plans[seq.name]
+                heads = int(seq.stca_num_heads or mc.num_heads)
+                mod = nn.Module()
+                mod.step = _MLP(sp.out_ld, sp.out_width, d * int(seq.stca_expansion_ratio), d, device=device)
+                mod.target = _MLP(kp, kp, d * int(seq.stca_expansion_ratio), d, device=device)
+                mod.encoder = STCAEncoder(d, heads, int(seq.stca_layers), int(seq.stca_expansion_ratio), device=device)
+                self.stca[seq.name] = mod
+                cols = torch.tensor([plan.phys_col(c) for c in range(c0, c0 + w)], dtype=torch.long)
+                self._stca_meta[seq.name] = (cols, ti, int(seq.max_length or 0))
+                ti += 1
         self.K = self.encoder.slice_k
         self.Kpad = self.encoder.slice_stride
         T, D, H, K, Kp = self.T, self.D, self.H, self.K, self.Kpad
@@ -110,6 +138,7 @@ class RankMixerModel(nn.Module):
         names = {"tok_weight", "head_w1"}
         for i in range(self.L):
             names |= {f"blocks.{i}.w_in", f"blocks.{i}.w_out"}
+        names |= {n for n, p in self.stca.named_parameters(prefix="stca") if getattr(p, "_mdl_gemm", False)}
         return names
 
     def dense_buckets(self) -> list[list[str]]:
@@ -118,7 +147,7 @@ class RankMixerModel(nn.Module):
         heads = ["head_w1", "head_b1", "head_w2", "head_b2"]
         blocks = [[f"blocks.{i}.{n}" for n in ("w_in", "b_in", "w_out", "b_out", "ln1_weight", "ln1_bias",
                                                "ln2_weight", "ln2_bias")] for i in reversed(range(self.L))]
-        return [heads, *blocks, ["tok_weight", "tok_bias"]]
+        return [heads, *blocks, ["tok_weight", "tok_bias", *[n for n, _ in self.stca.named_parameters(prefix="stca")]]]
 
     @property
     def store(self):
@@ -132,9 +161,36 @@ class RankMixerModel(nn.Module):
         from ..ops.embedding import fused_lookup
 
         x0 = fused_lookup(self.store, self.encoder.plan, batch.ids, batch.offsets, batch.dense, batch.rows, anchor)
+        if len(self.stca):
+            x0 = self._add_stca(x0, batch, anchor)
         if batch.ids.is_cuda and self.config.runtime.kernel_backend == "native":
             return self._forward_cuda(x0, batch, task_scale)
         return self.forward_reference(x0, batch, task_scale)
+
+    def _add_stca(self, x0, batch, anchor):
+        """STCA summary tokens of the encoded sequences into their tokenizer columns."""
+
+        from ..ops.embedding import fused_lookup
+
+        native = batch.ids.is_cuda and self.config.runtime.kernel_backend == "native"
+        B = batch.rows
+        targets = fused_lookup(self.store, self.encoder.domain_plan, batch.ids, batch.offsets, batch.dense, B, anchor)
+        kp = self.encoder.domain_k_pad
+        for name, mod in self.stca.items():
+            cols, ti, L = self._stca_meta[name]
+            seq = batch.sequences[name]
+            ids = seq["ids"].reshape(-1)
+            nf = len(self.encoder.seq_fields[name])
+            offsets = torch.arange(nf * B * L + 1, dtype=torch.int64, device=ids.device)
+            seq_in = fused_lookup(self.store, self.encoder.seq_plans[name], ids, offsets, seq.get("dense"), B * L,
+                                  anchor)
+            hist = mod.step(seq_in, native).view(B, L, -1)
+            target = mod.target(targets[:, ti * kp:(ti + 1) * kp], native)
+            e = torch.arange(L, device=hist.device)
+            valid = e.view(1, -1) >= (L - seq["lengths"].clamp(0, L)).view(-1, 1)
+            z = mod.encoder(hist, valid, target, native)
+            x0 = x0.index_add(1, cols.to(x0.device), z.to(x0.dtype))
+        return x0
 
     def _forward_cuda(self, x0, batch, task_scale):
         from ..ops.fused import HeadsBCEFn, PerTokenLinearFn, RankMixerBlockFn

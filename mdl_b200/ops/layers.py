@@ -369,3 +369,51 @@ def swiglu(x: torch.Tensor, w_ug: torch.Tensor, w_o: torch.Tensor, native: bool 
     H = w_o.shape[2]
     ug = torch.einsum("bnd,nhd->bnh", x.float(), w_ug)
     return torch.einsum("bnh,ndh->bnd", ug[..., :H] * F.silu(ug[..., H:]), w_o)
+
+
+class LayerNormFn(torch.autograd.Function):
+    """LayerNorm over the last dim of a bf16 tensor on the CUDA kernels (fp32 statistics)."""
+
+    @staticmethod
+    def forward(ctx, x, w, b, eps):
+        D = x.shape[-1]
+        x = x.contiguous().to(torch.bfloat16)
+        rows = x.numel() // D
+        out = torch.empty_like(x)
+        mean = torch.empty(rows, dtype=torch.float32, device=x.device)
+        rstd = torch.empty_like(mean)
+        ext().ln_fwd(x, None, w, b, out, mean, rstd, rows, 1, D, False, eps)
+        ctx.save_for_backward(x, mean, rstd)
+        ctx.params = (w, b)
+        return out
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, mean, rstd = ctx.saved_tensors
+        w, b = ctx.params
+        D = x.shape[-1]
+        rows = x.numel() // D
+        C = ext()
+        grid = C.ln_bwd_grid(rows)
+        partials = torch.empty(grid, 2 * D, dtype=torch.float32, device=x.device)
+        dx = torch.empty_like(x)
+        C.ln_bwd(dy.contiguous().to(torch.bfloat16), None, 1.0, x, None, mean, rstd, w, dx, None, partials, _grad(w),
+                 _grad(b), rows, 1, D, False, grid)
+        return dx, None, None, None
+
+
+def layer_norm(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float = 1e-5,
+               native: bool = False) -> torch.Tensor:
+    if native:
+        return LayerNormFn.apply(x, w, b, eps)
+    return F.layer_norm(x.float(), (x.shape[-1],), w, b, eps)
+
+
+def linear_nb(x: torch.Tensor, w: torch.Tensor, native: bool = False) -> torch.Tensor:
+    """Bias-free ``x W^T`` over the last dim (tcgen05 GEMM on CUDA)."""
+
+    if native:
+        shape = x.shape
+        y = LinearFn.apply(x.reshape(-1, shape[-1]).to(torch.bfloat16).contiguous(), w, None)
+        return y.view(*shape[:-1], w.shape[0])
+    return x.float() @ w.t()

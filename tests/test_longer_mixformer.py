@@ -83,3 +83,44 @@ def test_cuda_step_matches_cpu_reference(make):
     ref = cpu_model.store.grad
     got = gpu_model.store.grad.cpu()
     assert ((ref - got).norm() / (ref.norm() + 1e-9)) < 0.08
+
+
+def _stca_rankmixer():
+    """A small RankMixer whose feature tokens include an STCA-encoded behaviour sequence."""
+
+    m, spec = scaled_config(2, 1e-4, num_fields=12, batch=64)
+    from mdl_b200.data.synthetic import FieldSpec, SequenceSpec
+
+    m["features"].append({"name": "target_item", "kind": "categorical", "source": "target_item", "embedding_dim": 16,
+                          "encoding": {"type": "identity", "max_id": 500}})
+    spec.fields["target_item"] = FieldSpec(vocab=500)
+    m["sequences"] = [{"name": "clicks", "max_length": 30, "encoder": "stca", "target_inputs": ["target_item"],
+                       "stca_dim": 32, "stca_layers": 2, "stca_num_heads": 2, "stca_expansion_ratio": 2,
+                       "fields": [{"name": "item", "kind": "categorical", "embedding_dim": 16,
+                                   "encoding": {"type": "identity", "max_id": 500, "share_with": "target_item",
+                                                "share_embedding": True}}]}]
+    m["tokenization"]["num_feature_tokens"] = 4
+    m["model"].update({"token_dim": 64, "hidden_dim": 128, "task_head_hidden_dim": 32})
+    m["training"].update({"lr_warmup_steps": 0, "dense_optimizer": "adam", "lr_dense": 1e-3})
+    spec.sequences = {"clicks": SequenceSpec(fields={"item": FieldSpec(vocab=500)}, max_len=30, min_len=5)}
+    return app_config_from_mapping(m), spec
+
+
+def test_stca_rankmixer_trains_on_cpu():
+    cfg, spec = _stca_rankmixer()
+    torch.manual_seed(0)
+    model = build_model(cfg, device="cpu", base_seed=1)
+    assert "clicks" in model.stca
+    tr = Trainer(cfg, model, device=torch.device("cpu"))
+    batch = SyntheticGenerator(model.encoder.batch_plan, spec).batch(64)
+    losses = [float(tr.train_step(batch).loss) for _ in range(6)]
+    assert losses[-1] < losses[0]
+    tr.forward_backward(batch)
+    name = "stca.clicks.encoder.layers.1.wk"
+    o, n = tr.dense.offsets[name], tr.dense.params[name].numel()
+    assert float(tr.dense.grad[o:o + n].abs().sum()) > 0  # the summary reaches the loss
+
+
+@pytest.mark.gpu
+def test_stca_rankmixer_cuda_matches_cpu():
+    test_cuda_step_matches_cpu_reference(_stca_rankmixer)
