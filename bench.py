@@ -43,6 +43,8 @@ MODEL_DESC = {
     5: "longer (BASELINE config 5: 100-2000 item ids padded to 2000, target-item global token, cross block to 256 "
        "recent tokens + target, 2 self blocks d=256 8 heads, MixFormer-style head over 32 NS tokens, click head)",
 }
+MDL_ONETRANS_DESC = ("mdl_onetrans (workload 4 backbone + 5 scenario tokens + global and 3 task tokens reading the "
+                     "NS tokens after every layer, click/like/finish heads)")
 DEFAULT_BATCH = {2: 2048, 3: 2048, 4: 1024, 5: 512}
 SEQ_LEN = {4: 512, 5: 2000}
 
@@ -86,7 +88,8 @@ def run_ours(args) -> dict:
     device = torch.device("cuda", local)
     if args.batch is None:
         args.batch = DEFAULT_BATCH[args.config]
-    mapping, spec = baseline_config(args.config, batch=args.batch)
+    extra = {"mdl": True} if args.mdl else {}
+    mapping, spec = baseline_config(args.config, batch=args.batch, **extra)
     if args.pyramid and args.config == 4:
         mapping["model"]["pyramid_schedule"] = args.pyramid
         if args.pyramid == "linear":
@@ -158,7 +161,7 @@ def run_ours(args) -> dict:
         "dtype": "bf16",
         "data": "synthetic (seeded Zipf(1.05) ids, N(0,1) dense, labels from a hidden model); random-init weights",
         "config": {
-            "model": MODEL_DESC[args.config],
+            "model": MODEL_DESC[args.config] if not args.mdl else MDL_ONETRANS_DESC,
             "global_batch": args.batch * world,
             "seq_len": SEQ_LEN.get(args.config),
             "parallelism": f"dp{world}+emb-rowwise/tablewise-mp{world}",
@@ -177,6 +180,9 @@ def run_ours(args) -> dict:
 def run_reference(args) -> dict:
     """The unmodified reference on the same workload (see baseline/reference_harness.py)."""
 
+    if args.mdl:
+        return {"impl": "reference", "unavailable": "reference arm is wired for workloads 2 and 4; the MDL variant of "
+                                                     "workload 4 needs MDL priors the harness does not build"}
     if args.config not in (2, 4):
         return {"impl": "reference", "unavailable": f"reference arm is wired for workloads 2 and 4 (asked {args.config}); "
                                                      "workload 3 needs MDL priors the harness does not build, workload 5 "
@@ -206,10 +212,13 @@ def main(argv=None) -> int:
     p.add_argument("--pool", type=int, default=4, help="distinct pinned host batches rotated per step")
     p.add_argument("--pyramid", choices=["halve", "linear"], default=None,
                    help="workload 4: pyramid schedule (linear = the reference's, final_s_tokens 32)")
+    p.add_argument("--mdl", action="store_true", help="workload 4: its MDL variant (mdl_onetrans)")
     p.add_argument("--ref-no-graphs", action="store_true", help="reference arm: disable its CUDA-graph backbone")
     args = p.parse_args(argv)
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
+    if args.mdl and args.config != 4:
+        raise SystemExit("--mdl applies to workload 4")
     result = run_reference(args) if args.impl == "reference" else run_ours(args)
     rank = int(os.environ.get("RANK", "0"))
     if rank == 0 and result is not None:

@@ -43,6 +43,30 @@ def config3(num_fields: int = 300, batch: int = 2048, tokens_per_scenario: int =
     m = _rankmixer_common("mdl_rankmixer", tasks, batch, "bf16", "cuda")
     feats, fields = _config2_features(num_fields)
     feats = copy.deepcopy(feats)
+    fields = dict(fields)
+    m["features"] = feats
+    scenes = _add_mdl_domains(m, feats, fields, tasks, tokens_per_scenario)
+    m["tokenization"] = {
+        "feature_tokenizer": "rankmixer",
+        "num_feature_tokens": 16,
+        "scenario_tokens": [{"name": s, "important_inputs": ["scene_id"]} for s in scenes]
+        + [{"name": "global", "important_inputs": ["scene_id"]}],
+        "task_tokens": [{"name": t, "important_inputs": [f"prior_{t}"]} for t in tasks],
+    }
+    m["model"].update({"embedding_dim": 64, "token_dim": 768, "num_layers": 2, "num_heads": 12, "hidden_dim": 3072,
+                       "task_head_hidden_dim": 1536, "ffn_activation": "gelu", "scene_feature_bias": scene_feature_bias,
+                       "mdl_feature_interaction": "residual_ffn"})
+    m["training"].update({"lr_dense": 1e-4, "lr_sparse": 0.05, "dense_optimizer": "rmsprop", "lr_warmup_steps": 1000,
+                          "rmsprop_alpha": 0.99999, "adagrad_initial_accumulator_value": 0.0})
+    spec = SyntheticSpec(fields=fields, dense_width=64, task_rates=list(tasks.values()), zipf_s=1.05, seed=0,
+                         num_scenarios=MDL_SCENES, scene_field="scene_id", scene_effect=0.5)
+    return m, spec
+
+
+def _add_mdl_domains(m: dict, feats: list[dict], fields: dict, tasks: dict, tokens_per_scenario: int) -> list[str]:
+    """Scene id (scope ``scenario``) and one prior per task (scope ``task``) as the
+    inputs of the scenario / task tokens; returns the scene names."""
+
     scenes = [f"scene{i}" for i in range(MDL_SCENES)]
     feats.append({"name": "scene_id", "kind": "categorical", "source": "scene_id", "embedding_dim": 64,
                   "embedding_scope": "scenario", "encoding": {"type": "identity", "max_id": MDL_SCENES}})
@@ -52,34 +76,26 @@ def config3(num_fields: int = 300, batch: int = 2048, tokens_per_scenario: int =
         feats.append({"name": name, "kind": "categorical", "source": name, "embedding_dim": 64,
                       "embedding_scope": "task", "encoding": {"type": "identity", "max_id": 1000}})
         fields[name] = FieldSpec(vocab=1000)
-    m["features"] = feats
     m["scenarios"] = {"names": scenes, "source": "scene_id"}
-    m["tokenization"] = {
-        "feature_tokenizer": "rankmixer",
-        "num_feature_tokens": 16,
-        "scenario_tokens": [{"name": s, "important_inputs": ["scene_id"]} for s in scenes]
-        + [{"name": "global", "important_inputs": ["scene_id"]}],
-        "task_tokens": [{"name": t, "important_inputs": [f"prior_{t}"]} for t in tasks],
-    }
-    m["model"].update({"embedding_dim": 64, "token_dim": 768, "num_layers": 2, "num_heads": 12, "hidden_dim": 3072,
-                       "task_head_hidden_dim": 1536, "ffn_activation": "gelu", "use_task_tokens": True,
-                       "use_scenario_tokens": True, "use_global_scenario_token": True,
-                       "tokens_per_scenario": tokens_per_scenario, "scene_feature_bias": scene_feature_bias,
-                       "mdl_feature_interaction": "residual_ffn", "mdl_token_state": "coupled"})
-    m["training"].update({"lr_dense": 1e-4, "lr_sparse": 0.05, "dense_optimizer": "rmsprop", "lr_warmup_steps": 1000,
-                          "rmsprop_alpha": 0.99999, "adagrad_initial_accumulator_value": 0.0})
-    spec = SyntheticSpec(fields=fields, dense_width=64, task_rates=list(tasks.values()), zipf_s=1.05, seed=0,
-                         num_scenarios=MDL_SCENES, scene_field="scene_id", scene_effect=0.5)
-    return m, spec
+    m["model"].update({"use_task_tokens": True, "use_scenario_tokens": True, "use_global_scenario_token": True,
+                       "use_task_feature_interaction": True, "use_scenario_feature_interaction": True,
+                       "tokens_per_scenario": tokens_per_scenario, "mdl_token_state": "coupled"})
+    return scenes
 
 
 def config4(num_fields: int = 300, batch: int = 1024, seq_len: int = 512, side_fields: int = 4,
             item_vocab: int = 10_000_000, side_vocab: int = 100_000, num_layers: int = 6,
-            pyramid_schedule: str = "halve") -> tuple[dict, SyntheticSpec]:
-    tasks = {"click": 0.05}
-    m = _rankmixer_common("onetrans", tasks, batch, "bf16", "cuda")
+            pyramid_schedule: str = "halve", mdl: bool = False) -> tuple[dict, SyntheticSpec]:
+    """Workload 4; ``mdl=True`` gives its MDL variant (``mdl_onetrans``): the scene id
+    and task priors of workload 3 feed 5 x 1 + 1 scenario tokens and 3 task tokens that
+    read the NS tokens after every layer, click / like / finish heads."""
+
+    tasks = dict(MDL_TASKS) if mdl else {"click": 0.05}
+    m = _rankmixer_common("mdl_onetrans" if mdl else "onetrans", tasks, batch, "bf16", "cuda")
     feats, fields = _config2_features(num_fields)
-    m["features"] = copy.deepcopy(feats)
+    feats = copy.deepcopy(feats)
+    fields = dict(fields)
+    m["features"] = feats
     seq_fields = [{"name": "item_id", "kind": "categorical", "source": "behavior_item_id", "embedding_dim": 64,
                    "encoding": {"type": "identity", "max_id": item_vocab}}]
     seq_fields += [{"name": f"side{k}", "kind": "categorical", "source": f"behavior_side{k}", "embedding_dim": 64,
@@ -101,8 +117,15 @@ def config4(num_fields: int = 300, batch: int = 1024, seq_len: int = 512, side_f
     seq = SequenceSpec(fields={"item_id": FieldSpec(vocab=item_vocab),
                                **{f"side{k}": FieldSpec(vocab=side_vocab) for k in range(side_fields)}},
                        max_len=seq_len)
+    scene_kw = {}
+    if mdl:
+        scenes = _add_mdl_domains(m, feats, fields, tasks, 1)
+        m["tokenization"]["scenario_tokens"] = ([{"name": s, "important_inputs": ["scene_id"]} for s in scenes]
+                                                + [{"name": "global", "important_inputs": ["scene_id"]}])
+        m["tokenization"]["task_tokens"] = [{"name": t, "important_inputs": [f"prior_{t}"]} for t in tasks]
+        scene_kw = dict(num_scenarios=MDL_SCENES, scene_field="scene_id", scene_effect=0.5)
     spec = SyntheticSpec(fields=fields, dense_width=64, task_rates=list(tasks.values()), zipf_s=1.05, seed=0,
-                         sequences={"behavior": seq})
+                         sequences={"behavior": seq}, **scene_kw)
     return m, spec
 
 

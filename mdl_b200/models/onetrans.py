@@ -381,7 +381,8 @@ class OneTransModel(nn.Module):
     ``intent_ordered`` sequence group."""
 
     def __init__(self, config: AppConfig, *, device: torch.device, rank: int = 0, world: int = 1, process_group=None,
-                 vocab_sizes: dict[str, int] | None = None, base_seed: int | None = None) -> None:
+                 vocab_sizes: dict[str, int] | None = None, base_seed: int | None = None,
+                 domain_tokens: list[list[str]] | None = None, task_heads: bool = True) -> None:
         super().__init__()
         m = config.model
         if m.ns_tokenizer != "auto_split":
@@ -400,10 +401,10 @@ class OneTransModel(nn.Module):
         ns_inputs = list(config.resolved.tokenization.feature_token_inputs)
         self.encoder = FeatureEncoder(config, device=device, rank=rank, world=world, process_group=process_group,
                                       vocab_sizes=vocab_sizes, input_names=ns_inputs, slice_tokens=1,
-                                      base_seed=base_seed, sequences=[self.seq])
+                                      base_seed=base_seed, sequences=[self.seq], domain_tokens=domain_tokens)
         D, Hd = int(m.token_dim), int(m.hidden_dim)
         N = int(m.num_ns_tokens or max(1, len(ns_inputs)))
-        self.token_dim, self.hidden_dim, self.num_ns, self.heads = D, Hd, N, int(m.num_heads)
+        self.token_dim, self.hidden_dim, self.num_ns, self.attn_heads = D, Hd, N, int(m.num_heads)
         self.eps = 1e-6
         seq_plan = self.encoder.seq_plans[self.seq.name]
         self.Ks, self.Ks_log = seq_plan.out_ld, seq_plan.out_width
@@ -429,8 +430,9 @@ class OneTransModel(nn.Module):
         self.layers = nn.ModuleList(OneTransLayer(D, Hd, N, device=device) for _ in range(m.num_layers))
         self.query_counts = pyramid_query_counts(config, self.L, N)
         self.ntask = len(config.task_names)
-        self.heads_mod = TaskHeads(self.ntask, N * D, int(m.task_head_hidden_dim or Hd), m.task_head_activation,
-                                   device=device)
+        if task_heads:
+            self.heads_mod = TaskHeads(self.ntask, N * D, int(m.task_head_hidden_dim or Hd),
+                                       m.task_head_activation, device=device)
 
     # ------------------------------------------------------------------ params
     def gemm_param_names(self) -> set[str]:
@@ -492,7 +494,7 @@ class OneTransModel(nn.Module):
         for i, layer in enumerate(self.layers):
             X = grad_ready(X, hooks, nl - i)
             q = self.query_counts[i]
-            X = OneTransLayerFn.apply(X, ks, layer, s_in, q, self.heads, self.eps)
+            X = OneTransLayerFn.apply(X, ks, layer, s_in, q, self.attn_heads, self.eps)
             ks = (ks - (s_in - q)).clamp(min=0)
             s_in = q
         X = grad_ready(X, hooks, 0)
@@ -500,10 +502,10 @@ class OneTransModel(nn.Module):
         readout = X[:, s_in:, :].reshape(B, self.num_ns * D)
         return self.heads_mod.forward_shared(readout, batch.labels, batch.label_mask, task_scale)
 
-    def forward_reference(self, seq_in, ns_in, kstart, batch, task_scale=None):
-        """Plain PyTorch fp32 definition (CPU path and test oracle)."""
+    def tokenize_reference(self, seq_in, ns_in, kstart, B):
+        """fp32 PyTorch tokenizer: ``[B, L + N, d]`` with positions on the valid tokens."""
 
-        B, L, D, N = batch.rows, self.L, self.token_dim, self.num_ns
+        L, D, N = self.L, self.token_dim, self.num_ns
         s = F.gelu(seq_in.float()[:, :self.Ks_log] @ self.seq_w1[:, :self.Ks_log].t() + self.seq_b1)
         s = (s @ self.seq_w2.t() + self.seq_b2).view(B, L, D)
         v = F.gelu(ns_in.float()[:, :self.Kn_log] @ self.ns_w1[:, :self.Kn_log].t() + self.ns_b1)
@@ -513,11 +515,18 @@ class OneTransModel(nn.Module):
         ks = kstart.to(X.device).long()
         valid = e.view(1, -1) >= ks.view(-1, 1)
         pid = (e.view(1, -1) - ks.view(-1, 1)).clamp(min=0)
-        X = X + self.pos[pid] * valid.unsqueeze(-1)
+        return X + self.pos[pid] * valid.unsqueeze(-1)
+
+    def forward_reference(self, seq_in, ns_in, kstart, batch, task_scale=None):
+        """Plain PyTorch fp32 definition (CPU path and test oracle)."""
+
+        B, L, D, N = batch.rows, self.L, self.token_dim, self.num_ns
+        X = self.tokenize_reference(seq_in, ns_in, kstart, B)
+        ks = kstart.to(X.device).long()
         s_in = L
         for i, layer in enumerate(self.layers):
             q = self.query_counts[i]
-            X = layer.forward_reference(X, ks, s_in, q, self.heads, self.eps)
+            X = layer.forward_reference(X, ks, s_in, q, self.attn_heads, self.eps)
             ks = (ks - (s_in - q)).clamp(min=0)
             s_in = q
         readout = X[:, s_in:, :].reshape(B, N * D)
@@ -547,4 +556,6 @@ class OneTransModel(nn.Module):
 def build_onetrans(config: AppConfig, **kw):
     if config.model.name == "onetrans":
         return OneTransModel(config, **kw)
-    raise NotImplementedError("mdl_onetrans (OneTrans backbone with MDL domain blocks) is not built yet")
+    from .mdl_onetrans import MDLOneTransModel
+
+    return MDLOneTransModel(config, **kw)

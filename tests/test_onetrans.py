@@ -82,3 +82,96 @@ def test_onetrans_cuda_step_matches_cpu_reference(variant):
     ref = cpu_model.store.grad
     got = gpu_model.store.grad.cpu()
     assert ((ref - got).norm() / (ref.norm() + 1e-9)) < 0.06
+
+
+# ----------------------------------------------------------------------------- MDL on OneTrans
+def _small_mdl(first_seq=None, **model):
+    m, spec = scaled_config(4, 1e-4, num_fields=12, batch=64, seq_len=40, num_layers=3, mdl=True)
+    m["model"].update({"hidden_dim": 128, "token_dim": 64, "num_heads": 2, "num_ns_tokens": 4,
+                       "task_head_hidden_dim": 64, "pyramid_round_to": 8, "first_domain_sequence_layer": first_seq})
+    m["model"].update(model)
+    m["training"].update({"lr_warmup_steps": 0, "dense_optimizer": "adam", "lr_dense": 1e-3})
+    spec.sequences["behavior"].min_len = 10
+    return app_config_from_mapping(m), spec
+
+
+@pytest.mark.parametrize("variant", [
+    dict(),
+    dict(first_seq=1),
+    dict(mdl_token_state="split"),
+    dict(scene_feature_bias="film"),
+    dict(use_task_tokens=False),
+    dict(use_scenario_tokens=False),
+    dict(use_task_feature_interaction=False, use_scenario_feature_interaction=False),
+])
+def test_mdl_onetrans_cpu_trains(variant):
+    cfg, spec = _small_mdl(**variant)
+    torch.manual_seed(0)
+    model = build_model(cfg, device="cpu", base_seed=1)
+    assert type(model).__name__ == "MDLOneTransModel"
+    tr = Trainer(cfg, model, device=torch.device("cpu"))
+    batch = SyntheticGenerator(model.encoder.batch_plan, spec).batch(64)
+    out = tr.forward_backward(batch)
+    assert out["logits"].shape == (64, 3)
+    losses = [float(tr.train_step(batch).loss) for _ in range(8)]
+    assert losses[-1] < losses[0]
+
+
+def test_mdl_onetrans_block_layout():
+    cfg, _ = _small_mdl(first_seq=2)
+    model = build_model(cfg, device="cpu", base_seed=1)
+    assert model.Ns == 6 and model.Nt == 3
+    assert [b.scenario_sequence_attention is not None for b in model.blocks] == [False, False, True]
+    assert model.blocks[0].task_attention.key_projection.num_tokens == model.num_ns
+    # the fixed-width NS readers are not built where the sequence reader replaces them
+    assert model.blocks[2].scenario_attention is None
+    buckets = model.dense_buckets()
+    assert any(n.startswith("blocks.2.") for n in buckets[1]) and any(n.startswith("layers.2.") for n in buckets[1])
+    assert sorted(n for g in buckets for n in g) == sorted(n for n, _ in model.named_parameters())
+
+
+def test_sequence_domain_attention_masks_padding():
+    """Keys before ``kstart`` do not change the output (reference
+    ``VariableLengthDomainAttention`` masks padded sequence positions)."""
+
+    from mdl_b200.models.mdl import SequenceDomainAttention
+
+    torch.manual_seed(0)
+    att = SequenceDomainAttention(32, 4)
+    q = torch.randn(3, 5, 32)
+    mem = torch.randn(3, 9, 32)
+    ks = torch.tensor([0, 3, 8])
+    out = att(q, mem, ks)
+    mem2 = mem.clone()
+    mem2[1, :3] = 100.0
+    mem2[2, :8] = -7.0
+    torch.testing.assert_close(att(q, mem2, ks), out)
+    ref = att(q[2:], mem[2:, 8:], torch.zeros(1, dtype=torch.long))
+    torch.testing.assert_close(out[2:], ref)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("variant", [dict(), dict(first_seq=1, scene_feature_bias="film")])
+def test_mdl_onetrans_cuda_step_matches_cpu_reference(variant):
+    cfg, spec = _small_mdl(**variant)
+    torch.manual_seed(0)
+    cpu_model = build_model(cfg, device="cpu", base_seed=1)
+    gpu_model = build_model(cfg, device="cuda", base_seed=1)
+    gpu_model.load_state_dict({k: v.cuda() for k, v in cpu_model.state_dict().items()})
+    gpu_model.store.slab.copy_(cpu_model.store.slab)
+    cpu_tr = Trainer(cfg, cpu_model, device=torch.device("cpu"))
+    gpu_tr = Trainer(cfg, gpu_model, device=torch.device("cuda"))
+    batch = SyntheticGenerator(cpu_model.encoder.batch_plan, spec).batch(64)
+    out_c = cpu_tr.forward_backward(batch)
+    out_g = gpu_tr.forward_backward(batch.to("cuda"))
+    torch.cuda.synchronize()
+    check_error_word(0)
+    torch.testing.assert_close(out_g["logits"].cpu(), out_c["logits"].detach(), atol=6e-2, rtol=6e-2)
+    gc, gg = cpu_tr.dense.grad, gpu_tr.dense.grad.cpu()
+    scale = gc.norm().item()
+    for name in cpu_tr.dense.names:
+        o = cpu_tr.dense.offsets[name]
+        n = cpu_tr.dense.params[name].numel()
+        ref, got = gc[o:o + n], gg[o:o + n]
+        err = (ref - got).norm().item()
+        assert err <= 0.1 * ref.norm().item() + 2e-3 * scale, (name, err, ref.norm().item())
