@@ -55,20 +55,34 @@ class SwiGLUStack(nn.Module):
         return swiglu(x, self.w_ug, self.w_o, native)
 
 
-def head_mixing(x: torch.Tensor) -> torch.Tensor:
-    """``[B, N, D] -> [B, N, N, D/N] -> transpose(1, 2) -> [B, N, D]``."""
+def head_mixing(x: torch.Tensor, user_heads: int | None = None) -> torch.Tensor:
+    """``[B, N, D] -> [B, N, N, D/N] -> transpose(1, 2) -> [B, N, D]``.
+
+    With ``user_heads = u`` (UI-MixFormer decoupling, reference
+    ``MixFormerHeadMixing`` ``src/modules/mixformer.py:118-174``) the first ``u``
+    output heads keep only the chunks that came from the first ``u`` input heads
+    (columns ``[0, u * D/N)``); item heads keep everything."""
 
     B, N, D = x.shape
-    return x.reshape(B, N, N, D // N).transpose(1, 2).reshape(B, N, D)
+    y = x.reshape(B, N, N, D // N).transpose(1, 2).reshape(B, N, D)
+    if user_heads is None:
+        return y
+    keep = torch.ones(N, D, dtype=y.dtype, device=y.device)
+    keep[:user_heads, user_heads * (D // N):] = 0
+    return y * keep
 
 
 class MixFormerBlock(nn.Module):
-    def __init__(self, num_heads: int, dim: int, hidden: int, seq_hidden: int, device=None) -> None:
+    def __init__(self, num_heads: int, dim: int, hidden: int, seq_hidden: int, device=None,
+                 user_heads: int | None = None) -> None:
         super().__init__()
         if dim % num_heads:
             raise ValueError("MixFormer head width must be divisible by the head count")
+        if user_heads is not None and not 0 < user_heads < num_heads:
+            raise ValueError("mixformer_user_head_count must be inside (0, heads)")
         N, D = num_heads, dim
         self.N, self.D = N, D
+        self.user_heads = user_heads
         self.qm_norm = nn.Parameter(torch.ones(D, device=device))
         self.qm_ffn_norm = nn.Parameter(torch.ones(D, device=device))
         self.qm_ffn = SwiGLUStack(N, D, hidden, device=device)
@@ -91,13 +105,23 @@ class MixFormerBlock(nn.Module):
         h = flat + self.seq_ffn(rms_norm(flat, self.seq_norm, native=native), native)
         return h.view(B, L, self.N, self.D)
 
+    def query_mix(self, x: torch.Tensor, native: bool) -> torch.Tensor:
+        """Query Mixer: ``x + HeadMixing(RMSNorm(x))``, then ``+ SwiGLU_n(RMSNorm(.))``."""
+
+        x = x + head_mixing(rms_norm(x, self.qm_norm, native=native), self.user_heads)
+        return x + self.qm_ffn(rms_norm(x, self.qm_ffn_norm, native=native), native)
+
+    def output_fusion(self, x: torch.Tensor, native: bool) -> torch.Tensor:
+        return x + self.of_ffn(rms_norm(x, self.of_norm, native=native), native)
+
     def forward(self, x: torch.Tensor, seq: torch.Tensor, valid: torch.Tensor, native: bool) -> torch.Tensor:
         """``x [B, N, D]`` heads, ``seq [B, L, N*D]``, ``valid [B, L]`` -> ``[B, N, D]``."""
 
-        # Query Mixer
-        x = x + head_mixing(rms_norm(x, self.qm_norm, native=native))
-        x = x + self.qm_ffn(rms_norm(x, self.qm_ffn_norm, native=native), native)
-        # Cross Attention (reordered single-query form)
+        return self.output_fusion(self.cross_attention(self.query_mix(x, native), seq, valid, native), native)
+
+    def cross_attention(self, x: torch.Tensor, seq: torch.Tensor, valid: torch.Tensor, native: bool) -> torch.Tensor:
+        """Reordered single-query cross attention of each head over the history."""
+
         hist = self.history(seq, native)
         qn = rms_norm(x, self.q_norm, native=native).float()
         sq = torch.einsum("bno,noi->bni", qn, self.key_weight)                 # q' = q W_k
@@ -106,9 +130,7 @@ class MixFormerBlock(nn.Module):
         scores = scores.masked_fill(~mask, float("-inf"))
         w = torch.nan_to_num(torch.softmax(scores, dim=-1)) * mask
         ctx = torch.einsum("bnl,blni->bni", w, hist.float())
-        x = x + torch.einsum("bni,noi->bno", ctx, self.value_weight).to(x.dtype)
-        # Output Fusion
-        return x + self.of_ffn(rms_norm(x, self.of_norm, native=native), native)
+        return x + torch.einsum("bni,noi->bno", ctx, self.value_weight).to(x.dtype)
 
     def reference_state_dict(self, prefix: str) -> dict[str, torch.Tensor]:
         H = self.qm_ffn.hidden
@@ -138,7 +160,7 @@ class MixFormerHead(nn.Module):
     the heads are flattened for the task heads."""
 
     def __init__(self, k_in: int, k_log: int, seq_width: int, num_heads: int, dim: int, hidden: int, seq_hidden: int,
-                 layers: int, device=None) -> None:
+                 layers: int, device=None, user_heads: int | None = None) -> None:
         super().__init__()
         from .longer import _MLP  # deferred: longer imports this module
 
@@ -146,11 +168,13 @@ class MixFormerHead(nn.Module):
         self.feature_mlp = _MLP(k_in, k_log, hidden, num_heads * dim, device=device)
         self.seq_proj = gemm_param(torch.empty(num_heads * dim, seq_width, device=device))
         nn.init.kaiming_uniform_(self.seq_proj.data, a=math.sqrt(5))
-        self.blocks = nn.ModuleList(MixFormerBlock(num_heads, dim, hidden, seq_hidden, device=device)
-                                    for _ in range(layers))
+        self.blocks = nn.ModuleList(MixFormerBlock(num_heads, dim, hidden, seq_hidden, device=device,
+                                                   user_heads=user_heads) for _ in range(layers))
         self.output_dim = num_heads * dim
 
-    def forward(self, feat_in: torch.Tensor, seq: torch.Tensor, valid: torch.Tensor, native: bool) -> torch.Tensor:
+    def inputs(self, feat_in: torch.Tensor, seq: torch.Tensor, native: bool):
+        """Feature heads ``[B, N, D]`` and the projected sequence ``[B, L, N * D]``."""
+
         B, L, W = seq.shape
         x = self.feature_mlp(feat_in, native).view(B, self.N, self.D)
         if native:
@@ -159,9 +183,13 @@ class MixFormerHead(nn.Module):
             s = LinearFn.apply(seq.reshape(B * L, W).to(torch.bfloat16), self.seq_proj, None).view(B, L, -1)
         else:
             s = (seq.float().reshape(B * L, W) @ self.seq_proj.t()).view(B, L, self.N * self.D)
+        return x, s
+
+    def forward(self, feat_in: torch.Tensor, seq: torch.Tensor, valid: torch.Tensor, native: bool) -> torch.Tensor:
+        x, s = self.inputs(feat_in, seq, native)
         for blk in self.blocks:
             x = blk(x, s, valid, native)
-        return x.reshape(B, self.N * self.D)
+        return x.reshape(x.shape[0], self.N * self.D)
 
 
 class MixFormerModel(nn.Module):
@@ -172,7 +200,8 @@ class MixFormerModel(nn.Module):
     task heads (reference ``MixFormerModel`` ``src/model.py:8473-8578``)."""
 
     def __init__(self, config, *, device: torch.device, rank: int = 0, world: int = 1, process_group=None,
-                 vocab_sizes: dict[str, int] | None = None, base_seed: int | None = None) -> None:
+                 vocab_sizes: dict[str, int] | None = None, base_seed: int | None = None,
+                 domain_tokens: list[list[str]] | None = None, task_heads: bool = True) -> None:
         super().__init__()
         from .features import FeatureEncoder
         from .heads import TaskHeads
@@ -188,17 +217,19 @@ class MixFormerModel(nn.Module):
         ns_inputs = [n for n in config.resolved.tokenization.feature_token_inputs if n in by_name]
         self.encoder = FeatureEncoder(config, device=device, rank=rank, world=world, process_group=process_group,
                                       vocab_sizes=vocab_sizes, input_names=ns_inputs, slice_tokens=1,
-                                      base_seed=base_seed, sequences=[self.seq])
+                                      base_seed=base_seed, sequences=[self.seq], domain_tokens=domain_tokens)
         N = int(m.num_ns_tokens or config.resolved.tokenization.feature_token_count)
         Dh = int(m.token_dim)
         self.N, self.D, self.L = N, Dh, int(self.seq.max_length)
         plan = self.encoder.seq_plans[self.seq.name]
         self.step = _MLP(plan.out_ld, plan.out_width, int(m.hidden_dim), N * Dh, device=device)
         self.mixer = MixFormerHead(self.encoder.plan.out_ld, self.encoder.plan.out_width, N * Dh, N, Dh,
-                                   int(m.hidden_dim), int(m.hidden_dim), max(1, int(m.num_layers)), device=device)
+                                   int(m.hidden_dim), int(m.hidden_dim), max(1, int(m.num_layers)), device=device,
+                                   user_heads=m.mixformer_user_head_count)
         self.ntask = len(config.task_names)
-        self.heads_mod = TaskHeads(self.ntask, N * Dh, int(m.task_head_hidden_dim or 4 * Dh), m.task_head_activation,
-                                   device=device)
+        if task_heads:
+            self.heads_mod = TaskHeads(self.ntask, N * Dh, int(m.task_head_hidden_dim or 4 * Dh),
+                                       m.task_head_activation, device=device)
 
     def gemm_param_names(self) -> set[str]:
         return {n for n, p in self.named_parameters() if getattr(p, "_mdl_gemm", False)}
@@ -211,11 +242,11 @@ class MixFormerModel(nn.Module):
     def store(self):
         return self.encoder.store
 
-    def forward(self, batch, task_scale: torch.Tensor | None = None) -> dict[str, torch.Tensor]:
+    def _inputs(self, batch, anchor, native: bool):
+        """Scalar inputs ``[B, K]``, event tokens ``[B, L, N * D]`` and their validity ``[B, L]``."""
+
         from ..ops.embedding import fused_lookup
 
-        native = batch.ids.is_cuda and self.config.runtime.kernel_backend == "native"
-        anchor = torch.zeros(0, device=batch.ids.device, requires_grad=True)
         seq = batch.sequences[self.seq.name]
         B, L = batch.rows, self.L
         ids = seq["ids"].reshape(-1)
@@ -228,6 +259,13 @@ class MixFormerModel(nn.Module):
         lengths = seq["lengths"]
         e = torch.arange(L, device=tokens.device)
         valid = e.view(1, -1) >= (L - lengths.clamp(0, L)).view(-1, 1)
+        return feat_in, tokens, valid
+
+    def forward(self, batch, task_scale: torch.Tensor | None = None) -> dict[str, torch.Tensor]:
+        native = batch.ids.is_cuda and self.config.runtime.kernel_backend == "native"
+        anchor = torch.zeros(0, device=batch.ids.device, requires_grad=True)
+        B = batch.rows
+        feat_in, tokens, valid = self._inputs(batch, anchor, native)
         # the head's sequence projection sees the already N*D-wide event tokens
         readout = self.mixer(feat_in, tokens, valid, native)
         if task_scale is None:
@@ -235,7 +273,35 @@ class MixFormerModel(nn.Module):
         return self.heads_mod.forward_shared(readout, batch.labels, batch.label_mask, task_scale)
 
 
+class ScenarioQueryRouter(nn.Module):
+    """Routes the active scene's state into the MixFormer query heads (reference
+    ``ScenarioConditionedQueryRouter`` ``src/model.py:8581-8619``):
+    ``q + sigmoid(W_g c + b_g)[:, :, None] * (W_d c)[:, None]`` with ``c = RMSNorm(ctx)``;
+    ``W_d`` starts at zero (the router starts as the identity) and ``b_g`` at -2."""
+
+    def __init__(self, num_heads: int, dim: int, device=None) -> None:
+        super().__init__()
+        from ..ops.layers import Linear
+
+        self.context_norm = nn.Parameter(torch.ones(dim, device=device))
+        self.head_gate = Linear(dim, num_heads, device=device)
+        self.context_delta = Linear(dim, dim, bias=False, device=device)
+        nn.init.kaiming_uniform_(self.head_gate.weight, a=math.sqrt(5))
+        nn.init.constant_(self.head_gate.bias, -2.0)
+        nn.init.zeros_(self.context_delta.weight)
+
+    def forward(self, queries: torch.Tensor, context: torch.Tensor, native: bool) -> torch.Tensor:
+        c = rms_norm(context.unsqueeze(1), self.context_norm, native=native).squeeze(1)
+        if not native:
+            c = c.float()
+        gates = torch.sigmoid(self.head_gate(c).float()).unsqueeze(-1)
+        delta = self.context_delta(c.contiguous()).float().unsqueeze(1)
+        return (queries.float() + gates * delta).to(queries.dtype)
+
+
 def build_mixformer(config, **kw):
     if config.model.name == "mixformer":
         return MixFormerModel(config, **kw)
-    raise NotImplementedError("mdl_mixformer (MixFormer with MDL scenario routing) is not built yet")
+    from .mdl_mixformer import MDLMixFormerModel
+
+    return MDLMixFormerModel(config, **kw)

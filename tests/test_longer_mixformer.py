@@ -30,6 +30,50 @@ def _mixformer():
     return app_config_from_mapping(m), spec
 
 
+def _mdl_mixformer(**model):
+    m, spec = scaled_config(4, 1e-4, num_fields=12, batch=64, seq_len=40, num_layers=2, mdl=True)
+    m["model"].update({"name": "mdl_mixformer", "token_dim": 32, "hidden_dim": 64, "num_ns_tokens": 4,
+                       "num_heads": 2, "task_head_hidden_dim": 32})
+    m["model"].update(model)
+    m["training"].update({"lr_warmup_steps": 0, "dense_optimizer": "adam", "lr_dense": 1e-3})
+    spec.sequences["behavior"].min_len = 10
+    return app_config_from_mapping(m), spec
+
+
+def test_head_mixing_user_heads_decoupling():
+    """User heads keep only the chunks of user heads (UI-MixFormer mask)."""
+
+    x = torch.randn(2, 4, 8)
+    y = head_mixing(x, user_heads=1)
+    full = head_mixing(x)
+    assert torch.equal(y[:, 1:], full[:, 1:])
+    assert torch.equal(y[:, 0, :2], full[:, 0, :2]) and not y[:, 0, 2:].any()
+
+
+@pytest.mark.parametrize("variant", [dict(), dict(mdl_token_state="split"),
+                                     dict(mdl_mixformer_query_conditioning=False, scene_feature_bias="additive"),
+                                     dict(mixformer_user_head_count=1, use_task_tokens=False)])
+def test_mdl_mixformer_trains_on_cpu(variant):
+    cfg, spec = _mdl_mixformer(**variant)
+    torch.manual_seed(0)
+    model = build_model(cfg, device="cpu", base_seed=1)
+    assert type(model).__name__ == "MDLMixFormerModel"
+    assert (model.blocks[0].query_router is not None) == cfg.model.mdl_mixformer_query_conditioning
+    tr = Trainer(cfg, model, device=torch.device("cpu"))
+    batch = SyntheticGenerator(model.encoder.batch_plan, spec).batch(64)
+    assert tr.forward_backward(batch)["logits"].shape == (64, 3)
+    losses = [float(tr.train_step(batch).loss) for _ in range(8)]
+    assert losses[-1] < losses[0]
+
+
+def test_query_router_starts_as_identity():
+    from mdl_b200.models.mixformer import ScenarioQueryRouter
+
+    r = ScenarioQueryRouter(4, 16)
+    q = torch.randn(3, 4, 16)
+    torch.testing.assert_close(r(q, torch.randn(3, 16), native=False), q)
+
+
 def test_head_mixing_is_the_chunk_transpose():
     x = torch.arange(2 * 4 * 8, dtype=torch.float32).view(2, 4, 8)
     y = head_mixing(x)
@@ -51,7 +95,7 @@ def test_trains_on_cpu(make):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("make", [lambda: _longer("none"), lambda: _longer("none", seq_len=300, min_len=50, R=130),
-                                  lambda: _longer("mixformer"), _mixformer])
+                                  lambda: _longer("mixformer"), _mixformer, _mdl_mixformer])
 def test_cuda_step_matches_cpu_reference(make):
     cfg, spec = make()
     torch.manual_seed(0)
