@@ -46,6 +46,7 @@ class ResolvedTokenization:
     scenario_token_specs: tuple[ResolvedDomainToken, ...]
     task_token_specs: tuple[ResolvedDomainToken, ...]
     sequence_names: tuple[str, ...]
+    ns_token_groups: tuple[ResolvedTokenGroup, ...] = ()
 
 
 @dataclass(frozen=True)
@@ -118,6 +119,18 @@ def resolve_tokenization(config: AppConfig) -> ResolvedTokenization:
     else:
         count = int(tok.num_feature_tokens or len(inputs))
     seq_groups = tuple(ResolvedTokenGroup(g.name, tuple(g.inputs)) for g in tok.sequence_tokens)
+    # OneTrans groupwise NS tokens (reference ``_scalar_token_groups`` src/config.py:4083-4106):
+    # tokenization.ns_tokens, else the all-scalar feature_tokens groups, else one per feature
+    seq_names = {s.name for s in config.sequences}
+    feat_names = {f.name for f in config.features}
+    if tok.ns_tokens:
+        ns_groups = tuple(ResolvedTokenGroup(g.name, tuple(g.inputs)) for g in tok.ns_tokens)
+    elif tok.feature_tokens:
+        ns_groups = tuple(ResolvedTokenGroup(g.name, tuple(g.inputs)) for g in tok.feature_tokens
+                          if all(n in feat_names and n not in seq_names for n in g.inputs))
+    else:
+        ns_groups = tuple(ResolvedTokenGroup(f.name, (f.name,)) for f in config.features
+                          if f.embedding_scope in ("feature", "shared"))
 
     scenario_specs: list[ResolvedDomainToken] = []
     by_name = {t.name: t for t in tok.scenario_tokens}
@@ -170,6 +183,7 @@ def resolve_tokenization(config: AppConfig) -> ResolvedTokenization:
         scenario_token_specs=tuple(scenario_specs),
         task_token_specs=task_specs,
         sequence_names=tuple(s.name for s in config.sequences),
+        ns_token_groups=ns_groups,
     )
 
 

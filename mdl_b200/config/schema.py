@@ -470,7 +470,7 @@ class ModelConfig:
     sparse_moe_regularization_initial: float = 1.0e-8
     sparse_moe_regularization_multiplier: float = 1.2
     sparse_moe_loss_weight: float = 1.0
-    sparse_moe_dtsi_training_output: Literal["dense", "sparse"] | None = None
+    sparse_moe_dtsi_training_output: Literal["dense_router", "mean"] | None = None
     experimental_model_acknowledged: bool = False
 
 

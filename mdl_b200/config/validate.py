@@ -58,6 +58,24 @@ def validate_app_config(config: AppConfig) -> None:
         _require(model.token_dim % model.num_heads == 0, "token_dim must be divisible by num_heads")
     if model.name.startswith("mdl_"):
         _require(model.tokens_per_scenario >= 1, "tokens_per_scenario must be >= 1")
+    if model.name in ("mdl_onetrans", "mdl_mixformer"):
+        # experimental compositions (reference ``ModelConfig`` validation, src/config.py:2826-2833)
+        _require(model.experimental_model_acknowledged,
+                 f"{model.name} is an experimental composition: set model.experimental_model_acknowledged: true")
+    if model.first_domain_sequence_layer is not None:
+        _require(0 <= model.first_domain_sequence_layer < model.num_layers,
+                 "model.first_domain_sequence_layer must be in [0, model.num_layers)")
+    if model.rankmixer_ffn_type == "sparse_moe":
+        _require(model.sparse_moe_num_experts > 0, "model.sparse_moe_num_experts must be positive")
+        _require(0.0 < model.sparse_moe_target_active_ratio <= 1.0,
+                 "model.sparse_moe_target_active_ratio must be in (0, 1]")
+        _require(model.sparse_moe_regularization_initial > 0.0,
+                 "model.sparse_moe_regularization_initial must be positive")
+        _require(model.sparse_moe_regularization_multiplier > 1.0,
+                 "model.sparse_moe_regularization_multiplier must be greater than 1")
+        _require(model.sparse_moe_loss_weight >= 0.0, "model.sparse_moe_loss_weight must be non-negative")
+        _require(not model.sparse_moe_use_dtsi or model.sparse_moe_dtsi_training_output is not None,
+                 "DTSI needs model.sparse_moe_dtsi_training_output (dense_router or mean)")
     train = config.training
     _require(train.batch_size > 0, "training.batch_size must be positive")
     _require(train.gradient_accumulation_steps >= 1, "gradient_accumulation_steps must be >= 1")

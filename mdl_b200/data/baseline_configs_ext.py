@@ -123,6 +123,7 @@ def config4(num_fields: int = 300, batch: int = 1024, seq_len: int = 512, side_f
         m["tokenization"]["scenario_tokens"] = ([{"name": s, "important_inputs": ["scene_id"]} for s in scenes]
                                                 + [{"name": "global", "important_inputs": ["scene_id"]}])
         m["tokenization"]["task_tokens"] = [{"name": t, "important_inputs": [f"prior_{t}"]} for t in tasks]
+        m["model"]["experimental_model_acknowledged"] = True
         scene_kw = dict(num_scenarios=MDL_SCENES, scene_field="scene_id", scene_effect=0.5)
     spec = SyntheticSpec(fields=fields, dense_width=64, task_rates=list(tasks.values()), zipf_s=1.05, seed=0,
                          sequences={"behavior": seq}, **scene_kw)

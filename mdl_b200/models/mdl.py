@@ -181,7 +181,8 @@ class MDLDomainMixin:
         """Domain-token projectors (reference ``DomainTokenProjector``: ``Linear -> act ->
         Linear -> ReLU``) and the split-mode readout seeds."""
 
-        widths = self.encoder.domain_widths
+        off = getattr(self, "_dom_offset", 0)  # leading per-token inputs that are not domain tokens
+        widths = self.encoder.domain_widths[off:]
         Kd = self.encoder.domain_k_pad
         self.Kd = Kd
         self.scenario_projector = None
@@ -273,9 +274,10 @@ class MDLDomainMixin:
 
         enc = self.encoder
         s_prompt = t_prompt = None
-        if enc.domain_plan is not None:
+        if self.Ns + self.Nt:
             d0 = fused_lookup(self.store, enc.domain_plan, batch.ids, batch.offsets, batch.dense, B, anchor)
-            dom = d0.view(B, self.Ns + self.Nt, self.Kd)
+            off = getattr(self, "_dom_offset", 0)
+            dom = d0.view(B, -1, self.Kd)[:, off:off + self.Ns + self.Nt]
             if not cuda:
                 dom = dom.float()
             if self.Ns:
@@ -371,8 +373,7 @@ class MDLRankMixerModel(MDLDomainMixin, nn.Module):
         T, D, H = self.T, self.D, self.H
         if D % T:
             raise ValueError("mdl_rankmixer requires token_dim divisible by the feature token count")
-        if mc.rankmixer_ffn_type != "dense":
-            raise NotImplementedError("mdl_rankmixer implements the dense per-token FFN")
+        self.moe = mc.rankmixer_ffn_type == "sparse_moe"
         dom_inputs = self._domain_specs(config)
         self.encoder = FeatureEncoder(config, device=dev, rank=rank, world=world, process_group=process_group,
                                       vocab_sizes=vocab_sizes, slice_tokens=T, base_seed=base_seed,
@@ -394,15 +395,20 @@ class MDLRankMixerModel(MDLDomainMixin, nn.Module):
         blk = nn.Module()
         blk.ln1_weight = nn.Parameter(torch.ones(D, device=dev))
         blk.ln1_bias = nn.Parameter(torch.zeros(D, device=dev))
-        blk.w_in = gemm_param(torch.empty(T, H, D, device=dev))
-        blk.b_in = nn.Parameter(torch.empty(T, H, device=dev))
-        blk.w_out = gemm_param(torch.empty(T, D, H, device=dev))
-        blk.b_out = nn.Parameter(torch.empty(T, D, device=dev))
-        for t in range(T):
-            _kaiming_uniform_(blk.w_in.data[t], D)
-            _kaiming_uniform_(blk.b_in.data[t], D)
-            _kaiming_uniform_(blk.w_out.data[t], H)
-            _kaiming_uniform_(blk.b_out.data[t], H)
+        if self.moe:
+            from ..ops.moe import build_rankmixer_moe
+
+            blk.ffn = build_rankmixer_moe(self.config, T, device=dev)
+        else:
+            blk.w_in = gemm_param(torch.empty(T, H, D, device=dev))
+            blk.b_in = nn.Parameter(torch.empty(T, H, device=dev))
+            blk.w_out = gemm_param(torch.empty(T, D, H, device=dev))
+            blk.b_out = nn.Parameter(torch.empty(T, D, device=dev))
+            for t in range(T):
+                _kaiming_uniform_(blk.w_in.data[t], D)
+                _kaiming_uniform_(blk.b_in.data[t], D)
+                _kaiming_uniform_(blk.w_out.data[t], H)
+                _kaiming_uniform_(blk.b_out.data[t], H)
         if self.residual_ffn:
             blk.ln2_weight = nn.Parameter(torch.ones(D, device=dev))
             blk.ln2_bias = nn.Parameter(torch.zeros(D, device=dev))
@@ -441,6 +447,22 @@ class MDLRankMixerModel(MDLDomainMixin, nn.Module):
 
     def _feature_block(self, blk, x: torch.Tensor, cuda: bool) -> torch.Tensor:
         D = self.D
+        if self.moe:
+            if cuda:
+                from ..ops.fused import MixLayerNormFn
+                from ..ops.layers import LayerNormFn
+
+                m = MixLayerNormFn.apply(x, blk.ln1_weight, blk.ln1_bias, self.ln_eps)
+                f = blk.ffn(m)
+                if not self.residual_ffn:
+                    return f
+                return LayerNormFn.apply(f + m, blk.ln2_weight, blk.ln2_bias, self.ln_eps)
+            xf = x.float()
+            m = F.layer_norm(token_mix(xf) + xf, (D,), blk.ln1_weight, blk.ln1_bias, self.ln_eps)
+            f = blk.ffn(m).float()
+            if not self.residual_ffn:
+                return f.to(x.dtype)
+            return F.layer_norm(f + m, (D,), blk.ln2_weight, blk.ln2_bias, self.ln_eps).to(x.dtype)
         if cuda and not self.ffn_relu:
             from ..ops.fused import MixLayerNormFn, RankMixerBlockFn
             from ..ops.layers import PerTokenFFNFn
@@ -485,4 +507,9 @@ class MDLRankMixerModel(MDLDomainMixin, nn.Module):
         if task_scale is None:
             task_scale = torch.full((self.ntask,), 1.0 / max(1, B), device=x.device)
         pred = grad_ready(pred, hooks, 0)
-        return self.heads(pred, batch.labels, batch.label_mask, task_scale)
+        out = self.heads(pred, batch.labels, batch.label_mask, task_scale)
+        if self.moe:
+            from ..ops.moe import add_moe_loss
+
+            add_moe_loss(out, self, float(self.config.model.sparse_moe_loss_weight))
+        return out

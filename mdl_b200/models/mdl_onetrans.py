@@ -84,6 +84,8 @@ class MDLOneTransModel(MDLDomainMixin, OneTransModel):
         L = self.L
         if cuda:
             seq_in = grad_ready(seq_in, hooks, nl + 1)
+            if self.ns_mode != "auto_split":
+                ns_in = self.ns_tokens(ns_in).to(torch.bfloat16)
             X = OneTransTokenizeFn.apply(seq_in, ns_in, kstart, self, L)
             ks = kstart
         else:

@@ -229,7 +229,11 @@ class OneTransLayerFn(torch.autograd.Function):
 
 
 class OneTransTokenizeFn(torch.autograd.Function):
-    """S tokens (event projection MLP) + NS tokens (auto_split MLP) + positions -> ``[B, L + N, d]``."""
+    """S tokens (event projection MLP) + NS tokens + positions -> ``[B, L + N, d]``.
+
+    ``auto_split`` NS tokens are computed here (MLP GEMMs writing the NS rows);
+    for the other NS encoders ``ns_in`` is the finished ``[B, N * d]`` token
+    matrix, copied into the NS rows (its gradient is the NS rows of ``dX0``)."""
 
     @staticmethod
     def forward(ctx, seq_in, ns_in, kstart, model, L):
@@ -246,12 +250,16 @@ class OneTransTokenizeFn(torch.autograd.Function):
         X0 = torch.empty(B, Lt, D, dtype=torch.bfloat16, device=dev)
         bgemm(u, _shadow(model.seq_w2), X0, M=L, N=D, K=Hd, G=B, lda=Hd, gsA=L * Hd, ldb=Hd, gsB=0, ldc=D,
               gsC=Lt * D, bias=model.seq_b2)
-        vg = torch.empty(B, Hd, dtype=torch.bfloat16, device=dev)
-        v = torch.empty_like(vg)
-        bgemm(ns_in, _shadow(model.ns_w1), vg, M=B, N=Hd, K=Kn, lda=ns_in.stride(0), ldb=Kn, ldc=Hd, out2=v,
-              bias=model.ns_b1, act=ACT_GELU_GRAD)
-        bgemm(v, _shadow(model.ns_w2), _off(X0, L * D), M=B, N=N * D, K=Hd, lda=Hd, ldb=Hd, ldc=Lt * D,
-              bias=model.ns_b2)
+        if model.ns_mode == "auto_split":
+            vg = torch.empty(B, Hd, dtype=torch.bfloat16, device=dev)
+            v = torch.empty_like(vg)
+            bgemm(ns_in, _shadow(model.ns_w1), vg, M=B, N=Hd, K=Kn, lda=ns_in.stride(0), ldb=Kn, ldc=Hd, out2=v,
+                  bias=model.ns_b1, act=ACT_GELU_GRAD)
+            bgemm(v, _shadow(model.ns_w2), _off(X0, L * D), M=B, N=N * D, K=Hd, lda=Hd, ldb=Hd, ldc=Lt * D,
+                  bias=model.ns_b2)
+        else:
+            X0[:, L:, :].copy_(ns_in.view(B, N, D))
+            vg = v = ns_in.new_empty(0)
         ks = kstart.to(torch.int32).contiguous()
         C.position_add(X0, model.pos, ks, B, Lt, D)
         ctx.save_for_backward(seq_in, ns_in, ks, ug, u, vg, v)
@@ -283,6 +291,8 @@ class OneTransTokenizeFn(torch.autograd.Function):
         dseq = torch.empty(B * L, Ks, dtype=torch.bfloat16, device=dev)
         bgemm(du, _shadow(model.seq_w1), dseq, M=B * L, N=Ks, K=Hd, lda=Hd, ldb=Ks, b_mn=True, ldc=Ks)
         del du
+        if model.ns_mode != "auto_split":
+            return dseq, dX0[:, L:, :].reshape(B, N * D), None, None, None
         # NS: auto_split MLP
         dns_tok = _off(dX0, L * D)
         dv = torch.empty(B, Hd, dtype=torch.bfloat16, device=dev)
@@ -385,8 +395,9 @@ class OneTransModel(nn.Module):
                  domain_tokens: list[list[str]] | None = None, task_heads: bool = True) -> None:
         super().__init__()
         m = config.model
-        if m.ns_tokenizer != "auto_split":
-            raise NotImplementedError(f"OneTrans ns_tokenizer {m.ns_tokenizer!r}: auto_split is implemented")
+        self.ns_mode = m.ns_tokenizer
+        if self.ns_mode not in ("auto_split", "dcnv2", "groupwise"):
+            raise NotImplementedError(f"OneTrans ns_tokenizer {m.ns_tokenizer!r}")
         groups = config.resolved.tokenization.sequence_token_groups
         seq_by_name = {s.name: s for s in config.sequences}
         if len(groups) != 1 or len(groups[0].inputs) != 1 or groups[0].inputs[0] not in seq_by_name:
@@ -399,11 +410,23 @@ class OneTransModel(nn.Module):
             raise ValueError(f"sequence {self.seq.name!r} needs max_length")
         self.L = int(self.seq.max_length)
         ns_inputs = list(config.resolved.tokenization.feature_token_inputs)
+        # groupwise NS tokens read per-group input slices: the encoder's per-token input plan
+        # (shared with the MDL domain tokens, which follow the NS groups)
+        ns_groups = [list(g.inputs) for g in config.resolved.tokenization.ns_token_groups]
+        if self.ns_mode == "groupwise":
+            if not ns_groups:
+                raise ValueError("groupwise OneTrans tokenizer requires tokenization.ns_tokens or scalar features")
+            ns_inputs = []
+            domain_tokens = ns_groups + list(domain_tokens or [])
+        self._dom_offset = len(ns_groups) if self.ns_mode == "groupwise" else 0
         self.encoder = FeatureEncoder(config, device=device, rank=rank, world=world, process_group=process_group,
                                       vocab_sizes=vocab_sizes, input_names=ns_inputs, slice_tokens=1,
-                                      base_seed=base_seed, sequences=[self.seq], domain_tokens=domain_tokens)
+                                      base_seed=base_seed, sequences=[self.seq], domain_tokens=domain_tokens or None)
         D, Hd = int(m.token_dim), int(m.hidden_dim)
-        N = int(m.num_ns_tokens or max(1, len(ns_inputs)))
+        if self.ns_mode == "groupwise":
+            N = len(ns_groups)
+        else:
+            N = int(m.num_ns_tokens or max(1, len(ns_inputs)))
         self.token_dim, self.hidden_dim, self.num_ns, self.attn_heads = D, Hd, N, int(m.num_heads)
         self.eps = 1e-6
         seq_plan = self.encoder.seq_plans[self.seq.name]
@@ -413,18 +436,31 @@ class OneTransModel(nn.Module):
         self.seq_b1 = nn.Parameter(torch.empty(Hd, device=device))
         self.seq_w2 = gemm_param(torch.empty(D, Hd, device=device))
         self.seq_b2 = nn.Parameter(torch.empty(D, device=device))
-        self.ns_w1 = gemm_param(torch.zeros(Hd, self.Kn, device=device))
-        self.ns_b1 = nn.Parameter(torch.empty(Hd, device=device))
-        self.ns_w2 = gemm_param(torch.empty(N * D, Hd, device=device))
-        self.ns_b2 = nn.Parameter(torch.empty(N * D, device=device))
         _kaiming_uniform_(self.seq_w1.data[:, :self.Ks_log], self.Ks_log)  # padded input columns stay zero
         _kaiming_uniform_(self.seq_b1.data, self.Ks_log)
         _kaiming_uniform_(self.seq_w2.data, Hd)
         _kaiming_uniform_(self.seq_b2.data, Hd)
-        _kaiming_uniform_(self.ns_w1.data[:, :self.Kn_log], self.Kn_log)
-        _kaiming_uniform_(self.ns_b1.data, self.Kn_log)
-        _kaiming_uniform_(self.ns_w2.data, Hd)
-        _kaiming_uniform_(self.ns_b2.data, Hd)
+        if self.ns_mode == "auto_split":
+            self.ns_w1 = gemm_param(torch.zeros(Hd, self.Kn, device=device))
+            self.ns_b1 = nn.Parameter(torch.empty(Hd, device=device))
+            self.ns_w2 = gemm_param(torch.empty(N * D, Hd, device=device))
+            self.ns_b2 = nn.Parameter(torch.empty(N * D, device=device))
+            _kaiming_uniform_(self.ns_w1.data[:, :self.Kn_log], self.Kn_log)
+            _kaiming_uniform_(self.ns_b1.data, self.Kn_log)
+            _kaiming_uniform_(self.ns_w2.data, Hd)
+            _kaiming_uniform_(self.ns_b2.data, Hd)
+        elif self.ns_mode == "dcnv2":
+            from .ns_encoders import DCNv2Encoder
+
+            proj = int(m.ns_dcn_projection_dim or Hd)
+            self.ns_dcn = DCNv2Encoder(self.Kn, self.Kn_log, N * D, proj, int(m.ns_dcn_cross_layers),
+                                       int(m.ns_dcn_deep_layers), int(m.ns_dcn_deep_dim or proj), m.ffn_activation,
+                                       m.ns_dcn_low_rank, device=device)
+        else:
+            from .ns_encoders import GroupwiseNS
+
+            self.ns_group = GroupwiseNS(self.encoder.domain_widths[:N], self.encoder.domain_k_pad, D, Hd,
+                                        m.ffn_activation, device=device)
         P = max(int(config.resolved.onetrans_max_position_embeddings), self.L + N)
         self.pos = nn.Parameter(torch.empty(P, D, device=device).normal_(0.0, m.init_std))
         self.layers = nn.ModuleList(OneTransLayer(D, Hd, N, device=device) for _ in range(m.num_layers))
@@ -470,8 +506,22 @@ class OneTransModel(nn.Module):
         ids = seq["ids"].reshape(-1)
         seq_in = fused_lookup(self.store, plan, ids, self._seq_offsets(B * L, ids.device), seq.get("dense"), B * L,
                               anchor)
-        ns_in = fused_lookup(self.store, self.encoder.plan, batch.ids, batch.offsets, batch.dense, B, anchor)
+        if self.ns_mode == "groupwise":
+            ns_in = fused_lookup(self.store, self.encoder.domain_plan, batch.ids, batch.offsets, batch.dense, B, anchor)
+        else:
+            ns_in = fused_lookup(self.store, self.encoder.plan, batch.ids, batch.offsets, batch.dense, B, anchor)
         return seq_in, ns_in, kstart
+
+    def ns_tokens(self, ns_in: torch.Tensor) -> torch.Tensor:
+        """``[B, N * d]`` NS tokens of the ``dcnv2`` / ``groupwise`` encoders (``auto_split``
+        runs inside the tokenizer)."""
+
+        B = ns_in.shape[0]
+        if self.ns_mode == "dcnv2":
+            return self.ns_dcn(ns_in)
+        kp = self.encoder.domain_k_pad
+        v = ns_in.as_strided((B, self.num_ns * kp), (ns_in.stride(0), 1))
+        return self.ns_group(v).reshape(B, self.num_ns * self.token_dim)
 
     # ------------------------------------------------------------------ forward
     def forward(self, batch, task_scale: torch.Tensor | None = None) -> dict[str, torch.Tensor]:
@@ -489,6 +539,8 @@ class OneTransModel(nn.Module):
         hooks = getattr(self, "dense_hooks", None)
         nl = len(self.layers)
         seq_in = grad_ready(seq_in, hooks, nl + 1)
+        if self.ns_mode != "auto_split":
+            ns_in = self.ns_tokens(ns_in).to(torch.bfloat16)
         X = OneTransTokenizeFn.apply(seq_in, ns_in, kstart, self, self.L)
         s_in, ks = self.L, kstart
         for i, layer in enumerate(self.layers):
@@ -508,8 +560,11 @@ class OneTransModel(nn.Module):
         L, D, N = self.L, self.token_dim, self.num_ns
         s = F.gelu(seq_in.float()[:, :self.Ks_log] @ self.seq_w1[:, :self.Ks_log].t() + self.seq_b1)
         s = (s @ self.seq_w2.t() + self.seq_b2).view(B, L, D)
-        v = F.gelu(ns_in.float()[:, :self.Kn_log] @ self.ns_w1[:, :self.Kn_log].t() + self.ns_b1)
-        ns = (v @ self.ns_w2.t() + self.ns_b2).view(B, N, D)
+        if self.ns_mode == "auto_split":
+            v = F.gelu(ns_in.float()[:, :self.Kn_log] @ self.ns_w1[:, :self.Kn_log].t() + self.ns_b1)
+            ns = (v @ self.ns_w2.t() + self.ns_b2).view(B, N, D)
+        else:
+            ns = self.ns_tokens(ns_in).float().view(B, N, D)
         X = torch.cat([s, ns], dim=1)
         e = torch.arange(L + N, device=X.device)
         ks = kstart.to(X.device).long()
@@ -541,12 +596,17 @@ class OneTransModel(nn.Module):
               p + "tokenizer.sequence_projectors.0.0.bias": self.seq_b1,
               p + "tokenizer.sequence_projectors.0.2.weight": self.seq_w2,
               p + "tokenizer.sequence_projectors.0.2.bias": self.seq_b2,
-              p + "tokenizer.auto_ns_projection.0.weight": self.ns_w1[:, :self.Kn_log],
-              p + "tokenizer.auto_ns_projection.0.bias": self.ns_b1,
-              p + "tokenizer.auto_ns_projection.2.weight": self.ns_w2,
-              p + "tokenizer.auto_ns_projection.2.bias": self.ns_b2,
               p + "unified_position_embeddings.weight": self.pos}
+        if self.ns_mode == "auto_split":
+            sd.update({p + "tokenizer.auto_ns_projection.0.weight": self.ns_w1[:, :self.Kn_log],
+                       p + "tokenizer.auto_ns_projection.0.bias": self.ns_b1,
+                       p + "tokenizer.auto_ns_projection.2.weight": self.ns_w2,
+                       p + "tokenizer.auto_ns_projection.2.bias": self.ns_b2})
         sd = {k: v.detach().clone() for k, v in sd.items()}
+        if self.ns_mode == "dcnv2":
+            sd.update(self.ns_dcn.reference_state_dict(p + "tokenizer.dcn_ns_encoder."))
+        elif self.ns_mode == "groupwise":
+            sd.update(self.ns_group.reference_state_dict(p + "tokenizer.ns_projectors."))
         for i, layer in enumerate(self.layers):
             sd.update(layer.reference_state_dict(f"{p}blocks.{i}."))
         sd.update(self.heads_mod.reference_state_dict())

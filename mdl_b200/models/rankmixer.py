@@ -61,6 +61,7 @@ class RankMixerModel(nn.Module):
         self.Hh = int(mc.task_head_hidden_dim or mc.hidden_dim)
         self.head_relu = mc.task_head_activation == "relu"
         self.ffn_relu = mc.ffn_activation == "relu"
+        self.moe = mc.rankmixer_ffn_type == "sparse_moe"
         if self.D % self.T:
             raise ValueError("rankmixer requires token_dim divisible by the feature token count")
         by_name = {f.name: f for f in config.features}
@@ -107,17 +108,22 @@ class RankMixerModel(nn.Module):
             blk = nn.Module()
             blk.ln1_weight = nn.Parameter(torch.ones(D, device=dev))
             blk.ln1_bias = nn.Parameter(torch.zeros(D, device=dev))
-            blk.w_in = nn.Parameter(torch.empty(T, H, D, device=dev))
-            blk.b_in = nn.Parameter(torch.empty(T, H, device=dev))
-            blk.w_out = nn.Parameter(torch.empty(T, D, H, device=dev))
-            blk.b_out = nn.Parameter(torch.empty(T, D, device=dev))
+            if self.moe:
+                from ..ops.moe import build_rankmixer_moe
+
+                blk.ffn = build_rankmixer_moe(config, T, device=dev)
+            else:
+                blk.w_in = nn.Parameter(torch.empty(T, H, D, device=dev))
+                blk.b_in = nn.Parameter(torch.empty(T, H, device=dev))
+                blk.w_out = nn.Parameter(torch.empty(T, D, H, device=dev))
+                blk.b_out = nn.Parameter(torch.empty(T, D, device=dev))
+                for t in range(T):
+                    _kaiming_uniform_(blk.w_in.data[t], D)
+                    _kaiming_uniform_(blk.b_in.data[t], D)
+                    _kaiming_uniform_(blk.w_out.data[t], H)
+                    _kaiming_uniform_(blk.b_out.data[t], H)
             blk.ln2_weight = nn.Parameter(torch.ones(D, device=dev))
             blk.ln2_bias = nn.Parameter(torch.zeros(D, device=dev))
-            for t in range(T):
-                _kaiming_uniform_(blk.w_in.data[t], D)
-                _kaiming_uniform_(blk.b_in.data[t], D)
-                _kaiming_uniform_(blk.w_out.data[t], H)
-                _kaiming_uniform_(blk.b_out.data[t], H)
             self.blocks.append(blk)
         Hh, nt = self.Hh, self.ntask
         self.head_w1 = nn.Parameter(torch.empty(nt, Hh, D, device=dev))
@@ -137,7 +143,9 @@ class RankMixerModel(nn.Module):
 
         names = {"tok_weight", "head_w1"}
         for i in range(self.L):
-            names |= {f"blocks.{i}.w_in", f"blocks.{i}.w_out"}
+            if not self.moe:
+                names |= {f"blocks.{i}.w_in", f"blocks.{i}.w_out"}
+        names |= {n for n, p in self.blocks.named_parameters(prefix="blocks") if getattr(p, "_mdl_gemm", False)}
         names |= {n for n, p in self.stca.named_parameters(prefix="stca") if getattr(p, "_mdl_gemm", False)}
         return names
 
@@ -145,8 +153,8 @@ class RankMixerModel(nn.Module):
         """Parameter groups in the order their gradients become final in the backward."""
 
         heads = ["head_w1", "head_b1", "head_w2", "head_b2"]
-        blocks = [[f"blocks.{i}.{n}" for n in ("w_in", "b_in", "w_out", "b_out", "ln1_weight", "ln1_bias",
-                                               "ln2_weight", "ln2_bias")] for i in reversed(range(self.L))]
+        blocks = [[n for n, _ in self.blocks[i].named_parameters(prefix=f"blocks.{i}")]
+                  for i in reversed(range(self.L))]
         return [heads, *blocks, ["tok_weight", "tok_bias", *[n for n, _ in self.stca.named_parameters(prefix="stca")]]]
 
     @property
@@ -164,8 +172,14 @@ class RankMixerModel(nn.Module):
         if len(self.stca):
             x0 = self._add_stca(x0, batch, anchor)
         if batch.ids.is_cuda and self.config.runtime.kernel_backend == "native":
-            return self._forward_cuda(x0, batch, task_scale)
-        return self.forward_reference(x0, batch, task_scale)
+            out = self._forward_cuda(x0, batch, task_scale)
+        else:
+            out = self.forward_reference(x0, batch, task_scale)
+        if self.moe:
+            from ..ops.moe import add_moe_loss
+
+            add_moe_loss(out, self, float(self.config.model.sparse_moe_loss_weight))
+        return out
 
     def _add_stca(self, x0, batch, anchor):
         """STCA summary tokens of the encoded sequences into their tokenizer columns."""
@@ -204,6 +218,13 @@ class RankMixerModel(nn.Module):
         x = PerTokenLinearFn.apply(x0, self.tok_weight, self.tok_bias, self.T, self.K, self.Kpad)
         for i, blk in enumerate(self.blocks):
             x = grad_ready(x, hooks, self.L - i)
+            if self.moe:
+                from ..ops.fused import MixLayerNormFn
+                from ..ops.layers import LayerNormFn
+
+                m = MixLayerNormFn.apply(x, blk.ln1_weight, blk.ln1_bias, self.ln_eps)
+                x = LayerNormFn.apply(blk.ffn(m) + m, blk.ln2_weight, blk.ln2_bias, self.ln_eps)
+                continue
             x = RankMixerBlockFn.apply(x, blk.ln1_weight, blk.ln1_bias, blk.w_in, blk.b_in, blk.w_out, blk.b_out,
                                        blk.ln2_weight, blk.ln2_bias, self.ln_eps)
         x = grad_ready(x, hooks, 0)
@@ -224,8 +245,11 @@ class RankMixerModel(nn.Module):
         act_fn = F.relu if self.ffn_relu else F.gelu
         for blk in self.blocks:
             m = F.layer_norm(token_mix(x) + x, (D,), blk.ln1_weight, blk.ln1_bias, self.ln_eps)
-            h = act_fn(torch.einsum("btd,thd->bth", m, blk.w_in) + blk.b_in.unsqueeze(0))
-            f = torch.einsum("bth,tdh->btd", h, blk.w_out) + blk.b_out.unsqueeze(0)
+            if self.moe:
+                f = blk.ffn(m).float()
+            else:
+                h = act_fn(torch.einsum("btd,thd->bth", m, blk.w_in) + blk.b_in.unsqueeze(0))
+                f = torch.einsum("bth,tdh->btd", h, blk.w_out) + blk.b_out.unsqueeze(0)
             x = F.layer_norm(f + m, (D,), blk.ln2_weight, blk.ln2_bias, self.ln_eps)
         pooled = x.mean(dim=1)
         head_act = F.relu if self.head_relu else F.gelu
@@ -253,10 +277,13 @@ class RankMixerModel(nn.Module):
             p = f"blocks.{i}."
             sd[p + "feature_norm.weight"] = blk.ln1_weight.detach().clone()
             sd[p + "feature_norm.bias"] = blk.ln1_bias.detach().clone()
-            sd[p + "feature_ffn.input_weight"] = blk.w_in.detach().clone()
-            sd[p + "feature_ffn.input_bias"] = blk.b_in.detach().clone()
-            sd[p + "feature_ffn.output_weight"] = blk.w_out.detach().clone()
-            sd[p + "feature_ffn.output_bias"] = blk.b_out.detach().clone()
+            if self.moe:
+                sd.update(blk.ffn.reference_state_dict(p + "feature_ffn."))
+            else:
+                sd[p + "feature_ffn.input_weight"] = blk.w_in.detach().clone()
+                sd[p + "feature_ffn.input_bias"] = blk.b_in.detach().clone()
+                sd[p + "feature_ffn.output_weight"] = blk.w_out.detach().clone()
+                sd[p + "feature_ffn.output_bias"] = blk.b_out.detach().clone()
             sd[p + "feature_ffn_norm.weight"] = blk.ln2_weight.detach().clone()
             sd[p + "feature_ffn_norm.bias"] = blk.ln2_bias.detach().clone()
         for t in range(self.ntask):
@@ -269,6 +296,8 @@ class RankMixerModel(nn.Module):
 
     @torch.no_grad()
     def load_reference_state_dict(self, sd: dict[str, torch.Tensor]) -> None:
+        if self.moe:
+            raise NotImplementedError("loading reference weights covers the dense per-token FFN")
         K = self.K
         self.tok_weight[:, :, :K].copy_(sd["feature_projector.projection.weight"])
         self.tok_weight[:, :, K:].zero_()

@@ -75,6 +75,9 @@ class Trainer:
                                          dtype=torch.float32, device=self.device)
         self.step_index = 0
         self.micro_index = 0
+        from ..ops.moe import moe_modules
+
+        self.moe = moe_modules(model)
 
     def task_scale(self, batch) -> torch.Tensor:
         """Per-task multiplier of the summed BCE terms (see module docstring)."""
@@ -109,6 +112,10 @@ class Trainer:
         self.step_index += 1
         t = self.config.training
         lr_dense, lr_sparse = self._lrs(self.step_index)
+        if self.moe:
+            from ..ops.moe import step_moe_controllers
+
+            step_moe_controllers(self.moe, self.world, self.group)
         dn = self.dense.step(lr=lr_dense, clip_norm=t.dense_clip_norm)
         sn = self.store.step(lr=lr_sparse, clip_norm=t.sparse_clip_norm)
         return dn, sn

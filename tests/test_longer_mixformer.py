@@ -32,8 +32,8 @@ def _mixformer():
 
 def _mdl_mixformer(**model):
     m, spec = scaled_config(4, 1e-4, num_fields=12, batch=64, seq_len=40, num_layers=2, mdl=True)
-    m["model"].update({"name": "mdl_mixformer", "token_dim": 32, "hidden_dim": 64, "num_ns_tokens": 4,
-                       "num_heads": 2, "task_head_hidden_dim": 32})
+    m["model"].update({"name": "mdl_mixformer", "experimental_model_acknowledged": True, "token_dim": 32,
+                       "hidden_dim": 64, "num_ns_tokens": 4, "num_heads": 2, "task_head_hidden_dim": 32})
     m["model"].update(model)
     m["training"].update({"lr_warmup_steps": 0, "dense_optimizer": "adam", "lr_dense": 1e-3})
     spec.sequences["behavior"].min_len = 10

@@ -175,3 +175,66 @@ def test_mdl_onetrans_cuda_step_matches_cpu_reference(variant):
         ref, got = gc[o:o + n], gg[o:o + n]
         err = (ref - got).norm().item()
         assert err <= 0.1 * ref.norm().item() + 2e-3 * scale, (name, err, ref.norm().item())
+
+
+# ----------------------------------------------------------------------------- NS tokenizers
+def _ns_variant(mode, mdl=False, **model):
+    m, spec = scaled_config(4, 1e-4, num_fields=12, batch=64, seq_len=40, num_layers=2, mdl=mdl)
+    m["model"].update({"hidden_dim": 128, "token_dim": 64, "num_heads": 2, "num_ns_tokens": 4,
+                       "task_head_hidden_dim": 64, "pyramid_round_to": 8, "ns_tokenizer": mode})
+    m["model"].update(model)
+    if mode == "groupwise":
+        feats = [f["name"] for f in m["features"] if f.get("embedding_scope", "feature") == "feature"]
+        m["tokenization"]["ns_tokens"] = [{"name": f"g{i}", "inputs": feats[i::3]} for i in range(3)]
+    m["training"].update({"lr_warmup_steps": 0, "dense_optimizer": "adam", "lr_dense": 1e-3})
+    spec.sequences["behavior"].min_len = 10
+    return app_config_from_mapping(m), spec
+
+
+@pytest.mark.parametrize("mode,mdl,extra", [("dcnv2", False, {}), ("dcnv2", False, {"ns_dcn_low_rank": 16,
+                                                                                     "ns_dcn_deep_layers": 0}),
+                                            ("groupwise", False, {}), ("groupwise", True, {})])
+def test_ns_tokenizers_train(mode, mdl, extra):
+    cfg, spec = _ns_variant(mode, mdl, **extra)
+    torch.manual_seed(0)
+    model = build_model(cfg, device="cpu", base_seed=1)
+    if mode == "groupwise":
+        assert model.num_ns == 3
+        assert model.encoder.plan.out_width == 0     # the NS inputs come from the per-group plan only
+    tr = Trainer(cfg, model, device=torch.device("cpu"))
+    batch = SyntheticGenerator(model.encoder.batch_plan, spec).batch(64)
+    losses = [float(tr.train_step(batch).loss) for _ in range(8)]
+    assert losses[-1] < losses[0]
+    sd = model.reference_state_dict() if not mdl else {}
+    if mode == "dcnv2" and not extra:
+        assert "backbone.tokenizer.dcn_ns_encoder.cross_layers.2.weight" in sd
+        assert sd["backbone.tokenizer.dcn_ns_encoder.output_proj.weight"].shape == (4 * 64, 256)
+    if mode == "groupwise" and not mdl:
+        assert "backbone.tokenizer.ns_projectors.2.2.bias" in sd
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("mode,mdl", [("dcnv2", False), ("groupwise", True)])
+def test_ns_tokenizers_cuda_match_cpu(mode, mdl):
+    cfg, spec = _ns_variant(mode, mdl)
+    torch.manual_seed(0)
+    cpu_model = build_model(cfg, device="cpu", base_seed=1)
+    gpu_model = build_model(cfg, device="cuda", base_seed=1)
+    gpu_model.load_state_dict({k: v.cuda() for k, v in cpu_model.state_dict().items()})
+    gpu_model.store.slab.copy_(cpu_model.store.slab)
+    cpu_tr = Trainer(cfg, cpu_model, device=torch.device("cpu"))
+    gpu_tr = Trainer(cfg, gpu_model, device=torch.device("cuda"))
+    batch = SyntheticGenerator(cpu_model.encoder.batch_plan, spec).batch(64)
+    out_c = cpu_tr.forward_backward(batch)
+    out_g = gpu_tr.forward_backward(batch.to("cuda"))
+    torch.cuda.synchronize()
+    check_error_word(0)
+    torch.testing.assert_close(out_g["logits"].cpu(), out_c["logits"].detach(), atol=6e-2, rtol=6e-2)
+    gc, gg = cpu_tr.dense.grad, gpu_tr.dense.grad.cpu()
+    scale = gc.norm().item()
+    for name in cpu_tr.dense.names:
+        o = cpu_tr.dense.offsets[name]
+        n = cpu_tr.dense.params[name].numel()
+        ref, got = gc[o:o + n], gg[o:o + n]
+        err = (ref - got).norm().item()
+        assert err <= 0.1 * ref.norm().item() + 2e-3 * scale, (name, err, ref.norm().item())
