@@ -62,6 +62,8 @@ def validate_app_config(config: AppConfig) -> None:
         # experimental compositions (reference ``ModelConfig`` validation, src/config.py:2826-2833)
         _require(model.experimental_model_acknowledged,
                  f"{model.name} is an experimental composition: set model.experimental_model_acknowledged: true")
+    _require(model.readout != "task_query" or model.name in ("onetrans", "mixformer"),
+             "model.readout=task_query is the equal-readout control of the onetrans and mixformer baselines")
     if model.first_domain_sequence_layer is not None:
         _require(0 <= model.first_domain_sequence_layer < model.num_layers,
                  "model.first_domain_sequence_layer must be in [0, model.num_layers)")

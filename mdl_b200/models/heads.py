@@ -176,3 +176,27 @@ class TaskHeads(nn.Module):
             sd[p + "3.weight"] = self.w2.detach()[t].view(1, -1).clone()
             sd[p + "3.bias"] = self.b2.detach()[t:t + 1].clone()
         return sd
+
+
+class TaskQueryReadout(nn.Module):
+    """Equal-readout control (``model.readout: task_query``; reference
+    ``TaskQueryReadout`` ``src/model.py:900-946``): one learned query per task reads the
+    final feature tokens with domain-aware attention, then a per-token FFN with a
+    residual, giving one ``token_dim`` state per task for the task heads."""
+
+    def __init__(self, num_tasks: int, token_dim: int, num_heads: int, num_feature_tokens: int, hidden_dim: int,
+                 activation: str, init_std: float, device=None) -> None:
+        super().__init__()
+        from ..ops.layers import DomainAwareAttention, PerTokenFFN
+
+        self.queries = nn.Parameter(torch.empty(num_tasks, token_dim, device=device).normal_(0.0, init_std))
+        self.attention = DomainAwareAttention(token_dim, num_heads, num_tasks, num_feature_tokens, hidden_dim,
+                                              activation, device=device)
+        self.ffn = PerTokenFFN(num_tasks, token_dim, hidden_dim, activation, device=device)
+
+    def forward(self, feature_tokens: torch.Tensor) -> torch.Tensor:
+        B = feature_tokens.shape[0]
+        dt = torch.bfloat16 if feature_tokens.is_cuda else feature_tokens.dtype
+        q = self.queries.to(dt).unsqueeze(0).expand(B, -1, -1)
+        states = q + self.attention(q, feature_tokens).to(dt)
+        return states + self.ffn(states).to(dt)

@@ -227,8 +227,16 @@ class MixFormerModel(nn.Module):
                                    int(m.hidden_dim), int(m.hidden_dim), max(1, int(m.num_layers)), device=device,
                                    user_heads=m.mixformer_user_head_count)
         self.ntask = len(config.task_names)
+        self.task_query = None
         if task_heads:
-            self.heads_mod = TaskHeads(self.ntask, N * Dh, int(m.task_head_hidden_dim or 4 * Dh),
+            head_in = N * Dh
+            if m.readout == "task_query":
+                from .heads import TaskQueryReadout
+
+                self.task_query = TaskQueryReadout(self.ntask, Dh, int(m.num_heads), N, int(m.hidden_dim),
+                                                   m.ffn_activation, float(m.init_std), device=device)
+                head_in = Dh
+            self.heads_mod = TaskHeads(self.ntask, head_in, int(m.task_head_hidden_dim or 4 * Dh),
                                        m.task_head_activation, device=device)
 
     def gemm_param_names(self) -> set[str]:
@@ -270,6 +278,9 @@ class MixFormerModel(nn.Module):
         readout = self.mixer(feat_in, tokens, valid, native)
         if task_scale is None:
             task_scale = torch.full((self.ntask,), 1.0 / max(1, B), device=readout.device)
+        if self.task_query is not None:
+            states = self.task_query(readout.view(B, self.N, self.D))
+            return self.heads_mod(states, batch.labels, batch.label_mask, task_scale)
         return self.heads_mod.forward_shared(readout, batch.labels, batch.label_mask, task_scale)
 
 

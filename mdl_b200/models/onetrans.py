@@ -466,8 +466,16 @@ class OneTransModel(nn.Module):
         self.layers = nn.ModuleList(OneTransLayer(D, Hd, N, device=device) for _ in range(m.num_layers))
         self.query_counts = pyramid_query_counts(config, self.L, N)
         self.ntask = len(config.task_names)
+        self.task_query = None
         if task_heads:
-            self.heads_mod = TaskHeads(self.ntask, N * D, int(m.task_head_hidden_dim or Hd),
+            head_in = N * D
+            if m.readout == "task_query":
+                from .heads import TaskQueryReadout
+
+                self.task_query = TaskQueryReadout(self.ntask, D, int(m.num_heads), N, Hd, m.ffn_activation,
+                                                   float(m.init_std), device=device)
+                head_in = D
+            self.heads_mod = TaskHeads(self.ntask, head_in, int(m.task_head_hidden_dim or Hd),
                                        m.task_head_activation, device=device)
 
     # ------------------------------------------------------------------ params
@@ -550,9 +558,16 @@ class OneTransModel(nn.Module):
             ks = (ks - (s_in - q)).clamp(min=0)
             s_in = q
         X = grad_ready(X, hooks, 0)
-        B, Lq, D = X.shape
-        readout = X[:, s_in:, :].reshape(B, self.num_ns * D)
-        return self.heads_mod.forward_shared(readout, batch.labels, batch.label_mask, task_scale)
+        return self._task_logits(X[:, s_in:, :], batch, task_scale)
+
+    def _task_logits(self, ns: torch.Tensor, batch, task_scale) -> dict[str, torch.Tensor]:
+        """Heads over the flattened final NS tokens, or over the task-query states
+        (reference ``_task_readout_logits`` ``src/model.py:960-972``)."""
+
+        if self.task_query is not None:
+            return self.heads_mod(self.task_query(ns), batch.labels, batch.label_mask, task_scale)
+        B = ns.shape[0]
+        return self.heads_mod.forward_shared(ns.reshape(B, -1), batch.labels, batch.label_mask, task_scale)
 
     def tokenize_reference(self, seq_in, ns_in, kstart, B):
         """fp32 PyTorch tokenizer: ``[B, L + N, d]`` with positions on the valid tokens."""
@@ -584,8 +599,7 @@ class OneTransModel(nn.Module):
             X = layer.forward_reference(X, ks, s_in, q, self.attn_heads, self.eps)
             ks = (ks - (s_in - q)).clamp(min=0)
             s_in = q
-        readout = X[:, s_in:, :].reshape(B, N * D)
-        return self.heads_mod.forward_shared(readout, batch.labels, batch.label_mask, task_scale)
+        return self._task_logits(X[:, s_in:, :], batch, task_scale)
 
     # ------------------------------------------------------------------ reference layout
     def reference_state_dict(self) -> dict[str, torch.Tensor]:
@@ -610,6 +624,9 @@ class OneTransModel(nn.Module):
         for i, layer in enumerate(self.layers):
             sd.update(layer.reference_state_dict(f"{p}blocks.{i}."))
         sd.update(self.heads_mod.reference_state_dict())
+        if self.task_query is not None:
+            sd.update({"task_query_readout." + k: v.detach().clone()
+                       for k, v in self.task_query.state_dict().items()})
         return sd
 
 

@@ -12,11 +12,11 @@ from mdl_b200.ops._ext import check_error_word
 from mdl_b200.train.trainer import Trainer
 
 
-def _small(seq_len=40, layers=3, min_len=10, heads=2, schedule="halve"):
+def _small(seq_len=40, layers=3, min_len=10, heads=2, schedule="halve", readout="default"):
     m, spec = scaled_config(4, 1e-4, num_fields=12, batch=64, seq_len=seq_len, num_layers=layers,
                             pyramid_schedule=schedule)
     m["model"].update({"hidden_dim": 128, "token_dim": 32 * heads, "num_heads": heads, "num_ns_tokens": 4,
-                       "task_head_hidden_dim": 64, "pyramid_round_to": 8})
+                       "task_head_hidden_dim": 64, "pyramid_round_to": 8, "readout": readout})
     m["training"].update({"lr_warmup_steps": 0, "dense_optimizer": "adam", "lr_dense": 1e-3})
     spec.sequences["behavior"].min_len = min_len
     return app_config_from_mapping(m), spec
@@ -54,7 +54,8 @@ def test_onetrans_reference_state_dict_names():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("variant", [dict(), dict(seq_len=300, layers=4, min_len=50, heads=4)])
+@pytest.mark.parametrize("variant", [dict(), dict(seq_len=300, layers=4, min_len=50, heads=4),
+                                     dict(readout="task_query")])
 def test_onetrans_cuda_step_matches_cpu_reference(variant):
     cfg, spec = _small(**variant)
     torch.manual_seed(0)
@@ -238,3 +239,19 @@ def test_ns_tokenizers_cuda_match_cpu(mode, mdl):
         ref, got = gc[o:o + n], gg[o:o + n]
         err = (ref - got).norm().item()
         assert err <= 0.1 * ref.norm().item() + 2e-3 * scale, (name, err, ref.norm().item())
+
+
+def test_task_query_readout_trains():
+    cfg, spec = _small(layers=2, readout="task_query")
+    torch.manual_seed(0)
+    model = build_model(cfg, device="cpu", base_seed=1)
+    assert model.task_query is not None and model.heads_mod.input_dim == 64
+    tr = Trainer(cfg, model, device=torch.device("cpu"))
+    batch = SyntheticGenerator(model.encoder.batch_plan, spec).batch(64)
+    losses = [float(tr.train_step(batch).loss) for _ in range(8)]
+    assert losses[-1] < losses[0]
+    assert "task_query_readout.queries" in model.reference_state_dict()
+    m, _ = scaled_config(2, 1e-4, num_fields=12, batch=64)
+    m["model"]["readout"] = "task_query"
+    with pytest.raises(Exception, match="task_query"):
+        app_config_from_mapping(m)
