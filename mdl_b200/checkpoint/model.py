@@ -82,10 +82,16 @@ def save_model_checkpoint(config, trainer, store: CheckpointStore, *, chunk_byte
 
     emb = trainer.store
     rank, world, group = trainer.rank, trainer.world, trainer.group
+    # table shards are laid out over emb.world ranks (1 for replicated tables, whose
+    # identical copies only rank 0 writes)
+    emb_rank, emb_world = emb.rank, emb.world
+    writes_tables = emb.replicas == 1 or rank == 0
     written: list[str] = []
     store.makedirs()
     chunks = plan_chunks(emb, chunk_bytes)
     for index, names in enumerate(chunks):
+        if not writes_tables:
+            break
         tables = {}
         for name in names:
             t = emb.layouts[emb.index[name]]
@@ -98,8 +104,8 @@ def save_model_checkpoint(config, trainer, store: CheckpointStore, *, chunk_byte
                 "optimizer_state": {"sum": emb.accumulator(name).detach().cpu().clone(),
                                     "step": torch.tensor(float(sparse_step), dtype=torch.float64)},
             }
-        name = shard_chunk_file(index, rank, world)
-        store.write_torch({"format": SHARDED_FORMAT, "rank": rank, "world_size": world, "chunk": index,
+        name = shard_chunk_file(index, emb_rank, emb_world)
+        store.write_torch({"format": SHARDED_FORMAT, "rank": emb_rank, "world_size": emb_world, "chunk": index,
                            "tables": tables}, name)
         written.append(name)
     state = dense_state(trainer)  # collective (all ranks) when the dense update is sharded
@@ -112,9 +118,10 @@ def save_model_checkpoint(config, trainer, store: CheckpointStore, *, chunk_byte
             "format": SHARDED_FORMAT,
             "version": 2,
             "world_size": world,
+            "embedding_world_size": emb_world,
             "dense_file": DENSE_FILE,
             "chunks": [{"index": i, "tables": names,
-                        "rank_files": [shard_chunk_file(i, r, world) for r in range(world)]}
+                        "rank_files": [shard_chunk_file(i, r, emb_world) for r in range(emb_world)]}
                        for i, names in enumerate(chunks)],
             "tables": {t.name: {"num_embeddings": t.num_embeddings, "embedding_dim": t.dim, "padding_idx": 0}
                        for t in emb.layouts},
@@ -145,15 +152,15 @@ def load_model_checkpoint(config, trainer, store: CheckpointStore, *, strict: bo
     if strict and manifest.get("model_name") != config.model.name:
         raise ValueError(f"checkpoint is a {manifest.get('model_name')!r} model, config builds {config.model.name!r}")
     emb = trainer.store
-    rank, world = trainer.rank, trainer.world
-    saved_world = int(manifest["world_size"])
+    rank = emb.rank  # shard coordinates of the tables (0 of 1 for replicated tables)
+    saved_world = int(manifest.get("embedding_world_size", manifest["world_size"]))
     dense = store.read_torch(manifest.get("dense_file", DENSE_FILE))["model_state_dict"]
     dp = trainer.dense
     missing = [n for n in dp.params if n not in dense]
     if strict and missing:
         raise KeyError(f"dense parameters missing from the checkpoint: {missing[:5]}")
     dp.load_state_dict({"params": {n: v for n, v in dense.items() if n in dp.params}})
-    reshard = saved_world != world
+    reshard = saved_world != emb.world
     for chunk in manifest["chunks"]:
         files = chunk["rank_files"] if reshard else [chunk["rank_files"][rank]]
         for fname in files:

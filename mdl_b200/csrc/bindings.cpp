@@ -294,11 +294,13 @@ void adagrad_apply(const at::Tensor& slab, const at::Tensor& grad_slab, const at
                    int64_t total_rows, const at::Tensor& t_base, const at::Tensor& t_row_base,
                    const at::Tensor& t_dim, double lr, double eps, double grad_scale,
                    const std::optional<at::Tensor>& clip, const std::optional<at::Tensor>& err, int64_t max_dim,
-                   const std::optional<at::Tensor>& list, const std::optional<at::Tensor>& count) {
+                   const std::optional<at::Tensor>& list, const std::optional<at::Tensor>& count, bool full) {
   c10::cuda::CUDAGuard guard(slab.device());
   auto a = adagrad_args(slab, grad_slab, acc, flags, total_rows, t_base, t_row_base, t_dim, lr, eps, grad_scale,
                         clip, err, max_dim);
   set_list(a, list, count);
+  a.full = full;
+  TORCH_CHECK(!full || acc.numel() >= slab.numel(), "full Adagrad: one accumulator per weight element");
   check(mdl::rowwise_adagrad_apply(a, stream_of(slab)), "rowwise_adagrad_apply");
   g_launches += 1;
 }

@@ -961,6 +961,27 @@ __global__ void __launch_bounds__(kThreads) adagrad_list_kernel(const AdagradArg
       if (sub == 0) sq_total += sq;
       continue;
     }
+    if (a.full) {  // per-element sums live at the weight's offsets
+#pragma unroll
+      for (int v = 0; v < NV; ++v) {
+        const int col = (sub + v * G) * 4;
+        if (col < dim) {
+          float4* s4 = reinterpret_cast<float4*>(a.acc + base + col);
+          float4* w = reinterpret_cast<float4*>(a.slab + base + col);
+          float4 sacc = *s4, x = *w;
+          sacc.x += g[v].x * g[v].x; sacc.y += g[v].y * g[v].y;
+          sacc.z += g[v].z * g[v].z; sacc.w += g[v].w * g[v].w;
+          x.x -= a.lr * g[v].x / (sqrtf(sacc.x) + a.eps);
+          x.y -= a.lr * g[v].y / (sqrtf(sacc.y) + a.eps);
+          x.z -= a.lr * g[v].z / (sqrtf(sacc.z) + a.eps);
+          x.w -= a.lr * g[v].w / (sqrtf(sacc.w) + a.eps);
+          *s4 = sacc;
+          *w = x;
+          *reinterpret_cast<float4*>(a.grad_slab + base + col) = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+      continue;
+    }
     const float acc = a.acc[rs] + sq / static_cast<float>(dim);
     const float step = a.lr / (sqrtf(acc) + a.eps);
 #pragma unroll
@@ -1140,6 +1161,7 @@ cudaError_t compact_touched(const AdagradArgs& a, cudaStream_t stream) {
 cudaError_t rowwise_adagrad_apply(const AdagradArgs& a, cudaStream_t stream) {
   if (a.total_rows <= 0) return cudaSuccess;
   if (a.list != nullptr) return launch_list<false>(a, nullptr, stream);
+  if (a.full) return cudaErrorInvalidValue;  // the per-element update walks the touched list
   const int grid = scan_grid(a.total_rows);
   if (a.max_dim <= 128) {
     int dev = 0, sms = 148;

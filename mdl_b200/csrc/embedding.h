@@ -137,6 +137,9 @@ struct AdagradArgs {
   // scanning the flags.
   unsigned* list = nullptr;
   unsigned* count = nullptr;
+  // Full (per-element) Adagrad: acc holds one fp32 sum per weight element at the
+  // weight's slab offset (torch.optim.Adagrad / ShardedAdagrad semantics); needs the list.
+  bool full = false;
 };
 cudaError_t rowwise_adagrad_apply(const AdagradArgs& a, cudaStream_t stream);
 

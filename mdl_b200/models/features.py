@@ -216,16 +216,22 @@ class FeatureEncoder:
         specs = [EmbeddingTableSpec(n, r, d, 4 if train.embedding_weight_dtype == "fp32" else 2)
                  for n, (r, d) in sorted(tables.items())]
         self.table_shapes = tables
+        # replicated tables: every rank holds all rows (one shard) and trains them with
+        # torch.optim.Adagrad semantics (reference src/train.py:6619-6629); sharded tables
+        # use the configured row-wise or full Adagrad
+        replicated = train.embedding_distribution == "replicated"
+        shard_world = 1 if replicated else world
+        layout = "full" if replicated or train.sparse_optimizer != "rowwise_adagrad" else "rowwise"
         self.shard_plan = plan_embedding_shards(
-            specs, world_size=world, strategy=train.embedding_sharding.strategy,
-            table_wise_max_rows=train.embedding_sharding.table_wise_max_rows,
-            optimizer_state_layout="rowwise" if train.sparse_optimizer == "rowwise_adagrad" else "full")
+            specs, world_size=shard_world, strategy=train.embedding_sharding.strategy,
+            table_wise_max_rows=train.embedding_sharding.table_wise_max_rows, optimizer_state_layout=layout)
         lr_sparse = train.lr_sparse if train.lr_sparse is not None else train.lr_dense
         self.store = EmbeddingStore(
-            [(n, r, d) for n, (r, d) in sorted(tables.items())], self.shard_plan, rank=rank, world=world,
-            device=device, init_std=config.model.init_std, lr=lr_sparse, eps=train.adagrad_eps,
+            [(n, r, d) for n, (r, d) in sorted(tables.items())], self.shard_plan, rank=0 if replicated else rank,
+            world=shard_world, device=device, init_std=config.model.init_std, lr=lr_sparse, eps=train.adagrad_eps,
             initial_accumulator_value=train.adagrad_initial_accumulator_value, process_group=process_group,
-            base_seed=base_seed)
+            base_seed=base_seed, optimizer=layout, lr_decay=train.adagrad_lr_decay,
+            replicas=world if replicated else 1, replica_group=process_group)
 
     # ids arrive already encoded (tensorization applies the encodings on the host)
     _device_hash = False

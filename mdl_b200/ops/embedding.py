@@ -63,12 +63,27 @@ class EmbeddingStore:
     def __init__(self, tables: Sequence[tuple[str, int, int]], plan: EmbeddingShardingPlan, *, rank: int,
                  world: int, device: torch.device, init_std: float = 0.02, lr: float = 0.01, eps: float = 1e-10,
                  initial_accumulator_value: float = 0.1,
-                 process_group=None, base_seed: int | None = None) -> None:
+                 process_group=None, base_seed: int | None = None, optimizer: str = "rowwise",
+                 lr_decay: float = 0.0, replicas: int = 1, replica_group=None) -> None:
+        """``world`` / ``rank`` describe the table sharding; ``replicas > 1`` makes every
+        rank of ``replica_group`` hold a full copy (``world == 1``) whose touched-row
+        gradients are summed across the replicas before each update.
+        ``optimizer``: ``rowwise`` (one accumulator per row) or ``full`` (one per element,
+        ``torch.optim.Adagrad`` semantics); ``lr_decay`` gives ``lr / (1 + (step - 1) * lr_decay)``."""
+
+        if optimizer not in ("rowwise", "full"):
+            raise ValueError(f"sparse optimizer layout {optimizer!r}")
+        if replicas > 1 and world != 1:
+            raise ValueError("replicated tables are laid out as one shard (world 1)")
         self.rank = rank
         self.world = world
         self.device = torch.device(device)
         self.lr = lr
         self.eps = eps
+        self.full = optimizer == "full"
+        self.lr_decay = float(lr_decay)
+        self.replicas = int(replicas)
+        self.replica_group = replica_group
         self.process_group = process_group
         self.layouts: list[TableLayout] = []
         self.index: dict[str, int] = {}
@@ -142,7 +157,7 @@ class EmbeddingStore:
             self.slab = torch.empty(self.total_elems, dtype=torch.float32, device=dev)
             self.grad = torch.zeros(self.total_elems, dtype=torch.float32, device=dev)
             self.flags = torch.zeros(flag_len, dtype=torch.uint8, device=dev)
-        self.acc = torch.empty(self.total_rows, dtype=torch.float32, device=dev)
+        self.acc = torch.empty(self.total_elems if self.full else self.total_rows, dtype=torch.float32, device=dev)
         # touched-row list rebuilt every step from the flags (CUDA): the update then walks
         # only those rows, each with coalesced 16-byte lanes
         self.touched_list = (torch.empty(max(self.total_rows, 1), dtype=torch.int32, device=dev)
@@ -164,7 +179,11 @@ class EmbeddingStore:
         return self.grad[t.base:t.base + t.local_rows * t.dim].view(t.local_rows, t.dim)
 
     def accumulator(self, name: str) -> torch.Tensor:
+        """``[local_rows]`` (row-wise) or ``[local_rows, dim]`` (full) Adagrad sums."""
+
         t = self.layouts[self.index[name]]
+        if self.full:
+            return self.acc[t.base:t.base + t.local_rows * t.dim].view(t.local_rows, t.dim)
         return self.acc[t.row_base:t.row_base + t.local_rows]
 
     @torch.no_grad()
@@ -215,14 +234,19 @@ class EmbeddingStore:
     # ------------------------------------------------------------ optimizer
     @torch.no_grad()
     def step(self, lr: float | None = None, clip_norm: float | None = None) -> torch.Tensor | None:
-        """Row-wise Adagrad on every row touched since the last step.
+        """Adagrad (row-wise or full) on every row touched since the last step.
 
         Returns the (pre-clip) global sparse gradient norm when ``clip_norm`` is set.
         """
 
         lr = self.lr if lr is None else lr
         self.step_count += 1
+        if self.lr_decay:
+            lr = lr / (1.0 + (self.step_count - 1) * self.lr_decay)
         grad_scale = 1.0 / self.world
+        if self.replicas > 1:
+            self._sync_replicas()
+            grad_scale = 1.0 / self.replicas
         if self.device.type != "cuda":
             return self._cpu_step(lr, grad_scale, clip_norm)
         m = self.table_meta()
@@ -246,7 +270,7 @@ class EmbeddingStore:
             norm = sq.sqrt()
         C.adagrad_apply(self.slab, self.grad, self.acc, self.flags, self.total_rows, m["t_base"], m["t_row_base"],
                         m["t_dim"], float(lr), float(self.eps), grad_scale, clip, error_word(self.device), max_dim,
-                        self.touched_list, self.touched_count)
+                        self.touched_list, self.touched_count, self.full)
         if self._symm is not None:
             self._symm.barrier()  # updated rows visible before any peer reads them
         return norm
@@ -274,12 +298,81 @@ class EmbeddingStore:
                 continue
             g = self.grad_view(t.name)[rows] * scale
             acc = self.accumulator(t.name)
-            acc[rows] += g.square().mean(dim=1)
             w = self.weight(t.name)
-            w[rows] -= lr * g / (acc[rows].sqrt() + self.eps).unsqueeze(1)
+            if self.full:
+                acc[rows] += g.square()
+                w[rows] -= lr * g / (acc[rows].sqrt() + self.eps)
+            else:
+                acc[rows] += g.square().mean(dim=1)
+                w[rows] -= lr * g / (acc[rows].sqrt() + self.eps).unsqueeze(1)
             self.grad_view(t.name)[rows] = 0.0
         self._cpu_touched.zero_()
         return norm
+
+    # ------------------------------------------------------------ replicas
+    def _row_elems(self, rows: torch.Tensor):
+        """Element index ``[n, max_dim]`` of each row-space index and its column mask."""
+
+        m = self.table_meta()
+        rb = m["t_row_base"].to(rows.device)
+        t = torch.searchsorted(rb, rows, right=True) - 1
+        dim = m["t_dim"].to(rows.device).long()[t]
+        base = m["t_base"].to(rows.device)[t] + (rows - rb[t]) * dim
+        col = torch.arange(self.max_dim, device=rows.device)
+        mask = col.view(1, -1) < dim.view(-1, 1)
+        idx = torch.where(mask, base.view(-1, 1) + col.view(1, -1), torch.zeros_like(base).view(-1, 1))
+        return idx, mask
+
+    def _touched_rows(self) -> torch.Tensor:
+        if self.device.type == "cuda":
+            return self.flags[:self.total_rows].nonzero().flatten()
+        return self._cpu_touched.nonzero().flatten()
+
+    def _sync_replicas(self) -> None:
+        """Sum the touched-row gradients of every replica into every replica (reference
+        ``_ReplicatedSparseGradientSynchronizer`` ``src/train.py:5026-5255``).
+
+        Rows and values are all-gathered (padded to the largest count); every rank then
+        reduces the same gathered data in the same order (rows sorted stably, each row's
+        contributions added in rank order), so the replicas stay bit-identical."""
+
+        W, group = self.replicas, self.replica_group
+        rows = self._touched_rows()
+        idx, mask = self._row_elems(rows)
+        vals = self.grad[idx] * mask
+        dev = rows.device
+        n = torch.tensor([rows.numel()], dtype=torch.int64, device=dev)
+        counts = [torch.zeros_like(n) for _ in range(W)]
+        dist.all_gather(counts, n, group=group)
+        cap = max(int(c.item()) for c in counts)
+        if cap == 0:
+            return
+        prow = torch.full((cap,), -1, dtype=torch.int64, device=dev)
+        prow[:rows.numel()] = rows
+        pval = torch.zeros(cap, self.max_dim, dtype=torch.float32, device=dev)
+        pval[:rows.numel()] = vals
+        all_rows = [torch.empty_like(prow) for _ in range(W)]
+        all_vals = [torch.empty_like(pval) for _ in range(W)]
+        dist.all_gather(all_rows, prow, group=group)
+        dist.all_gather(all_vals, pval, group=group)
+        r = torch.cat(all_rows)
+        v = torch.cat(all_vals)
+        keep = r >= 0
+        r, v = r[keep], v[keep]
+        r_sorted, order = torch.sort(r, stable=True)
+        v = v[order]
+        uniq, cnt = torch.unique_consecutive(r_sorted, return_counts=True)
+        starts = torch.cumsum(cnt, 0) - cnt
+        total = torch.zeros(uniq.numel(), self.max_dim, dtype=torch.float32, device=dev)
+        for k in range(W):
+            sel = cnt > k
+            total[sel] += v[starts[sel] + k]
+        uidx, umask = self._row_elems(uniq)
+        self.grad[uidx[umask]] = total[umask]
+        if self.device.type == "cuda":
+            self.flags[uniq] = 1
+        else:
+            self._cpu_touched[uniq] = True
 
     def state_dict(self) -> dict:
         return {

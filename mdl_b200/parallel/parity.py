@@ -30,7 +30,8 @@ from ..config import app_config_from_mapping
 
 
 def tiny_mapping(num_fields: int = 10, batch: int = 64, token_dim: int = 128, tokens: int = 4,
-                 optimizer: str = "adam") -> tuple[dict, object]:
+                 optimizer: str = "adam", distribution: str = "sharded",
+                 sparse_optimizer: str = "rowwise_adagrad") -> tuple[dict, object]:
     """A small RankMixer workload with row-wise and table-wise tables and multi-hot bags."""
 
     from ..data.baseline_configs import scaled_config
@@ -47,7 +48,8 @@ def tiny_mapping(num_fields: int = 10, batch: int = 64, token_dim: int = 128, to
                        "num_heads": 4})
     m["tokenization"]["num_feature_tokens"] = tokens
     m["training"].update({"dense_optimizer": optimizer, "lr_dense": 1e-3, "lr_sparse": 0.05, "lr_warmup_steps": 0,
-                          "adagrad_initial_accumulator_value": 0.1})
+                          "adagrad_initial_accumulator_value": 0.1, "embedding_distribution": distribution,
+                          "sparse_optimizer": sparse_optimizer, "adagrad_lr_decay": 0.01})
     return m, spec
 
 
@@ -96,14 +98,11 @@ def _setup(rank: int, world: int, backend: str, init_file: str, device_type: str
 
 
 def run_parity(rank: int, world: int, backend: str, device_type: str, init_file: str, out_path: str,
-               optimizer: str = "adam") -> None:
-    from ..data.synthetic import SyntheticGenerator
-    from ..models.factory import build_model
-    from ..train.trainer import Trainer
-
+               optimizer: str = "adam", distribution: str = "sharded", sparse_optimizer: str = "rowwise_adagrad",
+               ) -> None:
     _setup(rank, world, backend, init_file, device_type)
     try:
-        _run_parity_body(rank, world, device_type, out_path, optimizer)
+        _run_parity_body(rank, world, device_type, out_path, optimizer, distribution, sparse_optimizer)
     except BaseException:
         # A failed rank exits at once: tearing down a process group whose peers may
         # be blocked in a collective can itself block.
@@ -114,14 +113,16 @@ def run_parity(rank: int, world: int, backend: str, device_type: str, init_file:
     dist.destroy_process_group()
 
 
-def _run_parity_body(rank: int, world: int, device_type: str, out_path: str, optimizer: str) -> None:
+def _run_parity_body(rank: int, world: int, device_type: str, out_path: str, optimizer: str, distribution: str,
+                     sparse_optimizer: str) -> None:
     from ..data.synthetic import SyntheticGenerator
     from ..models.factory import build_model
     from ..train.trainer import Trainer
 
     if True:
         device = torch.device(device_type, rank) if device_type == "cuda" else torch.device("cpu")
-        mapping, spec = tiny_mapping(optimizer=optimizer)
+        mapping, spec = tiny_mapping(optimizer=optimizer, distribution=distribution,
+                                     sparse_optimizer=sparse_optimizer)
         cfg = app_config_from_mapping(mapping)
         B = cfg.training.batch_size
         torch.manual_seed(0)
@@ -142,6 +143,9 @@ def _run_parity_body(rank: int, world: int, device_type: str, out_path: str, opt
         dist.all_reduce(grads_dense)
         grads_dense /= world
         grad_tables = gather_tables(model.store, "grad")
+        if model.store.replicas > 1:  # every replica holds its own W-scaled contribution: sum them
+            for g in grad_tables.values():
+                dist.all_reduce(g)
         trainer.optimizer_step()
         if device.type == "cuda":
             torch.cuda.synchronize(device)

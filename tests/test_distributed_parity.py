@@ -16,10 +16,12 @@ import torch.multiprocessing as mp
 from mdl_b200.parallel.parity import run_parity
 
 
-def _run(tmp_path, world, backend, device_type, optimizer="adam"):
+def _run(tmp_path, world, backend, device_type, optimizer="adam", distribution="sharded",
+         sparse_optimizer="rowwise_adagrad"):
     init_file = str(tmp_path / "pg_init")
     out = str(tmp_path / "parity.json")
-    ctx = mp.start_processes(run_parity, args=(world, backend, device_type, init_file, out, optimizer),
+    ctx = mp.start_processes(run_parity, args=(world, backend, device_type, init_file, out, optimizer, distribution,
+                                               sparse_optimizer),
                              nprocs=world, join=False, start_method="spawn")
     deadline = time.monotonic() + 300
     while not ctx.join(timeout=5):
@@ -32,9 +34,12 @@ def _run(tmp_path, world, backend, device_type, optimizer="adam"):
         return json.load(fh)
 
 
-@pytest.mark.parametrize("optimizer", ["adam", "rmsprop"])
-def test_gloo_two_ranks_match_union_batch(tmp_path, optimizer):
-    r = _run(tmp_path, 2, "gloo", "cpu", optimizer)
+@pytest.mark.parametrize("optimizer,distribution,sparse", [("adam", "sharded", "rowwise_adagrad"),
+                                                           ("rmsprop", "sharded", "rowwise_adagrad"),
+                                                           ("adam", "sharded", "adagrad"),
+                                                           ("adam", "replicated", "adagrad")])
+def test_gloo_two_ranks_match_union_batch(tmp_path, optimizer, distribution, sparse):
+    r = _run(tmp_path, 2, "gloo", "cpu", optimizer, distribution, sparse)
     assert abs(r["loss"] - r["ref_loss"]) < 1e-5 * max(1.0, abs(r["ref_loss"]))
     assert r["dense_grad_rel"] < 1e-4, r
     assert r["table_grad_rel"] < 1e-4, r
@@ -44,11 +49,12 @@ def test_gloo_two_ranks_match_union_batch(tmp_path, optimizer):
 
 @pytest.mark.gpu
 @pytest.mark.multigpu
-def test_nccl_nvlink_two_gpus_match_union_batch(tmp_path):
+@pytest.mark.parametrize("distribution", [("sharded", "rowwise_adagrad"), ("replicated", "adagrad")])
+def test_nccl_nvlink_two_gpus_match_union_batch(tmp_path, distribution):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-    r = _run(tmp_path, 2, "nccl", "cuda", "adam")
+    r = _run(tmp_path, 2, "nccl", "cuda", "adam", *distribution)
     assert abs(r["loss"] - r["ref_loss"]) < 2e-2 * max(1.0, abs(r["ref_loss"])), r
     assert r["dense_grad_rel"] < 5e-2, r
     assert r["table_grad_rel"] < 5e-2, r
