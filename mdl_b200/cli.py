@@ -16,7 +16,6 @@ generator in the shapes of the config.
 from __future__ import annotations
 
 import argparse
-import datetime
 import json
 import os
 import subprocess
@@ -73,18 +72,38 @@ def _relaunch(args, argv) -> int | None:
 
 def _setup_runtime(config):
     import torch
-    import torch.distributed as dist
+
+    from .parallel.runtime import set_local_cpu_affinity, setup_distributed
 
     rank, world, local = _launched_world()
     use_cuda = torch.cuda.is_available() and config.runtime.device != "cpu"
     device = torch.device("cuda", local) if use_cuda else torch.device("cpu")
     if use_cuda:
         torch.cuda.set_device(device)
-    if world > 1 and not dist.is_initialized():
-        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        kw = {"device_id": device} if use_cuda else {}
-        dist.init_process_group("nccl" if use_cuda else "gloo", timeout=datetime.timedelta(minutes=10), **kw)
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
+    if local_world > 1:
+        set_local_cpu_affinity(local, local_world)
+    setup_distributed(device, timeout_s=600.0, local_world=local_world)
     return rank, world, device
+
+
+def load_external_adapter(dotted: str | None):
+    """``package.module:function`` or ``package.module.function`` (reference
+    ``_load_external_train_adapter`` ``src/train.py:1500-1520``)."""
+
+    import importlib
+
+    if not dotted:
+        raise ValueError("external parameter-server training needs training.sparse_parameter_server_adapter")
+    module, sep, attr = dotted.partition(":")
+    if not sep:
+        module, _, attr = dotted.rpartition(".")
+    if not module or not attr:
+        raise ValueError("sparse_parameter_server_adapter must be 'package.module:function' or 'package.module.function'")
+    fn = getattr(importlib.import_module(module), attr)
+    if not callable(fn):
+        raise TypeError(f"{dotted} is not callable")
+    return fn
 
 
 def _build(config, rank, world, device, seed=1234):
@@ -231,8 +250,18 @@ def cmd_train(args, argv) -> int:
     from .train.watchdog import StepWatchdog, abort_on_cuda_oom
 
     cfg = load_cli_config(args)
+    if cfg.training.sparse_update_mode == "external_parameter_server":
+        # the whole run is delegated to the configured adapter (reference src/train.py:6539-6542)
+        result = load_external_adapter(cfg.training.sparse_parameter_server_adapter)(config=cfg,
+                                                                                      max_steps=args.max_steps)
+        print(json.dumps({"done": True, "external": True, "result": repr(result)}), flush=True)
+        return 0
     rank, world, device = _setup_runtime(cfg)
     model, trainer = _build(cfg, rank, world, device)
+    if world > 1:
+        from .parallel.runtime import validate_shard_metadata
+
+        validate_shard_metadata(model.store)
     run = open_checkpoint_store(args.checkpoint_dir) if args.checkpoint_dir else None
     start = 0
     if run is not None:

@@ -1,0 +1,103 @@
+"""Distributed runtime helpers: backend choice, NCCL environment policy, CPU shares,
+shard-metadata agreement (gloo ranks), gradient auditor, host memory tools and the
+external parameter-server hook."""
+
+import json
+import os
+import time
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from mdl_b200.parallel import runtime
+from mdl_b200.utils import hostmem
+
+
+def test_backend_and_nccl_env(monkeypatch):
+    monkeypatch.delenv("MDL_DIST_BACKEND", raising=False)
+    assert runtime.resolve_backend(torch.device("cpu")) == "gloo"
+    assert runtime.resolve_backend(torch.device("cuda", 0)) == "nccl"
+    monkeypatch.setenv("MDL_DIST_BACKEND", "gloo")
+    assert runtime.resolve_backend(torch.device("cuda", 0)) == "gloo"
+    env = {"TORCH_NCCL_ASYNC_ERROR_HANDLING": "0"}
+    applied = runtime.configure_nccl_env(8, env=env, p2p_ok=False)
+    assert env["TORCH_NCCL_ASYNC_ERROR_HANDLING"] == "0"      # the user's choice stays
+    assert applied == {"NCCL_P2P_DISABLE": "1"}
+    env = {}
+    runtime.configure_nccl_env(8, env=env, p2p_ok=True)
+    assert env == {"TORCH_NCCL_ASYNC_ERROR_HANDLING": "1"}
+
+
+def test_cpu_shares_cover_all_cores_once():
+    cpus = list(range(26))
+    shares = [runtime.set_local_cpu_affinity(r, 4, cpus, apply=False) for r in range(4)]
+    assert sorted(c for s in shares for c in s) == cpus
+    assert [len(s) for s in shares] == [6, 6, 6, 8]
+
+
+def _meta_rank(rank, world, init_file, out_dir, mismatch):
+    import torch.distributed as dist
+
+    from mdl_b200.ops.embedding import EmbeddingStore
+    from mdl_b200.parallel.sharding import EmbeddingTableSpec, plan_embedding_shards
+
+    dist.init_process_group("gloo", init_method=f"file://{init_file}", rank=rank, world_size=world)
+    rows = 100 + (7 if (mismatch and rank == 1) else 0)
+    plan = plan_embedding_shards([EmbeddingTableSpec("t", rows, 8, 4)], world_size=world, strategy="row_wise",
+                                 table_wise_max_rows=0)
+    store = EmbeddingStore([("t", rows, 8)], plan, rank=rank, world=world, device="cpu", process_group=None)
+    try:
+        runtime.validate_shard_metadata(store)
+        ok = True
+    except RuntimeError:
+        ok = False
+    with open(os.path.join(out_dir, f"r{rank}.json"), "w") as fh:
+        json.dump({"ok": ok}, fh)
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("mismatch", [False, True])
+def test_shard_metadata_agreement(tmp_path, mismatch):
+    ctx = mp.start_processes(_meta_rank, args=(2, str(tmp_path / "pg"), str(tmp_path), mismatch), nprocs=2,
+                             join=False, start_method="spawn")
+    deadline = time.monotonic() + 120
+    while not ctx.join(timeout=2):
+        assert time.monotonic() < deadline, "ranks did not finish"
+    res = [json.load(open(tmp_path / f"r{r}.json"))["ok"] for r in range(2)]
+    assert res == [not mismatch] * 2
+
+
+def test_gradient_auditor_flags_unused_parameters():
+    class FakeDense:
+        names = ["a", "b"]
+        offsets = {"a": 0, "b": 4}
+        params = {"a": torch.zeros(4), "b": torch.zeros(4)}
+        grad = torch.zeros(8)
+
+    d = FakeDense()
+    aud = runtime.GradientAuditor(d, steps=2)
+    d.grad[:4] = 1.0
+    aud.observe()
+    aud.observe()
+    rep = aud.report()
+    assert rep["never_updated"] == ["b"] and rep["static_graph_safe"]
+
+
+def test_host_memory_tools():
+    assert hostmem.process_resident_bytes() > 0
+    assert isinstance(hostmem.trim_process_heap(), bool)
+    assert hostmem.arrow_pool_bytes() >= 0
+
+
+def test_external_parameter_server_hook(capsys):
+    from mdl_b200.cli import load_external_adapter, main
+
+    assert load_external_adapter("builtins:dict")(config=1, max_steps=2) == {"config": 1, "max_steps": 2}
+    with pytest.raises(ValueError):
+        load_external_adapter("nodots")
+    rc = main(["train", "--benchmark-config", "1", "--max-steps", "3",
+               "--set", "training.sparse_update_mode=external_parameter_server",
+               "--set", "training.sparse_parameter_server_adapter=builtins.dict"])
+    assert rc == 0
+    assert '"external": true' in capsys.readouterr().out
