@@ -101,3 +101,17 @@ def test_external_parameter_server_hook(capsys):
                "--set", "training.sparse_parameter_server_adapter=builtins.dict"])
     assert rc == 0
     assert '"external": true' in capsys.readouterr().out
+
+
+def test_benchmark_matrix_summary_and_commands():
+    from mdl_b200.benchmark.matrix import bench_command, summarize
+
+    rows = [{"matrix_config": 2, "matrix_gpus": 1, "impl": "ours", "value": 100.0},
+            {"matrix_config": 2, "matrix_gpus": 2, "impl": "ours", "value": 180.0},
+            {"matrix_config": 2, "matrix_gpus": 1, "impl": "reference", "value": 10.0},
+            {"matrix_config": 2, "matrix_gpus": 2, "impl": "ours", "error": "exit 1"}]
+    text = summarize(rows)
+    assert "| 2 | ours | 2 | 180 | 90 | 0.900 | - |" in text
+    assert "| 2 | ours | 1 | 100 | 100 | 1.000 | 10.00 |" in text
+    cmd = bench_command(4, 4, "ours", 10, 3, 29999)
+    assert "--nproc-per-node=4" in cmd and "--master-addr=127.0.0.1" in cmd and cmd[-1] == "ours"
