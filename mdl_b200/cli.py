@@ -270,6 +270,9 @@ def cmd_train(args, argv) -> int:
             start = state.step
     source = _batches(cfg, model, rank, world, synthetic=args.synthetic)
     batches = iter(source)
+    from .train.fixed_eval import FixedTestEval
+
+    fixed = FixedTestEval(cfg, trainer, rank=rank, world=world)
     dog = StepWatchdog(cfg.training.step_watchdog_sec if args.watchdog_sec is None else args.watchdog_sec).start()
     t0 = time.time()
     last = None
@@ -285,6 +288,11 @@ def cmd_train(args, argv) -> int:
             if step % args.log_every == 0 and rank == 0:
                 last = float(res.loss)
                 print(json.dumps({"step": step, "loss": last, "elapsed_s": round(time.time() - t0, 2)}), flush=True)
+            if fixed.due(step):
+                dog.beat("fixed_test_eval", step)
+                ev = fixed.run(model)
+                if rank == 0:
+                    print(json.dumps({"step": step, "fixed_test_eval": ev}), flush=True)
             if run is not None and args.save_every and step % args.save_every == 0:
                 save_training_checkpoint(cfg, trainer, run, step, keep_last=args.keep_last)
     finally:

@@ -95,3 +95,17 @@ def test_cli_train_checkpoint_evaluate_predict(tmp_path):
     assert pr["rows"] == 256 and t.num_rows == 256 and "pred_click" in t.column_names
     st = _run("check-checkpoint-store", "--checkpoint-dir", str(run))[-1]
     assert st["round_trip_ok"] and st["resume_from"] == "step-000000008"
+
+
+def test_cli_fixed_test_eval_during_training(tmp_path):
+    data = tmp_path / "data"
+    _run("make-synthetic-parquet", "--benchmark", "1", "--files", "2", "--rows", "384", "--out", str(data))
+    over = ["--benchmark-config", "1", "--set", f"data.train.inputs=[{str(data)}]",
+            "--set", f"data.test.inputs=[{str(data)}]", "--set", "training.batch_size=128",
+            "--set", "training.fixed_test_eval.enabled=true", "--set", "training.fixed_test_eval.every_steps=2",
+            "--set", "training.fixed_test_eval.files_per_rank=1"]
+    logs = _run("train", *over, "--max-steps", "4", "--log-every", "10")
+    evals = [l for l in logs if "fixed_test_eval" in l]
+    assert [l["step"] for l in evals] == [2, 4]
+    ev = evals[-1]["fixed_test_eval"]
+    assert ev["batches"] == 3 and 0.0 <= ev["tasks"]["click"]["auc"] <= 1.0
