@@ -87,6 +87,12 @@ def _setup_runtime(config):
     return rank, world, device
 
 
+def _resolve_scenarios(cfg, rank, world):
+    from .data.scenarios import resolve_auto_scenarios_distributed
+
+    return resolve_auto_scenarios_distributed(cfg, rank, world)
+
+
 def load_external_adapter(dotted: str | None):
     """``package.module:function`` or ``package.module.function`` (reference
     ``_load_external_train_adapter`` ``src/train.py:1500-1520``)."""
@@ -257,6 +263,7 @@ def cmd_train(args, argv) -> int:
         print(json.dumps({"done": True, "external": True, "result": repr(result)}), flush=True)
         return 0
     rank, world, device = _setup_runtime(cfg)
+    cfg = _resolve_scenarios(cfg, rank, world)
     model, trainer = _build(cfg, rank, world, device)
     if world > 1:
         from .parallel.runtime import validate_shard_metadata
@@ -316,6 +323,7 @@ def cmd_benchmark(args, argv) -> int:
 
     cfg = load_cli_config(args)
     rank, world, device = _setup_runtime(cfg)
+    cfg = _resolve_scenarios(cfg, rank, world)
     model, trainer = _build(cfg, rank, world, device)
     it = _batches(cfg, model, rank, world, synthetic=True)
     pool = [next(it) for _ in range(3)]
@@ -362,6 +370,7 @@ def _eval_setup(args, argv):
 
     cfg = load_cli_config(args)
     rank, world, device = _setup_runtime(cfg)
+    cfg = _resolve_scenarios(cfg, rank, world)
     model, trainer = _build(cfg, rank, world, device)
     if args.checkpoint:
         store = open_checkpoint_store(args.checkpoint)

@@ -343,7 +343,8 @@ class ScenarioConfig:
     source: str | None = None
     source_encoding: Literal["auto", "raw", "index"] = "auto"
     auto_discover: bool = False
-    max_discovered: int | None = None
+    max_discovered: int = 256
+    discovery_cache_path: str | None = None
 
 
 @_frozen
