@@ -83,8 +83,12 @@ def _setup_runtime(config):
     local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
     if local_world > 1:
         set_local_cpu_affinity(local, local_world)
-    setup_distributed(device, timeout_s=600.0, local_world=local_world)
+    global _RUNTIME
+    _RUNTIME = setup_distributed(device, timeout_s=600.0, local_world=local_world)
     return rank, world, device
+
+
+_RUNTIME = None
 
 
 def _resolve_scenarios(cfg, rank, world):
@@ -284,9 +288,37 @@ def cmd_train(args, argv) -> int:
     t0 = time.time()
     last = None
     step = start
+    # several ranks on finite data: every step votes on the batch supply (train / replay / retry / stop)
+    from .train.supply import BATCH_NOT_READY, BudgetedIterator, start_supply_count, supply_verdict, zero_weight
+
+    voting = world > 1 and not args.synthetic
+    if voting:
+        batches = BudgetedIterator(batches)
+    control = _RUNTIME.control_group if _RUNTIME is not None else None
+    last_batch = None
     try:
         while step < args.max_steps:
-            batch = next(batches)
+            if voting:
+                try:
+                    batch = batches.next_within(args.batch_budget_sec)
+                    exhausted = False
+                except StopIteration:
+                    batch, exhausted = BATCH_NOT_READY, True
+                has = batch is not BATCH_NOT_READY
+                active, done = start_supply_count(has, exhausted, world, control).wait()
+                verdict = supply_verdict(has, active, done, world)
+                if verdict == "stop":
+                    break
+                if verdict == "retry":
+                    dog.beat("batch_retry", step)
+                    continue
+                if verdict == "replay":
+                    if last_batch is None:
+                        raise RuntimeError(f"rank {rank} has no training data while its peers train")
+                    batch = zero_weight(last_batch)
+                last_batch = batch
+            else:
+                batch = next(batches)
             if device.type == "cuda":
                 batch = batch.to(device, non_blocking=True)
             res = abort_on_cuda_oom(trainer.train_step, batch)
@@ -304,6 +336,8 @@ def cmd_train(args, argv) -> int:
                 save_training_checkpoint(cfg, trainer, run, step, keep_last=args.keep_last)
     finally:
         dog.stop()
+        if voting:
+            batches.close()
         _close(source)
     if run is not None:
         save_training_checkpoint(cfg, trainer, run, step, keep_last=args.keep_last)
@@ -475,6 +509,8 @@ def build_parser() -> argparse.ArgumentParser:
             p.add_argument("--keep-last", type=int, default=3)
             p.add_argument("--log-every", type=int, default=10)
             p.add_argument("--watchdog-sec", type=float, default=None)
+            p.add_argument("--batch-budget-sec", type=float, default=30.0,
+                           help="several ranks: seconds to wait for a batch before voting 'not ready'")
         if name == "benchmark":
             p.add_argument("--steps", type=int, default=20)
             p.add_argument("--warmup", type=int, default=5)

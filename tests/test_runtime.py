@@ -115,3 +115,51 @@ def test_benchmark_matrix_summary_and_commands():
     assert "| 2 | ours | 1 | 100 | 100 | 1.000 | 10.00 |" in text
     cmd = bench_command(4, 4, "ours", 10, 3, 29999)
     assert "--nproc-per-node=4" in cmd and "--master-addr=127.0.0.1" in cmd and cmd[-1] == "ours"
+
+
+def test_supply_iterator_and_verdicts():
+    import threading
+
+    from mdl_b200.train.supply import BATCH_NOT_READY, BudgetedIterator, supply_verdict
+
+    gate = threading.Event()
+
+    def slow():
+        yield 1
+        gate.wait(5)
+        yield 2
+
+    it = BudgetedIterator(slow())
+    assert it.next_within(2.0) == 1
+    assert it.next_within(0.05) is BATCH_NOT_READY
+    gate.set()
+    assert it.next_within(2.0) == 2
+    with pytest.raises(StopIteration):
+        it.next_within(2.0)
+    with pytest.raises(StopIteration):
+        it.next_within(2.0)
+    assert supply_verdict(True, 1, 1, 2) == "train"
+    assert supply_verdict(False, 1, 1, 2) == "replay"
+    assert supply_verdict(False, 0, 1, 2) == "retry"
+    assert supply_verdict(False, 0, 2, 2) == "stop"
+
+
+def _vote_rank(rank, world, init_file, out_dir):
+    import torch.distributed as dist
+
+    from mdl_b200.train.supply import start_supply_count
+
+    dist.init_process_group("gloo", init_method=f"file://{init_file}", rank=rank, world_size=world)
+    got = start_supply_count(rank == 0, rank == 1, world).wait()
+    with open(os.path.join(out_dir, f"v{rank}.json"), "w") as fh:
+        json.dump(list(got), fh)
+    dist.destroy_process_group()
+
+
+def test_supply_vote_over_gloo(tmp_path):
+    ctx = mp.start_processes(_vote_rank, args=(2, str(tmp_path / "pg"), str(tmp_path)), nprocs=2, join=False,
+                             start_method="spawn")
+    deadline = time.monotonic() + 120
+    while not ctx.join(timeout=2):
+        assert time.monotonic() < deadline
+    assert [json.load(open(tmp_path / f"v{r}.json")) for r in range(2)] == [[1, 1], [1, 1]]
