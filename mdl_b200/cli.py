@@ -157,9 +157,12 @@ def _batches(config, model, rank, world, *, split="train", synthetic=False, batc
 
 # ------------------------------------------------------------------ commands
 def cmd_validate(args) -> int:
+    from .ops.preflight import attention_preflight
+
     cfg = load_cli_config(args)
     res = cfg.resolved.tokenization
     print(json.dumps({"valid": True, "model": cfg.model.name, "features": len(cfg.features),
+                      "attention": attention_preflight(cfg)["paths"],
                       "feature_token_inputs": len(res.feature_token_inputs),
                       "feature_tokens": res.feature_token_count, "scenario_tokens": len(res.scenario_token_specs),
                       "task_tokens": len(res.task_token_specs), "tasks": list(cfg.task_names)}))
@@ -266,8 +269,12 @@ def cmd_train(args, argv) -> int:
                                                                                       max_steps=args.max_steps)
         print(json.dumps({"done": True, "external": True, "result": repr(result)}), flush=True)
         return 0
+    from .ops.preflight import attention_preflight
+
+    attention_preflight(cfg)  # before the runtime and any data scan
     rank, world, device = _setup_runtime(cfg)
     cfg = _resolve_scenarios(cfg, rank, world)
+    attention_preflight(cfg, device)
     model, trainer = _build(cfg, rank, world, device)
     if world > 1:
         from .parallel.runtime import validate_shard_metadata

@@ -163,3 +163,18 @@ def test_supply_vote_over_gloo(tmp_path):
     while not ctx.join(timeout=2):
         assert time.monotonic() < deadline
     assert [json.load(open(tmp_path / f"v{r}.json")) for r in range(2)] == [[1, 1], [1, 1]]
+
+
+def test_attention_preflight():
+    from mdl_b200.config import app_config_from_mapping
+    from mdl_b200.data.baseline_configs import scaled_config
+    from mdl_b200.ops.preflight import attention_preflight
+
+    m, _ = scaled_config(4, 1e-3, num_fields=8, batch=8)
+    assert "flash" in attention_preflight(app_config_from_mapping(m))["paths"]["mixed_causal"]
+    m["model"]["num_heads"] = 4           # d=256 / 4 heads = head_dim 64
+    with pytest.raises(ValueError, match="head_dim 32"):
+        attention_preflight(app_config_from_mapping(m))
+    m, _ = scaled_config(5, 1e-3, num_fields=8, batch=8, seq_len=64, min_len=8, query_tokens=16)
+    paths = attention_preflight(app_config_from_mapping(m))["paths"]
+    assert "longer:behavior" in paths and "mixformer_cross" in paths
