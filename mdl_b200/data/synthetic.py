@@ -49,6 +49,9 @@ class SequenceSpec:
     max_len: int
     min_len: int | None = None       # None: every row is full length
     dense_width: int = 0
+    # request-level batching: consecutive groups of this many candidate rows share one
+    # request's sequence, stored once per request with ``row_indices`` (candidate -> request)
+    candidates_per_request: int = 1
 
 
 @dataclass
@@ -172,6 +175,9 @@ class SyntheticGenerator:
         for name, ss in (spec.sequences or {}).items():
             L = ss.max_len
             lo = ss.min_len if ss.min_len is not None else L
+            cpr = max(1, int(ss.candidates_per_request))
+            cand_rows = rows
+            rows = (cand_rows + cpr - 1) // cpr        # request rows
             lengths = rng.integers(lo, L + 1, size=rows, dtype=np.int64) if lo < L else np.full(rows, L, np.int64)
             valid = np.arange(L)[None, :] >= (L - lengths)[:, None]          # prefix padding
             ids = np.zeros((len(ss.fields), rows, L), dtype=np.int64)
@@ -184,12 +190,15 @@ class SyntheticGenerator:
                 if k == 0:  # mean score of the valid events of the first field
                     sc = _id_score(ids[k].reshape(-1), int.from_bytes(sha256(key.encode()).digest()[:4], "little"))
                     sc = (sc.reshape(rows, L) * valid).sum(1) / np.maximum(lengths, 1)
-                    scores.append(sc * 2.0)
+                    scores.append(np.repeat(sc, cpr)[:cand_rows] * 2.0)
             seq = {"ids": torch.from_numpy(ids.reshape(len(ss.fields), rows * L)),
                    "lengths": torch.from_numpy(lengths)}
             if ss.dense_width:
                 seq["dense"] = torch.from_numpy(rng.standard_normal((rows * L, ss.dense_width)).astype(np.float32))
+            if cpr > 1:
+                seq["row_indices"] = torch.arange(cand_rows, dtype=torch.int64) // cpr
             sequences[name] = seq
+            rows = cand_rows
         per_field = np.stack(scores, axis=1) if scores else np.zeros((rows, 0))
         logits = self._calibrate(self._truth_logits(per_field, dense.astype(np.float64), scen))
         probs = 1.0 / (1.0 + np.exp(-logits))

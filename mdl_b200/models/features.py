@@ -174,6 +174,7 @@ class FeatureEncoder:
         self.batch_plan = LookupPlan([make(n, 0) for n in batch_names], out_width=0, dense_width=dense_total)
         # Raw event sequences (OneTrans S tokens): one plan per sequence whose rows are the
         # events (rows * max_length), categorical fields first, then dense fields.
+        self._seq_offsets: dict = {}  # per (sequence, rows) CSR offsets of the one-id-per-event lookups
         self.seq_plans: dict[str, LookupPlan] = {}
         self.seq_fields: dict[str, list[str]] = {}
         self.seq_dense_fields: dict[str, list[str]] = {}
@@ -243,3 +244,32 @@ class FeatureEncoder:
     @property
     def slice_stride(self) -> int:
         return self.plan.slice_stride
+
+
+def lookup_sequence(encoder: FeatureEncoder, batch, name: str, rows: int, max_len: int, anchor: torch.Tensor):
+    """Event rows ``[rows * max_len, out_ld]`` of sequence ``name`` and its lengths ``[rows]``.
+
+    With request-level batching (``row_indices`` in the sequence payload, reference
+    ``_batch_gather_indexed_rows`` ``src/model.py:701-750``) the events are looked up
+    once per request (``R * max_len`` rows) and each candidate row then takes its
+    request's rows (``index_select``; its backward sums the candidates of a request)."""
+
+    from ..ops.embedding import fused_lookup
+
+    seq = batch.sequences[name]
+    ids = seq["ids"].reshape(-1)
+    lengths = seq["lengths"]
+    R = lengths.numel()
+    nf = len(encoder.seq_fields[name])
+    key = (name, R, max_len, str(ids.device))
+    cache = encoder._seq_offsets
+    if key not in cache:
+        cache.clear()
+        cache[key] = torch.arange(nf * R * max_len + 1, dtype=torch.int64, device=ids.device)
+    x = fused_lookup(encoder.store, encoder.seq_plans[name], ids, cache[key], seq.get("dense"), R * max_len, anchor)
+    ri = seq.get("row_indices")
+    if ri is None:
+        return x, lengths
+    ri = ri.to(x.device)
+    x = x.view(R, max_len * x.shape[1]).index_select(0, ri).view(rows * max_len, x.shape[1])
+    return x, lengths.index_select(0, ri.to(lengths.device))

@@ -358,15 +358,6 @@ class LongerModel(nn.Module):
     def store(self):
         return self.encoder.store
 
-    def _seq_offsets(self, rows: int, device) -> torch.Tensor:
-        key = (rows, str(device))
-        cache = getattr(self, "_offsets_cache", None)
-        if cache is None or cache[0] != key:
-            n = len(self.encoder.seq_fields[self.seq.name]) * rows
-            cache = (key, torch.arange(n + 1, dtype=torch.int64, device=device))
-            self._offsets_cache = cache
-        return cache[1]
-
     def encode(self, batch):
         """LONGER output ``[B, R + G, d]`` (token order ``[recent; globals]``), the
         event validity of those tokens, the scalar-feature matrix (MixFormer head)."""
@@ -375,11 +366,10 @@ class LongerModel(nn.Module):
 
         native = batch.ids.is_cuda and self.config.runtime.kernel_backend == "native"
         anchor = torch.zeros(0, device=batch.ids.device, requires_grad=True)
-        seq = batch.sequences[self.seq.name]
+        from .features import lookup_sequence
+
         B, L = batch.rows, self.longer.L
-        ids = seq["ids"].reshape(-1)
-        seq_in = fused_lookup(self.store, self.encoder.seq_plans[self.seq.name], ids, self._seq_offsets(B * L, ids.device),
-                              seq.get("dense"), B * L, anchor)
+        seq_in, lengths = lookup_sequence(self.encoder, batch, self.seq.name, B, L, anchor)
         target_in = user_in = None
         if self.has_target or self.has_user:
             g = fused_lookup(self.store, self.encoder.domain_plan, batch.ids, batch.offsets, batch.dense, B, anchor)
@@ -388,7 +378,6 @@ class LongerModel(nn.Module):
             user_in = g[:, (kp if self.has_target else 0):][:, :kp] if self.has_user else None
         feat_in = (fused_lookup(self.store, self.encoder.plan, batch.ids, batch.offsets, batch.dense, B, anchor)
                    if self.mix else None)
-        lengths = seq["lengths"]
         X = self.longer(seq_in, lengths, target_in, user_in, native)
         R, G = self.longer.R, self.longer.G
         e = torch.arange(R + G, device=X.device)

@@ -254,17 +254,12 @@ class MixFormerModel(nn.Module):
         """Scalar inputs ``[B, K]``, event tokens ``[B, L, N * D]`` and their validity ``[B, L]``."""
 
         from ..ops.embedding import fused_lookup
+        from .features import lookup_sequence
 
-        seq = batch.sequences[self.seq.name]
         B, L = batch.rows, self.L
-        ids = seq["ids"].reshape(-1)
-        n = len(self.encoder.seq_fields[self.seq.name]) * B * L
-        offsets = torch.arange(n + 1, dtype=torch.int64, device=ids.device)
-        seq_in = fused_lookup(self.store, self.encoder.seq_plans[self.seq.name], ids, offsets, seq.get("dense"), B * L,
-                              anchor)
+        seq_in, lengths = lookup_sequence(self.encoder, batch, self.seq.name, B, L, anchor)
         feat_in = fused_lookup(self.store, self.encoder.plan, batch.ids, batch.offsets, batch.dense, B, anchor)
         tokens = self.step(seq_in, native).view(B, L, self.N * self.D)
-        lengths = seq["lengths"]
         e = torch.arange(L, device=tokens.device)
         valid = e.view(1, -1) >= (L - lengths.clamp(0, L)).view(-1, 1)
         return feat_in, tokens, valid

@@ -494,26 +494,13 @@ class OneTransModel(nn.Module):
         return self.encoder.store
 
     # ------------------------------------------------------------------ inputs
-    def _seq_offsets(self, rows: int, device) -> torch.Tensor:
-        key = (rows, str(device))
-        cache = getattr(self, "_offsets_cache", None)
-        if cache is None or cache[0] != key:
-            n = len(self.encoder.seq_fields[self.seq.name]) * rows
-            cache = (key, torch.arange(n + 1, dtype=torch.int64, device=device))
-            self._offsets_cache = cache
-        return cache[1]
-
     def _inputs(self, batch, anchor):
         from ..ops.embedding import fused_lookup
+        from .features import lookup_sequence
 
-        seq = batch.sequences[self.seq.name]
         B, L = batch.rows, self.L
-        lengths = seq["lengths"].to(torch.int64)
-        kstart = (L - lengths.clamp(0, L)).to(torch.int32)
-        plan = self.encoder.seq_plans[self.seq.name]
-        ids = seq["ids"].reshape(-1)
-        seq_in = fused_lookup(self.store, plan, ids, self._seq_offsets(B * L, ids.device), seq.get("dense"), B * L,
-                              anchor)
+        seq_in, lengths = lookup_sequence(self.encoder, batch, self.seq.name, B, L, anchor)
+        kstart = (L - lengths.to(torch.int64).clamp(0, L)).to(torch.int32)
         if self.ns_mode == "groupwise":
             ns_in = fused_lookup(self.store, self.encoder.domain_plan, batch.ids, batch.offsets, batch.dense, B, anchor)
         else:

@@ -185,6 +185,7 @@ class RankMixerModel(nn.Module):
         """STCA summary tokens of the encoded sequences into their tokenizer columns."""
 
         from ..ops.embedding import fused_lookup
+        from .features import lookup_sequence
 
         native = batch.ids.is_cuda and self.config.runtime.kernel_backend == "native"
         B = batch.rows
@@ -192,16 +193,11 @@ class RankMixerModel(nn.Module):
         kp = self.encoder.domain_k_pad
         for name, mod in self.stca.items():
             cols, ti, L = self._stca_meta[name]
-            seq = batch.sequences[name]
-            ids = seq["ids"].reshape(-1)
-            nf = len(self.encoder.seq_fields[name])
-            offsets = torch.arange(nf * B * L + 1, dtype=torch.int64, device=ids.device)
-            seq_in = fused_lookup(self.store, self.encoder.seq_plans[name], ids, offsets, seq.get("dense"), B * L,
-                                  anchor)
+            seq_in, lengths = lookup_sequence(self.encoder, batch, name, B, L, anchor)
             hist = mod.step(seq_in, native).view(B, L, -1)
             target = mod.target(targets[:, ti * kp:(ti + 1) * kp], native)
             e = torch.arange(L, device=hist.device)
-            valid = e.view(1, -1) >= (L - seq["lengths"].clamp(0, L)).view(-1, 1)
+            valid = e.view(1, -1) >= (L - lengths.clamp(0, L)).view(-1, 1)
             z = mod.encoder(hist, valid, target, native)
             x0 = x0.index_add(1, cols.to(x0.device), z.to(x0.dtype))
         return x0

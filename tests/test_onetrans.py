@@ -255,3 +255,48 @@ def test_task_query_readout_trains():
     m["model"]["readout"] = "task_query"
     with pytest.raises(Exception, match="task_query"):
         app_config_from_mapping(m)
+
+
+# ----------------------------------------------------------------------------- request-level batching
+@pytest.mark.parametrize("make", ["onetrans", "longer", "mixformer"])
+def test_request_level_sequences_match_expanded_rows(make):
+    """Sequences stored once per request (``row_indices``) give the same loss and
+    gradients as the same sequences repeated on every candidate row."""
+
+    import copy
+
+    from mdl_b200.data.batch import PackedBatch
+
+    if make == "onetrans":
+        cfg, spec = _small(layers=2)
+    elif make == "longer":
+        from tests.test_longer_mixformer import _longer
+
+        cfg, spec = _longer("mixformer")
+    else:
+        from tests.test_longer_mixformer import _mixformer
+
+        cfg, spec = _mixformer()
+    spec = copy.deepcopy(spec)
+    spec.sequences["behavior"].candidates_per_request = 4
+    torch.manual_seed(0)
+    model = build_model(cfg, device="cpu", base_seed=1)
+    tr = Trainer(cfg, model, device=torch.device("cpu"))
+    b = SyntheticGenerator(model.encoder.batch_plan, spec).batch(64)
+    seq = b.sequences["behavior"]
+    assert seq["lengths"].numel() == 16 and seq["row_indices"].numel() == 64
+    ri = seq["row_indices"]
+    L = cfg.sequences[0].max_length
+    ids = seq["ids"].view(seq["ids"].shape[0], 16, L)[:, ri].reshape(seq["ids"].shape[0], 64 * L)
+    flat = {"ids": ids.clone(), "lengths": seq["lengths"][ri].clone()}
+    expanded = PackedBatch.pack(b.ids, b.offsets, b.dense, b.labels, b.label_mask, b.scenario_id, b.rows,
+                                sequences={"behavior": flat})
+    out_r = tr.forward_backward(b)
+    g_r = tr.dense.grad.clone()
+    e_r = model.store.grad.clone()
+    tr.dense.grad.zero_()
+    model.store.grad.zero_()
+    out_e = tr.forward_backward(expanded)
+    torch.testing.assert_close(out_r["loss"], out_e["loss"])
+    torch.testing.assert_close(g_r, tr.dense.grad, atol=1e-6, rtol=1e-4)
+    torch.testing.assert_close(e_r, model.store.grad, atol=1e-6, rtol=1e-4)
