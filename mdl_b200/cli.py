@@ -238,6 +238,17 @@ def cmd_fit_vocab(args) -> int:
     return 0
 
 
+def cmd_audit_cardinality(args) -> int:
+    from .data.audit import audit_cardinality
+    from .data.parquet import discover_parquet_inputs
+
+    cfg = load_cli_config(args)
+    sp = getattr(cfg.data, args.split) or cfg.data.train
+    out = audit_cardinality(cfg, discover_parquet_inputs(args.inputs or sp.inputs), max_rows=args.max_rows)
+    print(json.dumps(out))
+    return 0 if out["passed"] or not args.strict else 3
+
+
 def cmd_check_store(args) -> int:
     from .checkpoint import latest_committed_checkpoint, open_checkpoint_store
 
@@ -499,6 +510,12 @@ def build_parser() -> argparse.ArgumentParser:
     _add_config(p)
     p.add_argument("--inputs", nargs="*")
     p.add_argument("--out", required=True)
+    p = sub.add_parser("audit-cardinality")
+    _add_config(p)
+    p.add_argument("--split", choices=["train", "test"], default="train")
+    p.add_argument("--inputs", nargs="*")
+    p.add_argument("--max-rows", type=int, default=100_000)
+    p.add_argument("--strict", action="store_true", help="exit 3 when a single-value feature holds lists")
     p = sub.add_parser("check-checkpoint-store")
     p.add_argument("--checkpoint-dir", required=True)
     p.add_argument("--probe-mib", type=int, default=8)
@@ -549,6 +566,8 @@ def main(argv=None) -> int:
         return cmd_fit_vocab(args)
     if cmd == "check-checkpoint-store":
         return cmd_check_store(args)
+    if cmd == "audit-cardinality":
+        return cmd_audit_cardinality(args)
     if cmd == "train":
         return cmd_train(args, argv)
     if cmd == "benchmark":

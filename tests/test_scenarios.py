@@ -55,3 +55,21 @@ def test_mdl_template_expansion(tmp_path):
     assert toks["7"].prior_inputs == ("scenario_7_prior_scene_id_hn",)
     with pytest.raises(ValueError):
         resolve_auto_scenarios(cfg, [1, 1])
+
+
+def test_cardinality_audit_reports_scalar_multis(tmp_path):
+    from mdl_b200.data.audit import audit_cardinality
+
+    m, _ = baseline_config(1)
+    cfg = app_config_from_mapping(m)
+    cats = [f for f in cfg.features if f.kind == "categorical"]
+    single, other = cats[0], cats[1]
+    path = tmp_path / "x.parquet"
+    pq.write_table(pa.table({single.source or single.name: pa.array([[1], [2, 3], None, [4, 5, 6]]),
+                             other.source or other.name: pa.array([7, 8, 9, 10])}), path)
+    out = audit_cardinality(cfg, [str(path)])
+    st = out["scalar_stats"][single.name]
+    assert out["raw_rows_seen"] == 4 and st["multi_rows"] == 2 and st["nulls"] == 1 and st["max_len"] == 3
+    assert st["samples"] == [[2, 3], [4, 5, 6]]
+    assert out["scalar_multis"] == [single.name] and not out["passed"]
+    assert out["scalar_stats"][other.name]["multi_rows"] == 0
