@@ -141,6 +141,16 @@ def _batches(config, model, rank, world, *, split="train", synthetic=False, batc
     if not synthetic and sp.inputs:
         paths = discover_parquet_inputs(sp.inputs)
         r = sp.reader
+        if r.host_prepare_prefetch > 0:
+            # tensorisation in a spawned child, batches handed over in shared memory
+            from .config.schema import thaw
+            from .data.prepare_process import ProcessBatchIterator, parquet_batches
+
+            args = (thaw(config), model.encoder.batch_plan, paths, rows, rank, world, split,
+                    loop and split == "train", r.shuffle_buffer_rows, r.shuffle_seed)
+            return ProcessBatchIterator(parquet_batches, args, depth=r.host_prepare_prefetch, pin=r.pin_memory,
+                                        startup_timeout_s=r.host_prepare_startup_timeout_sec,
+                                        idle_timeout_s=r.host_prepare_idle_timeout_sec)
         return ParquetBatchIterator(paths, Tensorizer(config, model.encoder.batch_plan, split=split), rows, rank=rank,
                                     world=world, shard_unit=r.shard_unit, shuffle_rows=r.shuffle_buffer_rows,
                                     seed=r.shuffle_seed, prefetch=r.prefetch_batches, loop=loop and split == "train",

@@ -90,3 +90,55 @@ def test_train_from_parquet(tmp_path):
     losses = [float(tr.train_step(b).loss) for b in it]
     assert len(losses) == 4 and all(np.isfinite(losses))
     assert it.position == len(it.refs)
+
+
+def _failing_factory(n):
+    yield from ()
+    raise ValueError(f"broken reader {n}")
+
+
+def test_host_prepare_process_matches_in_process(tmp_path):
+    from mdl_b200.cli import main
+    from mdl_b200.config.schema import thaw
+    from mdl_b200.data.prepare_process import ProcessBatchIterator, parquet_batches
+
+    data = tmp_path / "data"
+    assert main(["make-synthetic-parquet", "--benchmark", "1", "--files", "2", "--rows", "256",
+                 "--out", str(data)]) == 0
+    m, _ = baseline_config(1)
+    m["runtime"]["device"] = "cpu"
+    cfg = app_config_from_mapping(m)
+    model = build_model(cfg, device="cpu", base_seed=0)
+    plan = model.encoder.batch_plan
+    paths = discover_parquet_inputs([str(data)])
+    ref = list(ParquetBatchIterator(paths, Tensorizer(cfg, plan), 128))
+    it = ProcessBatchIterator(parquet_batches, (thaw(cfg), plan, paths, 128, 0, 1, "train", False, 0, 0))
+    got = list(it)
+    it.close()
+    assert len(got) == len(ref) == 4
+    for a, b in zip(got, ref):
+        assert torch.equal(a.ids, b.ids) and torch.equal(a.offsets, b.offsets) and torch.equal(a.labels, b.labels)
+    bad = ProcessBatchIterator(_failing_factory, (7,))
+    with pytest.raises(RuntimeError, match="broken reader 7"):
+        list(bad)
+    bad.close()
+
+
+def _stalling_factory(seconds):
+    import time as _t
+
+    _t.sleep(seconds)
+    yield from ()
+
+
+def test_host_prepare_startup_timeout():
+    from mdl_b200.data.prepare_process import ProcessBatchIterator
+
+    # heartbeats keep a slow start alive; a child silent past the limit is reported
+    it = ProcessBatchIterator(_stalling_factory, (20.0,), startup_timeout_s=12.0, beat_s=0.5)
+    assert list(it) == []
+    it.close()
+    it = ProcessBatchIterator(_stalling_factory, (30.0,), startup_timeout_s=1.0, beat_s=60.0)
+    with pytest.raises(TimeoutError):
+        list(it)
+    it.close(join_timeout_s=1.0)
