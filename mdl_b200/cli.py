@@ -134,6 +134,7 @@ def _build(config, rank, world, device, seed=1234):
 
 def _batches(config, model, rank, world, *, split="train", synthetic=False, batch=None, loop=True):
     from .data.parquet import ParquetBatchIterator, Tensorizer, discover_parquet_inputs
+    from .data.remote_io import RemoteIoPolicy
     from .data.synthetic import SyntheticGenerator, synthetic_spec_from_config
 
     rows = batch or config.training.batch_size
@@ -154,7 +155,7 @@ def _batches(config, model, rank, world, *, split="train", synthetic=False, batc
         return ParquetBatchIterator(paths, Tensorizer(config, model.encoder.batch_plan, split=split), rows, rank=rank,
                                     world=world, shard_unit=r.shard_unit, shuffle_rows=r.shuffle_buffer_rows,
                                     seed=r.shuffle_seed, prefetch=r.prefetch_batches, loop=loop and split == "train",
-                                    pin=r.pin_memory)
+                                    pin=r.pin_memory, io_policy=RemoteIoPolicy.from_reader(r))
     gen = SyntheticGenerator(model.encoder.batch_plan, synthetic_spec_from_config(config, model.encoder.batch_plan),
                              rank=rank)
 
@@ -563,6 +564,16 @@ def build_parser() -> argparse.ArgumentParser:
 
 
 def main(argv=None) -> int:
+    from .data.remote_io import RemoteIoStallError
+
+    try:
+        return _dispatch(argv)
+    except RemoteIoStallError as error:  # a launcher may restart the job on this code
+        print(json.dumps({"error": "remote_io_stall", "detail": str(error)}), file=sys.stderr, flush=True)
+        return error.exit_code
+
+
+def _dispatch(argv=None) -> int:
     argv = list(sys.argv[1:] if argv is None else argv)
     args = build_parser().parse_args(argv)
     cmd = args.command

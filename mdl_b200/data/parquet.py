@@ -342,8 +342,10 @@ class ParquetBatchIterator:
     def __init__(self, paths: Sequence[str], tensorizer: Tensorizer, batch_size: int, *, rank: int = 0,
                  world: int = 1, shard_unit: str = "row_group", shuffle_rows: int = 0, seed: int = 0,
                  drop_last: bool = True, prefetch: int = 2, pin: bool = False, start_position: int = 0,
-                 loop: bool = False) -> None:
+                 loop: bool = False, io_policy=None) -> None:
         self.refs = plan_row_groups(paths, rank, world, shard_unit)
+        self.io = io_policy  # RemoteIoPolicy: timeouts, retries and skips of remote reads
+        self.rank = rank
         self.tz = tensorizer
         self.batch_size = batch_size
         self.shuffle_rows = shuffle_rows
@@ -361,13 +363,21 @@ class ParquetBatchIterator:
         pa, pq = _pa()
         cols = self.tz.columns()
         while not self._stop.is_set():
+            if self.io is not None and self.position == 0:
+                self.io.stagger(self.rank)
             while self.position < len(self.refs) and not self._stop.is_set():
                 ref = self.refs[self.position]
-                f = pq.ParquetFile(ref.path)
-                present = [c for c in cols if c in f.schema_arrow.names]
-                t = f.read(columns=present) if ref.index < 0 else f.read_row_group(ref.index, columns=present)
+
+                def read(ref=ref):
+                    f = pq.ParquetFile(ref.path)
+                    present = [c for c in cols if c in f.schema_arrow.names]
+                    return f.read(columns=present) if ref.index < 0 else f.read_row_group(ref.index, columns=present)
+
+                t = read() if self.io is None else self.io.run(read, f"read {ref.path}#{ref.index}", opening=True,
+                                                                 path=ref.path)
                 self.position += 1
-                yield t
+                if t is not None:
+                    yield t
             if not self.loop or not self.refs:
                 return
             self.position = 0
