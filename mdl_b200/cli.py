@@ -148,11 +148,12 @@ def _batches(config, model, rank, world, *, split="train", synthetic=False, batc
             from .data.prepare_process import ProcessBatchIterator, parquet_batches
 
             args = (thaw(config), model.encoder.batch_plan, paths, rows, rank, world, split,
-                    loop and split == "train", r.shuffle_buffer_rows, r.shuffle_seed)
+                    loop and split == "train", r.shuffle_buffer_rows, r.shuffle_seed, list(model.encoder.seq_plans))
             return ProcessBatchIterator(parquet_batches, args, depth=r.host_prepare_prefetch, pin=r.pin_memory,
                                         startup_timeout_s=r.host_prepare_startup_timeout_sec,
                                         idle_timeout_s=r.host_prepare_idle_timeout_sec)
-        return ParquetBatchIterator(paths, Tensorizer(config, model.encoder.batch_plan, split=split), rows, rank=rank,
+        tz = Tensorizer(config, model.encoder.batch_plan, split=split, seq_names=list(model.encoder.seq_plans))
+        return ParquetBatchIterator(paths, tz, rows, rank=rank,
                                     world=world, shard_unit=r.shard_unit, shuffle_rows=r.shuffle_buffer_rows,
                                     seed=r.shuffle_seed, prefetch=r.prefetch_batches, loop=loop and split == "train",
                                     pin=r.pin_memory, io_policy=RemoteIoPolicy.from_reader(r))

@@ -218,7 +218,8 @@ def load_vocab_map(path: str) -> dict[str, int]:
 class Tensorizer:
     """Arrow table (one sample per row) -> ``PackedBatch`` for a batch layout."""
 
-    def __init__(self, config, batch_plan, *, split: str = "train", vocab_maps: dict[str, dict] | None = None):
+    def __init__(self, config, batch_plan, *, split: str = "train", vocab_maps: dict[str, dict] | None = None,
+                 seq_names=None):
         self.config = config
         self.plan = batch_plan
         by_name = {f.name: f for f in config.features}
@@ -240,6 +241,17 @@ class Tensorizer:
         self.scene_source = sc.source
         self.scene_index = {str(n): i for i, n in enumerate(sc.names)}
         self.scene_encoding = sc.source_encoding
+        # event sequences (one list column per field) and request-level deduplication
+        by_seq = {q.name: q for q in config.sequences}
+        self.sequences = [by_seq[n] for n in (seq_names or [])]
+        self.seq_encoders = {}
+        for q in self.sequences:
+            for fl in q.fields:
+                if fl.kind == "categorical":
+                    self.seq_encoders[(q.name, fl.name)] = CategoricalEncoder(fl, vocab_maps.get(f"{q.name}.{fl.name}"))
+        self.request_id = sp.request_id if sp.reader.deduplicate_request_features else None
+        if sp.reader.deduplicate_request_features and not sp.request_id:
+            raise ValueError("reader.deduplicate_request_features needs the split's request_id column")
 
     def columns(self) -> list[str]:
         cols = [f.source or f.name for f in self.features]
@@ -247,7 +259,93 @@ class Tensorizer:
         cols += list(self.label_masks.values())
         if self.scene_source:
             cols.append(self.scene_source)
+        for q in self.sequences:
+            cols += [fl.source or fl.name for fl in q.fields]
+        if self.request_id:
+            cols.append(self.request_id)
         return list(dict.fromkeys(cols))
+
+    def _event_matrix(self, q, col, rows: int) -> tuple[np.ndarray, np.ndarray]:
+        """``[rows, L]`` positions into the column's flat values (-1 = padding) and lengths.
+
+        Truncation keeps the first (``head``) or last (``tail``) ``max_length`` events of
+        the stored order; the kept events are laid out oldest to newest and left-padded,
+        the layout the sequence models read (valid events at the end)."""
+
+        import pyarrow as pa
+
+        L = int(q.max_length)
+        col = col.combine_chunks() if isinstance(col, pa.ChunkedArray) else col
+        offs = col.offsets.to_numpy().astype(np.int64)
+        starts, ends = offs[:-1], offs[1:]
+        if col.null_count:
+            nul = col.is_null().to_numpy(zero_copy_only=False)
+            ends = np.where(nul, starts, ends)
+        n = ends - starts
+        keep = np.minimum(n, L)
+        src0 = starts if q.truncation == "head" else ends - keep
+        j = np.arange(L)[None, :] - (L - keep)[:, None]          # rank among the kept events
+        valid = j >= 0
+        if q.sequence_order == "newest_to_oldest":
+            pos = src0[:, None] + (keep[:, None] - 1 - j)
+        else:
+            pos = src0[:, None] + j
+        return np.where(valid, pos, -1), keep
+
+    def _sequence(self, q, table, rows: int) -> dict:
+        import pyarrow as pa
+
+        L = int(q.max_length)
+        cats = [fl for fl in q.fields if fl.kind == "categorical"]
+        dens = [fl for fl in q.fields if fl.kind == "dense"]
+        first = table.column((cats or dens)[0].source or (cats or dens)[0].name)
+        pos, lengths = self._event_matrix(q, first, rows)
+        ids = np.zeros((len(cats), rows, L), dtype=np.int64)
+        for k, fl in enumerate(cats):
+            col = table.column(fl.source or fl.name)
+            col = col.combine_chunks() if isinstance(col, pa.ChunkedArray) else col
+            flat = self.seq_encoders[(q.name, fl.name)].encode(col.values.to_numpy(zero_copy_only=False))
+            safe = np.clip(pos, 0, max(0, len(flat) - 1))
+            ids[k] = np.where(pos >= 0, flat[safe] if len(flat) else 0, 0)
+        out = {"ids": torch.from_numpy(ids.reshape(len(cats), rows * L)), "lengths": torch.from_numpy(lengths)}
+        if dens:
+            width = sum(int(fl.dimension) for fl in dens)
+            dense = np.zeros((rows, L, width), dtype=np.float32)
+            c = 0
+            for fl in dens:
+                col = table.column(fl.source or fl.name)
+                col = col.combine_chunks() if isinstance(col, pa.ChunkedArray) else col
+                d = int(fl.dimension)
+                flat = np.asarray(col.values.to_numpy(zero_copy_only=False), dtype=np.float32).reshape(-1, d)
+                safe = np.clip(pos, 0, max(0, len(flat) - 1))
+                dense[:, :, c:c + d] = np.where((pos >= 0)[..., None], flat[safe] if len(flat) else 0.0, 0.0)
+                c += d
+            out["dense"] = torch.from_numpy(dense.reshape(rows * L, width))
+        return out
+
+    def _sequences(self, table) -> dict:
+        """Sequence payloads; with request deduplication one row per distinct ``request_id``
+        (in order of first appearance) plus ``row_indices`` (candidate -> request row)."""
+
+        if not self.sequences:
+            return {}
+        ri = None
+        src = table
+        if self.request_id:
+            keys = np.asarray(table.column(self.request_id).to_pylist(), dtype=object)
+            _, first, inv = np.unique(keys.astype(str), return_index=True, return_inverse=True)
+            order = np.argsort(first, kind="stable")          # requests in order of first appearance
+            rank_of = np.empty_like(order)
+            rank_of[order] = np.arange(len(order))
+            ri = torch.from_numpy(rank_of[inv].astype(np.int64))
+            src = table.take(first[order])
+        out = {}
+        for q in self.sequences:
+            seq = self._sequence(q, src, src.num_rows)
+            if ri is not None:
+                seq["row_indices"] = ri
+            out[q.name] = seq
+        return out
 
     def _bag(self, f, col) -> tuple[np.ndarray, np.ndarray]:
         """(flat raw values, lengths) of one categorical column; scalars are bags of one."""
@@ -329,7 +427,8 @@ class Tensorizer:
                 scen = np.array([self.scene_index.get(str(v), 0) for v in vals], dtype=np.int64)
         return PackedBatch.pack(torch.from_numpy(ids), torch.from_numpy(offsets),
                                 torch.from_numpy(dense) if self.dense_width else None, torch.from_numpy(labels),
-                                torch.from_numpy(mask) if any_mask else None, torch.from_numpy(scen), rows, pin=pin)
+                                torch.from_numpy(mask) if any_mask else None, torch.from_numpy(scen), rows,
+                                sequences=self._sequences(table), pin=pin)
 
 
 # ------------------------------------------------------------------ iteration
@@ -498,6 +597,20 @@ def write_synthetic_parquet(path: str, batch: PackedBatch, batch_plan, config, r
             cols[f.source or f.name] = pa.array([s[0] for s in seg], type=pa.int64())
         else:
             cols[f.source or f.name] = pa.array(seg, type=pa.list_(pa.int64()))
+    # event sequences: one list column per categorical field, valid (non-padding) events
+    # oldest to newest; request-level payloads are expanded to the candidate rows
+    by_seq = {q.name: q for q in config.sequences}
+    for name, seq in batch.sequences.items():
+        q = by_seq[name]
+        L = int(q.max_length)
+        cats = [fl for fl in q.fields if fl.kind == "categorical"]
+        R = seq["lengths"].numel()
+        sid = seq["ids"].numpy().reshape(len(cats), R, L)
+        lens = seq["lengths"].numpy()
+        ri = seq["row_indices"].numpy() if "row_indices" in seq else np.arange(rows)
+        for k, fl in enumerate(cats):
+            cols[fl.source or fl.name] = pa.array([sid[k, r, L - lens[r]:].tolist() for r in ri],
+                                                  type=pa.list_(pa.int64()))
     sp = config.data.train
     for t, task in enumerate(config.task_names):
         cols[sp.labels.get(task, task)] = pa.array(batch.labels.numpy()[:, t].astype(np.float32))

@@ -31,14 +31,14 @@ _BATCH, _END, _ERROR, _BEAT = 0, 1, 2, 3
 
 
 def parquet_batches(config_mapping: dict, batch_plan, paths: list[str], batch_size: int, rank: int, world: int,
-                    split: str, loop: bool, shuffle_rows: int, seed: int):
+                    split: str, loop: bool, shuffle_rows: int, seed: int, seq_names=None):
     """Child-side factory: the rank's Parquet batches (no pinning in the child)."""
 
     from ..config.loader import app_config_from_mapping
     from .parquet import ParquetBatchIterator, Tensorizer
 
     cfg = app_config_from_mapping(config_mapping)
-    it = ParquetBatchIterator(paths, Tensorizer(cfg, batch_plan, split=split), batch_size, rank=rank, world=world,
+    it = ParquetBatchIterator(paths, Tensorizer(cfg, batch_plan, split=split, seq_names=seq_names), batch_size, rank=rank, world=world,
                               shuffle_rows=shuffle_rows, seed=seed, loop=loop, prefetch=2, pin=False)
     return iter(it)
 

@@ -57,7 +57,8 @@ class FixedTestEval:
         from ..data.parquet import ParquetBatchIterator, Tensorizer
 
         test = self.config.data.test
-        it = ParquetBatchIterator(self.files, Tensorizer(self.config, model.encoder.batch_plan, split="test"),
+        it = ParquetBatchIterator(self.files, Tensorizer(self.config, model.encoder.batch_plan, split="test",
+                                                         seq_names=list(model.encoder.seq_plans)),
                                   batch_size, rank=self.rank, world=self.world, shard_unit=test.reader.shard_unit,
                                   drop_last=False, prefetch=2, loop=False)
         rows = sum(ref.rows for ref in it.refs)

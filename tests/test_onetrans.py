@@ -300,3 +300,67 @@ def test_request_level_sequences_match_expanded_rows(make):
     torch.testing.assert_close(out_r["loss"], out_e["loss"])
     torch.testing.assert_close(g_r, tr.dense.grad, atol=1e-6, rtol=1e-4)
     torch.testing.assert_close(e_r, model.store.grad, atol=1e-6, rtol=1e-4)
+
+
+@pytest.mark.parametrize("dedup", [False, True])
+def test_sequence_parquet_round_trip(tmp_path, dedup):
+    """Synthetic batch -> Parquet list columns -> tensorizer gives the same sequence payload
+    (and, with request deduplication, the same request rows and ``row_indices``)."""
+
+    import copy
+
+    import pyarrow as pa
+    import pyarrow.parquet as pq
+
+    from mdl_b200.data.parquet import Tensorizer, write_synthetic_parquet
+
+    m, spec = scaled_config(4, 1e-4, num_fields=12, batch=64, seq_len=40, num_layers=2)
+    m["model"].update({"hidden_dim": 128, "token_dim": 64, "num_heads": 2, "num_ns_tokens": 4,
+                       "task_head_hidden_dim": 64, "pyramid_round_to": 8})
+    if dedup:
+        m.setdefault("data", {}).setdefault("train", {})["request_id"] = "req"
+        m["data"]["train"].setdefault("reader", {})["deduplicate_request_features"] = True
+    cfg = app_config_from_mapping(m)
+    spec = copy.deepcopy(spec)
+    spec.sequences["behavior"].min_len = 5
+    spec.sequences["behavior"].candidates_per_request = 4
+    model = build_model(cfg, device="cpu", base_seed=1)
+    b = SyntheticGenerator(model.encoder.batch_plan, spec).batch(64)
+    path = tmp_path / "s.parquet"
+    write_synthetic_parquet(str(path), b, model.encoder.batch_plan, cfg)
+    t = pq.read_table(path)
+    t = t.append_column("req", pa.array(b.sequences["behavior"]["row_indices"].numpy() * 7 + 3))
+    tz = Tensorizer(cfg, model.encoder.batch_plan, seq_names=["behavior"])
+    got = tz(t).sequences["behavior"]
+    want = b.sequences["behavior"]
+    if dedup:
+        assert torch.equal(got["row_indices"], want["row_indices"])
+        assert torch.equal(got["ids"], want["ids"]) and torch.equal(got["lengths"], want["lengths"])
+    else:
+        ri = want["row_indices"]
+        F = want["ids"].shape[0]
+        L = 40
+        exp = want["ids"].view(F, -1, L)[:, ri].reshape(F, -1)
+        assert torch.equal(got["ids"], exp) and torch.equal(got["lengths"], want["lengths"][ri])
+
+
+@pytest.mark.parametrize("trunc,order,expect", [
+    ("tail", "oldest_to_newest", [[0, 0, 1, 2], [3, 4, 5, 6]]),
+    ("head", "oldest_to_newest", [[0, 0, 1, 2], [1, 2, 3, 4]]),
+    ("tail", "newest_to_oldest", [[0, 0, 2, 1], [6, 5, 4, 3]]),
+])
+def test_sequence_truncation_layout(trunc, order, expect):
+    import pyarrow as pa
+
+    from mdl_b200.data.parquet import Tensorizer
+
+    m, _ = scaled_config(4, 1e-4, num_fields=12, batch=8, seq_len=4, num_layers=1)
+    m["sequences"][0].update({"truncation": trunc, "sequence_order": order})
+    m["sequences"][0]["fields"] = m["sequences"][0]["fields"][:1]
+    cfg = app_config_from_mapping(m)
+    tz = Tensorizer(cfg, build_model(cfg, device="cpu", base_seed=1).encoder.batch_plan, seq_names=["behavior"])
+    col = pa.array([[1, 2], [1, 2, 3, 4, 5, 6]], type=pa.list_(pa.int64()))
+    pos, keep = tz._event_matrix(cfg.sequences[0], col, 2)
+    flat = col.values.to_numpy()
+    got = [[int(flat[p]) if p >= 0 else 0 for p in row] for row in pos]
+    assert got == expect and keep.tolist() == [2, 4]
