@@ -38,8 +38,9 @@ def parquet_batches(config_mapping: dict, batch_plan, paths: list[str], batch_si
     from .parquet import ParquetBatchIterator, Tensorizer
 
     cfg = app_config_from_mapping(config_mapping)
-    it = ParquetBatchIterator(paths, Tensorizer(cfg, batch_plan, split=split, seq_names=seq_names), batch_size, rank=rank, world=world,
-                              shuffle_rows=shuffle_rows, seed=seed, loop=loop, prefetch=2, pin=False)
+    tz = Tensorizer(cfg, batch_plan, split=split, seq_names=seq_names)
+    it = ParquetBatchIterator(paths, tz, batch_size, rank=rank, world=world, shuffle_rows=shuffle_rows, seed=seed,
+                              loop=loop, prefetch=2, pin=False)
     return iter(it)
 
 
