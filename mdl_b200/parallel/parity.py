@@ -145,7 +145,9 @@ def _run_parity_body(rank: int, world: int, device_type: str, out_path: str, opt
         grad_tables = gather_tables(model.store, "grad")
         if model.store.replicas > 1:  # every replica holds its own W-scaled contribution: sum them
             for g in grad_tables.values():
-                dist.all_reduce(g)
+                on_dev = g.to(device)  # NCCL reduces device tensors only
+                dist.all_reduce(on_dev)
+                g.copy_(on_dev.cpu())
         trainer.optimizer_step()
         if device.type == "cuda":
             torch.cuda.synchronize(device)
