@@ -109,3 +109,20 @@ def test_cli_fixed_test_eval_during_training(tmp_path):
     assert [l["step"] for l in evals] == [2, 4]
     ev = evals[-1]["fixed_test_eval"]
     assert ev["batches"] == 3 and 0.0 <= ev["tasks"]["click"]["auc"] <= 1.0
+
+
+def test_cli_two_ranks_from_parquet_with_checkpoint(tmp_path):
+    """Two gloo ranks through the CLI relaunch: runtime set-up, shard-metadata agreement,
+    the batch supply vote on Parquet input, a sharded checkpoint, then a resume."""
+
+    data = tmp_path / "data"
+    _run("make-synthetic-parquet", "--benchmark", "1", "--files", "2", "--rows", "512", "--out", str(data))
+    over = ["--benchmark-config", "1", "--set", f"data.train.inputs=[{str(data)}]", "--set", "training.batch_size=128",
+            "--set", "runtime.device=cpu", "--nproc-per-node", "2", "--master-port", "29563"]
+    run = tmp_path / "run"
+    logs = _run("train", *over, "--max-steps", "4", "--log-every", "2", "--checkpoint-dir", str(run),
+                "--save-every", "4")
+    assert logs[-1]["done"] and logs[-1]["steps"] == 4
+    assert (run / "step-000000004" / "_COMMIT").exists()
+    logs = _run("train", *over, "--max-steps", "6", "--log-every", "1", "--checkpoint-dir", str(run))
+    assert [l["step"] for l in logs if "loss" in l][0] == 5
