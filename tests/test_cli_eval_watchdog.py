@@ -126,3 +126,28 @@ def test_cli_two_ranks_from_parquet_with_checkpoint(tmp_path):
     assert (run / "step-000000004" / "_COMMIT").exists()
     logs = _run("train", *over, "--max-steps", "6", "--log-every", "1", "--checkpoint-dir", str(run))
     assert [l["step"] for l in logs if "loss" in l][0] == 5
+
+
+def test_cli_replicated_tables_checkpoint_reshards(tmp_path):
+    """Replicated tables with full Adagrad on two gloo ranks: rank 0 writes one copy of
+    each table; the checkpoint resumes on two ranks and loads into a sharded layout."""
+
+    data = tmp_path / "data"
+    _run("make-synthetic-parquet", "--benchmark", "1", "--files", "2", "--rows", "512", "--out", str(data))
+    base = ["--benchmark-config", "1", "--set", f"data.train.inputs=[{str(data)}]", "--set", "training.batch_size=128",
+            "--set", "runtime.device=cpu", "--set", "training.sparse_optimizer=adagrad"]
+    rep = base + ["--set", "training.embedding_distribution=replicated"]
+    run = tmp_path / "run"
+    logs = _run("train", *rep, "--nproc-per-node", "2", "--master-port", "29565", "--max-steps", "3",
+                "--checkpoint-dir", str(run), "--log-every", "1")
+    assert logs[-1]["done"]
+    manifest = json.loads((run / "step-000000003" / "model" / "manifest.json").read_text())
+    assert manifest["embedding_world_size"] == 1
+    assert all(len(c["rank_files"]) == 1 for c in manifest["chunks"])
+    logs = _run("train", *rep, "--nproc-per-node", "2", "--master-port", "29567", "--max-steps", "4",
+                "--checkpoint-dir", str(run), "--log-every", "1")
+    assert [l["step"] for l in logs if "loss" in l][0] == 4
+    shard = base + ["--set", "training.embedding_distribution=sharded"]
+    logs = _run("train", *shard, "--nproc-per-node", "2", "--master-port", "29569", "--max-steps", "5",
+                "--checkpoint-dir", str(run), "--log-every", "1")
+    assert [l["step"] for l in logs if "loss" in l][0] == 5
