@@ -123,13 +123,18 @@ class MixFormerBlock(nn.Module):
         """Reordered single-query cross attention of each head over the history."""
 
         hist = self.history(seq, native)
+        B, L = hist.shape[0], hist.shape[1]
+        # one fp32 copy of the history in head-major order [B, N, L, D] (conversion and
+        # transpose in a single pass), read by both batched products
+        hf = torch.empty(B, self.N, L, self.D, dtype=torch.float32, device=hist.device)
+        hf.copy_(hist.permute(0, 2, 1, 3))
         qn = rms_norm(x, self.q_norm, native=native).float()
         sq = torch.einsum("bno,noi->bni", qn, self.key_weight)                 # q' = q W_k
-        scores = torch.einsum("bni,blni->bnl", sq, hist.float()) / math.sqrt(self.D)
+        scores = torch.matmul(sq.unsqueeze(2), hf.transpose(-1, -2)).squeeze(2) / math.sqrt(self.D)  # [B, N, L]
         mask = valid.bool().unsqueeze(1)
         scores = scores.masked_fill(~mask, float("-inf"))
         w = torch.nan_to_num(torch.softmax(scores, dim=-1)) * mask
-        ctx = torch.einsum("bnl,blni->bni", w, hist.float())
+        ctx = torch.matmul(w.unsqueeze(2), hf).squeeze(2)                      # [B, N, D]
         return x + torch.einsum("bni,noi->bno", ctx, self.value_weight).to(x.dtype)
 
     def reference_state_dict(self, prefix: str) -> dict[str, torch.Tensor]:
