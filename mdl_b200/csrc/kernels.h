@@ -8,3 +8,4 @@
 #include "gemm.h"
 #include "misc.h"
 #include "norm.h"
+#include "sqa.h"

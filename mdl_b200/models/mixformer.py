@@ -124,6 +124,15 @@ class MixFormerBlock(nn.Module):
 
         hist = self.history(seq, native)
         B, L = hist.shape[0], hist.shape[1]
+        if native:
+            # fused kernel: the bf16 history is streamed once, in place (valid events are a suffix)
+            from ..ops.attention import single_query_attention
+
+            qn = rms_norm(x, self.q_norm, native=native).float()
+            sq = torch.einsum("bno,noi->bni", qn, self.key_weight)
+            kstart = (L - valid.sum(dim=1)).to(torch.int32)
+            ctx = single_query_attention(sq, hist, kstart, 1.0 / math.sqrt(self.D))
+            return x + torch.einsum("bni,noi->bno", ctx, self.value_weight).to(x.dtype)
         # one fp32 copy of the history in head-major order [B, N, L, D] (conversion and
         # transpose in a single pass), read by both batched products
         hf = torch.empty(B, self.N, L, self.D, dtype=torch.float32, device=hist.device)

@@ -96,3 +96,50 @@ def suffix_attention(qkv: torch.Tensor, kstart: torch.Tensor, heads: int, lq: in
     if qkv.is_cuda:
         return SuffixAttentionFn.apply(qkv, kstart, heads, lq, causal, ktail)
     return suffix_attention_reference(qkv, kstart, heads, lq, causal, ktail=ktail)
+
+
+# ----------------------------------------------------------------------------- single-query attention
+def single_query_attention_reference(q: torch.Tensor, hist: torch.Tensor, kstart: torch.Tensor,
+                                     scale: float) -> torch.Tensor:
+    """fp32 definition: per sample and head, ``softmax(scale * q . h_l)`` over the events
+    ``l >= kstart[b]`` of ``hist [B, L, N, D]``, weighted sum of ``h_l``; ``q [B, N, D]``;
+    a sample without a valid event gives zero."""
+
+    B, L, N, D = hist.shape
+    hf = hist.float().permute(0, 2, 1, 3)                                   # [B, N, L, D]
+    s = torch.matmul(q.float().unsqueeze(2), hf.transpose(-1, -2)).squeeze(2) * scale   # [B, N, L]
+    valid = torch.arange(L, device=hist.device).view(1, 1, L) >= kstart.to(hist.device).long().view(B, 1, 1)
+    w = torch.nan_to_num(torch.softmax(s.masked_fill(~valid, float("-inf")), dim=-1)) * valid
+    return torch.matmul(w.unsqueeze(2), hf).squeeze(2)
+
+
+class SingleQueryAttentionFn(torch.autograd.Function):
+    """CUDA kernels of ``csrc/sqa.cu``: one warp per (sample, head) streams the bf16 history
+    once (online softmax); the backward recomputes the weights from the saved log-sum-exp."""
+
+    @staticmethod
+    def forward(ctx, q, hist, kstart, scale):
+        q = q.float().contiguous()
+        hist = hist.to(torch.bfloat16).contiguous()
+        ks = kstart.to(torch.int32).contiguous()
+        B, L, N, D = hist.shape
+        out = torch.empty(B, N, D, dtype=torch.float32, device=q.device)
+        lse = torch.empty(B, N, dtype=torch.float32, device=q.device)
+        ext().sqa_fwd(q, hist, ks, out, lse, float(scale))
+        ctx.save_for_backward(q, hist, ks, out, lse)
+        ctx.scale = float(scale)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        q, hist, ks, out, lse = ctx.saved_tensors
+        dq = torch.empty_like(q)
+        dhist = torch.empty_like(hist)
+        ext().sqa_bwd(q, hist, ks, out, lse, dout.float().contiguous(), dq, dhist, ctx.scale)
+        return dq, dhist, None, None
+
+
+def single_query_attention(q: torch.Tensor, hist: torch.Tensor, kstart: torch.Tensor, scale: float) -> torch.Tensor:
+    if q.is_cuda:
+        return SingleQueryAttentionFn.apply(q, hist, kstart, scale)
+    return single_query_attention_reference(q, hist, kstart, scale)

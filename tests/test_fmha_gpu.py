@@ -103,3 +103,46 @@ def test_fmha_forward_backward(case):
         sl = slice(part * 32 * H, (part + 1) * 32 * H)
         pr = ((g[..., sl] - gr[..., sl]).norm() / gr[..., sl].norm().clamp_min(1e-6)).item()
         assert pr < 3e-2, f"part {part} relative error {pr}"
+
+
+@pytest.mark.parametrize("B,L,N,D", [(3, 17, 4, 16), (5, 70, 8, 64), (2, 40, 3, 100)])
+def test_single_query_attention_cpu_reference_matches_masked_softmax(B, L, N, D):
+    from mdl_b200.ops.attention import single_query_attention_reference
+
+    torch.manual_seed(0)
+    q, hist = torch.randn(B, N, D), torch.randn(B, L, N, D)
+    ks = torch.randint(0, L + 1, (B,))
+    out = single_query_attention_reference(q, hist, ks, 0.3)
+    for b in range(B):
+        for n in range(N):
+            if ks[b] >= L:
+                assert not out[b, n].any()
+                continue
+            h = hist[b, ks[b]:, n]
+            w = torch.softmax(0.3 * h @ q[b, n], 0)
+            torch.testing.assert_close(out[b, n], w @ h, atol=1e-5, rtol=1e-5)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B,L,N,D", [(3, 17, 4, 16), (64, 257, 32, 64), (7, 90, 3, 100), (4, 33, 2, 128)])
+def test_single_query_attention_kernel_matches_fp32(B, L, N, D):
+    from mdl_b200.ops.attention import SingleQueryAttentionFn, single_query_attention_reference
+
+    torch.manual_seed(1)
+    dev = torch.device("cuda")
+    q = torch.randn(B, N, D, device=dev, requires_grad=True)
+    hist = torch.randn(B, L, N, D, device=dev).bfloat16().requires_grad_(True)
+    ks = torch.randint(0, L, (B,), device=dev)
+    ks[0] = L  # a sample without a valid event
+    out = SingleQueryAttentionFn.apply(q, hist, ks, 0.25)
+    ref_q = q.detach().clone().requires_grad_(True)
+    ref_h = hist.detach().float().requires_grad_(True)
+    ref = single_query_attention_reference(ref_q, ref_h, ks, 0.25)
+    torch.testing.assert_close(out, ref, atol=2e-3, rtol=2e-3)
+    g = torch.randn_like(ref)
+    out.backward(g)
+    ref.backward(g)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(q.grad, ref_q.grad, atol=5e-3, rtol=5e-3)
+    torch.testing.assert_close(hist.grad.float(), ref_h.grad, atol=2e-2, rtol=2e-2)
+    assert not hist.grad[0].any()
