@@ -18,6 +18,7 @@ namespace {
 
 constexpr int kMaxSlots = 4;  // head width up to 128
 constexpr int kWarps = 8;
+constexpr int kUnroll = 4;    // events per loop iteration
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -44,22 +45,40 @@ __global__ void __launch_bounds__(kWarps * 32) sqa_fwd_kernel(SqaArgs a) {
   float m = -INFINITY, l = 0.f;
   const __nv_bfloat16* h = a.hist + (static_cast<long long>(b) * L * a.N + n) * D;
   const long long lstride = static_cast<long long>(a.N) * D;
-  for (int e = k0; e < L; ++e) {
-    float hv[S];
-    float dot = 0.f;
+  // kUnroll events per iteration: their loads and warp reductions are independent, so the
+  // dependent load -> reduce -> exp chain of one event overlaps with the next ones
+  for (int e0 = k0; e0 < L; e0 += kUnroll) {
+    float hv[kUnroll][S];
+    float dot[kUnroll];
 #pragma unroll
-    for (int s = 0; s < S; ++s) {
-      const int k = lane + 32 * s;
-      hv[s] = k < D ? __bfloat162float(h[e * lstride + k]) : 0.f;
-      dot += q[s] * hv[s];
+    for (int u = 0; u < kUnroll; ++u) {
+      const int e = e0 + u;
+      dot[u] = 0.f;
+#pragma unroll
+      for (int s = 0; s < S; ++s) {
+        const int k = lane + 32 * s;
+        hv[u][s] = (k < D && e < L) ? __bfloat162float(h[e * lstride + k]) : 0.f;
+        dot[u] += q[s] * hv[u][s];
+      }
     }
-    dot = warp_sum(dot);
-    const float mn = fmaxf(m, dot);
-    const float corr = expf(m - mn);  // 0 on the first event (m = -inf)
-    const float p = expf(dot - mn);
-    l = l * corr + p;
 #pragma unroll
-    for (int s = 0; s < S; ++s) acc[s] = acc[s] * corr + p * hv[s];
+    for (int u = 0; u < kUnroll; ++u) dot[u] = warp_sum(dot[u]);
+    float mn = m;
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u)
+      if (e0 + u < L) mn = fmaxf(mn, dot[u]);
+    const float corr = expf(m - mn);  // 0 on the first chunk (m = -inf)
+    l *= corr;
+#pragma unroll
+    for (int s = 0; s < S; ++s) acc[s] *= corr;
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      if (e0 + u >= L) break;
+      const float p = expf(dot[u] - mn);
+      l += p;
+#pragma unroll
+      for (int s = 0; s < S; ++s) acc[s] += p * hv[u][s];
+    }
     m = mn;
   }
   const float inv = l > 0.f ? 1.f / l : 0.f;
@@ -95,33 +114,48 @@ __global__ void __launch_bounds__(kWarps * 32) sqa_bwd_kernel(SqaArgs a) {
   const __nv_bfloat16* h = a.hist + (static_cast<long long>(b) * L * a.N + n) * D;
   __nv_bfloat16* dh = a.dhist + (static_cast<long long>(b) * L * a.N + n) * D;
   const long long lstride = static_cast<long long>(a.N) * D;
-  for (int e = 0; e < L; ++e) {
-    if (e < k0 || !(lse > -INFINITY)) {  // padding (or no valid event): zero gradient
+  const bool any = lse > -INFINITY;
+  const int first = any ? k0 : L;
+  for (int e = 0; e < first; ++e) {  // padding (or no valid event): zero gradient
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+      const int k = lane + 32 * s;
+      if (k < D) dh[e * lstride + k] = __float2bfloat16_rn(0.f);
+    }
+  }
+  for (int e0 = first; e0 < L; e0 += kUnroll) {
+    float hv[kUnroll][S];
+    float dot[kUnroll], dp[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int e = e0 + u;
+      dot[u] = 0.f;
+      dp[u] = 0.f;
 #pragma unroll
       for (int s = 0; s < S; ++s) {
         const int k = lane + 32 * s;
-        if (k < D) dh[e * lstride + k] = __float2bfloat16_rn(0.f);
+        hv[u][s] = (k < D && e < L) ? __bfloat162float(h[e * lstride + k]) : 0.f;
+        dot[u] += q[s] * hv[u][s];
+        dp[u] += dc[s] * hv[u][s];
       }
-      continue;
     }
-    float hv[S];
-    float dot = 0.f, dp = 0.f;
 #pragma unroll
-    for (int s = 0; s < S; ++s) {
-      const int k = lane + 32 * s;
-      hv[s] = k < D ? __bfloat162float(h[e * lstride + k]) : 0.f;
-      dot += q[s] * hv[s];
-      dp += dc[s] * hv[s];
+    for (int u = 0; u < kUnroll; ++u) {
+      dot[u] = warp_sum(dot[u]);
+      dp[u] = warp_sum(dp[u]);
     }
-    dot = warp_sum(dot);
-    dp = warp_sum(dp);
-    const float p = expf(dot * a.scale - lse);
-    const float ds = p * (dp - dsum);
 #pragma unroll
-    for (int s = 0; s < S; ++s) {
-      const int k = lane + 32 * s;
-      dq[s] += ds * a.scale * hv[s];
-      if (k < D) dh[e * lstride + k] = __float2bfloat16_rn(p * dc[s] + ds * a.scale * q[s]);
+    for (int u = 0; u < kUnroll; ++u) {
+      const int e = e0 + u;
+      if (e >= L) break;
+      const float p = expf(dot[u] * a.scale - lse);
+      const float ds = p * (dp[u] - dsum);
+#pragma unroll
+      for (int s = 0; s < S; ++s) {
+        const int k = lane + 32 * s;
+        dq[s] += ds * a.scale * hv[u][s];
+        if (k < D) dh[e * lstride + k] = __float2bfloat16_rn(p * dc[s] + ds * a.scale * q[s]);
+      }
     }
   }
 #pragma unroll
