@@ -32,7 +32,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-BASELINE_VALUE = None  # BASELINE.md publishes no B200 number for this workload
+BASELINE_VALUE = None  # the reference publishes no B200 number for this workload
 METRIC = "train samples/sec"
 MODEL_DESC = {
     2: "rankmixer (BASELINE config 2: 300 fields, ~200M x 64 fp32 rows, T=16 D=768 L=2 FFNx4, 2 heads)",

@@ -142,15 +142,58 @@ def _saved_ids(spec: dict, rows: int, saved_rank: int, num_embeddings: int) -> t
     return ids[ids < num_embeddings]
 
 
+def _restore_rows(emb, name: str, t, tab: dict, saved_rank: int, rank: int, filled: torch.Tensor) -> None:
+    """Copy the rows of one saved shard that this rank owns into its local table and
+    mark them in ``filled``. A shard saved by this rank under the same shard spec is
+    copied as a whole; anything else is remapped through global ids."""
+
+    w = tab["weight"]
+    acc = (tab.get("optimizer_state") or {}).get("sum")
+    dst_w = emb.weight(name)
+    dst_a = emb.accumulator(name)
+    if saved_rank == rank and tab.get("shard_spec") == asdict(t.spec):
+        if w.shape[0] != t.local_rows:
+            raise ValueError(f"table {name!r}: {w.shape[0]} saved rows, {t.local_rows} local rows")
+        dst_w.copy_(w.to(dst_w.device, dst_w.dtype))
+        if acc is not None:
+            dst_a.copy_(acc.to(dst_a.device, dst_a.dtype))
+        filled.fill_(True)
+        return
+    ids = _saved_ids(tab["shard_spec"], w.shape[0], saved_rank, t.num_embeddings)
+    if ids.numel() != w.shape[0]:
+        raise ValueError(f"table {name!r}: shard of rank {saved_rank} holds {w.shape[0]} rows, its spec "
+                         f"owns {ids.numel()}")
+    mine = t.spec.owner(ids) == rank
+    if not bool(mine.any()):
+        return
+    local = t.spec.local_row_ids(ids[mine])
+    sel = mine.nonzero().flatten()
+    dst_w[local.to(dst_w.device)] = w[sel].to(dst_w.device, dst_w.dtype)
+    if acc is not None:
+        dst_a[local.to(dst_a.device)] = acc[sel].to(dst_a.device, dst_a.dtype)
+    filled[local] = True
+
+
 @torch.no_grad()
 def load_model_checkpoint(config, trainer, store: CheckpointStore, *, strict: bool = True) -> dict[str, Any]:
-    """Restore dense parameters and every table shard (resharding when the world size changed)."""
+    """Restore dense parameters and every table shard (resharding when the world size
+    or a table's shard spec changed).
+
+    Every local row of every model table must be restored: like the reference
+    (``src/checkpoint.py:722-790``) a per-table mask records the rows written and a
+    table with any row left out (a table missing from the checkpoint, or shard files
+    that do not cover it) raises. At the saved world size a rank first reads only its
+    own files; tables whose saved shard spec differs from the current one are then
+    completed from the other ranks' files."""
 
     manifest = store.read_json(MANIFEST)
     if manifest.get("format") != SHARDED_FORMAT:
         raise ValueError(f"unsupported checkpoint format {manifest.get('format')!r}")
     if strict and manifest.get("model_name") != config.model.name:
         raise ValueError(f"checkpoint is a {manifest.get('model_name')!r} model, config builds {config.model.name!r}")
+    saved_opt = manifest.get("training_metadata", {}).get("sparse_optimizer")
+    if saved_opt not in (None, config.training.sparse_optimizer):
+        raise ValueError(f"checkpoint sparse_optimizer {saved_opt!r} != config {config.training.sparse_optimizer!r}")
     emb = trainer.store
     rank = emb.rank  # shard coordinates of the tables (0 of 1 for replicated tables)
     saved_world = int(manifest.get("embedding_world_size", manifest["world_size"]))
@@ -160,41 +203,44 @@ def load_model_checkpoint(config, trainer, store: CheckpointStore, *, strict: bo
     if strict and missing:
         raise KeyError(f"dense parameters missing from the checkpoint: {missing[:5]}")
     dp.load_state_dict({"params": {n: v for n, v in dense.items() if n in dp.params}})
-    reshard = saved_world != emb.world
+    filled = {t.name: torch.zeros(t.local_rows, dtype=torch.bool) for t in emb.layouts}
+
+    def read(fname: str, only: set[str] | None) -> None:
+        payload = store.read_torch(fname)
+        saved_rank = int(payload["rank"])
+        if int(payload.get("world_size", saved_world)) != saved_world:
+            raise ValueError(f"{fname}: world size {payload.get('world_size')} != manifest {saved_world}")
+        for name, tab in payload["tables"].items():
+            if name not in emb.index:
+                if strict:
+                    raise KeyError(f"checkpoint table {name!r} is not in the model")
+                continue
+            if only is not None and name not in only:
+                continue
+            t = emb.layouts[emb.index[name]]
+            if (tab["num_embeddings"] != t.num_embeddings or tab["embedding_dim"] != t.dim
+                    or int(tab.get("padding_idx", 0)) != 0):
+                raise ValueError(f"table {name!r}: checkpoint (rows {tab['num_embeddings']}, dim "
+                                 f"{tab['embedding_dim']}, padding_idx {tab.get('padding_idx', 0)}) != model "
+                                 f"(rows {t.num_embeddings}, dim {t.dim}, padding_idx 0)")
+            _restore_rows(emb, name, t, tab, saved_rank, rank, filled[name])
+
+    same_world = saved_world == emb.world
     for chunk in manifest["chunks"]:
-        files = chunk["rank_files"] if reshard else [chunk["rank_files"][rank]]
-        for fname in files:
-            payload = store.read_torch(fname)
-            saved_rank = int(payload["rank"])
-            for name, tab in payload["tables"].items():
-                if name not in emb.index:
-                    if strict:
-                        raise KeyError(f"checkpoint table {name!r} is not in the model")
-                    continue
-                t = emb.layouts[emb.index[name]]
-                if tab["num_embeddings"] != t.num_embeddings or tab["embedding_dim"] != t.dim:
-                    raise ValueError(f"table {name!r}: checkpoint shape ({tab['num_embeddings']}, "
-                                     f"{tab['embedding_dim']}) != model ({t.num_embeddings}, {t.dim})")
-                w = tab["weight"]
-                acc = (tab.get("optimizer_state") or {}).get("sum")
-                dst_w = emb.weight(name)
-                dst_a = emb.accumulator(name)
-                if not reshard:
-                    if w.shape[0] != t.local_rows:
-                        raise ValueError(f"table {name!r}: {w.shape[0]} saved rows, {t.local_rows} local rows")
-                    dst_w.copy_(w.to(dst_w.device, dst_w.dtype))
-                    if acc is not None:
-                        dst_a.copy_(acc.to(dst_a.device, dst_a.dtype))
-                    continue
-                ids = _saved_ids(tab["shard_spec"], w.shape[0], saved_rank, t.num_embeddings)
-                mine = t.spec.owner(ids) == rank
-                if not bool(mine.any()):
-                    continue
-                local = t.spec.local_row_ids(ids[mine]).to(dst_w.device)
-                sel = mine.nonzero().flatten()
-                dst_w[local] = w[sel].to(dst_w.device, dst_w.dtype)
-                if acc is not None:
-                    dst_a[local] = acc[sel].to(dst_a.device, dst_a.dtype)
-            del payload
+        for fname in ([chunk["rank_files"][rank]] if same_world else chunk["rank_files"]):
+            read(fname, None)
+    if same_world:
+        # tables saved under another shard spec: their rows live in other ranks' files
+        saved_tables = {n for chunk in manifest["chunks"] for n in chunk["tables"]}
+        pending = {n for n, m in filled.items() if n in saved_tables and not bool(m.all())}
+        if pending:
+            for chunk in manifest["chunks"]:
+                if pending & set(chunk["tables"]):
+                    for r, fname in enumerate(chunk["rank_files"]):
+                        if r != rank:
+                            read(fname, pending)
+    incomplete = sorted(n for n, m in filled.items() if not bool(m.all()))
+    if incomplete:
+        raise ValueError("checkpoint did not cover all local rows for tables: " + ", ".join(incomplete))
     emb.sync_peers()
     return manifest

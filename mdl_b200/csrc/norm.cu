@@ -8,6 +8,7 @@
 // (mean, rstd), so only those two floats per row are kept from the forward.
 // gamma/beta and the per-token bias gradient of the producing layer are
 // accumulated per CTA in registers and folded by a second small kernel.
+#include <atomic>
 #include "common.cuh"
 #include "norm.h"
 
@@ -464,12 +465,18 @@ __global__ void __launch_bounds__(256) rms_bwd_kernel(const RMSArgs p) {
   }
 }
 
+// SM count of the current device, cached per device (atomics: callers may run on
+// any host thread, with any device current).
+constexpr int kMaxDevices = 64;
+std::atomic<int> g_sm_count[kMaxDevices];
+
 int sm_count() {
-  static int n = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+  int n = g_sm_count[dev].load(std::memory_order_relaxed);
   if (n == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+    g_sm_count[dev].store(n, std::memory_order_relaxed);
   }
   return n;
 }
@@ -500,21 +507,20 @@ int layernorm_bwd_grid(int B) {
   return B < cap ? (B > 0 ? B : 1) : cap;
 }
 
+size_t layernorm_bwd_smem(int T, int D) { return static_cast<size_t>(T > 8 ? T : 8) * D * sizeof(float); }
+
 cudaError_t layernorm_bwd(const LNBwdArgs& a, cudaStream_t stream) {
   if (a.D % 8 || a.T <= 0) return cudaErrorInvalidValue;
   if (a.mix && ((a.D % a.T) || ((a.D / a.T) % 8))) return cudaErrorInvalidValue;
   if (a.B == 0) return cudaSuccess;
   const int grid = a.grid > 0 ? a.grid : layernorm_bwd_grid(a.B);
-  const size_t smem = static_cast<size_t>(a.T > 8 ? a.T : 8) * a.D * sizeof(float);
-#define LNB(N)                                                                                    \
-  if (a.mix) {                                                                                    \
-    auto k = ln_bwd_kernel<N, true>;                                                              \
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)); \
-    k<<<grid, 256, smem, stream>>>(a);                                                            \
-  } else {                                                                                        \
-    auto k = ln_bwd_kernel<N, false>;                                                             \
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)); \
-    k<<<grid, 256, smem, stream>>>(a);                                                            \
+  const size_t smem = layernorm_bwd_smem(a.T, a.D);
+#define LNB(N)                                                                                         \
+  {                                                                                                    \
+    auto k = a.mix ? ln_bwd_kernel<N, true> : ln_bwd_kernel<N, false>;                                 \
+    cudaError_t ea = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)); \
+    if (ea != cudaSuccess) return ea;                                                                  \
+    k<<<grid, 256, smem, stream>>>(a);                                                                 \
   }
   MDL_NCH_DISPATCH(a.D, LNB)
 #undef LNB
@@ -608,8 +614,19 @@ extern "C" int mdl_layernorm_bwd_noalloc(const void* dy, const void* dy_bcast, f
   const long long max_grid = kNoAllocScratchFloats / per_cta;
   if (max_grid < 1) return noalloc_reject("mdl_layernorm_bwd_noalloc: D exceeds the 2 MiB scratch array");
   if (B == 0) return 0;
+  int dev = 0, smem_max = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  if (mdl::layernorm_bwd_smem(T, D) > static_cast<size_t>(smem_max)) {
+    char msg[200];
+    std::snprintf(msg, sizeof(msg),
+                  "mdl_layernorm_bwd_noalloc: max(T, 8) * D * 4 = %zu bytes of shared memory exceeds the device's %d",
+                  mdl::layernorm_bwd_smem(T, D), smem_max);
+    return noalloc_reject(msg);
+  }
   float* scratch = nullptr;
-  cudaError_t e = noalloc_scratch(&scratch);
+  e = noalloc_scratch(&scratch);
   if (e != cudaSuccess) return static_cast<int>(e);
   int grid = mdl::layernorm_bwd_grid(B);
   if (grid > max_grid) grid = static_cast<int>(max_grid);

@@ -47,6 +47,8 @@ struct LNBwdArgs {
   int grid = 0;  // number of CTAs (partials rows); 0 = choose
 };
 int layernorm_bwd_grid(int B);
+// Dynamic shared memory of one backward CTA: max(T, 8) * D fp32.
+size_t layernorm_bwd_smem(int T, int D);
 cudaError_t layernorm_bwd(const LNBwdArgs& a, cudaStream_t stream);
 
 // RMSNorm over rows of width D (fp32 statistics, reference src/model.py:4550-4568):

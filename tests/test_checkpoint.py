@@ -152,3 +152,39 @@ def test_commit_protocol_and_retention(tmp_path):
     removed = prune_run_directory(run, keep_last=2)
     assert removed == [step_directory_name(1)]
     assert [c.step for c in list_committed_checkpoints(run)] == [2, 3]
+
+
+def test_load_rejects_checkpoint_that_misses_a_table(tmp_path):
+    # a model table absent from the checkpoint must not keep its random init silently
+    import json
+
+    cfg, spec = _cfg()
+    model, tr = _trainer(cfg)
+    store = open_checkpoint_store(tmp_path / "ck")
+    save_model_checkpoint(cfg, tr, store)
+    manifest = json.loads((tmp_path / "ck" / "manifest.json").read_text())
+    dropped = manifest["chunks"][0]["tables"][0]
+    for fname in manifest["chunks"][0]["rank_files"]:
+        payload = torch.load(tmp_path / "ck" / fname, weights_only=False)
+        payload["tables"].pop(dropped)
+        torch.save(payload, tmp_path / "ck" / fname)
+    manifest["chunks"][0]["tables"].remove(dropped)
+    (tmp_path / "ck" / "manifest.json").write_text(json.dumps(manifest))
+    _model2, tr2 = _trainer(cfg, seed=7)
+    with pytest.raises(ValueError, match="did not cover all local rows"):
+        load_model_checkpoint(cfg, tr2, store)
+
+
+def test_load_rejects_padding_idx_mismatch(tmp_path):
+    cfg, spec = _cfg()
+    model, tr = _trainer(cfg)
+    store = open_checkpoint_store(tmp_path / "ck")
+    save_model_checkpoint(cfg, tr, store)
+    fname = tmp_path / "ck" / "shard-0000-rank-00000-of-00001.pt"
+    payload = torch.load(fname, weights_only=False)
+    first = next(iter(payload["tables"]))
+    payload["tables"][first]["padding_idx"] = 3
+    torch.save(payload, fname)
+    _model2, tr2 = _trainer(cfg, seed=7)
+    with pytest.raises(ValueError, match="padding_idx"):
+        load_model_checkpoint(cfg, tr2, store)

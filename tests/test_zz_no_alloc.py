@@ -51,42 +51,77 @@ def _case(B, T, D, mix, seed):
     return x, (None if mix else r), gamma, dy, mean, rstd
 
 
-def _regular(x, r, gamma, dy, mean, rstd, B, T, D, mix):
+def _regular(x, r, gamma, dy, mean, rstd, B, T, D, mix, bcast=None, scale=1.0, want_dx2=False):
     from mdl_b200.ops._ext import ext
 
     C = ext()
     dx = torch.empty_like(x)
+    dx2 = torch.empty_like(x) if want_dx2 else None
     dg = torch.zeros(D, device="cuda")
     db = torch.zeros(D, device="cuda")
     grid = C.ln_bwd_grid(B)
     partials = torch.empty(grid, 2 * D, device="cuda")
-    C.ln_bwd(dy, None, 1.0, x, r, mean, rstd, gamma, dx, None, partials, dg, db, B, T, D, mix, grid)
-    return dx, dg, db
+    C.ln_bwd(None if bcast is not None else dy, bcast, scale, x, r, mean, rstd, gamma, dx, dx2, partials, dg, db,
+             B, T, D, mix, grid)
+    return dx, dg, db, dx2
 
 
-def _noalloc(lib, x, r, gamma, dy, mean, rstd, B, T, D, mix):
+def _noalloc(lib, x, r, gamma, dy, mean, rstd, B, T, D, mix, bcast=None, scale=1.0, want_dx2=False):
     dx = torch.empty_like(x)
+    dx2 = torch.empty_like(x) if want_dx2 else None
     dg = torch.zeros(D, device="cuda")
     db = torch.zeros(D, device="cuda")
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-    rc = lib.mdl_layernorm_bwd_noalloc(_ptr(dy), None, 1.0, _ptr(x), _ptr(r), _ptr(mean), _ptr(rstd), _ptr(gamma),
-                                       _ptr(dx), None, _ptr(dg), _ptr(db), B, T, D, int(mix), stream)
+    rc = lib.mdl_layernorm_bwd_noalloc(_ptr(None if bcast is not None else dy), _ptr(bcast), scale, _ptr(x), _ptr(r),
+                                       _ptr(mean), _ptr(rstd), _ptr(gamma), _ptr(dx), _ptr(dx2), _ptr(dg), _ptr(db),
+                                       B, T, D, int(mix), stream)
     assert rc == 0, lib.mdl_noalloc_last_error().decode()
-    return dx, dg, db
+    return dx, dg, db, dx2
+
+
+def _check(got, ref):
+    torch.cuda.synchronize()
+    torch.testing.assert_close(got[0].float(), ref[0].float(), atol=8e-2, rtol=3e-2)
+    torch.testing.assert_close(got[1], ref[1], atol=0.5, rtol=2e-2)
+    torch.testing.assert_close(got[2], ref[2], atol=0.5, rtol=2e-2)
+    if ref[3] is not None:
+        torch.testing.assert_close(got[3].float(), ref[3].float(), atol=8e-2, rtol=3e-2)
 
 
 @pytest.mark.parametrize("mix", [True, False])
 def test_noalloc_matches_regular_entry_point_twice(mix):
     lib = _lib()
-    B, T, D = 300, 16, 768
-    for seed in (1, 2):  # two calls in a row: the second must not see the first's leftovers
+    T, D = 16, 768
+    # Two calls in a row. The first (B=2048) fills every row of the array the CTA
+    # cap allows (341 CTAs at D=768); the second uses fewer CTAs (B=300), so a call
+    # that read rows it did not write would pick up the first call's partial sums.
+    for seed, B in ((1, 2048), (2, 300)):
         x, r, gamma, dy, mean, rstd = _case(B, T, D, mix, seed)
         ref = _regular(x, r, gamma, dy, mean, rstd, B, T, D, mix)
         got = _noalloc(lib, x, r, gamma, dy, mean, rstd, B, T, D, mix)
-        torch.cuda.synchronize()
-        torch.testing.assert_close(got[0].float(), ref[0].float(), atol=8e-2, rtol=3e-2)
-        torch.testing.assert_close(got[1], ref[1], atol=0.5, rtol=2e-2)
-        torch.testing.assert_close(got[2], ref[2], atol=0.5, rtol=2e-2)
+        _check(got, ref)
+
+
+def test_noalloc_cta_cap_at_wide_rows():
+    # D=2048 leaves room for 128 CTAs in the array; B=600 would otherwise take 600 or more
+    lib = _lib()
+    T, D = 16, 2048
+    for seed, B in ((3, 600), (4, 50)):
+        x, r, gamma, dy, mean, rstd = _case(B, T, D, False, seed)
+        ref = _regular(x, r, gamma, dy, mean, rstd, B, T, D, False)
+        got = _noalloc(lib, x, r, gamma, dy, mean, rstd, B, T, D, False)
+        _check(got, ref)
+
+
+def test_noalloc_broadcast_gradient_and_second_copy():
+    # dy[b, t, :] = dy_bcast[b, :] * scale (backward of a token mean), plus the dx2 copy
+    lib = _lib()
+    B, T, D = 700, 16, 768
+    x, r, gamma, dy, mean, rstd = _case(B, T, D, True, 5)
+    bcast = torch.randn(B, D, device="cuda").bfloat16()
+    ref = _regular(x, r, gamma, dy, mean, rstd, B, T, D, True, bcast=bcast, scale=1.0 / T, want_dx2=True)
+    got = _noalloc(lib, x, r, gamma, dy, mean, rstd, B, T, D, True, bcast=bcast, scale=1.0 / T, want_dx2=True)
+    _check(got, ref)
 
 
 def test_noalloc_rejects_sizes_beyond_its_limits():
@@ -96,3 +131,8 @@ def test_noalloc_rejects_sizes_beyond_its_limits():
                                        None, None, 4, 1, 4096, 0, None)
     assert rc == -1
     assert b"2048" in lib.mdl_noalloc_last_error()
+    # 32 tokens of 2048 columns need 256 KB of shared memory per CTA, above the device limit
+    rc = lib.mdl_layernorm_bwd_noalloc(_ptr(x), None, 1.0, _ptr(x), None, _ptr(x), _ptr(x), None, _ptr(x), None,
+                                       None, None, 4, 32, 2048, 0, None)
+    assert rc == -1
+    assert b"shared memory" in lib.mdl_noalloc_last_error()
