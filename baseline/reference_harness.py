@@ -63,6 +63,8 @@ def reference_mapping(mapping: dict, cuda_graphs: bool) -> dict:
     if model.pop("pyramid_schedule", "linear") != "linear":
         model["final_s_tokens"] = 32
     model.pop("pyramid_halve_every", None)
+    # the reference has one token per scene (workload 3 asks for 4; recorded in the result)
+    model.pop("tokens_per_scenario", None)
     model.pop("sequence_head", None)
     m.setdefault("vocab_strategy", {"defaults": {}, "features": {}})
     m["runtime"]["cuda_graph_backbone"] = bool(cuda_graphs)
@@ -107,7 +109,7 @@ def to_feature_batch(rdata, packed, plan, device=None, sequences=None):
                   enumerate(field_names)}
         features[name] = {"fields": fields, "lengths": lengths.clone()}
     batch = rdata.FeatureBatch(features=features, labels=packed.labels.clone(), label_mask=None,
-                               scenario_id=torch.zeros(rows, dtype=torch.long), group_id=[])
+                               scenario_id=packed.scenario_id.clone().long(), group_id=[])
     if device is not None:
         batch = rdata.move_feature_batch(batch, device)
     return batch
@@ -121,6 +123,8 @@ class ReferenceTrainer:
         rconfig, rdata, rtrain, roptim = _import_reference()
         self.rdata, self.rtrain = rdata, rtrain
         ref_map = reference_mapping(mapping, cuda_graphs and device.type == "cuda")
+        if device.type != "cuda":  # CPU runs (tests): fp32 and the reference's SDPA attention
+            ref_map["runtime"].update({"device": "cpu", "precision": "fp32", "attention_backend": "sdpa"})
         with tempfile.NamedTemporaryFile("w", suffix=".yaml", delete=False) as fh:
             yaml.safe_dump(ref_map, fh)
             path = fh.name
@@ -146,11 +150,11 @@ class ReferenceTrainer:
                 sharded, lr=lr, lr_decay=t.adagrad_lr_decay, weight_decay=t.adagrad_weight_decay,
                 initial_accumulator_value=t.adagrad_initial_accumulator_value, eps=t.adagrad_eps))
         replicated = list(groups.embedding_optimizer)
+        # tables the reference replicates on every rank (src/train.py:6582-6630): its
+        # rank-0 broadcast at start and its touched-row gradient synchronizer per step
+        rtrain._synchronize_sparse_parameter_replicas(self.context, groups.sparse_sync)
+        self.sparse_sync = rtrain._ReplicatedSparseGradientSynchronizer(self.context, groups.sparse_sync)
         if replicated:
-            # small tables the reference replicates (src/train.py:6619-6630); their
-            # cross-rank sparse sync is not reproduced here, so one rank only
-            if world > 1:
-                raise RuntimeError("replicated embedding tables with more than one rank are not wired here")
             self.optimizers.append(torch.optim.Adagrad(
                 replicated, lr=t.lr_sparse or t.lr_dense, lr_decay=t.adagrad_lr_decay,
                 weight_decay=t.adagrad_weight_decay,
@@ -167,24 +171,18 @@ class ReferenceTrainer:
                 loss_reduction=self.config.training.loss_reduction, task_loss_weights=None, rank_active=True,
                 active_rank_count=self.context.world_size)
         loss.backward()
+        self.sparse_sync.synchronize(rank_active=True)
         for opt in self.optimizers:
             opt.step()
         return loss.detach()
 
 
-def run(args, rank: int, world: int, local: int) -> dict:
-    from mdl_b200.data.baseline_configs import baseline_config
-    from mdl_b200.data.synthetic import BatchPool, SyntheticGenerator
-    from mdl_b200.models.features import FeatureEncoder  # noqa: F401  (plan only, no tables on this path)
-    from mdl_b200.ops.embedding import LookupFeature, LookupPlan, POOL_MEAN, POOL_NONE, POOL_SUM
-    from mdl_b200.utils.clocks import ClockSampler
+def synthetic_plan(mapping: dict, spec):
+    """A lookup plan of the workload's feature order, only to drive the shared
+    synthetic generator (no tables are built on this path)."""
 
-    device = torch.device("cuda", local)
-    mapping, spec = baseline_config(args.config, batch=args.batch)
-    torch.manual_seed(1234)
-    trainer = ReferenceTrainer(mapping, device=device, rank=rank, world=world, local=local,
-                               cuda_graphs=not getattr(args, "ref_no_graphs", False))
-    # a lookup plan of the same feature order, only to drive the shared synthetic generator
+    from mdl_b200.ops.embedding import LookupFeature, LookupPlan, POOL_MEAN, POOL_NONE, POOL_SUM
+
     feats, col = [], 0
     for f in mapping["features"]:
         if f["kind"] == "dense":
@@ -194,7 +192,32 @@ def run(args, rank: int, world: int, local: int) -> dict:
             pool = {"none": POOL_NONE, "mean": POOL_MEAN, "sum": POOL_SUM}[f.get("pooling", "none")]
             feats.append(LookupFeature(f["name"], f["name"], pooling=pool, width=f["embedding_dim"], out_col=col))
             col += f["embedding_dim"]
-    plan = LookupPlan(feats, out_width=col, dense_width=spec.dense_width)
+    return LookupPlan(feats, out_width=col, dense_width=spec.dense_width)
+
+
+def reference_batches(trainer: "ReferenceTrainer", mapping: dict, spec, batch: int, count: int, rank: int = 0,
+                      device=None):
+    """``count`` seeded synthetic batches of the workload as the reference's FeatureBatch."""
+
+    from mdl_b200.data.synthetic import SyntheticGenerator
+
+    plan = synthetic_plan(mapping, spec)
+    gen = SyntheticGenerator(plan, spec, rank=rank)
+    seqs = {s["name"]: [fl["name"] for fl in s["fields"]] for s in mapping.get("sequences", [])}
+    return [to_feature_batch(trainer.rdata, gen.batch(batch), plan, device, seqs) for _ in range(count)]
+
+
+def run(args, rank: int, world: int, local: int) -> dict:
+    from mdl_b200.data.baseline_configs import baseline_config
+    from mdl_b200.data.synthetic import BatchPool, SyntheticGenerator
+    from mdl_b200.utils.clocks import ClockSampler
+
+    device = torch.device("cuda", local)
+    mapping, spec = baseline_config(args.config, batch=args.batch, **({"mdl": True} if args.mdl else {}))
+    torch.manual_seed(1234)
+    trainer = ReferenceTrainer(mapping, device=device, rank=rank, world=world, local=local,
+                               cuda_graphs=not getattr(args, "ref_no_graphs", False))
+    plan = synthetic_plan(mapping, spec)
     gen = SyntheticGenerator(plan, spec, rank=rank)
     pool = BatchPool(gen, args.batch, count=args.pool, pin=False)
     rd = trainer.rdata
@@ -259,7 +282,10 @@ def run(args, rank: int, world: int, local: int) -> dict:
                      "pooling mean (no sum in the reference); cuda_graph_backbone="
                      + str(bool(trainer.config.runtime.cuda_graph_backbone))
                      + (f"; pyramid linear, final_s_tokens={trainer.config.model.final_s_tokens}"
-                        if trainer.config.model.name == "onetrans" else ""),
+                        if trainer.config.model.name == "onetrans" else "")
+                     + ("; 1 scenario token per scene (the reference has no tokens_per_scenario; ours uses "
+                        f"{mapping['model'].get('tokens_per_scenario', 1)})"
+                        if trainer.config.model.name == "mdl_rankmixer" else ""),
             "global_batch": args.batch * world,
             "seq_len": (mapping.get("sequences") or [{}])[0].get("max_length"),
             "parallelism": f"ddp{world}+sharded-embeddings{world}",

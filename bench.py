@@ -94,6 +94,8 @@ def run_ours(args) -> dict:
         mapping["model"]["pyramid_schedule"] = args.pyramid
         if args.pyramid == "linear":
             mapping["model"]["final_s_tokens"] = 32
+    if args.comm:
+        mapping["training"]["comm"] = args.comm
     cfg = app_config_from_mapping(mapping)
     torch.manual_seed(1234)
     pg = dist.group.WORLD if world > 1 else None
@@ -180,14 +182,10 @@ def run_ours(args) -> dict:
 def run_reference(args) -> dict:
     """The unmodified reference on the same workload (see baseline/reference_harness.py)."""
 
-    if args.mdl:
-        return {"impl": "reference", "unavailable": "reference arm is wired for workloads 2 and 4; the MDL variant of "
-                                                     "workload 4 needs MDL priors the harness does not build"}
-    if args.config not in (2, 4):
-        return {"impl": "reference", "unavailable": f"reference arm is wired for workloads 2 and 4 (asked {args.config}); "
-                                                     "workload 3 needs MDL priors the harness does not build, workload 5 "
-                                                     "combines LONGER with a MixFormer head, which the reference has no "
-                                                     "model for"}
+    if args.config not in (2, 3, 4):
+        return {"impl": "reference", "unavailable": f"reference arm runs workloads 2, 3 and 4 (asked {args.config}); "
+                                                     "workload 5 combines LONGER with a MixFormer head, which the "
+                                                     "reference has no model for"}
     if args.batch is None:
         args.batch = DEFAULT_BATCH[args.config]
     try:
@@ -214,6 +212,8 @@ def main(argv=None) -> int:
                    help="workload 4: pyramid schedule (linear = the reference's, final_s_tokens 32)")
     p.add_argument("--mdl", action="store_true", help="workload 4: its MDL variant (mdl_onetrans)")
     p.add_argument("--ref-no-graphs", action="store_true", help="reference arm: disable its CUDA-graph backbone")
+    p.add_argument("--comm", choices=["fused", "nccl"], default=None,
+                   help="dense gradient exchange: fused NVLink kernel (default) or the NCCL baseline")
     args = p.parse_args(argv)
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

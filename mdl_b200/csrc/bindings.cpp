@@ -568,6 +568,14 @@ at::Tensor tensor_from_ptr(int64_t ptr_, int64_t numel, at::ScalarType dtype, in
   return torch::from_blob(reinterpret_cast<void*>(ptr_), {numel}, opts);
 }
 
+void mbar_timeout_selftest(const at::Tensor& err, const at::Tensor& returned) {
+  c10::cuda::CUDAGuard guard(err.device());
+  TORCH_CHECK(err.scalar_type() == at::kInt && returned.scalar_type() == at::kInt, "int32 words");
+  check(mdl::mbar_timeout_selftest(err.data_ptr<int>(), returned.data_ptr<int>(), stream_of(err)),
+        "mbar_timeout_selftest");
+  g_launches += 1;
+}
+
 void set_barrier_limit(double seconds) { mdl::set_barrier_limit_ns(static_cast<uint64_t>(seconds * 1e9)); }
 
 void barrier(const std::vector<int64_t>& signals, const at::Tensor& counter, int64_t rank,
@@ -862,6 +870,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_free", &ipc_free);
   m.def("tensor_from_ptr", &tensor_from_ptr);
   m.def("set_barrier_limit", &set_barrier_limit);
+  m.def("mbar_timeout_selftest", &mbar_timeout_selftest);
   m.def("barrier", &barrier);
   m.def("dense_sync", &dense_sync);
   m.def("small_allreduce", &small_allreduce);

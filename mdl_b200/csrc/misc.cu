@@ -375,6 +375,23 @@ cudaError_t clip_factor(const float* sum_sq, float max_norm, float* clip, cudaSt
   return cudaGetLastError();
 }
 
+namespace {
+// One thread waits on an mbarrier that nothing arrives on: the bounded wait runs
+// out, records MDL_ERR_MBAR_TIMEOUT and the kernel returns (self-test of the
+// timeout path every tcgen05 pipeline in this library relies on).
+__global__ void mbar_timeout_selftest_kernel(int* err, int* returned) {
+  __shared__ __align__(8) uint64_t bar;
+  mbar_init(&bar, 1);
+  fence_barrier_init();
+  if (!mbar_wait(&bar, 0, err, nullptr)) atomicAdd(returned, 1);
+}
+}  // namespace
+
+cudaError_t mbar_timeout_selftest(int* err, int* returned, cudaStream_t stream) {
+  mbar_timeout_selftest_kernel<<<1, 1, 0, stream>>>(err, returned);
+  return cudaGetLastError();
+}
+
 cudaError_t cast_f32_bf16(const float* src, void* dst, long long n, cudaStream_t stream) {
   if (n == 0) return cudaSuccess;
   cast_kernel<<<grid_for(n), 256, 0, stream>>>(src, reinterpret_cast<__nv_bfloat16*>(dst), n);

@@ -73,5 +73,8 @@ cudaError_t grad_sqnorm(const float* grad, long long n, float grad_scale, float*
 cudaError_t clip_factor(const float* sum_sq, float max_norm, float* clip, cudaStream_t stream);
 // dst(bf16) = src(fp32)
 cudaError_t cast_f32_bf16(const float* src, void* dst, long long n, cudaStream_t stream);
+// Waits on an mbarrier that never completes; the bounded wait records
+// MDL_ERR_MBAR_TIMEOUT in *err and increments *returned (test of the timeout path).
+cudaError_t mbar_timeout_selftest(int* err, int* returned, cudaStream_t stream);
 
 }  // namespace mdl

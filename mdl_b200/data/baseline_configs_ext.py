@@ -18,8 +18,9 @@ Workload 3, MDL on the RankMixer backbone of workload 2:
 * a scene id uniform over 5 scenes (``scene_id``, embedding scope
   ``scenario``) feeds the scenario tokens: 4 tokens per scene plus the global
   token (``tokens_per_scenario: 4``);
-* one prior feature per task (``prior_<task>``, scope ``task``) feeds each
-  task token;
+* one prior feature per scene (``prior_scene<i>``, scope ``scenario``) and one
+  per task (``prior_<task>``, scope ``task``) are the token-unique priors of each
+  scenario / task token;
 * scene-conditioned feature bias (FiLM on the feature tokens);
 * click / like / finish heads at positive rates 0.08 / 0.02 / 0.3, whose
   ground truth depends on the scene;
@@ -49,9 +50,8 @@ def config3(num_fields: int = 300, batch: int = 2048, tokens_per_scenario: int =
     m["tokenization"] = {
         "feature_tokenizer": "rankmixer",
         "num_feature_tokens": 16,
-        "scenario_tokens": [{"name": s, "important_inputs": ["scene_id"]} for s in scenes]
-        + [{"name": "global", "important_inputs": ["scene_id"]}],
-        "task_tokens": [{"name": t, "important_inputs": [f"prior_{t}"]} for t in tasks],
+        "scenario_tokens": _scenario_tokens(scenes),
+        "task_tokens": _task_tokens(tasks),
     }
     m["model"].update({"embedding_dim": 64, "token_dim": 768, "num_layers": 2, "num_heads": 12, "hidden_dim": 3072,
                        "task_head_hidden_dim": 1536, "ffn_activation": "gelu", "scene_feature_bias": scene_feature_bias,
@@ -63,6 +63,15 @@ def config3(num_fields: int = 300, batch: int = 2048, tokens_per_scenario: int =
     return m, spec
 
 
+def _scenario_tokens(scenes: list[str]) -> list[dict]:
+    return ([{"name": s, "important_inputs": ["scene_id"], "prior_inputs": [f"prior_{s}"]} for s in scenes]
+            + [{"name": "global", "important_inputs": ["scene_id"]}])
+
+
+def _task_tokens(tasks: dict) -> list[dict]:
+    return [{"name": t, "important_inputs": [f"prior_{t}"], "prior_inputs": [f"prior_{t}"]} for t in tasks]
+
+
 def _add_mdl_domains(m: dict, feats: list[dict], fields: dict, tasks: dict, tokens_per_scenario: int) -> list[str]:
     """Scene id (scope ``scenario``) and one prior per task (scope ``task``) as the
     inputs of the scenario / task tokens; returns the scene names."""
@@ -71,6 +80,13 @@ def _add_mdl_domains(m: dict, feats: list[dict], fields: dict, tasks: dict, toke
     feats.append({"name": "scene_id", "kind": "categorical", "source": "scene_id", "embedding_dim": 64,
                   "embedding_scope": "scenario", "encoding": {"type": "identity", "max_id": MDL_SCENES}})
     fields["scene_id"] = FieldSpec(vocab=MDL_SCENES)
+    # one scenario-scoped prior per scene (the reference requires a token-unique prior
+    # for every scenario token once there are several scenes)
+    for s in scenes:
+        name = f"prior_{s}"
+        feats.append({"name": name, "kind": "categorical", "source": name, "embedding_dim": 64,
+                      "embedding_scope": "scenario", "encoding": {"type": "identity", "max_id": 1000}})
+        fields[name] = FieldSpec(vocab=1000)
     for task in tasks:
         name = f"prior_{task}"
         feats.append({"name": name, "kind": "categorical", "source": name, "embedding_dim": 64,
@@ -120,9 +136,8 @@ def config4(num_fields: int = 300, batch: int = 1024, seq_len: int = 512, side_f
     scene_kw = {}
     if mdl:
         scenes = _add_mdl_domains(m, feats, fields, tasks, 1)
-        m["tokenization"]["scenario_tokens"] = ([{"name": s, "important_inputs": ["scene_id"]} for s in scenes]
-                                                + [{"name": "global", "important_inputs": ["scene_id"]}])
-        m["tokenization"]["task_tokens"] = [{"name": t, "important_inputs": [f"prior_{t}"]} for t in tasks]
+        m["tokenization"]["scenario_tokens"] = _scenario_tokens(scenes)
+        m["tokenization"]["task_tokens"] = _task_tokens(tasks)
         m["model"]["experimental_model_acknowledged"] = True
         scene_kw = dict(num_scenarios=MDL_SCENES, scene_field="scene_id", scene_effect=0.5)
     spec = SyntheticSpec(fields=fields, dense_width=64, task_rates=list(tasks.values()), zipf_s=1.05, seed=0,

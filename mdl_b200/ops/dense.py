@@ -53,8 +53,12 @@ class DenseParams:
                  bf16_names: set[str] | None = None, world: int = 1, rank: int = 0, process_group=None,
                  optimizer: str = "adam", lr: float = 1e-3, betas=(0.9, 0.999), eps: float = 1e-8,
                  weight_decay: float = 0.0, rmsprop_alpha: float = 0.99, comm: str = "fused",
-                 buckets: list[list[str]] | None = None, overlap: bool = False) -> None:
+                 buckets: list[list[str]] | None = None, overlap: bool = False, peers=None) -> None:
+        """``peers``: an ``EmulatedPeers`` to lay several ranks out on one GPU (tests of
+        the fused multi-rank update); by default ranks are processes joined over CUDA IPC."""
+
         self.device = torch.device(device)
+        self._peers = peers
         self.world, self.rank, self.group = world, rank, process_group
         self.optimizer, self.lr, self.betas, self.eps = optimizer, lr, betas, eps
         self.weight_decay, self.rmsprop_alpha = weight_decay, rmsprop_alpha
@@ -128,8 +132,11 @@ class DenseParams:
         if dev.type == "cuda" and self.world > 1 and self.comm == "fused":
             from ..parallel.symm import SymmetricBuffers
 
-            self._symm = SymmetricBuffers({"master": (n, torch.float32), "grad": (n, torch.float32),
-                                           "shadow": (n, torch.bfloat16)}, device=dev, process_group=self.group)
+            spec = {"master": (n, torch.float32), "grad": (n, torch.float32), "shadow": (n, torch.bfloat16)}
+            if self._peers is not None:
+                self._symm = self._peers.buffers("dense", self.rank, spec)
+            else:
+                self._symm = SymmetricBuffers(spec, device=dev, process_group=self.group)
             self.master = self._symm.local("master")
             self.grad = self._symm.local("grad")
             self.shadow = self._symm.local("shadow")
@@ -214,6 +221,17 @@ class DenseParams:
         else:
             C.rmsprop(self.master[sl], self.grad[sl], self.state1[sl], shadow, h["lr"], self.rmsprop_alpha, self.eps,
                       self.weight_decay, scale, None, True, max_blocks)
+
+    @torch.no_grad()
+    def update_buckets(self, lr: float | None = None) -> None:
+        """One optimizer step of this rank's buckets without the closing barrier and
+        gradient reset of ``step``: with emulated peers the caller issues every rank's
+        update, then resets the gradients, in stream order."""
+
+        self.step_count += 1
+        h = self._hyper(self.lr if lr is None else lr)
+        for k in range(len(self.buckets)):
+            self._update_bucket(k, h)
 
     @torch.no_grad()
     def step(self, lr: float | None = None, clip_norm: float | None = None) -> torch.Tensor | None:

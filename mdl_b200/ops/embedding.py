@@ -64,12 +64,14 @@ class EmbeddingStore:
                  world: int, device: torch.device, init_std: float = 0.02, lr: float = 0.01, eps: float = 1e-10,
                  initial_accumulator_value: float = 0.1,
                  process_group=None, base_seed: int | None = None, optimizer: str = "rowwise",
-                 lr_decay: float = 0.0, replicas: int = 1, replica_group=None) -> None:
+                 lr_decay: float = 0.0, replicas: int = 1, replica_group=None, peers=None) -> None:
         """``world`` / ``rank`` describe the table sharding; ``replicas > 1`` makes every
         rank of ``replica_group`` hold a full copy (``world == 1``) whose touched-row
         gradients are summed across the replicas before each update.
         ``optimizer``: ``rowwise`` (one accumulator per row) or ``full`` (one per element,
-        ``torch.optim.Adagrad`` semantics); ``lr_decay`` gives ``lr / (1 + (step - 1) * lr_decay)``."""
+        ``torch.optim.Adagrad`` semantics); ``lr_decay`` gives ``lr / (1 + (step - 1) * lr_decay)``.
+        ``peers``: an ``EmulatedPeers`` to lay several ranks out on one GPU (tests of the
+        multi-rank kernels); by default ranks are processes joined over CUDA IPC."""
 
         if optimizer not in ("rowwise", "full"):
             raise ValueError(f"sparse optimizer layout {optimizer!r}")
@@ -85,6 +87,7 @@ class EmbeddingStore:
         self.replicas = int(replicas)
         self.replica_group = replica_group
         self.process_group = process_group
+        self._peers = peers
         self.layouts: list[TableLayout] = []
         self.index: dict[str, int] = {}
         elem = 0
@@ -136,15 +139,15 @@ class EmbeddingStore:
         if dev.type == "cuda" and self.world > 1:
             from ..parallel import symm
 
-            self._symm = symm.SymmetricBuffers(
-                {
-                    "slab": (self.total_elems, torch.float32),
-                    "grad": (self.total_elems, torch.float32),
-                    "flags": (flag_len, torch.uint8),
-                },
-                device=dev,
-                process_group=self.process_group,
-            )
+            spec = {
+                "slab": (self.total_elems, torch.float32),
+                "grad": (self.total_elems, torch.float32),
+                "flags": (flag_len, torch.uint8),
+            }
+            if self._peers is not None:
+                self._symm = self._peers.buffers("store", self.rank, spec)
+            else:
+                self._symm = symm.SymmetricBuffers(spec, device=dev, process_group=self.process_group)
             self.slab = self._symm.local("slab")
             self.grad = self._symm.local("grad")
             self.flags = self._symm.local("flags")
@@ -656,8 +659,12 @@ class _Exchange:
         from ..parallel.symm import SymmetricBuffers
 
         dev = store.device
-        t = torch.tensor([n_ids, rows], dtype=torch.int64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=store.process_group)
+        peers = store._peers
+        if peers is not None:  # emulated ranks: sizes given up front
+            t = torch.tensor([max(n_ids, peers.exchange_ids), max(rows, peers.exchange_rows)], dtype=torch.int64)
+        else:
+            t = torch.tensor([n_ids, rows], dtype=torch.int64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=store.process_group)
         if max((lay.local_rows for lay in store.layouts), default=0) >= 2 ** 31:
             raise ValueError("owner-push lookup keeps 32-bit local row indices")
         if len(plan.features) >= 2 ** 16:
@@ -667,10 +674,13 @@ class _Exchange:
         self.cap_bundles = max(1, len(plan.features) * self.rows_cap)
         self.cap_rows = 2 * int(t[0]) + 4096
         self.n_out = (self.rows_cap * plan.out_ld + 7) // 8 * 8
-        self.symm = SymmetricBuffers({"bundles": (W * self.cap_bundles * 4, torch.int32),
-                                      "rows": (W * self.cap_rows, torch.int32), "counts": (16, torch.int32),
-                                      "acc": (self.n_out, torch.float32), "grad": (self.n_out, torch.bfloat16)},
-                                     device=dev, process_group=store.process_group)
+        spec = {"bundles": (W * self.cap_bundles * 4, torch.int32), "rows": (W * self.cap_rows, torch.int32),
+                "counts": (16, torch.int32), "acc": (self.n_out, torch.float32),
+                "grad": (self.n_out, torch.bfloat16)}
+        if peers is not None:
+            self.symm = peers.buffers(("exchange", len(store._exchanges)), store.rank, spec)
+        else:
+            self.symm = SymmetricBuffers(spec, device=dev, process_group=store.process_group)
         self.counts = self.symm.local("counts")
         self.acc = self.symm.local("acc")
         self.grad = self.symm.local("grad")
@@ -726,40 +736,81 @@ def _exchange(store: EmbeddingStore, plan: LookupPlan, ids: torch.Tensor, rows: 
     return ex
 
 
-def _owner_forward(store, plan, ids, offsets, dense, rows):
-    """Multi-rank lookup: route (bag, owner) bundles, owners push pooled vectors back."""
+def owner_route(store, plan, ids, offsets, dense, rows) -> _Exchange:
+    """Owner-push lookup, phase 1 (this rank as requester): zero this rank's
+    accumulator and route its bags into per-(bag, owner) bundles in each owner's
+    staging (dense columns are written into the accumulator directly)."""
 
     C = ext()
     ex = _exchange(store, plan, ids, rows)
     meta, chunks, max_vec = plan.device_meta(store, rows)
-    err = error_word(ids.device)
     ex.counts.zero_()
     ex.acc[:rows * plan.out_ld].zero_()
     bundles, row_lists, counts, capb, capr = ex.ptrs()
     C.emb_route(meta, store.peer_ptrs("slab"), store.rank, ids, offsets, bundles, row_lists, counts, capb, capr,
-                ex.acc, dense, plan.dense_width, chunks, err, max_vec)
-    ex.symm.barrier()  # every rank's bundles routed, every accumulator zeroed
-    C.emb_owner_forward(meta, store.peer_ptrs("slab"), store.rank, ids, offsets, bundles, row_lists, counts, capb,
-                        capr, ex.symm.peer_ptrs("acc"), store.max_dim, err)
-    ex.symm.barrier()  # every owner's vectors have landed
+                ex.acc, dense, plan.dense_width, chunks, error_word(ids.device), max_vec)
+    return ex
+
+
+def owner_push(store, plan, ids, offsets, rows) -> None:
+    """Phase 2 (this rank as owner; every rank has routed): gather and pool the rows
+    of every bundle routed to this rank from local HBM and add each pooled vector
+    into its requester's accumulator over NVLink."""
+
+    ex = _exchange(store, plan, ids, rows)
+    meta, _chunks, _max_vec = plan.device_meta(store, rows)
+    bundles, row_lists, counts, capb, capr = ex.ptrs()
+    ext().emb_owner_forward(meta, store.peer_ptrs("slab"), store.rank, ids, offsets, bundles, row_lists, counts, capb,
+                            capr, ex.symm.peer_ptrs("acc"), store.max_dim, error_word(ids.device))
+
+
+def owner_collect(store, plan, ids, rows) -> torch.Tensor:
+    """Phase 3 (every owner has pushed): the accumulator as the bf16 lookup output."""
+
+    ex = _exchange(store, plan, ids, rows)
     out = torch.empty(rows, plan.out_ld, dtype=torch.bfloat16, device=ids.device)
-    C.emb_acc_to_bf16(ex.acc, out)
+    ext().emb_acc_to_bf16(ex.acc, out)
     return out
+
+
+def owner_stage_grad(store, plan, ids, grad_out, rows) -> None:
+    """Backward, phase 1 (this rank as requester): stage d(out) in peer-visible memory."""
+
+    ex = _exchange(store, plan, ids, rows)
+    g = grad_out if grad_out.dtype == torch.bfloat16 else grad_out.to(torch.bfloat16)
+    ex.grad[:g.numel()].copy_(g.reshape(-1))
+
+
+def owner_pull_grad(store, plan, ids, offsets, rows) -> None:
+    """Backward, phase 2 (this rank as owner; every requester has staged): read each
+    bundle's d(out) slice from its requester once and add it into every local row of
+    the bundle, marking the rows touched for the sparse optimizer."""
+
+    ex = _exchange(store, plan, ids, rows)
+    meta, _chunks, _max_vec = plan.device_meta(store, rows)
+    bundles, row_lists, counts, capb, capr = ex.ptrs()
+    ext().emb_owner_backward(meta, store.peer_ptrs("slab"), store.peer_ptrs("grad"), store.peer_ptrs("flags"),
+                             store.rank, ids, offsets, bundles, row_lists, counts, capb, capr,
+                             ex.symm.peer_ptrs("grad"), store.max_dim, error_word(ids.device))
+
+
+def _owner_forward(store, plan, ids, offsets, dense, rows):
+    """Multi-rank lookup: route (bag, owner) bundles, owners push pooled vectors back."""
+
+    ex = owner_route(store, plan, ids, offsets, dense, rows)
+    ex.symm.barrier()  # every rank's bundles routed, every accumulator zeroed
+    owner_push(store, plan, ids, offsets, rows)
+    ex.symm.barrier()  # every owner's vectors have landed
+    return owner_collect(store, plan, ids, rows)
 
 
 def _owner_backward(store, plan, ids, offsets, grad_out, rows):
     """Multi-rank gradient: owners pull each requester's d(out) slices into their own grad rows."""
 
-    C = ext()
+    owner_stage_grad(store, plan, ids, grad_out, rows)
     ex = _exchange(store, plan, ids, rows)
-    meta, chunks, max_vec = plan.device_meta(store, rows)
-    g = grad_out if grad_out.dtype == torch.bfloat16 else grad_out.to(torch.bfloat16)
-    ex.grad[:g.numel()].copy_(g.reshape(-1))
-    bundles, row_lists, counts, capb, capr = ex.ptrs()
     ex.symm.barrier()  # every requester's gradient staged
-    C.emb_owner_backward(meta, store.peer_ptrs("slab"), store.peer_ptrs("grad"), store.peer_ptrs("flags"), store.rank,
-                         ids, offsets, bundles, row_lists, counts, capb, capr, ex.symm.peer_ptrs("grad"),
-                         store.max_dim, error_word(ids.device))
+    owner_pull_grad(store, plan, ids, offsets, rows)
     ex.symm.barrier()  # bundles / staged gradients may be overwritten after this point
 
 

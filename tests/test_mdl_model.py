@@ -38,7 +38,8 @@ def test_batch_layout_covers_domain_inputs():
     model = build_model(cfg, device="cpu", base_seed=0)
     enc = model.encoder
     assert enc.batch_names[: len(enc.inputs)] == enc.inputs
-    assert set(enc.batch_names[len(enc.inputs):]) == {"scene_id", "prior_click", "prior_like", "prior_finish"}
+    assert set(enc.batch_names[len(enc.inputs):]) == ({"scene_id", "prior_click", "prior_like", "prior_finish"}
+                                                      | {f"prior_scene{i}" for i in range(5)})
     assert model.Ns == 21 and model.Nt == 3
     # the scene id feature carries scenario_id + 1
     batch = SyntheticGenerator(enc.batch_plan, spec).batch(32)
