@@ -5,7 +5,8 @@
 
 Phases, each timed over 5 repetitions between barriers: the full step, forward +
 backward, the dense update, the sparse update, and the embedding lookup forward
-alone. Rank 0 prints one JSON line.
+alone; then the device time of each phase inside full steps (events between the
+forward, backward, dense update and sparse update). Rank 0 prints one JSON line.
 """
 
 from __future__ import annotations
@@ -68,6 +69,16 @@ def main(argv=None) -> int:
         res[name] = round(float(v), 4)
 
     timed("step_ms", lambda i: tr.train_step(batches[i % 3]))
+    # the same steps with events between their phases (device time inside the step)
+    tr.enable_phase_events(True)
+    for i in range(5):
+        tr.train_step(batches[i % 3])
+    for name, ms in tr.phase_ms().items():
+        v = torch.tensor([ms], device=dev)
+        if world > 1:
+            dist.all_reduce(v, op=dist.ReduceOp.MAX)
+        res[f"in_step_{name}_ms"] = round(float(v), 4)
+    tr.enable_phase_events(False)
     timed("forward_backward_ms", lambda i: tr.forward_backward(batches[i % 3]))
     timed("dense_update_ms", lambda i: tr.dense.step(lr=0.0))
     timed("sparse_update_ms", lambda i: tr.store.step(lr=0.0))

@@ -594,9 +594,15 @@ void dense_sync(const std::vector<int64_t>& grads, const std::vector<int64_t>& p
                 int64_t begin, int64_t end, int64_t fp32_from, int64_t rank, int64_t optimizer, double lr,
                 double beta1, double beta2, double eps, double wd, double bc1, double bc2, double alpha,
                 double grad_scale, const std::optional<at::Tensor>& clip, const std::optional<at::Tensor>& sqnorm_out,
-                int64_t phase, int64_t max_blocks) {
+                int64_t phase, int64_t max_blocks, const std::vector<int64_t>& multicast) {
   c10::cuda::CUDAGuard guard(state1.device());
   mdl::DenseSyncArgs a;
+  TORCH_CHECK(multicast.empty() || multicast.size() == 3, "multicast: [] or [grad, master, shadow] addresses");
+  if (!multicast.empty()) {
+    a.mc_grad = reinterpret_cast<float*>(multicast[0]);
+    a.mc_master = reinterpret_cast<float*>(multicast[1]);
+    a.mc_shadow = reinterpret_cast<void*>(multicast[2]);
+  }
   a.world = static_cast<int>(grads.size());
   TORCH_CHECK(a.world >= 1 && a.world <= mdl::kMaxWorld, "world out of range");
   for (int r = 0; r < a.world; ++r) {

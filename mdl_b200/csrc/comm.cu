@@ -8,7 +8,10 @@
 // dense_sync_update replaces the reference's DDP reducer + RMSprop step
 // (src/train.py:5311-5324, :4826-4893): a reduce-scatter of the fp32 gradient
 // (peer loads), the optimizer on the owned slice, and an all-gather of the
-// updated bf16 weights (peer stores), fused in one kernel per bucket.
+// updated bf16 weights (peer stores), fused in one kernel per bucket. On
+// NVSwitch systems with multicast the same kernel shape runs on multimem
+// instructions: the switch sums the gradient slice (ld_reduce) and replicates
+// the updated weights (st), so each element crosses NVLink once.
 #include "comm.h"
 #include "common.cuh"
 
@@ -147,6 +150,98 @@ __global__ void __launch_bounds__(256) dense_sync_kernel(const DenseSyncArgs a, 
   }
 }
 
+// ---- NVLS variant: the switch reduces, the switch replicates ----------------
+// Per owned element: NVLink ingress of 4 bytes (one reduced fp32 value instead of
+// W-1 peer loads) and egress of 2 bytes (one multicast bf16 store instead of W-1
+// peer stores); fp32-broadcast elements add a 4-byte multicast store.
+__device__ __forceinline__ float4 mc_ld_reduce_f32x4(const float* mc) {
+  float4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(mc)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void mc_st_f32x4(float* mc, float4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "f"(v.x), "f"(v.y),
+               "f"(v.z), "f"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void mc_st_b32x2(void* mc, uint32_t a, uint32_t b) {
+  asm volatile("multimem.st.relaxed.sys.global.v2.f32 [%0], {%1, %2};" ::"l"(mc), "f"(__uint_as_float(a)),
+               "f"(__uint_as_float(b))
+               : "memory");
+}
+
+// Multicast loads and stores travel through the switch and have long latency: each
+// thread keeps kNvlsUnroll reductions in flight before it updates any of them.
+constexpr int kNvlsUnroll = 4;
+
+__global__ void __launch_bounds__(256) dense_sync_nvls_kernel(const DenseSyncArgs a) {
+  const long long total = a.end - a.begin;
+  const long long chunk = ((total / a.world) + 3) / 4 * 4;
+  const long long lo = a.begin + chunk * a.rank;
+  const long long hi = min(a.end, lo + chunk);
+  const float scale = a.grad_scale * (a.clip != nullptr && a.phase != 1 ? *a.clip : 1.f);
+  float* grads = a.grads[a.rank];
+  float* params = a.params[a.rank];
+  float sq = 0.f;
+  const long long nvec = (hi > lo) ? (hi - lo) / 4 : 0;
+  const long long step = static_cast<long long>(gridDim.x) * blockDim.x * kNvlsUnroll;
+  for (long long base = static_cast<long long>(blockIdx.x) * blockDim.x * kNvlsUnroll + threadIdx.x; base < nvec;
+       base += step) {
+    float4 g[kNvlsUnroll];
+#pragma unroll
+    for (int u = 0; u < kNvlsUnroll; ++u) {
+      const long long v = base + static_cast<long long>(u) * blockDim.x;
+      if (v < nvec) {
+        const long long i = lo + v * 4;
+        g[u] = a.phase == 2 ? *reinterpret_cast<const float4*>(grads + i) : mc_ld_reduce_f32x4(a.mc_grad + i);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kNvlsUnroll; ++u) {
+      const long long v = base + static_cast<long long>(u) * blockDim.x;
+      if (v >= nvec) continue;
+      const long long i = lo + v * 4;
+      if (a.phase == 1) {
+        *reinterpret_cast<float4*>(grads + i) = g[u];
+        const float s = a.grad_scale;
+        sq += (g[u].x * g[u].x + g[u].y * g[u].y + g[u].z * g[u].z + g[u].w * g[u].w) * s * s;
+        continue;
+      }
+      const float gv[4] = {g[u].x * scale, g[u].y * scale, g[u].z * scale, g[u].w * scale};
+      float4 p = *reinterpret_cast<const float4*>(params + i);
+      float pv[4] = {p.x, p.y, p.z, p.w};
+      float4 s1 = *reinterpret_cast<const float4*>(a.state1 + i);
+      float s1v[4] = {s1.x, s1.y, s1.z, s1.w};
+      float s2v[4] = {0.f, 0.f, 0.f, 0.f};
+      if (a.optimizer == 0) {
+        const float4 s2 = *reinterpret_cast<const float4*>(a.state2 + i);
+        s2v[0] = s2.x; s2v[1] = s2.y; s2v[2] = s2.z; s2v[3] = s2.w;
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) opt_update(a, pv[k], gv[k], s1v[k], s2v[k]);
+      p = make_float4(pv[0], pv[1], pv[2], pv[3]);
+      *reinterpret_cast<float4*>(a.state1 + i) = make_float4(s1v[0], s1v[1], s1v[2], s1v[3]);
+      if (a.optimizer == 0) *reinterpret_cast<float4*>(a.state2 + i) = make_float4(s2v[0], s2v[1], s2v[2], s2v[3]);
+      if (i >= a.fp32_from) {
+        mc_st_f32x4(a.mc_master + i, p);  // every rank's master (this rank's included)
+      } else {
+        *reinterpret_cast<float4*>(params + i) = p;
+      }
+      __nv_bfloat162 h0 = __floats2bfloat162_rn(pv[0], pv[1]);
+      __nv_bfloat162 h1 = __floats2bfloat162_rn(pv[2], pv[3]);
+      mc_st_b32x2(reinterpret_cast<__nv_bfloat16*>(a.mc_shadow) + i, *reinterpret_cast<uint32_t*>(&h0),
+                  *reinterpret_cast<uint32_t*>(&h1));
+    }
+  }
+  if (a.phase == 1 && a.sqnorm_out != nullptr) {
+    sq = warp_sum(sq);
+    if ((threadIdx.x & 31) == 0) atomicAdd(a.sqnorm_out, sq);
+  }
+}
+
 struct SmallPtrs {
   float* p[kMaxWorld];
 };
@@ -190,7 +285,13 @@ cudaError_t dense_sync_update(const DenseSyncArgs& a, cudaStream_t stream) {
   if (blocks > sms * 4) blocks = sms * 4;
   if (a.max_blocks > 0 && blocks > a.max_blocks) blocks = a.max_blocks;
   if (blocks < 1) blocks = 1;
-  dense_sync_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(a, p);
+  if (a.mc_grad != nullptr) {
+    if (a.mc_shadow == nullptr || a.mc_master == nullptr || a.params[a.rank] == nullptr || a.grads[a.rank] == nullptr)
+      return cudaErrorInvalidValue;
+    dense_sync_nvls_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(a);
+  } else {
+    dense_sync_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(a, p);
+  }
   return cudaGetLastError();
 }
 

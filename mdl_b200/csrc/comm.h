@@ -50,6 +50,14 @@ struct DenseSyncArgs {
   float* sqnorm_out = nullptr;     // phase "norm": sum of squares of the reduced slice
   int phase = 0;                   // 0: fused update, 1: only reduce -> local grad slice + sqnorm
   int max_blocks = 0;              // grid cap (0: fill the GPU) when running beside other kernels
+  // NVLS (NVSwitch multicast) variant: multicast addresses of the grad / master /
+  // shadow buffers. When mc_grad is set, the owned slice's gradient is summed in the
+  // switch (multimem.ld_reduce) and the updated weights are written to every rank
+  // with one multicast store (multimem.st); grads/params/shadows then only need this
+  // rank's own entries.
+  float* mc_grad = nullptr;
+  float* mc_master = nullptr;
+  void* mc_shadow = nullptr;
 };
 cudaError_t dense_sync_update(const DenseSyncArgs& a, cudaStream_t stream);
 

@@ -225,10 +225,25 @@ class BatchPool:
 
 
 def synthetic_spec_from_config(config, batch_plan, *, zipf_s: float | None = 1.05, seed: int = 0,
-                               task_rate: float = 0.1) -> SyntheticSpec:
+                               task_rate: float = 0.1, sequences: list | None = None) -> SyntheticSpec:
     """A ``SyntheticSpec`` for any config: every categorical input of the batch layout draws
     ids over its table (``max_id`` / ``num_buckets``; ``vocab`` features over a
-    1000-entry vocabulary), bags draw lengths in [1, max_length or 8]."""
+    1000-entry vocabulary), bags draw lengths in [1, max_length or 8]. ``sequences``
+    (sequence configs, e.g. the model encoder's) get event sequences of lengths in
+    [1, max_length] with their categorical fields and dense fields."""
+
+    def vocab_of(enc) -> int:
+        if enc is not None and enc.max_id:
+            return int(enc.max_id)
+        if enc is not None and enc.num_buckets:
+            return int(enc.num_buckets)
+        return 1000
+
+    seq_specs = {}
+    for seq in sequences or []:
+        cats = {fl.name: FieldSpec(vocab=vocab_of(fl.encoding)) for fl in seq.fields if fl.kind == "categorical"}
+        dense = sum(int(fl.dimension) for fl in seq.fields if fl.kind == "dense")
+        seq_specs[seq.name] = SequenceSpec(fields=cats, max_len=int(seq.max_length), min_len=1, dense_width=dense)
 
     by_name = {f.name: f for f in config.features}
     fields = {}
@@ -246,4 +261,4 @@ def synthetic_spec_from_config(config, batch_plan, *, zipf_s: float | None = 1.0
         fields[f.name] = FieldSpec(vocab=vocab, multi_hot=multi, min_len=1, max_len=(f.max_length or 8) if multi else 1)
     return SyntheticSpec(fields=fields, dense_width=batch_plan.dense_width,
                          task_rates=[task_rate] * len(config.task_names), zipf_s=zipf_s,
-                         num_scenarios=len(config.scenarios.names), seed=seed)
+                         num_scenarios=len(config.scenarios.names), seed=seed, sequences=seq_specs or None)

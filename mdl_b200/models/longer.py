@@ -250,29 +250,48 @@ class _MLP(nn.Module):
 
 
 class LongerEncoder(nn.Module):
-    """Sequence tokens + global tokens -> cross block -> self blocks -> ``[B, R + G, d]``."""
+    """Sequence tokens + global tokens -> cross block -> self blocks -> ``[B, R + G, d]``.
 
-    def __init__(self, config: AppConfig, seq, encoder: FeatureEncoder, target_plan, user_plan, device=None) -> None:
+    Global tokens, in order: user globals (``longer_user_global_inputs``), ``extra_globals``
+    learned tokens passed to ``forward`` (the CLS tokens of a feature-encoder LONGER),
+    candidate globals (``target_inputs``). With ``time_delta = (c0, c1)`` (the event
+    columns of ``time_delta_field``) a learned position embedding is added to the other
+    event columns before the step projector (reference ``_longer_sequence_projector_inputs``
+    ``src/model.py:3393-3436``). The tcgen05 attention kernels take head_dim 32; other
+    head widths run the PyTorch definition (``runtime.kernel_backend: torch``)."""
+
+    def __init__(self, config: AppConfig, seq, encoder: FeatureEncoder, target_plan, user_plan, device=None,
+                 extra_globals: int = 0, time_delta: tuple[int, int] | None = None) -> None:
         super().__init__()
         m = config.model
         D = int(seq.longer_dim)
-        if D % 32:
-            raise NotImplementedError("LONGER attention kernels use head_dim 32: longer_dim must be a multiple of 32")
         if int(seq.longer_token_merge) != 1 or int(seq.longer_inner_layers) != 0:
             raise NotImplementedError("LONGER token merge size 1 without inner layers is implemented")
         self.D = D
-        self.heads = int(seq.longer_num_heads or max(1, D // 32))
-        if D // self.heads != 32:
-            raise NotImplementedError("LONGER attention kernels use head_dim 32")
+        heads = seq.longer_num_heads  # reference SequenceConfig.resolved_longer_num_heads
+        if heads is None:
+            heads = int(m.num_heads) if D % int(m.num_heads) == 0 else next(h for h in (8, 4, 2, 1) if D % h == 0)
+        self.heads = int(heads)
+        if D % self.heads:
+            raise ValueError(f"LONGER sequence {seq.name!r}: longer_dim {D} not divisible by {self.heads} heads")
+        self.head_dim = D // self.heads
         hidden = int(seq.longer_hidden_dim or 4 * D)
         self.R = int(seq.longer_query_tokens)
         self.L = int(seq.max_length)
         plan = encoder.seq_plans[seq.name]
         self.step = _MLP(plan.out_ld, plan.out_width, hidden, D, device=device)
         self.Gu = int(seq.longer_user_global_tokens) if user_plan is not None else 0
+        self.Gx = int(extra_globals)
         cand = seq.longer_candidate_global_tokens
-        self.Gc = (int(cand) if cand is not None else 1) if target_plan is not None else 0
-        self.G = self.Gu + self.Gc
+        if target_plan is None:
+            self.Gc = 0
+        elif cand is not None:
+            self.Gc = int(cand)
+        elif extra_globals or self.Gu:
+            self.Gc = max(0, int(seq.rankmixer_summary_tokens) - self.Gu - self.Gx)
+        else:
+            self.Gc = 1
+        self.G = self.Gu + self.Gx + self.Gc
         self.cand_mlp = (_MLP(target_plan.out_ld, target_plan.out_width, hidden, self.Gc * D, device=device)
                          if self.Gc else None)
         self.user_mlp = (_MLP(user_plan.out_ld, user_plan.out_width, hidden, self.Gu * D, device=device)
@@ -280,13 +299,35 @@ class LongerEncoder(nn.Module):
         self.cross = LongerBlock(D, hidden, device=device)
         self.selfs = nn.ModuleList(LongerBlock(D, hidden, device=device) for _ in range(int(seq.longer_self_layers)))
         self.output_tokens = self.R + self.G
+        self.pos = None
+        self.pos_cols = 0
+        if time_delta is not None:
+            c0, c1 = time_delta
+            if c1 != plan.out_width:
+                raise NotImplementedError("LONGER positions expect the time delta as the last event columns")
+            self.pos_cols = c0
+            self.pos = nn.Parameter(torch.randn(self.L, c0, device=device) * float(m.init_std))
+            self._pad_cols = plan.out_ld - c0
 
-    def forward(self, seq_in, lengths, target_in, user_in, native: bool) -> torch.Tensor:
+    def forward(self, seq_in, lengths, target_in, user_in, native: bool, cls_tokens=None) -> torch.Tensor:
         B, L, D, R, G = lengths.shape[0], self.L, self.D, self.R, self.G
+        if native and self.head_dim != 32:
+            raise NotImplementedError(f"LONGER head_dim {self.head_dim}: the tcgen05 attention kernels take head_dim "
+                                      "32 (set runtime.kernel_backend: torch for this model)")
+        if self.pos is not None:
+            from .sequence_encoders import positions
+
+            pe = self.pos[positions(lengths, L)].view(B * L, self.pos_cols)
+            pe = F.pad(pe, (0, self._pad_cols)) if self._pad_cols else pe
+            seq_in = seq_in + pe.to(seq_in.dtype)
         tokens = self.step(seq_in, native).view(B, L, D)
         parts = [tokens]
         if self.Gu:
             parts.append(self.user_mlp(user_in, native).view(B, self.Gu, D))
+        if self.Gx:
+            if cls_tokens is None:
+                raise ValueError("LONGER encoder built with extra global tokens needs cls_tokens")
+            parts.append(cls_tokens.to(tokens.dtype).expand(B, -1, -1))
         if self.Gc:
             parts.append(self.cand_mlp(target_in, native).view(B, self.Gc, D))
         X = torch.cat(parts, dim=1) if len(parts) > 1 else tokens

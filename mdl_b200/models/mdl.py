@@ -266,9 +266,12 @@ class MDLDomainMixin:
             return domain + attention(domain, feature).to(domain.dtype)
         return rankmixer(domain, feature)
 
-    def _domain_prompts(self, batch, B: int, anchor: torch.Tensor, cuda: bool, dt: torch.dtype):
+    def _domain_prompts(self, batch, B: int, anchor: torch.Tensor, cuda: bool, dt: torch.dtype,
+                        summaries: dict | None = None):
         """Scenario / task prompts ``[B, Ns, D]`` / ``[B, Nt, D]`` from the domain-token
-        lookup (``None`` for a disabled set)."""
+        lookup (``None`` for a disabled set). Sequence summaries among the domain inputs
+        (prior sequences) are added into their columns; they are computed here unless
+        the caller passes them."""
 
         from ..ops.embedding import fused_lookup
 
@@ -276,6 +279,13 @@ class MDLDomainMixin:
         s_prompt = t_prompt = None
         if self.Ns + self.Nt:
             d0 = fused_lookup(self.store, enc.domain_plan, batch.ids, batch.offsets, batch.dense, B, anchor)
+            cols = enc.summary_cols["domain"]
+            if cols:
+                from .sequence_encoders import add_summaries
+
+                if summaries is None:
+                    summaries = self.summaries(enc, batch, anchor, cuda)
+                d0 = add_summaries(d0, summaries, cols)
             off = getattr(self, "_dom_offset", 0)
             dom = d0.view(B, -1, self.Kd)[:, off:off + self.Ns + self.Nt]
             if not cuda:
@@ -375,17 +385,30 @@ class MDLRankMixerModel(MDLDomainMixin, nn.Module):
             raise ValueError("mdl_rankmixer requires token_dim divisible by the feature token count")
         self.moe = mc.rankmixer_ffn_type == "sparse_moe"
         dom_inputs = self._domain_specs(config)
+        groupwise = config.tokenization.feature_tokenizer == "groupwise"
+        token_groups = [list(g.inputs) for g in res.feature_token_groups] if groupwise else None
+        if groupwise and len(token_groups) != T:
+            raise ValueError(f"groupwise tokenizer: {len(token_groups)} groups for {T} tokens")
         self.encoder = FeatureEncoder(config, device=dev, rank=rank, world=world, process_group=process_group,
-                                      vocab_sizes=vocab_sizes, slice_tokens=T, base_seed=base_seed,
-                                      domain_tokens=dom_inputs or None)
-        self.K = self.encoder.slice_k
-        self.Kpad = self.encoder.slice_stride
-        # feature tokenizer: T per-token linear maps of the concatenated inputs
+                                      vocab_sizes=vocab_sizes, slice_tokens=0 if groupwise else T, base_seed=base_seed,
+                                      domain_tokens=dom_inputs or None, token_groups=token_groups)
+        from .sequence_encoders import SequenceSummaries
+
+        # sequences summarised into feature-token or domain-token inputs
+        self.summaries = SequenceSummaries(config, self.encoder, self.encoder.summary_names, device=dev)
+        if groupwise:
+            self.K = self.Kpad = self.encoder.group_k_pad
+            fan_in = self.encoder.group_widths
+        else:
+            self.K = self.encoder.slice_k
+            self.Kpad = self.encoder.slice_stride
+            fan_in = [self.K] * T
+        # feature tokenizer: T per-token linear maps of the concatenated (or grouped) inputs
         self.tok_weight = gemm_param(torch.zeros(T, D, self.Kpad, device=dev))
         self.tok_bias = nn.Parameter(torch.empty(T, D, device=dev))
         for t in range(T):
-            _kaiming_uniform_(self.tok_weight.data[t, :, :self.K], self.K)
-            _kaiming_uniform_(self.tok_bias.data[t], self.K)
+            _kaiming_uniform_(self.tok_weight.data[t, :, :fan_in[t]], fan_in[t])
+            _kaiming_uniform_(self.tok_bias.data[t], fan_in[t])
         self._init_domain_inputs(config, dev, D, H)
         self.blocks = nn.ModuleList(self._make_block(dev) for _ in range(self.L))
         self._init_domain_outputs(config, dev, D, H)
@@ -490,10 +513,15 @@ class MDLRankMixerModel(MDLDomainMixin, nn.Module):
         cuda = self._cuda(batch)
         anchor = torch.zeros(0, device=batch.ids.device, requires_grad=True)
         x0 = fused_lookup(self.store, self.encoder.plan, batch.ids, batch.offsets, batch.dense, B, anchor)
+        summaries = self.summaries(self.encoder, batch, anchor, cuda) if self.summaries.names else {}
+        if summaries and self.encoder.summary_cols["plan"]:
+            from .sequence_encoders import add_summaries
+
+            x0 = add_summaries(x0, summaries, self.encoder.summary_cols["plan"])
         x = self._tokenize(x0, B, cuda)
         dt = x.dtype
         mask = scenario_mask_from_ids(batch.scenario_id, self.S).to(x.device)
-        s_prompt, t_prompt = self._domain_prompts(batch, B, anchor, cuda, dt)
+        s_prompt, t_prompt = self._domain_prompts(batch, B, anchor, cuda, dt, summaries)
         s, t = self._initial_states(s_prompt, t_prompt, B, dt)
         if self.scene_feature_bias is not None:
             x = self._apply_scene_bias(x, s_prompt, mask)

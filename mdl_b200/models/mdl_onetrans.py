@@ -35,7 +35,7 @@ from torch import nn
 
 from ..config.schema import AppConfig
 from .mdl import MDLDomainMixin, scenario_mask_from_ids
-from .onetrans import OneTransLayerFn, OneTransModel, OneTransTokenizeFn
+from .onetrans import OneTransAssembleFn, OneTransLayerFn, OneTransModel, OneTransTokenizeFn
 
 
 class MDLOneTransModel(MDLDomainMixin, OneTransModel):
@@ -86,7 +86,13 @@ class MDLOneTransModel(MDLDomainMixin, OneTransModel):
             seq_in = grad_ready(seq_in, hooks, nl + 1)
             if self.ns_mode != "auto_split":
                 ns_in = self.ns_tokens(ns_in).to(torch.bfloat16)
-            X = OneTransTokenizeFn.apply(seq_in, ns_in, kstart, self, L)
+            if self.head_dim != 32:
+                raise NotImplementedError(f"OneTrans head_dim {self.head_dim}: the tcgen05 attention kernels take "
+                                          "head_dim 32 (set runtime.kernel_backend: torch for this model)")
+            if self.multi:
+                X = OneTransAssembleFn.apply(seq_in.to(torch.bfloat16), ns_in, kstart, self, L)
+            else:
+                X = OneTransTokenizeFn.apply(seq_in, ns_in, kstart, self, L)
             ks = kstart
         else:
             X = self.tokenize_reference(seq_in, ns_in, kstart, B)

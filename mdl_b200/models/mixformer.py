@@ -222,21 +222,45 @@ class MixFormerModel(nn.Module):
         from .longer import _MLP
 
         m = config.model
-        raw = [s for s in config.sequences if s.encoder == "raw"]
-        if len(raw) != 1 or not raw[0].max_length:
-            raise NotImplementedError("MixFormer: one raw sequence with max_length is implemented")
+        seq_by_name = {s.name: s for s in config.sequences}
+        groups = config.resolved.tokenization.sequence_token_groups
+        if groups:
+            raw = []
+            for g in groups:
+                if len(g.inputs) != 1 or g.inputs[0] not in seq_by_name:
+                    raise NotImplementedError(f"MixFormer sequence token group {g.name!r}: a group holds one raw "
+                                              "sequence")
+                raw.append(seq_by_name[g.inputs[0]])
+        else:
+            raw = [s for s in config.sequences if s.encoder == "raw"]
+        if not raw or any(not s.max_length for s in raw):
+            raise ValueError("MixFormer needs at least one raw sequence with max_length")
         self.config = config
         self.seq = raw[0]
+        self.group_seqs = raw
+        self.multi = len(raw) > 1
         by_name = {f.name: f for f in config.features}
         ns_inputs = [n for n in config.resolved.tokenization.feature_token_inputs if n in by_name]
         self.encoder = FeatureEncoder(config, device=device, rank=rank, world=world, process_group=process_group,
                                       vocab_sizes=vocab_sizes, input_names=ns_inputs, slice_tokens=1,
-                                      base_seed=base_seed, sequences=[self.seq], domain_tokens=domain_tokens)
+                                      base_seed=base_seed, sequences=raw, domain_tokens=domain_tokens)
+        from .sequence_encoders import SequenceSummaries
+
+        # prior sequences of the MDL domain tokens (mean_pool / attention_pool / longer / stca)
+        self.summaries = SequenceSummaries(config, self.encoder, self.encoder.summary_names, device=device)
         N = int(m.num_ns_tokens or config.resolved.tokenization.feature_token_count)
         Dh = int(m.token_dim)
         self.N, self.D, self.L = N, Dh, int(self.seq.max_length)
-        plan = self.encoder.seq_plans[self.seq.name]
-        self.step = _MLP(plan.out_ld, plan.out_width, int(m.hidden_dim), N * Dh, device=device)
+        if self.multi:
+            # several behaviour sequences: one bias-free alignment to N * D per group, then
+            # SEP tokens (intent_ordered) or type embeddings + time order (timestamp_aware)
+            from .sequence_fusion import SequenceGroups
+
+            self.seq_groups = SequenceGroups(config, self.encoder, raw, N * Dh, projection="linear", device=device)
+            self.L = self.seq_groups.S
+        else:
+            plan = self.encoder.seq_plans[self.seq.name]
+            self.step = _MLP(plan.out_ld, plan.out_width, int(m.hidden_dim), N * Dh, device=device)
         self.mixer = MixFormerHead(self.encoder.plan.out_ld, self.encoder.plan.out_width, N * Dh, N, Dh,
                                    int(m.hidden_dim), int(m.hidden_dim), max(1, int(m.num_layers)), device=device,
                                    user_heads=m.mixformer_user_head_count)
@@ -271,9 +295,14 @@ class MixFormerModel(nn.Module):
         from .features import lookup_sequence
 
         B, L = batch.rows, self.L
-        seq_in, lengths = lookup_sequence(self.encoder, batch, self.seq.name, B, L, anchor)
         feat_in = fused_lookup(self.store, self.encoder.plan, batch.ids, batch.offsets, batch.dense, B, anchor)
-        tokens = self.step(seq_in, native).view(B, L, self.N * self.D)
+        if self.multi:
+            tokens, lengths = self.seq_groups(self.encoder, batch, anchor, native)
+            if native:
+                tokens = tokens.to(torch.bfloat16)
+        else:
+            seq_in, lengths = lookup_sequence(self.encoder, batch, self.seq.name, B, L, anchor)
+            tokens = self.step(seq_in, native).view(B, L, self.N * self.D)
         e = torch.arange(L, device=tokens.device)
         valid = e.view(1, -1) >= (L - lengths.clamp(0, L)).view(-1, 1)
         return feat_in, tokens, valid

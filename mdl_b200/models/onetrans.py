@@ -250,16 +250,7 @@ class OneTransTokenizeFn(torch.autograd.Function):
         X0 = torch.empty(B, Lt, D, dtype=torch.bfloat16, device=dev)
         bgemm(u, _shadow(model.seq_w2), X0, M=L, N=D, K=Hd, G=B, lda=Hd, gsA=L * Hd, ldb=Hd, gsB=0, ldc=D,
               gsC=Lt * D, bias=model.seq_b2)
-        if model.ns_mode == "auto_split":
-            vg = torch.empty(B, Hd, dtype=torch.bfloat16, device=dev)
-            v = torch.empty_like(vg)
-            bgemm(ns_in, _shadow(model.ns_w1), vg, M=B, N=Hd, K=Kn, lda=ns_in.stride(0), ldb=Kn, ldc=Hd, out2=v,
-                  bias=model.ns_b1, act=ACT_GELU_GRAD)
-            bgemm(v, _shadow(model.ns_w2), _off(X0, L * D), M=B, N=N * D, K=Hd, lda=Hd, ldb=Hd, ldc=Lt * D,
-                  bias=model.ns_b2)
-        else:
-            X0[:, L:, :].copy_(ns_in.view(B, N, D))
-            vg = v = ns_in.new_empty(0)
+        vg, v = _ns_rows_forward(model, ns_in, X0, L)
         ks = kstart.to(torch.int32).contiguous()
         C.position_add(X0, model.pos, ks, B, Lt, D)
         ctx.save_for_backward(seq_in, ns_in, ks, ug, u, vg, v)
@@ -291,21 +282,79 @@ class OneTransTokenizeFn(torch.autograd.Function):
         dseq = torch.empty(B * L, Ks, dtype=torch.bfloat16, device=dev)
         bgemm(du, _shadow(model.seq_w1), dseq, M=B * L, N=Ks, K=Hd, lda=Hd, ldb=Ks, b_mn=True, ldc=Ks)
         del du
-        if model.ns_mode != "auto_split":
-            return dseq, dX0[:, L:, :].reshape(B, N * D), None, None, None
-        # NS: auto_split MLP
-        dns_tok = _off(dX0, L * D)
-        dv = torch.empty(B, Hd, dtype=torch.bfloat16, device=dev)
-        bgemm(dns_tok, _shadow(model.ns_w2), dv, M=B, N=Hd, K=N * D, lda=Lt * D, ldb=Hd, b_mn=True, ldc=Hd, aux=vg,
-              ld_aux=Hd, act=ACT_DMUL, colsum=_grad(model.ns_b1))
-        bgemm(dns_tok, v, _grad(model.ns_w2), M=N * D, N=Hd, K=B, lda=Lt * D, a_mn=True, ldb=Hd, b_mn=True, ldc=Hd,
-              accumulate=True)
-        C.colsum(dns_tok, _grad(model.ns_b2), 1, B, N * D, Lt * D, 0, 1.0)
-        bgemm(dv, ns_in, _grad(model.ns_w1), M=Hd, N=Kn, K=B, lda=Hd, a_mn=True, ldb=ns_in.stride(0), b_mn=True,
-              ldc=Kn, accumulate=True)
-        dns = torch.empty(B, Kn, dtype=torch.bfloat16, device=dev)
-        bgemm(dv, _shadow(model.ns_w1), dns, M=B, N=Kn, K=Hd, lda=Hd, ldb=Kn, b_mn=True, ldc=Kn)
-        return dseq, dns, None, None, None
+        return dseq, _ns_rows_backward(model, ns_in, dX0, L, vg, v), None, None, None
+
+
+def _ns_rows_forward(model, ns_in, X0, L):
+    """NS rows ``[L, L + N)`` of the token buffer: the ``auto_split`` MLP (GEMMs writing
+    the rows in place) or a copy of the finished ``[B, N * d]`` tokens."""
+
+    B = ns_in.shape[0]
+    D, N, Hd = model.token_dim, model.num_ns, model.hidden_dim
+    Kn, Lt, dev = ns_in.shape[1], L + N, ns_in.device
+    if model.ns_mode == "auto_split":
+        vg = torch.empty(B, Hd, dtype=torch.bfloat16, device=dev)
+        v = torch.empty_like(vg)
+        bgemm(ns_in, _shadow(model.ns_w1), vg, M=B, N=Hd, K=Kn, lda=ns_in.stride(0), ldb=Kn, ldc=Hd, out2=v,
+              bias=model.ns_b1, act=ACT_GELU_GRAD)
+        bgemm(v, _shadow(model.ns_w2), _off(X0, L * D), M=B, N=N * D, K=Hd, lda=Hd, ldb=Hd, ldc=Lt * D,
+              bias=model.ns_b2)
+        return vg, v
+    X0[:, L:, :].copy_(ns_in.view(B, N, D))
+    empty = ns_in.new_empty(0)
+    return empty, empty
+
+
+def _ns_rows_backward(model, ns_in, dX0, L, vg, v):
+    """Gradient of ``ns_in`` from the NS rows of ``dX0`` (weight gradients accumulated)."""
+
+    B = ns_in.shape[0]
+    D, N, Hd = model.token_dim, model.num_ns, model.hidden_dim
+    Kn, Lt, dev = ns_in.shape[1], L + N, ns_in.device
+    if model.ns_mode != "auto_split":
+        return dX0[:, L:, :].reshape(B, N * D)
+    C = ext()
+    dns_tok = _off(dX0, L * D)
+    dv = torch.empty(B, Hd, dtype=torch.bfloat16, device=dev)
+    bgemm(dns_tok, _shadow(model.ns_w2), dv, M=B, N=Hd, K=N * D, lda=Lt * D, ldb=Hd, b_mn=True, ldc=Hd, aux=vg,
+          ld_aux=Hd, act=ACT_DMUL, colsum=_grad(model.ns_b1))
+    bgemm(dns_tok, v, _grad(model.ns_w2), M=N * D, N=Hd, K=B, lda=Lt * D, a_mn=True, ldb=Hd, b_mn=True, ldc=Hd,
+          accumulate=True)
+    C.colsum(dns_tok, _grad(model.ns_b2), 1, B, N * D, Lt * D, 0, 1.0)
+    bgemm(dv, ns_in, _grad(model.ns_w1), M=Hd, N=Kn, K=B, lda=Hd, a_mn=True, ldb=ns_in.stride(0), b_mn=True,
+          ldc=Kn, accumulate=True)
+    dns = torch.empty(B, Kn, dtype=torch.bfloat16, device=dev)
+    bgemm(dv, _shadow(model.ns_w1), dns, M=B, N=Kn, K=Hd, lda=Hd, ldb=Kn, b_mn=True, ldc=Kn)
+    return dns
+
+
+class OneTransAssembleFn(torch.autograd.Function):
+    """Finished S tokens (several fused sequence groups) + NS tokens + positions ->
+    ``[B, S + N, d]`` (the multi-group counterpart of ``OneTransTokenizeFn``)."""
+
+    @staticmethod
+    def forward(ctx, s_tokens, ns_in, kstart, model, S):
+        B = ns_in.shape[0]
+        D, N = model.token_dim, model.num_ns
+        X0 = torch.empty(B, S + N, D, dtype=torch.bfloat16, device=ns_in.device)
+        X0[:, :S].copy_(s_tokens)
+        vg, v = _ns_rows_forward(model, ns_in, X0, S)
+        ks = kstart.to(torch.int32).contiguous()
+        ext().position_add(X0, model.pos, ks, B, S + N, D)
+        ctx.save_for_backward(ns_in, ks, vg, v)
+        ctx.meta = (model, S)
+        return X0
+
+    @staticmethod
+    def backward(ctx, dX0):
+        ns_in, ks, vg, v = ctx.saved_tensors
+        model, S = ctx.meta
+        B = ns_in.shape[0]
+        D, N = model.token_dim, model.num_ns
+        dX0 = dX0.to(torch.bfloat16).contiguous()
+        ext().position_grad(dX0, _grad(model.pos), ks, B, S + N, D)
+        dns = _ns_rows_backward(model, ns_in, dX0, S, vg, v)
+        return dX0[:, :S], dns, None, None, None
 
 
 # ----------------------------------------------------------------------------- modules
@@ -400,12 +449,20 @@ class OneTransModel(nn.Module):
             raise NotImplementedError(f"OneTrans ns_tokenizer {m.ns_tokenizer!r}")
         groups = config.resolved.tokenization.sequence_token_groups
         seq_by_name = {s.name: s for s in config.sequences}
-        if len(groups) != 1 or len(groups[0].inputs) != 1 or groups[0].inputs[0] not in seq_by_name:
-            raise NotImplementedError("OneTrans: one sequence token group over one raw sequence is implemented")
-        if m.token_dim % m.num_heads or m.token_dim // m.num_heads != 32:
-            raise NotImplementedError("OneTrans attention kernels use head_dim 32")
+        if not groups:
+            raise ValueError("OneTrans requires at least one sequence token group")
+        group_seqs = []
+        for g in groups:
+            if len(g.inputs) != 1 or g.inputs[0] not in seq_by_name:
+                raise NotImplementedError(f"OneTrans sequence token group {g.name!r}: a group holds one raw sequence")
+            group_seqs.append(seq_by_name[g.inputs[0]])
+        if m.token_dim % m.num_heads:
+            raise ValueError("token_dim must be divisible by num_heads")
+        self.head_dim = m.token_dim // m.num_heads
         self.config = config
-        self.seq = seq_by_name[groups[0].inputs[0]]
+        self.seq = group_seqs[0]
+        self.group_seqs = group_seqs
+        self.multi = len(group_seqs) > 1
         if not self.seq.max_length:
             raise ValueError(f"sequence {self.seq.name!r} needs max_length")
         self.L = int(self.seq.max_length)
@@ -421,7 +478,11 @@ class OneTransModel(nn.Module):
         self._dom_offset = len(ns_groups) if self.ns_mode == "groupwise" else 0
         self.encoder = FeatureEncoder(config, device=device, rank=rank, world=world, process_group=process_group,
                                       vocab_sizes=vocab_sizes, input_names=ns_inputs, slice_tokens=1,
-                                      base_seed=base_seed, sequences=[self.seq], domain_tokens=domain_tokens or None)
+                                      base_seed=base_seed, sequences=group_seqs, domain_tokens=domain_tokens or None)
+        from .sequence_encoders import SequenceSummaries
+
+        # prior sequences of the MDL domain tokens (mean_pool / attention_pool / longer / stca)
+        self.summaries = SequenceSummaries(config, self.encoder, self.encoder.summary_names, device=device)
         D, Hd = int(m.token_dim), int(m.hidden_dim)
         if self.ns_mode == "groupwise":
             N = len(ns_groups)
@@ -429,17 +490,25 @@ class OneTransModel(nn.Module):
             N = int(m.num_ns_tokens or max(1, len(ns_inputs)))
         self.token_dim, self.hidden_dim, self.num_ns, self.attn_heads = D, Hd, N, int(m.num_heads)
         self.eps = 1e-6
-        seq_plan = self.encoder.seq_plans[self.seq.name]
-        self.Ks, self.Ks_log = seq_plan.out_ld, seq_plan.out_width
         self.Kn, self.Kn_log = self.encoder.plan.out_ld, self.encoder.plan.out_width
-        self.seq_w1 = gemm_param(torch.zeros(Hd, self.Ks, device=device))
-        self.seq_b1 = nn.Parameter(torch.empty(Hd, device=device))
-        self.seq_w2 = gemm_param(torch.empty(D, Hd, device=device))
-        self.seq_b2 = nn.Parameter(torch.empty(D, device=device))
-        _kaiming_uniform_(self.seq_w1.data[:, :self.Ks_log], self.Ks_log)  # padded input columns stay zero
-        _kaiming_uniform_(self.seq_b1.data, self.Ks_log)
-        _kaiming_uniform_(self.seq_w2.data, Hd)
-        _kaiming_uniform_(self.seq_b2.data, Hd)
+        if self.multi:
+            # several groups: per-group projection MLPs, SEP tokens / time order, compaction
+            from .sequence_fusion import SequenceGroups
+
+            self.seq_groups = SequenceGroups(config, self.encoder, group_seqs, D, projection="mlp", hidden=Hd,
+                                             device=device)
+            self.L = self.seq_groups.S
+        else:
+            seq_plan = self.encoder.seq_plans[self.seq.name]
+            self.Ks, self.Ks_log = seq_plan.out_ld, seq_plan.out_width
+            self.seq_w1 = gemm_param(torch.zeros(Hd, self.Ks, device=device))
+            self.seq_b1 = nn.Parameter(torch.empty(Hd, device=device))
+            self.seq_w2 = gemm_param(torch.empty(D, Hd, device=device))
+            self.seq_b2 = nn.Parameter(torch.empty(D, device=device))
+            _kaiming_uniform_(self.seq_w1.data[:, :self.Ks_log], self.Ks_log)  # padded input columns stay zero
+            _kaiming_uniform_(self.seq_b1.data, self.Ks_log)
+            _kaiming_uniform_(self.seq_w2.data, Hd)
+            _kaiming_uniform_(self.seq_b2.data, Hd)
         if self.ns_mode == "auto_split":
             self.ns_w1 = gemm_param(torch.zeros(Hd, self.Kn, device=device))
             self.ns_b1 = nn.Parameter(torch.empty(Hd, device=device))
@@ -499,8 +568,13 @@ class OneTransModel(nn.Module):
         from .features import lookup_sequence
 
         B, L = batch.rows, self.L
-        seq_in, lengths = lookup_sequence(self.encoder, batch, self.seq.name, B, L, anchor)
-        kstart = (L - lengths.to(torch.int64).clamp(0, L)).to(torch.int32)
+        if self.multi:
+            native = batch.ids.is_cuda and self.config.runtime.kernel_backend == "native"
+            seq_in, valid = self.seq_groups(self.encoder, batch, anchor, native)  # finished S tokens
+            kstart = (L - valid.to(torch.int64)).to(torch.int32)
+        else:
+            seq_in, lengths = lookup_sequence(self.encoder, batch, self.seq.name, B, L, anchor)
+            kstart = (L - lengths.to(torch.int64).clamp(0, L)).to(torch.int32)
         if self.ns_mode == "groupwise":
             ns_in = fused_lookup(self.store, self.encoder.domain_plan, batch.ids, batch.offsets, batch.dense, B, anchor)
         else:
@@ -536,7 +610,13 @@ class OneTransModel(nn.Module):
         seq_in = grad_ready(seq_in, hooks, nl + 1)
         if self.ns_mode != "auto_split":
             ns_in = self.ns_tokens(ns_in).to(torch.bfloat16)
-        X = OneTransTokenizeFn.apply(seq_in, ns_in, kstart, self, self.L)
+        if self.head_dim != 32:
+            raise NotImplementedError(f"OneTrans head_dim {self.head_dim}: the tcgen05 attention kernels take head_dim "
+                                      "32 (set runtime.kernel_backend: torch for this model)")
+        if self.multi:
+            X = OneTransAssembleFn.apply(seq_in.to(torch.bfloat16), ns_in, kstart, self, self.L)
+        else:
+            X = OneTransTokenizeFn.apply(seq_in, ns_in, kstart, self, self.L)
         s_in, ks = self.L, kstart
         for i, layer in enumerate(self.layers):
             X = grad_ready(X, hooks, nl - i)
@@ -560,8 +640,11 @@ class OneTransModel(nn.Module):
         """fp32 PyTorch tokenizer: ``[B, L + N, d]`` with positions on the valid tokens."""
 
         L, D, N = self.L, self.token_dim, self.num_ns
-        s = F.gelu(seq_in.float()[:, :self.Ks_log] @ self.seq_w1[:, :self.Ks_log].t() + self.seq_b1)
-        s = (s @ self.seq_w2.t() + self.seq_b2).view(B, L, D)
+        if self.multi:
+            s = seq_in.float().view(B, L, D)
+        else:
+            s = F.gelu(seq_in.float()[:, :self.Ks_log] @ self.seq_w1[:, :self.Ks_log].t() + self.seq_b1)
+            s = (s @ self.seq_w2.t() + self.seq_b2).view(B, L, D)
         if self.ns_mode == "auto_split":
             v = F.gelu(ns_in.float()[:, :self.Kn_log] @ self.ns_w1[:, :self.Kn_log].t() + self.ns_b1)
             ns = (v @ self.ns_w2.t() + self.ns_b2).view(B, N, D)

@@ -64,45 +64,31 @@ class RankMixerModel(nn.Module):
         self.moe = mc.rankmixer_ffn_type == "sparse_moe"
         if self.D % self.T:
             raise ValueError("rankmixer requires token_dim divisible by the feature token count")
-        by_name = {f.name: f for f in config.features}
-        stca_seqs = [s for s in config.sequences if s.encoder == "stca" and s.name in res.feature_token_inputs]
-        stca_targets = [[n for n in s.target_inputs if n in by_name] for s in stca_seqs]
+        groupwise = config.tokenization.feature_tokenizer == "groupwise"
+        token_groups = [list(g.inputs) for g in res.feature_token_groups] if groupwise else None
+        if groupwise and len(token_groups) != self.T:
+            raise ValueError(f"groupwise tokenizer: {len(token_groups)} groups for {self.T} tokens")
         self.encoder = FeatureEncoder(config, device=device, rank=rank, world=world, process_group=process_group,
-                                      vocab_sizes=vocab_sizes, slice_tokens=self.T, base_seed=base_seed,
-                                      sequences=stca_seqs or None,
-                                      domain_tokens=[t for t in stca_targets if t] or None)
-        self.stca = nn.ModuleDict()
-        self._stca_meta = {}
-        if stca_seqs:
-            from .longer import _MLP
-            from .stca import STCAEncoder
+                                      vocab_sizes=vocab_sizes, slice_tokens=0 if groupwise else self.T,
+                                      base_seed=base_seed, token_groups=token_groups)
+        from .sequence_encoders import SequenceSummaries
 
-            plan = self.encoder.plan
-            kp = self.encoder.domain_k_pad
-            ti = 0
-            for seq, tgt, (name, c0, w) in zip(stca_seqs, stca_targets, self.encoder.extra_inputs):
-                if not tgt:
-                    raise ValueError(f"STCA sequence {seq.name!r} needs target_inputs")
-                d = int(seq.stca_dim)
-                sp = self.encoder.seq_plans[seq.name]
-                heads = int(seq.stca_num_heads or mc.num_heads)
-                mod = nn.Module()
-                mod.step = _MLP(sp.out_ld, sp.out_width, d * int(seq.stca_expansion_ratio), d, device=device)
-                mod.target = _MLP(kp, kp, d * int(seq.stca_expansion_ratio), d, device=device)
-                mod.encoder = STCAEncoder(d, heads, int(seq.stca_layers), int(seq.stca_expansion_ratio), device=device)
-                self.stca[seq.name] = mod
-                cols = torch.tensor([plan.phys_col(c) for c in range(c0, c0 + w)], dtype=torch.long)
-                self._stca_meta[seq.name] = (cols, ti, int(seq.max_length or 0))
-                ti += 1
-        self.K = self.encoder.slice_k
-        self.Kpad = self.encoder.slice_stride
+        # sequences summarised into feature-token inputs (mean_pool / attention_pool / longer / stca)
+        self.summaries = SequenceSummaries(config, self.encoder, self.encoder.summary_names, device=device)
+        if groupwise:
+            self.K = self.Kpad = self.encoder.group_k_pad
+            fan_in = self.encoder.group_widths
+        else:
+            self.K = self.encoder.slice_k
+            self.Kpad = self.encoder.slice_stride
+            fan_in = [self.K] * self.T
         T, D, H, K, Kp = self.T, self.D, self.H, self.K, self.Kpad
         dev = torch.device(device)
         self.tok_weight = nn.Parameter(torch.zeros(T, D, Kp, device=dev))
         self.tok_bias = nn.Parameter(torch.empty(T, D, device=dev))
-        for t in range(T):
-            _kaiming_uniform_(self.tok_weight.data[t, :, :K], K)
-            _kaiming_uniform_(self.tok_bias.data[t], K)
+        for t in range(T):  # each token's fan-in is its own input width; padded columns stay zero
+            _kaiming_uniform_(self.tok_weight.data[t, :, :fan_in[t]], fan_in[t])
+            _kaiming_uniform_(self.tok_bias.data[t], fan_in[t])
         self.blocks = nn.ModuleList()
         for _ in range(self.L):
             blk = nn.Module()
@@ -146,7 +132,7 @@ class RankMixerModel(nn.Module):
             if not self.moe:
                 names |= {f"blocks.{i}.w_in", f"blocks.{i}.w_out"}
         names |= {n for n, p in self.blocks.named_parameters(prefix="blocks") if getattr(p, "_mdl_gemm", False)}
-        names |= {n for n, p in self.stca.named_parameters(prefix="stca") if getattr(p, "_mdl_gemm", False)}
+        names |= {n for n, p in self.summaries.named_parameters(prefix="summaries") if getattr(p, "_mdl_gemm", False)}
         return names
 
     def dense_buckets(self) -> list[list[str]]:
@@ -155,7 +141,8 @@ class RankMixerModel(nn.Module):
         heads = ["head_w1", "head_b1", "head_w2", "head_b2"]
         blocks = [[n for n, _ in self.blocks[i].named_parameters(prefix=f"blocks.{i}")]
                   for i in reversed(range(self.L))]
-        return [heads, *blocks, ["tok_weight", "tok_bias", *[n for n, _ in self.stca.named_parameters(prefix="stca")]]]
+        return [heads, *blocks,
+                ["tok_weight", "tok_bias", *[n for n, _ in self.summaries.named_parameters(prefix="summaries")]]]
 
     @property
     def store(self):
@@ -169,9 +156,13 @@ class RankMixerModel(nn.Module):
         from ..ops.embedding import fused_lookup
 
         x0 = fused_lookup(self.store, self.encoder.plan, batch.ids, batch.offsets, batch.dense, batch.rows, anchor)
-        if len(self.stca):
-            x0 = self._add_stca(x0, batch, anchor)
-        if batch.ids.is_cuda and self.config.runtime.kernel_backend == "native":
+        native = batch.ids.is_cuda and self.config.runtime.kernel_backend == "native"
+        if self.summaries.names:
+            from .sequence_encoders import add_summaries
+
+            x0 = add_summaries(x0, self.summaries(self.encoder, batch, anchor, native),
+                               self.encoder.summary_cols["plan"])
+        if native:
             out = self._forward_cuda(x0, batch, task_scale)
         else:
             out = self.forward_reference(x0, batch, task_scale)
@@ -180,27 +171,6 @@ class RankMixerModel(nn.Module):
 
             add_moe_loss(out, self, float(self.config.model.sparse_moe_loss_weight))
         return out
-
-    def _add_stca(self, x0, batch, anchor):
-        """STCA summary tokens of the encoded sequences into their tokenizer columns."""
-
-        from ..ops.embedding import fused_lookup
-        from .features import lookup_sequence
-
-        native = batch.ids.is_cuda and self.config.runtime.kernel_backend == "native"
-        B = batch.rows
-        targets = fused_lookup(self.store, self.encoder.domain_plan, batch.ids, batch.offsets, batch.dense, B, anchor)
-        kp = self.encoder.domain_k_pad
-        for name, mod in self.stca.items():
-            cols, ti, L = self._stca_meta[name]
-            seq_in, lengths = lookup_sequence(self.encoder, batch, name, B, L, anchor)
-            hist = mod.step(seq_in, native).view(B, L, -1)
-            target = mod.target(targets[:, ti * kp:(ti + 1) * kp], native)
-            e = torch.arange(L, device=hist.device)
-            valid = e.view(1, -1) >= (L - lengths.clamp(0, L)).view(-1, 1)
-            z = mod.encoder(hist, valid, target, native)
-            x0 = x0.index_add(1, cols.to(x0.device), z.to(x0.dtype))
-        return x0
 
     def _forward_cuda(self, x0, batch, task_scale):
         from ..ops.fused import HeadsBCEFn, PerTokenLinearFn, RankMixerBlockFn

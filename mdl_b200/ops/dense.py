@@ -125,16 +125,34 @@ class DenseParams:
         self._launched: list[bool] = [False] * len(self.buckets)
         self._side = torch.cuda.Stream(device=self.device) if self.device.type == "cuda" else None
 
+    def _use_multicast(self) -> bool:
+        """NVSwitch multicast for the fused update, when every rank has it (collective)."""
+
+        if os.environ.get("MDL_B200_NVLS", "0") != "1":  # opt-in until it measures faster than peer loads
+            return False
+        from ..parallel.symm import MulticastBuffers
+
+        ok = torch.tensor([1 if MulticastBuffers.available(self.device.index if self.device.index is not None else torch.cuda.current_device()) else 0], dtype=torch.int32,
+                          device=self.device)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=self.group)
+        return bool(int(ok.item()))
+
     def _alloc(self) -> None:
         dev = self.device
         n = self.total
         self._symm = None
+        self._mc: list[int] = []  # multicast addresses of grad / master / shadow (NVLS path)
         if dev.type == "cuda" and self.world > 1 and self.comm == "fused":
             from ..parallel.symm import SymmetricBuffers
 
             spec = {"master": (n, torch.float32), "grad": (n, torch.float32), "shadow": (n, torch.bfloat16)}
             if self._peers is not None:
                 self._symm = self._peers.buffers("dense", self.rank, spec)
+            elif self._use_multicast():
+                from ..parallel.symm import MulticastBuffers
+
+                self._symm = MulticastBuffers(spec, device=dev, process_group=self.group)
+                self._mc = [self._symm.multicast_ptr(k) for k in ("grad", "master", "shadow")]
             else:
                 self._symm = SymmetricBuffers(spec, device=dev, process_group=self.group)
             self.master = self._symm.local("master")
@@ -211,7 +229,8 @@ class DenseParams:
             sym.barrier()  # every rank's gradients of this bucket are final
             C.dense_sync(sym.peer_ptrs("grad"), sym.peer_ptrs("master"), sym.peer_ptrs("shadow"), self.state1,
                          self.state2, begin, end, fp32_from, self.rank, h["opt"], h["lr"], h["b1"], h["b2"], self.eps,
-                         self.weight_decay, h["bc1"], h["bc2"], self.rmsprop_alpha, scale, None, None, 0, max_blocks)
+                         self.weight_decay, h["bc1"], h["bc2"], self.rmsprop_alpha, scale, None, None, 0, max_blocks,
+                         self._mc)
             return
         sl = slice(begin, end)
         shadow = None if self.shadow is None else self.shadow[sl]
@@ -271,7 +290,7 @@ class DenseParams:
                     C.dense_sync(sym.peer_ptrs("grad"), sym.peer_ptrs("master"), sym.peer_ptrs("shadow"), self.state1,
                                  self.state2, begin, end, fp32_from, self.rank, h["opt"], lr, h["b1"], h["b2"],
                                  self.eps, self.weight_decay, h["bc1"], h["bc2"], self.rmsprop_alpha, scale, None,
-                                 self._sq, 1, 0)
+                                 self._sq, 1, 0, self._mc)
                 sym.allreduce_small(self._sq)
                 C.clip_factor(self._sq, float(clip_norm), self._clip)
                 norm = self._sq.sqrt()
@@ -280,7 +299,7 @@ class DenseParams:
                 C.dense_sync(sym.peer_ptrs("grad"), sym.peer_ptrs("master"), sym.peer_ptrs("shadow"), self.state1,
                              self.state2, begin, end, fp32_from, self.rank, h["opt"], lr, h["b1"], h["b2"], self.eps,
                              self.weight_decay, h["bc1"], h["bc2"], self.rmsprop_alpha, scale, clip, None,
-                             2 if clip_norm is not None else 0, 0)
+                             2 if clip_norm is not None else 0, 0, self._mc)
             sym.barrier()
             self.grad.zero_()
             return norm

@@ -99,3 +99,89 @@ class SymmetricBuffers:
         for p in self._local_ptrs.values():
             C.ipc_free(p, self.dev_index)
         self._local_ptrs = {}
+
+
+class MulticastBuffers:
+    """Named buffers of identical size on every rank, in PyTorch symmetric memory,
+    with both per-rank pointers (peer loads / stores) and NVSwitch multicast
+    addresses (``multimem`` loads with in-switch reduction, multicast stores).
+
+    ``torch.distributed._symmetric_memory`` does the plumbing (physical allocation,
+    handle exchange, multicast object); the kernels that use the addresses are this
+    library's. Construction raises when the GPUs or the driver offer no multicast,
+    and callers fall back to ``SymmetricBuffers``.
+    """
+
+    def __init__(self, spec: dict[str, tuple[int, torch.dtype]], *, device: torch.device, process_group=None) -> None:
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.device = torch.device(device)
+        self.dev_index = self.device.index if self.device.index is not None else torch.cuda.current_device()
+        self.group = process_group if process_group is not None else dist.group.WORLD
+        self.rank = dist.get_rank(self.group)
+        self.world = dist.get_world_size(self.group)
+        if not self.available(self.dev_index):
+            raise RuntimeError("no NVSwitch multicast support on this device")
+        spec = dict(spec)
+        spec["__signals"] = (64, torch.int32)
+        spec["__scratch"] = (256, torch.float32)
+        self._tensors: dict[str, torch.Tensor] = {}
+        self._peer_ptrs: dict[str, list[int]] = {}
+        self._mc: dict[str, int] = {}
+        self._handles = []
+        for name, (numel, dtype) in spec.items():
+            n = max(int(numel), 256 // _DTYPE_SIZE[dtype])
+            t = symm_mem.empty(n, dtype=dtype, device=self.device)
+            h = symm_mem.rendezvous(t, self.group)
+            base = list(h.buffer_ptrs)
+            off = t.data_ptr() - base[self.rank]
+            if off < 0:
+                raise RuntimeError(f"symmetric buffer {name}: tensor below its block")
+            self._tensors[name] = t
+            self._peer_ptrs[name] = [b + off for b in base]
+            mc = int(h.multicast_ptr)
+            if mc == 0:
+                raise RuntimeError(f"symmetric buffer {name}: no multicast address")
+            self._mc[name] = mc + off
+            self._handles.append(h)
+        self._tensors["__signals"].zero_()
+        self.counter = torch.zeros(1, dtype=torch.int32, device=self.device)
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+
+    @staticmethod
+    def available(dev_index: int) -> bool:
+        try:
+            from torch._C._distributed_c10d import _SymmetricMemory
+
+            return bool(_SymmetricMemory.has_multicast_support(torch._C._autograd.DeviceType.CUDA, dev_index))
+        except Exception:  # noqa: BLE001 - old torch / no symmetric memory: no multicast
+            return False
+
+    def local(self, name: str) -> torch.Tensor:
+        return self._tensors[name]
+
+    def peer_ptrs(self, name: str) -> list[int]:
+        return self._peer_ptrs[name]
+
+    def multicast_ptr(self, name: str) -> int:
+        return self._mc[name]
+
+    def barrier(self) -> None:
+        ext().barrier(self._peer_ptrs["__signals"], self.counter, self.rank, error_word(self.device))
+
+    def barrier_host(self) -> None:
+        dist.barrier(group=self.group)
+
+    def allreduce_small(self, values: torch.Tensor) -> torch.Tensor:
+        n = values.numel()
+        self._tensors["__scratch"][:n].copy_(values.flatten())
+        self.barrier()
+        ext().small_allreduce(self._peer_ptrs["__scratch"], values, n)
+        self.barrier()
+        return values
+
+    def close(self) -> None:
+        torch.cuda.synchronize(self.device)
+        self._handles = []
+        self._tensors = {}

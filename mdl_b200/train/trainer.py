@@ -97,9 +97,40 @@ class Trainer:
         scale = torch.where(global_counts > 0, W / global_counts.clamp_min(1.0), torch.zeros_like(global_counts))
         return scale * self.task_weights
 
+    def enable_phase_events(self, on: bool = True) -> None:
+        """Record CUDA events between the phases of every step (forward, backward,
+        dense update, sparse update); ``phase_ms()`` then gives their device times."""
+
+        self._phase_marks: list | None = [] if on else None
+
+    def _mark(self, name: str) -> None:
+        marks = getattr(self, "_phase_marks", None)
+        if marks is not None and self.device.type == "cuda":
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            marks.append((name, ev))
+
+    def phase_ms(self) -> dict[str, float]:
+        """Mean device time of each phase over the recorded steps (synchronizes)."""
+
+        marks = getattr(self, "_phase_marks", None) or []
+        torch.cuda.synchronize(self.device)
+        sums: dict[str, float] = {}
+        counts: dict[str, int] = {}
+        for (_n0, e0), (n1, e1) in zip(marks, marks[1:]):
+            if n1 == "start":
+                continue
+            sums[n1] = sums.get(n1, 0.0) + e0.elapsed_time(e1)
+            counts[n1] = counts.get(n1, 0) + 1
+        self._phase_marks = []
+        return {k: sums[k] / counts[k] for k in sums}
+
     def forward_backward(self, batch) -> dict:
+        self._mark("start")
         out = self.model(batch, task_scale=self.task_scale(batch))
+        self._mark("forward")
         out["loss"].backward()
+        self._mark("backward")
         return out
 
     def _lrs(self, step: int) -> tuple[float, float]:
@@ -117,7 +148,9 @@ class Trainer:
 
             step_moe_controllers(self.moe, self.world, self.group)
         dn = self.dense.step(lr=lr_dense, clip_norm=t.dense_clip_norm)
+        self._mark("dense_update")
         sn = self.store.step(lr=lr_sparse, clip_norm=t.sparse_clip_norm)
+        self._mark("sparse_update")
         return dn, sn
 
     def train_step(self, batch) -> StepResult:

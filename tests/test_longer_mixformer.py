@@ -154,13 +154,13 @@ def test_stca_rankmixer_trains_on_cpu():
     cfg, spec = _stca_rankmixer()
     torch.manual_seed(0)
     model = build_model(cfg, device="cpu", base_seed=1)
-    assert "clicks" in model.stca
+    assert "clicks" in model.summaries.mods
     tr = Trainer(cfg, model, device=torch.device("cpu"))
     batch = SyntheticGenerator(model.encoder.batch_plan, spec).batch(64)
     losses = [float(tr.train_step(batch).loss) for _ in range(6)]
     assert losses[-1] < losses[0]
     tr.forward_backward(batch)
-    name = "stca.clicks.encoder.layers.1.wk"
+    name = "summaries.mods.clicks.encoder.layers.1.wk"
     o, n = tr.dense.offsets[name], tr.dense.params[name].numel()
     assert float(tr.dense.grad[o:o + n].abs().sum()) > 0  # the summary reaches the loss
 
