@@ -305,3 +305,85 @@ def _max(v: float, world: int) -> float:
     t = torch.tensor([v], dtype=torch.float64, device="cuda")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def auc_parity_worker(rank: int, world: int, init_file: str, out_path: str, steps: int = 200,
+                      batch: int = 256) -> None:
+    """One gloo rank of the AUC parity run (BASELINE workload 1 on CPU).
+
+    Every rank builds this framework's workload-1 model at ``world`` ranks and the
+    reference's, both from identical starting weights (the dense weights and full
+    embedding tables of a one-rank model built from the same seeds, each rank keeping
+    the rows it owns), trains both for ``steps`` steps on its slice of the same union
+    batches, scores its slice of the held-out batches, and rank 0 writes both AUCs
+    and the losses to ``out_path`` (JSON)."""
+
+    import json
+
+    from mdl_b200.config import app_config_from_mapping
+    from mdl_b200.data.baseline_configs import baseline_config
+    from mdl_b200.data.synthetic import SyntheticGenerator
+    from mdl_b200.metrics.auc import binary_auc
+    from mdl_b200.models.factory import build_model
+    from mdl_b200.train.trainer import Trainer
+
+    torch.set_num_threads(max(1, (os.cpu_count() or 2) // max(1, world)))
+    dist.init_process_group("gloo", init_method=f"file://{init_file}", rank=rank, world_size=world)
+    try:
+        mapping, spec = baseline_config(1)
+        mapping["training"]["dense_optimizer"] = "rmsprop"  # the reference's only dense optimizer
+        cfg = app_config_from_mapping(mapping)
+        torch.manual_seed(0)
+        full = build_model(cfg, device="cpu", base_seed=0)  # one-rank model: the starting weights
+        init_dense = full.reference_state_dict()
+        tables = {t.name: full.store.weight(t.name).clone() for t in full.store.layouts}
+        torch.manual_seed(0)
+        ours = build_model(cfg, device="cpu", rank=rank, world=world, process_group=dist.group.WORLD, base_seed=0)
+        ours.load_reference_state_dict(init_dense)
+        with torch.no_grad():
+            for t in ours.store.layouts:
+                gids = t.spec.global_ids(t.num_embeddings, rank)
+                ours.store.weight(t.name).copy_(tables[t.name][gids])
+        trainer = Trainer(cfg, ours, device=torch.device("cpu"), rank=rank, world=world, process_group=dist.group.WORLD)
+        ref = ReferenceTrainer(mapping, device=torch.device("cpu"), rank=rank, world=world, local=rank,
+                               cuda_graphs=False)
+        ref.base.load_state_dict(init_dense, strict=False)
+        with torch.no_grad():
+            for name, emb in ref.base.encoder_bank.embeddings.items():
+                spec_r = emb.shard_spec
+                g = torch.arange(tables[name].shape[0])
+                own = g[spec_r.owner(g) == rank]
+                emb.weight[spec_r.local_row_ids(own)] = tables[name][own].to(emb.weight.dtype)
+        plan = full.encoder.batch_plan
+        nf = plan.num_src
+        gen = SyntheticGenerator(plan, spec)
+        lo, hi = rank * batch, (rank + 1) * batch
+        losses_o, losses_r = [], []
+        for _ in range(steps):
+            union = gen.batch(batch * world)
+            mine = union.slice_rows(lo, hi, nf)
+            losses_o.append(float(trainer.train_step(mine).loss))
+            losses_r.append(float(ref.step(to_feature_batch(ref.rdata, mine, plan))))
+        ref.model.eval()
+        so, sr, ys = [], [], []
+        with torch.no_grad():
+            for _ in range(8):
+                union = gen.batch(batch * world)
+                mine = union.slice_rows(lo, hi, nf)
+                so.append(trainer.predict_logits(mine)[:, 0].float())
+                fb = to_feature_batch(ref.rdata, mine, plan)
+                sr.append(ref.model(fb.features, fb.scenario_id)["logits"][:, 0].float())
+                ys.append(mine.labels[:, 0].float())
+        local = torch.stack([torch.cat(so), torch.cat(sr), torch.cat(ys)])
+        gathered = [torch.zeros_like(local) for _ in range(world)]
+        dist.all_gather(gathered, local)
+        if rank == 0:
+            allv = torch.cat(gathered, dim=1)
+            result = {"auc_ours": binary_auc(allv[0], allv[2]), "auc_reference": binary_auc(allv[1], allv[2]),
+                      "first_loss": [losses_o[0], losses_r[0]], "last_loss": [losses_o[-1], losses_r[-1]],
+                      "world": world, "steps": steps}
+            with open(out_path, "w") as fh:
+                json.dump(result, fh)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()

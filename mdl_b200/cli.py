@@ -156,7 +156,9 @@ def _batches(config, model, rank, world, *, split="train", synthetic=False, batc
         return ParquetBatchIterator(paths, tz, rows, rank=rank,
                                     world=world, shard_unit=r.shard_unit, shuffle_rows=r.shuffle_buffer_rows,
                                     seed=r.shuffle_seed, prefetch=r.prefetch_batches, loop=loop and split == "train",
-                                    pin=r.pin_memory, io_policy=RemoteIoPolicy.from_reader(r))
+                                    pin=r.pin_memory, io_policy=RemoteIoPolicy.from_reader(r),
+                                    length_buckets=[(b.max_length, b.batch_size) for b in r.length_buckets],
+                                    length_bucket_metric=r.length_bucket_metric)
     gen = SyntheticGenerator(model.encoder.batch_plan, synthetic_spec_from_config(config, model.encoder.batch_plan),
                              rank=rank)
 

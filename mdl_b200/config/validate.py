@@ -47,7 +47,27 @@ def validate_app_config(config: AppConfig) -> None:
     for item in tok.feature_token_inputs:
         _require(item in known, f"tokenization.feature_token_inputs: unknown input {item!r}")
 
+    # options this framework implements differently or not at all are rejected, never
+    # silently changed into something else
+    rt = config.runtime
+    _require(rt.precision != "fp16", "runtime.precision fp16 (autocast with a GradScaler) is not implemented; use bf16")
+    if rt.device == "cuda" and rt.kernel_backend == "native":
+        _require(rt.precision == "bf16", f"runtime.precision {rt.precision!r} on CUDA: the sm_100a kernels compute in "
+                                         "bf16 (use precision bf16, or kernel_backend torch for fp32 math)")
+    seq_by_name = {s.name: s for s in config.sequences}
+    for sequence in config.sequences:
+        if sequence.encoder == "longer":
+            _require(int(sequence.longer_token_merge) == 1 and int(sequence.longer_inner_layers) == 0,
+                     f"sequence {sequence.name!r}: LONGER token merging (longer_token_merge > 1, "
+                     "longer_inner_layers) is not implemented")
     model = config.model
+    if model.name in ("rankmixer", "mdl_rankmixer"):
+        raw = [n for n in config.resolved.tokenization.feature_token_inputs
+               if n in seq_by_name and seq_by_name[n].encoder == "raw"]
+        _require(not raw, f"{model.name} feature tokens cannot read raw sequences {raw}: give them a summary encoder "
+                          "(mean_pool, attention_pool, longer or stca)")
+    _require(model.sequence_fusion in ("intent_ordered", "timestamp_aware"),
+             f"model.sequence_fusion {model.sequence_fusion!r}")
     _require(model.token_dim > 0 and model.num_layers >= 0 and model.hidden_dim > 0, "model dims must be positive")
     if model.name in ("rankmixer", "mdl_rankmixer"):
         count = config.resolved.tokenization.feature_token_count
@@ -80,6 +100,7 @@ def validate_app_config(config: AppConfig) -> None:
                  "DTSI needs model.sparse_moe_dtsi_training_output (dense_router or mean)")
     train = config.training
     _require(train.batch_size > 0, "training.batch_size must be positive")
+    _require(not train.rmsprop_momentum, "training.rmsprop_momentum: RMSprop with momentum is not implemented")
     _require(train.gradient_accumulation_steps >= 1, "gradient_accumulation_steps must be >= 1")
     _require(train.lr_dense > 0, "lr_dense must be positive")
     for task in train.task_loss_weights:

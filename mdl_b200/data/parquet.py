@@ -323,6 +323,29 @@ class Tensorizer:
             out["dense"] = torch.from_numpy(dense.reshape(rows * L, width))
         return out
 
+    def sequence_lengths(self, table, metric: str = "max") -> np.ndarray:
+        """Per-row sequence work (reference ``_table_effective_sequence_lengths``
+        ``src/train.py:1936-1952``): over the model's sequences, the max (or sum) of each
+        row's event count, capped at each sequence's ``max_length``."""
+
+        import pyarrow as pa
+
+        out = np.zeros(table.num_rows, dtype=np.int64)
+        for q in self.sequences:
+            if not q.fields:
+                continue
+            fl = q.fields[0]
+            col = table.column(fl.source or fl.name)
+            col = col.combine_chunks() if isinstance(col, pa.ChunkedArray) else col
+            offs = col.offsets.to_numpy().astype(np.int64)
+            n = offs[1:] - offs[:-1]
+            if col.null_count:
+                n = np.where(col.is_null().to_numpy(zero_copy_only=False), 0, n)
+            if q.max_length:
+                n = np.minimum(n, int(q.max_length))
+            out = out + n if metric == "sum" else np.maximum(out, n)
+        return out
+
     def _sequences(self, table) -> dict:
         """Sequence payloads; with request deduplication one row per distinct ``request_id``
         (in order of first appearance) plus ``row_indices`` (candidate -> request row)."""
@@ -441,8 +464,17 @@ class ParquetBatchIterator:
     def __init__(self, paths: Sequence[str], tensorizer: Tensorizer, batch_size: int, *, rank: int = 0,
                  world: int = 1, shard_unit: str = "row_group", shuffle_rows: int = 0, seed: int = 0,
                  drop_last: bool = True, prefetch: int = 2, pin: bool = False, start_position: int = 0,
-                 loop: bool = False, io_policy=None) -> None:
+                 loop: bool = False, io_policy=None, length_buckets: Sequence = (),
+                 length_bucket_metric: str = "max") -> None:
+        """``length_buckets``: ``(max_length or None, batch_size)`` pairs in increasing
+        length order (the last may be the catch-all ``None``): rows are grouped by their
+        sequence work (``Tensorizer.sequence_lengths``) and each bucket yields batches of
+        its own size, so short-history rows are not padded to the longest history
+        (reference ``_iter_length_bucketed_tables`` ``src/train.py:1955-2077``)."""
+
         self.refs = plan_row_groups(paths, rank, world, shard_unit)
+        self.buckets = [(None if m is None else int(m), int(b)) for m, b in length_buckets]
+        self.bucket_metric = length_bucket_metric
         self.io = io_policy  # RemoteIoPolicy: timeouts, retries and skips of remote reads
         self.rank = rank
         self.tz = tensorizer
@@ -481,7 +513,36 @@ class ParquetBatchIterator:
                 return
             self.position = 0
 
+    def _bucketed(self):
+        """Length-bucketed batches: shuffled rows routed to their bucket's buffer."""
+
+        pa, _ = _pa()
+        bounds = np.array([m for m, _ in self.buckets if m is not None], dtype=np.int64)
+        bufs: list = [None] * len(self.buckets)
+        for t in self._tables():
+            if self.shuffle_rows:
+                t = t.take(pa.array(self.rng.permutation(t.num_rows)))
+            which = np.searchsorted(bounds, self.tz.sequence_lengths(t, self.bucket_metric), side="left")
+            if self.buckets[-1][0] is not None and (which >= len(self.buckets)).any():
+                raise ValueError("a row's sequence length exceeds every reader.length_buckets max_length "
+                                 "(add a catch-all bucket without max_length)")
+            for k, (_m, size) in enumerate(self.buckets):
+                sel = np.nonzero(which == k)[0]
+                if not len(sel):
+                    continue
+                part = t.take(pa.array(sel))
+                bufs[k] = part if bufs[k] is None else pa.concat_tables([bufs[k], part])
+                while bufs[k].num_rows >= size:
+                    yield self.tz(bufs[k].slice(0, size), pin=self.pin)
+                    bufs[k] = bufs[k].slice(size)
+        for k, buf in enumerate(bufs):
+            if buf is not None and buf.num_rows and not self.drop_last:
+                yield self.tz(buf, pin=self.pin)
+
     def _batches(self):
+        if self.buckets and self.tz.sequences:
+            yield from self._bucketed()
+            return
         pa, _ = _pa()
         buf = None
         for t in self._tables():

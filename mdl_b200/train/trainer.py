@@ -4,9 +4,9 @@ One ``Trainer`` owns a model, its flat dense parameters (``DenseParams``) and
 its embedding store, and runs the reference's optimizer-step semantics
 (``train_mdl`` ``src/train.py:6529-7431``, hot loop :6832-7360):
 
-* loss reduction ``sum`` / ``mean_per_task`` with per-task weights, scaled so
-  that the rank-averaged gradient equals the global objective
-  (``_loss_terms_from_batch`` ``src/train.py:5890-6031``);
+* loss reduction ``sum`` / ``mean_per_task`` / ``mean_per_request_per_task``
+  with per-task weights, scaled so that the rank-averaged gradient equals the
+  global objective (``_loss_terms_from_batch`` ``src/train.py:5890-6031``);
 * LR schedule: linear warmup then constant or cosine (``src/train.py:5495-5512``);
 * dense optimizer (RMSprop or Adam) after the gradient average, optional
   global clip (``src/train.py:5745-5826``);
@@ -125,8 +125,52 @@ class Trainer:
         self._phase_marks = []
         return {k: sums[k] / counts[k] for k in sums}
 
+    def request_weights(self, batch):
+        """``mean_per_request_per_task`` (reference ``_loss_terms_from_batch``
+        ``src/train.py:5921-5957``): each request's candidates share one mean per task.
+
+        Returns ``(batch with per-row weights, task_scale)``: the label mask becomes
+        ``mask / count(request, task)`` for rows of requests with a labelled candidate,
+        and the per-task scale is ``W / global number of such requests`` -- the same
+        loss as averaging per request, then over requests, then summing over tasks."""
+
+        import dataclasses
+
+        rows = batch.rows
+        ri = None
+        for seq in (batch.sequences or {}).values():
+            cand = seq.get("row_indices") if isinstance(seq, dict) else None
+            if cand is not None and cand.numel() == rows:
+                if ri is not None and not torch.equal(ri, cand.to(ri.device)):
+                    raise ValueError("request-level loss requires one consistent row_indices mapping")
+                ri = cand
+        if ri is None:
+            raise ValueError("mean_per_request_per_task requires request-deduplicated features with "
+                             "candidate-to-request row_indices")
+        dev = self.device
+        ri = ri.to(dev).long()
+        ntask = len(self.config.task_names)
+        mask = (batch.label_mask.to(dev).float() if batch.label_mask is not None
+                else torch.ones(rows, ntask, device=dev))
+        _req, inv = torch.unique(ri, sorted=True, return_inverse=True)
+        counts = torch.zeros(_req.numel(), ntask, device=dev).index_add_(0, inv, mask)
+        per_row = mask / counts[inv].clamp_min(1.0)
+        valid = (counts > 0).float().sum(dim=0)
+        if self.world > 1 and dist.is_initialized():
+            dist.all_reduce(valid, group=self.group)
+        W = float(self.world)
+        scale = torch.where(valid > 0, W / valid.clamp_min(1.0), torch.zeros_like(valid)) * self.task_weights
+        return dataclasses.replace(batch, label_mask=per_row), scale
+
     def forward_backward(self, batch) -> dict:
         self._mark("start")
+        if self.config.training.loss_reduction == "mean_per_request_per_task":
+            batch, scale = self.request_weights(batch)
+            out = self.model(batch, task_scale=scale)
+            self._mark("forward")
+            out["loss"].backward()
+            self._mark("backward")
+            return out
         out = self.model(batch, task_scale=self.task_scale(batch))
         self._mark("forward")
         out["loss"].backward()

@@ -1,0 +1,68 @@
+"""Loss reductions of the training step against the reference's definitions
+(``_loss_terms_from_batch``, ``src/train.py:5890-6031``), written out here in plain
+PyTorch: ``sum``, ``mean_per_task`` and ``mean_per_request_per_task`` (per-request
+means over candidates, then the mean over requests with a labelled candidate)."""
+
+import copy
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from mdl_b200.config import app_config_from_mapping
+from mdl_b200.data.baseline_configs import scaled_config
+from mdl_b200.data.synthetic import SequenceSpec, FieldSpec, SyntheticGenerator
+from mdl_b200.models.factory import build_model
+from mdl_b200.train.trainer import Trainer
+
+
+def _setup(reduction, cpr=4):
+    m, spec = scaled_config(2, 0.0002, num_fields=8, batch=64)
+    m["runtime"].update({"device": "cpu", "precision": "fp32"})
+    m["model"].update({"token_dim": 64, "hidden_dim": 128, "task_head_hidden_dim": 32, "num_heads": 4})
+    m["tokenization"]["num_feature_tokens"] = 4
+    m["sequences"] = [{"name": "hist", "max_length": 12, "encoder": "mean_pool", "pool_dim": 16,
+                       "fields": [{"name": "item", "kind": "categorical", "source": "hist_item", "embedding_dim": 8,
+                                   "encoding": {"type": "identity", "max_id": 500}}]}]
+    m["tokenization"]["feature_token_inputs"] = [f["name"] for f in m["features"]] + ["hist"]
+    m["training"]["loss_reduction"] = reduction
+    cfg = app_config_from_mapping(m)
+    torch.manual_seed(0)
+    model = build_model(cfg, device="cpu", base_seed=0)
+    spec = copy.deepcopy(spec)
+    spec.sequences = {"hist": SequenceSpec(fields={"item": FieldSpec(vocab=500)}, max_len=12, min_len=1,
+                                           candidates_per_request=cpr)}
+    batch = SyntheticGenerator(model.encoder.batch_plan, spec).batch(64)
+    g = torch.Generator().manual_seed(1)
+    batch.label_mask = (torch.rand(batch.labels.shape, generator=g) > 0.3).float()
+    return cfg, model, Trainer(cfg, model, device=torch.device("cpu")), batch
+
+
+def _reference_loss(logits, labels, mask, reduction, row_indices=None):
+    element = F.binary_cross_entropy_with_logits(logits, labels, reduction="none")
+    if reduction == "mean_per_request_per_task":
+        req, inv = torch.unique(row_indices, sorted=True, return_inverse=True)
+        num = torch.zeros(req.numel(), logits.shape[1]).index_add(0, inv, element * mask)
+        cnt = torch.zeros(req.numel(), logits.shape[1]).index_add(0, inv, mask)
+        means = torch.where(cnt > 0, num / cnt.clamp_min(1.0), torch.zeros_like(num))
+        task_num, task_cnt = means.sum(0), (cnt > 0).float().sum(0)
+    else:
+        task_num, task_cnt = (element * mask).sum(0), mask.sum(0)
+    if reduction == "sum":
+        return task_num.sum()
+    return (task_num * torch.where(task_cnt > 0, 1.0 / task_cnt.clamp_min(1.0), torch.zeros_like(task_cnt))).sum()
+
+
+@pytest.mark.parametrize("reduction", ["sum", "mean_per_task", "mean_per_request_per_task"])
+def test_loss_matches_reference_definition(reduction):
+    cfg, model, tr, batch = _setup(reduction)
+    out = tr.forward_backward(batch)
+    ri = batch.sequences["hist"]["row_indices"]
+    want = _reference_loss(out["logits"].detach().float(), batch.labels.float(), batch.label_mask, reduction, ri)
+    torch.testing.assert_close(out["loss"].detach().float(), want, rtol=1e-5, atol=1e-6)
+
+
+def test_mean_per_request_needs_request_rows():
+    cfg, model, tr, batch = _setup("mean_per_request_per_task", cpr=1)
+    with pytest.raises(ValueError, match="row_indices"):
+        tr.forward_backward(batch)

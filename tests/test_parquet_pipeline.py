@@ -142,3 +142,48 @@ def test_host_prepare_startup_timeout():
     with pytest.raises(TimeoutError):
         list(it)
     it.close(join_timeout_s=1.0)
+
+
+def test_length_buckets_group_rows_by_sequence_work(tmp_path):
+    """reader.length_buckets: every batch holds rows of one length bucket, in that
+    bucket's batch size; no row is lost or duplicated."""
+
+    import pyarrow as pa
+    import pyarrow.parquet as pq
+
+    from mdl_b200.ops.embedding import LookupFeature, LookupPlan
+
+    rng = np.random.default_rng(0)
+    n = 200
+    lengths = rng.integers(0, 12, size=n)
+    hist = [list(range(1, int(k) + 1)) for k in lengths]
+    table = pa.table({"f": pa.array(np.arange(1, n + 1) % 50, type=pa.int64()),
+                      "hist_item": pa.array(hist, type=pa.list_(pa.int64())),
+                      "click": pa.array(rng.integers(0, 2, size=n).astype(np.float32))})
+    pq.write_table(table, str(tmp_path / "part.parquet"), row_group_size=50)
+    m = {"data": {"train": {"format": "flat_parquet", "inputs": [str(tmp_path)], "labels": {"click": "click"},
+                            "reader": {"length_buckets": [{"max_length": 4, "batch_size": 16},
+                                                          {"batch_size": 8}]}}},
+         "features": [{"name": "f", "kind": "categorical", "source": "f", "embedding_dim": 8,
+                       "encoding": {"type": "identity", "max_id": 100}}],
+         "sequences": [{"name": "hist", "max_length": 10, "encoder": "mean_pool", "pool_dim": 8,
+                        "fields": [{"name": "item", "kind": "categorical", "source": "hist_item", "embedding_dim": 8,
+                                    "encoding": {"type": "identity", "max_id": 100}}]}],
+         "model": {"name": "rankmixer", "token_dim": 16, "num_layers": 1, "hidden_dim": 32},
+         "tokenization": {"feature_tokenizer": "rankmixer", "num_feature_tokens": 2},
+         "runtime": {"device": "cpu", "precision": "fp32"}, "training": {"batch_size": 16}}
+    cfg = app_config_from_mapping(m)
+    plan = LookupPlan([LookupFeature("f", "f", width=8)], out_width=8)
+    tz = Tensorizer(cfg, plan, seq_names=["hist"])
+    r = cfg.data.train.reader
+    it = ParquetBatchIterator([str(tmp_path / "part.parquet")], tz, 16, drop_last=False, shuffle_rows=0,
+                              length_buckets=[(b.max_length, b.batch_size) for b in r.length_buckets])
+    seen = []
+    for b in it:
+        ln = b.sequences["hist"]["lengths"].numpy()
+        short = ln <= 4
+        assert short.all() or (~short).all(), ln
+        full = 16 if short.all() else 8
+        assert b.rows <= full
+        seen += (b.ids[:b.rows].numpy() - 1).tolist()  # f = (row + 1) % 50 identifies rows up to 50
+    assert len(seen) == n
