@@ -153,7 +153,12 @@ def _batches(config, model, rank, world, *, split="train", synthetic=False, batc
                                         startup_timeout_s=r.host_prepare_startup_timeout_sec,
                                         idle_timeout_s=r.host_prepare_idle_timeout_sec)
         tz = Tensorizer(config, model.encoder.batch_plan, split=split, seq_names=list(model.encoder.seq_plans))
-        return ParquetBatchIterator(paths, tz, rows, rank=rank,
+        adapter = None
+        if sp.format in ("adapter_parquet", "agg_parquet"):
+            from .data.agg import AggAdapter, AggPlan
+
+            adapter = AggAdapter(AggPlan.from_config(config, split))
+        return ParquetBatchIterator(paths, tz, rows, rank=rank, adapter=adapter,
                                     world=world, shard_unit=r.shard_unit, shuffle_rows=r.shuffle_buffer_rows,
                                     seed=r.shuffle_seed, prefetch=r.prefetch_batches, loop=loop and split == "train",
                                     pin=r.pin_memory, io_policy=RemoteIoPolicy.from_reader(r),

@@ -26,7 +26,10 @@ def _cap_encoding(enc: dict | None, max_rows: int) -> None:
 
 
 def shrink_mapping(mapping: dict[str, Any], *, max_rows: int = 512, max_length: int = 16, batch: int = 16,
-                   device: str = "cpu") -> dict[str, Any]:
+                   device: str = "cpu", max_hidden: int | None = None) -> dict[str, Any]:
+    """``max_hidden`` also caps the FFN / head hidden widths (token widths, token counts
+    and head counts stay as configured)."""
+
     m = copy.deepcopy(mapping)
     for f in m.get("features", []):
         _cap_encoding(f.get("encoding"), max_rows)
@@ -42,6 +45,13 @@ def shrink_mapping(mapping: dict[str, Any], *, max_rows: int = 512, max_length: 
         if s.get("longer_query_tokens"):
             s["longer_query_tokens"] = min(int(s["longer_query_tokens"]), max(1, max_length // 2))
     model = m.setdefault("model", {})
+    if max_hidden:
+        for key in ("hidden_dim", "task_head_hidden_dim"):
+            if model.get(key):
+                model[key] = min(int(model[key]), int(max_hidden))
+        for s in m.get("sequences", []):
+            if s.get("longer_hidden_dim"):
+                s["longer_hidden_dim"] = min(int(s["longer_hidden_dim"]), int(max_hidden))
     if model.get("max_position_embeddings"):
         model["max_position_embeddings"] = min(int(model["max_position_embeddings"]), 64 * max_length)
     runtime = m.setdefault("runtime", {})

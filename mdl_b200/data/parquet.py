@@ -465,7 +465,7 @@ class ParquetBatchIterator:
                  world: int = 1, shard_unit: str = "row_group", shuffle_rows: int = 0, seed: int = 0,
                  drop_last: bool = True, prefetch: int = 2, pin: bool = False, start_position: int = 0,
                  loop: bool = False, io_policy=None, length_buckets: Sequence = (),
-                 length_bucket_metric: str = "max") -> None:
+                 length_bucket_metric: str = "max", adapter=None) -> None:
         """``length_buckets``: ``(max_length or None, batch_size)`` pairs in increasing
         length order (the last may be the catch-all ``None``): rows are grouped by their
         sequence work (``Tensorizer.sequence_lengths``) and each bucket yields batches of
@@ -473,6 +473,9 @@ class ParquetBatchIterator:
         (reference ``_iter_length_bucketed_tables`` ``src/train.py:1955-2077``)."""
 
         self.refs = plan_row_groups(paths, rank, world, shard_unit)
+        # adapter: raw Arrow table -> flat rows (e.g. the agg layout, ``data/agg.py``);
+        # the files are then read with the adapter's raw columns
+        self.adapter = adapter
         self.buckets = [(None if m is None else int(m), int(b)) for m, b in length_buckets]
         self.bucket_metric = length_bucket_metric
         self.io = io_policy  # RemoteIoPolicy: timeouts, retries and skips of remote reads
@@ -492,7 +495,7 @@ class ParquetBatchIterator:
 
     def _tables(self):
         pa, pq = _pa()
-        cols = self.tz.columns()
+        cols = self.adapter.plan.raw_columns() if self.adapter is not None else self.tz.columns()
         while not self._stop.is_set():
             if self.io is not None and self.position == 0:
                 self.io.stagger(self.rank)
@@ -508,7 +511,7 @@ class ParquetBatchIterator:
                                                                  path=ref.path)
                 self.position += 1
                 if t is not None:
-                    yield t
+                    yield self.adapter(t) if self.adapter is not None else t
             if not self.loop or not self.refs:
                 return
             self.position = 0

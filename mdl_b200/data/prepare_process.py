@@ -39,9 +39,15 @@ def parquet_batches(config_mapping: dict, batch_plan, paths: list[str], batch_si
 
     cfg = app_config_from_mapping(config_mapping)
     tz = Tensorizer(cfg, batch_plan, split=split, seq_names=seq_names)
-    r = (getattr(cfg.data, split) or cfg.data.train).reader
+    sp = getattr(cfg.data, split) or cfg.data.train
+    r = sp.reader
+    adapter = None
+    if sp.format in ("adapter_parquet", "agg_parquet"):
+        from .agg import AggAdapter, AggPlan
+
+        adapter = AggAdapter(AggPlan.from_config(cfg, split))
     it = ParquetBatchIterator(paths, tz, batch_size, rank=rank, world=world, shuffle_rows=shuffle_rows, seed=seed,
-                              loop=loop, prefetch=2, pin=False,
+                              loop=loop, prefetch=2, pin=False, adapter=adapter,
                               length_buckets=[(b.max_length, b.batch_size) for b in r.length_buckets],
                               length_bucket_metric=r.length_bucket_metric)
     return iter(it)

@@ -1,10 +1,10 @@
 """Every config the reference ships builds here and trains one step on CPU.
 
 The reference's ``configs/*.yaml`` load unchanged through this framework's loader;
-``shrink_mapping`` then caps table rows, sequence lengths and the batch (the
-architecture stays as configured: feature groups, sequence encoders, token layout,
-model family and widths), and one training step runs on synthetic data of that
-shape. Skipped when the reference sources are not available."""
+``shrink_mapping`` then caps table rows, sequence lengths, the batch and the FFN
+hidden widths (the architecture stays as configured: feature groups, sequence
+encoders, token layout, model family and token widths), and one training step runs
+on synthetic data of that shape. Skipped when the reference sources are not available."""
 
 import math
 import os
@@ -28,7 +28,8 @@ def test_reference_config_builds_and_trains_one_step(name):
     from mdl_b200.models.factory import build_model
     from mdl_b200.train.trainer import Trainer
 
-    mapping = shrink_mapping(load_config_mapping(os.path.join(CONFIG_DIR, f"{name}.yaml")), batch=8)
+    mapping = shrink_mapping(load_config_mapping(os.path.join(CONFIG_DIR, f"{name}.yaml")), batch=8,
+                             max_hidden=256)
     cfg = app_config_from_mapping(mapping)
     torch.manual_seed(0)
     model = build_model(cfg, device="cpu", base_seed=0)
