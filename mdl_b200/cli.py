@@ -164,8 +164,9 @@ def _batches(config, model, rank, world, *, split="train", synthetic=False, batc
                                     pin=r.pin_memory, io_policy=RemoteIoPolicy.from_reader(r),
                                     length_buckets=[(b.max_length, b.batch_size) for b in r.length_buckets],
                                     length_bucket_metric=r.length_bucket_metric)
-    gen = SyntheticGenerator(model.encoder.batch_plan, synthetic_spec_from_config(config, model.encoder.batch_plan),
-                             rank=rank)
+    seqs = [s for s in config.sequences if s.name in getattr(model.encoder, "seq_plans", {})]
+    gen = SyntheticGenerator(model.encoder.batch_plan,
+                             synthetic_spec_from_config(config, model.encoder.batch_plan, sequences=seqs), rank=rank)
 
     def forever():
         while True:
@@ -389,44 +390,20 @@ def cmd_benchmark(args, argv) -> int:
     rc = _relaunch(args, argv)
     if rc is not None:
         return rc
-    import torch
-    import torch.distributed as dist
-
     cfg = load_cli_config(args)
     rank, world, device = _setup_runtime(cfg)
     cfg = _resolve_scenarios(cfg, rank, world)
     model, trainer = _build(cfg, rank, world, device)
-    it = _batches(cfg, model, rank, world, synthetic=True)
-    pool = [next(it) for _ in range(3)]
-    dev = [b.to(device) for b in pool] if device.type == "cuda" else pool
-    for i in range(args.warmup):
-        trainer.train_step(dev[i % 3])
-    sync = torch.cuda.synchronize if device.type == "cuda" else (lambda *a: None)
-    sync(device) if device.type == "cuda" else None
-    if world > 1:
-        dist.barrier()
-    t0 = time.perf_counter()
-    if device.type == "cuda":
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-    for i in range(args.steps):
-        trainer.train_step(dev[i % 3])
-    if device.type == "cuda":
-        e1.record()
-        torch.cuda.synchronize(device)
-        ms = e0.elapsed_time(e1)
-    else:
-        ms = (time.perf_counter() - t0) * 1e3
-    t = torch.tensor([ms], dtype=torch.float64, device=device if device.type == "cuda" else "cpu")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t)
-    rows = cfg.training.batch_size * world * args.steps
+    from .benchmark.modes import run as run_mode
+
+    synthetic = args.mode in ("compute", "embedding")
+    it = _batches(cfg, model, rank, world, synthetic=synthetic)
+    res = run_mode(args.mode, cfg, model, trainer, iter(it), rank=rank, world=world, device=device,
+                   steps=args.steps, warmup=args.warmup, min_util=args.min_util)
+    _close(it)
     if rank == 0:
-        print(json.dumps({"metric": "train samples/sec", "value": round(rows / (ms / 1e3), 1), "n_gpus": world,
-                          "ms_per_step": round(ms / args.steps, 4), "model": cfg.model.name,
-                          "global_batch": cfg.training.batch_size * world}), flush=True)
-    return 0
+        print(json.dumps(res), flush=True)
+    return 3 if "util_gate" in res else 0
 
 
 def _close(it) -> None:
@@ -557,6 +534,11 @@ def build_parser() -> argparse.ArgumentParser:
         if name == "benchmark":
             p.add_argument("--steps", type=int, default=20)
             p.add_argument("--warmup", type=int, default=5)
+            p.add_argument("--mode", choices=["compute", "end-to-end", "data", "embedding"], default="compute",
+                           help="compute: device-resident synthetic batches; end-to-end: the input pipeline + "
+                                "H2D + training; data: the input pipeline only; embedding: lookup + sparse update")
+            p.add_argument("--min-util", type=float, default=None,
+                           help="utilisation gate: report a failure (exit 3) below this mean GPU utilisation")
         if name in ("evaluate", "predict"):
             p.add_argument("--checkpoint")
             p.add_argument("--max-batches", type=int, default=10)

@@ -340,13 +340,18 @@ class FeatureEncoder:
         return self.plan.slice_stride
 
 
-def lookup_sequence(encoder: FeatureEncoder, batch, name: str, rows: int, max_len: int, anchor: torch.Tensor):
+def lookup_sequence(encoder: FeatureEncoder, batch, name: str, rows: int, max_len: int, anchor: torch.Tensor,
+                    expand: bool = True):
     """Event rows ``[rows * max_len, out_ld]`` of sequence ``name`` and its lengths ``[rows]``.
 
     With request-level batching (``row_indices`` in the sequence payload, reference
     ``_batch_gather_indexed_rows`` ``src/model.py:701-750``) the events are looked up
     once per request (``R * max_len`` rows) and each candidate row then takes its
-    request's rows (``index_select``; its backward sums the candidates of a request)."""
+    request's rows (``index_select``; its backward sums the candidates of a request).
+    With ``expand=False`` the request-level rows come back as ``(rows [R * max_len, out_ld],
+    lengths [R], row_indices or None)``, so request-only work (event projections) runs
+    once per request before ``expand_requests`` hands each candidate its request's result
+    (the training-time counterpart of the reference's request caches)."""
 
     from ..ops.embedding import fused_lookup
 
@@ -363,8 +368,18 @@ def lookup_sequence(encoder: FeatureEncoder, batch, name: str, rows: int, max_le
         cache[key] = torch.arange(nf * R * max_len + 1, dtype=torch.int64, device=ids.device)
     x = fused_lookup(encoder.store, encoder.seq_plans[name], ids, cache[key], seq.get("dense"), R * max_len, anchor)
     ri = seq.get("row_indices")
+    if not expand:
+        return x, lengths, (None if ri is None else ri.to(x.device))
     if ri is None:
         return x, lengths
     ri = ri.to(x.device)
     x = x.view(R, max_len * x.shape[1]).index_select(0, ri).view(rows * max_len, x.shape[1])
     return x, lengths.index_select(0, ri.to(lengths.device))
+
+
+def expand_requests(t: torch.Tensor, row_indices: torch.Tensor | None) -> torch.Tensor:
+    """Request-level rows (leading axis) -> candidate rows (identity without request batching)."""
+
+    if row_indices is None:
+        return t
+    return t.index_select(0, row_indices.to(t.device))

@@ -309,18 +309,28 @@ class LongerEncoder(nn.Module):
             self.pos = nn.Parameter(torch.randn(self.L, c0, device=device) * float(m.init_std))
             self._pad_cols = plan.out_ld - c0
 
-    def forward(self, seq_in, lengths, target_in, user_in, native: bool, cls_tokens=None) -> torch.Tensor:
+    def project(self, seq_in, lengths, native: bool) -> torch.Tensor:
+        """Event tokens ``[rows, L, d]`` (positions added to the event values first)."""
+
+        rows, L = lengths.shape[0], self.L
+        if self.pos is not None:
+            from .sequence_encoders import positions
+
+            pe = self.pos[positions(lengths, L)].view(rows * L, self.pos_cols)
+            pe = F.pad(pe, (0, self._pad_cols)) if self._pad_cols else pe
+            seq_in = seq_in + pe.to(seq_in.dtype)
+        return self.step(seq_in, native).view(rows, L, self.D)
+
+    def forward(self, seq_in, lengths, target_in, user_in, native: bool, cls_tokens=None,
+                tokens=None) -> torch.Tensor:
+        """``tokens``: event tokens already projected (``project``), else ``seq_in`` is projected here."""
+
         B, L, D, R, G = lengths.shape[0], self.L, self.D, self.R, self.G
         if native and self.head_dim != 32:
             raise NotImplementedError(f"LONGER head_dim {self.head_dim}: the tcgen05 attention kernels take head_dim "
                                       "32 (set runtime.kernel_backend: torch for this model)")
-        if self.pos is not None:
-            from .sequence_encoders import positions
-
-            pe = self.pos[positions(lengths, L)].view(B * L, self.pos_cols)
-            pe = F.pad(pe, (0, self._pad_cols)) if self._pad_cols else pe
-            seq_in = seq_in + pe.to(seq_in.dtype)
-        tokens = self.step(seq_in, native).view(B, L, D)
+        if tokens is None:
+            tokens = self.project(seq_in, lengths, native)
         parts = [tokens]
         if self.Gu:
             parts.append(self.user_mlp(user_in, native).view(B, self.Gu, D))

@@ -93,15 +93,25 @@ class PoolSequenceEncoder(nn.Module):
             else:
                 self.query = nn.Parameter(torch.randn(1, self.S, self.P, device=device) * init_std)
 
-    def forward(self, seq_in: torch.Tensor, lengths: torch.Tensor, target: torch.Tensor | None) -> torch.Tensor:
-        B, L, P = lengths.shape[0], self.L, self.P
-        tokens = self.step(seq_in).float().view(B, L, P)
+    def forward(self, seq_in: torch.Tensor, lengths: torch.Tensor, target: torch.Tensor | None,
+                row_indices: torch.Tensor | None = None) -> torch.Tensor:
+        """``seq_in``/``lengths`` per request (``row_indices``: candidate -> request) or per
+        candidate; the event projection and the mean pool run once per request."""
+
+        from .features import expand_requests
+
+        R, L, P = lengths.shape[0], self.L, self.P
+        tokens = self.step(seq_in).float().view(R, L, P)
         tokens = tokens + self.pos.float()[positions(lengths, L)]
         mask = valid_mask(lengths, L)
         m = mask.unsqueeze(-1).float()
         if self.mode == "mean_pool":
             pooled = (tokens * m).sum(dim=1) / m.sum(dim=1).clamp_min(1.0)
+            pooled = expand_requests(pooled, row_indices)
             return pooled.repeat(1, self.S) if self.S > 1 else pooled
+        tokens = expand_requests(tokens, row_indices)
+        mask = expand_requests(mask, row_indices)
+        B = tokens.shape[0]
         if self.query_proj is not None:
             q = self.query_proj(target).float().view(B, self.S, P)
         else:
@@ -135,10 +145,14 @@ class LongerSummaryEncoder(nn.Module):
                              f"{self.longer.Gu} + cls {self.cls} + candidate {self.longer.Gc}) != "
                              f"rankmixer_summary_tokens {want}")
 
-    def forward(self, seq_in, lengths, target, user, native: bool) -> torch.Tensor:
+    def forward(self, seq_in, lengths, target, user, native: bool, row_indices=None) -> torch.Tensor:
+        from .features import expand_requests
         from .longer import LongerEncoder
 
-        X = self.longer(seq_in, lengths, target, user, native, cls_tokens=self.cls_tokens)
+        # event tokens once per request, then each candidate takes its request's tokens
+        tokens = expand_requests(self.longer.project(seq_in, lengths, native), row_indices)
+        lengths = expand_requests(lengths, row_indices)
+        X = self.longer(None, lengths, target, user, native, cls_tokens=self.cls_tokens, tokens=tokens)
         G = self.longer.G
         B = lengths.shape[0]
         if self.summary:
@@ -228,17 +242,20 @@ class SequenceSummaries(nn.Module):
         for name in self.names:
             kind, L, ti, ui = self.meta[name]
             mod = self.mods[name]
-            seq_in, lengths = lookup_sequence(enc, batch, name, B, L, anchor)
+            seq_in, lengths, ri = lookup_sequence(enc, batch, name, B, L, anchor, expand=False)
             if not native:
                 seq_in = seq_in.float()
             if kind in ("mean_pool", "attention_pool"):
-                out[name] = mod(seq_in, lengths, group(ti))
+                out[name] = mod(seq_in, lengths, group(ti), ri)
             elif kind == "longer":
-                out[name] = mod(seq_in, lengths, group(ti), group(ui), native)
+                out[name] = mod(seq_in, lengths, group(ti), group(ui), native, ri)
             else:  # stca
-                hist = mod.step(seq_in, native).view(B, L, -1)
+                from .features import expand_requests
+
+                hist = expand_requests(mod.step(seq_in, native).view(lengths.shape[0], L, -1), ri)
                 target = mod.target(group(ti), native)
-                out[name] = mod.encoder(hist, valid_mask(lengths, L), target, native).float()
+                valid = expand_requests(valid_mask(lengths, L), ri)
+                out[name] = mod.encoder(hist, valid, target, native).float()
         return out
 
 

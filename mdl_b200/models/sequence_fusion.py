@@ -92,13 +92,16 @@ class SequenceGroups(nn.Module):
         return self.proj[g](x if native else x.float())
 
     def forward(self, encoder, batch, anchor: torch.Tensor, native: bool):
-        from .features import lookup_sequence
+        from .features import expand_requests, lookup_sequence
 
         B = batch.rows
         parts, masks, keys = [], [], []
         for g, (name, L) in enumerate(zip(self.names, self.lengths)):
-            seq_in, lengths = lookup_sequence(encoder, batch, name, B, L, anchor)
-            tok = self._project(g, seq_in, native).view(B, L, self.width)
+            # events projected once per request, then handed to the request's candidates
+            seq_in, lengths, ri = lookup_sequence(encoder, batch, name, B, L, anchor, expand=False)
+            tok = self._project(g, seq_in, native).view(lengths.shape[0], L, self.width)
+            tok = expand_requests(tok, ri)
+            lengths = expand_requests(lengths, ri)
             if not native:
                 tok = tok.float()
             if self.type_emb is not None:

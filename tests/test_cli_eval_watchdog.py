@@ -151,3 +151,18 @@ def test_cli_replicated_tables_checkpoint_reshards(tmp_path):
     logs = _run("train", *shard, "--nproc-per-node", "2", "--master-port", "29569", "--max-steps", "5",
                 "--checkpoint-dir", str(run), "--log-every", "1")
     assert [l["step"] for l in logs if "loss" in l][0] == 5
+
+
+def test_cli_benchmark_modes(tmp_path):
+    """``benchmark --mode compute | embedding | data | end-to-end`` on CPU: every mode
+    reports throughput and step-time percentiles; compute / end-to-end add the dense
+    GEMM MFU; end-to-end and data read the Parquet inputs."""
+
+    data = tmp_path / "data"
+    _run("make-synthetic-parquet", "--benchmark", "1", "--files", "1", "--rows", "512", "--out", str(data))
+    over = ["--benchmark-config", "1", "--set", f"data.train.inputs=[{str(data)}]", "--set", "training.batch_size=64"]
+    for mode in ("compute", "embedding", "data", "end-to-end"):
+        res = _run("benchmark", *over, "--mode", mode, "--steps", "4", "--warmup", "1")[-1]
+        assert res["mode"] == mode and res["value"] > 0 and res["ms_p95"] >= res["ms_p50"] > 0, res
+        if mode in ("compute", "end-to-end"):
+            assert 0 < res["mfu_dense_gemm"] < 1, res

@@ -66,3 +66,55 @@ def test_mean_per_request_needs_request_rows():
     cfg, model, tr, batch = _setup("mean_per_request_per_task", cpr=1)
     with pytest.raises(ValueError, match="row_indices"):
         tr.forward_backward(batch)
+
+
+def test_request_level_sequence_work_matches_per_candidate_sequences():
+    """Sequence work done once per request (request-level rows + row_indices) gives the
+    same loss and gradients as the same sequences copied onto every candidate row."""
+
+    m, spec = scaled_config(2, 0.0002, num_fields=8, batch=64)
+    m["runtime"].update({"device": "cpu", "precision": "fp32"})
+    m["model"].update({"token_dim": 64, "hidden_dim": 128, "task_head_hidden_dim": 32, "num_heads": 4})
+    feats = [f["name"] for f in m["features"]]
+    field = {"name": "item", "kind": "categorical", "source": "x_item", "embedding_dim": 8,
+             "encoding": {"type": "identity", "max_id": 500}}
+    age = {"name": "age", "kind": "dense", "source": "x_age", "dimension": 1}
+    m["sequences"] = [
+        {"name": "s_mean", "max_length": 12, "encoder": "mean_pool", "pool_dim": 16, "fields": [field]},
+        {"name": "s_att", "max_length": 12, "encoder": "attention_pool", "pool_dim": 16, "fields": [field],
+         "target_inputs": [feats[0]]},
+        {"name": "s_longer", "max_length": 16, "encoder": "longer", "fields": [field, age], "time_delta_field": "age",
+         "longer_dim": 32, "longer_num_heads": 1, "longer_query_tokens": 4, "longer_cls_tokens": 1,
+         "longer_candidate_global_tokens": 1, "rankmixer_summary_tokens": 2, "target_inputs": [feats[1]],
+         "longer_output": "summary"},
+    ]
+    m["tokenization"]["num_feature_tokens"] = 4
+    m["tokenization"]["feature_token_inputs"] = feats + ["s_mean", "s_att", "s_longer"]
+    cfg = app_config_from_mapping(m)
+    spec = copy.deepcopy(spec)
+    spec.sequences = {
+        "s_mean": SequenceSpec(fields={"item": FieldSpec(vocab=500)}, max_len=12, min_len=1, candidates_per_request=4),
+        "s_att": SequenceSpec(fields={"item": FieldSpec(vocab=500)}, max_len=12, min_len=1, candidates_per_request=4),
+        "s_longer": SequenceSpec(fields={"item": FieldSpec(vocab=500)}, max_len=16, min_len=1, dense_width=1,
+                                 candidates_per_request=4),
+    }
+    results = []
+    for expanded in (False, True):
+        torch.manual_seed(0)
+        model = build_model(cfg, device="cpu", base_seed=0)
+        tr = Trainer(cfg, model, device=torch.device("cpu"))
+        batch = SyntheticGenerator(model.encoder.batch_plan, spec).batch(64)
+        if expanded:  # every candidate row carries its own copy of its request's events
+            for seq in batch.sequences.values():
+                ri = seq.pop("row_indices")
+                L = seq["ids"].shape[1] // seq["lengths"].numel()
+                ids = seq["ids"].view(seq["ids"].shape[0], -1, L)
+                seq["ids"] = ids.index_select(1, ri).reshape(ids.shape[0], -1)
+                seq["lengths"] = seq["lengths"].index_select(0, ri)
+                if "dense" in seq:
+                    d = seq["dense"].view(-1, L, seq["dense"].shape[1])
+                    seq["dense"] = d.index_select(0, ri).reshape(-1, d.shape[2])
+        out = tr.forward_backward(batch)
+        results.append((float(out["loss"].detach()), tr.dense.grad.clone()))
+    assert abs(results[0][0] - results[1][0]) < 1e-5, results
+    torch.testing.assert_close(results[0][1], results[1][1], rtol=1e-4, atol=1e-6)
