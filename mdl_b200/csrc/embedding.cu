@@ -6,21 +6,24 @@
 // mean pooling of bags (src/model.py:509-678) and its Triton row-wise Adagrad
 // (src/optim.py:31-62).
 //
-// Every rank's table shards live in one fp32 slab. Peer slabs are mapped into
-// this process (CUDA IPC over NVLink), so a lookup is ONE kernel: each warp
-// hashes its ids, computes owner = (id + cyclic_offset) % W and
-// row = id / W (the reference's EmbeddingShardSpec.owner/local_row_ids, kept
-// bit-compatible for checkpoints), loads the rows straight from the owner's
-// slab with plain global loads (local HBM or NVLink peer memory), pools them
-// in registers and stores bf16 into the tokenizer GEMM's input layout. There
-// is no id exchange, no split-count host sync and no unpooled row traffic back
-// to the requester.
+// Every rank's table shards live in one fp32 slab. With one rank a lookup is ONE
+// kernel (emb_pool_fwd_kernel): each warp walks its bags, computes the table row
+// (the reference's EmbeddingShardSpec owner/local-row mapping, kept
+// bit-compatible for checkpoints), pools the rows in registers and stores bf16
+// into the tokenizer GEMM's input layout; its backward pushes each id's gradient
+// into the grad slab and marks the row in the touched-row byte flags.
 //
-// The backward pushes each id's gradient into the owner's fp32 grad slab with
-// vector reductions (red.add.v4.f32, system scope when peers are involved) and
-// marks the row in the owner's touched-row byte flags (a plain store: no
-// atomic counter, no capacity limit). After a device-side barrier the owner
-// scans its flags and applies row-wise Adagrad to exactly those rows.
+// With several ranks every random row access stays local (owner-push): random
+// peer reads over NVLink are dominated by address translation and latency.
+// emb_route_kernel groups this rank's bags into per-(bag, owner) bundles in its
+// own peer-visible staging; after a device barrier emb_owner_fwd_kernel (on each
+// owner) gathers and pools the rows of the bundles routed to it from local HBM and
+// adds one pooled fp32 vector per bundle into the requester's accumulator with
+// vector reductions over NVLink; acc_to_bf16_kernel converts the accumulator. In
+// the backward emb_owner_bwd_kernel reads each bundle's bf16 output-gradient slice
+// from the requester once and adds it into the owner's local gradient rows,
+// marking them touched. The owner then compacts its touched rows and applies
+// row-wise Adagrad to exactly those rows.
 #include "common.cuh"
 #include "embedding.h"
 

@@ -125,11 +125,13 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const LNFwdArgs p) {
 // CTAs of 8 warps. Non-mix: warps walk rows in a grid-stride loop. Mix: a CTA
 // walks whole samples (all T rows of sample b are needed to undo the token
 // permutation); the dv rows of the current sample are staged in shared memory.
-// gamma/beta gradients are accumulated per warp in registers and written as one
-// partial row per CTA.
+// gamma/beta gradients are accumulated per warp in shared memory (each lane owns
+// its columns of its warp's row, so no atomics) and written as one partial row per
+// CTA. Keeping them out of registers lets two CTAs share an SM.
 template <int NCH, bool MIX>
-__global__ void __launch_bounds__(256) ln_bwd_kernel(const LNBwdArgs p) {
-  extern __shared__ float sm[];  // [max(T, 8)][D] fp32
+__global__ void __launch_bounds__(256, NCH <= 4 ? 2 : 1) ln_bwd_kernel(const LNBwdArgs p) {
+  // MIX: [T][D] staging of the current sample's dv rows; then [8 warps][2][D] partial sums
+  extern __shared__ float sm[];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int T = p.T, D = p.D;
@@ -139,11 +141,11 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const LNBwdArgs p) {
   const auto* dyb = reinterpret_cast<const __nv_bfloat16*>(p.dy_bcast);
   auto* dx = reinterpret_cast<__nv_bfloat16*>(p.dx);
   auto* dx2 = reinterpret_cast<__nv_bfloat16*>(p.dx2);
-  float dg[NCH][8], db[NCH][8];
-#pragma unroll
-  for (int k = 0; k < NCH; ++k)
-#pragma unroll
-    for (int e = 0; e < 8; ++e) dg[k][e] = db[k][e] = 0.f;
+  float* acc = sm + (MIX ? T * D : 0);
+  float* my_dg = acc + warp * 2 * D;  // this warp's dgamma partials, then its dbeta partials
+  float* my_db = my_dg + D;
+  for (int c = lane * 4; c < 2 * D; c += 128) *reinterpret_cast<float4*>(my_dg + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+  __syncwarp();
 
   // dv of row (b, i); returns via `dv` (registers); accumulates dg/db
   auto row_dv = [&](long long b, int i, float (*dv)[8]) {
@@ -181,12 +183,16 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const LNBwdArgs p) {
     for (int k = 0; k < NCH; ++k) {
       const int c = (lane + 32 * k) * 8;
       if (c < D) {
+        float4* pg = reinterpret_cast<float4*>(my_dg + c);
+        float4* pb = reinterpret_cast<float4*>(my_db + c);
+        float4 g0 = pg[0], g1 = pg[1], b0 = pb[0], b1 = pb[1];
+        g0.x += g[k][0] * xh[k][0]; g0.y += g[k][1] * xh[k][1]; g0.z += g[k][2] * xh[k][2]; g0.w += g[k][3] * xh[k][3];
+        g1.x += g[k][4] * xh[k][4]; g1.y += g[k][5] * xh[k][5]; g1.z += g[k][6] * xh[k][6]; g1.w += g[k][7] * xh[k][7];
+        b0.x += g[k][0]; b0.y += g[k][1]; b0.z += g[k][2]; b0.w += g[k][3];
+        b1.x += g[k][4]; b1.y += g[k][5]; b1.z += g[k][6]; b1.w += g[k][7];
+        pg[0] = g0; pg[1] = g1; pb[0] = b0; pb[1] = b1;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          dv[k][e] = rstd * (gy[k][e] - s1 - xh[k][e] * s2);
-          dg[k][e] += g[k][e] * xh[k][e];
-          db[k][e] += g[k][e];
-        }
+        for (int e = 0; e < 8; ++e) dv[k][e] = rstd * (gy[k][e] - s1 - xh[k][e] * s2);
       }
     }
   };
@@ -245,23 +251,14 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const LNBwdArgs p) {
       }
     }
   }
-  // ---- fold per-warp gamma/beta partials into this CTA's row of `partials`
+  // ---- fold the 8 warps' gamma/beta partials into this CTA's row of `partials`
   float* prow = p.partials + static_cast<long long>(blockIdx.x) * 2 * D;
-  for (int pass = 0; pass < 2; ++pass) {
-    __syncthreads();
+  __syncthreads();
+  for (int c = threadIdx.x; c < 2 * D; c += blockDim.x) {
+    float t = 0.f;
 #pragma unroll
-    for (int k = 0; k < NCH; ++k) {
-      const int c = (lane + 32 * k) * 8;
-      if (c < D)
-#pragma unroll
-        for (int e = 0; e < 8; ++e) sm[warp * D + c + e] = pass == 0 ? dg[k][e] : db[k][e];
-    }
-    __syncthreads();
-    for (int c = threadIdx.x; c < D; c += blockDim.x) {
-      float s = 0.f;
-      for (int w = 0; w < 8; ++w) s += sm[w * D + c];
-      prow[pass * D + c] = s;
-    }
+    for (int w = 0; w < 8; ++w) t += acc[w * 2 * D + c];
+    prow[c] = t;
   }
 }
 
@@ -507,14 +504,16 @@ int layernorm_bwd_grid(int B) {
   return B < cap ? (B > 0 ? B : 1) : cap;
 }
 
-size_t layernorm_bwd_smem(int T, int D) { return static_cast<size_t>(T > 8 ? T : 8) * D * sizeof(float); }
+size_t layernorm_bwd_smem(int T, int D, int mix) {
+  return static_cast<size_t>((mix ? T : 0) + 16) * D * sizeof(float);  // [T][D] staging + [8][2][D] partials
+}
 
 cudaError_t layernorm_bwd(const LNBwdArgs& a, cudaStream_t stream) {
   if (a.D % 8 || a.T <= 0) return cudaErrorInvalidValue;
   if (a.mix && ((a.D % a.T) || ((a.D / a.T) % 8))) return cudaErrorInvalidValue;
   if (a.B == 0) return cudaSuccess;
   const int grid = a.grid > 0 ? a.grid : layernorm_bwd_grid(a.B);
-  const size_t smem = layernorm_bwd_smem(a.T, a.D);
+  const size_t smem = layernorm_bwd_smem(a.T, a.D, a.mix);
 #define LNB(N)                                                                                         \
   {                                                                                                    \
     auto k = a.mix ? ln_bwd_kernel<N, true> : ln_bwd_kernel<N, false>;                                 \
@@ -618,11 +617,11 @@ extern "C" int mdl_layernorm_bwd_noalloc(const void* dy, const void* dy_bcast, f
   cudaError_t e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&smem_max, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   if (e != cudaSuccess) return static_cast<int>(e);
-  if (mdl::layernorm_bwd_smem(T, D) > static_cast<size_t>(smem_max)) {
+  if (mdl::layernorm_bwd_smem(T, D, mix) > static_cast<size_t>(smem_max)) {
     char msg[200];
     std::snprintf(msg, sizeof(msg),
-                  "mdl_layernorm_bwd_noalloc: max(T, 8) * D * 4 = %zu bytes of shared memory exceeds the device's %d",
-                  mdl::layernorm_bwd_smem(T, D), smem_max);
+                  "mdl_layernorm_bwd_noalloc: ((mix ? T : 0) + 16) * D * 4 = %zu bytes of shared memory exceeds the "
+                  "device's %d", mdl::layernorm_bwd_smem(T, D, mix), smem_max);
     return noalloc_reject(msg);
   }
   float* scratch = nullptr;

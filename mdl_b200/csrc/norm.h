@@ -47,8 +47,9 @@ struct LNBwdArgs {
   int grid = 0;  // number of CTAs (partials rows); 0 = choose
 };
 int layernorm_bwd_grid(int B);
-// Dynamic shared memory of one backward CTA: max(T, 8) * D fp32.
-size_t layernorm_bwd_smem(int T, int D);
+// Dynamic shared memory of one backward CTA: the [T][D] dv staging of token mixing
+// (mix only) plus the [8 warps][2][D] gamma/beta partial sums, fp32.
+size_t layernorm_bwd_smem(int T, int D, int mix);
 cudaError_t layernorm_bwd(const LNBwdArgs& a, cudaStream_t stream);
 
 // RMSNorm over rows of width D (fp32 statistics, reference src/model.py:4550-4568):

@@ -18,10 +18,12 @@
 //     (2 MiB) per GPU, held by every GPU that loads the library until the
 //     process exits. The number of CTAs is capped so that their partial sums
 //     fit; D must be a multiple of 8 and at most 2048 (the same limits as the
-//     regular path), and one CTA stages max(T, 8) * D fp32 values in shared
-//     memory, which must fit the device's per-block opt-in limit (227 KB on
-//     B200: T * D <= 58,112 for T >= 8, e.g. T = 28 at D = 2048). Anything
-//     else is rejected with an error message.
+//     regular path), and one CTA keeps ((mix ? T : 0) + 16) * D fp32 values in
+//     shared memory (the token-mixing staging and the per-warp gamma/beta
+//     partial sums), which must fit the device's per-block opt-in limit
+//     (227 KB on B200: D <= 3,632 without mixing; (T + 16) * D <= 58,112 with
+//     it, e.g. T = 16 at D = 1,816). Anything else is rejected with an error
+//     message.
 //   * The first call on a device looks up the device address of the array
 //     (cudaGetSymbolAddress, with that device current) and caches it; make that
 //     first call before any stream capture on that device.

@@ -212,12 +212,16 @@ class FeatureEncoder:
                 else:
                     features.append(make(name, col))
                 col += w
+            width = col
             if slice_tokens:
-                # per-token slices of the RankMixer tokenizer, padded to a multiple of 8 columns (16 bytes)
+                # per-token slices of the RankMixer tokenizer: the inputs padded to slice_tokens x
+                # slice_k logical columns (reference RankMixerSliceTokenizer), each slice padded
+                # to a multiple of 8 columns (16-byte rows for TMA)
                 slice_k = (col + slice_tokens - 1) // slice_tokens
                 slice_stride = (slice_k + 7) // 8 * 8
-            self.plan = LookupPlan(features, out_width=col, slice_k=slice_k, slice_stride=slice_stride,
-                                   dense_width=dense_total, zero_fill=bool(spans))
+                width = slice_k * slice_tokens
+            self.plan = LookupPlan(features, out_width=width, slice_k=slice_k, slice_stride=slice_stride,
+                                   dense_width=dense_total, zero_fill=bool(spans), written_width=col)
             self.summary_cols["plan"] = [
                 (n, torch.tensor([self.plan.phys_col(c) for c in range(c0, c0 + w)], dtype=torch.long))
                 for n, c0, w in spans]

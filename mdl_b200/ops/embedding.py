@@ -2,11 +2,15 @@
 
 ``EmbeddingStore`` keeps the local shard of every table of a model in one fp32
 *slab* per rank (plus the fp32 gradient slab, the row-wise Adagrad
-accumulator and one touched-row byte flag per local row). On CUDA
-with ``world > 1`` those buffers are exported over CUDA IPC and every rank maps
-its peers' buffers, so the lookup kernel loads rows straight from the owner's
-HBM over NVLink and the backward kernel reduces gradients straight into the
-owner's gradient slab (``csrc/embedding.cu``).
+accumulator and one touched-row byte flag per local row). With one rank the
+lookup is one kernel that gathers, pools and writes the tokenizer input. With
+``world > 1`` (CUDA) every random row access stays on the owner's own HBM
+(owner-push, ``csrc/embedding.cu``): each rank routes its bags into per-(bag, owner)
+bundles in peer-visible staging; after a device barrier every owner gathers and
+pools the rows of the bundles routed to it and adds one pooled vector per bundle
+into the requester's fp32 accumulator over NVLink; in the backward every owner
+reads each bundle's bf16 output-gradient slice from its requester once and adds it
+into its own gradient rows, marking them for the row-wise Adagrad update.
 
 ``LookupPlan`` describes one batched lookup: which features, their tables,
 pooling and where each pooled result lands in the output matrix (including the
@@ -424,6 +428,7 @@ class LookupPlan:
     slice_stride: int = 0
     dense_width: int = 0
     zero_fill: bool = False      # output has columns no feature writes (must read as zero)
+    written_width: int = 0       # logical columns the features write (0: all of out_width)
     _meta: dict = field(default_factory=dict)
 
     @property
@@ -449,6 +454,26 @@ class LookupPlan:
         """Batch features (CSR blocks) the plan reads."""
 
         return max((self.src_of(i) for i, f in enumerate(self.features) if f.table is not None), default=-1) + 1
+
+    def zero_unwritten(self, out: torch.Tensor) -> None:
+        """Zero the output columns no feature writes (they must read as zero): only the
+        per-token slice padding (a few columns per slice, strided) when that is all,
+        else the whole matrix (``zero_fill``: reserved summary columns, group padding)."""
+
+        if self.zero_fill:
+            out.zero_()
+            return
+        if not self.slice_k or (self.out_ld == self.out_width and not self.written_width):
+            return
+        T, K, P = self.out_ld // self.slice_stride, self.slice_k, self.slice_stride
+        o3 = out.view(out.shape[0], T, P)
+        if P > K:
+            o3[:, :, K:].zero_()
+        w = self.written_width or self.out_width
+        for t in range(w // K, T):  # logical columns past the written ones
+            start = max(w - t * K, 0)
+            if start < K:
+                o3[:, t, start:K].zero_()
 
     def phys_col(self, c: int) -> int:
         return (c // self.slice_k) * self.slice_stride + c % self.slice_k if self.slice_k else c
@@ -702,8 +727,7 @@ class _FusedLookup(torch.autograd.Function):
         if ids.is_cuda:
             meta, chunks, max_vec = plan.device_meta(store, rows)
             out = torch.empty(rows, plan.out_ld, dtype=torch.bfloat16, device=ids.device)
-            if plan.zero_fill or (plan.slice_k and plan.out_ld != plan.out_width):
-                out.zero_()  # padding columns of the per-token slices must read as zero
+            plan.zero_unwritten(out)
             ext().emb_forward(meta, store.peer_ptrs("slab"), store.rank, ids, offsets, dense,
                               plan.dense_width, out, chunks, error_word(ids.device), max_vec)
             return out

@@ -131,8 +131,9 @@ def test_noalloc_rejects_sizes_beyond_its_limits():
                                        None, None, 4, 1, 4096, 0, None)
     assert rc == -1
     assert b"2048" in lib.mdl_noalloc_last_error()
-    # 32 tokens of 2048 columns need 256 KB of shared memory per CTA, above the device limit
+    # token mixing of 32 tokens x 2048 columns needs (32 + 16) * 2048 * 4 = 384 KB of shared
+    # memory per CTA, above the device limit
     rc = lib.mdl_layernorm_bwd_noalloc(_ptr(x), None, 1.0, _ptr(x), None, _ptr(x), _ptr(x), None, _ptr(x), None,
-                                       None, None, 4, 32, 2048, 0, None)
+                                       None, None, 4, 32, 2048, 1, None)
     assert rc == -1
     assert b"shared memory" in lib.mdl_noalloc_last_error()
