@@ -837,6 +837,8 @@ void fmha_bwd(const at::Tensor& qkv, const at::Tensor& kstart, const at::Tensor&
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "mdl_b200 native sm_100a kernels";
+  m.def("gemm_pair_mode", &mdl::gemm_pair_mode, "set the CTA-pair GEMM mode (-1 auto, 0 off, 1 on); returns the previous",
+        py::arg("mode"));
   m.def("gemm", &gemm, "tcgen05 batched GEMM with fused epilogue", py::arg("A"), py::arg("lda"), py::arg("gsA"),
         py::arg("a_mn"), py::arg("B"), py::arg("ldb"), py::arg("gsB"), py::arg("b_mn"), py::arg("M"), py::arg("N"),
         py::arg("K"), py::arg("G"), py::arg("out"), py::arg("ldc"), py::arg("gsC"), py::arg("out2") = py::none(),

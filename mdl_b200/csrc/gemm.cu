@@ -23,6 +23,8 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -39,12 +41,10 @@ void bind_context_once() {
   }
 }
 
-constexpr int BM = 128;
+constexpr int BM = 128;  // accumulator rows per CTA (TMEM lanes)
 constexpr int BN = 256;
 constexpr int BK = 64;   // 64 bf16 = 128 bytes = one swizzle row
-constexpr int STAGES = 3;
 constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KB
-constexpr int B_STAGE_BYTES = BN * BK * 2;  // 32 KB
 constexpr int TMEM_COLS = 2 * BN;           // double-buffered accumulator
 constexpr int NUM_EPI_WARPS = 16;                // four warps per TMEM lane quarter
 constexpr int NUM_THREADS = 64 + NUM_EPI_WARPS * 32;
@@ -52,9 +52,21 @@ constexpr int MN_CHUNK_BYTES = BK * 128;    // one 64-wide MN chunk of BK rows (
 constexpr int EPI_PITCH = 36;               // floats per staged row (32 + 4 pad)
 constexpr int EPI_WARP_FLOATS = 32 * EPI_PITCH;
 constexpr int EPI_BYTES = NUM_EPI_WARPS * EPI_WARP_FLOATS * 4;  // 72 KB
-constexpr int SMEM_BYTES =
-    1024 + STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + EPI_BYTES + (2 * STAGES + 4) * 8 + 16;
-static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+
+// Single CTA: a 128 x 256 tile per CTA, all of B's 256 rows staged per k-block.
+// CTA pair (cta_group::2, cluster of two): a 256 x 256 tile per pair; each CTA stages
+// 128 rows of A and 128 rows of B per k-block (32 KB instead of 48 KB per 128 x 256 of
+// output), which leaves room for a fourth pipeline stage.
+template <bool PAIR>
+struct Cfg {
+  static constexpr int TILE_M = PAIR ? 2 * BM : BM;
+  static constexpr int B_ROWS = PAIR ? BN / 2 : BN;
+  static constexpr int B_STAGE_BYTES = B_ROWS * BK * 2;
+  static constexpr int STAGES = PAIR ? 4 : 3;
+  static constexpr int SMEM_BYTES =
+      1024 + STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + EPI_BYTES + (2 * STAGES + 4) * 8 + 16;
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+};
 
 struct EpiParams {
   void* out;
@@ -89,10 +101,15 @@ constexpr int EPI_AUX = 2;       // bf16 out scaled by GELU'(aux), ReLU'(aux) or
 constexpr int EPI_ACC_BF16 = 3;  // bf16 out += result
 constexpr int EPI_F32 = 4;       // fp32 out (= or +=)
 
-template <bool A_MN, bool B_MN, int EPI>
+template <bool A_MN, bool B_MN, int EPI, bool PAIR>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB, const EpiParams ep) {
+  using C = Cfg<PAIR>;
+  constexpr int STAGES = C::STAGES;
+  constexpr int B_STAGE_BYTES = C::B_STAGE_BYTES;
+  constexpr int TILE_M = C::TILE_M;
+  constexpr int B_ROWS = C::B_ROWS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -109,7 +126,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int m_tiles = (ep.M + BM - 1) / BM;
+  // pair rank (0 = leader: issues the MMAs, owns the full / tempty barriers); units are
+  // distributed over pairs
+  const uint32_t cr = PAIR ? cluster_ctarank() : 0u;
+  const int unit0 = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int unit_step = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  const int m_tiles = (ep.M + TILE_M - 1) / TILE_M;
   const int n_tiles = (ep.N + BN - 1) / BN;
   const int tiles_per_group = m_tiles * n_tiles;
   const int num_tiles = tiles_per_group * ep.G;
@@ -125,19 +147,31 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], NUM_EPI_WARPS);
+      mbar_init(&tempty[a], PAIR ? 2 * NUM_EPI_WARPS : NUM_EPI_WARPS);
     }
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) {
+    cluster_sync();  // both CTAs' barriers initialised before any cross-CTA signal
+  } else {
+    __syncthreads();
+  }
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // the leader's full / tempty barriers as cluster addresses (TMA completion, epilogue release)
+  const uint32_t full_lead = PAIR ? mapa_shared(smem_u32(full), 0) : smem_u32(full);
+  const uint32_t tempty_lead = PAIR ? mapa_shared(smem_u32(tempty), 0) : smem_u32(tempty);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -147,7 +181,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t phase = 0;
       int issued = 0;  // stages filled but possibly not yet consumed
       bool ok = true;
-      for (int unit = blockIdx.x; unit < num_units && ok; unit += gridDim.x) {
+      for (int unit = unit0; unit < num_units && ok; unit += unit_step) {
         const int tile = unit / ep.splits;
         const int kb0 = (unit - tile * ep.splits) * ep.kb_per_split;
         const int kb1 = min(k_blocks, kb0 + ep.kb_per_split);
@@ -155,12 +189,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int rem = tile - g * tiles_per_group;
         const int mb = rem / n_tiles;
         const int nb = rem - mb * n_tiles;
+        const int a_row0 = mb * TILE_M + static_cast<int>(cr) * BM;     // this CTA's A rows
+        const int b_row0 = nb * BN + static_cast<int>(cr) * B_ROWS;     // this CTA's B rows
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, ep.err, abort_flag)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], A_STAGE_BYTES + B_STAGE_BYTES);
+          // the leader expects the bytes of both CTAs' copies on its own barrier
+          if (cr == 0) mbar_arrive_expect_tx(&full[stage], (PAIR ? 2 : 1) * (A_STAGE_BYTES + B_STAGE_BYTES));
           // third map coordinate: the batch group, or the K range when KG > 1
           const int kr = ep.KG > 1 ? kb / kb_per_range : 0;
           const int k0 = (kb - kr * kb_per_range) * BK;
@@ -168,19 +205,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const int zb = ep.KG > 1 ? kr : (ep.b_shared ? 0 : g);
           uint8_t* a_dst = sA + stage * A_STAGE_BYTES;
           uint8_t* b_dst = sB + stage * B_STAGE_BYTES;
+          const uint32_t fb = full_lead + static_cast<uint32_t>(stage) * 8u;
+          auto load = [&](uint8_t* dst, const CUtensorMap* map, int c0, int c1, int c2) {
+            if constexpr (PAIR) {
+              tma_load_3d_pair(dst, map, fb, c0, c1, c2);
+            } else {
+              tma_load_3d(dst, map, &full[stage], c0, c1, c2);
+            }
+          };
           if (!A_MN) {
-            tma_load_3d(a_dst, &tmA, &full[stage], k0, mb * BM, za);
+            load(a_dst, &tmA, k0, a_row0, za);
           } else {
 #pragma unroll
-            for (int c = 0; c < BM / 64; ++c)
-              tma_load_3d(a_dst + c * MN_CHUNK_BYTES, &tmA, &full[stage], mb * BM + c * 64, k0, za);
+            for (int c = 0; c < BM / 64; ++c) load(a_dst + c * MN_CHUNK_BYTES, &tmA, a_row0 + c * 64, k0, za);
           }
           if (!B_MN) {
-            tma_load_3d(b_dst, &tmB, &full[stage], k0, nb * BN, zb);
+            load(b_dst, &tmB, k0, b_row0, zb);
           } else {
 #pragma unroll
-            for (int c = 0; c < BN / 64; ++c)
-              tma_load_3d(b_dst + c * MN_CHUNK_BYTES, &tmB, &full[stage], nb * BN + c * 64, k0, zb);
+            for (int c = 0; c < B_ROWS / 64; ++c) load(b_dst + c * MN_CHUNK_BYTES, &tmB, b_row0 + c * 64, k0, zb);
           }
           ++issued;
           if (++stage == STAGES) {
@@ -190,18 +233,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
       if (!ok) {
-        // Drain copies still in flight into this CTA's smem before exiting.
-        int s = stage, p = phase;
-        for (int i = 0; i < STAGES && i < issued; ++i) {
-          s = (s + STAGES - 1) % STAGES;
-          if (s == STAGES - 1) p ^= 1;
-          mbar_wait(&full[s], p, nullptr, nullptr);
+        // Drain copies still in flight into this CTA's smem before exiting (their bytes
+        // count on the leader's barriers, so a pair member waits a fixed 2 ms instead).
+        if (PAIR && cr != 0) {
+          const uint64_t t0 = globaltimer_ns();
+          while (globaltimer_ns() - t0 < 2000000ull) {
+          }
+        } else {
+          int s = stage, p = phase;
+          for (int i = 0; i < STAGES && i < issued; ++i) {
+            s = (s + STAGES - 1) % STAGES;
+            if (s == STAGES - 1) p ^= 1;
+            mbar_wait(&full[s], p, nullptr, nullptr);
+          }
         }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_bf16(BM, BN, A_MN, B_MN);
+    if (lane == 0 && cr == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(TILE_M, BN, A_MN, B_MN);
       const uint32_t a_base = smem_u32(sA);
       const uint32_t b_base = smem_u32(sB);
       int stage = 0;
@@ -209,7 +259,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int unit = blockIdx.x; unit < num_units && ok; unit += gridDim.x) {
+      for (int unit = unit0; unit < num_units && ok; unit += unit_step) {
         const int tile = unit / ep.splits;
         const int kb0 = (unit - tile * ep.splits) * ep.kb_per_split;
         const int kb1 = min(k_blocks, kb0 + ep.kb_per_split);
@@ -232,16 +282,28 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                                         : make_smem_desc(a_stage + kk * 32, 16, 1024);
             const uint64_t bdesc = B_MN ? make_smem_desc(b_stage + kk * 2048, MN_CHUNK_BYTES, 1024)
                                         : make_smem_desc(b_stage + kk * 32, 16, 1024);
-            tc_mma_bf16(d_tmem, adesc, bdesc, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
+            if constexpr (PAIR) {
+              tc_mma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
+            } else {
+              tc_mma_bf16(d_tmem, adesc, bdesc, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
+            }
           }
-          tc_commit(&empty[stage]);
+          if constexpr (PAIR) {
+            tc_commit_pair(&empty[stage]);  // frees the stage in both CTAs
+          } else {
+            tc_commit(&empty[stage]);
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        tc_commit(&tfull[acc]);
+        if constexpr (PAIR) {
+          tc_commit_pair(&tfull[acc]);  // both CTAs' epilogues may read their halves
+        } else {
+          tc_commit(&tfull[acc]);
+        }
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1u;
       }
@@ -267,7 +329,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     const bool atomic_out = ep.splits > 1;  // K slices of one tile add into the fp32 output
-    for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x) {
+    for (int unit = unit0; unit < num_units; unit += unit_step) {
       const int tile = unit / ep.splits;
       // warp-uniform outcome: the tcgen05.ld below must be executed by the whole warp
       if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, ep.err, abort_flag))) break;
@@ -276,7 +338,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int rem = tile - g * tiles_per_group;
       const int mb = rem / n_tiles;
       const int nb = rem - mb * n_tiles;
-      const int row0 = mb * BM + quarter * 32;  // first row of this warp's 32-row slab
+      const int row0 = mb * TILE_M + static_cast<int>(cr) * BM + quarter * 32;  // this warp's 32-row slab
       for (int c0 = cgroup * (BN / 4); c0 < (cgroup + 1) * (BN / 4); c0 += 32) {
         const int col0 = nb * BN + c0;
         if (col0 >= ep.N) break;  // warp-uniform
@@ -479,15 +541,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (lane == 0) {
+        if constexpr (PAIR) {
+          mbar_arrive_cluster(tempty_lead + static_cast<uint32_t>(acc) * 8u);  // the leader's barrier
+        } else {
+          mbar_arrive(&tempty[acc]);
+        }
+      }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
   }
-  __syncthreads();
+  if constexpr (PAIR) {
+    tc_fence_before();
+    cluster_sync();  // no CTA leaves while its partner still reads its smem or signals its barriers
+  } else {
+    __syncthreads();
+  }
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    if constexpr (PAIR) {
+      tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    } else {
+      tmem_dealloc(tmem_base, TMEM_COLS);
+    }
   }
 }
 
@@ -535,30 +612,92 @@ int num_sms() {
   return n;
 }
 
-template <bool A_MN, bool B_MN, int EPI>
+template <bool A_MN, bool B_MN, int EPI, bool PAIR>
 cudaError_t launch_kind(const CUtensorMap& ta, const CUtensorMap& tb, const EpiParams& ep, int grid,
                         cudaStream_t stream) {
-  auto kern = gemm_tcgen05_kernel<A_MN, B_MN, EPI>;
+  auto kern = gemm_tcgen05_kernel<A_MN, B_MN, EPI, PAIR>;
+  constexpr int smem = Cfg<PAIR>::SMEM_BYTES;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  kern<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ta, tb, ep);
-  return cudaGetLastError();
+  if constexpr (PAIR) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+    cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    // A persistent grid must be co-resident: clusters beyond what the GPCs can hold at
+    // once would only start after the others finish.
+    static int max_clusters = 0;
+    if (max_clusters == 0) {
+      cfg.gridDim = dim3(static_cast<unsigned>(2 * (num_sms() / 2)), 1, 1);
+      int n = 0;
+      cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+      if (e != cudaSuccess || n <= 0) return e != cudaSuccess ? e : cudaErrorInvalidConfiguration;
+      max_clusters = n;
+    }
+    if (grid > 2 * max_clusters) grid = 2 * max_clusters;
+    cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+    return cudaLaunchKernelEx(&cfg, kern, ta, tb, ep);
+  } else {
+    kern<<<grid, NUM_THREADS, smem, stream>>>(ta, tb, ep);
+    return cudaGetLastError();
+  }
 }
 
-template <bool A_MN, bool B_MN>
+template <bool A_MN, bool B_MN, bool PAIR>
 cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const EpiParams& ep, int epi, int grid,
                    cudaStream_t stream) {
   switch (epi) {
-    case EPI_PLAIN: return launch_kind<A_MN, B_MN, EPI_PLAIN>(ta, tb, ep, grid, stream);
-    case EPI_GELU: return launch_kind<A_MN, B_MN, EPI_GELU>(ta, tb, ep, grid, stream);
-    case EPI_AUX: return launch_kind<A_MN, B_MN, EPI_AUX>(ta, tb, ep, grid, stream);
-    case EPI_ACC_BF16: return launch_kind<A_MN, B_MN, EPI_ACC_BF16>(ta, tb, ep, grid, stream);
-    default: return launch_kind<A_MN, B_MN, EPI_F32>(ta, tb, ep, grid, stream);
+    case EPI_PLAIN: return launch_kind<A_MN, B_MN, EPI_PLAIN, PAIR>(ta, tb, ep, grid, stream);
+    case EPI_GELU: return launch_kind<A_MN, B_MN, EPI_GELU, PAIR>(ta, tb, ep, grid, stream);
+    case EPI_AUX: return launch_kind<A_MN, B_MN, EPI_AUX, PAIR>(ta, tb, ep, grid, stream);
+    case EPI_ACC_BF16: return launch_kind<A_MN, B_MN, EPI_ACC_BF16, PAIR>(ta, tb, ep, grid, stream);
+    default: return launch_kind<A_MN, B_MN, EPI_F32, PAIR>(ta, tb, ep, grid, stream);
   }
+}
+
+template <bool PAIR>
+cudaError_t launch_any(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const EpiParams& ep,
+                       int epi, int grid, cudaStream_t stream) {
+  if (a_mn) {
+    return b_mn ? launch<true, true, PAIR>(ta, tb, ep, epi, grid, stream)
+                : launch<true, false, PAIR>(ta, tb, ep, epi, grid, stream);
+  }
+  return b_mn ? launch<false, true, PAIR>(ta, tb, ep, epi, grid, stream)
+              : launch<false, false, PAIR>(ta, tb, ep, epi, grid, stream);
+}
+
+// CTA pairs for GEMMs with enough 256 x 256 tiles to fill the GPU (MDL_B200_GEMM_PAIR=0
+// turns them off, =1 forces them where the shape allows; gemm_pair_mode() overrides).
+std::atomic<int> g_pair_mode{-2};  // -2: not read from the environment yet
+
+int pair_mode() {
+  int m = g_pair_mode.load();
+  if (m == -2) {
+    const char* e = std::getenv("MDL_B200_GEMM_PAIR");
+    int want = e == nullptr ? -1 : std::atoi(e);
+    g_pair_mode.compare_exchange_strong(m, want);
+    m = g_pair_mode.load();
+  }
+  return m;
+}
+
+bool use_pair(long long pair_tiles, int splits) {
+  const int mode = pair_mode();
+  if (mode == 0 || splits > 1) return false;
+  if (mode == 1) return true;
+  return pair_tiles >= num_sms();  // at least two waves of pairs
 }
 
 // Epilogue kind of a call; -1 for a combination no kernel implements.
@@ -574,6 +713,12 @@ int epilogue_kind(const GemmArgs& a) {
 }
 
 }  // namespace
+
+int gemm_pair_mode(int mode) {
+  const int prev = pair_mode();
+  if (mode >= -1 && mode <= 1) g_pair_mode.store(mode);
+  return prev;
+}
 
 cudaError_t gemm_bf16_tcgen05(const GemmArgs& a, cudaStream_t stream) {
   if (a.M <= 0 || a.N <= 0 || a.K <= 0 || a.G <= 0 || a.KG <= 0) return cudaSuccess;
@@ -592,6 +737,8 @@ cudaError_t gemm_bf16_tcgen05(const GemmArgs& a, cudaStream_t stream) {
     return cudaErrorInvalidValue;
   const int epi = epilogue_kind(a);
   if (epi < 0) return cudaErrorInvalidValue;
+  const long long pair_tiles =
+      static_cast<long long>((a.M + 2 * BM - 1) / (2 * BM)) * ((a.N + BN - 1) / BN) * static_cast<long long>(a.G);
   CUtensorMap ta, tb;
   bool ok;
   // third map dimension: K ranges (KG > 1), batch groups, or 1 for a shared operand
@@ -605,11 +752,6 @@ cudaError_t gemm_bf16_tcgen05(const GemmArgs& a, cudaStream_t stream) {
     ok = encode_map(&ta, a.A, a.K, a.M, za, a.lda, sa, BM);
   else
     ok = encode_map(&ta, a.A, a.M, a.K, za, a.lda, sa, BK);
-  if (!ok) return cudaErrorInvalidValue;
-  if (!a.b_mn_major)
-    ok = encode_map(&tb, a.B, a.K, a.N, zb, a.ldb, sb, BN);
-  else
-    ok = encode_map(&tb, a.B, a.N, a.K, zb, a.ldb, sb, BK);
   if (!ok) return cudaErrorInvalidValue;
 
   EpiParams ep;
@@ -636,7 +778,7 @@ cudaError_t gemm_bf16_tcgen05(const GemmArgs& a, cudaStream_t stream) {
   ep.a_shared = a_shared ? 1 : 0;
   ep.b_shared = b_shared ? 1 : 0;
   ep.err = a.err;
-  const long long tiles =
+  long long tiles =
       static_cast<long long>((a.M + BM - 1) / BM) * ((a.N + BN - 1) / BN) * static_cast<long long>(a.G);
   // Split K across CTAs when the output has too few tiles to fill the GPU (weight
   // gradients: a few output tiles over a K of many thousand rows). Only for an fp32
@@ -652,16 +794,25 @@ cudaError_t gemm_bf16_tcgen05(const GemmArgs& a, cudaStream_t stream) {
       ep.splits = (total_kb + ep.kb_per_split - 1) / ep.kb_per_split;
     }
   }
+  const bool pair = use_pair(pair_tiles, ep.splits) && a.max_ctas <= 0;
+  // B operand map: each CTA of a pair stages half of the tile's 256 B rows
+  const uint32_t b_box = pair ? BN / 2 : BN;
+  if (!a.b_mn_major)
+    ok = encode_map(&tb, a.B, a.K, a.N, zb, a.ldb, sb, b_box);
+  else
+    ok = encode_map(&tb, a.B, a.N, a.K, zb, a.ldb, sb, BK);
+  if (!ok) return cudaErrorInvalidValue;
+  if (pair) {
+    tiles = pair_tiles;
+    int clusters = num_sms() / 2;
+    if (tiles < clusters) clusters = static_cast<int>(tiles);
+    return launch_any<true>(a.a_mn_major, a.b_mn_major, ta, tb, ep, epi, 2 * clusters, stream);
+  }
   const long long units = tiles * ep.splits;
   int grid = num_sms();
   if (a.max_ctas > 0 && a.max_ctas < grid) grid = a.max_ctas;
   if (units < grid) grid = static_cast<int>(units);
-  if (a.a_mn_major) {
-    return a.b_mn_major ? launch<true, true>(ta, tb, ep, epi, grid, stream)
-                        : launch<true, false>(ta, tb, ep, epi, grid, stream);
-  }
-  return a.b_mn_major ? launch<false, true>(ta, tb, ep, epi, grid, stream)
-                      : launch<false, false>(ta, tb, ep, epi, grid, stream);
+  return launch_any<false>(a.a_mn_major, a.b_mn_major, ta, tb, ep, epi, grid, stream);
 }
 
 }  // namespace mdl

@@ -64,4 +64,8 @@ struct GemmArgs {
 // Returns cudaSuccess or the launch/encode error.
 cudaError_t gemm_bf16_tcgen05(const GemmArgs& args, cudaStream_t stream);
 
+// CTA-pair (cta_group::2) tiles: -1 = by shape, 0 = off, 1 = wherever the shape allows.
+// Returns the previous mode.
+int gemm_pair_mode(int mode);
+
 }  // namespace mdl

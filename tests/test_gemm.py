@@ -6,6 +6,18 @@ import torch
 from mdl_b200.ops import gemm as G
 
 
+@pytest.fixture(params=["auto", "single", "pair"])
+def pair_mode(request):
+    """Runs a GPU test with the GEMM's CTA-pair tiles chosen by shape, off, and forced on."""
+
+    from mdl_b200.ops._ext import ext
+
+    mode = {"auto": -1, "single": 0, "pair": 1}[request.param]
+    prev = ext().gemm_pair_mode(mode)
+    yield request.param
+    ext().gemm_pair_mode(prev)
+
+
 def _ref(a, b, M, N, K, Gn, lda, gsA, a_mn, ldb, gsB, b_mn):
     av = G._view(a, Gn, M, K, gsA, lda, a_mn).float()
     bv = G._view(b, Gn, N, K, gsB, ldb, b_mn).float()
@@ -46,7 +58,7 @@ def test_gemm_cpu_reference_matches_bmm(a_mn, b_mn, shape):
 @pytest.mark.parametrize("a_mn", [False, True])
 @pytest.mark.parametrize("b_mn", [False, True])
 @pytest.mark.parametrize("shape", [(128, 256, 64, 1), (256, 512, 192, 3), (200, 296, 136, 2), (1024, 768, 1024, 4)])
-def test_gemm_tcgen05_layouts(a_mn, b_mn, shape):
+def test_gemm_tcgen05_layouts(a_mn, b_mn, shape, pair_mode):
     M, N, K, Gn = shape
     a, lda, gsA, b, ldb, gsB = _operands(M, N, K, Gn, a_mn, b_mn, "cuda")
     out = torch.empty(Gn, M, N, device="cuda", dtype=torch.float32)
@@ -60,7 +72,7 @@ def test_gemm_tcgen05_layouts(a_mn, b_mn, shape):
 @pytest.mark.gpu
 @pytest.mark.parametrize("act", [G.ACT_NONE, G.ACT_GELU, G.ACT_DGELU, G.ACT_RELU, G.ACT_DRELU, G.ACT_GELU_GRAD,
                                  G.ACT_DMUL])
-def test_gemm_tcgen05_epilogues(act):
+def test_gemm_tcgen05_epilogues(act, pair_mode):
     M, N, K, Gn = 384, 512, 256, 2
     a, lda, gsA, b, ldb, gsB = _operands(M, N, K, Gn, False, True, "cuda")
     bias = torch.randn(Gn, N, device="cuda")
@@ -85,7 +97,7 @@ def test_gemm_tcgen05_epilogues(act):
 
 
 @pytest.mark.gpu
-def test_gemm_tcgen05_accumulate_fp32():
+def test_gemm_tcgen05_accumulate_fp32(pair_mode):
     M, N, K = 256, 256, 128
     a, lda, gsA, b, ldb, gsB = _operands(M, N, K, 1, True, True, "cuda")
     out = torch.ones(M, N, device="cuda")
@@ -129,7 +141,7 @@ def test_gemm_shared_operand_and_k_ranges_cpu():
 
 
 @pytest.mark.gpu
-def test_gemm_shared_operand_and_k_ranges_tcgen05():
+def test_gemm_shared_operand_and_k_ranges_tcgen05(pair_mode):
     out, ref, gw, gref, add, add_ref, K, s = _shared_and_krange("cuda")
     torch.cuda.synchronize()
     torch.testing.assert_close(out, ref, atol=2e-3 * K ** 0.5, rtol=1e-3)
