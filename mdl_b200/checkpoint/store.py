@@ -134,6 +134,34 @@ class CheckpointStore:
 
         self._do(put, f"write {p}")
 
+    def upload_file(self, source: str | os.PathLike[str], *parts: str, chunk_bytes: int = 64 << 20) -> int:
+        """Copy a local file to ``parts`` (atomic like ``write_bytes``) without holding it
+        in memory; returns the bytes copied."""
+
+        p = self.path(*parts)
+        tmp = p + f".tmp-{os.getpid()}"
+        if not self.remote:
+            os.makedirs(os.path.dirname(p), exist_ok=True)
+            shutil.copyfile(source, tmp)
+            with open(tmp, "rb+") as fh:
+                os.fsync(fh.fileno())
+            os.replace(tmp, p)
+            return os.path.getsize(p)
+
+        def put():
+            n = 0
+            with open(source, "rb") as inp, self._fs.open_output_stream(tmp) as out:
+                while True:
+                    block = inp.read(chunk_bytes)
+                    if not block:
+                        break
+                    out.write(block)
+                    n += len(block)
+            self._fs.move(tmp, p)
+            return n
+
+        return self._do(put, f"upload {p}")
+
     def read_bytes(self, *parts: str) -> bytes:
         p = self.path(*parts)
         if not self.remote:

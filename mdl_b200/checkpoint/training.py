@@ -158,41 +158,89 @@ def _rng_state() -> dict[str, Any]:
     return state
 
 
+def _commit_step(run: CheckpointStore, step: int, name: str, manifest: dict, keep_last: int) -> None:
+    """Rank 0, after every rank's READY marker: manifest, ``_COMMIT``, latest pointer,
+    retention."""
+
+    run.write_json(manifest, name, CHECKPOINT_MANIFEST)
+    run.write_bytes(b"", name, COMMIT_MARKER)
+    run.write_json({"step": step, "directory": name}, LATEST_POINTER)
+    if keep_last > 0:
+        prune_run_directory(run, keep_last)
+
+
 def save_training_checkpoint(config, trainer, run: CheckpointStore, step: int, *,
                              cursor: DataCursor | None = None, keep_last: int = 0,
-                             extra: dict | None = None) -> CommittedCheckpoint:
-    """Collective: every rank writes its files, rank 0 commits after all are READY."""
+                             extra: dict | None = None, uploader=None,
+                             chunk_bytes: int | None = None) -> CommittedCheckpoint:
+    """Collective: every rank writes its files, rank 0 commits after all are READY.
+
+    With an ``uploader`` (``checkpoint.uploader.CheckpointUploader``) the files go to the
+    rank's local staging directory and the uploader's thread publishes and commits them;
+    the call returns once the step is staged (the returned record is committed when the
+    uploader reports the step in ``published_steps``)."""
 
     name = step_directory_name(step)
-    run.makedirs(name)
-    save_model_checkpoint(config, trainer, run.child(name, MODEL_SUBDIR), sparse_step=trainer.step_index)
+    target = run
+    if uploader is not None:
+        target = uploader.stage_store(name)
+    else:
+        run.makedirs(name)
+    model_store = target.child(MODEL_SUBDIR) if uploader is not None else run.child(name, MODEL_SUBDIR)
+    kw = {} if chunk_bytes is None else {"chunk_bytes": int(chunk_bytes)}
+    save_model_checkpoint(config, trainer, model_store, sparse_step=trainer.step_index, **kw)
     dense_state = trainer.dense.state_dict()  # collective under the sharded update
+    parts = (name,) if uploader is None else ()
     if trainer.rank == 0:
-        run.write_torch({
+        target.write_torch({
             "format": TRAINING_FORMAT,
             "dense_optimizer": dense_state,
             "step_index": trainer.step_index,
             "micro_index": trainer.micro_index,
             "rng": _rng_state(),
             "extra": extra or {},
-        }, name, TRAIN_STATE_FILE)
+        }, *parts, TRAIN_STATE_FILE)
     cur = cursor or DataCursor(position=trainer.step_index, rank=trainer.rank, world_size=trainer.world)
-    run.write_json(asdict(cur), name, rank_progress_file(trainer.rank))
+    target.write_json(asdict(cur), *parts, rank_progress_file(trainer.rank))
+    saved_at = time.time()
+    manifest = {"format": TRAINING_FORMAT, "step": step, "world_size": trainer.world,
+                "saved_at": saved_at, "model_name": config.model.name}
+    if uploader is not None:
+        uploader.submit(step, name, manifest if trainer.rank == 0 else None)
+        return CommittedCheckpoint(step, name, run.uri(name), trainer.world, saved_at)
     run.write_bytes(b"", name, rank_ready_marker(trainer.rank))
     _barrier(trainer)
-    saved_at = time.time()
     if trainer.rank == 0:
         missing = [r for r in range(trainer.world) if not run.exists(name, rank_ready_marker(r))]
         if missing:
             raise RuntimeError(f"checkpoint {name}: ranks {missing} did not finish writing")
-        run.write_json({"format": TRAINING_FORMAT, "step": step, "world_size": trainer.world,
-                        "saved_at": saved_at, "model_name": config.model.name}, name, CHECKPOINT_MANIFEST)
-        run.write_bytes(b"", name, COMMIT_MARKER)
-        run.write_json({"step": step, "directory": name}, LATEST_POINTER)
-        if keep_last > 0:
-            prune_run_directory(run, keep_last)
+        _commit_step(run, step, name, manifest, keep_last)
     _barrier(trainer)
     return CommittedCheckpoint(step, name, run.uri(name), trainer.world, saved_at)
+
+
+def make_uploader(config, trainer, run: CheckpointStore, *, keep_last: int | None = None,
+                  local_ranks: int = 1, asynchronous: bool | None = None):
+    """The uploader a run's checkpoint settings ask for (``training.checkpoint``), after
+    the staging-space preflight; None for synchronous saves."""
+
+    from .uploader import CheckpointUploader, check_staging_space, estimate_staging_bytes
+
+    ck = config.training.checkpoint
+    use_async = ck.async_upload if asynchronous is None else asynchronous
+    if not use_async:
+        return None
+    uploader = CheckpointUploader(run, rank=trainer.rank, world=trainer.world, staging_dir=ck.staging_dir,
+                                  keep_last=ck.keep_last if keep_last is None else keep_last,
+                                  ready_timeout_sec=ck.ready_timeout_sec, commit_fn=_commit_step)
+    if ck.preflight_staging:
+        try:
+            check_staging_space(uploader.staging_root, estimate_staging_bytes(trainer, ck.shard_chunk_bytes),
+                                local_ranks=local_ranks)
+        except Exception:
+            uploader.close()
+            raise
+    return uploader
 
 
 @dataclass

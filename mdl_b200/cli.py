@@ -290,7 +290,7 @@ def cmd_train(args, argv) -> int:
         return rc
     import torch
 
-    from .checkpoint import load_training_checkpoint, open_checkpoint_store, save_training_checkpoint
+    from .checkpoint import load_training_checkpoint, make_uploader, open_checkpoint_store, save_training_checkpoint
     from .train.watchdog import StepWatchdog, abort_on_cuda_oom
 
     cfg = load_cli_config(args)
@@ -311,12 +311,23 @@ def cmd_train(args, argv) -> int:
         from .parallel.runtime import validate_shard_metadata
 
         validate_shard_metadata(model.store)
-    run = open_checkpoint_store(args.checkpoint_dir) if args.checkpoint_dir else None
+    ck = cfg.training.checkpoint
+    ck_dir = args.checkpoint_dir or (os.path.join(ck.dir, ck.run_name) if ck.dir and ck.run_name else ck.dir)
+    run = open_checkpoint_store(ck_dir) if ck_dir else None
+    save_every = args.save_every or ck.every_steps
+    keep_last = ck.keep_last if args.keep_last is None else args.keep_last
+    uploader = None
     start = 0
     if run is not None:
-        state = load_training_checkpoint(cfg, trainer, run, args.resume)
+        state = load_training_checkpoint(cfg, trainer, run, args.resume or ck.resume or "auto")
         if state is not None:
             start = state.step
+        uploader = make_uploader(cfg, trainer, run, keep_last=keep_last,
+                                 local_ranks=int(os.environ.get("LOCAL_WORLD_SIZE", "1")))
+
+    def save(step_no):
+        save_training_checkpoint(cfg, trainer, run, step_no, keep_last=keep_last, uploader=uploader,
+                                 chunk_bytes=ck.shard_chunk_bytes)
     source = _batches(cfg, model, rank, world, synthetic=args.synthetic)
     batches = iter(source)
     from .train.fixed_eval import FixedTestEval
@@ -370,15 +381,21 @@ def cmd_train(args, argv) -> int:
                 ev = fixed.run(model)
                 if rank == 0:
                     print(json.dumps({"step": step, "fixed_test_eval": ev}), flush=True)
-            if run is not None and args.save_every and step % args.save_every == 0:
-                save_training_checkpoint(cfg, trainer, run, step, keep_last=args.keep_last)
+            if run is not None and save_every and step % save_every == 0:
+                dog.beat("checkpoint", step)
+                save(step)
     finally:
         dog.stop()
         if voting:
             batches.close()
         _close(source)
     if run is not None:
-        save_training_checkpoint(cfg, trainer, run, step, keep_last=args.keep_last)
+        if ck.save_on_exit and (not save_every or step % save_every != 0):
+            save(step)
+        if uploader is not None:
+            uploader.close()  # publishes (and on rank 0 commits) every staged step first
+            for failed, why in uploader.failed_steps:
+                print(json.dumps({"rank": rank, "checkpoint_failed": failed, "error": why}), flush=True)
     if device.type == "cuda":
         torch.cuda.synchronize(device)
     if rank == 0:
@@ -524,9 +541,9 @@ def build_parser() -> argparse.ArgumentParser:
         if name == "train":
             p.add_argument("--max-steps", type=int, default=100)
             p.add_argument("--checkpoint-dir")
-            p.add_argument("--resume", default="auto")
+            p.add_argument("--resume", default=None)
             p.add_argument("--save-every", type=int, default=0)
-            p.add_argument("--keep-last", type=int, default=3)
+            p.add_argument("--keep-last", type=int, default=None)
             p.add_argument("--log-every", type=int, default=10)
             p.add_argument("--watchdog-sec", type=float, default=None)
             p.add_argument("--batch-budget-sec", type=float, default=30.0,

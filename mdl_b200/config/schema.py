@@ -508,8 +508,19 @@ class CheckpointConfig:
     run_name: str | None = None
     every_steps: int = 0
     keep_last: int = 3
+    save_on_exit: bool = True
     resume: str | None = None
+    # stage each step on local disk and publish it to the run directory from a
+    # background thread (training does not wait for the run directory)
+    async_upload: bool = True
     staging_dir: str | None = None
+    shard_chunk_bytes: int = 2 * 1024 ** 3
+    # refuse to start when the staging filesystem cannot hold this node's ranks' files
+    preflight_staging: bool = True
+    # rank 0 waits this long for every rank's READY marker before committing a step
+    ready_timeout_sec: float = 1800.0
+    data_resume: bool = True
+    data_resume_rewind: int = 1
 
 
 @_frozen
