@@ -415,8 +415,26 @@ def cmd_benchmark(args, argv) -> int:
 
     synthetic = args.mode in ("compute", "embedding")
     it = _batches(cfg, model, rank, world, synthetic=synthetic)
-    res = run_mode(args.mode, cfg, model, trainer, iter(it), rank=rank, world=world, device=device,
+    batches = iter(it)
+    res = run_mode(args.mode, cfg, model, trainer, batches, rank=rank, world=world, device=device,
                    steps=args.steps, warmup=args.warmup, min_util=args.min_util)
+    if args.profile_steps > 0 or args.comm_stats:
+        extra = next(batches)
+        dev_batch = extra.to(device) if device.type == "cuda" else extra
+        if args.comm_stats:
+            from .ops.embedding_stats import communication_stats
+
+            stats = communication_stats(model.store, model.encoder.plan, dev_batch.ids, dev_batch.offsets,
+                                        dev_batch.rows, collective=world > 1, group=model.store.process_group)
+            res["embedding_comm"] = {k: v.as_dict() for k, v in sorted(stats.items())}
+            res["embedding_comm_bytes_per_step"] = sum(v.total_communication_bytes for v in stats.values())
+        if args.profile_steps > 0:
+            from .benchmark.modes import dense_gemm_flops_per_row
+            from .benchmark.profile_summary import profile_steps
+
+            flops = dense_gemm_flops_per_row(model) * cfg.training.batch_size
+            res["profile"] = profile_steps(lambda: trainer.train_step(dev_batch), args.profile_steps,
+                                           device=device, gemm_flops_per_step=flops)
     _close(it)
     if rank == 0:
         print(json.dumps(res), flush=True)
@@ -556,6 +574,11 @@ def build_parser() -> argparse.ArgumentParser:
                                 "H2D + training; data: the input pipeline only; embedding: lookup + sparse update")
             p.add_argument("--min-util", type=float, default=None,
                            help="utilisation gate: report a failure (exit 3) below this mean GPU utilisation")
+            p.add_argument("--profile-steps", type=int, default=0,
+                           help="after the timed steps, profile this many compute steps (device time by kernel "
+                                "class, top kernels, named ranges)")
+            p.add_argument("--comm-stats", action="store_true",
+                           help="add the embedding lookup's per-table communication statistics of one batch")
         if name in ("evaluate", "predict"):
             p.add_argument("--checkpoint")
             p.add_argument("--max-batches", type=int, default=10)

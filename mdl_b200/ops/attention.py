@@ -31,6 +31,7 @@ import math
 import torch
 
 from ._ext import error_word, ext
+from ..utils.trace import trace_range
 
 LOG2E = 1.4426950408889634
 
@@ -93,9 +94,10 @@ class SuffixAttentionFn(torch.autograd.Function):
 
 def suffix_attention(qkv: torch.Tensor, kstart: torch.Tensor, heads: int, lq: int, causal: bool = True,
                      ktail: int = 0) -> torch.Tensor:
-    if qkv.is_cuda:
-        return SuffixAttentionFn.apply(qkv, kstart, heads, lq, causal, ktail)
-    return suffix_attention_reference(qkv, kstart, heads, lq, causal, ktail=ktail)
+    with trace_range("mdl.attention.suffix"):
+        if qkv.is_cuda:
+            return SuffixAttentionFn.apply(qkv, kstart, heads, lq, causal, ktail)
+        return suffix_attention_reference(qkv, kstart, heads, lq, causal, ktail=ktail)
 
 
 # ----------------------------------------------------------------------------- single-query attention
@@ -140,6 +142,7 @@ class SingleQueryAttentionFn(torch.autograd.Function):
 
 
 def single_query_attention(q: torch.Tensor, hist: torch.Tensor, kstart: torch.Tensor, scale: float) -> torch.Tensor:
-    if q.is_cuda:
-        return SingleQueryAttentionFn.apply(q, hist, kstart, scale)
-    return single_query_attention_reference(q, hist, kstart, scale)
+    with trace_range("mdl.attention.single_query"):
+        if q.is_cuda:
+            return SingleQueryAttentionFn.apply(q, hist, kstart, scale)
+        return single_query_attention_reference(q, hist, kstart, scale)

@@ -40,6 +40,7 @@ import torch
 import torch.distributed as dist
 
 from ..parallel.sharding import EmbeddingShardingPlan, EmbeddingShardSpec
+from ..utils.trace import trace_range
 from ._ext import error_word, ext
 
 POOL_NONE, POOL_MEAN, POOL_SUM = 0, 1, 2
@@ -728,8 +729,9 @@ class _FusedLookup(torch.autograd.Function):
             meta, chunks, max_vec = plan.device_meta(store, rows)
             out = torch.empty(rows, plan.out_ld, dtype=torch.bfloat16, device=ids.device)
             plan.zero_unwritten(out)
-            ext().emb_forward(meta, store.peer_ptrs("slab"), store.rank, ids, offsets, dense,
-                              plan.dense_width, out, chunks, error_word(ids.device), max_vec)
+            with trace_range("mdl.embedding.lookup"):
+                ext().emb_forward(meta, store.peer_ptrs("slab"), store.rank, ids, offsets, dense,
+                                  plan.dense_width, out, chunks, error_word(ids.device), max_vec)
             return out
         return lookup_reference(store, plan, ids, offsets, dense, rows, out_dtype=torch.float32)
 
@@ -821,21 +823,26 @@ def owner_pull_grad(store, plan, ids, offsets, rows) -> None:
 def _owner_forward(store, plan, ids, offsets, dense, rows):
     """Multi-rank lookup: route (bag, owner) bundles, owners push pooled vectors back."""
 
-    ex = owner_route(store, plan, ids, offsets, dense, rows)
-    ex.symm.barrier()  # every rank's bundles routed, every accumulator zeroed
-    owner_push(store, plan, ids, offsets, rows)
-    ex.symm.barrier()  # every owner's vectors have landed
-    return owner_collect(store, plan, ids, rows)
+    with trace_range("mdl.embedding.route"):
+        ex = owner_route(store, plan, ids, offsets, dense, rows)
+        ex.symm.barrier()  # every rank's bundles routed, every accumulator zeroed
+    with trace_range("mdl.embedding.owner_push"):
+        owner_push(store, plan, ids, offsets, rows)
+        ex.symm.barrier()  # every owner's vectors have landed
+    with trace_range("mdl.embedding.collect"):
+        return owner_collect(store, plan, ids, rows)
 
 
 def _owner_backward(store, plan, ids, offsets, grad_out, rows):
     """Multi-rank gradient: owners pull each requester's d(out) slices into their own grad rows."""
 
-    owner_stage_grad(store, plan, ids, grad_out, rows)
-    ex = _exchange(store, plan, ids, rows)
-    ex.symm.barrier()  # every requester's gradient staged
-    owner_pull_grad(store, plan, ids, offsets, rows)
-    ex.symm.barrier()  # bundles / staged gradients may be overwritten after this point
+    with trace_range("mdl.embedding.stage_grad"):
+        owner_stage_grad(store, plan, ids, grad_out, rows)
+        ex = _exchange(store, plan, ids, rows)
+        ex.symm.barrier()  # every requester's gradient staged
+    with trace_range("mdl.embedding.owner_pull_grad"):
+        owner_pull_grad(store, plan, ids, offsets, rows)
+        ex.symm.barrier()  # bundles / staged gradients may be overwritten after this point
 
 
 def fused_lookup(store: EmbeddingStore, plan: LookupPlan, ids: torch.Tensor, offsets: torch.Tensor,

@@ -25,6 +25,7 @@ import torch.distributed as dist
 
 from ..config.schema import AppConfig
 from ..ops.dense import DenseParams
+from ..utils.trace import trace_range
 
 
 def lr_multiplier(config: AppConfig, step: int, decay_steps: int | None = None) -> float:
@@ -164,16 +165,15 @@ class Trainer:
 
     def forward_backward(self, batch) -> dict:
         self._mark("start")
-        if self.config.training.loss_reduction == "mean_per_request_per_task":
-            batch, scale = self.request_weights(batch)
+        with trace_range("mdl.forward"):
+            if self.config.training.loss_reduction == "mean_per_request_per_task":
+                batch, scale = self.request_weights(batch)
+            else:
+                scale = self.task_scale(batch)
             out = self.model(batch, task_scale=scale)
-            self._mark("forward")
-            out["loss"].backward()
-            self._mark("backward")
-            return out
-        out = self.model(batch, task_scale=self.task_scale(batch))
         self._mark("forward")
-        out["loss"].backward()
+        with trace_range("mdl.backward"):
+            out["loss"].backward()
         self._mark("backward")
         return out
 
@@ -191,9 +191,11 @@ class Trainer:
             from ..ops.moe import step_moe_controllers
 
             step_moe_controllers(self.moe, self.world, self.group)
-        dn = self.dense.step(lr=lr_dense, clip_norm=t.dense_clip_norm)
+        with trace_range("mdl.dense_update"):
+            dn = self.dense.step(lr=lr_dense, clip_norm=t.dense_clip_norm)
         self._mark("dense_update")
-        sn = self.store.step(lr=lr_sparse, clip_norm=t.sparse_clip_norm)
+        with trace_range("mdl.sparse_update"):
+            sn = self.store.step(lr=lr_sparse, clip_norm=t.sparse_clip_norm)
         self._mark("sparse_update")
         return dn, sn
 

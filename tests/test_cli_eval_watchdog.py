@@ -166,3 +166,12 @@ def test_cli_benchmark_modes(tmp_path):
         assert res["mode"] == mode and res["value"] > 0 and res["ms_p95"] >= res["ms_p50"] > 0, res
         if mode in ("compute", "end-to-end"):
             assert 0 < res["mfu_dense_gemm"] < 1, res
+    # profiler pass and lookup statistics after the timed steps
+    res = _run("benchmark", *over, "--mode", "compute", "--steps", "2", "--warmup", "1", "--profile-steps", "2",
+               "--comm-stats")[-1]
+    prof = res["profile"]
+    assert {"mdl.forward", "mdl.backward", "mdl.dense_update", "mdl.sparse_update"} <= set(
+        prof["ranges_cpu_ms_per_step"]), prof
+    comm = res["embedding_comm"]
+    assert comm and all(v["raw_ids"] >= v["active_ids"] >= 0 for v in comm.values())
+    assert res["embedding_comm_bytes_per_step"] == 0  # one rank: nothing crosses NVLink
