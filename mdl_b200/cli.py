@@ -486,7 +486,7 @@ def cmd_evaluate(args, argv) -> int:
     from .train.evaluate import evaluate
 
     cfg, rank, trainer, batches = _eval_setup(args, argv)
-    res = evaluate(trainer, batches)
+    res = evaluate(trainer, batches, bins=args.auc_bins, group_metric=args.group_metric)
     if rank == 0:
         print(json.dumps(res, default=str), flush=True)
     return 0
@@ -582,6 +582,10 @@ def build_parser() -> argparse.ArgumentParser:
         if name in ("evaluate", "predict"):
             p.add_argument("--checkpoint")
             p.add_argument("--max-batches", type=int, default=10)
+        if name == "evaluate":
+            p.add_argument("--group-metric", choices=["qauc", "uauc"], default=None,
+                           help="mean per-group AUC over the split's group_id column (one process)")
+            p.add_argument("--auc-bins", type=int, default=4096)
         if name == "predict":
             p.add_argument("--output", required=True)
     p = sub.add_parser("make-synthetic-parquet")

@@ -34,6 +34,7 @@ class PackedBatch:
     scenario_id: torch.Tensor
     rows: int
     sequences: dict[str, Any] = field(default_factory=dict)
+    group_key: torch.Tensor | None = None   # int64 per row: the split's group_id (QAUC / UAUC), hashed
     _flat: tuple = field(default=(), repr=False)
 
     @property
@@ -46,17 +47,18 @@ class PackedBatch:
         return sum(t.numel() * t.element_size() for t in self._leaves() if t is not None)
 
     def _leaves(self) -> list:
-        out = [self.ids, self.offsets, self.dense, self.labels, self.label_mask, self.scenario_id]
+        out = [self.ids, self.offsets, self.dense, self.labels, self.label_mask, self.scenario_id, self.group_key]
         for v in self.sequences.values():
             out.extend(v.values() if isinstance(v, dict) else [v])
         return out
 
     @staticmethod
-    def pack(ids, offsets, dense, labels, label_mask, scenario_id, rows, sequences=None, pin: bool = False):
+    def pack(ids, offsets, dense, labels, label_mask, scenario_id, rows, sequences=None, pin: bool = False,
+             group_key=None):
         """Build a batch whose leaves are views of one int64 and one fp32 flat buffer."""
 
         sequences = sequences or {}
-        i64_parts = [("ids", ids), ("offsets", offsets), ("scenario_id", scenario_id)]
+        i64_parts = [("ids", ids), ("offsets", offsets), ("scenario_id", scenario_id), ("group_key", group_key)]
         f32_parts = [("dense", dense), ("labels", labels), ("label_mask", label_mask)]
         for name, seq in sequences.items():
             for k, v in seq.items():
@@ -97,7 +99,8 @@ class PackedBatch:
                     seqs.setdefault(sname, {})[key] = view(buf, spec)
         batch = PackedBatch(ids=view(b64, v64["ids"]), offsets=view(b64, v64["offsets"]), dense=view(b32, v32["dense"]),
                             labels=view(b32, v32["labels"]), label_mask=view(b32, v32["label_mask"]),
-                            scenario_id=view(b64, v64["scenario_id"]), rows=rows, sequences=seqs)
+                            scenario_id=view(b64, v64["scenario_id"]), rows=rows, sequences=seqs,
+                            group_key=view(b64, v64.get("group_key")))
         batch._flat = (b64, b32)
         batch._views = (v64, v32)
         return batch
@@ -107,7 +110,7 @@ class PackedBatch:
 
         if not self._flat:
             return self.pack(self.ids, self.offsets, self.dense, self.labels, self.label_mask, self.scenario_id,
-                             self.rows, self.sequences).to(device, non_blocking)
+                             self.rows, self.sequences, group_key=self.group_key).to(device, non_blocking)
         b64, b32 = self._flat
         d64 = b64.to(device, non_blocking=non_blocking)
         d32 = b32.to(device, non_blocking=non_blocking)
@@ -140,12 +143,12 @@ class PackedBatch:
         seqs = {name: {k: v.cpu()[start:stop].clone() for k, v in seq.items()} for name, seq in self.sequences.items()}
         return PackedBatch.pack(torch.cat(id_parts) if id_parts else torch.zeros(0, dtype=torch.int64), offsets,
                                 cut(self.dense), cut(self.labels), cut(self.label_mask), cut(self.scenario_id), n,
-                                seqs)
+                                seqs, group_key=cut(self.group_key))
 
     def pin_memory(self) -> "PackedBatch":
         if self._flat and self._flat[0].is_pinned():
             return self
         b = self if self._flat else self.pack(self.ids, self.offsets, self.dense, self.labels, self.label_mask,
-                                              self.scenario_id, self.rows, self.sequences)
+                                              self.scenario_id, self.rows, self.sequences, group_key=self.group_key)
         b64, b32 = b._flat
         return PackedBatch._from_flat(b64.pin_memory(), b._views[0], b32.pin_memory(), b._views[1], b.rows)

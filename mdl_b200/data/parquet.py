@@ -215,6 +215,26 @@ def load_vocab_map(path: str) -> dict[str, int]:
 
 
 # ------------------------------------------------------------------ tensorization
+def group_keys(column) -> np.ndarray:
+    """int64 key per row of a group-id column (QAUC / UAUC groups): integer ids as they
+    are, anything else by a deterministic 64-bit hash of its text (the same on every
+    rank and process); missing values share key -1."""
+
+    import pyarrow as pa
+
+    col = column.combine_chunks() if hasattr(column, "combine_chunks") else column
+    if pa.types.is_integer(col.type):
+        return np.asarray(col.fill_null(-1).to_numpy(zero_copy_only=False), dtype=np.int64)
+    from pandas.util import hash_array
+
+    vals = col.cast(pa.string()).to_numpy(zero_copy_only=False)
+    missing = np.array([v is None for v in vals])
+    keys = hash_array(np.where(missing, "", vals).astype(object), categorize=False).view(np.int64)
+    keys = keys & np.int64(0x7FFFFFFFFFFFFFFF)
+    keys[missing] = -1
+    return keys
+
+
 class Tensorizer:
     """Arrow table (one sample per row) -> ``PackedBatch`` for a batch layout."""
 
@@ -250,6 +270,7 @@ class Tensorizer:
                 if fl.kind == "categorical":
                     self.seq_encoders[(q.name, fl.name)] = CategoricalEncoder(fl, vocab_maps.get(f"{q.name}.{fl.name}"))
         self.request_id = sp.request_id if sp.reader.deduplicate_request_features else None
+        self.group_id = sp.group_id
         if sp.reader.deduplicate_request_features and not sp.request_id:
             raise ValueError("reader.deduplicate_request_features needs the split's request_id column")
 
@@ -259,6 +280,8 @@ class Tensorizer:
         cols += list(self.label_masks.values())
         if self.scene_source:
             cols.append(self.scene_source)
+        if self.group_id:
+            cols.append(self.group_id)
         for q in self.sequences:
             cols += [fl.source or fl.name for fl in q.fields]
         if self.request_id:
@@ -448,10 +471,13 @@ class Tensorizer:
                 scen = np.array([0 if v is None else int(v) for v in vals], dtype=np.int64)
             else:
                 scen = np.array([self.scene_index.get(str(v), 0) for v in vals], dtype=np.int64)
+        group = None
+        if self.group_id and self.group_id in table.column_names:
+            group = torch.from_numpy(group_keys(table.column(self.group_id)))
         return PackedBatch.pack(torch.from_numpy(ids), torch.from_numpy(offsets),
                                 torch.from_numpy(dense) if self.dense_width else None, torch.from_numpy(labels),
                                 torch.from_numpy(mask) if any_mask else None, torch.from_numpy(scen), rows,
-                                sequences=self._sequences(table), pin=pin)
+                                sequences=self._sequences(table), pin=pin, group_key=group)
 
 
 # ------------------------------------------------------------------ iteration

@@ -73,7 +73,7 @@ def _child(factory, args, q, stop, beat_s: float) -> None:
                 return
             if not batch._flat:
                 batch = PackedBatch.pack(batch.ids, batch.offsets, batch.dense, batch.labels, batch.label_mask,
-                                         batch.scenario_id, batch.rows, batch.sequences)
+                                         batch.scenario_id, batch.rows, batch.sequences, group_key=batch.group_key)
             b64, b32 = batch._flat
             q.put((_BATCH, (b64, batch._views[0], b32, batch._views[1], batch.rows)))
         done.set()

@@ -107,4 +107,4 @@ def zero_weight(batch: PackedBatch) -> PackedBatch:
 
     mask = torch.zeros_like(batch.labels) if batch.labels is not None else None
     return PackedBatch(batch.ids, batch.offsets, batch.dense, batch.labels, mask, batch.scenario_id, batch.rows,
-                       batch.sequences)
+                       batch.sequences, group_key=batch.group_key)
