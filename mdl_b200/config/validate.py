@@ -57,9 +57,8 @@ def validate_app_config(config: AppConfig) -> None:
     seq_by_name = {s.name: s for s in config.sequences}
     for sequence in config.sequences:
         if sequence.encoder == "longer":
-            _require(int(sequence.longer_token_merge) == 1 and int(sequence.longer_inner_layers) == 0,
-                     f"sequence {sequence.name!r}: LONGER token merging (longer_token_merge > 1, "
-                     "longer_inner_layers) is not implemented")
+            _require(int(sequence.longer_token_merge) >= 1 and int(sequence.longer_inner_layers) >= 0,
+                     f"sequence {sequence.name!r}: longer_token_merge must be >= 1 and longer_inner_layers >= 0")
     model = config.model
     if model.name in ("rankmixer", "mdl_rankmixer"):
         raw = [n for n in config.resolved.tokenization.feature_token_inputs

@@ -5,8 +5,12 @@ Reference: ``LongerSequenceAttentionBlock`` ``src/model.py:1033-1414``,
 ``LongerModel`` ``:6563-6612``.
 
 * Sequence tokens: each event's field embeddings (one lookup per field, rows =
-  events) through a ``Linear -> GELU -> Linear`` step projector to ``d``; token
-  merge size 1 (the merger is then the identity).
+  events) through a ``Linear -> GELU -> Linear`` step projector to ``d``
+  (``longer_dim``). The token merger groups ``m`` (``longer_token_merge``)
+  consecutive events (left-padded to a multiple of ``m``), runs
+  ``longer_inner_layers`` blocks at width ``d`` inside each group, zeroes padding
+  slots and lays each group's slots side by side: ``ceil(L / m)`` tokens of width
+  ``m * d``, the width of every later block, global token and output token.
 * Global tokens: candidate globals from the sequence's ``target_inputs`` and user
   globals from ``longer_user_global_inputs``, each group concatenated and
   projected by an MLP to ``count * d``.
@@ -85,16 +89,23 @@ class LongerBlockFn(torch.autograd.Function):
         r0 = max(0, Lk - 128 * ((Lq + 127) // 128))
         if Lk - Lq > r0:  # Q of rows in the first query tile that are not queries must be finite
             qkv[:, r0:Lk - Lq, :D].zero_()
-        bgemm(xq, _shadow(blk.wq), _off(qkv, (Lk - Lq) * 3 * D), M=Lq, N=D, K=D, G=B, lda=D, gsA=Lq * D, ldb=D, gsB=0,
-              ldc=3 * D, gsC=Lk * 3 * D, bias=blk.bq, gs_bias=0)
+        if Lq == Lk:  # every token is a query: one flat product instead of B tiny ones
+            bgemm(xq, _shadow(blk.wq), qkv, M=B * Lk, N=D, K=D, lda=D, ldb=D, ldc=3 * D, bias=blk.bq)
+        else:
+            bgemm(xq, _shadow(blk.wq), _off(qkv, (Lk - Lq) * 3 * D), M=Lq, N=D, K=D, G=B, lda=D, gsA=Lq * D, ldb=D,
+                  gsB=0, ldc=3 * D, gsC=Lk * 3 * D, bias=blk.bq, gs_bias=0)
         bgemm(xk, _shadow(blk.wkv), _off(qkv, D), M=B * Lk, N=2 * D, K=D, lda=D, ldb=D, ldc=3 * D, bias=blk.bkv)
         ks = kstart.to(torch.int32).contiguous()
         att = torch.empty(B, Lq, D, dtype=torch.bfloat16, device=dev)
         lse = torch.empty(B, heads, Lq, dtype=torch.float32, device=dev)
         ext().fmha_fwd(qkv, ks, att, lse, heads, Lq, bool(causal), 0.0, error_word(dev), int(ktail))
         h = torch.empty(B, Lq, D, dtype=torch.bfloat16, device=dev)
-        bgemm(att, _shadow(blk.wo), h, M=Lq, N=D, K=D, G=B, lda=D, gsA=Lq * D, ldb=D, gsB=0, ldc=D, gsC=Lq * D,
-              bias=blk.bo, aux=_off(X, (Lk - Lq) * D), ld_aux=D, gs_aux=Lk * D, act=ACT_ADD)
+        if Lq == Lk:
+            bgemm(att, _shadow(blk.wo), h, M=B * Lq, N=D, K=D, lda=D, ldb=D, ldc=D, bias=blk.bo, aux=X, ld_aux=D,
+                  act=ACT_ADD)
+        else:
+            bgemm(att, _shadow(blk.wo), h, M=Lq, N=D, K=D, G=B, lda=D, gsA=Lq * D, ldb=D, gsB=0, ldc=D, gsC=Lq * D,
+                  bias=blk.bo, aux=_off(X, (Lk - Lq) * D), ld_aux=D, gs_aux=Lk * D, act=ACT_ADD)
         hn, mean_f, rstd_f = _ln_fwd(h.view(B * Lq, D), blk.lnf_w, blk.lnf_b, eps)
         ug = torch.empty(B * Lq, Hd, dtype=torch.bfloat16, device=dev)
         u = torch.empty_like(ug)
@@ -145,11 +156,17 @@ class LongerBlockFn(torch.autograd.Function):
         # Q projection (query rows only)
         dq_rows = _off(dqkv, (Lk - Lq) * 3 * D)
         dxq = torch.empty(B * Lq, D, dtype=torch.bfloat16, device=dev)
-        bgemm(dq_rows, _shadow(blk.wq), dxq, M=Lq, N=D, K=D, G=B, lda=3 * D, gsA=Lk * 3 * D, ldb=D, gsB=0, b_mn=True,
-              ldc=D, gsC=Lq * D)
-        bgemm(dq_rows, xq, _grad(blk.wq), M=D, N=D, K=Lq, lda=3 * D, a_mn=True, ldb=D, b_mn=True, ldc=D,
-              accumulate=True, kg=B, ksA=Lk * 3 * D, ksB=Lq * D)
-        C.colsum(dq_rows, _grad(blk.bq), B, Lq, D, 3 * D, Lk * 3 * D, 1.0, 0)
+        if Lq == Lk:
+            bgemm(dq_rows, _shadow(blk.wq), dxq, M=B * Lq, N=D, K=D, lda=3 * D, ldb=D, b_mn=True, ldc=D)
+            bgemm(dq_rows, xq, _grad(blk.wq), M=D, N=D, K=B * Lq, lda=3 * D, a_mn=True, ldb=D, b_mn=True, ldc=D,
+                  accumulate=True)
+            C.colsum(dq_rows, _grad(blk.bq), 1, B * Lq, D, 3 * D, 0, 1.0)
+        else:
+            bgemm(dq_rows, _shadow(blk.wq), dxq, M=Lq, N=D, K=D, G=B, lda=3 * D, gsA=Lk * 3 * D, ldb=D, gsB=0,
+                  b_mn=True, ldc=D, gsC=Lq * D)
+            bgemm(dq_rows, xq, _grad(blk.wq), M=D, N=D, K=Lq, lda=3 * D, a_mn=True, ldb=D, b_mn=True, ldc=D,
+                  accumulate=True, kg=B, ksA=Lk * 3 * D, ksB=Lq * D)
+            C.colsum(dq_rows, _grad(blk.bq), B, Lq, D, 3 * D, Lk * 3 * D, 1.0, 0)
         # K/V projection (all rows)
         dkv = _off(dqkv, D)
         dxk = torch.empty(B * Lk, D, dtype=torch.bfloat16, device=dev)
@@ -264,22 +281,29 @@ class LongerEncoder(nn.Module):
                  extra_globals: int = 0, time_delta: tuple[int, int] | None = None) -> None:
         super().__init__()
         m = config.model
-        D = int(seq.longer_dim)
-        if int(seq.longer_token_merge) != 1 or int(seq.longer_inner_layers) != 0:
-            raise NotImplementedError("LONGER token merge size 1 without inner layers is implemented")
-        self.D = D
+        Din = int(seq.longer_dim)
+        self.merge = int(seq.longer_token_merge)
+        if self.merge < 1 or int(seq.longer_inner_layers) < 0:
+            raise ValueError(f"LONGER sequence {seq.name!r}: longer_token_merge >= 1 and longer_inner_layers >= 0")
+        D = Din * self.merge           # merged token width: every block after the merger runs at it
+        self.Din, self.D = Din, D
         heads = seq.longer_num_heads  # reference SequenceConfig.resolved_longer_num_heads
         if heads is None:
-            heads = int(m.num_heads) if D % int(m.num_heads) == 0 else next(h for h in (8, 4, 2, 1) if D % h == 0)
+            heads = int(m.num_heads) if Din % int(m.num_heads) == 0 else next(h for h in (8, 4, 2, 1) if Din % h == 0)
         self.heads = int(heads)
-        if D % self.heads:
-            raise ValueError(f"LONGER sequence {seq.name!r}: longer_dim {D} not divisible by {self.heads} heads")
+        if Din % self.heads:
+            raise ValueError(f"LONGER sequence {seq.name!r}: longer_dim {Din} not divisible by {self.heads} heads")
         self.head_dim = D // self.heads
-        hidden = int(seq.longer_hidden_dim or 4 * D)
+        hidden_in = int(seq.longer_hidden_dim or 4 * Din)
+        hidden = hidden_in * self.merge
         self.R = int(seq.longer_query_tokens)
         self.L = int(seq.max_length)
         plan = encoder.seq_plans[seq.name]
-        self.step = _MLP(plan.out_ld, plan.out_width, hidden, D, device=device)
+        self.step = _MLP(plan.out_ld, plan.out_width, hidden_in, Din, device=device)
+        # token merger (reference LongerTokenMerger): inner blocks at the event width over
+        # each group of `merge` consecutive events, then each group's slots side by side
+        self.inner = nn.ModuleList(LongerBlock(Din, hidden_in, device=device)
+                                   for _ in range(int(seq.longer_inner_layers)))
         self.Gu = int(seq.longer_user_global_tokens) if user_plan is not None else 0
         self.Gx = int(extra_globals)
         cand = seq.longer_candidate_global_tokens
@@ -309,8 +333,34 @@ class LongerEncoder(nn.Module):
             self.pos = nn.Parameter(torch.randn(self.L, c0, device=device) * float(m.init_std))
             self._pad_cols = plan.out_ld - c0
 
+    def merge_tokens(self, tokens: torch.Tensor, kst: torch.Tensor, native: bool):
+        """``[B, L, d]`` event tokens with ``kst`` leading padding events -> ``[B, ceil(L/m), m*d]``
+        merged tokens and their padding count (reference ``LongerTokenMerger.forward``
+        ``src/model.py:1489-1517``): left-pad to a multiple of ``m``, run the inner blocks
+        over each group of ``m`` tokens (full attention among the group's valid tokens),
+        zero the padding slots, lay each group's slots side by side."""
+
+        m = self.merge
+        B, L, Din = tokens.shape
+        pad = (-L) % m
+        if pad:
+            tokens = F.pad(tokens, (0, 0, pad, 0))
+            kst = kst + pad
+        Lp = L + pad
+        ng = Lp // m
+        if len(self.inner):
+            h = tokens.reshape(B * ng, m, Din)
+            starts = torch.arange(ng, device=kst.device, dtype=kst.dtype) * m
+            gk = (kst.view(B, 1) - starts.view(1, ng)).clamp(0, m).reshape(B * ng).to(torch.int32)
+            for blk in self.inner:
+                h = blk(h, gk, m, self.heads, False, 0, native)
+            tokens = h.reshape(B, Lp, Din)
+        valid = torch.arange(Lp, device=tokens.device).view(1, Lp) >= kst.view(B, 1)
+        tokens = tokens * valid.unsqueeze(-1).to(tokens.dtype)
+        return tokens.reshape(B, ng, m * Din), torch.div(kst, m, rounding_mode="floor")
+
     def project(self, seq_in, lengths, native: bool) -> torch.Tensor:
-        """Event tokens ``[rows, L, d]`` (positions added to the event values first)."""
+        """Event tokens ``[rows, L, longer_dim]`` (positions added to the event values first)."""
 
         rows, L = lengths.shape[0], self.L
         if self.pos is not None:
@@ -319,18 +369,26 @@ class LongerEncoder(nn.Module):
             pe = self.pos[positions(lengths, L)].view(rows * L, self.pos_cols)
             pe = F.pad(pe, (0, self._pad_cols)) if self._pad_cols else pe
             seq_in = seq_in + pe.to(seq_in.dtype)
-        return self.step(seq_in, native).view(rows, L, self.D)
+        return self.step(seq_in, native).view(rows, L, self.Din)
 
     def forward(self, seq_in, lengths, target_in, user_in, native: bool, cls_tokens=None,
                 tokens=None) -> torch.Tensor:
         """``tokens``: event tokens already projected (``project``), else ``seq_in`` is projected here."""
 
         B, L, D, R, G = lengths.shape[0], self.L, self.D, self.R, self.G
-        if native and self.head_dim != 32:
-            raise NotImplementedError(f"LONGER head_dim {self.head_dim}: the tcgen05 attention kernels take head_dim "
-                                      "32 (set runtime.kernel_backend: torch for this model)")
+        if native and (self.head_dim != 32 or (len(self.inner) and self.Din // self.heads != 32)):
+            raise NotImplementedError(f"LONGER head_dim {self.head_dim} (inner {self.Din // self.heads}): the tcgen05 "
+                                      "attention kernels take head_dim 32 (set runtime.kernel_backend: torch)")
         if tokens is None:
             tokens = self.project(seq_in, lengths, native)
+        kst = (L - lengths.clamp(0, L)).to(torch.int32)
+        if self.merge > 1 or len(self.inner):
+            tokens, kst = self.merge_tokens(tokens, kst, native)
+            L = tokens.shape[1]
+        if L < R:  # fewer (merged) tokens than recent queries: left-pad, the padding is masked
+            tokens = F.pad(tokens, (0, 0, R - L, 0))
+            kst = kst + (R - L)
+            L = R
         parts = [tokens]
         if self.Gu:
             parts.append(self.user_mlp(user_in, native).view(B, self.Gu, D))
@@ -341,7 +399,6 @@ class LongerEncoder(nn.Module):
         if self.Gc:
             parts.append(self.cand_mlp(target_in, native).view(B, self.Gc, D))
         X = torch.cat(parts, dim=1) if len(parts) > 1 else tokens
-        kst = (L - lengths.clamp(0, L)).to(torch.int32)
         X = self.cross(X, kst, R + G, self.heads, True, G, native)     # [B, R + G, D]: [recent; globals]
         kst = (kst - (L - R)).clamp(min=0)
         for blk in self.selfs:
