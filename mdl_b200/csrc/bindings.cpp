@@ -777,7 +777,7 @@ void position_grad(const at::Tensor& dx, const at::Tensor& dpos, const at::Tenso
 // ------------------------------------------------------------------ flash attention
 mdl::FmhaArgs fmha_args(const at::Tensor& qkv, const at::Tensor& kstart, const at::Tensor& out, const at::Tensor& lse,
                         int64_t H, int64_t Lq, bool causal, double scale, const std::optional<at::Tensor>& err,
-                        int64_t ktail) {
+                        int64_t ktail, int64_t kexcl) {
   require_cuda(qkv, "qkv");
   TORCH_CHECK(qkv.scalar_type() == at::kBFloat16 && qkv.dim() == 3 && qkv.is_contiguous(), "qkv must be [B, Lk, 3D] bf16");
   TORCH_CHECK(kstart.scalar_type() == at::kInt && kstart.numel() == qkv.size(0), "kstart must be int32 [B]");
@@ -795,6 +795,7 @@ mdl::FmhaArgs fmha_args(const at::Tensor& qkv, const at::Tensor& kstart, const a
   a.Lq = static_cast<int>(Lq);
   a.causal = causal;
   a.ktail = static_cast<int>(ktail);
+  a.kexcl = static_cast<int>(kexcl);
   a.scale = static_cast<float>(scale);
   a.err = optr<int>(err);
   TORCH_CHECK(qkv.size(2) == 3 * H * a.hd, "qkv width must be 3 * H * head_dim");
@@ -804,9 +805,10 @@ mdl::FmhaArgs fmha_args(const at::Tensor& qkv, const at::Tensor& kstart, const a
 }
 
 void fmha_fwd(const at::Tensor& qkv, const at::Tensor& kstart, const at::Tensor& out, const at::Tensor& lse, int64_t H,
-              int64_t Lq, bool causal, double scale, const std::optional<at::Tensor>& err, int64_t ktail) {
+              int64_t Lq, bool causal, double scale, const std::optional<at::Tensor>& err, int64_t ktail,
+              int64_t kexcl) {
   c10::cuda::CUDAGuard guard(qkv.device());
-  auto a = fmha_args(qkv, kstart, out, lse, H, Lq, causal, scale, err, ktail);
+  auto a = fmha_args(qkv, kstart, out, lse, H, Lq, causal, scale, err, ktail, kexcl);
   cudaError_t e = mdl::fmha_fwd(a, stream_of(qkv));
   if (e != cudaSuccess) throw std::runtime_error(std::string(mdl::fmha_last_error()) + ": " + cudaGetErrorString(e));
   g_launches += 1;
@@ -815,9 +817,9 @@ void fmha_fwd(const at::Tensor& qkv, const at::Tensor& kstart, const at::Tensor&
 void fmha_bwd(const at::Tensor& qkv, const at::Tensor& kstart, const at::Tensor& out, const at::Tensor& lse,
               const at::Tensor& dout, const at::Tensor& dqkv, const at::Tensor& dq_acc, const at::Tensor& dsum,
               int64_t H, int64_t Lq, bool causal, double scale, const std::optional<at::Tensor>& err,
-              int64_t ktail) {
+              int64_t ktail, int64_t kexcl) {
   c10::cuda::CUDAGuard guard(qkv.device());
-  auto a = fmha_args(qkv, kstart, out, lse, H, Lq, causal, scale, err, ktail);
+  auto a = fmha_args(qkv, kstart, out, lse, H, Lq, causal, scale, err, ktail, kexcl);
   TORCH_CHECK(dout.scalar_type() == at::kBFloat16 && dout.is_contiguous() && dout.numel() == out.numel(),
               "dout must be contiguous bf16 like out");
   TORCH_CHECK(dqkv.scalar_type() == at::kBFloat16 && dqkv.is_contiguous() && dqkv.numel() == qkv.numel(),
@@ -886,12 +888,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("small_attn_fwd", &small_attn_fwd);
   m.def("small_attn_bwd", &small_attn_bwd);
   m.def("fmha_fwd", &fmha_fwd, py::arg("qkv"), py::arg("kstart"), py::arg("out"), py::arg("lse"), py::arg("H"),
-        py::arg("Lq"), py::arg("causal"), py::arg("scale"), py::arg("err") = py::none(), py::arg("ktail") = 0);
+        py::arg("Lq"), py::arg("causal"), py::arg("scale"), py::arg("err") = py::none(), py::arg("ktail") = 0,
+        py::arg("kexcl") = 0);
   m.def("position_add", &position_add);
   m.def("position_grad", &position_grad);
   m.def("sqa_fwd", &sqa_fwd);
   m.def("sqa_bwd", &sqa_bwd);
   m.def("fmha_bwd", &fmha_bwd, py::arg("qkv"), py::arg("kstart"), py::arg("out"), py::arg("lse"), py::arg("dout"),
         py::arg("dqkv"), py::arg("dq_acc"), py::arg("dsum"), py::arg("H"), py::arg("Lq"), py::arg("causal"),
-        py::arg("scale"), py::arg("err") = py::none(), py::arg("ktail") = 0);
+        py::arg("scale"), py::arg("err") = py::none(), py::arg("ktail") = 0,
+        py::arg("kexcl") = 0);
 }

@@ -89,6 +89,7 @@ struct Params {
   void* dqkv;
   int B, H, Lk, Lq, D, causal;
   int ktail;  // the last ktail tokens see and are seen by every token (causal only)
+  int kexcl;  // of those, the last kexcl are seen only by themselves (causal only)
   float scale, scale2;
   int* err;
 };
@@ -463,11 +464,14 @@ __global__ void __launch_bounds__(F_THREADS, 2)
           }
         } else if (it.kst > kbase || (p.causal && (t == it.i || t == 0))) {
           const int tail0 = Lk - p.ktail;
+          const int excl0 = Lk - p.kexcl;  // keys from here on: only queries from here on see them
           const bool q_tail = qrow >= tail0;
+          const bool q_excl = qrow >= excl0;
 #pragma unroll
           for (int c = 0; c < TILE; ++c) {
             const int jj = kbase + c;
-            const bool vis = jj >= it.kst && (!p.causal || jj <= qrow || jj >= tail0 || q_tail);
+            const bool vis = jj >= it.kst && (!p.causal || jj <= qrow || jj >= tail0 || q_tail) &&
+                             (jj < excl0 || q_excl);
             if (!vis) sr[c] = __float_as_uint(-CUDART_INF_F);
           }
         }
@@ -843,6 +847,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const int tail0 = Lk - p.ktail;
           const int causal_min = krow >= tail0 ? INT_MIN / 2 : min(krow, tail0) - qcol0;
           cmin = max(cmin, causal_min);
+          // an excluded trailing key is seen only by the queries of the excluded block
+          if (krow >= Lk - p.kexcl) cmin = max(cmin, Lk - p.kexcl - qcol0);
         }
         if (!key_ok) cmin = INT_MAX / 2;
 #pragma unroll
@@ -979,6 +985,7 @@ Params make_params(const FmhaArgs& a) {
   p.D = a.H * HD;
   p.causal = a.causal ? 1 : 0;
   p.ktail = a.causal ? a.ktail : 0;
+  p.kexcl = a.causal ? a.kexcl : 0;
   p.scale = a.scale > 0.f ? a.scale : 1.f / sqrtf(static_cast<float>(HD));
   p.scale2 = p.scale * kLog2e;
   p.err = a.err;
@@ -1025,7 +1032,7 @@ cudaError_t fail(const char* why, cudaError_t e) {
 
 bool shapes_ok(const FmhaArgs& a) {
   return a.hd == HD && a.B > 0 && a.H > 0 && a.Lq > 0 && a.Lq <= a.Lk && a.kstart != nullptr && a.ktail >= 0 &&
-         a.ktail <= TILE && a.ktail <= a.Lq &&
+         a.ktail <= TILE && a.ktail <= a.Lq && a.kexcl >= 0 && a.kexcl <= a.ktail &&
          (reinterpret_cast<uintptr_t>(a.qkv) & 15) == 0;
 }
 

@@ -14,7 +14,7 @@ namespace mdl {
 //   qkv   [B, Lk, 3*D] bf16: per token Q | K | V, D = H * 32 (head h at h*32)
 //   the queries are the last Lq tokens (rows Lk-Lq .. Lk-1) of each sample
 //   key j is visible to query row p iff kstart[b] <= j and (!causal or j <= p or
-//   j >= Lk - ktail or p >= Lk - ktail)
+//   j >= Lk - ktail or p >= Lk - ktail) and (j < Lk - kexcl or p >= Lk - kexcl)
 //   out   [B, Lq, D] bf16, rows whose query has no visible key are zero
 //   lse   [B, H, Lq] fp32: base-2 log-sum-exp of the scaled scores (+inf for
 //         rows without a visible key), saved for the backward
@@ -38,6 +38,9 @@ struct FmhaArgs {
   // With causal: the last ktail tokens (<= 128, all queries) see every key and are
   // seen by every query (LONGER's global tokens placed after the sequence).
   int ktail = 0;
+  // With causal: the last kexcl (<= ktail) of those tokens are seen only by each
+  // other (LONGER's candidate global tokens: no other token attends to them).
+  int kexcl = 0;
   float scale = 0.f;            // softmax scale (1/sqrt(hd) when 0)
   int* err = nullptr;
 };

@@ -15,20 +15,24 @@ Reference: ``LongerSequenceAttentionBlock`` ``src/model.py:1033-1414``,
   globals from ``longer_user_global_inputs``, each group concatenated and
   projected by an MLP to ``count * d``.
 * Cross block: queries = the global tokens + the last ``R`` (``longer_query_tokens``)
-  sequence tokens, keys = globals + all sequence tokens; globals see every valid
-  key, recent queries are bottom-right causal and see the globals
-  (``mixed_allowed_mask`` ``:1110-1158``). Self blocks: full attention over the
-  cross block's outputs. Every block: pre-LayerNorm queries and keys (separate
-  norms), Q and fused K/V projections, attention, output projection, residual,
-  pre-LayerNorm GELU FFN, residual.
+  sequence tokens, keys = globals + all sequence tokens. User / CLS globals see
+  every valid key except the candidate globals; recent queries are bottom-right
+  causal and see the user / CLS globals (``mixed_allowed_mask`` ``:1110-1158``);
+  candidate globals see every valid key and are seen by no other query, so every
+  output but theirs is independent of the candidate (the reference's request-side
+  / candidate-side split, ``:1706-1730, 2036-2296``). Self blocks: the same
+  visibility over the cross block's ``R + G`` outputs. Every block: pre-LayerNorm
+  queries and keys (separate norms), Q and fused K/V projections, attention,
+  output projection, residual, pre-LayerNorm GELU FFN, residual.
 * Output: the ``G + R`` tokens flattened (``longer_output: full``).
 
-Layout. A sample's tokens are ``[sequence (left-padded); globals]`` -- the
-globals after the sequence, so the cross block's visibility is the causal query
-suffix plus ``ktail = G`` always-visible trailing tokens of the tcgen05 flash
-attention (``ops/attention.py``), and padding stays a per-sample prefix.
-The query order inside the model is ``[recent; globals]``; ``reference_order``
-maps it to the reference's ``[globals; recent]``.
+Layout. A sample's tokens are ``[sequence (left-padded); user; CLS; candidate
+globals]`` -- the globals after the sequence, so the visibility is the causal
+query suffix plus ``ktail = G`` trailing global tokens, of which the last
+``kexcl = Gc`` are hidden from the others, in the tcgen05 flash attention
+(``ops/attention.py``), and padding stays a per-sample prefix. The query order
+inside the model is ``[recent; globals]``; ``reference_order`` maps it to the
+reference's ``[globals; recent]``.
 """
 
 from __future__ import annotations
@@ -76,7 +80,7 @@ class LongerBlockFn(torch.autograd.Function):
     (queries are the last ``Lq`` tokens)."""
 
     @staticmethod
-    def forward(ctx, X, kstart, blk, Lq, heads, causal, ktail):
+    def forward(ctx, X, kstart, blk, Lq, heads, causal, ktail, kexcl=0):
         B, Lk, D = X.shape
         Hd = blk.hidden_dim
         dev = X.device
@@ -98,7 +102,7 @@ class LongerBlockFn(torch.autograd.Function):
         ks = kstart.to(torch.int32).contiguous()
         att = torch.empty(B, Lq, D, dtype=torch.bfloat16, device=dev)
         lse = torch.empty(B, heads, Lq, dtype=torch.float32, device=dev)
-        ext().fmha_fwd(qkv, ks, att, lse, heads, Lq, bool(causal), 0.0, error_word(dev), int(ktail))
+        ext().fmha_fwd(qkv, ks, att, lse, heads, Lq, bool(causal), 0.0, error_word(dev), int(ktail), int(kexcl))
         h = torch.empty(B, Lq, D, dtype=torch.bfloat16, device=dev)
         if Lq == Lk:
             bgemm(att, _shadow(blk.wo), h, M=B * Lq, N=D, K=D, lda=D, ldb=D, ldc=D, bias=blk.bo, aux=X, ld_aux=D,
@@ -116,14 +120,14 @@ class LongerBlockFn(torch.autograd.Function):
               act=ACT_ADD)
         ctx.save_for_backward(X, xk, mean_k, rstd_k, xq_in, xq, mean_q, rstd_q, qkv, ks, att, lse, h, hn, mean_f,
                               rstd_f, ug, u)
-        ctx.meta = (blk, Lq, heads, bool(causal), int(ktail))
+        ctx.meta = (blk, Lq, heads, bool(causal), int(ktail), int(kexcl))
         return Y
 
     @staticmethod
     def backward(ctx, dY):
         (X, xk, mean_k, rstd_k, xq_in, xq, mean_q, rstd_q, qkv, ks, att, lse, h, hn, mean_f, rstd_f, ug,
          u) = ctx.saved_tensors
-        blk, Lq, heads, causal, ktail = ctx.meta
+        blk, Lq, heads, causal, ktail, kexcl = ctx.meta
         B, Lk, D = X.shape
         Hd = blk.hidden_dim
         dev = X.device
@@ -151,7 +155,7 @@ class LongerBlockFn(torch.autograd.Function):
         dq_acc = torch.empty(B, Lq, D, dtype=torch.float32, device=dev)
         dsum = torch.empty(B, heads, Lq, dtype=torch.float32, device=dev)
         C.fmha_bwd(qkv, ks, att, lse, datt.view(B, Lq, D), dqkv, dq_acc, dsum, heads, Lq, causal, 0.0, error_word(dev),
-                   ktail)
+                   ktail, kexcl)
         del dq_acc, dsum, datt
         # Q projection (query rows only)
         dq_rows = _off(dqkv, (Lk - Lq) * 3 * D)
@@ -178,7 +182,7 @@ class LongerBlockFn(torch.autograd.Function):
         dX = _ln_bwd(dxk, X.view(B * Lk, D), mean_k, rstd_k, blk.lnk_w, blk.lnk_b).view(B, Lk, D)
         dxq_in = _ln_bwd(dxq, xq_in, mean_q, rstd_q, blk.lnq_w, blk.lnq_b).view(B, Lq, D)
         dX[:, Lk - Lq:] += dxq_in + dh.view(B, Lq, D)
-        return dX, None, None, None, None, None, None
+        return dX, None, None, None, None, None, None, None
 
 
 class LongerBlock(nn.Module):
@@ -209,7 +213,7 @@ class LongerBlock(nn.Module):
             _kaiming_uniform_(w.data, fan)
             _kaiming_uniform_(b.data, fan)
 
-    def forward_reference(self, X, kstart, Lq, heads, causal, ktail):
+    def forward_reference(self, X, kstart, Lq, heads, causal, ktail, kexcl=0):
         B, Lk, D = X.shape
         X = X.float()
         xk = F.layer_norm(X, (D,), self.lnk_w, self.lnk_b, self.eps)
@@ -217,15 +221,16 @@ class LongerBlock(nn.Module):
         q = xq @ self.wq.t() + self.bq
         kv = xk @ self.wkv.t() + self.bkv
         qfull = torch.cat([torch.zeros(B, Lk - Lq, D, device=X.device), q], dim=1)
-        att = suffix_attention_reference(torch.cat([qfull, kv], dim=-1), kstart, heads, Lq, causal, ktail=ktail)
+        att = suffix_attention_reference(torch.cat([qfull, kv], dim=-1), kstart, heads, Lq, causal, ktail=ktail,
+                                         kexcl=kexcl)
         h = X[:, Lk - Lq:] + att @ self.wo.t() + self.bo
         hn = F.layer_norm(h, (D,), self.lnf_w, self.lnf_b, self.eps)
         return h + F.gelu(hn @ self.w1.t() + self.b1) @ self.w2.t() + self.b2
 
-    def forward(self, X, kstart, Lq, heads, causal, ktail, native: bool):
+    def forward(self, X, kstart, Lq, heads, causal, ktail, native: bool, kexcl: int = 0):
         if native:
-            return LongerBlockFn.apply(X, kstart, self, Lq, heads, causal, ktail)
-        return self.forward_reference(X, kstart, Lq, heads, causal, ktail)
+            return LongerBlockFn.apply(X, kstart, self, Lq, heads, causal, ktail, kexcl)
+        return self.forward_reference(X, kstart, Lq, heads, causal, ktail, kexcl)
 
     def reference_state_dict(self, prefix: str) -> dict[str, torch.Tensor]:
         sd = {prefix + "query_norm.weight": self.lnq_w, prefix + "query_norm.bias": self.lnq_b,
@@ -399,10 +404,16 @@ class LongerEncoder(nn.Module):
         if self.Gc:
             parts.append(self.cand_mlp(target_in, native).view(B, self.Gc, D))
         X = torch.cat(parts, dim=1) if len(parts) > 1 else tokens
-        X = self.cross(X, kst, R + G, self.heads, True, G, native)     # [B, R + G, D]: [recent; globals]
+        # [B, R + G, D]: [recent; globals]. Recent queries: bottom-right causal; user / CLS globals:
+        # every valid key; the candidate globals (last Gc) are seen by nobody else, so every
+        # output except theirs is candidate-independent (reference LongerSequenceEncoder: the
+        # request-side keys exclude the candidate globals, src/model.py:1706-1730, 2036-2296)
+        X = self.cross(X, kst, R + G, self.heads, True, G, native, kexcl=self.Gc)
         kst = (kst - (L - R)).clamp(min=0)
         for blk in self.selfs:
-            X = blk(X, kst, R + G, self.heads, False, 0, native)
+            # self blocks: the same visibility over [recent; globals] (reference mixed mask
+            # over [user; recent], candidates over everything)
+            X = blk(X, kst, R + G, self.heads, True, G, native, kexcl=self.Gc)
         return X
 
     @staticmethod

@@ -17,6 +17,11 @@ the packed valid tokens):
   ``src/model.py:1110-1158``: global tokens see everything, recent queries are
   bottom-right causal and see the globals) with the globals placed after the
   sequence instead of before it;
+* ``kexcl`` (``<= ktail``): the last ``kexcl`` of those tokens are seen only by
+  each other -- LONGER's candidate global tokens, which attend to everything
+  while no user global or sequence token attends to them (the reference keeps
+  them out of the request-side keys, ``LongerSequenceEncoder.forward``
+  ``src/model.py:2036-2296``);
 * returns ``[B, lq, D]``.
 
 CUDA: the tcgen05 flash attention in ``csrc/fmha.cu`` (forward saves the
@@ -37,7 +42,7 @@ LOG2E = 1.4426950408889634
 
 
 def suffix_attention_reference(qkv: torch.Tensor, kstart: torch.Tensor, heads: int, lq: int, causal: bool = True,
-                               scale: float | None = None, ktail: int = 0) -> torch.Tensor:
+                               scale: float | None = None, ktail: int = 0, kexcl: int = 0) -> torch.Tensor:
     """fp32 PyTorch definition (differentiable)."""
 
     B, Lk, W = qkv.shape
@@ -57,6 +62,8 @@ def suffix_attention_reference(qkv: torch.Tensor, kstart: torch.Tensor, heads: i
         tail0 = Lk - ktail
         allowed = allowed & ((kpos.view(1, 1, Lk) <= qpos.view(1, lq, 1)) | (kpos.view(1, 1, Lk) >= tail0)
                              | (qpos.view(1, lq, 1) >= tail0))
+        excl0 = Lk - kexcl
+        allowed = allowed & ((kpos.view(1, 1, Lk) < excl0) | (qpos.view(1, lq, 1) >= excl0))
     allowed = allowed & (qpos.view(1, lq, 1) >= ks)                      # padded queries output zero
     s = s.masked_fill(~allowed.unsqueeze(1), float("-inf"))
     p = torch.softmax(s, dim=-1)
@@ -67,37 +74,38 @@ def suffix_attention_reference(qkv: torch.Tensor, kstart: torch.Tensor, heads: i
 
 class SuffixAttentionFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, qkv, kstart, heads, lq, causal, ktail=0):
+    def forward(ctx, qkv, kstart, heads, lq, causal, ktail=0, kexcl=0):
         B, Lk, W = qkv.shape
         D = W // 3
         qkv = qkv.contiguous()
         ks = kstart.to(torch.int32).contiguous()
         out = torch.empty(B, lq, D, dtype=torch.bfloat16, device=qkv.device)
         lse = torch.empty(B, heads, lq, dtype=torch.float32, device=qkv.device)
-        ext().fmha_fwd(qkv, ks, out, lse, heads, lq, bool(causal), 0.0, error_word(qkv.device), int(ktail))
+        ext().fmha_fwd(qkv, ks, out, lse, heads, lq, bool(causal), 0.0, error_word(qkv.device), int(ktail),
+                       int(kexcl))
         ctx.save_for_backward(qkv, ks, out, lse)
-        ctx.meta = (heads, lq, bool(causal), int(ktail))
+        ctx.meta = (heads, lq, bool(causal), int(ktail), int(kexcl))
         return out
 
     @staticmethod
     def backward(ctx, dout):
         qkv, ks, out, lse = ctx.saved_tensors
-        heads, lq, causal, ktail = ctx.meta
+        heads, lq, causal, ktail, kexcl = ctx.meta
         dout = dout.to(torch.bfloat16).contiguous()
         dqkv = torch.empty_like(qkv)
         dq_acc = torch.empty(out.shape, dtype=torch.float32, device=qkv.device)
         dsum = torch.empty(lse.shape, dtype=torch.float32, device=qkv.device)
         ext().fmha_bwd(qkv, ks, out, lse, dout, dqkv, dq_acc, dsum, heads, lq, causal, 0.0, error_word(qkv.device),
-                       ktail)
-        return dqkv, None, None, None, None, None
+                       ktail, kexcl)
+        return dqkv, None, None, None, None, None, None
 
 
 def suffix_attention(qkv: torch.Tensor, kstart: torch.Tensor, heads: int, lq: int, causal: bool = True,
-                     ktail: int = 0) -> torch.Tensor:
+                     ktail: int = 0, kexcl: int = 0) -> torch.Tensor:
     with trace_range("mdl.attention.suffix"):
         if qkv.is_cuda:
-            return SuffixAttentionFn.apply(qkv, kstart, heads, lq, causal, ktail)
-        return suffix_attention_reference(qkv, kstart, heads, lq, causal, ktail=ktail)
+            return SuffixAttentionFn.apply(qkv, kstart, heads, lq, causal, ktail, kexcl)
+        return suffix_attention_reference(qkv, kstart, heads, lq, causal, ktail=ktail, kexcl=kexcl)
 
 
 # ----------------------------------------------------------------------------- single-query attention

@@ -48,6 +48,46 @@ def test_suffix_attention_ktail_matches_longer_mask():
     torch.testing.assert_close(out[:, :R], o[:, G:], atol=1e-5, rtol=1e-4)
 
 
+def test_suffix_attention_kexcl_matches_request_candidate_split():
+    """ktail = G globals after the sequence, the last Gc of them excluded: equal to the
+    reference's two-part LONGER attention -- user globals and recent queries over
+    [user; sequence] (mixed mask), candidate globals over [candidate; user; sequence]."""
+
+    torch.manual_seed(1)
+    B, L, Gu, Gc, R, H = 2, 30, 2, 3, 10, 2
+    G, D, hd = Gu + Gc, 32 * H, 32
+    qkv = torch.randn(B, L + G, 3 * D)
+    ks = torch.tensor([0, 9])
+    out = suffix_attention_reference(qkv, ks, H, R + G, True, ktail=G, kexcl=Gc)
+
+    def heads(x, part):
+        return x[..., part * D:(part + 1) * D].reshape(x.shape[0], x.shape[1], H, hd).transpose(1, 2)
+
+    def attend(q_rows, k_rows, allowed):
+        q, k, v = heads(q_rows, 0), heads(k_rows, 1), heads(k_rows, 2)
+        s = (q @ k.transpose(-1, -2)) / hd ** 0.5
+        p = torch.nan_to_num(torch.softmax(s.masked_fill(~allowed.unsqueeze(1), float("-inf")), -1))
+        return (p @ v).transpose(1, 2).reshape(q_rows.shape[0], q_rows.shape[1], D)
+
+    seq, user, cand = qkv[:, :L], qkv[:, L:L + Gu], qkv[:, L + Gu:]
+    # request side: keys [user; sequence]
+    rk = torch.cat([user, seq], dim=1)
+    kpos = torch.arange(Gu + L)
+    kvalid = (kpos.view(1, -1) < Gu) | (kpos.view(1, -1) >= Gu + ks.view(-1, 1))
+    qpos = torch.arange(Gu + L - R, Gu + L)
+    rec_allowed = kvalid.unsqueeze(1) & (kpos.view(1, 1, -1) <= qpos.view(1, R, 1))
+    rec_allowed = rec_allowed & (qpos.view(1, R, 1) >= Gu + ks.view(-1, 1, 1))
+    o_user = attend(user, rk, kvalid.unsqueeze(1).expand(B, Gu, -1))
+    o_rec = attend(seq[:, L - R:], rk, rec_allowed)
+    # candidate side: keys [candidate; user; sequence], all valid keys
+    ck = torch.cat([cand, user, seq], dim=1)
+    cvalid = torch.cat([torch.ones(B, Gc, dtype=torch.bool), kvalid], dim=1)
+    o_cand = attend(cand, ck, cvalid.unsqueeze(1).expand(B, Gc, -1))
+    torch.testing.assert_close(out[:, :R], o_rec, atol=1e-5, rtol=1e-4)
+    torch.testing.assert_close(out[:, R:R + Gu], o_user, atol=1e-5, rtol=1e-4)
+    torch.testing.assert_close(out[:, R + Gu:], o_cand, atol=1e-5, rtol=1e-4)
+
+
 def test_suffix_attention_reference_matches_loop():
     B, Lk, Lq, H = 2, 20, 9, 2
     qkv, ks, _ = _case(B, Lk, Lq, H, [0, 6], True, "cpu")
@@ -78,6 +118,9 @@ CASES = [
     (1, 64, 40, 4, [0], True),              # shorter than one tile
     (2, 300, 280, 8, [0, 120], True, 1),    # LONGER cross block: 1 trailing global token
     (2, 433, 300, 4, [7, 200], True, 24),   # 24 trailing globals, padded prefixes
+    (2, 300, 280, 8, [0, 120], True, 6, 2),  # 6 globals, the last 2 (candidates) hidden from the others
+    (3, 433, 300, 4, [7, 200, 420], True, 24, 8),
+    (2, 40, 40, 2, [0, 12], True, 8, 3),    # LONGER self block: every token a query
 ]
 
 
@@ -86,13 +129,14 @@ CASES = [
 def test_fmha_forward_backward(case):
     B, Lk, Lq, H, kstart, causal = case[:6]
     ktail = case[6] if len(case) > 6 else 0
+    kexcl = case[7] if len(case) > 7 else 0
     qkv, ks, dout = _case(B, Lk, Lq, H, kstart, causal, "cuda")
     q1 = qkv.clone().requires_grad_(True)
-    out = suffix_attention(q1, ks, H, Lq, causal, ktail)
+    out = suffix_attention(q1, ks, H, Lq, causal, ktail, kexcl)
     out.backward(dout)
     torch.cuda.synchronize()
     q2 = qkv.float().clone().requires_grad_(True)
-    ref = suffix_attention_reference(q2, ks, H, Lq, causal, ktail=ktail)
+    ref = suffix_attention_reference(q2, ks, H, Lq, causal, ktail=ktail, kexcl=kexcl)
     ref.backward(dout.float())
     err = (out.float() - ref).abs().max().item()
     assert err < 2e-2, f"forward max error {err}"

@@ -102,3 +102,30 @@ def test_merged_longer_cuda_matches_cpu():
     torch.testing.assert_close(out_g["logits"].cpu(), out_c["logits"].detach(), atol=6e-2, rtol=6e-2)
     gc, gg = cpu_tr.dense.grad, gpu_tr.dense.grad.cpu()
     assert ((gc - gg).norm() / gc.norm()) < 0.08
+
+
+def test_request_side_outputs_do_not_depend_on_the_candidate():
+    """Candidate global tokens are seen by no other token: changing the candidate's
+    inputs changes only the candidate outputs (what makes the request side cacheable)."""
+
+    m, spec = scaled_config(5, 1e-4, num_fields=12, batch=16, seq_len=40, min_len=5, query_tokens=6,
+                            self_layers=2, d=16, heads=2, sequence_head="none", ns_tokens=4)
+    m["sequences"][0].update({"longer_candidate_global_tokens": 2})
+    m["model"].update({"token_dim": 16, "hidden_dim": 64, "task_head_hidden_dim": 32})
+    cfg = app_config_from_mapping(m)
+    torch.manual_seed(0)
+    model = build_model(cfg, device="cpu", base_seed=1)
+    enc = model.longer
+    assert enc.Gc == 2
+    B, L = 4, enc.L
+    torch.manual_seed(5)
+    tokens = torch.randn(B, L, enc.Din)
+    lengths = torch.tensor([40, 17, 3, 0])
+    k_in = enc.cand_mlp.k_in
+    t1, t2 = torch.randn(B, k_in), torch.randn(B, k_in)
+    u = torch.randn(B, enc.user_mlp.k_in) if enc.Gu else None
+    x1 = enc(None, lengths, t1, u, False, tokens=tokens)
+    x2 = enc(None, lengths, t2, u, False, tokens=tokens)
+    n_req = enc.R + enc.Gu + enc.Gx
+    torch.testing.assert_close(x1[:, :n_req], x2[:, :n_req])
+    assert (x1[:, n_req:] - x2[:, n_req:]).abs().max() > 1e-3
