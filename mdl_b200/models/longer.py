@@ -227,6 +227,36 @@ class LongerBlock(nn.Module):
         hn = F.layer_norm(h, (D,), self.lnf_w, self.lnf_b, self.eps)
         return h + F.gelu(hn @ self.w1.t() + self.b1) @ self.w2.t() + self.b2
 
+    def request_kv(self, X: torch.Tensor) -> torch.Tensor:
+        """fp32 K | V ``[B, Lk, 2d]`` of request-side tokens (cached for candidate queries)."""
+
+        xk = F.layer_norm(X.float(), (self.token_dim,), self.lnk_w, self.lnk_b, self.eps)
+        return xk @ self.wkv.float().t() + self.bkv
+
+    def candidate_forward(self, C: torch.Tensor, kv_req: torch.Tensor, kstart: torch.Tensor,
+                          heads: int) -> torch.Tensor:
+        """Candidate global tokens ``C [B, Gc, d]`` through the block: they attend to the
+        cached request-side keys ``kv_req [B, Lk, 2d]`` (key ``j`` valid from ``kstart``)
+        and to every candidate token; no request-side token sees them."""
+
+        B, Gc, D = C.shape
+        X = C.float()
+        hd = D // heads
+        xq = F.layer_norm(X, (D,), self.lnq_w, self.lnq_b, self.eps)
+        q = (xq @ self.wq.float().t() + self.bq).view(B, Gc, heads, hd).transpose(1, 2)
+        kv = torch.cat([kv_req.float(), self.request_kv(X)], dim=1)                     # [B, Lk + Gc, 2D]
+        Lk = kv.shape[1]
+        k = kv[..., :D].reshape(B, Lk, heads, hd).transpose(1, 2)
+        v = kv[..., D:].reshape(B, Lk, heads, hd).transpose(1, 2)
+        valid = torch.arange(Lk, device=X.device).view(1, Lk) >= kstart.to(X.device).long().view(B, 1)
+        valid[:, Lk - Gc:] = True
+        s = (q @ k.transpose(-1, -2)) / (hd ** 0.5)
+        s = s.masked_fill(~valid.view(B, 1, 1, Lk), float("-inf"))
+        att = (torch.softmax(s, dim=-1) @ v).transpose(1, 2).reshape(B, Gc, D)
+        h = X + att @ self.wo.float().t() + self.bo
+        hn = F.layer_norm(h, (D,), self.lnf_w, self.lnf_b, self.eps)
+        return h + F.gelu(hn @ self.w1.float().t() + self.b1) @ self.w2.float().t() + self.b2
+
     def forward(self, X, kstart, Lq, heads, causal, ktail, native: bool, kexcl: int = 0):
         if native:
             return LongerBlockFn.apply(X, kstart, self, Lq, heads, causal, ktail, kexcl)
@@ -416,6 +446,70 @@ class LongerEncoder(nn.Module):
             X = blk(X, kst, R + G, self.heads, True, G, native, kexcl=self.Gc)
         return X
 
+    def _request_tokens(self, tokens, lengths, user_in, cls_tokens, native: bool):
+        """Request-side rows ``[sequence; user; CLS]`` and their padding count."""
+
+        B, L, R = lengths.shape[0], self.L, self.R
+        kst = (L - lengths.clamp(0, L)).to(torch.int32)
+        if self.merge > 1 or len(self.inner):
+            tokens, kst = self.merge_tokens(tokens, kst, native)
+            L = tokens.shape[1]
+        if L < R:
+            tokens = F.pad(tokens, (0, 0, R - L, 0))
+            kst = kst + (R - L)
+            L = R
+        parts = [tokens.float()]
+        if self.Gu:
+            parts.append(self.user_mlp(user_in, native).float().view(B, self.Gu, self.D))
+        if self.Gx:
+            if cls_tokens is None:
+                raise ValueError("LONGER encoder built with extra global tokens needs cls_tokens")
+            parts.append(cls_tokens.float().expand(B, -1, -1))
+        return torch.cat(parts, dim=1), kst, L
+
+    @torch.no_grad()
+    def request_cache(self, lengths, user_in=None, *, seq_in=None, tokens=None, cls_tokens=None,
+                      native: bool = False) -> dict:
+        """Candidate-independent LONGER state of each request (reference
+        ``LongerSequenceEncoder.precompute_cache`` ``src/model.py:1632-1800``): per block the
+        fp32 K/V of its request-side keys and their padding count, and the request-side
+        outputs ``[recent; user; CLS]`` after the last block. Rows are requests."""
+
+        if tokens is None:
+            tokens = self.project(seq_in, lengths, native)
+        X, kst, L = self._request_tokens(tokens, lengths, user_in, cls_tokens, native)
+        R, Gr = self.R, self.Gu + self.Gx
+        kv, ksts = [], []
+        kv.append(self.cross.request_kv(X))
+        ksts.append(kst)
+        X = self.cross.forward_reference(X, kst, R + Gr, self.heads, True, Gr)
+        kst = (kst - (L - R)).clamp(min=0)
+        for blk in self.selfs:
+            kv.append(blk.request_kv(X))
+            ksts.append(kst)
+            X = blk.forward_reference(X, kst, R + Gr, self.heads, True, Gr)
+        return {"kv": kv, "kstart": ksts, "out": X, "lengths": lengths}
+
+    @torch.no_grad()
+    def forward_candidates(self, cache: dict, target_in, row_indices=None, native: bool = False) -> torch.Tensor:
+        """LONGER output ``[C, R + G, d]`` (order ``[recent; globals]``) of candidate rows whose
+        request is ``row_indices[c]`` (identity when None), from a ``request_cache``: only the
+        candidate global tokens run through the blocks, against the cached request keys
+        (reference ``LongerSequenceEncoder.forward`` with a cache ``src/model.py:2036-2296``)."""
+
+        out = cache["out"]
+        ri = (torch.arange(out.shape[0], device=out.device) if row_indices is None
+              else row_indices.to(out.device).long())
+        req = out.index_select(0, ri)
+        if not self.Gc:
+            return req
+        C = ri.shape[0]
+        c = self.cand_mlp(target_in, native).float().view(C, self.Gc, self.D)
+        blocks = [self.cross, *self.selfs]
+        for blk, kv, kst in zip(blocks, cache["kv"], cache["kstart"]):
+            c = blk.candidate_forward(c, kv.index_select(0, ri), kst.index_select(0, ri), self.heads)
+        return torch.cat([req, c], dim=1)
+
     @staticmethod
     def reference_order(X: torch.Tensor, G: int) -> torch.Tensor:
         """``[recent; globals]`` (here) -> ``[globals; recent]`` (reference output order)."""
@@ -502,6 +596,58 @@ class LongerModel(nn.Module):
         e = torch.arange(R + G, device=X.device)
         valid = (e.view(1, -1) >= (R - lengths.clamp(0, R)).view(-1, 1)) | (e.view(1, -1) >= R)
         return X, valid, feat_in, native
+
+    @torch.no_grad()
+    def precompute_request_cache(self, batch) -> dict:
+        """Request-side LONGER state of a batch's requests (reference
+        ``LongerModel.precompute_request_cache`` ``src/model.py:6596-6599``): one row per
+        request of the sequence payload (``row_indices`` maps candidates to requests; every
+        candidate row is its own request without it). User-global inputs are read from each
+        request's first candidate row."""
+
+        from ..ops.embedding import fused_lookup
+        from .features import lookup_sequence
+
+        native = batch.ids.is_cuda and self.config.runtime.kernel_backend == "native"
+        anchor = torch.zeros(0, device=batch.ids.device)
+        seq_in, lengths, ri = lookup_sequence(self.encoder, batch, self.seq.name, batch.rows, self.longer.L, anchor,
+                                              expand=False)
+        nreq = lengths.numel()
+        user_in = None
+        if self.has_user:
+            g = fused_lookup(self.store, self.encoder.domain_plan, batch.ids, batch.offsets, batch.dense,
+                             batch.rows, anchor)
+            kp = self.encoder.domain_k_pad
+            user_rows = g[:, (kp if self.has_target else 0):][:, :kp]
+            if ri is not None:
+                first = torch.full((nreq,), -1, dtype=torch.long, device=user_rows.device)
+                idx = torch.arange(ri.numel(), device=user_rows.device)
+                first.scatter_reduce_(0, ri.long().to(user_rows.device), idx, reduce="amin", include_self=False)
+                user_rows = user_rows.index_select(0, first.clamp(min=0))
+            user_in = user_rows
+        return self.longer.request_cache(lengths.to(seq_in.device), user_in, seq_in=seq_in, native=native)
+
+    @torch.no_grad()
+    def forward_with_cache(self, batch, request_cache: dict) -> torch.Tensor:
+        """Logits ``[rows, tasks]`` of a candidate batch from a request cache: only the
+        candidate global tokens (and the heads) are computed per candidate."""
+
+        from ..ops.embedding import fused_lookup
+
+        if self.mix:
+            raise NotImplementedError("request caches cover the flattened LONGER readout (sequence_head: none)")
+        native = batch.ids.is_cuda and self.config.runtime.kernel_backend == "native"
+        anchor = torch.zeros(0, device=batch.ids.device)
+        target_in = None
+        if self.has_target:
+            g = fused_lookup(self.store, self.encoder.domain_plan, batch.ids, batch.offsets, batch.dense,
+                             batch.rows, anchor)
+            target_in = g[:, :self.encoder.domain_k_pad]
+        ri = (batch.sequences.get(self.seq.name) or {}).get("row_indices")
+        X = self.longer.forward_candidates(request_cache, target_in, ri, native)
+        readout = LongerEncoder.reference_order(X, self.longer.G).reshape(batch.rows, -1).contiguous()
+        scale = torch.ones(self.ntask, device=readout.device)
+        return self.heads_mod.forward_shared(readout.float(), None, None, scale)["logits"]
 
     def forward(self, batch, task_scale: torch.Tensor | None = None) -> dict[str, torch.Tensor]:
         X, valid, feat_in, native = self.encode(batch)

@@ -129,3 +129,35 @@ def test_request_side_outputs_do_not_depend_on_the_candidate():
     n_req = enc.R + enc.Gu + enc.Gx
     torch.testing.assert_close(x1[:, :n_req], x2[:, :n_req])
     assert (x1[:, n_req:] - x2[:, n_req:]).abs().max() > 1e-3
+
+
+@pytest.mark.parametrize("merge,inner,cand", [(1, 0, 1), (2, 1, 2)])
+def test_request_cache_matches_full_forward(merge, inner, cand):
+    """Scoring candidates from a request cache gives the full forward's logits: requests
+    shared by several candidates (request-level batching), candidate features per row."""
+
+    m, spec = scaled_config(5, 1e-4, num_fields=12, batch=24, seq_len=40, min_len=5, query_tokens=6,
+                            self_layers=2, d=8, heads=2, sequence_head="none", ns_tokens=4)
+    m["sequences"][0].update({"longer_candidate_global_tokens": cand, "longer_token_merge": merge,
+                              "longer_inner_layers": inner})
+    m["model"].update({"token_dim": 16, "hidden_dim": 64, "task_head_hidden_dim": 32})
+    cfg = app_config_from_mapping(m)
+    torch.manual_seed(0)
+    model = build_model(cfg, device="cpu", base_seed=1)
+    model.eval()
+    batch = SyntheticGenerator(model.encoder.batch_plan, spec).batch(24)
+    seq = batch.sequences["behavior"]
+    # three requests of eight candidates each: candidates share their request's events
+    ri = torch.arange(24) // 8
+    L = cfg.sequences[0].max_length
+    ids = seq["ids"].view(seq["ids"].shape[0], 24, L)[:, ::8].reshape(seq["ids"].shape[0], 3 * L)
+    req = {"ids": ids, "lengths": seq["lengths"][::8].clone(), "row_indices": ri}
+    from dataclasses import replace
+
+    rb = replace(batch, sequences={**batch.sequences, "behavior": req})
+    with torch.no_grad():
+        full = model(rb)["logits"]
+        cache = model.precompute_request_cache(rb)
+        assert cache["out"].shape[0] == 3
+        cached = model.forward_with_cache(rb, cache)
+    torch.testing.assert_close(cached, full.float(), atol=1e-4, rtol=1e-4)
