@@ -249,13 +249,10 @@ class SequenceSummaries(nn.Module):
                 out[name] = mod(seq_in, lengths, group(ti), ri)
             elif kind == "longer":
                 out[name] = mod(seq_in, lengths, group(ti), group(ui), native, ri)
-            else:  # stca
-                from .features import expand_requests
-
-                hist = expand_requests(mod.step(seq_in, native).view(lengths.shape[0], L, -1), ri)
+            else:  # stca: history projection and per-layer transforms once per request
+                hist = mod.step(seq_in, native).view(lengths.shape[0], L, -1)
                 target = mod.target(group(ti), native)
-                valid = expand_requests(valid_mask(lengths, L), ri)
-                out[name] = mod.encoder(hist, valid, target, native).float()
+                out[name] = mod.encoder(hist, valid_mask(lengths, L), target, native, row_indices=ri).float()
         return out
 
 

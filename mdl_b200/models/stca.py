@@ -95,11 +95,28 @@ class STCAEncoder(nn.Module):
         _linear_init(self.final_proj.data)
         self.final_ffn = _SwiGLU(dim, ratio * dim, device=device)
 
-    def forward(self, history: torch.Tensor, valid: torch.Tensor, target: torch.Tensor, native: bool) -> torch.Tensor:
+    def transform_histories(self, history: torch.Tensor, native: bool) -> list[torch.Tensor]:
+        """Every layer's transformed history ``LN_i(SwiGLU_i(X))``: candidate-independent, so
+        computed once per request (reference ``STCASequenceCache`` ``src/modules/stca.py:28-44``)."""
+
+        return [layer.transform(history, native) for layer in self.layers]
+
+    def forward(self, history: torch.Tensor | None, valid: torch.Tensor, target: torch.Tensor, native: bool,
+                row_indices: torch.Tensor | None = None,
+                transformed: list[torch.Tensor] | None = None) -> torch.Tensor:
+        """``history [R, L, d]`` / ``valid [R, L]`` per request (or per row), ``target [B, d]`` per
+        candidate row; ``row_indices [B]`` maps candidates to requests (request-level
+        batching: the history transforms run once per request). ``transformed`` replaces
+        ``history`` with cached ``transform_histories`` output."""
+
+        hs = transformed if transformed is not None else self.transform_histories(history, native)
+        if row_indices is not None:
+            ri = row_indices.to(valid.device).long()
+            valid = valid.index_select(0, ri)
         outs: list[torch.Tensor] = []
         q = self.layers[0].transform(target, native)
         for i, layer in enumerate(self.layers):
-            hist = layer.transform(history, native)
+            hist = hs[i] if row_indices is None else hs[i].index_select(0, ri.to(hs[i].device))
             outs.append(layer.attend(q, hist, valid, native).to(target.dtype))
             if i + 1 < self.M:
                 fused = linear_nb(torch.cat([*outs, target], dim=-1), self.fusion[i], native)
