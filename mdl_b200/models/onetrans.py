@@ -367,6 +367,8 @@ def _mixed_reference(x, s, w_s, b_s, w_ns, b_ns):
     """fp32: rows < s with the shared weight, rows >= s with their own."""
 
     ys = x[:, :s] @ w_s.t() + b_s
+    if x.shape[1] == s:  # S rows only (the request side of a request cache)
+        return ys
     yn = torch.einsum("bnk,nok->bno", x[:, s:], w_ns) + b_ns.unsqueeze(0)
     return torch.cat([ys, yn], dim=1)
 
@@ -670,6 +672,86 @@ class OneTransModel(nn.Module):
             ks = (ks - (s_in - q)).clamp(min=0)
             s_in = q
         return self._task_logits(X[:, s_in:, :], batch, task_scale)
+
+    # ------------------------------------------------------------------ request cache
+    @torch.no_grad()
+    def precompute_request_cache(self, batch) -> dict:
+        """Candidate-independent OneTrans state per request (reference
+        ``OneTransBackbone.precompute_request_cache`` ``src/model.py:6200-6398``). S tokens
+        precede the NS tokens and the attention is causal, so every S token's output is
+        independent of the candidate: per layer the cache keeps the K/V of the layer's S
+        keys and their padding count; candidates then run only their NS tokens. Rows are the
+        requests of the sequence payload (``row_indices``; one per row without it)."""
+
+        from .features import lookup_sequence
+
+        if self.multi:
+            raise NotImplementedError("OneTrans request cache: one sequence token group")
+        anchor = torch.zeros(0, device=batch.ids.device)
+        L, D = self.L, self.token_dim
+        seq_in, lengths, _ri = lookup_sequence(self.encoder, batch, self.seq.name, batch.rows, L, anchor,
+                                               expand=False)
+        R = lengths.numel()
+        ks = (L - lengths.to(seq_in.device).long().clamp(0, L))
+        x = F.gelu(seq_in.float()[:, :self.Ks_log] @ self.seq_w1[:, :self.Ks_log].t() + self.seq_b1)
+        S = (x @ self.seq_w2.t() + self.seq_b2).view(R, L, D)
+        e = torch.arange(L, device=S.device)
+        valid = e.view(1, -1) >= ks.view(-1, 1)
+        S = S + self.pos[(e.view(1, -1) - ks.view(-1, 1)).clamp(min=0)] * valid.unsqueeze(-1)
+        layers, s_in, kst = [], L, ks
+        for i, layer in enumerate(self.layers):
+            q = self.query_counts[i]
+            xn = _rms_reference(S, layer.norm1, self.eps)
+            kv = xn @ layer.wqkv_s[D:].t() + layer.bqkv_s[D:]                   # [R, s_in, 2D]
+            layers.append((kv, kst))
+            S = layer.forward_reference(S, kst, s_in, q, self.attn_heads, self.eps)  # S-only: q outputs
+            kst = (kst - (s_in - q)).clamp(min=0)
+            s_in = q
+        return {"layers": layers, "kstart": ks, "lengths": lengths}
+
+    @torch.no_grad()
+    def forward_with_cache(self, batch, request_cache: dict) -> torch.Tensor:
+        """Logits ``[rows, tasks]`` of candidate rows from a request cache: the NS tokens
+        attend to their request's cached S keys (valid from the cached padding count) and
+        causally to each other; the per-NS-token projections and FFNs run per candidate."""
+
+        from ..ops.embedding import fused_lookup
+
+        anchor = torch.zeros(0, device=batch.ids.device)
+        B, L, D, N, H = batch.rows, self.L, self.token_dim, self.num_ns, self.attn_heads
+        plan = self.encoder.domain_plan if self.ns_mode == "groupwise" else self.encoder.plan
+        ns_in = fused_lookup(self.store, plan, batch.ids, batch.offsets, batch.dense, B, anchor).float()
+        ri = (batch.sequences.get(self.seq.name) or {}).get("row_indices")
+        ri = (torch.arange(B, device=ns_in.device) if ri is None else ri.to(ns_in.device).long())
+        if self.ns_mode == "auto_split":
+            v = F.gelu(ns_in[:, :self.Kn_log] @ self.ns_w1[:, :self.Kn_log].t() + self.ns_b1)
+            X = (v @ self.ns_w2.t() + self.ns_b2).view(B, N, D)
+        else:
+            X = self.ns_tokens(ns_in).float().view(B, N, D)
+        ks0 = request_cache["kstart"].index_select(0, ri)
+        X = X + self.pos[(L + torch.arange(N, device=X.device).view(1, -1) - ks0.view(-1, 1)).clamp(min=0)]
+        hd = D // H
+        causal = torch.ones(N, N, dtype=torch.bool, device=X.device).tril()
+        for layer, (kv_s, kst) in zip(self.layers, request_cache["layers"]):
+            xn = _rms_reference(X, layer.norm1, self.eps)
+            qkv = torch.einsum("bnk,nok->bno", xn, layer.wqkv_ns) + layer.bqkv_ns.unsqueeze(0)   # [B, N, 3D]
+            kv = torch.cat([kv_s.index_select(0, ri), qkv[..., D:]], dim=1)                    # [B, s + N, 2D]
+            s_in = kv_s.shape[1]
+            k = kv[..., :D].reshape(B, s_in + N, H, hd).transpose(1, 2)
+            v = kv[..., D:].reshape(B, s_in + N, H, hd).transpose(1, 2)
+            qh = qkv[..., :D].reshape(B, N, H, hd).transpose(1, 2)
+            s_ok = torch.arange(s_in, device=X.device).view(1, 1, s_in) >= kst.index_select(0, ri).view(B, 1, 1)
+            allowed = torch.cat([s_ok.expand(B, N, s_in), causal.view(1, N, N).expand(B, N, N)], dim=2)
+            sc = (qh @ k.transpose(-1, -2)) / math.sqrt(hd)
+            att = torch.softmax(sc.masked_fill(~allowed.unsqueeze(1), float("-inf")), -1) @ v
+            h = X + att.transpose(1, 2).reshape(B, N, D) @ layer.wo.t() + layer.bo
+            hn = _rms_reference(h, layer.norm2, self.eps)
+            u = F.gelu(torch.einsum("bnk,nok->bno", hn, layer.w1_ns) + layer.b1_ns.unsqueeze(0))
+            X = h + torch.einsum("bnk,nok->bno", u, layer.w2_ns) + layer.b2_ns.unsqueeze(0)
+        scale = torch.ones(self.ntask, device=X.device)
+        from types import SimpleNamespace
+
+        return self._task_logits(X, SimpleNamespace(labels=None, label_mask=None), scale)["logits"]
 
     # ------------------------------------------------------------------ reference layout
     def reference_state_dict(self) -> dict[str, torch.Tensor]:

@@ -364,3 +364,35 @@ def test_sequence_truncation_layout(trunc, order, expect):
     flat = col.values.to_numpy()
     got = [[int(flat[p]) if p >= 0 else 0 for p in row] for row in pos]
     assert got == expect and keep.tolist() == [2, 4]
+
+
+@pytest.mark.parametrize("ns_mode", ["auto_split", "dcnv2"])
+def test_request_cache_matches_full_forward(ns_mode):
+    """NS tokens scored against a request cache of the S-token keys give the full
+    forward's logits (pyramid layers, padded sequences, requests shared by candidates)."""
+
+    from dataclasses import replace
+
+    cfg, spec = _small(seq_len=40, layers=3, min_len=3)
+    if ns_mode != "auto_split":
+        m, spec = scaled_config(4, 1e-4, num_fields=12, batch=64, seq_len=40, num_layers=3, pyramid_schedule="halve")
+        m["model"].update({"hidden_dim": 128, "token_dim": 64, "num_heads": 2, "num_ns_tokens": 4,
+                           "task_head_hidden_dim": 64, "pyramid_round_to": 8, "ns_tokenizer": ns_mode})
+        spec.sequences["behavior"].min_len = 3
+        cfg = app_config_from_mapping(m)
+    torch.manual_seed(0)
+    model = build_model(cfg, device="cpu", base_seed=1)
+    model.eval()
+    batch = SyntheticGenerator(model.encoder.batch_plan, spec).batch(24)
+    seq = batch.sequences["behavior"]
+    L = cfg.sequences[0].max_length
+    nf = seq["ids"].shape[0]
+    req = {"ids": seq["ids"].view(nf, 24, L)[:, ::6].reshape(nf, 4 * L), "lengths": seq["lengths"][::6].clone(),
+           "row_indices": torch.arange(24) // 6}
+    rb = replace(batch, sequences={**batch.sequences, "behavior": req})
+    with torch.no_grad():
+        full = model(rb)["logits"].float()
+        cache = model.precompute_request_cache(rb)
+        cached = model.forward_with_cache(rb, cache)
+    assert len(cache["layers"]) == 3 and cache["layers"][0][0].shape[0] == 4
+    torch.testing.assert_close(cached, full, atol=1e-4, rtol=1e-4)
