@@ -163,7 +163,7 @@ def _batches(config, model, rank, world, *, split="train", synthetic=False, batc
                                     seed=r.shuffle_seed, prefetch=r.prefetch_batches, loop=loop and split == "train",
                                     pin=r.pin_memory, io_policy=RemoteIoPolicy.from_reader(r),
                                     length_buckets=[(b.max_length, b.batch_size) for b in r.length_buckets],
-                                    length_bucket_metric=r.length_bucket_metric)
+                                    length_bucket_metric=r.length_bucket_metric, overlap=r.overlap_host_prepare)
     seqs = [s for s in config.sequences if s.name in getattr(model.encoder, "seq_plans", {})]
     gen = SyntheticGenerator(model.encoder.batch_plan,
                              synthetic_spec_from_config(config, model.encoder.batch_plan, sequences=seqs), rank=rank)
@@ -372,6 +372,9 @@ def cmd_train(args, argv) -> int:
                 batch = batch.to(device, non_blocking=True)
             res = abort_on_cuda_oom(trainer.train_step, batch)
             step = trainer.step_index
+            schedule = getattr(batches, "schedule_next", None)
+            if schedule is not None:  # same-thread prepare while the device runs the step
+                schedule()
             dog.beat("step", step)
             if step % args.log_every == 0 and rank == 0:
                 last = float(res.loss)

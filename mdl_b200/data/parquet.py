@@ -491,7 +491,7 @@ class ParquetBatchIterator:
                  world: int = 1, shard_unit: str = "row_group", shuffle_rows: int = 0, seed: int = 0,
                  drop_last: bool = True, prefetch: int = 2, pin: bool = False, start_position: int = 0,
                  loop: bool = False, io_policy=None, length_buckets: Sequence = (),
-                 length_bucket_metric: str = "max", adapter=None) -> None:
+                 length_bucket_metric: str = "max", adapter=None, overlap: bool = True) -> None:
         """``length_buckets``: ``(max_length or None, batch_size)`` pairs in increasing
         length order (the last may be the catch-all ``None``): rows are grouped by their
         sequence work (``Tensorizer.sequence_lengths``) and each bucket yields batches of
@@ -511,6 +511,10 @@ class ParquetBatchIterator:
         self.shuffle_rows = shuffle_rows
         self.rng = np.random.default_rng([seed, rank])
         self.drop_last = drop_last
+        # prefetch = 0: batches are prepared on the consuming thread (``overlap``: scheduled
+        # by ``OverlappedPrepareIterator.schedule_next`` between steps)
+        self.prefetch_thread = prefetch > 0
+        self.overlap = overlap
         self.prefetch = max(1, prefetch)
         self.pin = pin
         self.position = start_position
@@ -605,9 +609,20 @@ class ParquetBatchIterator:
             self._q.put(error)
 
     def __iter__(self) -> Iterator[PackedBatch]:
+        if self.prefetch_thread is False:
+            # no background thread: the caller's thread prepares every batch, and with
+            # ``overlap`` it does so when the training loop calls ``schedule_next`` right
+            # after launching a step (the device drains the step meanwhile)
+            it = OverlappedPrepareIterator(self._batches())
+            if not self.overlap:
+                return iter(it)
+            return it
         self._stop.clear()
         self._thread = threading.Thread(target=self._worker, daemon=True)
         self._thread.start()
+        return self._threaded()
+
+    def _threaded(self) -> Iterator[PackedBatch]:
         while True:
             item = self._q.get()
             if isinstance(item, StopIteration):
@@ -625,6 +640,51 @@ class ParquetBatchIterator:
                 pass
             self._thread.join(timeout=0.1)
         self._thread = None
+
+
+class OverlappedPrepareIterator:
+    """Same-thread batch preparation (reference ``_OverlappedHostPrepareIterator``
+    ``src/train.py:4360-4440``): ``next`` returns the batch prepared ahead, or prepares one
+    now; ``schedule_next`` prepares the following batch, and the training loop calls it
+    right after launching a step, so the Parquet read and tensorisation run on the
+    training thread while the device works through the step -- no second Python thread
+    contending for the interpreter lock with the step's launches."""
+
+    def __init__(self, batches) -> None:
+        self._gen = iter(batches)
+        self._ready = None
+        self._done = False
+        self.prepared_ahead = 0
+
+    def __iter__(self) -> "OverlappedPrepareIterator":
+        return self
+
+    def __next__(self) -> PackedBatch:
+        if self._ready is None:
+            self._advance()
+        else:
+            self.prepared_ahead += 1
+        if self._ready is None:
+            raise StopIteration
+        b, self._ready = self._ready, None
+        return b
+
+    def _advance(self) -> None:
+        if self._done:
+            return
+        try:
+            self._ready = next(self._gen)
+        except StopIteration:
+            self._done = True
+
+    def schedule_next(self) -> None:
+        if self._ready is None:
+            self._advance()
+
+    def close(self) -> None:
+        close = getattr(self._gen, "close", None)
+        if close is not None:
+            close()
 
 
 class DevicePrefetcher:

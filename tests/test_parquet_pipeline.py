@@ -41,6 +41,29 @@ def test_round_trip(tmp_path):
         torch.testing.assert_close(a.labels, b.labels)
 
 
+def test_same_thread_overlapped_prepare(tmp_path):
+    """prefetch 0: batches prepared on the consuming thread; ``schedule_next`` prepares the
+    next one between steps (overlap), and the batches equal the threaded reader's."""
+
+    from mdl_b200.data.parquet import OverlappedPrepareIterator
+
+    cfg, model, batches = _setup(tmp_path)
+    paths = discover_parquet_inputs([str(tmp_path)])
+    tz = Tensorizer(cfg, model.encoder.batch_plan)
+    threaded = list(ParquetBatchIterator(paths, tz, 256, prefetch=2))
+    it = iter(ParquetBatchIterator(paths, tz, 256, prefetch=0))
+    assert isinstance(it, OverlappedPrepareIterator)
+    got = []
+    for b in it:
+        got.append(b)
+        it.schedule_next()  # what the training loop does after launching a step
+    assert it.prepared_ahead == 2 and len(got) == 3
+    for a, b in zip(got, threaded):
+        assert torch.equal(a.ids, b.ids) and torch.equal(a.offsets, b.offsets)
+    plain = list(ParquetBatchIterator(paths, tz, 256, prefetch=0, overlap=False))
+    assert len(plain) == 3 and torch.equal(plain[0].ids, threaded[0].ids)
+
+
 def test_row_group_sharding_covers_everything_once(tmp_path):
     _setup(tmp_path, n_files=4)
     paths = discover_parquet_inputs([str(tmp_path / "*.parquet")])
