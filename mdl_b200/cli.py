@@ -269,6 +269,70 @@ def cmd_audit_cardinality(args) -> int:
     return 0 if out["passed"] or not args.strict else 3
 
 
+def cmd_profile_data(args) -> int:
+    from .data.parquet import discover_parquet_inputs
+    from .data.profile import profile_parquet
+
+    cfg = load_cli_config(args)
+    sp = getattr(cfg.data, args.split) or cfg.data.train
+    out = profile_parquet(cfg, discover_parquet_inputs(args.inputs or sp.inputs), max_rows=args.max_rows)
+    text = json.dumps(out, indent=1)
+    if args.out:
+        with open(args.out, "w", encoding="utf-8") as fh:
+            fh.write(text)
+    print(json.dumps({"rows": out["rows"], "features": len(out["features"]), "out": args.out}))
+    return 0
+
+
+def cmd_recommend(args) -> int:
+    from .data.profile import recommend_encodings, recommend_shapes
+
+    def load(path):
+        with open(path, encoding="utf-8") as fh:
+            return json.load(fh)
+
+    if args.command == "recommend-shapes":
+        out = recommend_shapes(load(args.small), load(args.large), horizon_rows=args.horizon_rows, load=args.load,
+                               min_dim=args.min_dim, max_dim=args.max_dim)
+    else:
+        out = recommend_encodings(load(args.profile), bits=args.bits)
+    print(json.dumps(out))
+    return 0
+
+
+def cmd_tune_batch_size(args) -> int:
+    import dataclasses
+
+    import torch
+
+    from .benchmark.tools import tune_batch_size
+
+    cfg0 = load_cli_config(args)
+    rank, world, device = _setup_runtime(cfg0)
+    if world != 1:
+        raise SystemExit("tune-batch-size runs on one device")
+
+    def build(b):
+        cfg = dataclasses.replace(cfg0, training=dataclasses.replace(cfg0.training, batch_size=b))
+        model, trainer = _build(cfg, 0, 1, device)
+        return cfg, model, trainer, iter(_batches(cfg, model, 0, 1, synthetic=True))
+
+    out = tune_batch_size(build, args.batch_sizes, steps=args.steps, warmup=args.warmup, device=device,
+                          memory_fraction=args.memory_fraction)
+    print(json.dumps(out))
+    if device.type == "cuda":
+        torch.cuda.synchronize(device)
+    return 0
+
+
+def cmd_summarize_benchmarks(args) -> int:
+    from .benchmark.tools import load_reports, markdown, summarize_benchmarks
+
+    summary = summarize_benchmarks(load_reports(args.files))
+    print(markdown(summary) if args.markdown else json.dumps(summary))
+    return 0
+
+
 def cmd_check_store(args) -> int:
     from .checkpoint import latest_committed_checkpoint, open_checkpoint_store
 
@@ -553,6 +617,31 @@ def build_parser() -> argparse.ArgumentParser:
     p = sub.add_parser("check-checkpoint-store")
     p.add_argument("--checkpoint-dir", required=True)
     p.add_argument("--probe-mib", type=int, default=8)
+    p = sub.add_parser("profile-data", help="categorical profile of Parquet inputs (distinct values, collisions)")
+    _add_config(p)
+    p.add_argument("--split", choices=["train", "test"], default="train")
+    p.add_argument("--inputs", nargs="*")
+    p.add_argument("--max-rows", type=int, default=1_000_000)
+    p.add_argument("--out")
+    p = sub.add_parser("recommend-shapes", help="embedding table sizes / widths from two nested-prefix profiles")
+    p.add_argument("--small", required=True)
+    p.add_argument("--large", required=True)
+    p.add_argument("--horizon-rows", type=int, required=True)
+    p.add_argument("--load", type=float, default=0.5)
+    p.add_argument("--min-dim", type=int, default=8)
+    p.add_argument("--max-dim", type=int, default=128)
+    p = sub.add_parser("recommend-encodings", help="per-feature categorical encoding from a profile")
+    p.add_argument("--profile", required=True)
+    p.add_argument("--bits", type=int, default=20)
+    p = sub.add_parser("tune-batch-size", help="compute-mode throughput and peak memory per batch size")
+    _add_config(p)
+    p.add_argument("--batch-sizes", type=int, nargs="+", required=True)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--memory-fraction", type=float, default=0.9)
+    p = sub.add_parser("summarize-benchmarks", help="group benchmark JSON lines; weak-scaling efficiency")
+    p.add_argument("files", nargs="+")
+    p.add_argument("--markdown", action="store_true")
     for name in ("train", "benchmark", "evaluate", "predict"):
         p = sub.add_parser(name)
         _add_config(p)
@@ -626,6 +715,14 @@ def _dispatch(argv=None) -> int:
         return cmd_check_store(args)
     if cmd == "audit-cardinality":
         return cmd_audit_cardinality(args)
+    if cmd == "profile-data":
+        return cmd_profile_data(args)
+    if cmd in ("recommend-shapes", "recommend-encodings"):
+        return cmd_recommend(args)
+    if cmd == "tune-batch-size":
+        return cmd_tune_batch_size(args)
+    if cmd == "summarize-benchmarks":
+        return cmd_summarize_benchmarks(args)
     if cmd == "train":
         return cmd_train(args, argv)
     if cmd == "benchmark":
