@@ -1,0 +1,354 @@
+// Suffix attention for small head widths (8, 16; also 64) on the CUDA cores.
+//
+// Same contract as the tcgen05 flash attention (fmha.h): qkv [B, Lk, 3*D] bf16 with
+// D = H * HD, the queries are the last Lq tokens, key j is visible to query row p iff
+// kstart[b] <= j and (!causal or j <= p or j >= Lk - ktail or p >= Lk - ktail) and
+// (j < Lk - kexcl or p >= Lk - kexcl); query rows before kstart[b] output zero. It
+// serves the head widths the tensor-core kernel does not take -- the reference's
+// production LONGER encoders run 32-wide tokens over 4 heads (head width 8) -- where an
+// MMA tile would be mostly padding.
+//
+// Forward: a thread owns one query row of one head (128 rows per CTA); the CTA stages
+// 64-key tiles of K and V (fp32) in shared memory and every thread runs an online
+// softmax in base 2 over 16-key chunks (one rescale per chunk). Causal CTAs stop at their
+// last query row and then visit only the trailing always-visible tokens.
+// Backward (three launches): D_q = dO . O per query; dQ with a thread per query row
+// (recomputing P from the saved log-sum-exp); dK and dV with a thread per key row over
+// staged query tiles. Every element of dqkv is written by exactly one thread (no
+// atomics); Q rows that are not queries get zero.
+#include "attn_simt.h"
+
+#include <cuda_bf16.h>
+#include <math_constants.h>
+
+namespace mdl {
+namespace {
+
+constexpr int kRows = 128;   // query (forward, dQ) or key (dK/dV) rows per CTA
+constexpr int kTile = 64;    // staged rows of the other side
+// keys per online-softmax rescale (fewer for wide heads, whose accumulators fill the registers)
+template <int HD>
+__host__ __device__ constexpr int chunk_of() { return HD >= 64 ? 4 : 16; }
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct Vis {
+  int Lk, Lq, kst, causal, tail0, excl0;
+  __device__ __forceinline__ bool operator()(int p, int j) const {
+    return j >= kst && (!causal || j <= p || j >= tail0 || p >= tail0) && (j < excl0 || p >= excl0);
+  }
+};
+
+__device__ __forceinline__ Vis make_vis(const AttnSimtArgs& a, int b) {
+  Vis v;
+  v.Lk = a.Lk;
+  v.Lq = a.Lq;
+  int k = a.kstart[b];
+  v.kst = k < 0 ? 0 : (k > a.Lk ? a.Lk : k);
+  v.causal = a.causal;
+  v.tail0 = a.causal ? a.Lk - a.ktail : a.Lk;
+  v.excl0 = a.causal ? a.Lk - a.kexcl : a.Lk;
+  return v;
+}
+
+// Rows [lo, hi) of head h's K (part 1) or V (part 2), or Q (part 0), as fp32 into s[kTile][HD].
+template <int HD>
+__device__ __forceinline__ void stage(float (*s)[HD], const __nv_bfloat16* base, long long row_stride, int col0,
+                                      int lo, int hi) {
+  for (int i = threadIdx.x; i < kTile * HD; i += blockDim.x) {
+    const int r = i / HD, c = i % HD;
+    const int j = lo + r;
+    s[r][c] = j < hi ? __bfloat162float(base[static_cast<long long>(j) * row_stride + col0 + c]) : 0.f;
+  }
+}
+
+// Grid: x = sample * row blocks + row block (samples can exceed the 65535 limit of y / z), y = head.
+__device__ __forceinline__ void block_coords(int rows, int& b, int& blk) {
+  const int nblk = (rows + kRows - 1) / kRows;
+  b = static_cast<int>(blockIdx.x / nblk);
+  blk = static_cast<int>(blockIdx.x - static_cast<unsigned>(b) * nblk);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kRows) attn_simt_fwd_kernel(AttnSimtArgs a) {
+  __shared__ float sK[kTile][HD];
+  __shared__ float sV[kTile][HD];
+  int b, blk;
+  block_coords(a.Lq, b, blk);
+  const int h = blockIdx.y;
+  const int qi = blk * kRows + threadIdx.x;
+  const int D = a.H * HD;
+  const long long rs = 3LL * D;
+  const __nv_bfloat16* base = a.qkv + static_cast<long long>(b) * a.Lk * rs;
+  const Vis vis = make_vis(a, b);
+  const int p = a.Lk - a.Lq + qi;
+  const bool qvalid = qi < a.Lq && p >= vis.kst;
+  float q[HD], o[HD];
+#pragma unroll
+  for (int d = 0; d < HD; ++d) {
+    q[d] = qvalid ? __bfloat162float(base[static_cast<long long>(p) * rs + h * HD + d]) * a.scale * kLog2e : 0.f;
+    o[d] = 0.f;
+  }
+  float m = -CUDART_INF_F, l = 0.f;
+  // key ranges: [kst, hi) and, for causal CTAs, the trailing tokens after hi
+  const int last_p = a.Lk - a.Lq + min(a.Lq, (blk + 1) * kRows) - 1;
+  const int hi = a.causal ? min(a.Lk, last_p + 1) : a.Lk;
+  const int tail_lo = a.causal ? max(hi, vis.tail0) : a.Lk;
+  for (int range = 0; range < 2; ++range) {
+    const int r0 = range == 0 ? vis.kst : max(tail_lo, vis.kst);
+    const int r1 = range == 0 ? hi : a.Lk;
+    for (int j0 = r0; j0 < r1; j0 += kTile) {
+      __syncthreads();
+      stage<HD>(sK, base, rs, D + h * HD, j0, r1);
+      stage<HD>(sV, base, rs, 2 * D + h * HD, j0, r1);
+      __syncthreads();
+      if (!qvalid) continue;
+      const int n = min(kTile, r1 - j0);
+      constexpr int kChunk = chunk_of<HD>();
+      for (int c0 = 0; c0 < n; c0 += kChunk) {
+        float s[kChunk];
+        float mc = m;
+#pragma unroll
+        for (int u = 0; u < kChunk; ++u) {
+          const int jj = c0 + u;
+          float t = -CUDART_INF_F;
+          if (jj < n && vis(p, j0 + jj)) {
+            t = 0.f;
+#pragma unroll
+            for (int d = 0; d < HD; ++d) t = fmaf(q[d], sK[jj][d], t);
+          }
+          s[u] = t;
+          mc = fmaxf(mc, t);
+        }
+        if (mc == -CUDART_INF_F) continue;  // nothing visible in this chunk yet
+        const float corr = exp2f(m - mc);   // 0 when m = -inf
+        l *= corr;
+#pragma unroll
+        for (int d = 0; d < HD; ++d) o[d] *= corr;
+#pragma unroll
+        for (int u = 0; u < kChunk; ++u) {
+          if (s[u] == -CUDART_INF_F) continue;
+          const float pr = exp2f(s[u] - mc);
+          l += pr;
+#pragma unroll
+          for (int d = 0; d < HD; ++d) o[d] = fmaf(pr, sV[c0 + u][d], o[d]);
+        }
+        m = mc;
+      }
+    }
+  }
+  if (qi >= a.Lq) return;
+  const bool any = qvalid && l > 0.f;
+  const float inv = any ? 1.f / l : 0.f;
+  __nv_bfloat16* out = a.out + (static_cast<long long>(b) * a.Lq + qi) * D + h * HD;
+#pragma unroll
+  for (int d = 0; d < HD; ++d) out[d] = __float2bfloat16(o[d] * inv);
+  a.lse[(static_cast<long long>(b) * a.H + h) * a.Lq + qi] = any ? m + log2f(l) : CUDART_INF_F;
+}
+
+// D_q = sum_d dO[q, d] * O[q, d] per (b, h, q).
+template <int HD>
+__global__ void attn_simt_dsum_kernel(AttnSimtArgs a) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long total = static_cast<long long>(a.B) * a.H * a.Lq;
+  if (i >= total) return;
+  const int qi = static_cast<int>(i % a.Lq);
+  const long long bh = i / a.Lq;
+  const int h = static_cast<int>(bh % a.H), b = static_cast<int>(bh / a.H);
+  const long long off = (static_cast<long long>(b) * a.Lq + qi) * a.H * HD + h * HD;
+  float s = 0.f;
+#pragma unroll
+  for (int d = 0; d < HD; ++d) s = fmaf(__bfloat162float(a.dout[off + d]), __bfloat162float(a.out[off + d]), s);
+  a.dsum[i] = s;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kRows) attn_simt_dq_kernel(AttnSimtArgs a) {
+  __shared__ float sK[kTile][HD];
+  __shared__ float sV[kTile][HD];
+  int b, blk;
+  block_coords(a.Lq, b, blk);
+  const int h = blockIdx.y;
+  const int qi = blk * kRows + threadIdx.x;
+  const int D = a.H * HD;
+  const long long rs = 3LL * D;
+  const __nv_bfloat16* base = a.qkv + static_cast<long long>(b) * a.Lk * rs;
+  const Vis vis = make_vis(a, b);
+  const int p = a.Lk - a.Lq + qi;
+  const long long qoff = (static_cast<long long>(b) * a.H + h) * a.Lq + qi;
+  const float lse = qi < a.Lq ? a.lse[qoff] : CUDART_INF_F;
+  const bool qvalid = qi < a.Lq && p >= vis.kst && lse != CUDART_INF_F;
+  const float c2 = a.scale * kLog2e;
+  float q[HD], dO[HD], dq[HD];
+  const long long ooff = (static_cast<long long>(b) * a.Lq + qi) * D + h * HD;
+#pragma unroll
+  for (int d = 0; d < HD; ++d) {
+    q[d] = qvalid ? __bfloat162float(base[static_cast<long long>(p) * rs + h * HD + d]) * c2 : 0.f;
+    dO[d] = qvalid ? __bfloat162float(a.dout[ooff + d]) : 0.f;
+    dq[d] = 0.f;
+  }
+  const float Dq = qvalid ? a.dsum[qoff] : 0.f;
+  const int last_p = a.Lk - a.Lq + min(a.Lq, (blk + 1) * kRows) - 1;
+  const int hi = a.causal ? min(a.Lk, last_p + 1) : a.Lk;
+  const int tail_lo = a.causal ? max(hi, vis.tail0) : a.Lk;
+  for (int range = 0; range < 2; ++range) {
+    const int r0 = range == 0 ? vis.kst : max(tail_lo, vis.kst);
+    const int r1 = range == 0 ? hi : a.Lk;
+    for (int j0 = r0; j0 < r1; j0 += kTile) {
+      __syncthreads();
+      stage<HD>(sK, base, rs, D + h * HD, j0, r1);
+      stage<HD>(sV, base, rs, 2 * D + h * HD, j0, r1);
+      __syncthreads();
+      if (!qvalid) continue;
+      const int n = min(kTile, r1 - j0);
+      for (int jj = 0; jj < n; ++jj) {
+        if (!vis(p, j0 + jj)) continue;
+        float s = 0.f, dp = 0.f;
+#pragma unroll
+        for (int d = 0; d < HD; ++d) {
+          s = fmaf(q[d], sK[jj][d], s);
+          dp = fmaf(dO[d], sV[jj][d], dp);
+        }
+        const float ds = exp2f(s - lse) * (dp - Dq);
+#pragma unroll
+        for (int d = 0; d < HD; ++d) dq[d] = fmaf(ds, sK[jj][d], dq[d]);
+      }
+    }
+  }
+  if (qi >= a.Lq) return;
+  __nv_bfloat16* dst = a.dqkv + (static_cast<long long>(b) * a.Lk + p) * rs + h * HD;
+#pragma unroll
+  for (int d = 0; d < HD; ++d) dst[d] = __float2bfloat16(dq[d] * a.scale);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kRows) attn_simt_dkv_kernel(AttnSimtArgs a) {
+  __shared__ float sQ[kTile][HD];
+  __shared__ float sO[kTile][HD];  // dO of the staged queries
+  __shared__ float sL[kTile];      // their log-sum-exp
+  __shared__ float sD[kTile];      // their D_q
+  int b, blk;
+  block_coords(a.Lk, b, blk);
+  const int h = blockIdx.y;
+  const int j = blk * kRows + threadIdx.x;  // key row
+  const int D = a.H * HD;
+  const long long rs = 3LL * D;
+  const __nv_bfloat16* base = a.qkv + static_cast<long long>(b) * a.Lk * rs;
+  const Vis vis = make_vis(a, b);
+  const bool kvalid = j < a.Lk && j >= vis.kst;
+  const float c2 = a.scale * kLog2e;
+  float k[HD], v[HD], dk[HD], dv[HD];
+#pragma unroll
+  for (int d = 0; d < HD; ++d) {
+    k[d] = kvalid ? __bfloat162float(base[static_cast<long long>(j) * rs + D + h * HD + d]) : 0.f;
+    v[d] = kvalid ? __bfloat162float(base[static_cast<long long>(j) * rs + 2 * D + h * HD + d]) : 0.f;
+    dk[d] = 0.f;
+    dv[d] = 0.f;
+  }
+  // queries that may see keys of this CTA: rows >= the first key row (causal) or every
+  // query when the CTA holds trailing tokens; all queries otherwise
+  const int q_first = a.Lk - a.Lq;
+  const int jmin = blk * kRows;
+  const int jmax = min(a.Lk, jmin + kRows) - 1;
+  int p_lo = max(q_first, vis.kst);
+  if (a.causal && jmax < vis.tail0) p_lo = max(p_lo, jmin);
+  const __nv_bfloat16* dO_base = a.dout + static_cast<long long>(b) * a.Lq * D + h * HD;
+  const long long lbase = (static_cast<long long>(b) * a.H + h) * a.Lq;
+  for (int p0 = p_lo; p0 < a.Lk; p0 += kTile) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < kTile * HD; i += blockDim.x) {
+      const int r = i / HD, c = i % HD;
+      const int p = p0 + r;
+      const bool ok = p < a.Lk;
+      sQ[r][c] = ok ? __bfloat162float(base[static_cast<long long>(p) * rs + h * HD + c]) * c2 : 0.f;
+      sO[r][c] = ok ? __bfloat162float(dO_base[static_cast<long long>(p - q_first) * D + c]) : 0.f;
+    }
+    for (int r = threadIdx.x; r < kTile; r += blockDim.x) {
+      const int p = p0 + r;
+      const bool ok = p < a.Lk;
+      sL[r] = ok ? a.lse[lbase + (p - q_first)] : CUDART_INF_F;
+      sD[r] = ok ? a.dsum[lbase + (p - q_first)] : 0.f;
+    }
+    __syncthreads();
+    if (!kvalid) continue;
+    const int n = min(kTile, a.Lk - p0);
+    for (int r = 0; r < n; ++r) {
+      const int p = p0 + r;
+      if (sL[r] == CUDART_INF_F || !vis(p, j)) continue;
+      float s = 0.f, dp = 0.f;
+#pragma unroll
+      for (int d = 0; d < HD; ++d) {
+        s = fmaf(sQ[r][d], k[d], s);
+        dp = fmaf(sO[r][d], v[d], dp);
+      }
+      const float pr = exp2f(s - sL[r]);
+      const float ds = pr * (dp - sD[r]);
+#pragma unroll
+      for (int d = 0; d < HD; ++d) {
+        dv[d] = fmaf(pr, sO[r][d], dv[d]);
+        dk[d] = fmaf(ds, sQ[r][d], dk[d]);  // sQ holds q * scale * log2(e)
+      }
+    }
+  }
+  if (j >= a.Lk) return;
+  __nv_bfloat16* dst = a.dqkv + (static_cast<long long>(b) * a.Lk + j) * rs + h * HD;
+#pragma unroll
+  for (int d = 0; d < HD; ++d) {
+    dst[D + d] = __float2bfloat16(dk[d] / kLog2e);
+    dst[2 * D + d] = __float2bfloat16(dv[d]);
+    if (j < q_first) dst[d] = __float2bfloat16(0.f);  // Q rows that are not queries
+  }
+}
+
+template <int HD>
+cudaError_t launch_fwd(const AttnSimtArgs& a, cudaStream_t st) {
+  const dim3 grid(static_cast<unsigned>(a.B) * ((a.Lq + kRows - 1) / kRows), a.H);
+  attn_simt_fwd_kernel<HD><<<grid, kRows, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+template <int HD>
+cudaError_t launch_bwd(const AttnSimtArgs& a, cudaStream_t st) {
+  const long long n = static_cast<long long>(a.B) * a.H * a.Lq;
+  attn_simt_dsum_kernel<HD><<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  attn_simt_dq_kernel<HD><<<dim3(static_cast<unsigned>(a.B) * ((a.Lq + kRows - 1) / kRows), a.H), kRows, 0, st>>>(a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  attn_simt_dkv_kernel<HD><<<dim3(static_cast<unsigned>(a.B) * ((a.Lk + kRows - 1) / kRows), a.H), kRows, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+bool args_ok(const AttnSimtArgs& a) {
+  return a.qkv != nullptr && a.kstart != nullptr && a.B > 0 && a.H > 0 && a.Lq > 0 && a.Lq <= a.Lk &&
+         a.ktail >= 0 && a.ktail <= a.Lq && a.kexcl >= 0 && a.kexcl <= a.ktail && a.H <= 65535 &&
+         static_cast<long long>(a.B) * ((a.Lk + kRows - 1) / kRows) <= 0x7fffffffLL;
+}
+
+}  // namespace
+
+bool attn_simt_supported(int hd) { return hd == 8 || hd == 16 || hd == 64; }
+
+cudaError_t attn_simt_fwd(const AttnSimtArgs& a, cudaStream_t stream) {
+  if (!args_ok(a) || a.out == nullptr || a.lse == nullptr) return cudaErrorInvalidValue;
+  switch (a.hd) {
+    case 8: return launch_fwd<8>(a, stream);
+    case 16: return launch_fwd<16>(a, stream);
+    case 64: return launch_fwd<64>(a, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t attn_simt_bwd(const AttnSimtArgs& a, cudaStream_t stream) {
+  if (!args_ok(a) || a.out == nullptr || a.lse == nullptr || a.dout == nullptr || a.dqkv == nullptr ||
+      a.dsum == nullptr)
+    return cudaErrorInvalidValue;
+  switch (a.hd) {
+    case 8: return launch_bwd<8>(a, stream);
+    case 16: return launch_bwd<16>(a, stream);
+    case 64: return launch_bwd<64>(a, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace mdl

@@ -5,6 +5,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
 
+#include <cmath>
 #include <optional>
 #include <stdexcept>
 #include <string>
@@ -835,6 +836,62 @@ void fmha_bwd(const at::Tensor& qkv, const at::Tensor& kstart, const at::Tensor&
   g_launches += 3;
 }
 
+// ------------------------------------------------------------------ CUDA-core attention (small heads)
+mdl::AttnSimtArgs simt_args(const at::Tensor& qkv, const at::Tensor& kstart, const at::Tensor& out,
+                            const at::Tensor& lse, int64_t H, int64_t Lq, bool causal, double scale, int64_t ktail,
+                            int64_t kexcl) {
+  require_cuda(qkv, "qkv");
+  TORCH_CHECK(qkv.scalar_type() == at::kBFloat16 && qkv.dim() == 3 && qkv.is_contiguous(), "qkv must be [B, Lk, 3D] bf16");
+  TORCH_CHECK(kstart.scalar_type() == at::kInt && kstart.is_contiguous() && kstart.numel() == qkv.size(0),
+              "kstart must be int32 [B]");
+  TORCH_CHECK(qkv.size(2) % (3 * H) == 0, "qkv width must be 3 * H * head_dim");
+  mdl::AttnSimtArgs a;
+  a.B = static_cast<int>(qkv.size(0));
+  a.Lk = static_cast<int>(qkv.size(1));
+  a.H = static_cast<int>(H);
+  a.hd = static_cast<int>(qkv.size(2) / 3 / H);
+  a.Lq = static_cast<int>(Lq);
+  TORCH_CHECK(mdl::attn_simt_supported(a.hd), "CUDA-core attention takes head widths 8, 16 and 64");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() &&
+                  out.numel() == static_cast<int64_t>(a.B) * Lq * H * a.hd, "out must be bf16 [B, Lq, D]");
+  TORCH_CHECK(lse.scalar_type() == at::kFloat && lse.is_contiguous() && lse.numel() == static_cast<int64_t>(a.B) * H * Lq,
+              "lse must be fp32 [B, H, Lq]");
+  a.qkv = reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr());
+  a.kstart = kstart.data_ptr<int>();
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.lse = lse.data_ptr<float>();
+  a.causal = causal ? 1 : 0;
+  a.ktail = static_cast<int>(ktail);
+  a.kexcl = static_cast<int>(kexcl);
+  a.scale = scale > 0 ? static_cast<float>(scale) : 1.f / std::sqrt(static_cast<float>(a.hd));
+  return a;
+}
+
+void attn_simt_fwd(const at::Tensor& qkv, const at::Tensor& kstart, const at::Tensor& out, const at::Tensor& lse,
+                   int64_t H, int64_t Lq, bool causal, double scale, int64_t ktail, int64_t kexcl) {
+  c10::cuda::CUDAGuard guard(qkv.device());
+  auto a = simt_args(qkv, kstart, out, lse, H, Lq, causal, scale, ktail, kexcl);
+  check(mdl::attn_simt_fwd(a, stream_of(qkv)), "attn_simt_fwd");
+  g_launches += 1;
+}
+
+void attn_simt_bwd(const at::Tensor& qkv, const at::Tensor& kstart, const at::Tensor& out, const at::Tensor& lse,
+                   const at::Tensor& dout, const at::Tensor& dqkv, const at::Tensor& dsum, int64_t H, int64_t Lq,
+                   bool causal, double scale, int64_t ktail, int64_t kexcl) {
+  c10::cuda::CUDAGuard guard(qkv.device());
+  auto a = simt_args(qkv, kstart, out, lse, H, Lq, causal, scale, ktail, kexcl);
+  TORCH_CHECK(dout.scalar_type() == at::kBFloat16 && dout.is_contiguous() && dout.numel() == out.numel(),
+              "dout must be contiguous bf16 like out");
+  TORCH_CHECK(dqkv.scalar_type() == at::kBFloat16 && dqkv.is_contiguous() && dqkv.numel() == qkv.numel(),
+              "dqkv must be contiguous bf16 like qkv");
+  TORCH_CHECK(dsum.scalar_type() == at::kFloat && dsum.numel() >= lse.numel(), "dsum must be fp32 [B, H, Lq]");
+  a.dout = reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr());
+  a.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
+  a.dsum = dsum.data_ptr<float>();
+  check(mdl::attn_simt_bwd(a, stream_of(qkv)), "attn_simt_bwd");
+  g_launches += 3;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -887,6 +944,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("launch_count", &launch_count);
   m.def("small_attn_fwd", &small_attn_fwd);
   m.def("small_attn_bwd", &small_attn_bwd);
+  m.def("attn_simt_fwd", &attn_simt_fwd, "suffix attention on CUDA cores (head widths 8, 16, 64)", py::arg("qkv"),
+        py::arg("kstart"), py::arg("out"), py::arg("lse"), py::arg("H"), py::arg("Lq"), py::arg("causal"),
+        py::arg("scale"), py::arg("ktail") = 0, py::arg("kexcl") = 0);
+  m.def("attn_simt_bwd", &attn_simt_bwd, py::arg("qkv"), py::arg("kstart"), py::arg("out"), py::arg("lse"),
+        py::arg("dout"), py::arg("dqkv"), py::arg("dsum"), py::arg("H"), py::arg("Lq"), py::arg("causal"),
+        py::arg("scale"), py::arg("ktail") = 0, py::arg("kexcl") = 0);
   m.def("fmha_fwd", &fmha_fwd, py::arg("qkv"), py::arg("kstart"), py::arg("out"), py::arg("lse"), py::arg("H"),
         py::arg("Lq"), py::arg("causal"), py::arg("scale"), py::arg("err") = py::none(), py::arg("ktail") = 0,
         py::arg("kexcl") = 0);

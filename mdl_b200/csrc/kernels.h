@@ -2,6 +2,7 @@
 #pragma once
 
 #include "attention.h"
+#include "attn_simt.h"
 #include "comm.h"
 #include "embedding.h"
 #include "fmha.h"

@@ -43,7 +43,7 @@ from torch import nn
 
 from ..config.schema import AppConfig
 from ..ops._ext import error_word, ext
-from ..ops.attention import suffix_attention_reference
+from ..ops.attention import NATIVE_HEAD_DIMS, attention_bwd, attention_fwd, suffix_attention_reference
 from ..ops.gemm import ACT_ADD, ACT_DMUL, ACT_GELU_GRAD, bgemm
 from ..ops.layers import _grad, _kaiming_uniform_, _shadow, gemm_param
 from .features import FeatureEncoder
@@ -102,7 +102,7 @@ class LongerBlockFn(torch.autograd.Function):
         ks = kstart.to(torch.int32).contiguous()
         att = torch.empty(B, Lq, D, dtype=torch.bfloat16, device=dev)
         lse = torch.empty(B, heads, Lq, dtype=torch.float32, device=dev)
-        ext().fmha_fwd(qkv, ks, att, lse, heads, Lq, bool(causal), 0.0, error_word(dev), int(ktail), int(kexcl))
+        attention_fwd(qkv, ks, att, lse, heads, Lq, bool(causal), int(ktail), int(kexcl))
         h = torch.empty(B, Lq, D, dtype=torch.bfloat16, device=dev)
         if Lq == Lk:
             bgemm(att, _shadow(blk.wo), h, M=B * Lq, N=D, K=D, lda=D, ldb=D, ldc=D, bias=blk.bo, aux=X, ld_aux=D,
@@ -152,11 +152,8 @@ class LongerBlockFn(torch.autograd.Function):
         C.colsum(dh, _grad(blk.bo), 1, B * Lq, D, D, 0, 1.0)
         # attention
         dqkv = torch.empty_like(qkv)
-        dq_acc = torch.empty(B, Lq, D, dtype=torch.float32, device=dev)
-        dsum = torch.empty(B, heads, Lq, dtype=torch.float32, device=dev)
-        C.fmha_bwd(qkv, ks, att, lse, datt.view(B, Lq, D), dqkv, dq_acc, dsum, heads, Lq, causal, 0.0, error_word(dev),
-                   ktail, kexcl)
-        del dq_acc, dsum, datt
+        attention_bwd(qkv, ks, att, lse, datt.view(B, Lq, D), dqkv, heads, Lq, causal, ktail, kexcl)
+        del datt
         # Q projection (query rows only)
         dq_rows = _off(dqkv, (Lk - Lq) * 3 * D)
         dxq = torch.empty(B * Lq, D, dtype=torch.bfloat16, device=dev)
@@ -411,9 +408,11 @@ class LongerEncoder(nn.Module):
         """``tokens``: event tokens already projected (``project``), else ``seq_in`` is projected here."""
 
         B, L, D, R, G = lengths.shape[0], self.L, self.D, self.R, self.G
-        if native and (self.head_dim != 32 or (len(self.inner) and self.Din // self.heads != 32)):
-            raise NotImplementedError(f"LONGER head_dim {self.head_dim} (inner {self.Din // self.heads}): the tcgen05 "
-                                      "attention kernels take head_dim 32 (set runtime.kernel_backend: torch)")
+        if native and (self.head_dim not in NATIVE_HEAD_DIMS
+                       or (len(self.inner) and self.Din // self.heads not in NATIVE_HEAD_DIMS)):
+            raise NotImplementedError(f"LONGER head_dim {self.head_dim} (inner {self.Din // self.heads}): the native "
+                                      f"attention kernels take {NATIVE_HEAD_DIMS} (or set runtime.kernel_backend: "
+                                      "torch)")
         if tokens is None:
             tokens = self.project(seq_in, lengths, native)
         kst = (L - lengths.clamp(0, L)).to(torch.int32)

@@ -42,7 +42,8 @@ from torch import nn
 
 from ..config.schema import AppConfig
 from ..ops._ext import error_word, ext
-from ..ops.attention import suffix_attention, suffix_attention_reference
+from ..ops.attention import (NATIVE_HEAD_DIMS, attention_bwd, attention_fwd, suffix_attention,
+                             suffix_attention_reference)
 from ..ops.gemm import ACT_ADD, ACT_DMUL, ACT_GELU_GRAD, bgemm
 from ..ops.layers import _grad, _kaiming_uniform_, _shadow, gemm_param
 from .features import FeatureEncoder
@@ -163,7 +164,7 @@ class OneTransLayerFn(torch.autograd.Function):
         ks = kstart.to(torch.int32).contiguous()
         att = torch.empty(B, Lq, D, dtype=torch.bfloat16, device=dev)
         lse = torch.empty(B, heads, Lq, dtype=torch.float32, device=dev)
-        C.fmha_fwd(qkv, ks, att, lse, heads, Lq, True, 0.0, error_word(dev), 0)
+        attention_fwd(qkv, ks, att, lse, heads, Lq, True)
         h = torch.empty(B, Lq, D, dtype=torch.bfloat16, device=dev)
         # h = X[:, Lk-Lq:] + att W_o^T + b_o
         bgemm(att, _shadow(layer.wo), h, M=Lq, N=D, K=D, G=B, lda=D, gsA=Lq * D, ldb=D, gsB=0, ldc=D, gsC=Lq * D,
@@ -213,10 +214,8 @@ class OneTransLayerFn(torch.autograd.Function):
         C.colsum(dh, _grad(layer.bo), 1, B * Lq, D, D, 0, 1.0)
         # ---- attention
         dqkv = torch.empty_like(qkv)
-        dq_acc = torch.empty(B, Lq, D, dtype=torch.float32, device=dev)
-        dsum = torch.empty(B, heads, Lq, dtype=torch.float32, device=dev)
-        C.fmha_bwd(qkv, ks, att, lse, datt, dqkv, dq_acc, dsum, heads, Lq, True, 0.0, error_word(dev), 0)
-        del dq_acc, dsum, datt
+        attention_bwd(qkv, ks, att, lse, datt, dqkv, heads, Lq, True)
+        del datt
         # ---- Q/K/V projections
         dxn = torch.empty_like(X)
         _mixed_dgrad(dqkv, Lk, s_in, 3 * D, D, _shadow(layer.wqkv_s), _shadow(layer.wqkv_ns), dxn)
@@ -612,9 +611,9 @@ class OneTransModel(nn.Module):
         seq_in = grad_ready(seq_in, hooks, nl + 1)
         if self.ns_mode != "auto_split":
             ns_in = self.ns_tokens(ns_in).to(torch.bfloat16)
-        if self.head_dim != 32:
-            raise NotImplementedError(f"OneTrans head_dim {self.head_dim}: the tcgen05 attention kernels take head_dim "
-                                      "32 (set runtime.kernel_backend: torch for this model)")
+        if self.head_dim not in NATIVE_HEAD_DIMS:
+            raise NotImplementedError(f"OneTrans head_dim {self.head_dim}: the native attention kernels take "
+                                      f"{NATIVE_HEAD_DIMS} (set runtime.kernel_backend: torch for this model)")
         if self.multi:
             X = OneTransAssembleFn.apply(seq_in.to(torch.bfloat16), ns_in, kstart, self, self.L)
         else:

@@ -72,6 +72,38 @@ def suffix_attention_reference(qkv: torch.Tensor, kstart: torch.Tensor, heads: i
     return o.transpose(1, 2).reshape(B, lq, D)
 
 
+NATIVE_HEAD_DIMS = (8, 16, 32, 64)
+
+
+def attention_fwd(qkv, ks, out, lse, heads: int, lq: int, causal: bool, ktail: int = 0, kexcl: int = 0) -> None:
+    """Native forward of the suffix attention: the tcgen05 flash attention for head width
+    32, the CUDA-core kernels (``csrc/attn_simt.cu``) for 8, 16 and 64."""
+
+    hd = qkv.shape[2] // 3 // heads
+    if hd == 32:
+        ext().fmha_fwd(qkv, ks, out, lse, heads, lq, bool(causal), 0.0, error_word(qkv.device), int(ktail),
+                       int(kexcl))
+    elif hd in NATIVE_HEAD_DIMS:
+        ext().attn_simt_fwd(qkv, ks, out, lse, heads, lq, bool(causal), 0.0, int(ktail), int(kexcl))
+    else:
+        raise NotImplementedError(f"attention head width {hd}: the native kernels take {NATIVE_HEAD_DIMS}")
+
+
+def attention_bwd(qkv, ks, out, lse, dout, dqkv, heads: int, lq: int, causal: bool, ktail: int = 0,
+                  kexcl: int = 0) -> None:
+    hd = qkv.shape[2] // 3 // heads
+    dsum = torch.empty(lse.shape, dtype=torch.float32, device=qkv.device)
+    if hd == 32:
+        dq_acc = torch.empty(out.shape, dtype=torch.float32, device=qkv.device)
+        ext().fmha_bwd(qkv, ks, out, lse, dout, dqkv, dq_acc, dsum, heads, lq, bool(causal), 0.0,
+                       error_word(qkv.device), int(ktail), int(kexcl))
+    elif hd in NATIVE_HEAD_DIMS:
+        ext().attn_simt_bwd(qkv, ks, out, lse, dout, dqkv, dsum, heads, lq, bool(causal), 0.0, int(ktail),
+                            int(kexcl))
+    else:
+        raise NotImplementedError(f"attention head width {hd}: the native kernels take {NATIVE_HEAD_DIMS}")
+
+
 class SuffixAttentionFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, qkv, kstart, heads, lq, causal, ktail=0, kexcl=0):
@@ -81,8 +113,7 @@ class SuffixAttentionFn(torch.autograd.Function):
         ks = kstart.to(torch.int32).contiguous()
         out = torch.empty(B, lq, D, dtype=torch.bfloat16, device=qkv.device)
         lse = torch.empty(B, heads, lq, dtype=torch.float32, device=qkv.device)
-        ext().fmha_fwd(qkv, ks, out, lse, heads, lq, bool(causal), 0.0, error_word(qkv.device), int(ktail),
-                       int(kexcl))
+        attention_fwd(qkv, ks, out, lse, heads, lq, causal, ktail, kexcl)
         ctx.save_for_backward(qkv, ks, out, lse)
         ctx.meta = (heads, lq, bool(causal), int(ktail), int(kexcl))
         return out
@@ -93,10 +124,7 @@ class SuffixAttentionFn(torch.autograd.Function):
         heads, lq, causal, ktail, kexcl = ctx.meta
         dout = dout.to(torch.bfloat16).contiguous()
         dqkv = torch.empty_like(qkv)
-        dq_acc = torch.empty(out.shape, dtype=torch.float32, device=qkv.device)
-        dsum = torch.empty(lse.shape, dtype=torch.float32, device=qkv.device)
-        ext().fmha_bwd(qkv, ks, out, lse, dout, dqkv, dq_acc, dsum, heads, lq, causal, 0.0, error_word(qkv.device),
-                       ktail, kexcl)
+        attention_bwd(qkv, ks, out, lse, dout, dqkv, heads, lq, causal, ktail, kexcl)
         return dqkv, None, None, None, None, None, None
 
 

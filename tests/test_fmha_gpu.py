@@ -7,9 +7,9 @@ import torch
 from mdl_b200.ops.attention import suffix_attention, suffix_attention_reference
 
 
-def _case(B, Lk, Lq, H, kstart, causal, device, seed=0):
+def _case(B, Lk, Lq, H, kstart, causal, device, seed=0, hd=32):
     g = torch.Generator(device="cpu").manual_seed(seed)
-    D = 32 * H
+    D = hd * H
     qkv = (torch.randn(B, Lk, 3 * D, generator=g) * 1.5).bfloat16().to(device)
     ks = torch.tensor(kstart, dtype=torch.int32).to(device)
     dout = torch.randn(B, Lq, D, generator=g).bfloat16().to(device)
@@ -190,3 +190,37 @@ def test_single_query_attention_kernel_matches_fp32(B, L, N, D):
     torch.testing.assert_close(q.grad, ref_q.grad, atol=5e-3, rtol=5e-3)
     torch.testing.assert_close(hist.grad.float(), ref_h.grad, atol=2e-2, rtol=2e-2)
     assert not hist.grad[0].any()
+
+
+SIMT_CASES = [
+    # hd, B, Lk, Lq, H, kstart, causal, ktail, kexcl
+    (8, 3, 300, 40, 4, [0, 120, 299], True, 6, 2),    # LONGER cross block, production widths (32 = 4 x 8)
+    (8, 2, 40, 40, 4, [0, 12], True, 8, 3),           # LONGER self block
+    (16, 2, 200, 200, 2, [5, 150], False, 0, 0),      # non-causal
+    (16, 2, 257, 130, 2, [0, 64], True, 0, 0),        # OneTrans-style suffix
+    (64, 2, 180, 100, 4, [3, 90], True, 0, 0),        # OneTrans d=256 / 4 heads
+    (8, 700, 2, 2, 4, [0, 1] * 350, False, 0, 0),     # LONGER inner blocks: many tiny groups
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", SIMT_CASES)
+def test_simt_attention_forward_backward(case):
+    """The CUDA-core suffix attention (head widths 8, 16, 64) against the fp32 definition."""
+
+    hd, B, Lk, Lq, H, kstart, causal, ktail, kexcl = case
+    qkv, ks, dout = _case(B, Lk, Lq, H, kstart, causal, "cuda", hd=hd)
+    q1 = qkv.clone().requires_grad_(True)
+    out = suffix_attention(q1, ks, H, Lq, causal, ktail, kexcl)
+    out.backward(dout)
+    torch.cuda.synchronize()
+    q2 = qkv.float().clone().requires_grad_(True)
+    ref = suffix_attention_reference(q2, ks, H, Lq, causal, ktail=ktail, kexcl=kexcl)
+    ref.backward(dout.float())
+    err = (out.float() - ref).abs().max().item()
+    assert err < 2e-2, f"forward max error {err}"
+    g, gr = q1.grad.float(), q2.grad
+    for part in range(3):  # Q, K and V gradients each
+        sl = slice(part * hd * H, (part + 1) * hd * H)
+        pr = ((g[..., sl] - gr[..., sl]).norm() / gr[..., sl].norm().clamp_min(1e-6)).item()
+        assert pr < 3e-2, f"part {part} relative error {pr}"

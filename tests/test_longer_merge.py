@@ -84,9 +84,13 @@ def test_merged_longer_trains_on_cpu(merge, inner):
 
 
 @pytest.mark.gpu
-def test_merged_longer_cuda_matches_cpu():
-    # merge 2 of 16-wide events, one head: the merged blocks run head_dim 32 on the tcgen05 kernels
-    cfg, spec = _cfg(merge=2, inner=0, d=16, heads=1, seq_len=120, R=24, min_len=20)
+@pytest.mark.parametrize("merge,inner,d,heads", [
+    (2, 0, 16, 1),   # merged blocks at head_dim 32: tcgen05 flash attention
+    (1, 0, 32, 4),   # the reference's production LONGER widths (head_dim 8): CUDA-core attention
+    (2, 1, 32, 4),   # inner blocks at head_dim 8, merged blocks at 16
+])
+def test_merged_longer_cuda_matches_cpu(merge, inner, d, heads):
+    cfg, spec = _cfg(merge=merge, inner=inner, d=d, heads=heads, seq_len=120, R=24, min_len=20)
     torch.manual_seed(0)
     cpu_model = build_model(cfg, device="cpu", base_seed=1)
     gpu_model = build_model(cfg, device="cuda", base_seed=1)

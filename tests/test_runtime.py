@@ -172,9 +172,13 @@ def test_attention_preflight():
 
     m, _ = scaled_config(4, 1e-3, num_fields=8, batch=8)
     assert "flash" in attention_preflight(app_config_from_mapping(m))["paths"]["mixed_causal"]
-    m["model"]["num_heads"] = 4           # d=256 / 4 heads = head_dim 64
-    with pytest.raises(ValueError, match="head_dim 32"):
+    m["model"]["num_heads"] = 4           # d=256 / 4 heads = head_dim 64: the CUDA-core kernels
+    assert "CUDA-core" in attention_preflight(app_config_from_mapping(m))["paths"]["mixed_causal"]
+    m["model"]["num_heads"] = 2           # head_dim 128: no native kernel
+    with pytest.raises(ValueError, match="head_dim"):
         attention_preflight(app_config_from_mapping(m))
+    m["runtime"] = {**m.get("runtime", {}), "kernel_backend": "torch"}
+    assert "PyTorch" in attention_preflight(app_config_from_mapping(m))["paths"]["mixed_causal"]
     m, _ = scaled_config(5, 1e-3, num_fields=8, batch=8, seq_len=64, min_len=8, query_tokens=16)
     paths = attention_preflight(app_config_from_mapping(m))["paths"]
     assert "longer:behavior" in paths and "mixformer_cross" in paths
