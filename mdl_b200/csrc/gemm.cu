@@ -17,9 +17,12 @@
 //
 // Epilogue data path: tcgen05.ld gives each lane one ROW of a 32x32 chunk, so
 // direct stores would touch 32 rows per instruction. Each warp instead stages
-// its chunk in shared memory (fp32, 36-float pitch: conflict-free 16-byte
-// accesses) and writes it back four rows x 128 bytes per instruction; the aux
-// operand of the activation-derivative epilogues is read the same way.
+// the chunk in shared memory 16 columns at a time (fp32, 64-byte rows whose four
+// 16-byte slots are XOR-swizzled by row pair: conflict-free writes by row and
+// reads by column group) and writes it back eight rows x 32 bytes per
+// instruction; the aux operand of the activation-derivative epilogues is read
+// the same way. The 32 KB staging buffer leaves room for a 4-stage (single CTA)
+// or 6-stage (CTA pair) operand ring.
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -29,6 +32,21 @@
 
 #include "common.cuh"
 #include "gemm.h"
+
+// Pipeline wait counters for tuning builds (-DMDL_GEMM_STATS): clock cycles the producer
+// waits for free stages, the MMA issuer for loaded stages and free accumulators, and one
+// epilogue lane for finished accumulators, summed over CTAs. Off in the library build.
+#ifdef MDL_GEMM_STATS
+__device__ unsigned long long g_gemm_stats[8];
+#define GSTAT_DECL(v) long long v = 0
+#define GSTAT_WAIT(v, expr) \
+  ([&]() { const long long t0_ = clock64(); const bool r_ = (expr); v += clock64() - t0_; return r_; }())
+#define GSTAT_FLUSH(i, v) atomicAdd(&g_gemm_stats[i], static_cast<unsigned long long>(v))
+#else
+#define GSTAT_DECL(v)
+#define GSTAT_WAIT(v, expr) (expr)
+#define GSTAT_FLUSH(i, v)
+#endif
 
 namespace mdl {
 namespace {
@@ -49,20 +67,23 @@ constexpr int TMEM_COLS = 2 * BN;           // double-buffered accumulator
 constexpr int NUM_EPI_WARPS = 16;                // four warps per TMEM lane quarter
 constexpr int NUM_THREADS = 64 + NUM_EPI_WARPS * 32;
 constexpr int MN_CHUNK_BYTES = BK * 128;    // one 64-wide MN chunk of BK rows (MN-major)
-constexpr int EPI_PITCH = 36;               // floats per staged row (32 + 4 pad)
+constexpr int EPI_PITCH = 16;               // floats per staged row (16 columns, float4 slots swizzled)
 constexpr int EPI_WARP_FLOATS = 32 * EPI_PITCH;
-constexpr int EPI_BYTES = NUM_EPI_WARPS * EPI_WARP_FLOATS * 4;  // 72 KB
+constexpr int EPI_BYTES = NUM_EPI_WARPS * EPI_WARP_FLOATS * 4;  // 32 KB
 
 // Single CTA: a 128 x 256 tile per CTA, all of B's 256 rows staged per k-block.
 // CTA pair (cta_group::2, cluster of two): a 256 x 256 tile per pair; each CTA stages
 // 128 rows of A and 128 rows of B per k-block (32 KB instead of 48 KB per 128 x 256 of
 // output), which leaves room for a fourth pipeline stage.
-template <bool PAIR>
+// Epilogues that read global memory per element (aux operands) or compute GELU keep
+// a shallower ring: the shared-memory carve-out then leaves more of the SM's unified
+// L1 for their loads, and their time is set by the epilogue, not by operand latency.
+template <bool PAIR, bool HEAVY_EPI = false>
 struct Cfg {
   static constexpr int TILE_M = PAIR ? 2 * BM : BM;
   static constexpr int B_ROWS = PAIR ? BN / 2 : BN;
   static constexpr int B_STAGE_BYTES = B_ROWS * BK * 2;
-  static constexpr int STAGES = PAIR ? 4 : 3;
+  static constexpr int STAGES = HEAVY_EPI ? (PAIR ? 4 : 3) : (PAIR ? 6 : 4);
   static constexpr int SMEM_BYTES =
       1024 + STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + EPI_BYTES + (2 * STAGES + 4) * 8 + 16;
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
@@ -105,7 +126,7 @@ template <bool A_MN, bool B_MN, int EPI, bool PAIR>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB, const EpiParams ep) {
-  using C = Cfg<PAIR>;
+  using C = Cfg<PAIR, EPI == EPI_GELU || EPI == EPI_AUX>;
   constexpr int STAGES = C::STAGES;
   constexpr int B_STAGE_BYTES = C::B_STAGE_BYTES;
   constexpr int TILE_M = C::TILE_M;
@@ -181,6 +202,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t phase = 0;
       int issued = 0;  // stages filled but possibly not yet consumed
       bool ok = true;
+      GSTAT_DECL(w_empty);
       for (int unit = unit0; unit < num_units && ok; unit += unit_step) {
         const int tile = unit / ep.splits;
         const int kb0 = (unit - tile * ep.splits) * ep.kb_per_split;
@@ -192,7 +214,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int a_row0 = mb * TILE_M + static_cast<int>(cr) * BM;     // this CTA's A rows
         const int b_row0 = nb * BN + static_cast<int>(cr) * B_ROWS;     // this CTA's B rows
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, ep.err, abort_flag)) {
+          if (!GSTAT_WAIT(w_empty, mbar_wait(&empty[stage], phase ^ 1u, ep.err, abort_flag))) {
             ok = false;
             break;
           }
@@ -248,6 +270,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
         }
       }
+      GSTAT_FLUSH(0, w_empty);
     }
   } else if (warp == 1) {
     if (lane == 0 && cr == 0) {
@@ -259,15 +282,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
+      GSTAT_DECL(w_full);
+      GSTAT_DECL(w_tempty);
+#ifdef MDL_GEMM_STATS
+      const long long t_start = clock64();
+#endif
       for (int unit = unit0; unit < num_units && ok; unit += unit_step) {
         const int tile = unit / ep.splits;
         const int kb0 = (unit - tile * ep.splits) * ep.kb_per_split;
         const int kb1 = min(k_blocks, kb0 + ep.kb_per_split);
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, ep.err, abort_flag)) break;
+        if (!GSTAT_WAIT(w_tempty, mbar_wait(&tempty[acc], acc_phase ^ 1u, ep.err, abort_flag))) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&full[stage], phase, ep.err, abort_flag)) {
+          if (!GSTAT_WAIT(w_full, mbar_wait(&full[stage], phase, ep.err, abort_flag))) {
             ok = false;
             break;
           }
@@ -307,6 +335,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1u;
       }
+      GSTAT_FLUSH(1, w_full);
+      GSTAT_FLUSH(2, w_tempty);
+#ifdef MDL_GEMM_STATS
+      GSTAT_FLUSH(3, clock64() - t_start);
+      GSTAT_FLUSH(5, 1);
+#endif
     }
   } else {
     // ------------------------------------------------------------ epilogue
@@ -324,15 +358,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int quarter = warp & 3;            // TMEM lane quarter this warp may read
     const int cgroup = (warp - 2) / 4;       // which 64-column group of the tile
     float* stg = sEpi + (warp - 2) * EPI_WARP_FLOATS;
-    const int q = lane & 7;                  // 4-column group in the chunk (write-back)
-    const int rsub = lane >> 3;              // row within each 4-row step (write-back)
+    const int q4 = lane & 3;                 // 4-column group in a 16-column half (write-back)
+    const int rq = lane >> 2;                // row within each 8-row step (write-back)
     int acc = 0;
     uint32_t acc_phase = 0;
     const bool atomic_out = ep.splits > 1;  // K slices of one tile add into the fp32 output
+    GSTAT_DECL(w_tfull);
     for (int unit = unit0; unit < num_units; unit += unit_step) {
       const int tile = unit / ep.splits;
       // warp-uniform outcome: the tcgen05.ld below must be executed by the whole warp
-      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, ep.err, abort_flag))) break;
+      if (!__all_sync(0xffffffffu, GSTAT_WAIT(w_tfull, mbar_wait(&tfull[acc], acc_phase, ep.err, abort_flag)))) break;
       tc_fence_after();
       const int g = tile / tiles_per_group;
       const int rem = tile - g * tiles_per_group;
@@ -342,25 +377,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int c0 = cgroup * (BN / 4); c0 < (cgroup + 1) * (BN / 4); c0 += 32) {
         const int col0 = nb * BN + c0;
         if (col0 >= ep.N) break;  // warp-uniform
-        const int gcol = col0 + q * 4;
-        const bool col_vec = gcol + 4 <= ep.N;
-        const int ncols = col_vec ? 4 : max(0, ep.N - gcol);
         constexpr bool need_aux = kAux;
-        // Global reads of the chunk (aux or old output) run PF rows ahead: rows 0..PF-1 are
-        // requested before the TMEM load, row r+PF as soon as row r is consumed.
+        // Steps s = 0..7 cover the 32 x 32 chunk: half h = s / 4 (16 columns), rows
+        // it * 8 + rq (it = s % 4); lane owns columns 4 * q4 .. +3 of the half.
+        auto gcol_of = [&](int h) { return col0 + h * 16 + q4 * 4; };
+        // Global reads of the chunk (aux or old output) run PF steps ahead: steps 0..PF-1
+        // are requested before the TMEM load, step s+PF as soon as step s is consumed.
         const bool need_read = need_aux || (accumulate && !atomic_out);
-        constexpr int PF = kF32 ? 2 : 4;  // rows in flight (fp32 rows need 4 registers each)
+        constexpr int PF = kF32 ? 2 : 4;  // steps in flight (fp32 rows need 4 registers each)
         uint4 pf[PF];
-        auto prefetch = [&](int it) -> uint4 {
+        auto prefetch = [&](int st) -> uint4 {
           uint4 r4 = make_uint4(0u, 0u, 0u, 0u);
-          const int grow = row0 + it * 4 + rsub;
-          if (grow < ep.M && col_vec) {
+          const int grow = row0 + (st & 3) * 8 + rq;
+          const int gc = gcol_of(st >> 2);
+          if (grow < ep.M && gc + 4 <= ep.N) {
             if constexpr (need_aux) {
               const uint2 a2 = __ldg(reinterpret_cast<const uint2*>(ep.aux + g * ep.gs_aux +
-                                                                   static_cast<long long>(grow) * ep.ld_aux + gcol));
+                                                                   static_cast<long long>(grow) * ep.ld_aux + gc));
               r4 = make_uint4(a2.x, a2.y, 0u, 0u);
             } else if (accumulate) {
-              const long long off = g * ep.gsC + static_cast<long long>(grow) * ep.ldc + gcol;
+              const long long off = g * ep.gsC + static_cast<long long>(grow) * ep.ldc + gc;
               if (kF32) {
                 r4 = *reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(ep.out) + off);
               } else {
@@ -372,170 +408,188 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           return r4;
         };
 #pragma unroll
-        for (int it = 0; it < PF; ++it) pf[it] = need_read ? prefetch(it) : make_uint4(0u, 0u, 0u, 0u);
-        float4 bias4 = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (ep.bias != nullptr && ncols > 0) {
-          const float* bp = ep.bias + g * ep.gs_bias + gcol;
-          if (col_vec && ((reinterpret_cast<uintptr_t>(bp) & 15) == 0)) {
-            bias4 = __ldg(reinterpret_cast<const float4*>(bp));
-          } else {
-            float b4[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int st = 0; st < PF; ++st) pf[st] = need_read ? prefetch(st) : make_uint4(0u, 0u, 0u, 0u);
+        float4 bias4[2];
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
-              if (e < ncols) b4[e] = __ldg(bp + e);
-            bias4 = make_float4(b4[0], b4[1], b4[2], b4[3]);
-          }
-        }
-        {
-          float v[32];
-          tmem_ld_32x32b_x32(
-              tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN + c0), v);
-#pragma unroll
-          for (int k = 0; k < 8; ++k)
-            reinterpret_cast<float4*>(stg + lane * EPI_PITCH)[k] =
-                make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
-        }
-        __syncwarp();
-        float csum[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int it = 0; it < 8; ++it) {
-          const int r = it * 4 + rsub;
-          const int grow = row0 + r;
-          const uint4 cur = pf[it % PF];
-          if (it + PF < 8 && need_read) pf[it % PF] = prefetch(it + PF);
-          if (grow >= ep.M || ncols == 0) continue;
-          const float4 s4 = reinterpret_cast<const float4*>(stg + r * EPI_PITCH)[q];
-          float t[4] = {s4.x, s4.y, s4.z, s4.w};
-          if (affine) {
-            t[0] = fmaf(t[0], ep.alpha, bias4.x);
-            t[1] = fmaf(t[1], ep.alpha, bias4.y);
-            t[2] = fmaf(t[2], ep.alpha, bias4.z);
-            t[3] = fmaf(t[3], ep.alpha, bias4.w);
-          }
-          const long long off = g * ep.gsC + static_cast<long long>(grow) * ep.ldc + gcol;
-          if constexpr (need_aux) {
-            uint32_t abits[4] = {cur.x & 0xFFFFu, cur.x >> 16, cur.y & 0xFFFFu, cur.y >> 16};
-            if (!col_vec) {
-              const __nv_bfloat16* ap = ep.aux + g * ep.gs_aux + static_cast<long long>(grow) * ep.ld_aux + gcol;
-#pragma unroll
-              for (int e = 0; e < 4; ++e) abits[e] = e < ncols ? __bfloat16_as_ushort(ap[e]) : 0u;
-            }
-            if (ep.act == GEMM_ACT_DMUL) {
-#pragma unroll
-              for (int e = 0; e < 4; ++e) t[e] *= bf16_bits_to_float(abits[e]);
-            } else if (ep.act == GEMM_ACT_ADD) {
-#pragma unroll
-              for (int e = 0; e < 4; ++e) t[e] += bf16_bits_to_float(abits[e]);
-            } else if (ep.act == GEMM_ACT_DGELU) {
-#pragma unroll
-              for (int e = 0; e < 4; ++e) t[e] *= gelu_grad_fast(bf16_bits_to_float(abits[e]));
+        for (int h = 0; h < 2; ++h) {
+          bias4[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+          const int gc = gcol_of(h);
+          const int nc = gc + 4 <= ep.N ? 4 : max(0, ep.N - gc);
+          if (ep.bias != nullptr && nc > 0) {
+            const float* bp = ep.bias + g * ep.gs_bias + gc;
+            if (nc == 4 && ((reinterpret_cast<uintptr_t>(bp) & 15) == 0)) {
+              bias4[h] = __ldg(reinterpret_cast<const float4*>(bp));
             } else {
-#pragma unroll
-              for (int e = 0; e < 4; ++e) t[e] = bf16_bits_to_float(abits[e]) > 0.f ? t[e] : 0.f;
-            }
-          } else if (relu) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) t[e] = fmaxf(t[e], 0.f);
-          }
-          if (ep.colsum != nullptr) {  // column sums of the product (before any accumulate)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) csum[e] += t[e];
-          }
-          if (kF32 && atomic_out) {
-            float* op = reinterpret_cast<float*>(ep.out) + off;
-            if (col_vec) {
-              asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(op), "f"(t[0]), "f"(t[1]),
-                           "f"(t[2]), "f"(t[3])
-                           : "memory");
-            } else {
+              float b4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
               for (int e = 0; e < 4; ++e)
-                if (e < ncols) atomicAdd(op + e, t[e]);
+                if (e < nc) b4[e] = __ldg(bp + e);
+              bias4[h] = make_float4(b4[0], b4[1], b4[2], b4[3]);
             }
-          } else if (kF32) {
-            float* op = reinterpret_cast<float*>(ep.out) + off;
-            if (col_vec) {
-              float4 o4 = make_float4(t[0], t[1], t[2], t[3]);
+          }
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          {
+            // stage this half: lane = row, four float4 slots swizzled by row pair (conflict-free
+            // 16-byte writes by row and reads by column group)
+            float v[16];
+            tmem_ld_32x32b_x16(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                                   static_cast<uint32_t>(acc * BN + c0 + h * 16),
+                               v);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              reinterpret_cast<float4*>(stg + lane * EPI_PITCH)[k ^ ((lane >> 1) & 3)] =
+                  make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+          }
+          __syncwarp();
+          const int gcol = gcol_of(h);
+          const bool col_vec = gcol + 4 <= ep.N;
+          const int ncols = col_vec ? 4 : max(0, ep.N - gcol);
+          float csum[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int it = 0; it < 4; ++it) {
+            const int st = h * 4 + it;
+            const int r = it * 8 + rq;
+            const int grow = row0 + r;
+            const uint4 cur = pf[st % PF];
+            if (st + PF < 8 && need_read) pf[st % PF] = prefetch(st + PF);
+            if (grow >= ep.M || ncols == 0) continue;
+            const float4 s4 = reinterpret_cast<const float4*>(stg + r * EPI_PITCH)[q4 ^ ((r >> 1) & 3)];
+            float t[4] = {s4.x, s4.y, s4.z, s4.w};
+            if (affine) {
+              t[0] = fmaf(t[0], ep.alpha, bias4[h].x);
+              t[1] = fmaf(t[1], ep.alpha, bias4[h].y);
+              t[2] = fmaf(t[2], ep.alpha, bias4[h].z);
+              t[3] = fmaf(t[3], ep.alpha, bias4[h].w);
+            }
+            const long long off = g * ep.gsC + static_cast<long long>(grow) * ep.ldc + gcol;
+            if constexpr (need_aux) {
+              uint32_t abits[4] = {cur.x & 0xFFFFu, cur.x >> 16, cur.y & 0xFFFFu, cur.y >> 16};
+              if (!col_vec) {
+                const __nv_bfloat16* ap = ep.aux + g * ep.gs_aux + static_cast<long long>(grow) * ep.ld_aux + gcol;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) abits[e] = e < ncols ? __bfloat16_as_ushort(ap[e]) : 0u;
+              }
+              if (ep.act == GEMM_ACT_DMUL) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) t[e] *= bf16_bits_to_float(abits[e]);
+              } else if (ep.act == GEMM_ACT_ADD) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) t[e] += bf16_bits_to_float(abits[e]);
+              } else if (ep.act == GEMM_ACT_DGELU) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) t[e] *= gelu_grad_fast(bf16_bits_to_float(abits[e]));
+              } else {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) t[e] = bf16_bits_to_float(abits[e]) > 0.f ? t[e] : 0.f;
+              }
+            } else if (relu) {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) t[e] = fmaxf(t[e], 0.f);
+            }
+            if (ep.colsum != nullptr) {  // column sums of the product (before any accumulate)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) csum[e] += t[e];
+            }
+            if (kF32 && atomic_out) {
+              float* op = reinterpret_cast<float*>(ep.out) + off;
+              if (col_vec) {
+                asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(op), "f"(t[0]), "f"(t[1]),
+                             "f"(t[2]), "f"(t[3])
+                             : "memory");
+              } else {
+  #pragma unroll
+                for (int e = 0; e < 4; ++e)
+                  if (e < ncols) atomicAdd(op + e, t[e]);
+              }
+            } else if (kF32) {
+              float* op = reinterpret_cast<float*>(ep.out) + off;
+              if (col_vec) {
+                float4 o4 = make_float4(t[0], t[1], t[2], t[3]);
+                if (accumulate) {
+                  const uint4 o = need_aux ? *reinterpret_cast<const uint4*>(op) : cur;
+                  o4.x += __uint_as_float(o.x);
+                  o4.y += __uint_as_float(o.y);
+                  o4.z += __uint_as_float(o.z);
+                  o4.w += __uint_as_float(o.w);
+                }
+                *reinterpret_cast<float4*>(op) = o4;
+              } else {
+  #pragma unroll
+                for (int e = 0; e < 4; ++e)
+                  if (e < ncols) op[e] = accumulate ? op[e] + t[e] : t[e];
+              }
+            } else {
+              __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(ep.out) + off;
               if (accumulate) {
-                const uint4 o = need_aux ? *reinterpret_cast<const uint4*>(op) : cur;
-                o4.x += __uint_as_float(o.x);
-                o4.y += __uint_as_float(o.y);
-                o4.z += __uint_as_float(o.z);
-                o4.w += __uint_as_float(o.w);
+                if (col_vec) {
+                  const uint2 o = need_aux ? *reinterpret_cast<const uint2*>(op) : make_uint2(cur.x, cur.y);
+                  t[0] += bf16_bits_to_float(o.x & 0xFFFFu);
+                  t[1] += bf16_bits_to_float(o.x >> 16);
+                  t[2] += bf16_bits_to_float(o.y & 0xFFFFu);
+                  t[3] += bf16_bits_to_float(o.y >> 16);
+                } else {
+  #pragma unroll
+                  for (int e = 0; e < 4; ++e)
+                    if (e < ncols) t[e] += __bfloat162float(op[e]);
+                }
               }
-              *reinterpret_cast<float4*>(op) = o4;
-            } else {
+              const uint32_t p01 = pack_bf16x2(t[0], t[1]), p23 = pack_bf16x2(t[2], t[3]);
+              if constexpr (kGelu) {
+                // GELU (and optionally GELU') of the bf16 pre-activation
+                const float x[4] = {bf16_bits_to_float(p01 & 0xFFFFu), bf16_bits_to_float(p01 >> 16),
+                                    bf16_bits_to_float(p23 & 0xFFFFu), bf16_bits_to_float(p23 >> 16)};
+                float a[4], d[4];
+  #pragma unroll
+                for (int e = 0; e < 4; ++e) gelu_and_grad_fast(x[e], a[e], d[e], store_grad);
+                const uint32_t o01 = store_grad ? pack_bf16x2(d[0], d[1]) : p01;
+                const uint32_t o23 = store_grad ? pack_bf16x2(d[2], d[3]) : p23;
+                if (col_vec) {
+                  *reinterpret_cast<uint2*>(op) = make_uint2(o01, o23);
+                } else {
+                  const float ov[4] = {store_grad ? d[0] : t[0], store_grad ? d[1] : t[1], store_grad ? d[2] : t[2],
+                                       store_grad ? d[3] : t[3]};
+  #pragma unroll
+                  for (int e = 0; e < 4; ++e)
+                    if (e < ncols) op[e] = __float2bfloat16_rn(ov[e]);
+                }
+                const float a0 = a[0], a1 = a[1], a2 = a[2], a3 = a[3];
+                if (col_vec) {
+                  *reinterpret_cast<uint2*>(ep.out2 + off) = make_uint2(pack_bf16x2(a0, a1), pack_bf16x2(a2, a3));
+                } else {
+                  const float av[4] = {a0, a1, a2, a3};
+  #pragma unroll
+                  for (int e = 0; e < 4; ++e)
+                    if (e < ncols) ep.out2[off + e] = __float2bfloat16_rn(av[e]);
+                }
+              } else {
+                if (col_vec) {
+                  *reinterpret_cast<uint2*>(op) = make_uint2(p01, p23);
+                } else {
+  #pragma unroll
+                  for (int e = 0; e < 4; ++e)
+                    if (e < ncols) op[e] = __float2bfloat16_rn(t[e]);
+                }
+              }
+            }
+          }
+          if (ep.colsum != nullptr) {
+            // lanes q4, q4+4, ..., q4+28 hold the same four columns: reduce, then lanes 0..3 add
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              csum[e] += __shfl_xor_sync(0xffffffffu, csum[e], 4);
+              csum[e] += __shfl_xor_sync(0xffffffffu, csum[e], 8);
+              csum[e] += __shfl_xor_sync(0xffffffffu, csum[e], 16);
+            }
+            if (rq == 0) {
+              float* cp = ep.colsum + g * ep.gs_colsum + gcol;
 #pragma unroll
               for (int e = 0; e < 4; ++e)
-                if (e < ncols) op[e] = accumulate ? op[e] + t[e] : t[e];
-            }
-          } else {
-            __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(ep.out) + off;
-            if (accumulate) {
-              if (col_vec) {
-                const uint2 o = need_aux ? *reinterpret_cast<const uint2*>(op) : make_uint2(cur.x, cur.y);
-                t[0] += bf16_bits_to_float(o.x & 0xFFFFu);
-                t[1] += bf16_bits_to_float(o.x >> 16);
-                t[2] += bf16_bits_to_float(o.y & 0xFFFFu);
-                t[3] += bf16_bits_to_float(o.y >> 16);
-              } else {
-#pragma unroll
-                for (int e = 0; e < 4; ++e)
-                  if (e < ncols) t[e] += __bfloat162float(op[e]);
-              }
-            }
-            const uint32_t p01 = pack_bf16x2(t[0], t[1]), p23 = pack_bf16x2(t[2], t[3]);
-            if constexpr (kGelu) {
-              // GELU (and optionally GELU') of the bf16 pre-activation
-              const float x[4] = {bf16_bits_to_float(p01 & 0xFFFFu), bf16_bits_to_float(p01 >> 16),
-                                  bf16_bits_to_float(p23 & 0xFFFFu), bf16_bits_to_float(p23 >> 16)};
-              float a[4], d[4];
-#pragma unroll
-              for (int e = 0; e < 4; ++e) gelu_and_grad_fast(x[e], a[e], d[e], store_grad);
-              const uint32_t o01 = store_grad ? pack_bf16x2(d[0], d[1]) : p01;
-              const uint32_t o23 = store_grad ? pack_bf16x2(d[2], d[3]) : p23;
-              if (col_vec) {
-                *reinterpret_cast<uint2*>(op) = make_uint2(o01, o23);
-              } else {
-                const float ov[4] = {store_grad ? d[0] : t[0], store_grad ? d[1] : t[1], store_grad ? d[2] : t[2],
-                                     store_grad ? d[3] : t[3]};
-#pragma unroll
-                for (int e = 0; e < 4; ++e)
-                  if (e < ncols) op[e] = __float2bfloat16_rn(ov[e]);
-              }
-              const float a0 = a[0], a1 = a[1], a2 = a[2], a3 = a[3];
-              if (col_vec) {
-                *reinterpret_cast<uint2*>(ep.out2 + off) = make_uint2(pack_bf16x2(a0, a1), pack_bf16x2(a2, a3));
-              } else {
-                const float av[4] = {a0, a1, a2, a3};
-#pragma unroll
-                for (int e = 0; e < 4; ++e)
-                  if (e < ncols) ep.out2[off + e] = __float2bfloat16_rn(av[e]);
-              }
-            } else {
-              if (col_vec) {
-                *reinterpret_cast<uint2*>(op) = make_uint2(p01, p23);
-              } else {
-#pragma unroll
-                for (int e = 0; e < 4; ++e)
-                  if (e < ncols) op[e] = __float2bfloat16_rn(t[e]);
-              }
+                if (e < ncols) atomicAdd(cp + e, csum[e]);
             }
           }
-        }
-        if (ep.colsum != nullptr) {
-          // lanes q, q+8, q+16, q+24 hold the same four columns: reduce, then lanes 0..7 add
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            csum[e] += __shfl_xor_sync(0xffffffffu, csum[e], 8);
-            csum[e] += __shfl_xor_sync(0xffffffffu, csum[e], 16);
-          }
-          if (rsub == 0) {
-            float* cp = ep.colsum + g * ep.gs_colsum + gcol;
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              if (e < ncols) atomicAdd(cp + e, csum[e]);
-          }
+          __syncwarp();  // the staging buffer is rewritten by the next half / chunk
         }
         __syncwarp();
       }
@@ -551,6 +605,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
+#ifdef MDL_GEMM_STATS
+    if (warp == 2 && lane == 0) GSTAT_FLUSH(4, w_tfull);
+#endif
   }
   if constexpr (PAIR) {
     tc_fence_before();
@@ -616,7 +673,7 @@ template <bool A_MN, bool B_MN, int EPI, bool PAIR>
 cudaError_t launch_kind(const CUtensorMap& ta, const CUtensorMap& tb, const EpiParams& ep, int grid,
                         cudaStream_t stream) {
   auto kern = gemm_tcgen05_kernel<A_MN, B_MN, EPI, PAIR>;
-  constexpr int smem = Cfg<PAIR>::SMEM_BYTES;
+  constexpr int smem = Cfg<PAIR, EPI == EPI_GELU || EPI == EPI_AUX>::SMEM_BYTES;
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -693,11 +750,14 @@ int pair_mode() {
   return m;
 }
 
-bool use_pair(long long pair_tiles, int splits) {
+// By shape: at least two waves of pairs and a main loop of at least 8 k-blocks per tile
+// (short-K products such as OneTrans' d=256 projections are bound by their epilogue,
+// and the pair's cross-CTA handshakes then cost more than the halved B traffic saves).
+bool use_pair(long long pair_tiles, int splits, int k_per_tile) {
   const int mode = pair_mode();
   if (mode == 0 || splits > 1) return false;
   if (mode == 1) return true;
-  return pair_tiles >= num_sms();  // at least two waves of pairs
+  return pair_tiles >= num_sms() && k_per_tile >= 8 * BK;
 }
 
 // Epilogue kind of a call; -1 for a combination no kernel implements.
@@ -794,7 +854,7 @@ cudaError_t gemm_bf16_tcgen05(const GemmArgs& a, cudaStream_t stream) {
       ep.splits = (total_kb + ep.kb_per_split - 1) / ep.kb_per_split;
     }
   }
-  const bool pair = use_pair(pair_tiles, ep.splits) && a.max_ctas <= 0;
+  const bool pair = use_pair(pair_tiles, ep.splits, ep.kb_per_split * BK) && a.max_ctas <= 0;
   // B operand map: each CTA of a pair stages half of the tile's 256 B rows
   const uint32_t b_box = pair ? BN / 2 : BN;
   if (!a.b_mn_major)
