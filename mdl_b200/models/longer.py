@@ -404,8 +404,11 @@ class LongerEncoder(nn.Module):
         return self.step(seq_in, native).view(rows, L, self.Din)
 
     def forward(self, seq_in, lengths, target_in, user_in, native: bool, cls_tokens=None,
-                tokens=None) -> torch.Tensor:
-        """``tokens``: event tokens already projected (``project``), else ``seq_in`` is projected here."""
+                tokens=None, summary_only: bool = False) -> torch.Tensor:
+        """``tokens``: event tokens already projected (``project``), else ``seq_in`` is projected here.
+        ``summary_only``: return only the ``G`` global tokens; the last block then runs only
+        their queries (reference ``forward_request_summary`` ``src/model.py:1906-2004``: the
+        recent outputs of the last layer cannot reach the summary)."""
 
         B, L, D, R, G = lengths.shape[0], self.L, self.D, self.R, self.G
         if native and (self.head_dim not in NATIVE_HEAD_DIMS
@@ -437,12 +440,16 @@ class LongerEncoder(nn.Module):
         # every valid key; the candidate globals (last Gc) are seen by nobody else, so every
         # output except theirs is candidate-independent (reference LongerSequenceEncoder: the
         # request-side keys exclude the candidate globals, src/model.py:1706-1730, 2036-2296)
-        X = self.cross(X, kst, R + G, self.heads, True, G, native, kexcl=self.Gc)
+        nblk = 1 + len(self.selfs)
+        summary_only = summary_only and G > 0
+        lq = G if (summary_only and nblk == 1) else R + G
+        X = self.cross(X, kst, lq, self.heads, True, G, native, kexcl=self.Gc)
         kst = (kst - (L - R)).clamp(min=0)
-        for blk in self.selfs:
+        for i, blk in enumerate(self.selfs):
             # self blocks: the same visibility over [recent; globals] (reference mixed mask
             # over [user; recent], candidates over everything)
-            X = blk(X, kst, R + G, self.heads, True, G, native, kexcl=self.Gc)
+            lq = G if (summary_only and i == nblk - 2) else R + G
+            X = blk(X, kst, lq, self.heads, True, G, native, kexcl=self.Gc)
         return X
 
     def _request_tokens(self, tokens, lengths, user_in, cls_tokens, native: bool):

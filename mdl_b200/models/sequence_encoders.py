@@ -152,11 +152,12 @@ class LongerSummaryEncoder(nn.Module):
         # event tokens once per request, then each candidate takes its request's tokens
         tokens = expand_requests(self.longer.project(seq_in, lengths, native), row_indices)
         lengths = expand_requests(lengths, row_indices)
-        X = self.longer(None, lengths, target, user, native, cls_tokens=self.cls_tokens, tokens=tokens)
+        X = self.longer(None, lengths, target, user, native, cls_tokens=self.cls_tokens, tokens=tokens,
+                        summary_only=self.summary)
         G = self.longer.G
         B = lengths.shape[0]
         if self.summary:
-            return X[:, X.shape[1] - G:].reshape(B, -1).float()
+            return X.reshape(B, -1).float()  # the G global tokens
         return LongerEncoder.reference_order(X, G).reshape(B, -1).float()
 
 

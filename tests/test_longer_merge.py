@@ -165,3 +165,27 @@ def test_request_cache_matches_full_forward(merge, inner, cand):
         assert cache["out"].shape[0] == 3
         cached = model.forward_with_cache(rb, cache)
     torch.testing.assert_close(cached, full.float(), atol=1e-4, rtol=1e-4)
+
+
+@pytest.mark.parametrize("self_layers", [0, 2])
+def test_summary_only_equals_the_global_slice(self_layers):
+    """``summary_only`` computes only the global queries in the last block: the same global
+    tokens as the full forward."""
+
+    m, spec = scaled_config(5, 1e-4, num_fields=12, batch=8, seq_len=30, min_len=3, query_tokens=6,
+                            self_layers=self_layers, d=16, heads=2, sequence_head="none", ns_tokens=4)
+    m["sequences"][0].update({"longer_candidate_global_tokens": 2})
+    cfg = app_config_from_mapping(m)
+    torch.manual_seed(0)
+    enc = build_model(cfg, device="cpu", base_seed=1).longer
+    torch.manual_seed(2)
+    B = 5
+    tokens = torch.randn(B, enc.L, enc.Din)
+    lengths = torch.tensor([30, 11, 3, 1, 0])
+    t_in = torch.randn(B, enc.cand_mlp.k_in)
+    u_in = torch.randn(B, enc.user_mlp.k_in) if enc.Gu else None
+    with torch.no_grad():
+        full = enc(None, lengths, t_in, u_in, False, tokens=tokens)
+        summ = enc(None, lengths, t_in, u_in, False, tokens=tokens, summary_only=True)
+    assert summ.shape[1] == enc.G
+    torch.testing.assert_close(summ, full[:, full.shape[1] - enc.G:], atol=1e-5, rtol=1e-5)
