@@ -409,8 +409,16 @@ def cmd_train(args, argv) -> int:
         batches = BudgetedIterator(batches)
     control = _RUNTIME.control_group if _RUNTIME is not None else None
     last_batch = None
+    from .train.train_log import TrainLog, environment, environment_line
+
+    tlog = TrainLog(cfg.task_names, world=world, micro_batches=cfg.training.gradient_accumulation_steps,
+                    checkpoint_every=save_every if run is not None else 0)
+    if rank == 0:
+        print(environment_line(environment(cfg, world=world, device=device)), flush=True)
     try:
         while step < args.max_steps:
+            t_wait = time.perf_counter()
+            starved = False
             if voting:
                 try:
                     batch = batches.next_within(args.batch_budget_sec)
@@ -429,9 +437,11 @@ def cmd_train(args, argv) -> int:
                     if last_batch is None:
                         raise RuntimeError(f"rank {rank} has no training data while its peers train")
                     batch = zero_weight(last_batch)
+                    starved = True
                 last_batch = batch
             else:
                 batch = next(batches)
+            wait_s = time.perf_counter() - t_wait
             if device.type == "cuda":
                 batch = batch.to(device, non_blocking=True)
             res = abort_on_cuda_oom(trainer.train_step, batch)
@@ -440,8 +450,12 @@ def cmd_train(args, argv) -> int:
             if schedule is not None:  # same-thread prepare while the device runs the step
                 schedule()
             dog.beat("step", step)
+            if rank == 0:
+                tlog.step(res, batch, wait_s, starved)
             if step % args.log_every == 0 and rank == 0:
                 last = float(res.loss)
+                for line in tlog.lines(step, last):
+                    print(line, flush=True)
                 print(json.dumps({"step": step, "loss": last, "elapsed_s": round(time.time() - t0, 2)}), flush=True)
             if fixed.due(step):
                 dog.beat("fixed_test_eval", step)

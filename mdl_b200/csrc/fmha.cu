@@ -226,6 +226,14 @@ __device__ __forceinline__ void red_add_v4(float* dst, float a, float b, float c
                : "memory");
 }
 
+// Bits [l, h] (inclusive, clipped) of 32-column word w of a 128-column tile.
+__device__ __forceinline__ uint32_t range_bits(int l, int h, int w) {
+  const int a = max(l - 32 * w, 0), b = min(h - 32 * w, 31);
+  if (a > b) return 0u;
+  const uint32_t upto = b == 31 ? 0xFFFFFFFFu : ((1u << (b + 1)) - 1u);
+  return upto & (0xFFFFFFFFu << a);
+}
+
 // ============================================================================ forward
 // Work item = (sample, head, query tile); items are numbered heaviest first (query
 // tile 0 = the last 128 rows sees the most key tiles under causality).
@@ -462,17 +470,30 @@ __global__ void __launch_bounds__(F_THREADS, 2)
             for (int c = 0; c < TILE; ++c)
               if (c < lo || c > hi) sr[c] = __float_as_uint(-CUDART_INF_F);
           }
-        } else if (it.kst > kbase || (p.causal && (t == it.i || t == 0))) {
+        } else if (it.kst > kbase || t == it.i || t == 0) {
+          // (ktail > 0 implies causal.) The row's visible columns are at most two intervals:
+          // [lo, h1] (the causal part, or everything a global query sees) and [l2, h2] (the
+          // trailing global keys a sequence query sees). They become a 128-bit mask, so each
+          // column costs a bit test and a select instead of the full visibility expression.
           const int tail0 = Lk - p.ktail;
           const int excl0 = Lk - p.kexcl;  // keys from here on: only queries from here on see them
-          const bool q_tail = qrow >= tail0;
-          const bool q_excl = qrow >= excl0;
+          const int lo = it.kst - kbase;
+          int h1, l2 = TILE, h2 = -1;
+          if (qrow >= excl0) {
+            h1 = TILE - 1;
+          } else if (qrow >= tail0) {
+            h1 = excl0 - 1 - kbase;
+          } else {
+            h1 = qrow - kbase;
+            l2 = max(lo, tail0 - kbase);
+            h2 = excl0 - 1 - kbase;
+          }
 #pragma unroll
-          for (int c = 0; c < TILE; ++c) {
-            const int jj = kbase + c;
-            const bool vis = jj >= it.kst && (!p.causal || jj <= qrow || jj >= tail0 || q_tail) &&
-                             (jj < excl0 || q_excl);
-            if (!vis) sr[c] = __float_as_uint(-CUDART_INF_F);
+          for (int w = 0; w < 4; ++w) {
+            const uint32_t vm = range_bits(lo, h1, w) | range_bits(l2, h2, w);
+#pragma unroll
+            for (int c = 0; c < 32; ++c)
+              if (!((vm >> c) & 1u)) sr[32 * w + c] = __float_as_uint(-CUDART_INF_F);
           }
         }
         float mx8[8];  // eight independent partial maxima (short dependency chains)
