@@ -467,8 +467,12 @@ __global__ void __launch_bounds__(F_THREADS, 2)
           const int hi = (p.causal && t == it.i) ? r : TILE - 1;  // columns > hi are in the future
           if (lo > 0 || hi < TILE - 1) {
 #pragma unroll
-            for (int c = 0; c < TILE; ++c)
-              if (c < lo || c > hi) sr[c] = __float_as_uint(-CUDART_INF_F);
+            for (int w = 0; w < 4; ++w) {
+              const uint32_t vm = range_bits(lo, hi, w);
+#pragma unroll
+              for (int c = 0; c < 32; ++c)
+                if (!((vm >> c) & 1u)) sr[32 * w + c] = __float_as_uint(-CUDART_INF_F);
+            }
           }
         } else if (it.kst > kbase || t == it.i || t == 0) {
           // (ktail > 0 implies causal.) The row's visible columns are at most two intervals:
