@@ -358,7 +358,7 @@ void ln_bwd(const std::optional<at::Tensor>& dy, const std::optional<at::Tensor>
             const at::Tensor& a, const std::optional<at::Tensor>& b, const at::Tensor& mean, const at::Tensor& rstd,
             const std::optional<at::Tensor>& gamma, const at::Tensor& dx, const std::optional<at::Tensor>& dx2,
             const at::Tensor& partials, const std::optional<at::Tensor>& dgamma, const std::optional<at::Tensor>& dbeta,
-            int64_t B, int64_t T, int64_t D, bool mix, int64_t grid) {
+            int64_t B, int64_t T, int64_t D, bool mix, int64_t grid, const std::optional<at::Tensor>& res) {
   c10::cuda::CUDAGuard guard(a.device());
   mdl::LNBwdArgs p;
   p.dy = optr(dy);
@@ -371,6 +371,7 @@ void ln_bwd(const std::optional<at::Tensor>& dy, const std::optional<at::Tensor>
   p.gamma = optr<const float>(gamma);
   p.dx = dx.data_ptr();
   p.dx2 = optr(dx2);
+  p.res = optr(res);
   p.partials = ptr<float>(partials);
   p.dgamma = optr<float>(dgamma);
   p.dbeta = optr<float>(dbeta);
@@ -917,7 +918,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("compact_touched", &compact_touched);
   m.def("ln_fwd", &ln_fwd);
   m.def("ln_bwd_grid", &ln_bwd_grid);
-  m.def("ln_bwd", &ln_bwd);
+  m.def("ln_bwd", &ln_bwd, py::arg("dy"), py::arg("dy_bcast"), py::arg("bcast_scale"), py::arg("a"), py::arg("b"),
+        py::arg("mean"), py::arg("rstd"), py::arg("gamma"), py::arg("dx"), py::arg("dx2"), py::arg("partials"),
+        py::arg("dgamma"), py::arg("dbeta"), py::arg("B"), py::arg("T"), py::arg("D"), py::arg("mix"), py::arg("grid"),
+        py::arg("res") = py::none());
   m.def("rms_fwd", &rms_fwd);
   m.def("rms_bwd", &rms_bwd, py::arg("x"), py::arg("w"), py::arg("rstd"), py::arg("dy"), py::arg("dx"), py::arg("dw"),
         py::arg("rows"), py::arg("D"), py::arg("dres") = py::none(), py::arg("res_period") = 0,

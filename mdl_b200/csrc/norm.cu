@@ -141,6 +141,7 @@ __global__ void __launch_bounds__(256, NCH <= 4 ? 2 : 1) ln_bwd_kernel(const LNB
   const auto* dyb = reinterpret_cast<const __nv_bfloat16*>(p.dy_bcast);
   auto* dx = reinterpret_cast<__nv_bfloat16*>(p.dx);
   auto* dx2 = reinterpret_cast<__nv_bfloat16*>(p.dx2);
+  const auto* res = reinterpret_cast<const __nv_bfloat16*>(p.res);
   float* acc = sm + (MIX ? T * D : 0);
   float* my_dg = acc + warp * 2 * D;  // this warp's dgamma partials, then its dbeta partials
   float* my_db = my_dg + D;
@@ -227,8 +228,16 @@ __global__ void __launch_bounds__(256, NCH <= 4 ? 2 : 1) ln_bwd_kernel(const LNB
             const float4 x0 = d0[0], x1 = d0[1], y0 = d1[0], y1 = d1[1];
             const float o[8] = {x0.x + y0.x, x0.y + y0.y, x0.z + y0.z, x0.w + y0.w,
                                 x1.x + y1.x, x1.y + y1.y, x1.z + y1.z, x1.w + y1.w};
-            store8(dx + r * D + c, o);
             if (dx2 != nullptr) store8(dx2 + r * D + c, o);
+            if (res != nullptr) {
+              float rv[8], o2[8];
+              load8(res + r * D + c, rv);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) o2[e] = o[e] + rv[e];
+              store8(dx + r * D + c, o2);
+            } else {
+              store8(dx + r * D + c, o);
+            }
           }
         }
       }
@@ -245,8 +254,14 @@ __global__ void __launch_bounds__(256, NCH <= 4 ? 2 : 1) ln_bwd_kernel(const LNB
       for (int k = 0; k < NCH; ++k) {
         const int c = (lane + 32 * k) * 8;
         if (c < D) {
-          store8(dx + r * D + c, dv[k]);
           if (dx2 != nullptr) store8(dx2 + r * D + c, dv[k]);
+          if (res != nullptr) {
+            float rv[8];
+            load8(res + r * D + c, rv);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) dv[k][e] += rv[e];
+          }
+          store8(dx + r * D + c, dv[k]);
         }
       }
     }

@@ -25,8 +25,9 @@ cudaError_t layernorm_fwd(const LNFwdArgs& a, cudaStream_t stream);
 
 // Backward of the above. dy is [B,T,D] bf16, or (dy == null) dy[b,t,:] =
 // dy_bcast[b,:] * bcast_scale (backward of a mean over tokens).
-//   dx  = mix ? dv + mix(dv) : dv          (bf16)
-//   dx2 = dv (optional second copy, bf16)
+//   dx  = (mix ? dv + mix(dv) : dv) + res  (bf16; res optional, [B*T, D] bf16: a residual
+//                                           gradient added in the same pass)
+//   dx2 = dx without res (optional second copy, bf16)
 // gamma/beta gradients are written as per-CTA partial sums into `partials`
 // ([grid, 2 * D] fp32) and folded by a second kernel into dgamma and dbeta (+=).
 struct LNBwdArgs {
@@ -40,6 +41,7 @@ struct LNBwdArgs {
   const float* gamma = nullptr;
   void* dx = nullptr;
   void* dx2 = nullptr;
+  const void* res = nullptr;
   float* partials = nullptr;
   float* dgamma = nullptr;
   float* dbeta = nullptr;

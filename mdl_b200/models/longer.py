@@ -64,14 +64,17 @@ def _ln_fwd(x2d, w, b, eps):
     return out, mean, rstd
 
 
-def _ln_bwd(dy2d, x2d, mean, rstd, w, b):
+def _ln_bwd(dy2d, x2d, mean, rstd, w, b, res=None):
+    """LayerNorm backward; ``res`` (same shape, bf16) is added to the input gradient in the
+    same pass (a residual branch's gradient)."""
+
     rows, D = x2d.shape
     C = ext()
     grid = C.ln_bwd_grid(rows)
     partials = torch.empty(grid, 2 * D, dtype=torch.float32, device=x2d.device)
     dx = torch.empty_like(x2d)
     C.ln_bwd(dy2d.contiguous(), None, 1.0, x2d, None, mean, rstd, w, dx, None, partials, _grad(w), _grad(b), rows, 1,
-             D, False, grid)
+             D, False, grid, None if res is None else res.contiguous())
     return dx
 
 
@@ -143,8 +146,7 @@ class LongerBlockFn(torch.autograd.Function):
         bgemm(du, _shadow(blk.w1), dhn, M=B * Lq, N=D, K=Hd, lda=Hd, ldb=D, b_mn=True, ldc=D)
         bgemm(du, hn, _grad(blk.w1), M=Hd, N=D, K=B * Lq, lda=Hd, a_mn=True, ldb=D, b_mn=True, ldc=D, accumulate=True)
         del du
-        dh = _ln_bwd(dhn, h.view(B * Lq, D), mean_f, rstd_f, blk.lnf_w, blk.lnf_b)
-        dh += dY
+        dh = _ln_bwd(dhn, h.view(B * Lq, D), mean_f, rstd_f, blk.lnf_w, blk.lnf_b, res=dY)
         # output projection
         datt = torch.empty_like(dh)
         bgemm(dh, _shadow(blk.wo), datt, M=B * Lq, N=D, K=D, lda=D, ldb=D, b_mn=True, ldc=D)
@@ -177,8 +179,8 @@ class LongerBlockFn(torch.autograd.Function):
         C.colsum(dkv, _grad(blk.bkv), 1, B * Lk, 2 * D, 3 * D, 0, 1.0)
         del dqkv
         dX = _ln_bwd(dxk, X.view(B * Lk, D), mean_k, rstd_k, blk.lnk_w, blk.lnk_b).view(B, Lk, D)
-        dxq_in = _ln_bwd(dxq, xq_in, mean_q, rstd_q, blk.lnq_w, blk.lnq_b).view(B, Lq, D)
-        dX[:, Lk - Lq:] += dxq_in + dh.view(B, Lq, D)
+        dxq_in = _ln_bwd(dxq, xq_in, mean_q, rstd_q, blk.lnq_w, blk.lnq_b, res=dh).view(B, Lq, D)
+        dX[:, Lk - Lq:] += dxq_in
         return dX, None, None, None, None, None, None, None
 
 

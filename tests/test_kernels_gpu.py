@@ -117,6 +117,15 @@ def test_layernorm_fused(mix, B, T, D):
         torch.testing.assert_close(dx2.float(), rf.grad, atol=8e-2, rtol=3e-2)
     torch.testing.assert_close(dg, gf.grad, atol=0.5, rtol=2e-2)
     torch.testing.assert_close(db, bf.grad, atol=0.5, rtol=2e-2)
+    # a residual gradient added in the same pass: dx + res, dx2 unchanged
+    res = torch.randn(B, T, D, device="cuda").bfloat16()
+    dxr = torch.empty_like(x)
+    dx2r = torch.empty_like(x)
+    C.ln_bwd(dy, None, 1.0, x, None if mix else r, mean, rstd, g, dxr, dx2r, partials, dg, db, B, T, D, mix, grid,
+             res)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(dxr.float(), dx.float() + res.float(), atol=2e-2, rtol=1e-2)
+    torch.testing.assert_close(dx2r, dx2)
 
 
 @pytest.mark.parametrize("D", [256, 512, 1024])
