@@ -12,6 +12,8 @@
 // 64-key tiles of K and V (fp32) in shared memory and every thread runs an online
 // softmax in base 2 over 16-key chunks (one rescale per chunk). Causal CTAs stop at their
 // last query row and then visit only the trailing always-visible tokens.
+// Few queries over many keys (Lq <= 64, head width <= 16): the key tiles are split over a
+// CTA's four warps instead (see attn_simt_fwd_split_kernel).
 // Backward (three launches): D_q = dO . O per query; dQ with a thread per query row
 // (recomputing P from the saved log-sum-exp); dK and dV with a thread per key row over
 // staged query tiles. Every element of dqkv is written by exactly one thread (no
@@ -143,6 +145,203 @@ __global__ void __launch_bounds__(kRows) attn_simt_fwd_kernel(AttnSimtArgs a) {
 #pragma unroll
   for (int d = 0; d < HD; ++d) out[d] = __float2bfloat16(o[d] * inv);
   a.lse[(static_cast<long long>(b) * a.H + h) * a.Lq + qi] = any ? m + log2f(l) : CUDART_INF_F;
+}
+
+// ---- few queries (LONGER cross blocks: R + G of a few dozen over thousands of keys)
+// A CTA takes 32 query rows and splits the key tiles over its four warps (tile k to warp
+// k % 4, each staging its own tiles: warp-local synchronisation only); the four partial
+// (max, sum, accumulator) triples are merged through shared memory at the end, so all 128
+// threads work although the query count is far below 128.
+constexpr int kSplit = 4;
+constexpr int kSplitRows = 32;
+
+__device__ __forceinline__ void split_coords(int rows, int& b, int& blk) {
+  const int nblk = (rows + kSplitRows - 1) / kSplitRows;
+  b = static_cast<int>(blockIdx.x / nblk);
+  blk = static_cast<int>(blockIdx.x - static_cast<unsigned>(b) * nblk);
+}
+
+template <int HD>
+__device__ __forceinline__ void stage_warp(float (*s)[HD], const __nv_bfloat16* base, long long row_stride, int col0,
+                                           int lo, int hi, int lane) {
+  for (int i = lane; i < kTile * HD; i += 32) {
+    const int r = i / HD, c = i % HD;
+    const int j = lo + r;
+    s[r][c] = j < hi ? __bfloat162float(base[static_cast<long long>(j) * row_stride + col0 + c]) : 0.f;
+  }
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kSplit * 32) attn_simt_fwd_split_kernel(AttnSimtArgs a) {
+  __shared__ float sK[kSplit][kTile][HD];
+  __shared__ float sV[kSplit][kTile][HD];
+  __shared__ float sM[kSplit][kSplitRows], sL[kSplit][kSplitRows];
+  __shared__ float sO[kSplit][kSplitRows][HD + 1];
+  int b, blk;
+  split_coords(a.Lq, b, blk);
+  const int h = blockIdx.y;
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qi = blk * kSplitRows + lane;
+  const int D = a.H * HD;
+  const long long rs = 3LL * D;
+  const __nv_bfloat16* base = a.qkv + static_cast<long long>(b) * a.Lk * rs;
+  const Vis vis = make_vis(a, b);
+  const int p = a.Lk - a.Lq + qi;
+  const bool qvalid = qi < a.Lq && p >= vis.kst;
+  float q[HD], o[HD];
+#pragma unroll
+  for (int d = 0; d < HD; ++d) {
+    q[d] = qvalid ? __bfloat162float(base[static_cast<long long>(p) * rs + h * HD + d]) * a.scale * kLog2e : 0.f;
+    o[d] = 0.f;
+  }
+  float m = -CUDART_INF_F, l = 0.f;
+  const int last_p = a.Lk - a.Lq + min(a.Lq, (blk + 1) * kSplitRows) - 1;
+  const int hi = a.causal ? min(a.Lk, last_p + 1) : a.Lk;
+  const int tail_lo = a.causal ? max(hi, vis.tail0) : a.Lk;
+  int idx = 0;
+  for (int range = 0; range < 2; ++range) {
+    const int r0 = range == 0 ? vis.kst : max(tail_lo, vis.kst);
+    const int r1 = range == 0 ? hi : a.Lk;
+    for (int j0 = r0; j0 < r1; j0 += kTile, ++idx) {
+      if (idx % kSplit != w) continue;
+      __syncwarp();
+      stage_warp<HD>(sK[w], base, rs, D + h * HD, j0, r1, lane);
+      stage_warp<HD>(sV[w], base, rs, 2 * D + h * HD, j0, r1, lane);
+      __syncwarp();
+      if (!qvalid) continue;
+      const int n = min(kTile, r1 - j0);
+      constexpr int kChunk = chunk_of<HD>();
+      for (int c0 = 0; c0 < n; c0 += kChunk) {
+        float s[kChunk];
+        float mc = m;
+#pragma unroll
+        for (int u = 0; u < kChunk; ++u) {
+          const int jj = c0 + u;
+          float t = -CUDART_INF_F;
+          if (jj < n && vis(p, j0 + jj)) {
+            t = 0.f;
+#pragma unroll
+            for (int d = 0; d < HD; ++d) t = fmaf(q[d], sK[w][jj][d], t);
+          }
+          s[u] = t;
+          mc = fmaxf(mc, t);
+        }
+        if (mc == -CUDART_INF_F) continue;
+        const float corr = exp2f(m - mc);
+        l *= corr;
+#pragma unroll
+        for (int d = 0; d < HD; ++d) o[d] *= corr;
+#pragma unroll
+        for (int u = 0; u < kChunk; ++u) {
+          if (s[u] == -CUDART_INF_F) continue;
+          const float pr = exp2f(s[u] - mc);
+          l += pr;
+#pragma unroll
+          for (int d = 0; d < HD; ++d) o[d] = fmaf(pr, sV[w][c0 + u][d], o[d]);
+        }
+        m = mc;
+      }
+    }
+  }
+  sM[w][lane] = m;
+  sL[w][lane] = l;
+#pragma unroll
+  for (int d = 0; d < HD; ++d) sO[w][lane][d] = o[d];
+  __syncthreads();
+  if (w != 0 || qi >= a.Lq) return;
+  float M = -CUDART_INF_F;
+#pragma unroll
+  for (int g = 0; g < kSplit; ++g) M = fmaxf(M, sM[g][lane]);
+  float L = 0.f, O[HD];
+#pragma unroll
+  for (int d = 0; d < HD; ++d) O[d] = 0.f;
+  if (M != -CUDART_INF_F) {
+#pragma unroll
+    for (int g = 0; g < kSplit; ++g) {
+      if (sM[g][lane] == -CUDART_INF_F) continue;
+      const float f = exp2f(sM[g][lane] - M);
+      L += sL[g][lane] * f;
+#pragma unroll
+      for (int d = 0; d < HD; ++d) O[d] = fmaf(sO[g][lane][d], f, O[d]);
+    }
+  }
+  const bool any = qvalid && L > 0.f;
+  const float inv = any ? 1.f / L : 0.f;
+  __nv_bfloat16* out = a.out + (static_cast<long long>(b) * a.Lq + qi) * D + h * HD;
+#pragma unroll
+  for (int d = 0; d < HD; ++d) out[d] = __float2bfloat16(O[d] * inv);
+  a.lse[(static_cast<long long>(b) * a.H + h) * a.Lq + qi] = any ? M + log2f(L) : CUDART_INF_F;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kSplit * 32) attn_simt_dq_split_kernel(AttnSimtArgs a) {
+  __shared__ float sK[kSplit][kTile][HD];
+  __shared__ float sV[kSplit][kTile][HD];
+  __shared__ float sQ[kSplit][kSplitRows][HD + 1];  // the warps' partial dQ
+  int b, blk;
+  split_coords(a.Lq, b, blk);
+  const int h = blockIdx.y;
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qi = blk * kSplitRows + lane;
+  const int D = a.H * HD;
+  const long long rs = 3LL * D;
+  const __nv_bfloat16* base = a.qkv + static_cast<long long>(b) * a.Lk * rs;
+  const Vis vis = make_vis(a, b);
+  const int p = a.Lk - a.Lq + qi;
+  const long long qoff = (static_cast<long long>(b) * a.H + h) * a.Lq + qi;
+  const float lse = qi < a.Lq ? a.lse[qoff] : CUDART_INF_F;
+  const bool qvalid = qi < a.Lq && p >= vis.kst && lse != CUDART_INF_F;
+  const float c2 = a.scale * kLog2e;
+  float q[HD], dO[HD], dq[HD];
+  const long long ooff = (static_cast<long long>(b) * a.Lq + qi) * D + h * HD;
+#pragma unroll
+  for (int d = 0; d < HD; ++d) {
+    q[d] = qvalid ? __bfloat162float(base[static_cast<long long>(p) * rs + h * HD + d]) * c2 : 0.f;
+    dO[d] = qvalid ? __bfloat162float(a.dout[ooff + d]) : 0.f;
+    dq[d] = 0.f;
+  }
+  const float Dq = qvalid ? a.dsum[qoff] : 0.f;
+  const int last_p = a.Lk - a.Lq + min(a.Lq, (blk + 1) * kSplitRows) - 1;
+  const int hi = a.causal ? min(a.Lk, last_p + 1) : a.Lk;
+  const int tail_lo = a.causal ? max(hi, vis.tail0) : a.Lk;
+  int idx = 0;
+  for (int range = 0; range < 2; ++range) {
+    const int r0 = range == 0 ? vis.kst : max(tail_lo, vis.kst);
+    const int r1 = range == 0 ? hi : a.Lk;
+    for (int j0 = r0; j0 < r1; j0 += kTile, ++idx) {
+      if (idx % kSplit != w) continue;
+      __syncwarp();
+      stage_warp<HD>(sK[w], base, rs, D + h * HD, j0, r1, lane);
+      stage_warp<HD>(sV[w], base, rs, 2 * D + h * HD, j0, r1, lane);
+      __syncwarp();
+      if (!qvalid) continue;
+      const int n = min(kTile, r1 - j0);
+      for (int jj = 0; jj < n; ++jj) {
+        if (!vis(p, j0 + jj)) continue;
+        float s = 0.f, dp = 0.f;
+#pragma unroll
+        for (int d = 0; d < HD; ++d) {
+          s = fmaf(q[d], sK[w][jj][d], s);
+          dp = fmaf(dO[d], sV[w][jj][d], dp);
+        }
+        const float ds = exp2f(s - lse) * (dp - Dq);
+#pragma unroll
+        for (int d = 0; d < HD; ++d) dq[d] = fmaf(ds, sK[w][jj][d], dq[d]);
+      }
+    }
+  }
+#pragma unroll
+  for (int d = 0; d < HD; ++d) sQ[w][lane][d] = dq[d];
+  __syncthreads();
+  if (w != 0 || qi >= a.Lq) return;
+  __nv_bfloat16* dst = a.dqkv + (static_cast<long long>(b) * a.Lk + p) * rs + h * HD;
+#pragma unroll
+  for (int d = 0; d < HD; ++d) {
+    float t = 0.f;
+#pragma unroll
+    for (int g = 0; g < kSplit; ++g) t += sQ[g][lane][d];
+    dst[d] = __float2bfloat16(t * a.scale);
+  }
 }
 
 // D_q = sum_d dO[q, d] * O[q, d] per (b, h, q).
@@ -299,8 +498,21 @@ __global__ void __launch_bounds__(kRows) attn_simt_dkv_kernel(AttnSimtArgs a) {
   }
 }
 
+// Few queries per sample: the key-split kernels (every thread busy); otherwise a thread per query.
+template <int HD>
+bool use_split(const AttnSimtArgs& a) {
+  return HD <= 16 && a.Lq <= 2 * kSplitRows && a.Lk >= 4 * kTile;
+}
+
 template <int HD>
 cudaError_t launch_fwd(const AttnSimtArgs& a, cudaStream_t st) {
+  if constexpr (HD <= 16) {
+    if (use_split<HD>(a)) {
+      const dim3 g(static_cast<unsigned>(a.B) * ((a.Lq + kSplitRows - 1) / kSplitRows), a.H);
+      attn_simt_fwd_split_kernel<HD><<<g, kSplit * 32, 0, st>>>(a);
+      return cudaGetLastError();
+    }
+  }
   const dim3 grid(static_cast<unsigned>(a.B) * ((a.Lq + kRows - 1) / kRows), a.H);
   attn_simt_fwd_kernel<HD><<<grid, kRows, 0, st>>>(a);
   return cudaGetLastError();
@@ -312,7 +524,15 @@ cudaError_t launch_bwd(const AttnSimtArgs& a, cudaStream_t st) {
   attn_simt_dsum_kernel<HD><<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  attn_simt_dq_kernel<HD><<<dim3(static_cast<unsigned>(a.B) * ((a.Lq + kRows - 1) / kRows), a.H), kRows, 0, st>>>(a);
+  bool split = false;
+  if constexpr (HD <= 16) {
+    split = use_split<HD>(a);
+    if (split)
+      attn_simt_dq_split_kernel<HD>
+          <<<dim3(static_cast<unsigned>(a.B) * ((a.Lq + kSplitRows - 1) / kSplitRows), a.H), kSplit * 32, 0, st>>>(a);
+  }
+  if (!split)
+    attn_simt_dq_kernel<HD><<<dim3(static_cast<unsigned>(a.B) * ((a.Lq + kRows - 1) / kRows), a.H), kRows, 0, st>>>(a);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   attn_simt_dkv_kernel<HD><<<dim3(static_cast<unsigned>(a.B) * ((a.Lk + kRows - 1) / kRows), a.H), kRows, 0, st>>>(a);

@@ -200,6 +200,8 @@ SIMT_CASES = [
     (16, 2, 257, 130, 2, [0, 64], True, 0, 0),        # OneTrans-style suffix
     (64, 2, 180, 100, 4, [3, 90], True, 0, 0),        # OneTrans d=256 / 4 heads
     (8, 700, 2, 2, 4, [0, 1] * 350, False, 0, 0),     # LONGER inner blocks: many tiny groups
+    (8, 3, 2051, 35, 4, [0, 1500, 2050], True, 3, 1),  # production LONGER cross block: key-split kernels
+    (16, 2, 700, 64, 2, [0, 650], False, 0, 0),       # key-split, non-causal, two 32-row blocks
 ]
 
 
