@@ -63,9 +63,19 @@ class PackedBatch:
         for name, seq in sequences.items():
             for k, v in seq.items():
                 (i64_parts if v.dtype == torch.int64 else f32_parts).append((f"seq:{name}:{k}", v))
+        lease = None
+        bufs = {}
+        if pin:  # both flat buffers from one slot of the pinned pool (returned with the batch)
+            from .pinned import default_pool
+
+            specs = [(dt, max(1, sum(p.numel() for _, p in parts if p is not None)))
+                     for dt, parts in ((torch.int64, i64_parts), (torch.float32, f32_parts))]
+            views, lease = default_pool().checkout(specs)
+            bufs = {torch.int64: views[0], torch.float32: views[1]}
+
         def flat(parts, dtype):
             total = sum(p.numel() for _, p in parts if p is not None)
-            buf = torch.empty(max(total, 1), dtype=dtype, pin_memory=pin)
+            buf = bufs[dtype] if pin else torch.empty(max(total, 1), dtype=dtype)
             views = {}
             off = 0
             for name, p in parts:
@@ -79,7 +89,9 @@ class PackedBatch:
             return buf, views
         b64, v64 = flat(i64_parts, torch.int64)
         b32, v32 = flat(f32_parts, torch.float32)
-        return PackedBatch._from_flat(b64, v64, b32, v32, rows)
+        batch = PackedBatch._from_flat(b64, v64, b32, v32, rows)
+        batch._lease = lease
+        return batch
 
     @staticmethod
     def _from_flat(b64, v64, b32, v32, rows):
@@ -114,6 +126,11 @@ class PackedBatch:
         b64, b32 = self._flat
         d64 = b64.to(device, non_blocking=non_blocking)
         d32 = b32.to(device, non_blocking=non_blocking)
+        lease = getattr(self, "_lease", None)
+        if lease is not None and torch.device(device).type == "cuda":
+            ev = torch.cuda.Event()
+            ev.record()
+            lease.fence(ev)  # the pinned slot is reusable once the copies have run
         v64, v32 = self._views
         return PackedBatch._from_flat(d64, v64, d32, v32, self.rows)
 
