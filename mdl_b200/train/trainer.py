@@ -231,6 +231,28 @@ class Trainer:
             loss_out.copy_(result.loss.reshape(loss_out.shape), non_blocking=True)
         return result
 
+    def train_from_host(self, host_batches, loss_out: torch.Tensor | None = None) -> int:
+        """Public end-to-end loop: train one step per (pinned) host batch, copying batch
+        k+1 to the device on a side stream while step k runs, and the loss of step i into
+        ``loss_out[i]`` (pinned host) without a host sync. Returns the number of steps."""
+
+        n = 0
+        if self.device.type != "cuda":
+            for b in host_batches:
+                res = self.train_step(b)
+                if loss_out is not None:
+                    loss_out[n:n + 1].copy_(res.loss.reshape(1))
+                n += 1
+            return n
+        from ..data.parquet import DevicePrefetcher
+
+        for dev in DevicePrefetcher(host_batches, self.device):
+            res = self.train_step(dev)
+            if loss_out is not None:
+                loss_out[n:n + 1].copy_(res.loss.reshape(1), non_blocking=True)
+            n += 1
+        return n
+
     @torch.no_grad()
     def predict_logits(self, batch) -> torch.Tensor:
         out = self.model(batch, task_scale=self.task_scale(batch))

@@ -64,3 +64,26 @@ def test_cli_train_prints_stable_prefixes():
     steps = [l for l in lines if l.startswith("Train step | ")]
     assert [l.split()[3] for l in steps] == ["step=2", "step=4"]
     assert any(l.startswith("Train task | step=4 task=") for l in lines)
+
+
+def test_train_from_host_matches_train_step():
+    from mdl_b200.config import app_config_from_mapping
+    from mdl_b200.data.baseline_configs import baseline_config
+    from mdl_b200.data.synthetic import SyntheticGenerator
+    from mdl_b200.models.factory import build_model
+    from mdl_b200.train.trainer import Trainer
+
+    m, spec = baseline_config(1)
+    cfg = app_config_from_mapping(m)
+    torch.manual_seed(0)
+    model = build_model(cfg, device="cpu", base_seed=1)
+    gen = SyntheticGenerator(model.encoder.batch_plan, spec)
+    batches = [gen.batch(64) for _ in range(3)]
+    a = Trainer(cfg, model, device=torch.device("cpu"))
+    losses = torch.zeros(3)
+    assert a.train_from_host(iter(batches), loss_out=losses) == 3 and a.step_index == 3
+    torch.manual_seed(0)
+    model2 = build_model(cfg, device="cpu", base_seed=1)
+    b = Trainer(cfg, model2, device=torch.device("cpu"))
+    ref = [float(b.train_step(x).loss) for x in batches]
+    torch.testing.assert_close(losses, torch.tensor(ref))
