@@ -691,10 +691,13 @@ class DevicePrefetcher:
     """Copies batch k+1 host->device on a side CUDA stream while step k runs; the consumer's
     stream waits on an event and the tensors are recorded on it (no host sync)."""
 
-    def __init__(self, batches, device: torch.device) -> None:
+    def __init__(self, batches, device: torch.device, stream: torch.cuda.Stream | None = None) -> None:
+        """``stream``: the copy stream to use (reuse one across prefetchers: the caching
+        allocator keeps its blocks per stream, so a fresh stream starts with none)."""
+
         self.it = iter(batches)
         self.device = torch.device(device)
-        self.stream = torch.cuda.Stream(device=self.device)
+        self.stream = stream if stream is not None else torch.cuda.Stream(device=self.device)
         self._next = None
         self._preload()
 

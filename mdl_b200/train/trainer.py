@@ -246,7 +246,9 @@ class Trainer:
             return n
         from ..data.parquet import DevicePrefetcher
 
-        for dev in DevicePrefetcher(host_batches, self.device):
+        if getattr(self, "_copy_stream", None) is None:
+            self._copy_stream = torch.cuda.Stream(device=self.device)  # one per trainer (allocator pools)
+        for dev in DevicePrefetcher(host_batches, self.device, self._copy_stream):
             res = self.train_step(dev)
             if loss_out is not None:
                 loss_out[n:n + 1].copy_(res.loss.reshape(1), non_blocking=True)
