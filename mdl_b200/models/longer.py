@@ -406,7 +406,7 @@ class LongerEncoder(nn.Module):
         return self.step(seq_in, native).view(rows, L, self.Din)
 
     def forward(self, seq_in, lengths, target_in, user_in, native: bool, cls_tokens=None,
-                tokens=None, summary_only: bool = False) -> torch.Tensor:
+                tokens=None, summary_only: bool = False, user_tokens=None, cand_tokens=None) -> torch.Tensor:
         """``tokens``: event tokens already projected (``project``), else ``seq_in`` is projected here.
         ``summary_only``: return only the ``G`` global tokens; the last block then runs only
         their queries (reference ``forward_request_summary`` ``src/model.py:1906-2004``: the
@@ -429,14 +429,18 @@ class LongerEncoder(nn.Module):
             kst = kst + (R - L)
             L = R
         parts = [tokens]
+        # user_tokens / cand_tokens: global tokens given directly ([B, Gu, D] / [B, Gc, D])
+        # instead of projected from user_in / target_in
         if self.Gu:
-            parts.append(self.user_mlp(user_in, native).view(B, self.Gu, D))
+            parts.append(user_tokens.to(tokens.dtype) if user_tokens is not None
+                         else self.user_mlp(user_in, native).view(B, self.Gu, D))
         if self.Gx:
             if cls_tokens is None:
                 raise ValueError("LONGER encoder built with extra global tokens needs cls_tokens")
             parts.append(cls_tokens.to(tokens.dtype).expand(B, -1, -1))
         if self.Gc:
-            parts.append(self.cand_mlp(target_in, native).view(B, self.Gc, D))
+            parts.append(cand_tokens.to(tokens.dtype) if cand_tokens is not None
+                         else self.cand_mlp(target_in, native).view(B, self.Gc, D))
         X = torch.cat(parts, dim=1) if len(parts) > 1 else tokens
         # [B, R + G, D]: [recent; globals]. Recent queries: bottom-right causal; user / CLS globals:
         # every valid key; the candidate globals (last Gc) are seen by nobody else, so every
@@ -447,12 +451,31 @@ class LongerEncoder(nn.Module):
         lq = G if (summary_only and nblk == 1) else R + G
         X = self.cross(X, kst, lq, self.heads, True, G, native, kexcl=self.Gc)
         kst = (kst - (L - R)).clamp(min=0)
+        # recent rows of padding (sequences shorter than R) are zeroed after every block,
+        # as the reference masks its recent outputs (src/model.py:1782-1785, 1874-1877)
+        keep = self._recent_keep(kst, R, G, X)
+        if keep is not None and X.shape[1] == R + G:
+            X = X * keep
         for i, blk in enumerate(self.selfs):
             # self blocks: the same visibility over [recent; globals] (reference mixed mask
             # over [user; recent], candidates over everything)
             lq = G if (summary_only and i == nblk - 2) else R + G
             X = blk(X, kst, lq, self.heads, True, G, native, kexcl=self.Gc)
+            if keep is not None and X.shape[1] == R + G:
+                X = X * keep
         return X
+
+    @staticmethod
+    def _recent_keep(kst, R, G, X):
+        """``[B, R + G, 1]`` row mask (0 for padded recent rows), or None when no sample is
+        shorter than ``R`` (a host-side check is avoided: the mask is always applied when
+        any padding row can exist, i.e. kst > 0 is possible)."""
+
+        if R == 0:
+            return None
+        rows = torch.arange(R + G, device=X.device).view(1, -1)
+        keep = (rows >= kst.to(X.device).view(-1, 1)) | (rows >= R)
+        return keep.unsqueeze(-1).to(X.dtype)
 
     def _request_tokens(self, tokens, lengths, user_in, cls_tokens, native: bool):
         """Request-side rows ``[sequence; user; CLS]`` and their padding count."""
@@ -492,10 +515,15 @@ class LongerEncoder(nn.Module):
         ksts.append(kst)
         X = self.cross.forward_reference(X, kst, R + Gr, self.heads, True, Gr)
         kst = (kst - (L - R)).clamp(min=0)
+        keep = self._recent_keep(kst, R, Gr, X)
+        if keep is not None:
+            X = X * keep
         for blk in self.selfs:
             kv.append(blk.request_kv(X))
             ksts.append(kst)
             X = blk.forward_reference(X, kst, R + Gr, self.heads, True, Gr)
+            if keep is not None:
+                X = X * keep
         return {"kv": kv, "kstart": ksts, "out": X, "lengths": lengths}
 
     @torch.no_grad()
