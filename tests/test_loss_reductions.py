@@ -118,3 +118,35 @@ def test_request_level_sequence_work_matches_per_candidate_sequences():
         results.append((float(out["loss"].detach()), tr.dense.grad.clone()))
     assert abs(results[0][0] - results[1][0]) < 1e-5, results
     torch.testing.assert_close(results[0][1], results[1][1], rtol=1e-4, atol=1e-6)
+
+
+@pytest.mark.parametrize("weighted", [False, True])
+@pytest.mark.parametrize("reduction", ["sum", "mean_per_task", "mean_per_request_per_task"])
+def test_loss_matches_reference_module(reduction, weighted):
+    """The training step's loss against the reference's own ``_loss_terms_from_batch`` on
+    the same logits, labels, label mask, candidate-to-request map and task loss weights."""
+
+    from baseline import install
+
+    if not install.installed():
+        pytest.skip("reference not installed under baseline/_ref")
+    from baseline import reference_harness as rh
+
+    rh._import_reference()
+    from src.dataloader import FeatureBatch
+    from src.train import _loss_terms_from_batch
+
+    cfg, model, tr, batch = _setup(reduction)
+    weights = None
+    if weighted:
+        weights = tuple(0.5 + i for i in range(len(cfg.task_names)))
+        tr.task_weights = torch.tensor(weights, dtype=tr.task_weights.dtype)
+    out = tr.forward_backward(batch)
+    logits = out["logits"].detach().float()
+    ri = batch.sequences["hist"]["row_indices"]
+    ref_batch = FeatureBatch(features={"hist": {"row_indices": ri}}, labels=batch.labels.float(),
+                             label_mask=batch.label_mask.float(),
+                             scenario_id=torch.zeros(batch.rows, dtype=torch.long), group_id=[])
+    want, _, _ = _loss_terms_from_batch({"logits": logits}, ref_batch, loss_reduction=reduction,
+                                     task_loss_weights=weights)
+    torch.testing.assert_close(out["loss"].detach().float(), want, rtol=1e-5, atol=1e-6)
