@@ -32,6 +32,9 @@ constexpr int kTile = 64;    // staged rows of the other side
 template <int HD>
 __host__ __device__ constexpr int chunk_of() { return HD >= 64 ? 4 : 16; }
 constexpr float kLog2e = 1.4426950408889634f;
+// threads per key row in the dK/dV kernel
+template <int HD>
+__host__ __device__ constexpr int keys_split() { return HD >= 64 ? 2 : 1; }
 
 struct Vis {
   int Lk, Lq, kst, causal, tail0, excl0;
@@ -421,33 +424,40 @@ __global__ void __launch_bounds__(kRows) attn_simt_dq_kernel(AttnSimtArgs a) {
 
 template <int HD>
 __global__ void __launch_bounds__(kRows) attn_simt_dkv_kernel(AttnSimtArgs a) {
+  // Wide heads (64) split a key's head dimension over TPK adjacent threads (dot products
+  // completed with a shuffle), so each thread's K, V, dK and dV accumulators stay in registers.
+  constexpr int TPK = keys_split<HD>();
+  constexpr int HW = HD / TPK;         // dimensions per thread
+  constexpr int KPC = kRows / TPK;     // keys per CTA
   __shared__ float sQ[kTile][HD];
   __shared__ float sO[kTile][HD];  // dO of the staged queries
   __shared__ float sL[kTile];      // their log-sum-exp
   __shared__ float sD[kTile];      // their D_q
-  int b, blk;
-  block_coords(a.Lk, b, blk);
+  const int nblk = (a.Lk + KPC - 1) / KPC;
+  const int b = static_cast<int>(blockIdx.x / nblk);
+  const int blk = static_cast<int>(blockIdx.x - static_cast<unsigned>(b) * nblk);
   const int h = blockIdx.y;
-  const int j = blk * kRows + threadIdx.x;  // key row
+  const int j = blk * KPC + static_cast<int>(threadIdx.x) / TPK;  // key row
+  const int d0 = (static_cast<int>(threadIdx.x) % TPK) * HW;     // this thread's dimensions
   const int D = a.H * HD;
   const long long rs = 3LL * D;
   const __nv_bfloat16* base = a.qkv + static_cast<long long>(b) * a.Lk * rs;
   const Vis vis = make_vis(a, b);
   const bool kvalid = j < a.Lk && j >= vis.kst;
   const float c2 = a.scale * kLog2e;
-  float k[HD], v[HD], dk[HD], dv[HD];
+  float k[HW], v[HW], dk[HW], dv[HW];
 #pragma unroll
-  for (int d = 0; d < HD; ++d) {
-    k[d] = kvalid ? __bfloat162float(base[static_cast<long long>(j) * rs + D + h * HD + d]) : 0.f;
-    v[d] = kvalid ? __bfloat162float(base[static_cast<long long>(j) * rs + 2 * D + h * HD + d]) : 0.f;
+  for (int d = 0; d < HW; ++d) {
+    k[d] = kvalid ? __bfloat162float(base[static_cast<long long>(j) * rs + D + h * HD + d0 + d]) : 0.f;
+    v[d] = kvalid ? __bfloat162float(base[static_cast<long long>(j) * rs + 2 * D + h * HD + d0 + d]) : 0.f;
     dk[d] = 0.f;
     dv[d] = 0.f;
   }
   // queries that may see keys of this CTA: rows >= the first key row (causal) or every
   // query when the CTA holds trailing tokens; all queries otherwise
   const int q_first = a.Lk - a.Lq;
-  const int jmin = blk * kRows;
-  const int jmax = min(a.Lk, jmin + kRows) - 1;
+  const int jmin = blk * KPC;
+  const int jmax = min(a.Lk, jmin + KPC) - 1;
   int p_lo = max(q_first, vis.kst);
   if (a.causal && jmax < vis.tail0) p_lo = max(p_lo, jmin);
   const __nv_bfloat16* dO_base = a.dout + static_cast<long long>(b) * a.Lq * D + h * HD;
@@ -468,6 +478,8 @@ __global__ void __launch_bounds__(kRows) attn_simt_dkv_kernel(AttnSimtArgs a) {
       sD[r] = ok ? a.dsum[lbase + (p - q_first)] : 0.f;
     }
     __syncthreads();
+    // threads of one key stay together (the partial dot products meet in a shuffle), so a
+    // key group skips as a whole: j and the visibility are the same for its TPK threads
     if (!kvalid) continue;
     const int n = min(kTile, a.Lk - p0);
     for (int r = 0; r < n; ++r) {
@@ -475,23 +487,31 @@ __global__ void __launch_bounds__(kRows) attn_simt_dkv_kernel(AttnSimtArgs a) {
       if (sL[r] == CUDART_INF_F || !vis(p, j)) continue;
       float s = 0.f, dp = 0.f;
 #pragma unroll
-      for (int d = 0; d < HD; ++d) {
-        s = fmaf(sQ[r][d], k[d], s);
-        dp = fmaf(sO[r][d], v[d], dp);
+      for (int d = 0; d < HW; ++d) {
+        s = fmaf(sQ[r][d0 + d], k[d], s);
+        dp = fmaf(sO[r][d0 + d], v[d], dp);
+      }
+      if constexpr (TPK > 1) {
+        const unsigned grp = ((1u << TPK) - 1u) << ((threadIdx.x & 31) & ~(TPK - 1));
+#pragma unroll
+        for (int o = 1; o < TPK; o <<= 1) {
+          s += __shfl_xor_sync(grp, s, o, TPK);
+          dp += __shfl_xor_sync(grp, dp, o, TPK);
+        }
       }
       const float pr = exp2f(s - sL[r]);
       const float ds = pr * (dp - sD[r]);
 #pragma unroll
-      for (int d = 0; d < HD; ++d) {
-        dv[d] = fmaf(pr, sO[r][d], dv[d]);
-        dk[d] = fmaf(ds, sQ[r][d], dk[d]);  // sQ holds q * scale * log2(e)
+      for (int d = 0; d < HW; ++d) {
+        dv[d] = fmaf(pr, sO[r][d0 + d], dv[d]);
+        dk[d] = fmaf(ds, sQ[r][d0 + d], dk[d]);  // sQ holds q * scale * log2(e)
       }
     }
   }
   if (j >= a.Lk) return;
-  __nv_bfloat16* dst = a.dqkv + (static_cast<long long>(b) * a.Lk + j) * rs + h * HD;
+  __nv_bfloat16* dst = a.dqkv + (static_cast<long long>(b) * a.Lk + j) * rs + h * HD + d0;
 #pragma unroll
-  for (int d = 0; d < HD; ++d) {
+  for (int d = 0; d < HW; ++d) {
     dst[D + d] = __float2bfloat16(dk[d] / kLog2e);
     dst[2 * D + d] = __float2bfloat16(dv[d]);
     if (j < q_first) dst[d] = __float2bfloat16(0.f);  // Q rows that are not queries
@@ -535,14 +555,15 @@ cudaError_t launch_bwd(const AttnSimtArgs& a, cudaStream_t st) {
     attn_simt_dq_kernel<HD><<<dim3(static_cast<unsigned>(a.B) * ((a.Lq + kRows - 1) / kRows), a.H), kRows, 0, st>>>(a);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  attn_simt_dkv_kernel<HD><<<dim3(static_cast<unsigned>(a.B) * ((a.Lk + kRows - 1) / kRows), a.H), kRows, 0, st>>>(a);
+  constexpr int kpc = kRows / keys_split<HD>();
+  attn_simt_dkv_kernel<HD><<<dim3(static_cast<unsigned>(a.B) * ((a.Lk + kpc - 1) / kpc), a.H), kRows, 0, st>>>(a);
   return cudaGetLastError();
 }
 
 bool args_ok(const AttnSimtArgs& a) {
   return a.qkv != nullptr && a.kstart != nullptr && a.B > 0 && a.H > 0 && a.Lq > 0 && a.Lq <= a.Lk &&
          a.ktail >= 0 && a.ktail <= a.Lq && a.kexcl >= 0 && a.kexcl <= a.ktail && a.H <= 65535 &&
-         static_cast<long long>(a.B) * ((a.Lk + kRows - 1) / kRows) <= 0x7fffffffLL;
+         static_cast<long long>(a.B) * ((a.Lk + kRows / 2 - 1) / (kRows / 2)) <= 0x7fffffffLL;
 }
 
 }  // namespace

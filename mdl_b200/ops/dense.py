@@ -120,7 +120,9 @@ class DenseParams:
         # ms, 2 GPUs 5.08 -> 5.64 ms), so it is opt-in (MDL_B200_DENSE_OVERLAP=1 or overlap=True).
         env = os.environ.get("MDL_B200_DENSE_OVERLAP")
         on = overlap if env is None else env != "0"
-        self.overlap = on and self.device.type == "cuda"
+        # per-bucket updates average gradients only through the peer buffers; the NCCL path
+        # reduces the whole gradient once, in ``step``
+        self.overlap = on and self.device.type == "cuda" and (self.world == 1 or self._symm is not None)
         self._active = False
         self._launched: list[bool] = [False] * len(self.buckets)
         self._side = torch.cuda.Stream(device=self.device) if self.device.type == "cuda" else None
