@@ -173,6 +173,54 @@ class CategoricalEncoder:
         out[nulls] = 0
         return out
 
+    def encode_arrow(self, values) -> np.ndarray:
+        """``values``: a flat Arrow array (nulls allowed). Numeric encodings convert the
+        buffer at once; ``hash`` / ``vocab`` encode each distinct value once (Arrow
+        ``dictionary_encode``), so the Python work is per distinct value, not per row."""
+
+        import pyarrow as pa
+        import pyarrow.compute as pc
+
+        n = len(values)
+        if n == 0:
+            return np.zeros(0, dtype=np.int64)
+        nulls = values.is_null().to_numpy(zero_copy_only=False) if values.null_count else None
+        if self.type in ("identity", "pre_hashed") and not (pa.types.is_integer(values.type)
+                                                            or pa.types.is_floating(values.type)
+                                                            or pa.types.is_boolean(values.type)):
+            values = pc.cast(values, pa.int64())
+        if self.type in ("identity", "pre_hashed"):
+            raw = np.asarray(values.fill_null(0).to_numpy(zero_copy_only=False)).astype(np.int64, copy=False)
+            enc = self.enc
+            if self.type == "pre_hashed":
+                nb = np.uint64(int(enc.num_buckets))
+                out = (raw.view(np.uint64) & (nb - np.uint64(1))).astype(np.int64) + 1
+            else:
+                out = raw.copy()
+                max_id = int(enc.max_id) if enc is not None and enc.max_id else None
+                if max_id is not None:
+                    bad = out > max_id
+                    if bad.any():
+                        if enc.out_of_range == "error":
+                            raise ValueError(f"feature {self.name!r}: ids above max_id {max_id}")
+                        out[bad] = max_id if enc.out_of_range == "clip" else 0
+                out[out < 0] = 0
+            if nulls is not None:
+                out[nulls] = 0
+            return out
+        d = pc.dictionary_encode(values)
+        uniq = d.dictionary.to_pylist()
+        if self.type == "hash":
+            nbk, salt = int(self.enc.num_buckets), self.enc.salt
+            mapped = np.array([stable_hash_bucket(u, nbk, salt) for u in uniq], dtype=np.int64)
+        else:
+            mapped = np.array([self.vocab.get(str(u), 0) for u in uniq], dtype=np.int64)
+        idx = np.asarray(d.indices.fill_null(0).to_numpy(zero_copy_only=False), dtype=np.int64)
+        out = mapped[idx] if len(mapped) else np.zeros(n, dtype=np.int64)
+        if nulls is not None:
+            out[nulls] = 0
+        return out
+
 
 def fit_vocabs(config, paths: Sequence[str], out_dir: str) -> dict[str, str]:
     """Count values of every ``vocab``-encoded feature and write ``value, id, count`` Parquet
@@ -235,8 +283,62 @@ def group_keys(column) -> np.ndarray:
     return keys
 
 
+def _combined(col):
+    """One contiguous Arrow array for a (chunked) column."""
+
+    import pyarrow as pa
+
+    return col.combine_chunks() if isinstance(col, pa.ChunkedArray) else col
+
+
+def _is_list(t) -> bool:
+    import pyarrow as pa
+
+    return pa.types.is_list(t) or pa.types.is_large_list(t) or pa.types.is_fixed_size_list(t)
+
+
+def _list_layout(arr) -> tuple[np.ndarray, np.ndarray | None]:
+    """``(offsets [n+1] into arr.values, null rows or None)`` of a list array; offsets
+    honour a sliced array (they index the unsliced child ``arr.values``)."""
+
+    import pyarrow as pa
+
+    if pa.types.is_fixed_size_list(arr.type):
+        size = arr.type.list_size
+        offs = (arr.offset + np.arange(len(arr) + 1, dtype=np.int64)) * size
+    else:
+        offs = np.asarray(arr.offsets.to_numpy(), dtype=np.int64)
+    nulls = arr.is_null().to_numpy(zero_copy_only=False) if arr.null_count else None
+    return offs, nulls
+
+
+def _ragged(starts: np.ndarray, counts: np.ndarray) -> np.ndarray:
+    """Concatenation of ``arange(starts[i], starts[i] + counts[i])`` over i."""
+
+    total = int(counts.sum())
+    if total == 0:
+        return np.zeros(0, dtype=np.int64)
+    first = np.cumsum(counts) - counts
+    return np.repeat(starts.astype(np.int64) - first, counts) + np.arange(total, dtype=np.int64)
+
+
+def _float_values(arr) -> np.ndarray:
+    """float32 numpy copy of a flat Arrow array, nulls as 0."""
+
+    import pyarrow as pa
+    import pyarrow.compute as pc
+
+    if not pa.types.is_floating(arr.type):
+        arr = pc.cast(arr, pa.float64())
+    return np.asarray(arr.fill_null(0.0).to_numpy(zero_copy_only=False), dtype=np.float32)
+
+
 class Tensorizer:
-    """Arrow table (one sample per row) -> ``PackedBatch`` for a batch layout."""
+    """Arrow table (one sample per row) -> ``PackedBatch`` for a batch layout.
+
+    Every column is converted with whole-array Arrow / NumPy operations (list offsets,
+    ragged gathers, ``dictionary_encode`` for hashed and vocabulary features); Python
+    runs per feature and per distinct hashed value, not per row."""
 
     def __init__(self, config, batch_plan, *, split: str = "train", vocab_maps: dict[str, dict] | None = None,
                  seq_names=None):
@@ -269,6 +371,10 @@ class Tensorizer:
             for fl in q.fields:
                 if fl.kind == "categorical":
                     self.seq_encoders[(q.name, fl.name)] = CategoricalEncoder(fl, vocab_maps.get(f"{q.name}.{fl.name}"))
+        for q in self.sequences:
+            if q.null_anchor_field is not None and q.null_anchor_field not in {fl.name for fl in q.fields}:
+                raise ValueError(f"sequence {q.name!r} null_anchor_field {q.null_anchor_field!r} is not one of "
+                                 "its fields")
         self.request_id = sp.request_id if sp.reader.deduplicate_request_features else None
         self.group_id = sp.group_id
         if sp.reader.deduplicate_request_features and not sp.request_id:
@@ -288,22 +394,38 @@ class Tensorizer:
             cols.append(self.request_id)
         return list(dict.fromkeys(cols))
 
-    def _event_matrix(self, q, col, rows: int) -> tuple[np.ndarray, np.ndarray]:
+    def _event_matrix(self, q, col, rows: int, anchor=None) -> tuple[np.ndarray, np.ndarray]:
         """``[rows, L]`` positions into the column's flat values (-1 = padding) and lengths.
 
-        Truncation keeps the first (``head``) or last (``tail``) ``max_length`` events of
-        the stored order; the kept events are laid out oldest to newest and left-padded,
-        the layout the sequence models read (valid events at the end)."""
-
-        import pyarrow as pa
+        With ``anchor`` (the ``null_anchor_field`` column, aligned with ``col``) the events
+        whose anchor value is null are dropped from every field first (reference
+        ``_compact_direct_sequence_by_anchor``, ``src/dataloader.py:9312``); other nulls stay
+        as padding values. Truncation then keeps the first (``head``) or last (``tail``)
+        ``max_length`` events of the stored order; the kept events are laid out oldest to
+        newest and left-padded, the layout the sequence models read (valid events at the end)."""
 
         L = int(q.max_length)
-        col = col.combine_chunks() if isinstance(col, pa.ChunkedArray) else col
+        col = _combined(col)
         offs = col.offsets.to_numpy().astype(np.int64)
         starts, ends = offs[:-1], offs[1:]
         if col.null_count:
             nul = col.is_null().to_numpy(zero_copy_only=False)
             ends = np.where(nul, starts, ends)
+        kept = None
+        if anchor is not None:
+            anchor = _combined(anchor)
+            aoffs = anchor.offsets.to_numpy().astype(np.int64)
+            if not np.array_equal(np.diff(aoffs), np.diff(offs)):
+                raise ValueError(f"sequence {q.name!r}: null_anchor_field lists differ in length from the "
+                                 "other fields")
+            ok = np.ones(len(col.values), dtype=bool)
+            if anchor.values.null_count:      # anchor validity moved to this column's flat positions
+                aok = ~anchor.values.is_null().to_numpy(zero_copy_only=False)
+                n_all = offs[1:] - offs[:-1]
+                ok[_ragged(offs[:-1], n_all)] = aok[_ragged(aoffs[:-1], n_all)]
+            kept = np.nonzero(ok)[0]
+            before = np.concatenate([[0], np.cumsum(ok)])      # kept events before each flat position
+            starts, ends = before[starts], before[ends]
         n = ends - starts
         keep = np.minimum(n, L)
         src0 = starts if q.truncation == "head" else ends - keep
@@ -313,6 +435,8 @@ class Tensorizer:
             pos = src0[:, None] + (keep[:, None] - 1 - j)
         else:
             pos = src0[:, None] + j
+        if kept is not None:
+            pos = kept[np.where(valid, pos, 0)] if len(kept) else np.zeros_like(pos)
         return np.where(valid, pos, -1), keep
 
     def _sequence(self, q, table, rows: int) -> dict:
@@ -322,12 +446,16 @@ class Tensorizer:
         cats = [fl for fl in q.fields if fl.kind == "categorical"]
         dens = [fl for fl in q.fields if fl.kind == "dense"]
         first = table.column((cats or dens)[0].source or (cats or dens)[0].name)
-        pos, lengths = self._event_matrix(q, first, rows)
+        anchor = None
+        if q.null_anchor_field is not None:
+            fa = next(fl for fl in q.fields if fl.name == q.null_anchor_field)
+            anchor = table.column(fa.source or fa.name)
+        pos, lengths = self._event_matrix(q, first, rows, anchor)
         ids = np.zeros((len(cats), rows, L), dtype=np.int64)
         for k, fl in enumerate(cats):
             col = table.column(fl.source or fl.name)
             col = col.combine_chunks() if isinstance(col, pa.ChunkedArray) else col
-            flat = self.seq_encoders[(q.name, fl.name)].encode(col.values.to_numpy(zero_copy_only=False))
+            flat = self.seq_encoders[(q.name, fl.name)].encode_arrow(col.values)
             safe = np.clip(pos, 0, max(0, len(flat) - 1))
             ids[k] = np.where(pos >= 0, flat[safe] if len(flat) else 0, 0)
         out = {"ids": torch.from_numpy(ids.reshape(len(cats), rows * L)), "lengths": torch.from_numpy(lengths)}
@@ -339,7 +467,7 @@ class Tensorizer:
                 col = table.column(fl.source or fl.name)
                 col = col.combine_chunks() if isinstance(col, pa.ChunkedArray) else col
                 d = int(fl.dimension)
-                flat = np.asarray(col.values.to_numpy(zero_copy_only=False), dtype=np.float32).reshape(-1, d)
+                flat = _float_values(col.values).reshape(-1, d)
                 safe = np.clip(pos, 0, max(0, len(flat) - 1))
                 dense[:, :, c:c + d] = np.where((pos >= 0)[..., None], flat[safe] if len(flat) else 0.0, 0.0)
                 c += d
@@ -378,13 +506,14 @@ class Tensorizer:
         ri = None
         src = table
         if self.request_id:
-            keys = np.asarray(table.column(self.request_id).to_pylist(), dtype=object)
-            _, first, inv = np.unique(keys.astype(str), return_index=True, return_inverse=True)
-            order = np.argsort(first, kind="stable")          # requests in order of first appearance
-            rank_of = np.empty_like(order)
-            rank_of[order] = np.arange(len(order))
-            ri = torch.from_numpy(rank_of[inv].astype(np.int64))
-            src = table.take(first[order])
+            import pyarrow.compute as pc
+
+            # dictionary indices number the requests in order of first appearance (nulls: one request)
+            d = pc.dictionary_encode(_combined(table.column(self.request_id)), null_encoding="encode")
+            inv = np.asarray(d.indices.to_numpy(zero_copy_only=False), dtype=np.int64)
+            _, first = np.unique(inv, return_index=True)
+            ri = torch.from_numpy(inv)
+            src = table.take(first)
         out = {}
         for q in self.sequences:
             seq = self._sequence(q, src, src.num_rows)
@@ -394,36 +523,55 @@ class Tensorizer:
         return out
 
     def _bag(self, f, col) -> tuple[np.ndarray, np.ndarray]:
-        """(flat raw values, lengths) of one categorical column; scalars are bags of one."""
+        """(encoded ids, lengths) of one categorical column; scalars are bags of one, a
+        null (scalar or list) is one padding id, lists keep the first (``head``) or last
+        (``tail``) ``max_length`` values."""
 
-        py = col.to_pylist()
-        rows = len(py)
-        lengths = np.zeros(rows, dtype=np.int64)
-        flat: list = []
+        arr = _combined(col)
+        rows = len(arr)
+        enc = self.encoders[f.name]
+        if not _is_list(arr.type):
+            return enc.encode_arrow(arr), np.ones(rows, dtype=np.int64)
+        offs, nulls = _list_layout(arr)
+        starts, n = offs[:-1], offs[1:] - offs[:-1]
+        if nulls is not None:
+            n = np.where(nulls, 0, n)
         cap = f.max_length
-        for i, v in enumerate(py):
-            if isinstance(v, list):
-                if cap is not None and len(v) > cap:
-                    v = v[-cap:] if f.truncation == "tail" else v[:cap]
-                flat.extend(v)
-                lengths[i] = len(v)
-            else:
-                flat.append(v)
-                lengths[i] = 1
-        return np.array(flat, dtype=object), lengths
+        if cap is not None:
+            keep = np.minimum(n, int(cap))
+            if f.truncation == "tail":
+                starts = starts + n - keep
+            n = keep
+        vals = enc.encode_arrow(arr.values.take(_ragged(starts, n)))
+        if nulls is None:
+            return vals, n
+        lengths = np.where(nulls, 1, n)
+        out = np.zeros(int(lengths.sum()), dtype=np.int64)
+        out[_ragged(np.cumsum(lengths) - lengths, n)] = vals
+        return out, lengths
 
     def _dense(self, f, col) -> np.ndarray:
-        py = col.to_pylist()
+        """``[rows, dimension (+1 presence)]``: a scalar fills the first column, a list its
+        first ``dimension`` values; null values are 0, a null row has presence 0."""
+
+        arr = _combined(col)
+        rows = len(arr)
         dim = int(f.dimension)
-        out = np.zeros((len(py), dim + (1 if f.presence else 0)), dtype=np.float32)
-        for i, v in enumerate(py):
-            if v is None:
-                continue
-            vals = v if isinstance(v, list) else [v]
-            vals = [0.0 if x is None else float(x) for x in vals[:dim]]
-            out[i, :len(vals)] = vals
-            if f.presence:
-                out[i, dim] = 1.0
+        out = np.zeros((rows, dim + (1 if f.presence else 0)), dtype=np.float32)
+        if _is_list(arr.type):
+            offs, nulls = _list_layout(arr)
+            n = offs[1:] - offs[:-1]
+            if nulls is not None:
+                n = np.where(nulls, 0, n)
+            k = np.minimum(n, dim)
+            vals = _float_values(arr.values.take(_ragged(offs[:-1], k)))
+            row = np.repeat(np.arange(rows), k)
+            out[row, _ragged(np.zeros(rows, dtype=np.int64), k)] = vals
+        else:
+            nulls = arr.is_null().to_numpy(zero_copy_only=False) if arr.null_count else None
+            out[:, 0] = _float_values(arr)
+        if f.presence:
+            out[:, dim] = 1.0 if nulls is None else (~nulls).astype(np.float32)
         return out
 
     def __call__(self, table, pin: bool = False) -> PackedBatch:
@@ -437,8 +585,8 @@ class Tensorizer:
                 dense[:, lf.dense_col:lf.dense_col + d.shape[1]] = d
                 len_parts.append(np.zeros(rows, dtype=np.int64))
                 continue
-            flat, lengths = self._bag(f, col)
-            ids_parts.append(self.encoders[f.name].encode(flat))
+            ids, lengths = self._bag(f, col)
+            ids_parts.append(ids)
             len_parts.append(lengths)
         offsets = np.zeros(len(self.plan.features) * rows + 1, dtype=np.int64)
         np.cumsum(np.concatenate(len_parts) if len_parts else np.zeros(0, np.int64), out=offsets[1:])
@@ -452,25 +600,26 @@ class Tensorizer:
                 mask[:, t] = 0.0
                 any_mask = True
                 continue
-            vals = table.column(name).to_pylist()
-            for i, v in enumerate(vals):
-                if v is None:
-                    mask[i, t] = 0.0
-                    any_mask = True
-                else:
-                    labels[i, t] = float(v)
+            arr = _combined(table.column(name))
+            labels[:, t] = _float_values(arr)
+            if arr.null_count:
+                mask[:, t] = (~arr.is_null().to_numpy(zero_copy_only=False)).astype(np.float32)
+                any_mask = True
             mname = self.label_masks.get(task)
             if mname and mname in table.column_names:
-                mv = np.array([0.0 if v is None else float(v) for v in table.column(mname).to_pylist()], np.float32)
-                mask[:, t] *= mv
+                mask[:, t] *= _float_values(_combined(table.column(mname)))
                 any_mask = True
         scen = np.zeros(rows, dtype=np.int64)
         if self.scene_source and self.scene_source in table.column_names:
-            vals = table.column(self.scene_source).to_pylist()
+            arr = _combined(table.column(self.scene_source))
             if self.scene_encoding == "index":
-                scen = np.array([0 if v is None else int(v) for v in vals], dtype=np.int64)
+                scen = np.asarray(arr.fill_null(0).to_numpy(zero_copy_only=False)).astype(np.int64)
             else:
-                scen = np.array([self.scene_index.get(str(v), 0) for v in vals], dtype=np.int64)
+                import pyarrow.compute as pc
+
+                d = pc.dictionary_encode(arr, null_encoding="encode")
+                names = np.array([self.scene_index.get(str(v), 0) for v in d.dictionary.to_pylist()], np.int64)
+                scen = names[np.asarray(d.indices.to_numpy(zero_copy_only=False), dtype=np.int64)]
         group = None
         if self.group_id and self.group_id in table.column_names:
             group = torch.from_numpy(group_keys(table.column(self.group_id)))
