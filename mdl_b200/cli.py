@@ -163,7 +163,8 @@ def _batches(config, model, rank, world, *, split="train", synthetic=False, batc
                                     seed=r.shuffle_seed, prefetch=r.prefetch_batches, loop=loop and split == "train",
                                     pin=r.pin_memory, io_policy=RemoteIoPolicy.from_reader(r),
                                     length_buckets=[(b.max_length, b.batch_size) for b in r.length_buckets],
-                                    length_bucket_metric=r.length_bucket_metric, overlap=r.overlap_host_prepare)
+                                    length_bucket_metric=r.length_bucket_metric, overlap=r.overlap_host_prepare,
+                                    agg_direct_mode=r.agg_direct_mode)
     seqs = [s for s in config.sequences if s.name in getattr(model.encoder, "seq_plans", {})]
     gen = SyntheticGenerator(model.encoder.batch_plan,
                              synthetic_spec_from_config(config, model.encoder.batch_plan, sequences=seqs), rank=rank)

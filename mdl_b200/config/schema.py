@@ -199,7 +199,7 @@ class ReaderConfig:
     schema_validation_samples: int = 64
     length_buckets: tuple[LengthBucketConfig, ...] = ()
     length_bucket_metric: Literal["max", "sum"] = "max"
-    agg_direct_mode: str = "direct"
+    agg_direct_mode: Literal["legacy", "direct", "direct_arrow", "compare"] = "legacy"
     from_hdfs: bool = False
     hdfs_close_timeout: float | None = None
     hdfs_file_lock: bool = False

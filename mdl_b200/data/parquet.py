@@ -497,15 +497,29 @@ class Tensorizer:
             out = out + n if metric == "sum" else np.maximum(out, n)
         return out
 
-    def _sequences(self, table) -> dict:
+    def _sequences(self, table, requests=None) -> dict:
         """Sequence payloads; with request deduplication one row per distinct ``request_id``
-        (in order of first appearance) plus ``row_indices`` (candidate -> request row)."""
+        (in order of first appearance) plus ``row_indices`` (candidate -> request row).
+
+        ``requests``: ``(request table, candidate -> request row)`` built by the caller (the
+        direct agg path); its rows are used as they are with deduplication, repeated per
+        candidate without it."""
 
         if not self.sequences:
             return {}
         ri = None
         src = table
-        if self.request_id:
+        if requests is not None:
+            req, rows = requests
+            rows = np.asarray(rows, dtype=np.int64)
+            if self.request_id:
+                ri = torch.from_numpy(rows)
+                src = req
+            else:
+                import pyarrow as pa
+
+                src = req.take(pa.array(rows))
+        elif self.request_id:
             import pyarrow.compute as pc
 
             # dictionary indices number the requests in order of first appearance (nulls: one request)
@@ -574,7 +588,7 @@ class Tensorizer:
             out[:, dim] = 1.0 if nulls is None else (~nulls).astype(np.float32)
         return out
 
-    def __call__(self, table, pin: bool = False) -> PackedBatch:
+    def __call__(self, table, pin: bool = False, requests=None) -> PackedBatch:
         rows = table.num_rows
         ids_parts, len_parts = [], []
         dense = np.zeros((rows, self.dense_width), dtype=np.float32)
@@ -626,7 +640,7 @@ class Tensorizer:
         return PackedBatch.pack(torch.from_numpy(ids), torch.from_numpy(offsets),
                                 torch.from_numpy(dense) if self.dense_width else None, torch.from_numpy(labels),
                                 torch.from_numpy(mask) if any_mask else None, torch.from_numpy(scen), rows,
-                                sequences=self._sequences(table), pin=pin, group_key=group)
+                                sequences=self._sequences(table, requests), pin=pin, group_key=group)
 
 
 # ------------------------------------------------------------------ iteration
@@ -640,17 +654,28 @@ class ParquetBatchIterator:
                  world: int = 1, shard_unit: str = "row_group", shuffle_rows: int = 0, seed: int = 0,
                  drop_last: bool = True, prefetch: int = 2, pin: bool = False, start_position: int = 0,
                  loop: bool = False, io_policy=None, length_buckets: Sequence = (),
-                 length_bucket_metric: str = "max", adapter=None, overlap: bool = True) -> None:
+                 length_bucket_metric: str = "max", adapter=None, overlap: bool = True,
+                 agg_direct_mode: str = "legacy") -> None:
         """``length_buckets``: ``(max_length or None, batch_size)`` pairs in increasing
         length order (the last may be the catch-all ``None``): rows are grouped by their
         sequence work (``Tensorizer.sequence_lengths``) and each bucket yields batches of
         its own size, so short-history rows are not padded to the longest history
-        (reference ``_iter_length_bucketed_tables`` ``src/train.py:1955-2077``)."""
+        (reference ``_iter_length_bucketed_tables`` ``src/train.py:1955-2077``).
+
+        ``agg_direct_mode`` (with an agg ``adapter``): ``legacy`` expands every raw table into
+        candidate rows first; ``direct`` / ``direct_arrow`` build batches from request groups
+        of the raw tables (``data/agg_direct.py``: groups stay whole, each request's events
+        are gathered once); ``compare`` trains on ``legacy`` and checks every raw table
+        against ``direct``."""
 
         self.refs = plan_row_groups(paths, rank, world, shard_unit)
         # adapter: raw Arrow table -> flat rows (e.g. the agg layout, ``data/agg.py``);
         # the files are then read with the adapter's raw columns
         self.adapter = adapter
+        if agg_direct_mode not in ("legacy", "direct", "direct_arrow", "compare"):
+            raise ValueError("reader.agg_direct_mode must be legacy, direct, direct_arrow or compare")
+        self.agg_mode = agg_direct_mode if adapter is not None else "legacy"
+        self.seed = seed
         self.buckets = [(None if m is None else int(m), int(b)) for m, b in length_buckets]
         self.bucket_metric = length_bucket_metric
         self.io = io_policy  # RemoteIoPolicy: timeouts, retries and skips of remote reads
@@ -672,7 +697,7 @@ class ParquetBatchIterator:
         self._thread: threading.Thread | None = None
         self._stop = threading.Event()
 
-    def _tables(self):
+    def _tables(self, raw: bool = False):
         pa, pq = _pa()
         cols = self.adapter.plan.raw_columns() if self.adapter is not None else self.tz.columns()
         while not self._stop.is_set():
@@ -689,8 +714,16 @@ class ParquetBatchIterator:
                 t = read() if self.io is None else self.io.run(read, f"read {ref.path}#{ref.index}", opening=True,
                                                                  path=ref.path)
                 self.position += 1
-                if t is not None:
-                    yield self.adapter(t) if self.adapter is not None else t
+                if t is None:
+                    continue
+                if raw or self.adapter is None:
+                    yield t
+                    continue
+                if self.agg_mode == "compare":
+                    from .agg_direct import compare_direct_to_legacy
+
+                    compare_direct_to_legacy(t, self.adapter.plan, self.tz)
+                yield self.adapter(t)
             if not self.loop or not self.refs:
                 return
             self.position = 0
@@ -722,6 +755,15 @@ class ParquetBatchIterator:
                 yield self.tz(buf, pin=self.pin)
 
     def _batches(self):
+        if self.agg_mode in ("direct", "direct_arrow"):
+            from .agg_direct import AggDirectBatches
+
+            yield from AggDirectBatches(self._tables(raw=True), self.adapter.plan, self.tz, self.batch_size,
+                                        shuffle_rows=self.shuffle_rows, seed=self.seed, rank=self.rank,
+                                        length_buckets=self.buckets if self.tz.sequences else (),
+                                        length_bucket_metric=self.bucket_metric, drop_last=self.drop_last,
+                                        pin=self.pin)
+            return
         if self.buckets and self.tz.sequences:
             yield from self._bucketed()
             return

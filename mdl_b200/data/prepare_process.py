@@ -49,7 +49,7 @@ def parquet_batches(config_mapping: dict, batch_plan, paths: list[str], batch_si
     it = ParquetBatchIterator(paths, tz, batch_size, rank=rank, world=world, shuffle_rows=shuffle_rows, seed=seed,
                               loop=loop, prefetch=2, pin=False, adapter=adapter,
                               length_buckets=[(b.max_length, b.batch_size) for b in r.length_buckets],
-                              length_bucket_metric=r.length_bucket_metric)
+                              length_bucket_metric=r.length_bucket_metric, agg_direct_mode=r.agg_direct_mode)
     return iter(it)
 
 
