@@ -605,6 +605,58 @@ def cmd_make_synthetic(args) -> int:
     return 0
 
 
+def cmd_build_config(args) -> int:
+    """Config YAMLs of the model families from a field contract (``data/config_builder.py``)."""
+
+    import yaml
+
+    from .config.loader import app_config_from_mapping
+    from .config.validate import validate_app_config
+    from .data.config_builder import FAMILIES, FieldContract, build_config, memory_summary, render, size_features
+    from .data.profile import profile_columns
+
+    with open(args.contract, encoding="utf-8") as fh:
+        contract = FieldContract.from_mapping(yaml.safe_load(fh) or {})
+
+    def load(path):
+        if not path:
+            return None
+        with open(path, encoding="utf-8") as fh:
+            return json.load(fh)
+
+    profile, shapes = load(args.profile), load(args.shapes)
+    if args.profile_inputs:
+        from .data.parquet import discover_parquet_inputs
+
+        cols = list(dict.fromkeys([*contract.context_features, *contract.item_features,
+                                   *(c for u in contract.ups.values() for c in u["fields"])]))
+        cols = [c for c in cols if c not in contract.dense_features]
+        profile = profile_columns(discover_parquet_inputs(args.profile_inputs), {c: c for c in cols},
+                                  max_rows=args.max_rows)
+    if profile is None and shapes is None and not args.estimate_from_names:
+        print(json.dumps({"error": "no sizing source: give --profile, --shapes or --profile-inputs, or "
+                                   "--estimate-from-names"}), file=sys.stderr)
+        return 2
+    sizes = size_features(contract, profile=profile, shapes=shapes, load=args.load, growth=args.growth,
+                          max_dim=args.max_dim)
+    families = list(FAMILIES) if args.family == "all" else [args.family]
+    os.makedirs(args.out_dir, exist_ok=True)
+    written = []
+    for fam in families:
+        variants = [False] + ([True] if args.fine and fam.startswith("mdl_") else [])
+        for fine in variants:
+            m = build_config(contract, fam, sizes=sizes, fine=fine, batch_size=args.batch_size,
+                             token_dim=args.token_dim, layers=args.layers, inputs=args.inputs)
+            validate_app_config(app_config_from_mapping(m))
+            summary = memory_summary(m, world_size=args.world_size, budget_gb=args.budget_gb)
+            path = os.path.join(args.out_dir, f"{fam}{'_fine' if fine else ''}.yaml")
+            with open(path, "w", encoding="utf-8") as fh:
+                fh.write(render(m, summary, sizes))
+            written.append({"path": path, **summary})
+    print(json.dumps({"configs": written}))
+    return 0
+
+
 def build_parser() -> argparse.ArgumentParser:
     ap = argparse.ArgumentParser(prog="python -m mdl_b200", description=__doc__,
                                  formatter_class=argparse.RawDescriptionHelpFormatter)
@@ -648,6 +700,27 @@ def build_parser() -> argparse.ArgumentParser:
     p = sub.add_parser("recommend-encodings", help="per-feature categorical encoding from a profile")
     p.add_argument("--profile", required=True)
     p.add_argument("--bits", type=int, default=20)
+    p = sub.add_parser("build-config", help="model config YAMLs from a field contract and a data profile")
+    p.add_argument("--contract", required=True, help="field contract YAML (see mdl_b200/data/config_builder.py)")
+    p.add_argument("--family", choices=["rankmixer", "mdl_rankmixer", "onetrans", "mdl_onetrans", "all"],
+                   default="all")
+    p.add_argument("--fine", action="store_true", help="also write the fine-scene siblings of the MDL families")
+    p.add_argument("--profile", help="profile-data style JSON report of the raw files")
+    p.add_argument("--shapes", help="recommend-shapes JSON")
+    p.add_argument("--profile-inputs", nargs="*", help="profile the contract's columns in these Parquet files")
+    p.add_argument("--max-rows", type=int, default=1_000_000)
+    p.add_argument("--estimate-from-names", action="store_true",
+                   help="size tables from column names where no profile covers them (marked in the output)")
+    p.add_argument("--load", type=float, default=0.5)
+    p.add_argument("--growth", type=float, default=4.0, help="distinct-value growth assumed beyond the profile")
+    p.add_argument("--max-dim", type=int, default=64)
+    p.add_argument("--batch-size", type=int, default=2048)
+    p.add_argument("--token-dim", type=int, default=None)
+    p.add_argument("--layers", type=int, default=None)
+    p.add_argument("--inputs", nargs="*", help="data.train.inputs of the written configs")
+    p.add_argument("--world-size", type=int, default=8)
+    p.add_argument("--budget-gb", type=float, default=None, help="per-GPU embedding memory budget (GiB)")
+    p.add_argument("--out-dir", required=True)
     p = sub.add_parser("tune-batch-size", help="compute-mode throughput and peak memory per batch size")
     _add_config(p)
     p.add_argument("--batch-sizes", type=int, nargs="+", required=True)
@@ -734,6 +807,8 @@ def _dispatch(argv=None) -> int:
         return cmd_profile_data(args)
     if cmd in ("recommend-shapes", "recommend-encodings"):
         return cmd_recommend(args)
+    if cmd == "build-config":
+        return cmd_build_config(args)
     if cmd == "tune-batch-size":
         return cmd_tune_batch_size(args)
     if cmd == "summarize-benchmarks":

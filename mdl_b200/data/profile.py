@@ -50,12 +50,19 @@ def collision_fraction(values: np.ndarray, bits: int) -> float:
     return float(counts[counts > 1].sum()) / float(values.size)
 
 
-def _flat_values(col) -> tuple[np.ndarray, int]:
+def _flat_values(col) -> tuple[np.ndarray, int, int, float]:
+    """(distinct-able uint64 values, null rows, list depth, mean length of the innermost lists)."""
+
     import pyarrow as pa
+    import pyarrow.compute as pc
 
     col = col.combine_chunks() if isinstance(col, pa.ChunkedArray) else col
     nulls = int(col.null_count)
+    depth, inner = 0, 0.0
     while pa.types.is_list(col.type) or pa.types.is_large_list(col.type):
+        depth += 1
+        ln = pc.list_value_length(col).drop_null()
+        inner = float(pc.mean(ln).as_py() or 0.0) if len(ln) else 0.0
         col = col.flatten()
     if pa.types.is_integer(col.type):
         vals = np.asarray(col.drop_null().to_numpy(zero_copy_only=False)).astype(np.int64).view(np.uint64)
@@ -64,13 +71,11 @@ def _flat_values(col) -> tuple[np.ndarray, int]:
 
         vals = hash_array(np.asarray(col.drop_null().cast(pa.string()).to_numpy(zero_copy_only=False),
                                      dtype=object), categorize=False)
-    return vals.astype(np.uint64), nulls
+    return vals.astype(np.uint64), nulls, depth, inner
 
 
 def profile_parquet(config, paths, *, max_rows: int = 1_000_000, bucket_bits=(16, 18, 20, 22, 24)) -> dict:
     """Categorical profile of the first ``max_rows`` rows of ``paths`` (see module doc)."""
-
-    import pyarrow.parquet as pq
 
     columns: dict[str, str] = {}
     for f in config.features:
@@ -80,8 +85,21 @@ def profile_parquet(config, paths, *, max_rows: int = 1_000_000, bucket_bits=(16
         for fl in q.fields:
             if fl.kind == "categorical":
                 columns[fl.source or fl.name] = f"{q.name}.{fl.name}"
+    return profile_columns(paths, columns, max_rows=max_rows, bucket_bits=bucket_bits)
+
+
+def profile_columns(paths, columns: dict[str, str], *, max_rows: int = 1_000_000,
+                    bucket_bits=(16, 18, 20, 22, 24)) -> dict:
+    """The profile of named columns (``{column: report name}``); besides the counts, each
+    entry has the column's list ``depth`` and the mean length of its innermost lists
+    (``inner_mean_length``: bag length in a flat file, values per request / candidate /
+    event position in an agg file)."""
+
+    import pyarrow.parquet as pq
+
     seen: dict[str, list[np.ndarray]] = {c: [] for c in columns}
     nulls = {c: 0 for c in columns}
+    shape = {c: [0, 0.0, 0] for c in columns}          # depth, sum of inner means, row groups
     rows = 0
     for path in paths:
         pf = pq.ParquetFile(path)
@@ -94,9 +112,12 @@ def profile_parquet(config, paths, *, max_rows: int = 1_000_000, bucket_bits=(16
             t = t.slice(0, take)
             rows += take
             for c in present:
-                v, n = _flat_values(t.column(c))
+                v, n, depth, inner = _flat_values(t.column(c))
                 seen[c].append(v)
                 nulls[c] += n
+                shape[c][0] = max(shape[c][0], depth)
+                shape[c][1] += inner
+                shape[c][2] += 1
         if rows >= max_rows:
             break
     report = {"rows": rows, "features": {}}
@@ -109,6 +130,7 @@ def profile_parquet(config, paths, *, max_rows: int = 1_000_000, bucket_bits=(16
             "column": c, "values": int(vals.size), "distinct": int(distinct.size), "null_rows": nulls[c],
             "max_id": int(distinct.view(np.int64).max()) if distinct.size else 0,
             "min_id": int(distinct.view(np.int64).min()) if distinct.size else 0,
+            "depth": shape[c][0], "inner_mean_length": round(shape[c][1] / max(1, shape[c][2]), 4),
             "collisions_raw": raw, "collisions_remixed": mixed,
         }
     return report
