@@ -657,6 +657,26 @@ def cmd_build_config(args) -> int:
     return 0
 
 
+def cmd_data_stages(args) -> int:
+    """Host-side stage costs of the input pipeline (``benchmark/data_stages.py``)."""
+
+    import torch
+
+    from .benchmark.data_stages import stage_costs
+    from .data.parquet import discover_parquet_inputs
+
+    cfg = load_cli_config(args)
+    device = torch.device("cuda", 0) if torch.cuda.is_available() else torch.device("cpu")
+    model, _trainer = _build(cfg, 0, 1, torch.device("cpu"))
+    sp = getattr(cfg.data, args.split) or cfg.data.train
+    paths = discover_parquet_inputs(args.inputs or sp.inputs)
+    res = stage_costs(cfg, paths, model.encoder.batch_plan, list(getattr(model.encoder, "seq_plans", {})),
+                      max_tables=args.max_tables, warmup=args.warmup, batch_size=args.batch_size, device=device,
+                      split=args.split)
+    print(json.dumps(res), flush=True)
+    return 0
+
+
 def build_parser() -> argparse.ArgumentParser:
     ap = argparse.ArgumentParser(prog="python -m mdl_b200", description=__doc__,
                                  formatter_class=argparse.RawDescriptionHelpFormatter)
@@ -721,6 +741,13 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--world-size", type=int, default=8)
     p.add_argument("--budget-gb", type=float, default=None, help="per-GPU embedding memory budget (GiB)")
     p.add_argument("--out-dir", required=True)
+    p = sub.add_parser("data-stages", help="input pipeline stage costs: read, expand, tensorize, pin, H2D")
+    _add_config(p)
+    p.add_argument("--split", choices=["train", "test"], default="train")
+    p.add_argument("--inputs", nargs="*")
+    p.add_argument("--max-tables", type=int, default=8)
+    p.add_argument("--warmup", type=int, default=1)
+    p.add_argument("--batch-size", type=int, default=None)
     p = sub.add_parser("tune-batch-size", help="compute-mode throughput and peak memory per batch size")
     _add_config(p)
     p.add_argument("--batch-sizes", type=int, nargs="+", required=True)
@@ -807,6 +834,8 @@ def _dispatch(argv=None) -> int:
         return cmd_profile_data(args)
     if cmd in ("recommend-shapes", "recommend-encodings"):
         return cmd_recommend(args)
+    if cmd == "data-stages":
+        return cmd_data_stages(args)
     if cmd == "build-config":
         return cmd_build_config(args)
     if cmd == "tune-batch-size":

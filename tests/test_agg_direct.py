@@ -278,3 +278,29 @@ def test_cli_trains_with_direct_agg_pipeline(tmp_path):
     done = [l for l in lines if l.get("done")]
     assert done and done[-1]["steps"] == 4, out.stdout[-2000:]
     assert all(math.isfinite(l["loss"]) for l in lines if "loss" in l)
+
+
+@pytest.mark.parametrize("mode", ["legacy", "direct"])
+def test_data_stage_costs(tmp_path, mode):
+    """data-stages: read / expand / tensorize seconds of the agg pipeline, every timed
+    candidate row counted once, the slowest stage named."""
+
+    m = _mapping(str(tmp_path))
+    m["data"]["train"]["reader"]["agg_direct_mode"] = mode
+    cfg = app_config_from_mapping(m)
+    write_mock_agg_parquet(cfg, str(tmp_path / "a.parquet"), rows=60, seed=0, row_group_size=20)
+    from mdl_b200.benchmark.data_stages import stage_costs
+
+    res = stage_costs(cfg, [str(tmp_path / "a.parquet")], _plan(cfg), ["impr"], max_tables=2, warmup=1,
+                      batch_size=16)
+    flat = AggAdapter(AggPlan.from_config(cfg))(pq.ParquetFile(str(tmp_path / "a.parquet")).read_row_group(1))
+    flat2 = AggAdapter(AggPlan.from_config(cfg))(pq.ParquetFile(str(tmp_path / "a.parquet")).read_row_group(2))
+    assert res["mode"] == mode and res["rows"] == flat.num_rows + flat2.num_rows
+    assert set(res["stages"]) >= {"read", "expand", "tensorize"} and res["bottleneck"] in res["stages"]
+    assert abs(sum(s["share"] for s in res["stages"].values()) - 1.0) < 1e-3
+    cfg_path = tmp_path / "agg.yaml"
+    cfg_path.write_text(yaml.safe_dump(m))
+    out = subprocess.run([sys.executable, "-m", "mdl_b200", "data-stages", "--config", str(cfg_path),
+                          "--max-tables", "2"], capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stderr[-2000:]
+    assert json.loads(out.stdout.strip().splitlines()[-1])["rows"] > 0
