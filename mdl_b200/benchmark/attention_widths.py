@@ -2,7 +2,10 @@
 flash attention for head width 32, the CUDA-core kernels for 8, 16 and 64) against its
 PyTorch definition, forward and backward, on LONGER / OneTrans shapes.
 
-    python -m mdl_b200.benchmark.attention_widths [--reps R] [--no-reference]
+    python -m mdl_b200.benchmark.attention_widths [--reps R] [--no-reference] [--shape NAME ...]
+                                                  [--batch B]
+
+``--shape`` keeps the named shapes, ``--batch`` overrides their batch (small profiler cases).
 
 Device time with CUDA events (after two warm-ups); random padding starts in [0, Lk/2).
 """
@@ -51,12 +54,18 @@ def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reps", type=int, default=10)
     ap.add_argument("--no-reference", action="store_true")
+    ap.add_argument("--shape", action="append", choices=sorted(SHAPES), default=None)
+    ap.add_argument("--batch", type=int, default=None)
     args = ap.parse_args(argv)
 
     def ref(qkv, ks, H, Lq, c, kt, ke):
         return suffix_attention_reference(qkv, ks, H, Lq, c, ktail=kt, kexcl=ke)
 
     for name, shape in SHAPES.items():
+        if args.shape and name not in args.shape:
+            continue
+        if args.batch:
+            shape = (args.batch,) + shape[1:]
         nf, nb = _time(suffix_attention, shape, args.reps)
         line = f"{name:26s} {shape}: native fwd {nf:.3f} ms bwd {nb:.3f} ms"
         if not args.no_reference:
