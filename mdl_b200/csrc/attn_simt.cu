@@ -426,6 +426,9 @@ template <int HD>
 __global__ void __launch_bounds__(kRows) attn_simt_dkv_kernel(AttnSimtArgs a) {
   // Wide heads (64) split a key's head dimension over TPK adjacent threads (dot products
   // completed with a shuffle), so each thread's K, V, dK and dV accumulators stay in registers.
+  // The threads of a key take interleaved dimensions (hsel, hsel + TPK, ...): their shared-memory
+  // reads of a staged row then fall in different banks (contiguous halves 32 words apart would
+  // share a bank).
   constexpr int TPK = keys_split<HD>();
   constexpr int HW = HD / TPK;         // dimensions per thread
   constexpr int KPC = kRows / TPK;     // keys per CTA
@@ -438,7 +441,7 @@ __global__ void __launch_bounds__(kRows) attn_simt_dkv_kernel(AttnSimtArgs a) {
   const int blk = static_cast<int>(blockIdx.x - static_cast<unsigned>(b) * nblk);
   const int h = blockIdx.y;
   const int j = blk * KPC + static_cast<int>(threadIdx.x) / TPK;  // key row
-  const int d0 = (static_cast<int>(threadIdx.x) % TPK) * HW;     // this thread's dimensions
+  const int hsel = static_cast<int>(threadIdx.x) % TPK;          // dimensions hsel + TPK * i
   const int D = a.H * HD;
   const long long rs = 3LL * D;
   const __nv_bfloat16* base = a.qkv + static_cast<long long>(b) * a.Lk * rs;
@@ -448,8 +451,9 @@ __global__ void __launch_bounds__(kRows) attn_simt_dkv_kernel(AttnSimtArgs a) {
   float k[HW], v[HW], dk[HW], dv[HW];
 #pragma unroll
   for (int d = 0; d < HW; ++d) {
-    k[d] = kvalid ? __bfloat162float(base[static_cast<long long>(j) * rs + D + h * HD + d0 + d]) : 0.f;
-    v[d] = kvalid ? __bfloat162float(base[static_cast<long long>(j) * rs + 2 * D + h * HD + d0 + d]) : 0.f;
+    k[d] = kvalid ? __bfloat162float(base[static_cast<long long>(j) * rs + D + h * HD + hsel + TPK * d]) : 0.f;
+    v[d] = kvalid ? __bfloat162float(base[static_cast<long long>(j) * rs + 2 * D + h * HD + hsel + TPK * d])
+                  : 0.f;
     dk[d] = 0.f;
     dv[d] = 0.f;
   }
@@ -488,8 +492,8 @@ __global__ void __launch_bounds__(kRows) attn_simt_dkv_kernel(AttnSimtArgs a) {
       float s = 0.f, dp = 0.f;
 #pragma unroll
       for (int d = 0; d < HW; ++d) {
-        s = fmaf(sQ[r][d0 + d], k[d], s);
-        dp = fmaf(sO[r][d0 + d], v[d], dp);
+        s = fmaf(sQ[r][hsel + TPK * d], k[d], s);
+        dp = fmaf(sO[r][hsel + TPK * d], v[d], dp);
       }
       if constexpr (TPK > 1) {
         const unsigned grp = ((1u << TPK) - 1u) << ((threadIdx.x & 31) & ~(TPK - 1));
@@ -503,18 +507,18 @@ __global__ void __launch_bounds__(kRows) attn_simt_dkv_kernel(AttnSimtArgs a) {
       const float ds = pr * (dp - sD[r]);
 #pragma unroll
       for (int d = 0; d < HW; ++d) {
-        dv[d] = fmaf(pr, sO[r][d0 + d], dv[d]);
-        dk[d] = fmaf(ds, sQ[r][d0 + d], dk[d]);  // sQ holds q * scale * log2(e)
+        dv[d] = fmaf(pr, sO[r][hsel + TPK * d], dv[d]);
+        dk[d] = fmaf(ds, sQ[r][hsel + TPK * d], dk[d]);  // sQ holds q * scale * log2(e)
       }
     }
   }
   if (j >= a.Lk) return;
-  __nv_bfloat16* dst = a.dqkv + (static_cast<long long>(b) * a.Lk + j) * rs + h * HD + d0;
+  __nv_bfloat16* dst = a.dqkv + (static_cast<long long>(b) * a.Lk + j) * rs + h * HD + hsel;
 #pragma unroll
   for (int d = 0; d < HW; ++d) {
-    dst[D + d] = __float2bfloat16(dk[d] / kLog2e);
-    dst[2 * D + d] = __float2bfloat16(dv[d]);
-    if (j < q_first) dst[d] = __float2bfloat16(0.f);  // Q rows that are not queries
+    dst[D + TPK * d] = __float2bfloat16(dk[d] / kLog2e);
+    dst[2 * D + TPK * d] = __float2bfloat16(dv[d]);
+    if (j < q_first) dst[TPK * d] = __float2bfloat16(0.f);  // Q rows that are not queries
   }
 }
 
