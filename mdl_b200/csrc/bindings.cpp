@@ -764,6 +764,61 @@ void sqa_bwd(const at::Tensor& q, const at::Tensor& hist, const at::Tensor& ksta
   g_launches += 1;
 }
 
+void sqa_shared_fwd(const at::Tensor& q, const at::Tensor& hist, const at::Tensor& kstart, const at::Tensor& ctx,
+                    const at::Tensor& lse, double scale) {
+  c10::cuda::CUDAGuard guard(q.device());
+  TORCH_CHECK(q.scalar_type() == at::kFloat && hist.scalar_type() == at::kBFloat16 &&
+                  kstart.scalar_type() == at::kInt && ctx.scalar_type() == at::kFloat && lse.scalar_type() == at::kFloat,
+              "sqa_shared_fwd: fp32 q / ctx / lse, bf16 history, int32 kstart");
+  TORCH_CHECK(hist.dim() == 3 && q.dim() == 3 && hist.is_contiguous() && q.is_contiguous() && ctx.is_contiguous() &&
+                  lse.is_contiguous(),
+              "sqa_shared_fwd: contiguous q [B, G, D] and history [B, L, D]");
+  mdl::SqaSharedArgs a;
+  a.B = static_cast<int>(hist.size(0)); a.L = static_cast<int>(hist.size(1)); a.D = static_cast<int>(hist.size(2));
+  a.G = static_cast<int>(q.size(1));
+  TORCH_CHECK(q.size(0) == a.B && q.size(2) == a.D && ctx.sizes() == q.sizes() &&
+                  lse.numel() == static_cast<int64_t>(a.B) * a.G && kstart.numel() >= a.B,
+              "sqa_shared_fwd: sizes");
+  TORCH_CHECK(mdl::sqa_shared_supported(a.G, a.D), "sqa_shared_fwd: unsupported G / D");
+  a.q = q.data_ptr<float>();
+  a.hist = reinterpret_cast<const __nv_bfloat16*>(hist.data_ptr());
+  a.kstart = kstart.data_ptr<int>();
+  a.ctx = ctx.data_ptr<float>();
+  a.lse = lse.data_ptr<float>();
+  a.scale = static_cast<float>(scale);
+  check(mdl::sqa_shared_fwd(a, stream_of(q)), "sqa_shared_fwd");
+  g_launches += 1;
+}
+
+void sqa_shared_bwd(const at::Tensor& q, const at::Tensor& hist, const at::Tensor& kstart, const at::Tensor& ctx,
+                    const at::Tensor& lse, const at::Tensor& dctx, const at::Tensor& dq, const at::Tensor& dhist,
+                    double scale) {
+  c10::cuda::CUDAGuard guard(q.device());
+  TORCH_CHECK(dctx.scalar_type() == at::kFloat && dq.scalar_type() == at::kFloat &&
+                  dhist.scalar_type() == at::kBFloat16 && dctx.is_contiguous() && dq.is_contiguous() &&
+                  dhist.is_contiguous() && dhist.sizes() == hist.sizes() && hist.is_contiguous() && hist.dim() == 3,
+              "sqa_shared_bwd: fp32 dctx / dq, bf16 dhist shaped like the history [B, L, D]");
+  mdl::SqaSharedArgs a;
+  a.B = static_cast<int>(hist.size(0)); a.L = static_cast<int>(hist.size(1)); a.D = static_cast<int>(hist.size(2));
+  a.G = static_cast<int>(q.size(1));
+  TORCH_CHECK(q.dim() == 3 && q.size(0) == a.B && q.size(2) == a.D && dctx.sizes() == q.sizes() &&
+                  dq.sizes() == q.sizes() && ctx.sizes() == q.sizes() &&
+                  lse.numel() == static_cast<int64_t>(a.B) * a.G && kstart.numel() >= a.B,
+              "sqa_shared_bwd: sizes");
+  TORCH_CHECK(mdl::sqa_shared_supported(a.G, a.D), "sqa_shared_bwd: unsupported G / D");
+  a.q = q.data_ptr<float>();
+  a.hist = reinterpret_cast<const __nv_bfloat16*>(hist.data_ptr());
+  a.kstart = kstart.data_ptr<int>();
+  a.ctx = ctx.data_ptr<float>();
+  a.lse = lse.data_ptr<float>();
+  a.dctx = dctx.data_ptr<float>();
+  a.dq = dq.data_ptr<float>();
+  a.dhist = reinterpret_cast<__nv_bfloat16*>(dhist.data_ptr());
+  a.scale = static_cast<float>(scale);
+  check(mdl::sqa_shared_bwd(a, stream_of(q)), "sqa_shared_bwd");
+  g_launches += 1;
+}
+
 void position_grad(const at::Tensor& dx, const at::Tensor& dpos, const at::Tensor& kstart, int64_t B, int64_t L,
                    int64_t D) {
   c10::cuda::CUDAGuard guard(dx.device());
@@ -960,6 +1015,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("position_add", &position_add);
   m.def("position_grad", &position_grad);
   m.def("sqa_fwd", &sqa_fwd);
+  m.def("sqa_shared_fwd", &sqa_shared_fwd);
+  m.def("sqa_shared_bwd", &sqa_shared_bwd);
+  m.def("sqa_shared_supported", [](int G, int D) { return mdl::sqa_shared_supported(G, D); });
   m.def("sqa_bwd", &sqa_bwd);
   m.def("fmha_bwd", &fmha_bwd, py::arg("qkv"), py::arg("kstart"), py::arg("out"), py::arg("lse"), py::arg("dout"),
         py::arg("dqkv"), py::arg("dq_acc"), py::arg("dsum"), py::arg("H"), py::arg("Lq"), py::arg("causal"),

@@ -14,7 +14,9 @@ length-sized K/V), then ``q_{i+1} = LN_{i+1}(SwiGLU_{i+1}(P_i [o_0 .. o_i, x_t])
 token ``x_t``. Projections are bias-free (the paper's parameterisation).
 
 History transforms are grouped-GEMM SwiGLUs and LayerNorm on the CUDA kernels; the
-per-sample single-query attention is two batched products over the history.
+per-sample attention of the H score vectors over the history is the shared-history kernel of
+``csrc/sqa.cu`` (one warp per sample, the bf16 history read once for every head; the
+history gradient summed over the heads in the same pass).
 """
 
 from __future__ import annotations
@@ -24,6 +26,7 @@ import math
 import torch
 from torch import nn
 
+from ..ops.attention import shared_query_attention, shared_query_supported
 from ..ops.layers import gemm_param, layer_norm, linear_nb, swiglu
 
 
@@ -71,11 +74,16 @@ class STCALayer(nn.Module):
         H, hd, d = self.heads, self.hd, self.dim
         pq = linear_nb(q, self.wq, native).float().view(B, H, hd)
         sv = torch.einsum("bhk,hkd->bhd", pq, self.wk.view(H, hd, d))          # score vector per head
-        hf = hist.float()
-        scores = torch.einsum("bhd,bld->bhl", sv, hf) / math.sqrt(hd)
-        mask = valid.bool().unsqueeze(1)
-        w = torch.nan_to_num(torch.softmax(scores.masked_fill(~mask, float("-inf")), dim=-1)) * mask
-        ctx = torch.einsum("bhl,bld->bhd", w, hf)                               # [B, H, d]
+        if native and hist.is_cuda and shared_query_supported(H, d):
+            # valid is a suffix mask (left-padded window): its first valid event is L - count
+            kstart = (hist.shape[1] - valid.sum(dim=-1)).to(torch.int32)
+            ctx = shared_query_attention(sv, hist, kstart, 1.0 / math.sqrt(hd))  # [B, H, d]
+        else:
+            hf = hist.float()
+            scores = torch.einsum("bhd,bld->bhl", sv, hf) / math.sqrt(hd)
+            mask = valid.bool().unsqueeze(1)
+            w = torch.nan_to_num(torch.softmax(scores.masked_fill(~mask, float("-inf")), dim=-1)) * mask
+            ctx = torch.einsum("bhl,bld->bhd", w, hf)                           # [B, H, d]
         vals = torch.einsum("bhd,hkd->bhk", ctx, self.wv.view(H, hd, d)).reshape(B, d)
         return linear_nb(vals, self.wo, native)
 

@@ -182,3 +182,69 @@ def single_query_attention(q: torch.Tensor, hist: torch.Tensor, kstart: torch.Te
         if q.is_cuda:
             return SingleQueryAttentionFn.apply(q, hist, kstart, scale)
         return single_query_attention_reference(q, hist, kstart, scale)
+
+
+def shared_query_attention_reference(q: torch.Tensor, hist: torch.Tensor, kstart: torch.Tensor,
+                                     scale: float) -> torch.Tensor:
+    """fp32 definition: for sample ``b`` and query ``g`` of ``q [B, G, D]``,
+    ``softmax(scale * q_g . h_l)`` over the events ``l >= kstart[b]`` of the shared history
+    ``hist [B, L, D]`` (keys = values = the rows), weighted sum of ``h_l``; a sample without a
+    valid event gives zero."""
+
+    B, L, D = hist.shape
+    hf = hist.float()
+    s = torch.matmul(q.float(), hf.transpose(-1, -2)) * scale                       # [B, G, L]
+    valid = torch.arange(L, device=hist.device).view(1, 1, L) >= kstart.to(hist.device).long().view(B, 1, 1)
+    w = torch.nan_to_num(torch.softmax(s.masked_fill(~valid, float("-inf")), dim=-1)) * valid
+    return torch.matmul(w, hf)
+
+
+class SharedQueryAttentionFn(torch.autograd.Function):
+    """CUDA kernels ``sqa_shared_*`` of ``csrc/sqa.cu``: one warp per sample runs all G queries
+    over the bf16 history, which is read once for all of them; the backward recomputes the
+    weights from the saved log-sum-exp and writes the history gradient summed over the queries."""
+
+    @staticmethod
+    def forward(ctx, q, hist, kstart, scale):
+        q = q.float().contiguous()
+        hist = hist.to(torch.bfloat16).contiguous()
+        ks = kstart.to(torch.int32).contiguous()
+        B, G, D = q.shape
+        out = torch.empty(B, G, D, dtype=torch.float32, device=q.device)
+        lse = torch.empty(B, G, dtype=torch.float32, device=q.device)
+        ext().sqa_shared_fwd(q, hist, ks, out, lse, float(scale))
+        ctx.save_for_backward(q, hist, ks, out, lse)
+        ctx.scale = float(scale)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        q, hist, ks, out, lse = ctx.saved_tensors
+        dq = torch.empty_like(q)
+        dhist = torch.empty_like(hist)
+        ext().sqa_shared_bwd(q, hist, ks, out, lse, dout.float().contiguous(), dq, dhist, ctx.scale)
+        return dq, dhist, None, None
+
+
+def shared_query_supported(groups: int, width: int) -> bool:
+    """Shapes of the native kernels: ``width`` even and at most 256, ``groups`` at most 8,
+    and (groups rounded up to 2, 4 or 8) x (ceil(width / 64) rounded up to 1, 2 or 4) <= 16."""
+
+    if groups < 1 or groups > 8 or width < 1 or width > 256 or width % 2:
+        return False
+    g = 2 if groups <= 2 else (4 if groups <= 4 else 8)
+    p = 1 if width <= 64 else (2 if width <= 128 else 4)
+    return g * p <= 16
+
+
+def shared_query_attention(q: torch.Tensor, hist: torch.Tensor, kstart: torch.Tensor, scale: float) -> torch.Tensor:
+    """``q [B, G, D]`` over ``hist [B, L, D]`` with prefix padding ``kstart [B]`` -> ``[B, G, D]``
+    fp32 (CUDA: the native kernels; CPU: the fp32 definition). CUDA shapes outside
+    ``shared_query_supported`` raise."""
+
+    with trace_range("mdl.attention.shared_query"):
+        if q.is_cuda:
+            if not shared_query_supported(q.shape[1], q.shape[2]):
+                raise NotImplementedError(f"shared-history attention: {q.shape[1]} queries of width {q.shape[2]}")
+            return SharedQueryAttentionFn.apply(q, hist, kstart, scale)
+        return shared_query_attention_reference(q, hist, kstart, scale)

@@ -226,3 +226,58 @@ def test_simt_attention_forward_backward(case):
         sl = slice(part * hd * H, (part + 1) * hd * H)
         pr = ((g[..., sl] - gr[..., sl]).norm() / gr[..., sl].norm().clamp_min(1e-6)).item()
         assert pr < 3e-2, f"part {part} relative error {pr}"
+
+
+@pytest.mark.parametrize("B,L,G,D", [(3, 17, 2, 16), (4, 40, 4, 64)])
+def test_shared_query_reference_matches_per_query_softmax(B, L, G, D):
+    from mdl_b200.ops.attention import shared_query_attention_reference
+
+    torch.manual_seed(0)
+    q, hist = torch.randn(B, G, D), torch.randn(B, L, D)
+    ks = torch.randint(0, L + 1, (B,))
+    out = shared_query_attention_reference(q, hist, ks, 0.3)
+    for b in range(B):
+        for g in range(G):
+            if ks[b] >= L:
+                assert not out[b, g].any()
+                continue
+            h = hist[b, ks[b]:]
+            w = torch.softmax(0.3 * h @ q[b, g], 0)
+            torch.testing.assert_close(out[b, g], w @ h, atol=1e-5, rtol=1e-5)
+
+
+def test_shared_query_supported_shapes():
+    from mdl_b200.ops.attention import shared_query_supported
+
+    assert shared_query_supported(2, 256) and shared_query_supported(4, 256) and shared_query_supported(8, 128)
+    assert not shared_query_supported(8, 256) and not shared_query_supported(2, 258)
+    assert not shared_query_supported(9, 64) and not shared_query_supported(2, 63)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B,L,G,D", [(3, 17, 1, 16), (64, 257, 2, 256), (9, 90, 3, 100), (5, 33, 8, 128),
+                                     (17, 64, 4, 256), (2, 5, 6, 62)])
+def test_shared_query_attention_kernel_matches_fp32(B, L, G, D):
+    from mdl_b200.ops.attention import SharedQueryAttentionFn, shared_query_attention_reference
+
+    torch.manual_seed(2)
+    dev = torch.device("cuda")
+    q = (0.3 * torch.randn(B, G, D, device=dev)).requires_grad_(True)
+    hist = torch.randn(B, L, D, device=dev).bfloat16().requires_grad_(True)
+    ks = torch.randint(0, L, (B,), device=dev)
+    ks[0] = L  # a sample without a valid event
+    out = SharedQueryAttentionFn.apply(q, hist, ks, 0.25)
+    ref_q = q.detach().clone().requires_grad_(True)
+    ref_h = hist.detach().float().requires_grad_(True)
+    ref = shared_query_attention_reference(ref_q, ref_h, ks, 0.25)
+    torch.testing.assert_close(out, ref, atol=2e-3, rtol=2e-3)
+    g = torch.randn_like(ref)
+    out.backward(g)
+    ref.backward(g)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(q.grad, ref_q.grad, atol=5e-3, rtol=5e-3)
+    torch.testing.assert_close(hist.grad.float(), ref_h.grad, atol=2e-2, rtol=2e-2)
+    assert not hist.grad[0].any()
+    for b in range(1, B):  # padding events get zero gradient
+        assert not hist.grad[b, :int(ks[b])].any()
+

@@ -51,6 +51,26 @@ def _rankmixer_mapping():
     return m
 
 
+def _stca_rankmixer_mapping():
+    """STCA summaries (native path: the shared-history single-query attention kernels) with
+    2 heads of width 128 and 4 heads of width 64 over 256-wide histories."""
+
+    m = _base("rankmixer")
+    feats = [f["name"] for f in m["features"]]
+    m["sequences"] = [
+        _seq("hist_stca", 30, "stca", stca_dim=256, stca_layers=2, stca_num_heads=2, stca_expansion_ratio=2,
+             target_inputs=[feats[0], feats[1]]),
+        _seq("hist_stca4", 20, "stca", stca_dim=256, stca_layers=1, stca_num_heads=4, stca_expansion_ratio=2,
+             target_inputs=[feats[2]]),
+    ]
+    groups = [{"name": f"g{i}", "inputs": feats[i * 3:(i + 1) * 3]} for i in range(5)]
+    groups += [{"name": "s_stca", "inputs": ["hist_stca"]}, {"name": "s_stca4", "inputs": ["hist_stca4"]},
+               {"name": "dense", "inputs": [feats[-1]]}]
+    m["tokenization"] = {"feature_tokenizer": "groupwise", "feature_tokens": groups}
+    m["model"].update({"token_dim": 256, "hidden_dim": 512, "task_head_hidden_dim": 128, "num_heads": 8})
+    return m
+
+
 def _onetrans_mapping():
     m = _base("onetrans")
     m["sequences"] = [_seq("s_a", 48, "raw"), _seq("s_b", 32, "raw"), _seq("s_c", 24, "raw")]
@@ -91,7 +111,8 @@ def _build(mapping, backend):
     return model, trainer, batch
 
 
-@pytest.mark.parametrize("make", [_rankmixer_mapping, _onetrans_mapping, _mixformer_mapping])
+@pytest.mark.parametrize("make", [_rankmixer_mapping, _stca_rankmixer_mapping, _onetrans_mapping,
+                                  _mixformer_mapping])
 def test_native_matches_fp32_definition(make):
     from mdl_b200.ops._ext import check_error_word
 
