@@ -157,8 +157,10 @@ def _stalling_factory(seconds):
 def test_host_prepare_startup_timeout():
     from mdl_b200.data.prepare_process import ProcessBatchIterator
 
-    # heartbeats keep a slow start alive; a child silent past the limit is reported
-    it = ProcessBatchIterator(_stalling_factory, (20.0,), startup_timeout_s=12.0, beat_s=0.5)
+    # heartbeats keep a slow start alive; a child silent past the limit is reported. The
+    # limit leaves room for a spawned child to import its modules on a loaded host (over
+    # 12 s with eight test workers on eight cores); the stall outlasts it.
+    it = ProcessBatchIterator(_stalling_factory, (40.0,), startup_timeout_s=30.0, beat_s=0.5)
     assert list(it) == []
     it.close()
     it = ProcessBatchIterator(_stalling_factory, (30.0,), startup_timeout_s=1.0, beat_s=60.0)
